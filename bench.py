@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Throughput benchmark of the PP-OCRv6 hot path on B200 (driver contract).
+
+Default workload: the tiny detector forward at 416x736 (benchmark configs 1
+and 3: the reference's ppocr-gpu-bench --kind det shape, batched 32 images per
+GPU), seeded uniform-RGB8 inputs, seeded random-init weights in the exact
+reference checkpoint layout, FP32 (the parity mode).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--kind det|rec] [--size tiny|small|medium] [--batch B]
+
+One process per GPU (torchrun for N > 1); images shard across ranks with no
+collective on the data path (weak scaling).  A step is one forward of the
+rank's batch.  `value` is device-timed throughput with inputs resident in HBM
+(the model's own input slot), each step bracketed by CUDA events on the
+launching stream with an L2 flush between steps; `e2e` is the same metric
+through the C ABI's host-buffer forward (pinned H2D input, D2H output).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "ppocr-rs_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, BF16_FALLBACK_TFLOPS, "fallback"
+
+
+def _workload(args):
+    if args.kind == "det":
+        h, w = 416, 736
+        shape = (args.batch, 3, h, w)
+        name = f"{args.size} detector forward, {args.batch}x3x{h}x{w} per GPU"
+        unit = "img/s"
+        metric = f"det img/s @416x736 ({args.size} detector, batch {args.batch}/GPU)"
+    else:
+        h, w = 48, 320
+        shape = (args.batch, 3, h, w)
+        name = f"{args.size} recognizer forward + greedy CTC, {args.batch}x3x{h}x{w} per GPU"
+        unit = "crops/s"
+        metric = f"rec crops/s @48x320 ({args.size} recognizer, batch {args.batch}/GPU)"
+    return shape, name, unit, metric
+
+
+def _inputs(kind, shape, seed):
+    from ppocr_b200 import seeded
+
+    if kind == "det":
+        return seeded.det_batch(shape[0], shape[2], shape[3], seed=seed)
+    return seeded.rec_batch(shape[0], shape[3], seed=seed)
+
+
+class _Clocks:
+    """nvidia-smi sampler for the timed region."""
+
+    def __init__(self, device):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+        self.device = device
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        sms, maxs, reasons = [], [], set()
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    maxs.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                     parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        except OSError:
+            pass
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def _device_view(ptr, count, torch):
+    """A torch float32 view of `count` floats at device address `ptr`."""
+
+    class _Ptr:
+        __cuda_array_interface__ = {"shape": (count,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+    return torch.as_tensor(_Ptr(), device="cuda")
+
+
+def cpu_baseline(args, shape, seconds=12.0):
+    """The oracle (CPU restatement of src/cpu/model.rs) on a bounded sample, all host threads."""
+    import torch
+
+    from oracle import model as om
+    from ppocr_b200 import seeded
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = om.Weights(seeded.make_weights(args.kind, args.size, 0, "spec"))
+    m = om.Detector(w, args.size) if args.kind == "det" else om.Recognizer(w, args.size)
+    sample = 1 if args.kind == "det" else min(shape[0], 8)
+    x = _inputs(args.kind, (sample,) + tuple(shape[1:]), seed=99)
+    fwd = m.forward if args.kind == "det" else m.forward
+    fwd(x)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 2:
+        fwd(x)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n * sample / dt, 3), "unit": "img/s" if args.kind == "det" else "crops/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} forwards of {sample}x{shape[1]}x{shape[2]}x{shape[3]} ({args.size}, FP32 torch-CPU oracle)"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm (the oracle port; the Rust crate cannot be built here)."""
+    rank = int(os.environ.get("RANK", "0"))
+    shape, name, unit, metric = _workload(args)
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import model as om
+    from ppocr_b200 import seeded
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = om.Weights(seeded.make_weights(args.kind, args.size, 0, "spec"))
+    m = om.Detector(w, args.size) if args.kind == "det" else om.Recognizer(w, args.size)
+    sample = min(shape[0], 2 if args.kind == "det" else 16)
+    x = _inputs(args.kind, (sample,) + tuple(shape[1:]), seed=99)
+    for _ in range(max(args.warmup, 1)):
+        m.forward(x)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        m.forward(x)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * args.steps / total
+    line = {
+        "impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": name, "sample_per_step": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{sample} of the {shape[0]} inputs per step, torch-CPU FP32 restatement of "
+                                   f"src/cpu/model.rs (ppocr-cpu-bench needs a Rust toolchain, absent here)"},
+        "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    shape, name, unit, metric = _workload(args)
+    precision = args.precision or ("fp32" if args.kind == "det" else "bf16")
+    tmp = tempfile.mkdtemp(prefix=f"ppocr_bench_{rank}_")
+    wpath = os.path.join(tmp, f"{args.kind}_{args.size}.safetensors")
+    seeded.write_weights(wpath, args.kind, args.size, 0, "spec")
+    gpu = P.Gpu(local)
+    Model = P.Detector if args.kind == "det" else P.Recognizer
+    model = Model.load(gpu, wpath, args.size, shape, precision=precision)
+    x = _inputs(args.kind, shape, seed=1000 + rank)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    din, dout = model.device_buffers()
+    _device_view(din, x.size, torch).copy_(torch.from_numpy(x.reshape(-1)))
+    torch.cuda.synchronize()
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        model.run(sptr)
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with _Clocks(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            model.run(sptr)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        wall = time.perf_counter() - w0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+    units = shape[0] * world * args.steps
+    value = units / (total_ms / 1000.0)
+
+    # Output sanity: the device forward produced finite values.
+    out = _device_view(dout, model.output_elements, torch)
+    finite = bool(torch.isfinite(out).all().item())
+
+    # Per-kernel timing (events around every op) for the roofline.
+    ops = model.ops()
+    prof = model.profile(runs=3)
+    fam = {}
+    for op, ms in zip(ops, prof):
+        f = fam.setdefault(op["kind"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "launches": 0})
+        f["ms"] += ms
+        f["bytes"] += op["bytes"]
+        f["flops"] += op["flops"]
+        f["launches"] += 1
+    dom_kind = max(fam, key=lambda k: fam[k]["ms"])
+    dom = fam[dom_kind]
+    hbm, tflops, peak_src = _peaks()
+    launches = dom["launches"]
+    per_launch_ms = dom["ms"] / launches
+    tensor_bound = dom_kind == "gemm" and precision == "bf16"
+    if tensor_bound:
+        achieved = dom["flops"] / launches / (per_launch_ms / 1000.0) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(achieved / tflops, 4)}
+    else:
+        achieved = dom["bytes"] / launches / (per_launch_ms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4)}
+    roof.update({"kernel": dom_kind, "launches_per_step": launches, "time_share": round(dom["ms"] / sum(prof), 4),
+                 "peak_source": peak_src, "traffic": None,
+                 "algorithmic_bytes_per_launch": round(dom["bytes"] / launches),
+                 "families": {k: {"ms": round(v["ms"], 4), "launches": v["launches"],
+                                  "GBps": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1)} for k, v in fam.items()}})
+    traffic_path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(traffic_path):
+        try:
+            with open(traffic_path) as f:
+                t = json.load(f).get(f"{args.kind}_{args.size}_{precision}", {}).get(dom_kind)
+            if t is not None:
+                roof["traffic"] = t
+        except Exception:
+            pass
+
+    # End to end through the C ABI with pinned host buffers.
+    e2e = None
+    if not args.no_e2e:
+        hin = torch.from_numpy(x.reshape(-1)).pin_memory()
+        hout = torch.empty(model.output_elements, dtype=torch.float32).pin_memory()
+        import ctypes as C
+
+        lib = P.library()
+        fin = C.cast(C.c_void_p(hin.data_ptr()), C.POINTER(C.c_float))
+        fout = C.cast(C.c_void_p(hout.data_ptr()), C.POINTER(C.c_float))
+        for _ in range(max(2, args.warmup // 2)):
+            P._check(lib.ppocr_model_forward(model._h, fin, x.size, fout, model.output_elements))
+        barrier()
+        e_steps = max(3, args.steps // 2)
+        t0 = time.perf_counter()
+        for _ in range(e_steps):
+            P._check(lib.ppocr_model_forward(model._h, fin, x.size, fout, model.output_elements))
+        et = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(shape[0] * world * e_steps / float(et.item()), 2), "unit": unit,
+               "h2d_bytes_per_step": int(x.size * 4), "d2h_bytes_per_step": int(model.output_elements * 4 + 8),
+               "steps": e_steps, "api": "ppocr_model_forward (host buffers, pinned)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, shape)
+
+    launches_per_step = sum(1 for op in ops)
+    if rank == 0:
+        line = {
+            "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if precision == "fp32" else "bf16",
+            "data": "synthetic (seeded uniform RGB8 inputs, seeded random-init weights in the reference layout)",
+            "config": {"workload": name, "batch_per_gpu": shape[0], "precision": precision,
+                       "parallelism": f"dp{world} (images sharded, no collective)",
+                       "l2": "256 MiB flush between timed steps", "cuda_graph": True},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(), "wall_s": round(wall, 3), "output_finite": finite,
+            "step_ms_min_max": [round(min(step_ms), 4), round(max(step_ms), 4)],
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    gpu.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--kind", default="det", choices=["det", "rec"])
+    ap.add_argument("--size", default="tiny", choices=["tiny", "small", "medium"])
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--precision", default=None, choices=[None, "fp32", "bf16"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.batch is None:
+        args.batch = 32 if args.kind == "det" else 256
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,216 @@
+/*
+ * ppocr_b200.h - C ABI of the B200-native PP-OCRv6 detector / recognizer backend.
+ *
+ * This is the drop-in boundary for ppocr-rs's direct-model GPU API
+ * (`ppocr_rs::gpu`, src/gpu/mod.rs:1-13).  Each entry point replaces one Rust
+ * item, cited beside it.  Conventions:
+ *   - every call returns an `int` status: PPOCR_OK (0) or one of the error
+ *     codes below, which map 1:1 onto the variants of `gpu::Error`
+ *     (src/gpu/error.rs:8-45); the message of the last failure on the calling
+ *     thread is returned by ppocr_last_error();
+ *   - handles are opaque; a handle is used by one thread at a time;
+ *   - host pointers are plain arrays owned by the caller; nothing crosses the
+ *     ABI as a C++ exception or a framework tensor type;
+ *   - shapes are NCHW [n, c, h, w] for inputs, [n, 1, h, w] for detector
+ *     outputs and [n, t, classes] for recognizer outputs, as in
+ *     `ModelOutput` (src/gpu/model.rs:38-42).
+ */
+#ifndef PPOCR_B200_H
+#define PPOCR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: one per `gpu::Error` variant (src/gpu/error.rs:8-45). */
+enum ppocr_status {
+    PPOCR_OK = 0,
+    PPOCR_ERR_READ_FILE = 1,            /* Error::ReadFile */
+    PPOCR_ERR_SAFETENSORS = 2,          /* Error::Safetensors */
+    PPOCR_ERR_TENSOR_NOT_FOUND = 3,     /* Error::TensorNotFound */
+    PPOCR_ERR_UNSUPPORTED_DTYPE = 4,    /* Error::UnsupportedDtype */
+    PPOCR_ERR_SHAPE_MISMATCH = 5,       /* Error::ShapeMismatch */
+    PPOCR_ERR_TENSOR_SIZE_OVERFLOW = 6, /* Error::TensorSizeOverflow */
+    PPOCR_ERR_TENSOR_BYTE_LENGTH = 7,   /* Error::TensorByteLength */
+    PPOCR_ERR_INVALID_TENSOR_RANGE = 8, /* Error::InvalidTensorRange */
+    PPOCR_ERR_INVALID_MODEL = 9,        /* Error::InvalidModel */
+    PPOCR_ERR_INVALID_INPUT = 10,       /* Error::InvalidInput */
+    PPOCR_ERR_GPU = 11                  /* Error::Gpu */
+};
+
+/* Model tiers: `ModelSize` (src/models.rs:62-69). */
+enum ppocr_model_size { PPOCR_MEDIUM = 0, PPOCR_SMALL = 1, PPOCR_TINY = 2 };
+
+/* Activation storage / GEMM precision of a loaded model.
+ * FP32: FP32 activations, FP32 arithmetic throughout (the reference's own
+ *       arithmetic; the parity mode).
+ * BF16: BF16 activations in HBM, tcgen05 BF16 tensor-core GEMMs with FP32
+ *       accumulation; all other arithmetic FP32 in registers. */
+enum ppocr_precision { PPOCR_PRECISION_FP32 = 0, PPOCR_PRECISION_BF16 = 1 };
+
+typedef struct ppocr_gpu ppocr_gpu;
+typedef struct ppocr_image ppocr_image;
+typedef struct ppocr_model ppocr_model;
+
+/* Options of ppocr_*_load_ex.  Zero-initialise, then set the fields. */
+typedef struct ppocr_load_options {
+    int precision;   /* enum ppocr_precision; default FP32 */
+    int use_graph;   /* 1: replay each forward as one captured CUDA graph */
+    int reserved[6];
+} ppocr_load_options;
+
+/* Fills `options` with the defaults (FP32, CUDA graphs on). */
+void ppocr_load_options_default(ppocr_load_options* options);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ppocr_last_error(void);
+
+/* Number of visible CUDA devices. New: ppocr-rs picks one wgpu adapter
+ * (src/gpu/runtime.rs:99-104); the B200 build shards across devices. */
+int ppocr_gpu_count(int* count);
+
+/* Gpu::new() (src/gpu/runtime.rs:94-167): binds `device`, creates its stream
+ * set and the per-device activation arena. */
+int ppocr_gpu_create(int device, ppocr_gpu** out);
+void ppocr_gpu_destroy(ppocr_gpu* gpu);
+
+/* Gpu::info() (src/gpu/runtime.rs:169-171): adapter name into `name`. */
+int ppocr_gpu_info(const ppocr_gpu* gpu, char* name, size_t capacity);
+
+/* Gpu::upload_rgb(width, height, &[u8]) (src/gpu/runtime.rs:174-229):
+ * interleaved RGB8, `len` must equal width*height*3. */
+int ppocr_upload_rgb(ppocr_gpu* gpu, uint32_t width, uint32_t height,
+                     const uint8_t* pixels, size_t len, ppocr_image** out);
+void ppocr_image_destroy(ppocr_image* image);
+
+/* gpu::Detector::load(&Gpu, path, ModelSize, [n,c,h,w]) (src/gpu/model.rs:50-93).
+ * Validates the shape (src/gpu/model.rs:268-276) and the tier's tensor count
+ * (src/gpu/model.rs:58-65), packs the safetensors weights. */
+int ppocr_detector_load(ppocr_gpu* gpu, const char* path, int size,
+                        const size_t input_shape[4], ppocr_model** out);
+int ppocr_detector_load_ex(ppocr_gpu* gpu, const char* path, int size,
+                           const size_t input_shape[4],
+                           const ppocr_load_options* options, ppocr_model** out);
+
+/* gpu::Recognizer::load (src/gpu/model.rs:156-220), shape rules at
+ * src/gpu/model.rs:278-286.  `shared_weights_from` (may be NULL) reuses the
+ * device weights of an already-loaded recognizer of the same file and tier,
+ * as `load_with_shared_weights` does (src/gpu/model.rs:168-218). */
+int ppocr_recognizer_load(ppocr_gpu* gpu, const char* path, int size,
+                          const size_t input_shape[4], ppocr_model** out);
+int ppocr_recognizer_load_ex(ppocr_gpu* gpu, const char* path, int size,
+                             const size_t input_shape[4],
+                             const ppocr_load_options* options,
+                             const ppocr_model* shared_weights_from,
+                             ppocr_model** out);
+void ppocr_model_destroy(ppocr_model* model);
+
+/* Device-free load check (new): runs every check of Detector::load /
+ * Recognizer::load (src/gpu/model.rs:50-93, 156-220: input shape, tensor
+ * count, names, shapes, dtypes, rank-one separability) and builds the plan
+ * without touching a GPU.  kind: 0 detector, 1 recognizer.  Any output
+ * pointer may be NULL. */
+int ppocr_inspect_model(const char* path, int kind, int size, const size_t input_shape[4], int precision,
+                        size_t* ops, size_t* arena_bytes, size_t* weight_bytes, size_t output_shape[4]);
+
+/* ModelOutput::shape: writes the output shape (rank 4 for the detector,
+ * rank 3 for the recognizer) and the element count. */
+int ppocr_model_output_shape(const ppocr_model* model, size_t shape[4],
+                             size_t* rank, size_t* elements);
+/* Input shape the model was loaded for. */
+int ppocr_model_input_shape(const ppocr_model* model, size_t shape[4]);
+
+/* Detector::forward / Recognizer::forward(&[f32]) (src/gpu/model.rs:95-114,
+ * 222-238): NCHW F32 host input of `input_len` values, host output of
+ * `output_capacity` values (>= ppocr_model_output_shape's element count).
+ * Detector output: probability map.  Recognizer output: per-step class
+ * probabilities (softmax), as the reference returns. */
+int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len,
+                        float* output, size_t output_capacity);
+
+/* forward_image(&GpuImage, ImagePreprocess) (src/gpu/model.rs:116-138,
+ * 240-259; ImagePreprocess::{detector, recognizer} src/gpu/runtime.rs:50-69):
+ * device-side quad resample, BGR swap, normalisation and right zero-padding
+ * past `content_width` (the detector passes the input width).  `corners`
+ * holds four (x, y) source points: top-left, top-right, bottom-right,
+ * bottom-left.  Batch must be 1. */
+int ppocr_model_forward_image(ppocr_model* model, const ppocr_image* image,
+                              const float corners[8], size_t content_width,
+                              float* output, size_t output_capacity);
+
+/* Detector::benchmark / Recognizer::benchmark(&[f32], warmup, runs)
+ * (src/gpu/model.rs:140-148, 261-266; timed region src/gpu/runtime.rs:1798-1830):
+ * uploads once, then times `runs` forwards on the device (submit + wait, no
+ * readback).  `samples_ms` receives `runs` values in milliseconds. */
+int ppocr_model_benchmark(ppocr_model* model, const float* input, size_t input_len,
+                          size_t warmup, size_t runs, double* samples_ms);
+
+/* Batched device-resident forward (new; the reference has no batched
+ * device API).  `device_input` is a device pointer to NCHW F32 input,
+ * `device_output` a device pointer receiving the F32 output, `stream` a
+ * cudaStream_t (NULL = the model's own stream).  Asynchronous: returns
+ * after enqueueing. */
+int ppocr_model_forward_device(ppocr_model* model, const float* device_input,
+                               float* device_output, void* stream);
+
+/* Zero-copy device residency (new): the device addresses of the model's own
+ * input slot (NCHW F32) and output (detector probability map / recognizer
+ * probabilities, F32) inside the activation arena.  Valid until another
+ * model on the same ppocr_gpu grows the arena (a later load); re-query after
+ * loading.  ppocr_model_run enqueues one forward over whatever the input
+ * slot holds on `stream` (NULL = the model's stream) and returns. */
+int ppocr_model_device_buffers(ppocr_model* model, float** device_input, float** device_output);
+int ppocr_model_run(ppocr_model* model, void* stream);
+
+/* Waits (bounded by `timeout_ms`; <= 0 means 60 s) for the model's stream;
+ * Error::Gpu on a timeout or an asynchronous device error. */
+int ppocr_model_synchronize(ppocr_model* model, int timeout_ms);
+
+/* Recognizer only: greedy CTC on the device (replaces the argmax scan of
+ * decode_ctc_greedy_for_input, src/ocr.rs:800-853).  For every (n, t) writes
+ * the arg-max class (ties resolve to the highest index, as Rust's
+ * Iterator::max_by does), its probability, and the top-2 logit margin.
+ * All three are host arrays of n*t entries; any may be NULL. */
+int ppocr_recognizer_forward_ctc(ppocr_model* model, const float* input, size_t input_len,
+                                 int32_t* indices, float* probabilities, float* margins);
+
+/* Per-op profile: the counterpart of PPOCR_GPU_PROFILE's per-dispatch
+ * timestamps (src/gpu/runtime.rs:1815-1817, 1832-1933).  op_info describes
+ * op `index` of the plan: name, kernel family, algorithmic bytes (every
+ * tensor read and written once plus weights) and FLOPs.  profile runs the
+ * plan op by op `runs` times over the current input slot, bracketing every op
+ * with CUDA events on the model's stream, and writes each op's mean time in
+ * milliseconds to op_ms[count]. */
+int ppocr_model_op_count(const ppocr_model* model, size_t* count);
+int ppocr_model_op_info(const ppocr_model* model, size_t index, char* name, size_t name_capacity,
+                        char* kind, size_t kind_capacity, double* bytes, double* flops);
+int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms);
+
+/* Recognizer only: the classifier's pre-softmax logits [n, t, classes]
+ * (new; the reference fuses the softmax, src/cpu/backend.rs:1288-1290, so it
+ * never exposes them). */
+int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size_t input_len,
+                                    float* logits, size_t logits_capacity);
+
+/* Device preprocessing alone (prepare_detector / prepare_recognizer,
+ * src/preprocess.rs:37-76): quad resample of `image` into an NCHW F32
+ * [1, 3, out_h, out_w] host array.  kind 0 = detector normalisation
+ * (ImageNet mean/std), 1 = recognizer ((x/255 - 0.5)/0.5); columns at and
+ * past `content_width` are zero. */
+int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
+                     size_t out_h, size_t out_w, int kind, float* output);
+
+/* Detector only: probability map plus the DB binarisation mask
+ * (prob >= threshold, src/ocr.rs:745,1047) as bytes of n*h*w. Either output
+ * may be NULL. */
+int ppocr_detector_forward_mask(ppocr_model* model, const float* input, size_t input_len,
+                                float threshold, float* probabilities, uint8_t* mask);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PPOCR_B200_H */

@@ -1,0 +1,679 @@
+// extern "C" boundary: the ppocr_rs::gpu API (src/gpu/mod.rs) as a C ABI.
+//
+// One ppocr_gpu per device owns a non-blocking stream and the activation
+// arena shared by every model loaded on it (grown to the largest plan, as
+// ppocr-rs's shared workspace is, src/gpu/runtime.rs:1718-1730).  A model
+// owns its packed weights (shareable between recognizers of one file), its
+// plan and, when enabled, the CUDA graph of its forward, re-captured when the
+// arena moves.  Every wait is bounded: a stuck stream surfaces as Error::Gpu.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "common.hpp"
+#include "models.hpp"
+#include "ppocr_b200.h"
+#include "safetensors.hpp"
+
+using namespace ppocr;
+
+namespace {
+thread_local std::string g_last_error;
+
+template <typename F>
+int guard(F&& f) {
+    try {
+        f();
+        g_last_error.clear();
+        return PPOCR_OK;
+    } catch (const Error& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "out of host memory";
+        return PPOCR_ERR_GPU;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return PPOCR_ERR_GPU;
+    }
+}
+
+struct DeviceWeights {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    std::vector<uint8_t> host;   // kept for sharing checks
+    ~DeviceWeights() {
+        if (ptr) cudaFree(ptr);
+    }
+};
+
+void wait_stream(cudaStream_t s, int timeout_ms) {
+    if (timeout_ms <= 0) timeout_ms = 60000;
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+    int spins = 0;
+    while (true) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) cuda_check(e, "device execution");
+        if (std::chrono::steady_clock::now() > deadline) fail(PPOCR_ERR_GPU, "device did not finish within the wait limit");
+        if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+}  // namespace
+
+struct ppocr_gpu {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    uint64_t arena_gen = 0;
+    std::string name;
+
+    void bind() const { cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
+    void ensure_arena(size_t bytes) {
+        if (bytes <= arena_bytes) return;
+        cuda_check(cudaStreamSynchronize(stream), "synchronize before arena growth");
+        if (arena) cudaFree(arena);
+        arena = nullptr;
+        arena_bytes = 0;
+        cuda_check(cudaMalloc(&arena, bytes), "allocate activation arena");
+        arena_bytes = bytes;
+        ++arena_gen;
+    }
+};
+
+struct ppocr_image {
+    ppocr_gpu* gpu = nullptr;
+    uint8_t* rgb = nullptr;
+    uint32_t width = 0, height = 0;
+};
+
+struct ppocr_model {
+    ppocr_gpu* gpu = nullptr;
+    BuiltModel m;
+    std::shared_ptr<DeviceWeights> weights;
+    ppocr_load_options opts{};
+    cudaGraphExec_t exec = nullptr;
+    uint64_t exec_gen = 0;
+    float exec_threshold = 0.f;
+    bool warmed = false;
+    int* dflags = nullptr;   // device: [0] non-finite input, [1] non-finite output
+    int* hflags = nullptr;   // pinned host copy
+
+    ~ppocr_model() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (dflags) cudaFree(dflags);
+        if (hflags) cudaFreeHost(hflags);
+    }
+
+    Ctx ctx() const {
+        Ctx c;
+        c.arena = static_cast<char*>(gpu->arena);
+        c.weights = static_cast<const char*>(weights->ptr);
+        c.tensors = &m.plan.tensors;
+        return c;
+    }
+    void* tensor(int tid) const { return tid < 0 ? nullptr : static_cast<char*>(gpu->arena) + m.plan.tensors[tid].offset; }
+
+    // Enqueue one forward over the arena input slot.
+    void run(cudaStream_t s) {
+        gpu->ensure_arena(m.plan.arena_bytes);
+        if (!warmed || !opts.use_graph) {
+            m.plan.run(ctx(), s);
+            warmed = true;
+            return;
+        }
+        if (!exec || exec_gen != gpu->arena_gen || exec_threshold != *m.mask_threshold) {
+            if (exec) { cudaGraphExecDestroy(exec); exec = nullptr; }
+            cudaStream_t cap;
+            cuda_check(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), "create capture stream");
+            cudaGraph_t g = nullptr;
+            cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+            if (e == cudaSuccess) {
+                try {
+                    m.plan.run(ctx(), cap);
+                } catch (...) {
+                    cudaStreamEndCapture(cap, &g);
+                    if (g) cudaGraphDestroy(g);
+                    cudaStreamDestroy(cap);
+                    throw;
+                }
+                e = cudaStreamEndCapture(cap, &g);
+            }
+            cudaStreamDestroy(cap);
+            cuda_check(e, "capture forward graph");
+            e = cudaGraphInstantiate(&exec, g, 0);
+            cudaGraphDestroy(g);
+            cuda_check(e, "instantiate forward graph");
+            exec_gen = gpu->arena_gen;
+            exec_threshold = *m.mask_threshold;
+        }
+        cuda_check(cudaGraphLaunch(exec, s), "launch forward graph");
+    }
+
+    int output_tid() const { return m.kind == Kind::Detector ? m.prob : m.probs; }
+    size_t input_elements() const { return (size_t)m.n * 3 * m.h * m.w; }
+};
+
+namespace {
+
+void upload_and_run(ppocr_model* model, const float* input, size_t len) {
+    if (!input) fail(PPOCR_ERR_INVALID_INPUT, "input pointer is null");
+    if (len != model->input_elements()) {
+        fail(PPOCR_ERR_INVALID_INPUT, "input has " + std::to_string(len) + " values; expected " +
+                                          std::to_string(model->input_elements()));
+    }
+    ppocr_gpu* g = model->gpu;
+    g->ensure_arena(model->m.plan.arena_bytes);
+    cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), g->stream), "reset flags");
+    cuda_check(cudaMemcpyAsync(model->tensor(model->m.input), input, len * 4, cudaMemcpyHostToDevice, g->stream), "upload input");
+    // Non-finite inputs are an InvalidInput (src/gpu/runtime.rs:1979-1983); the scan runs on the device.
+    cuda_check(launch_check_finite(static_cast<const float*>(model->tensor(model->m.input)), len, model->dflags, g->stream),
+               "check input");
+    model->run(g->stream);
+}
+
+// Enqueues the output scan and the flag readback, waits, and raises the
+// reference's errors: InvalidInput for a non-finite input, Error::Gpu for a
+// non-finite output (src/gpu/runtime.rs:2217-2219).
+void finish(ppocr_model* model, int checked_tid, size_t checked_count) {
+    cudaStream_t s = model->gpu->stream;
+    if (checked_tid >= 0)
+        cuda_check(launch_check_finite(static_cast<const float*>(model->tensor(checked_tid)), checked_count, model->dflags + 1, s),
+                   "check output");
+    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
+    wait_stream(s, 0);
+    if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
+    if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+}
+
+PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
+                                 size_t out_w, bool detector) {
+    PreprocessParams p;
+    p.rgb = image->rgb;
+    p.src_w = (int)image->width;
+    p.src_h = (int)image->height;
+    std::memcpy(p.corners, corners, sizeof(p.corners));
+    p.out_w = (int)out_w;
+    p.out_h = (int)out_h;
+    p.content_w = (int)content_width;
+    // Normalization::new (src/preprocess/kernels.rs:9-18): scale = 1/(255 std), bias = -mean/std, BGR order
+    const float det_mean[3] = {0.485f, 0.456f, 0.406f}, det_std[3] = {0.229f, 0.224f, 0.225f};
+    for (int c = 0; c < 3; ++c) {
+        const float mean = detector ? det_mean[c] : 0.5f, sd = detector ? det_std[c] : 0.5f;
+        p.scale[c] = 1.0f / (255.0f * sd);
+        p.bias[c] = -mean / sd;
+    }
+    return p;
+}
+
+void download(ppocr_model* model, int tid, void* dst, size_t bytes) {
+    cuda_check(cudaMemcpyAsync(dst, model->tensor(tid), bytes, cudaMemcpyDeviceToHost, model->gpu->stream), "read output");
+}
+
+ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t shape[4], const ppocr_load_options* options,
+                        const ppocr_model* shared, bool detector) {
+    if (!gpu) fail(PPOCR_ERR_INVALID_INPUT, "gpu handle is null");
+    if (!path) fail(PPOCR_ERR_INVALID_INPUT, "model path is null");
+    if (!shape) fail(PPOCR_ERR_INVALID_INPUT, "input shape is null");
+    ppocr_load_options o;
+    if (options) o = *options;
+    else ppocr_load_options_default(&o);
+    if (o.precision != PPOCR_PRECISION_FP32 && o.precision != PPOCR_PRECISION_BF16) fail(PPOCR_ERR_INVALID_INPUT, "unknown precision");
+    const DType dt = o.precision == PPOCR_PRECISION_BF16 ? DT_BF16 : DT_F32;
+    SafeTensors st = SafeTensors::load(path);
+    std::unique_ptr<ppocr_model> model(new ppocr_model());
+    model->gpu = gpu;
+    model->opts = o;
+    model->m = detector ? build_detector(st, size, shape, dt, true) : build_recognizer(st, size, shape, dt, true);
+    std::lock_guard<std::mutex> lock(gpu->mu);
+    gpu->bind();
+    const std::vector<uint8_t>& blob = model->m.blob.bytes();
+    if (shared && shared->weights && shared->weights->host == blob) {
+        model->weights = shared->weights;
+    } else {
+        auto w = std::make_shared<DeviceWeights>();
+        w->bytes = blob.size();
+        cuda_check(cudaMalloc(&w->ptr, std::max<size_t>(w->bytes, 256)), "allocate weights");
+        cuda_check(cudaMemcpy(w->ptr, blob.data(), w->bytes, cudaMemcpyHostToDevice), "upload weights");
+        w->host = blob;
+        model->weights = w;
+    }
+    gpu->ensure_arena(model->m.plan.arena_bytes);
+    cuda_check(cudaMalloc(&model->dflags, 2 * sizeof(int)), "allocate flags");
+    cuda_check(cudaMallocHost(&model->hflags, 2 * sizeof(int)), "allocate host flags");
+    return model.release();
+}
+
+}  // namespace
+
+extern "C" {
+
+void ppocr_load_options_default(ppocr_load_options* options) {
+    if (!options) return;
+    std::memset(options, 0, sizeof(*options));
+    options->precision = PPOCR_PRECISION_FP32;
+    options->use_graph = 1;
+}
+
+const char* ppocr_last_error(void) { return g_last_error.c_str(); }
+
+int ppocr_gpu_count(int* count) {
+    return guard([&] {
+        if (!count) fail(PPOCR_ERR_INVALID_INPUT, "count pointer is null");
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+            cudaGetLastError();
+            n = 0;
+        } else {
+            cuda_check(e, "cudaGetDeviceCount");
+        }
+        *count = n;
+    });
+}
+
+int ppocr_gpu_create(int device, ppocr_gpu** out) {
+    return guard([&] {
+        if (!out) fail(PPOCR_ERR_INVALID_INPUT, "output pointer is null");
+        *out = nullptr;
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess || n == 0) {
+            cudaGetLastError();
+            fail(PPOCR_ERR_GPU, "request CUDA device: no CUDA device is available");
+        }
+        if (device < 0 || device >= n) fail(PPOCR_ERR_GPU, "request CUDA device " + std::to_string(device) + ": out of range");
+        std::unique_ptr<ppocr_gpu> g(new ppocr_gpu());
+        g->device = device;
+        g->bind();
+        cudaDeviceProp prop;
+        cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major < 10) fail(PPOCR_ERR_GPU, std::string("device ") + prop.name + " is not sm_100 class; this build targets sm_100a");
+        g->name = prop.name;
+        cuda_check(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "create stream");
+        *out = g.release();
+    });
+}
+
+void ppocr_gpu_destroy(ppocr_gpu* gpu) {
+    if (!gpu) return;
+    cudaSetDevice(gpu->device);
+    if (gpu->stream) cudaStreamSynchronize(gpu->stream);
+    if (gpu->arena) cudaFree(gpu->arena);
+    if (gpu->stream) cudaStreamDestroy(gpu->stream);
+    delete gpu;
+}
+
+int ppocr_gpu_info(const ppocr_gpu* gpu, char* name, size_t capacity) {
+    return guard([&] {
+        if (!gpu || !name || capacity == 0) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        std::strncpy(name, gpu->name.c_str(), capacity - 1);
+        name[capacity - 1] = 0;
+    });
+}
+
+int ppocr_upload_rgb(ppocr_gpu* gpu, uint32_t width, uint32_t height, const uint8_t* pixels, size_t len, ppocr_image** out) {
+    return guard([&] {
+        if (!gpu || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        *out = nullptr;
+        // Gpu::upload_rgb checks (src/gpu/runtime.rs:175-197)
+        if (width == 0 || height == 0) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: source image dimensions must be non-zero");
+        const size_t expected = (size_t)width * height * 3;
+        if (len != expected || !pixels)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: source image has " + std::to_string(len) + " RGB bytes; expected " +
+                                              std::to_string(expected) + " for " + std::to_string(width) + "x" + std::to_string(height));
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        std::unique_ptr<ppocr_image> img(new ppocr_image());
+        img->gpu = gpu;
+        img->width = width;
+        img->height = height;
+        cuda_check(cudaMalloc(&img->rgb, expected), "allocate source image");
+        cuda_check(cudaMemcpy(img->rgb, pixels, expected, cudaMemcpyHostToDevice), "upload source image");
+        *out = img.release();
+    });
+}
+
+void ppocr_image_destroy(ppocr_image* image) {
+    if (!image) return;
+    if (image->rgb) {
+        cudaSetDevice(image->gpu->device);
+        cudaFree(image->rgb);
+    }
+    delete image;
+}
+
+int ppocr_detector_load(ppocr_gpu* gpu, const char* path, int size, const size_t input_shape[4], ppocr_model** out) {
+    return ppocr_detector_load_ex(gpu, path, size, input_shape, nullptr, out);
+}
+
+int ppocr_detector_load_ex(ppocr_gpu* gpu, const char* path, int size, const size_t input_shape[4],
+                           const ppocr_load_options* options, ppocr_model** out) {
+    return guard([&] {
+        if (!out) fail(PPOCR_ERR_INVALID_INPUT, "output pointer is null");
+        *out = nullptr;
+        *out = load_model(gpu, path, size, input_shape, options, nullptr, true);
+    });
+}
+
+int ppocr_recognizer_load(ppocr_gpu* gpu, const char* path, int size, const size_t input_shape[4], ppocr_model** out) {
+    return ppocr_recognizer_load_ex(gpu, path, size, input_shape, nullptr, nullptr, out);
+}
+
+int ppocr_recognizer_load_ex(ppocr_gpu* gpu, const char* path, int size, const size_t input_shape[4],
+                             const ppocr_load_options* options, const ppocr_model* shared_weights_from, ppocr_model** out) {
+    return guard([&] {
+        if (!out) fail(PPOCR_ERR_INVALID_INPUT, "output pointer is null");
+        *out = nullptr;
+        if (shared_weights_from && shared_weights_from->m.kind != Kind::Recognizer)
+            fail(PPOCR_ERR_INVALID_INPUT, "shared weights must come from a recognizer");
+        *out = load_model(gpu, path, size, input_shape, options, shared_weights_from, false);
+    });
+}
+
+void ppocr_model_destroy(ppocr_model* model) {
+    if (!model) return;
+    {
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        cudaStreamSynchronize(model->gpu->stream);
+    }
+    delete model;
+}
+
+int ppocr_inspect_model(const char* path, int kind, int size, const size_t input_shape[4], int precision, size_t* ops,
+                        size_t* arena_bytes, size_t* weight_bytes, size_t output_shape[4]) {
+    return guard([&] {
+        if (!path || !input_shape) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (kind != 0 && kind != 1) fail(PPOCR_ERR_INVALID_INPUT, "kind must be 0 (detector) or 1 (recognizer)");
+        if (precision != PPOCR_PRECISION_FP32 && precision != PPOCR_PRECISION_BF16) fail(PPOCR_ERR_INVALID_INPUT, "unknown precision");
+        const DType dt = precision == PPOCR_PRECISION_BF16 ? DT_BF16 : DT_F32;
+        SafeTensors st = SafeTensors::load(path);
+        BuiltModel m = kind == 0 ? build_detector(st, size, input_shape, dt, true) : build_recognizer(st, size, input_shape, dt, true);
+        if (ops) *ops = m.plan.ops.size();
+        if (arena_bytes) *arena_bytes = m.plan.arena_bytes;
+        if (weight_bytes) *weight_bytes = m.blob.bytes().size();
+        if (output_shape)
+            for (size_t i = 0; i < 4; ++i) output_shape[i] = i < m.output_shape.size() ? m.output_shape[i] : 0;
+    });
+}
+
+int ppocr_model_output_shape(const ppocr_model* model, size_t shape[4], size_t* rank, size_t* elements) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        const auto& s = model->m.output_shape;
+        if (shape)
+            for (size_t i = 0; i < 4; ++i) shape[i] = i < s.size() ? s[i] : 0;
+        if (rank) *rank = s.size();
+        if (elements) *elements = model->m.output_elements;
+    });
+}
+
+int ppocr_model_input_shape(const ppocr_model* model, size_t shape[4]) {
+    return guard([&] {
+        if (!model || !shape) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        shape[0] = model->m.n; shape[1] = 3; shape[2] = model->m.h; shape[3] = model->m.w;
+    });
+}
+
+int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len, float* output, size_t output_capacity) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (!output || output_capacity < model->m.output_elements)
+            fail(PPOCR_ERR_INVALID_INPUT, "output buffer holds " + std::to_string(output_capacity) + " values; " +
+                                              std::to_string(model->m.output_elements) + " required");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        upload_and_run(model, input, input_len);
+        download(model, model->output_tid(), output, model->m.output_elements * 4);
+        finish(model, model->output_tid(), model->m.output_elements);
+    });
+}
+
+int ppocr_model_forward_image(ppocr_model* model, const ppocr_image* image, const float corners[8], size_t content_width,
+                              float* output, size_t output_capacity) {
+    return guard([&] {
+        if (!model || !image || !corners) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (image->gpu != model->gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        if (model->m.n != 1) fail(PPOCR_ERR_INVALID_INPUT, "image forward requires batch 1");
+        if (!output || output_capacity < model->m.output_elements) fail(PPOCR_ERR_INVALID_INPUT, "output buffer is too small");
+        for (int i = 0; i < 8; ++i)
+            if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
+        const bool det = model->m.kind == Kind::Detector;
+        const size_t cw = det ? (size_t)model->m.w : content_width;
+        if (cw == 0 || cw > (size_t)model->m.w) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: content width outside 1..=input width");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        PreprocessParams p = make_preprocess(image, corners, cw, (size_t)model->m.h, (size_t)model->m.w, det);
+        p.out = static_cast<float*>(model->tensor(model->m.input));
+        cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), model->gpu->stream), "reset flags");
+        cuda_check(launch_preprocess(p, model->gpu->stream), "launch preprocess");
+        model->run(model->gpu->stream);
+        download(model, model->output_tid(), output, model->m.output_elements * 4);
+        finish(model, model->output_tid(), model->m.output_elements);
+    });
+}
+
+int ppocr_model_benchmark(ppocr_model* model, const float* input, size_t input_len, size_t warmup, size_t runs,
+                          double* samples_ms) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (runs > 0 && !samples_ms) fail(PPOCR_ERR_INVALID_INPUT, "samples pointer is null");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        upload_and_run(model, input, input_len);   // upload once (src/gpu/runtime.rs:1814)
+        finish(model, -1, 0);
+        cudaStream_t s = model->gpu->stream;
+        for (size_t i = 0; i < warmup; ++i) model->run(s);
+        wait_stream(s, 0);
+        cudaEvent_t a, b;
+        cuda_check(cudaEventCreate(&a), "event");
+        cuda_check(cudaEventCreate(&b), "event");
+        for (size_t i = 0; i < runs; ++i) {
+            cuda_check(cudaEventRecord(a, s), "record");
+            model->run(s);
+            cuda_check(cudaEventRecord(b, s), "record");
+            wait_stream(s, 0);
+            float ms = 0.f;
+            cuda_check(cudaEventElapsedTime(&ms, a, b), "elapsed");
+            samples_ms[i] = ms;
+        }
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+    });
+}
+
+int ppocr_model_forward_device(ppocr_model* model, const float* device_input, float* device_output, void* stream) {
+    return guard([&] {
+        if (!model || !device_input || !device_output) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : model->gpu->stream;
+        cuda_check(cudaMemcpyAsync(model->tensor(model->m.input), device_input, model->input_elements() * 4,
+                                   cudaMemcpyDeviceToDevice, s), "copy input");
+        model->run(s);
+        cuda_check(cudaMemcpyAsync(device_output, model->tensor(model->output_tid()), model->m.output_elements * 4,
+                                   cudaMemcpyDeviceToDevice, s), "copy output");
+    });
+}
+
+int ppocr_model_device_buffers(ppocr_model* model, float** device_input, float** device_output) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        if (device_input) *device_input = static_cast<float*>(model->tensor(model->m.input));
+        if (device_output) *device_output = static_cast<float*>(model->tensor(model->output_tid()));
+    });
+}
+
+int ppocr_model_run(ppocr_model* model, void* stream) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->run(stream ? static_cast<cudaStream_t>(stream) : model->gpu->stream);
+    });
+}
+
+int ppocr_model_synchronize(ppocr_model* model, int timeout_ms) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        model->gpu->bind();
+        wait_stream(model->gpu->stream, timeout_ms);
+    });
+}
+
+int ppocr_recognizer_forward_ctc(ppocr_model* model, const float* input, size_t input_len, int32_t* indices, float* probabilities,
+                                 float* margins) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "CTC decode needs a recognizer");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        upload_and_run(model, input, input_len);
+        const size_t rows = (size_t)model->m.n * model->m.t;
+        if (indices) download(model, model->m.index, indices, rows * 4);
+        if (probabilities) download(model, model->m.max_prob, probabilities, rows * 4);
+        if (margins) download(model, model->m.margin, margins, rows * 4);
+        finish(model, model->m.probs, model->m.output_elements);
+    });
+}
+
+int ppocr_model_op_count(const ppocr_model* model, size_t* count) {
+    return guard([&] {
+        if (!model || !count) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        *count = model->m.plan.ops.size();
+    });
+}
+
+int ppocr_model_op_info(const ppocr_model* model, size_t index, char* name, size_t name_capacity, char* kind,
+                        size_t kind_capacity, double* bytes, double* flops) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (index >= model->m.plan.ops.size()) fail(PPOCR_ERR_INVALID_INPUT, "op index out of range");
+        const OpRec& op = model->m.plan.ops[index];
+        if (name && name_capacity) {
+            std::strncpy(name, op.name.c_str(), name_capacity - 1);
+            name[name_capacity - 1] = 0;
+        }
+        if (kind && kind_capacity) {
+            std::strncpy(kind, op.kind.c_str(), kind_capacity - 1);
+            kind[kind_capacity - 1] = 0;
+        }
+        if (bytes) *bytes = model->m.plan.op_bytes(index);
+        if (flops) *flops = op.flops;
+    });
+}
+
+int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms) {
+    return guard([&] {
+        if (!model || !op_ms) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (runs == 0) fail(PPOCR_ERR_INVALID_INPUT, "runs must be positive");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        const auto& ops = model->m.plan.ops;
+        cudaStream_t s = model->gpu->stream;
+        std::vector<cudaEvent_t> ev(ops.size() + 1);
+        for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
+        std::vector<double> acc(ops.size(), 0.0);
+        const Ctx c = model->ctx();
+        try {
+            for (size_t r = 0; r < runs; ++r) {
+                cuda_check(cudaEventRecord(ev[0], s), "record");
+                for (size_t i = 0; i < ops.size(); ++i) {
+                    cuda_check(ops[i].fn(c, s), ops[i].name.c_str());
+                    cuda_check(cudaEventRecord(ev[i + 1], s), "record");
+                }
+                wait_stream(s, 0);
+                for (size_t i = 0; i < ops.size(); ++i) {
+                    float ms = 0.f;
+                    cuda_check(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "elapsed");
+                    acc[i] += ms;
+                }
+            }
+        } catch (...) {
+            for (auto& e : ev) cudaEventDestroy(e);
+            throw;
+        }
+        for (auto& e : ev) cudaEventDestroy(e);
+        for (size_t i = 0; i < ops.size(); ++i) op_ms[i] = acc[i] / (double)runs;
+    });
+}
+
+int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size_t input_len, float* logits,
+                                    size_t logits_capacity) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "logits output needs a recognizer");
+        if (!logits || logits_capacity < model->m.output_elements) fail(PPOCR_ERR_INVALID_INPUT, "logits buffer is too small");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        upload_and_run(model, input, input_len);
+        download(model, model->m.logits, logits, model->m.output_elements * 4);
+        finish(model, model->m.logits, model->m.output_elements);
+    });
+}
+
+int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
+                     size_t out_w, int kind, float* output) {
+    return guard([&] {
+        if (!gpu || !image || !corners || !output) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (image->gpu != gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        if (kind != 0 && kind != 1) fail(PPOCR_ERR_INVALID_INPUT, "kind must be 0 (detector) or 1 (recognizer)");
+        if (out_h == 0 || out_w == 0 || content_width == 0 || content_width > out_w)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: content width outside 1..=output width");
+        for (int i = 0; i < 8; ++i)
+            if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        PreprocessParams p = make_preprocess(image, corners, content_width, out_h, out_w, kind == 0);
+        const size_t bytes = 3 * out_h * out_w * 4;
+        float* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes), "allocate preprocess output");
+        p.out = d;
+        cudaError_t e = launch_preprocess(p, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(output, d, bytes, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "preprocess");
+    });
+}
+
+int ppocr_detector_forward_mask(ppocr_model* model, const float* input, size_t input_len, float threshold, float* probabilities,
+                                uint8_t* mask) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (model->m.kind != Kind::Detector) fail(PPOCR_ERR_INVALID_INPUT, "mask output needs a detector");
+        if (!(threshold >= 0.f && threshold <= 1.f)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: threshold must be in [0, 1]");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        *model->m.mask_threshold = threshold;
+        upload_and_run(model, input, input_len);
+        if (probabilities) download(model, model->m.prob, probabilities, model->m.output_elements * 4);
+        if (mask) download(model, model->m.mask, mask, model->m.output_elements);
+        finish(model, model->m.prob, model->m.output_elements);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,261 @@
+// Launch interface of the sm_100a kernels.  Plain structs of device pointers
+// and sizes; every launcher enqueues on `stream` and returns the launch error.
+//
+// Tensor layout: NHWC, channels contiguous, `cstride` elements between pixels
+// and `coff` the first channel of the view (concatenation is a channel offset
+// into a wider buffer).  DType selects the storage type of activations.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ppocr {
+
+enum DType : int { DT_F32 = 0, DT_BF16 = 1 };
+
+// Fused activations (src/cpu/kernels/mod.rs:2365-2403).
+enum Act : int {
+    ACT_NONE = 0,
+    ACT_RELU = 1,
+    ACT_SILU = 2,
+    ACT_GELU = 3,      // 0.5 x (1 + erf(x / sqrt 2)), erf by Abramowitz-Stegun 7.1.26
+    ACT_HSWISH = 4,    // x * clamp(x / 6 + 0.5, 0, 1)
+    ACT_SIGMOID = 5,
+};
+
+inline size_t dtype_size(DType t) { return t == DT_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------------------
+// Direct convolution (groups = 1): stems, 3x3 / 2x2 / k x k convs, detector
+// head conv_down.  The input is a virtual concatenation of up to four
+// sources, each read with nearest-neighbour upsampling by `scale` and
+// optionally through a 2x2 stride-1 "same-upper" max pool (the stem's pool
+// branch, src/cpu/ops.rs:1520-1535), so neither the concat nor the upsample
+// nor the pool is materialised.
+// ---------------------------------------------------------------------------
+enum SourceMode : int { SRC_NHWC = 0, SRC_NHWC_MAXPOOL = 1, SRC_NCHW_F32 = 2 };
+
+struct ConvSource {
+    const void* ptr = nullptr;
+    int channels = 0;   // channels this source contributes (multiple of 4 for NHWC)
+    int cstride = 0;    // pixel stride of the source buffer in elements
+    int coff = 0;       // first channel of the view
+    int scale = 1;      // nearest-neighbour upsampling factor
+    int mode = SRC_NHWC;
+};
+
+struct ConvParams {
+    int n = 0, hi = 0, wi = 0, cin = 0;   // logical input (after upsampling)
+    ConvSource src[4];
+    int nsrc = 0;
+    int ho = 0, wo = 0, cout = 0;
+    int kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
+    const float* weight = nullptr;        // [ceil(cout/8)][kh][kw][cin][8]
+    const float* bias = nullptr;          // [cout]
+    int act = 0;
+    const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
+    int res_scale = 1;
+    void* out = nullptr;
+    int out_cstride = 0, out_coff = 0;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Depthwise convolution, any k x k / stride, fused bias + activation +
+// residual (residual added after the activation, same shape as the output).
+// ---------------------------------------------------------------------------
+struct DwParams {
+    int n = 0, hi = 0, wi = 0, c = 0;
+    const void* in = nullptr;
+    int in_cstride = 0, in_coff = 0;
+    int ho = 0, wo = 0;
+    int kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
+    const float* weight = nullptr;   // [kh*kw][c]
+    const float* bias = nullptr;     // [c] or null
+    int act = 0;
+    const void* residual = nullptr;  // [n, ho, wo, c] tight, or null
+    void* out = nullptr;             // [n, ho, wo, c] tight
+    DType dtype = DT_F32;
+};
+cudaError_t launch_dwconv(const DwParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Pointwise GEMM  C[m, n] = act(A[m, k] * W + bias) (+ residual)
+//   A rows are NHWC pixels (or sequence steps); optionally every A element
+//   is multiplied by a per-(image, channel) SE gate first.  The residual may
+//   be read through the same gate (LCNet pair: the residual is the gated
+//   token output) and through nearest upsampling of the pixel grid.
+// ---------------------------------------------------------------------------
+struct GemmParams {
+    int m = 0, n = 0, k = 0;
+    const void* a = nullptr;
+    int lda = 0;
+    const float* gate = nullptr;      // [images][k], A *= gate[m / rows_per_image]
+    int rows_per_image = 1;
+    const float* w = nullptr;         // FP32 path: [k][n_pad4]
+    const void* w_tc = nullptr;       // tensor-core path: BF16 [n_pad][k_pad] K-major
+    int n_pad = 0, k_pad = 0;
+    const float* bias = nullptr;      // [n]
+    int act = 0;
+    const void* residual = nullptr;   // [rows][ldr] added after act
+    int ldr = 0;
+    const float* res_gate = nullptr;  // residual *= res_gate[img][col] (stride n)
+    int res_scale = 1, h = 1, w_px = 1;  // residual via nearest upsample of an h x w grid per image
+    void* c = nullptr;
+    int ldc = 0, coff = 0;
+    DType dtype = DT_F32;             // storage of A, residual and C
+    int c_f32 = 0;                    // 1: C is FP32 regardless of dtype
+};
+cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream);
+
+// Pointwise pair C = W2 * GELU(W1 * A + b1) + b2 (+ A), the hidden 2C tile
+// kept on chip (LCNet channel_conv1 / channel_conv2, src/cpu/backend.rs:443-695).
+struct PairParams {
+    int m = 0, cin = 0, hidden = 0, cout = 0;
+    const void* a = nullptr;
+    const float* gate = nullptr;
+    int rows_per_image = 1;
+    const void* w1_tc = nullptr;      // BF16 [hidden][cin]
+    const void* w2_tc = nullptr;      // BF16 [cout][hidden]
+    const float* b1 = nullptr;
+    const float* b2 = nullptr;
+    int residual = 0;
+    void* c = nullptr;
+    DType dtype = DT_BF16;
+};
+
+// Tensor-core (tcgen05) GEMM availability: BF16 storage, k_pad % 64 == 0, n_pad % 16 == 0.
+bool gemm_tc_supported(const GemmParams& p);
+
+// ---------------------------------------------------------------------------
+// Squeeze-excitation
+// ---------------------------------------------------------------------------
+// pool_sum[img][c] += sum over pixels of x[img, :, :, c]   (pool_sum zeroed first)
+struct PoolParams {
+    int n = 0, hw = 0, c = 0;
+    const void* in = nullptr;
+    int in_cstride = 0;
+    float* sum = nullptr;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream);
+
+// gate[img][c] = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5)
+struct SeMlpParams {
+    int n = 0, c = 0, r = 0, hw = 0;
+    const float* sum = nullptr;
+    const float* w1 = nullptr;  // [r][c]
+    const float* b1 = nullptr;  // [r]
+    const float* w2 = nullptr;  // [c][r]
+    const float* b2 = nullptr;  // [c]
+    float alpha = 1.f / 6.f;
+    float* gate = nullptr;      // [n][c]
+};
+cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream);
+
+// out = x * g (mode 0) or x + x * g (mode 1), then + upsample(addend, add_scale)
+struct GateApplyParams {
+    int n = 0, h = 0, w = 0, c = 0;
+    const void* x = nullptr;
+    const float* gate = nullptr;
+    int mode = 0;
+    const void* addend = nullptr;    // [n, h/add_scale, w/add_scale, c] or null
+    int add_scale = 1;
+    void* out = nullptr;
+    int out_cstride = 0, out_coff = 0;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_gate_apply(const GateApplyParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Detector head tail: ConvT 2x2 s2 (+folded BN) ReLU -> ConvT 2x2 s2 -> sigmoid,
+// one thread per input pixel writing its 4x4 output patch, plus the DB
+// binarisation mask (src/cpu/model.rs:1516-1520, src/ocr.rs:745).
+// ---------------------------------------------------------------------------
+struct HeadParams {
+    int n = 0, h = 0, w = 0, ch = 0;
+    const void* in = nullptr;     // [n, h, w, ch]
+    const float* w_up = nullptr;  // [4 taps][ch in][ch out]
+    const float* b_up = nullptr;  // [ch]
+    const float* w_fin = nullptr; // [4 taps][ch]
+    float b_fin = 0.f;
+    float* prob = nullptr;        // [n, 4h, 4w] or null
+    float* logits = nullptr;      // [n, 4h, 4w] or null
+    uint8_t* mask = nullptr;      // [n, 4h, 4w] or null
+    float threshold = 0.2f;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_det_head(const HeadParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Recognizer ops
+// ---------------------------------------------------------------------------
+// 3x2 stride-(3,2) average pool (src/cpu/ops.rs:1536-1566)
+struct AvgPoolParams {
+    int n = 0, h = 0, w = 0, c = 0;
+    const void* in = nullptr;
+    void* out = nullptr;          // [n, h/3, w/2, c]
+    DType dtype = DT_F32;
+};
+cudaError_t launch_avgpool_3x2(const AvgPoolParams& p, cudaStream_t stream);
+
+// Row LayerNorm, two-pass, eps (src/cpu/kernels/mod.rs:2288-2310); optional
+// residual added after the affine transform.
+struct LayerNormParams {
+    int rows = 0, c = 0;
+    const void* in = nullptr;
+    const float* weight = nullptr;
+    const float* bias = nullptr;
+    float eps = 1e-6f;
+    const void* residual = nullptr;
+    void* out = nullptr;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_layernorm(const LayerNormParams& p, cudaStream_t stream);
+
+// Multi-head self-attention over a [n, t, 3, heads, d] QKV buffer
+// (src/cpu/model.rs:1705-1725); output [n, t, heads * d].
+struct AttentionParams {
+    int n = 0, t = 0, heads = 0, d = 0;
+    const void* qkv = nullptr;
+    void* out = nullptr;
+    float scale = 1.f;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_attention(const AttentionParams& p, cudaStream_t stream);
+
+// Row softmax + greedy-CTC statistics over FP32 logits [rows, classes]:
+// probabilities, arg-max (last index among equal maxima), its probability and
+// the top-2 logit margin.  Any output may be null.
+struct SoftmaxParams {
+    int rows = 0, classes = 0;
+    const float* logits = nullptr;
+    float* prob = nullptr;
+    int32_t* index = nullptr;
+    float* max_prob = nullptr;
+    float* margin = nullptr;
+};
+cudaError_t launch_softmax_ctc(const SoftmaxParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Image preprocessing: quad -> rectangle bilinear resample of packed RGB8,
+// rounded to integers, BGR order, (x * scale + bias) per channel, zero past
+// content_width (src/preprocess/kernels.rs:94-165).  Output NCHW FP32.
+// ---------------------------------------------------------------------------
+struct PreprocessParams {
+    const uint8_t* rgb = nullptr;   // [src_h][src_w][3]
+    int src_w = 0, src_h = 0;
+    float corners[8] = {0};
+    int out_w = 0, out_h = 0, content_w = 0;
+    float scale[3] = {0}, bias[3] = {0};   // per output channel (B, G, R)
+    float* out = nullptr;           // [3][out_h][out_w]
+};
+cudaError_t launch_preprocess(const PreprocessParams& p, cudaStream_t stream);
+
+// Elementwise conversion between storage types / layouts.
+cudaError_t launch_nchw_to_nhwc(const float* in, void* out, int n, int c, int h, int w, DType dt, cudaStream_t stream);
+cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cudaStream_t stream);
+cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream);
+
+}  // namespace ppocr

@@ -1,0 +1,533 @@
+// Squeeze-excitation, detector-head tail, recognizer ops, preprocessing and
+// small conversion kernels.  Reference semantics are cited per kernel.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cfloat>
+
+namespace ppocr {
+namespace {
+
+// ---------------------------------------------------------------------------
+// SE: per-(image, channel) sums over pixels (global_avg_pool2d numerator,
+// src/cpu/model.rs:488).  grid = (chunks, images); each thread owns 4
+// channels of a pixel row slice; partials reduced in shared memory, then one
+// atomicAdd per channel per block.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
+    __shared__ float4 part[256];
+    const int cg = p.c / 4;
+    const int rows = blockDim.x / cg;          // pixel lanes per block
+    const int g = threadIdx.x % cg, r = threadIdx.x / cg;
+    const int img = blockIdx.y;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows) {
+        const T* base = static_cast<const T*>(p.in) + (size_t)img * p.hw * p.in_cstride + g * 4;
+        for (int px = blockIdx.x * rows + r; px < p.hw; px += gridDim.x * rows)
+            acc = f4_add(acc, load4(base + (size_t)px * p.in_cstride));
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (r == 0) {
+        for (int i = 1; i < rows; ++i) acc = f4_add(acc, part[i * cg + g]);
+        float* dst = p.sum + (size_t)img * p.c + g * 4;
+        atomicAdd(dst + 0, acc.x);
+        atomicAdd(dst + 1, acc.y);
+        atomicAdd(dst + 2, acc.z);
+        atomicAdd(dst + 3, acc.w);
+    }
+}
+
+// gate = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5)
+// (SqueezeExcitation src/cpu/model.rs:486-492, VariantSqueezeExcitation 1098-1104)
+__global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
+    extern __shared__ float sm[];
+    float* mean = sm;
+    float* hid = sm + p.c;
+    const int img = blockIdx.x;
+    const float inv = 1.f / (float)p.hw;
+    for (int i = threadIdx.x; i < p.c; i += blockDim.x) mean[i] = p.sum[(size_t)img * p.c + i] * inv;
+    __syncthreads();
+    for (int j = threadIdx.x; j < p.r; j += blockDim.x) {
+        float a = p.b1[j];
+        const float* w = p.w1 + (size_t)j * p.c;
+        for (int i = 0; i < p.c; ++i) a = fmaf(w[i], mean[i], a);
+        hid[j] = fmaxf(a, 0.f);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.c; i += blockDim.x) {
+        float a = p.b2[i];
+        const float* w = p.w2 + (size_t)i * p.r;
+        for (int j = 0; j < p.r; ++j) a = fmaf(w[j], hid[j], a);
+        p.gate[(size_t)img * p.c + i] = fminf(fmaxf(fmaf(a, p.alpha, 0.5f), 0.f), 1.f);
+    }
+}
+
+// out = x*g or x + x*g (residual_mul_in_place, src/cpu/kernels/mod.rs:777-796),
+// then + nearest-upsampled addend (upsample_add_nchw, src/cpu/model.rs:1265-1320).
+template <typename T>
+__global__ void __launch_bounds__(256) gate_apply_kernel(GateApplyParams p) {
+    const int cg = p.c / 4;
+    const long long total = (long long)p.n * p.h * p.w * cg;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(idx % cg) * 4;
+        const long long pix = idx / cg;
+        const int img = (int)(pix / ((long long)p.h * p.w));
+        float4 v = load4(static_cast<const T*>(p.x) + (size_t)pix * p.c + c);
+        if (p.gate) {
+            const float4 g = *reinterpret_cast<const float4*>(p.gate + (size_t)img * p.c + c);
+            const float4 s = f4_mul(v, g);
+            v = p.mode ? f4_add(s, v) : s;
+        }
+        if (p.addend) {
+            const int x = (int)(pix % p.w), y = (int)((pix / p.w) % p.h);
+            const int ah = p.h / p.add_scale, aw = p.w / p.add_scale;
+            const size_t ai = ((size_t)(img * ah + y / p.add_scale) * aw + x / p.add_scale) * p.c + c;
+            v = f4_add(v, load4(static_cast<const T*>(p.addend) + ai));
+        }
+        store4(static_cast<T*>(p.out) + (size_t)pix * p.out_cstride + p.out_coff + c, v);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Detector head tail (DetectorHead::forward after conv_down,
+// src/cpu/model.rs:1516-1520; ConvTranspose 2x2 s2 IOHW, backend.rs:996-1181):
+// each thread takes one conv_down pixel, expands it through both transposed
+// convs to its 4x4 output patch, applies the sigmoid and the DB threshold.
+// ---------------------------------------------------------------------------
+template <typename T, int CH>
+__global__ void __launch_bounds__(128) det_head_kernel(HeadParams p) {
+    extern __shared__ float hsm[];
+    float* wup = hsm;                  // [4][CH][CH]
+    float* bup = wup + 4 * CH * CH;    // [CH]
+    float* wfin = bup + CH;            // [4][CH]
+    for (int i = threadIdx.x; i < 4 * CH * CH; i += blockDim.x) wup[i] = p.w_up[i];
+    for (int i = threadIdx.x; i < CH; i += blockDim.x) bup[i] = p.b_up[i];
+    for (int i = threadIdx.x; i < 4 * CH; i += blockDim.x) wfin[i] = p.w_fin[i];
+    __syncthreads();
+    const long long total = (long long)p.n * p.h * p.w;
+    const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (pix >= total) return;
+    const int x = (int)(pix % p.w), y = (int)((pix / p.w) % p.h);
+    const int img = (int)(pix / ((long long)p.w * p.h));
+    float in[CH];
+    const T* src = static_cast<const T*>(p.in) + (size_t)pix * CH;
+#pragma unroll
+    for (int c = 0; c < CH; c += 4) {
+        const float4 v = load4(src + c);
+        in[c] = v.x; in[c + 1] = v.y; in[c + 2] = v.z; in[c + 3] = v.w;
+    }
+    const int W = p.w * 4;
+    // First transposed conv tap (a, b) puts hidden pixel (2y + a, 2x + b);
+    // the second tap (c, d) of that pixel lands at (4y + 2a + c, 4x + 2b + d).
+    for (int a = 0; a < 2; ++a) {
+        for (int b = 0; b < 2; ++b) {
+            float h[CH];
+#pragma unroll
+            for (int co = 0; co < CH; ++co) h[co] = bup[co];
+            const float* w0 = wup + (a * 2 + b) * CH * CH;
+#pragma unroll 2
+            for (int ci = 0; ci < CH; ++ci) {
+                const float v = in[ci];
+#pragma unroll
+                for (int co = 0; co < CH; ++co) h[co] = fmaf(v, w0[ci * CH + co], h[co]);
+            }
+#pragma unroll
+            for (int co = 0; co < CH; ++co) h[co] = fmaxf(h[co], 0.f);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float l[2];
+#pragma unroll
+                for (int d = 0; d < 2; ++d) {
+                    const float* wf = wfin + (c * 2 + d) * CH;
+                    float s = p.b_fin;
+#pragma unroll
+                    for (int co = 0; co < CH; ++co) s = fmaf(h[co], wf[co], s);
+                    l[d] = s;
+                }
+                const size_t o = ((size_t)img * p.h * 4 + (size_t)(4 * y + 2 * a + c)) * W + 4 * x + 2 * b;
+                if (p.logits) *reinterpret_cast<float2*>(p.logits + o) = make_float2(l[0], l[1]);
+                const float2 pr = make_float2(1.f / (1.f + expf(-l[0])), 1.f / (1.f + expf(-l[1])));
+                if (p.prob) *reinterpret_cast<float2*>(p.prob + o) = pr;
+                if (p.mask) {
+                    uchar2 m;
+                    m.x = pr.x >= p.threshold;
+                    m.y = pr.y >= p.threshold;
+                    *reinterpret_cast<uchar2*>(p.mask + o) = m;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Recognizer ops
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void avgpool_3x2_kernel(AvgPoolParams p) {
+    const int oh = p.h / 3, ow = p.w / 2, cg = p.c / 4;
+    const long long total = (long long)p.n * oh * ow * cg;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(idx % cg) * 4;
+        const long long pix = idx / cg;
+        const int ox = (int)(pix % ow), oy = (int)((pix / ow) % oh);
+        const int img = (int)(pix / ((long long)ow * oh));
+        const T* in = static_cast<const T*>(p.in);
+        auto at = [&](int yy, int xx) { return load4(in + ((size_t)(img * p.h + yy) * p.w + xx) * p.c + c); };
+        // (row0[x] + row0[x+1] + row1[x] + row1[x+1] + row2[x] + row2[x+1]) / 6, left to right.
+        float4 s = at(oy * 3, ox * 2);
+        s = f4_add(s, at(oy * 3, ox * 2 + 1));
+        s = f4_add(s, at(oy * 3 + 1, ox * 2));
+        s = f4_add(s, at(oy * 3 + 1, ox * 2 + 1));
+        s = f4_add(s, at(oy * 3 + 2, ox * 2));
+        s = f4_add(s, at(oy * 3 + 2, ox * 2 + 1));
+        s = make_float4(s.x / 6.f, s.y / 6.f, s.z / 6.f, s.w / 6.f);
+        store4(static_cast<T*>(p.out) + (size_t)pix * p.c + c, s);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_kernel(LayerNormParams p) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= p.rows) return;
+    const T* in = static_cast<const T*>(p.in) + (size_t)warp * p.c;
+    float s = 0.f;
+    for (int i = lane; i < p.c; i += 32) s += to_f(in[i]);
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)p.c;
+    float v = 0.f;
+    for (int i = lane; i < p.c; i += 32) { const float d = to_f(in[i]) - mean; v = fmaf(d, d, v); }
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float inv = 1.f / sqrtf(v / (float)p.c + p.eps);
+    T* out = static_cast<T*>(p.out) + (size_t)warp * p.c;
+    const T* res = p.residual ? static_cast<const T*>(p.residual) + (size_t)warp * p.c : nullptr;
+    for (int i = lane; i < p.c; i += 32) {
+        float y = fmaf(to_f(in[i]) - mean, inv * p.weight[i], p.bias[i]);
+        if (res) y += to_f(res[i]);
+        out[i] = from_f<T>(y);
+    }
+}
+
+// One block per (image, head).  K and V of the head in shared memory; each
+// warp takes query rows, holds its score row in shared memory, softmaxes it
+// (src/cpu/kernels/mod.rs:2218-2243) and accumulates P V with lanes over d.
+template <typename T>
+__global__ void __launch_bounds__(128) attention_kernel(AttentionParams p) {
+    extern __shared__ float sm[];
+    const int img = blockIdx.x / p.heads, head = blockIdx.x % p.heads;
+    const int hidden = p.heads * p.d;
+    const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* ks = sm;
+    float* vs = ks + p.t * p.d;
+    float* qs = vs + p.t * p.d;              // [warps][d]
+    float* sc = qs + warps * p.d;            // [warps][t]
+    const T* base = static_cast<const T*>(p.qkv) + (size_t)img * p.t * 3 * hidden;
+    for (int i = threadIdx.x; i < p.t * p.d; i += blockDim.x) {
+        const int r = i / p.d, j = i % p.d;
+        ks[i] = to_f(base[(size_t)r * 3 * hidden + hidden + head * p.d + j]);
+        vs[i] = to_f(base[(size_t)r * 3 * hidden + 2 * hidden + head * p.d + j]);
+    }
+    __syncthreads();
+    float* q = qs + warp * p.d;
+    float* s = sc + warp * p.t;
+    for (int row = warp; row < p.t; row += warps) {
+        for (int j = lane; j < p.d; j += 32) q[j] = to_f(base[(size_t)row * 3 * hidden + head * p.d + j]);
+        __syncwarp();
+        float mx = -FLT_MAX;
+        for (int key = lane; key < p.t; key += 32) {
+            float a = 0.f;
+            for (int j = 0; j < p.d; ++j) a = fmaf(q[j], ks[key * p.d + j], a);
+            a = a * p.scale;
+            s[key] = a;
+            mx = fmaxf(mx, a);
+        }
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+        for (int key = lane; key < p.t; key += 32) {
+            const float e = expf(s[key] - mx);
+            s[key] = e;
+            sum += e;
+        }
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float rcp = 1.f / sum;
+        __syncwarp();
+        T* out = static_cast<T*>(p.out) + ((size_t)img * p.t + row) * hidden + head * p.d;
+        for (int j = lane; j < p.d; j += 32) {
+            float a = 0.f;
+            for (int key = 0; key < p.t; ++key) a = fmaf(s[key] * rcp, vs[key * p.d + j], a);
+            out[j] = from_f<T>(a);
+        }
+        __syncwarp();
+    }
+}
+
+// Row softmax + greedy-CTC statistics.  Pass 1: max logit, runner-up logit;
+// pass 2: sum of exp; pass 3: probabilities and their arg-max with the last
+// index winning ties (Rust Iterator::max_by, src/ocr.rs:1171-1177).
+struct ArgMax {
+    float v;
+    int i;
+};
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
+    return (b.v > a.v || (b.v == a.v && b.i > a.i)) ? b : a;
+}
+
+__global__ void __launch_bounds__(256) softmax_ctc_kernel(SoftmaxParams p) {
+    __shared__ float r1[8], r2[8];
+    __shared__ ArgMax ra[8];
+    const int row = blockIdx.x;
+    const float* x = p.logits + (size_t)row * p.classes;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float m1 = -FLT_MAX, m2 = -FLT_MAX;   // top-2 logits
+    for (int i = threadIdx.x; i < p.classes; i += blockDim.x) {
+        const float v = x[i];
+        if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float a1 = __shfl_xor_sync(0xffffffffu, m1, o), a2 = __shfl_xor_sync(0xffffffffu, m2, o);
+        const float n1 = fmaxf(m1, a1);
+        const float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
+        m1 = n1; m2 = n2;
+    }
+    if (lane == 0) { r1[warp] = m1; r2[warp] = m2; }
+    __syncthreads();
+    m1 = r1[0]; m2 = r2[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+        const float a1 = r1[w], a2 = r2[w];
+        const float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
+        m1 = fmaxf(m1, a1); m2 = n2;
+    }
+    __syncthreads();
+    float sum = 0.f;
+    for (int i = threadIdx.x; i < p.classes; i += blockDim.x) sum += expf(x[i] - m1);
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) r1[warp] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) sum += r1[w];
+    const float rcp = 1.f / sum;
+    ArgMax best{-FLT_MAX, -1};
+    float* prob = p.prob ? p.prob + (size_t)row * p.classes : nullptr;
+    for (int i = threadIdx.x; i < p.classes; i += blockDim.x) {
+        const float pr = expf(x[i] - m1) * rcp;
+        if (prob) prob[i] = pr;
+        best = better(best, ArgMax{pr, i});
+    }
+    for (int o = 16; o; o >>= 1) {
+        ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+        best = better(best, other);
+    }
+    if (lane == 0) ra[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ArgMax b = ra[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) b = better(b, ra[w]);
+        if (p.index) p.index[row] = b.i;
+        if (p.max_prob) p.max_prob[row] = b.v;
+        if (p.margin) p.margin[row] = m1 - m2;
+    }
+}
+
+// Quad -> rectangle bilinear resample with integer rounding, BGR order and
+// per-channel affine normalisation, zero past content_w
+// (src/preprocess/kernels.rs:94-165, the scalar row kernel).  Explicit
+// round-to-nearest intrinsics keep every product and sum separately rounded,
+// as the reference's scalar code computes them (no FMA contraction).
+__global__ void __launch_bounds__(256) preprocess_kernel(PreprocessParams p) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y;
+    if (x >= p.out_w || y >= p.out_h) return;
+    const size_t plane = (size_t)p.out_h * p.out_w;
+    const size_t o = (size_t)y * p.out_w + x;
+    if (x >= p.content_w) {
+        p.out[o] = 0.f;
+        p.out[plane + o] = 0.f;
+        p.out[2 * plane + o] = 0.f;
+        return;
+    }
+    const float v = __fdiv_rn(__fadd_rn((float)y, 0.5f), (float)p.out_h);
+    const float omv = __fsub_rn(1.f, v);
+    const float u = __fdiv_rn(__fadd_rn((float)x, 0.5f), (float)p.content_w);
+    const float omu = __fsub_rn(1.f, u);
+    const float* c = p.corners;
+    float sx = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(c[0], omu), __fmul_rn(c[2], u)), omv),
+                         __fmul_rn(__fadd_rn(__fmul_rn(c[6], omu), __fmul_rn(c[4], u)), v));
+    float sy = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(c[1], omu), __fmul_rn(c[3], u)), omv),
+                         __fmul_rn(__fadd_rn(__fmul_rn(c[7], omu), __fmul_rn(c[5], u)), v));
+    sx = fminf(fmaxf(__fsub_rn(sx, 0.5f), 0.f), (float)(p.src_w - 1));
+    sy = fminf(fmaxf(__fsub_rn(sy, 0.5f), 0.f), (float)(p.src_h - 1));
+    const int x0 = (int)floorf(sx), y0 = (int)floorf(sy);
+    const int x1 = min(x0 + 1, p.src_w - 1), y1 = min(y0 + 1, p.src_h - 1);
+    const float tx = __fsub_rn(sx, (float)x0), ty = __fsub_rn(sy, (float)y0);
+    const float omtx = __fsub_rn(1.f, tx), omty = __fsub_rn(1.f, ty);
+    const uint8_t* r0 = p.rgb + ((size_t)y0 * p.src_w) * 3;
+    const uint8_t* r1 = p.rgb + ((size_t)y1 * p.src_w) * 3;
+    float rgb[3];
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+        const float tl = r0[x0 * 3 + ch], tr = r0[x1 * 3 + ch];
+        const float bl = r1[x0 * 3 + ch], br = r1[x1 * 3 + ch];
+        const float top = __fadd_rn(__fmul_rn(tl, omtx), __fmul_rn(tr, tx));
+        const float bottom = __fadd_rn(__fmul_rn(bl, omtx), __fmul_rn(br, tx));
+        const float val = __fadd_rn(__fmul_rn(top, omty), __fmul_rn(bottom, ty));
+        rgb[ch] = fminf(fmaxf(roundf(val), 0.f), 255.f);
+    }
+    // plane 0 = blue (rgb[2]), 1 = green, 2 = red
+    p.out[o] = __fadd_rn(__fmul_rn(rgb[2], p.scale[0]), p.bias[0]);
+    p.out[plane + o] = __fadd_rn(__fmul_rn(rgb[1], p.scale[1]), p.bias[1]);
+    p.out[2 * plane + o] = __fadd_rn(__fmul_rn(rgb[0], p.scale[2]), p.bias[2]);
+}
+
+template <typename T>
+__global__ void nchw_to_nhwc_kernel(const float* in, T* out, int n, int c, int h, int w) {
+    const long long total = (long long)n * c * h * w;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int ch = (int)(i % c);
+        const long long pix = i / c;
+        const int x = (int)(pix % w), y = (int)((pix / w) % h), img = (int)(pix / ((long long)w * h));
+        out[i] = from_f<T>(in[(((size_t)img * c + ch) * h + y) * w + x]);
+    }
+}
+
+template <typename T>
+__global__ void to_f32_kernel(const T* in, float* out, size_t count) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = to_f(in[i]);
+}
+
+__global__ void check_finite_kernel(const float* in, size_t count, int* flag) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+        if (!isfinite(in[i])) { *flag = 1; return; }
+}
+
+inline unsigned grid_for(long long total, int threads) {
+    long long b = (total + threads - 1) / threads;
+    if (b > 148LL * 32) b = 148LL * 32;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream) {
+    if (p.c % 4 || p.c / 4 > 256) return cudaErrorInvalidValue;
+    const int rows = 256 / (p.c / 4);
+    int chunks = (p.hw + rows * 8 - 1) / (rows * 8);
+    if (chunks > 64) chunks = 64;
+    if (chunks < 1) chunks = 1;
+    dim3 grid(chunks, p.n);
+    if (p.dtype == DT_F32) channel_sum_kernel<float><<<grid, 256, 0, stream>>>(p);
+    else channel_sum_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
+    const size_t smem = (size_t)(p.c + p.r) * sizeof(float);
+    se_mlp_kernel<<<p.n, 256, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gate_apply(const GateApplyParams& p, cudaStream_t stream) {
+    if (p.c % 4 || p.out_cstride % 4 || p.out_coff % 4) return cudaErrorInvalidValue;
+    const unsigned g = grid_for((long long)p.n * p.h * p.w * (p.c / 4), 256);
+    if (p.dtype == DT_F32) gate_apply_kernel<float><<<g, 256, 0, stream>>>(p);
+    else gate_apply_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_head_t(const HeadParams& p, cudaStream_t stream) {
+    const long long total = (long long)p.n * p.h * p.w;
+    const unsigned g = (unsigned)((total + 127) / 128);
+    const size_t smem = (size_t)(4 * p.ch * p.ch + p.ch + 4 * p.ch) * sizeof(float);
+    switch (p.ch) {
+        case 16: det_head_kernel<T, 16><<<g, 128, smem, stream>>>(p); break;
+        case 24: det_head_kernel<T, 24><<<g, 128, smem, stream>>>(p); break;
+        case 64: {
+            static bool configured = false;
+            if (!configured) {
+                cudaError_t e = cudaFuncSetAttribute(det_head_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                if (e != cudaSuccess) return e;
+                configured = true;
+            }
+            det_head_kernel<T, 64><<<g, 128, smem, stream>>>(p);
+            break;
+        }
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_det_head(const HeadParams& p, cudaStream_t stream) {
+    return p.dtype == DT_F32 ? launch_head_t<float>(p, stream) : launch_head_t<__nv_bfloat16>(p, stream);
+}
+
+cudaError_t launch_avgpool_3x2(const AvgPoolParams& p, cudaStream_t stream) {
+    if (p.c % 4) return cudaErrorInvalidValue;
+    const unsigned g = grid_for((long long)p.n * (p.h / 3) * (p.w / 2) * (p.c / 4), 256);
+    if (p.dtype == DT_F32) avgpool_3x2_kernel<float><<<g, 256, 0, stream>>>(p);
+    else avgpool_3x2_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(const LayerNormParams& p, cudaStream_t stream) {
+    const unsigned g = (unsigned)(((long long)p.rows * 32 + 255) / 256);
+    if (p.dtype == DT_F32) layernorm_kernel<float><<<g, 256, 0, stream>>>(p);
+    else layernorm_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttentionParams& p, cudaStream_t stream) {
+    const int warps = 4;
+    const size_t smem = (size_t)(2 * p.t * p.d + warps * p.d + warps * p.t) * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static bool configured[2] = {false, false};
+    const int key = p.dtype == DT_F32 ? 0 : 1;
+    if (!configured[key]) {
+        cudaError_t e = key == 0
+            ? cudaFuncSetAttribute(attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)
+            : cudaFuncSetAttribute(attention_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[key] = true;
+    }
+    if (p.dtype == DT_F32) attention_kernel<float><<<p.n * p.heads, warps * 32, smem, stream>>>(p);
+    else attention_kernel<__nv_bfloat16><<<p.n * p.heads, warps * 32, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_softmax_ctc(const SoftmaxParams& p, cudaStream_t stream) {
+    softmax_ctc_kernel<<<p.rows, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_preprocess(const PreprocessParams& p, cudaStream_t stream) {
+    dim3 grid((p.out_w + 255) / 256, p.out_h);
+    preprocess_kernel<<<grid, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_nchw_to_nhwc(const float* in, void* out, int n, int c, int h, int w, DType dt, cudaStream_t stream) {
+    const unsigned g = grid_for((long long)n * c * h * w, 256);
+    if (dt == DT_F32) nchw_to_nhwc_kernel<float><<<g, 256, 0, stream>>>(in, static_cast<float*>(out), n, c, h, w);
+    else nchw_to_nhwc_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(in, static_cast<__nv_bfloat16*>(out), n, c, h, w);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cudaStream_t stream) {
+    const unsigned g = grid_for((long long)count, 256);
+    if (dt == DT_F32) to_f32_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(in), out, count);
+    else to_f32_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(in), out, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream) {
+    const unsigned g = grid_for((long long)count, 256);
+    check_finite_kernel<<<g, 256, 0, stream>>>(in, count, flag);
+    return cudaGetLastError();
+}
+
+}  // namespace ppocr

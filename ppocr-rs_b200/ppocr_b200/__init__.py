@@ -1,0 +1,432 @@
+"""Python face of the B200 PP-OCRv6 backend, shaped like ``ppocr_rs::gpu``.
+
+ppocr-rs exposes ``Gpu``, ``GpuImage``, ``ImagePreprocess``, ``Detector``,
+``Recognizer``, ``ModelOutput`` and ``ModelSize`` (src/gpu/mod.rs:1-13).  This
+module mirrors them over the C ABI in include/ppocr_b200.h (ctypes, no
+framework types): same constructors, argument meaning and error variants.
+Every call goes to the compiled library; there is no fallback path, and a
+missing library raises ``ImportError`` on first use.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+__all__ = [
+    "Error", "ReadFile", "Safetensors", "TensorNotFound", "UnsupportedDtype", "ShapeMismatch",
+    "TensorSizeOverflow", "TensorByteLength", "InvalidTensorRange", "InvalidModel", "InvalidInput", "GpuError",
+    "ModelSize", "Precision", "Gpu", "GpuImage", "ImagePreprocess", "ModelOutput", "Detector", "Recognizer",
+    "library", "library_path", "gpu_count", "inspect_model",
+]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def library_path() -> str:
+    return os.environ.get("PPOCR_B200_LIB", os.path.join(_HERE, "libppocr_b200.so"))
+
+
+# ---------------------------------------------------------------------------
+# Errors: one class per gpu::Error variant (src/gpu/error.rs:8-45)
+# ---------------------------------------------------------------------------
+
+
+class Error(RuntimeError):
+    code = -1
+
+
+class ReadFile(Error):
+    code = 1
+
+
+class Safetensors(Error):
+    code = 2
+
+
+class TensorNotFound(Error):
+    code = 3
+
+
+class UnsupportedDtype(Error):
+    code = 4
+
+
+class ShapeMismatch(Error):
+    code = 5
+
+
+class TensorSizeOverflow(Error):
+    code = 6
+
+
+class TensorByteLength(Error):
+    code = 7
+
+
+class InvalidTensorRange(Error):
+    code = 8
+
+
+class InvalidModel(Error):
+    code = 9
+
+
+class InvalidInput(Error):
+    code = 10
+
+
+class GpuError(Error):
+    code = 11
+
+
+_ERRORS = {cls.code: cls for cls in (ReadFile, Safetensors, TensorNotFound, UnsupportedDtype, ShapeMismatch,
+                                      TensorSizeOverflow, TensorByteLength, InvalidTensorRange, InvalidModel,
+                                      InvalidInput, GpuError)}
+
+
+class ModelSize:
+    """ModelSize (src/models.rs:62-69)."""
+    MEDIUM = 0
+    SMALL = 1
+    TINY = 2
+
+    @staticmethod
+    def parse(value) -> int:
+        if isinstance(value, int):
+            return value
+        return {"medium": 0, "small": 1, "tiny": 2}[str(value).lower()]
+
+
+class Precision:
+    FP32 = 0
+    BF16 = 1
+
+    @staticmethod
+    def parse(value) -> int:
+        if isinstance(value, int):
+            return value
+        return {"fp32": 0, "bf16": 1}[str(value).lower()]
+
+
+class _LoadOptions(C.Structure):
+    _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("reserved", C.c_int * 6)]
+
+
+_SIZE4 = C.c_size_t * 4
+_lib = None
+
+
+def library() -> C.CDLL:
+    """The loaded C-ABI library (loaded once; raises ImportError if it is not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not os.path.exists(path):
+        raise ImportError(f"ppocr_b200 native library not found at {path}; build it with `make -C ppocr-rs_b200`")
+    lib = C.CDLL(path)
+    P, I, S = C.c_void_p, C.c_int, C.c_size_t
+    FP = C.POINTER(C.c_float)
+    sig = {
+        "ppocr_last_error": (C.c_char_p, []),
+        "ppocr_load_options_default": (None, [C.POINTER(_LoadOptions)]),
+        "ppocr_gpu_count": (I, [C.POINTER(C.c_int)]),
+        "ppocr_gpu_create": (I, [I, C.POINTER(P)]),
+        "ppocr_gpu_destroy": (None, [P]),
+        "ppocr_gpu_info": (I, [P, C.c_char_p, S]),
+        "ppocr_upload_rgb": (I, [P, C.c_uint32, C.c_uint32, C.POINTER(C.c_uint8), S, C.POINTER(P)]),
+        "ppocr_image_destroy": (None, [P]),
+        "ppocr_detector_load": (I, [P, C.c_char_p, I, _SIZE4, C.POINTER(P)]),
+        "ppocr_detector_load_ex": (I, [P, C.c_char_p, I, _SIZE4, C.POINTER(_LoadOptions), C.POINTER(P)]),
+        "ppocr_recognizer_load": (I, [P, C.c_char_p, I, _SIZE4, C.POINTER(P)]),
+        "ppocr_recognizer_load_ex": (I, [P, C.c_char_p, I, _SIZE4, C.POINTER(_LoadOptions), P, C.POINTER(P)]),
+        "ppocr_model_destroy": (None, [P]),
+        "ppocr_inspect_model": (I, [C.c_char_p, I, I, _SIZE4, I, C.POINTER(S), C.POINTER(S), C.POINTER(S), _SIZE4]),
+        "ppocr_model_output_shape": (I, [P, _SIZE4, C.POINTER(S), C.POINTER(S)]),
+        "ppocr_model_input_shape": (I, [P, _SIZE4]),
+        "ppocr_model_forward": (I, [P, FP, S, FP, S]),
+        "ppocr_model_forward_image": (I, [P, P, FP, S, FP, S]),
+        "ppocr_model_benchmark": (I, [P, FP, S, S, S, C.POINTER(C.c_double)]),
+        "ppocr_model_forward_device": (I, [P, P, P, P]),
+        "ppocr_model_device_buffers": (I, [P, C.POINTER(P), C.POINTER(P)]),
+        "ppocr_model_run": (I, [P, P]),
+        "ppocr_model_synchronize": (I, [P, I]),
+        "ppocr_recognizer_forward_ctc": (I, [P, FP, S, C.POINTER(C.c_int32), FP, FP]),
+        "ppocr_detector_forward_mask": (I, [P, FP, S, C.c_float, FP, C.POINTER(C.c_uint8)]),
+        "ppocr_recognizer_forward_logits": (I, [P, FP, S, FP, S]),
+        "ppocr_model_op_count": (I, [P, C.POINTER(S)]),
+        "ppocr_model_op_info": (I, [P, S, C.c_char_p, S, C.c_char_p, S, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+        "ppocr_model_profile": (I, [P, S, C.POINTER(C.c_double)]),
+        "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = library().ppocr_last_error().decode("utf-8", "replace")
+        raise _ERRORS.get(status, Error)(msg)
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def gpu_count() -> int:
+    n = C.c_int(0)
+    _check(library().ppocr_gpu_count(C.byref(n)))
+    return n.value
+
+
+def inspect_model(path: str, kind: str, size, input_shape: Sequence[int], precision="fp32") -> dict:
+    """Device-free load check; returns ops, arena_bytes, weight_bytes, output_shape."""
+    ops, arena, wbytes = C.c_size_t(), C.c_size_t(), C.c_size_t()
+    out = _SIZE4()
+    _check(library().ppocr_inspect_model(str(path).encode(), 0 if kind == "det" else 1, ModelSize.parse(size),
+                                         _SIZE4(*input_shape), Precision.parse(precision), C.byref(ops), C.byref(arena),
+                                         C.byref(wbytes), out))
+    rank = 4 if kind == "det" else 3
+    return {"ops": ops.value, "arena_bytes": arena.value, "weight_bytes": wbytes.value,
+            "output_shape": [int(v) for v in list(out)[:rank]]}
+
+
+# ---------------------------------------------------------------------------
+# Gpu / images (src/gpu/runtime.rs:24-229)
+# ---------------------------------------------------------------------------
+
+
+class Gpu:
+    """Gpu::new(): one CUDA device with its stream set and activation arena."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        _check(library().ppocr_gpu_create(int(device), C.byref(h)))
+        self._h = h
+        self.device = int(device)
+
+    def info(self) -> str:
+        buf = C.create_string_buffer(256)
+        _check(library().ppocr_gpu_info(self._h, buf, 256))
+        return buf.value.decode()
+
+    def upload_rgb(self, width: int, height: int, pixels) -> "GpuImage":
+        arr = np.ascontiguousarray(np.asarray(pixels, dtype=np.uint8).reshape(-1))
+        h = C.c_void_p()
+        _check(library().ppocr_upload_rgb(self._h, int(width), int(height),
+                                          arr.ctypes.data_as(C.POINTER(C.c_uint8)), arr.size, C.byref(h)))
+        return GpuImage(h, self, int(width), int(height))
+
+    def preprocess(self, image: "GpuImage", corners, content_width: int, out_h: int, out_w: int,
+                   kind: str = "det") -> np.ndarray:
+        """Device quad resample + normalisation into NCHW float32 [1, 3, out_h, out_w]."""
+        c = np.asarray(corners, dtype=np.float32).reshape(8)
+        out = np.empty((1, 3, int(out_h), int(out_w)), dtype=np.float32)
+        _check(library().ppocr_preprocess(self._h, image._h, _fptr(c), int(content_width), int(out_h), int(out_w),
+                                          0 if kind == "det" else 1, _fptr(out)))
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            library().ppocr_gpu_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class GpuImage:
+    def __init__(self, handle, gpu: Gpu, width: int, height: int):
+        self._h, self.gpu, self.width, self.height = handle, gpu, width, height
+
+    def __del__(self):
+        try:
+            if self._h:
+                library().ppocr_image_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+@dataclass
+class ImagePreprocess:
+    """ImagePreprocess::{detector, recognizer} (src/gpu/runtime.rs:50-69)."""
+    corners: Sequence[Sequence[float]]
+    content_width: Optional[int] = None
+
+    @classmethod
+    def detector(cls, corners) -> "ImagePreprocess":
+        return cls(corners, None)
+
+    @classmethod
+    def recognizer(cls, corners, content_width: int) -> "ImagePreprocess":
+        return cls(corners, int(content_width))
+
+
+@dataclass
+class ModelOutput:
+    """ModelOutput {shape, values} (src/gpu/model.rs:38-42)."""
+    shape: List[int]
+    values: np.ndarray
+
+
+class _Model:
+    _kind = "det"
+
+    def __init__(self, handle, gpu: Gpu, input_shape, owner_weights=None):
+        self._h = handle
+        self.gpu = gpu
+        self.input_shape = [int(v) for v in input_shape]
+        shape = _SIZE4()
+        rank, elems = C.c_size_t(), C.c_size_t()
+        _check(library().ppocr_model_output_shape(self._h, shape, C.byref(rank), C.byref(elems)))
+        self.output_shape = [int(v) for v in list(shape)[: rank.value]]
+        self.output_elements = elems.value
+        self._owner = owner_weights
+
+    def _input(self, values) -> np.ndarray:
+        return np.ascontiguousarray(np.asarray(values, dtype=np.float32).reshape(-1))
+
+    def forward(self, values) -> ModelOutput:
+        x = self._input(values)
+        out = np.empty(self.output_elements, dtype=np.float32)
+        _check(library().ppocr_model_forward(self._h, _fptr(x), x.size, _fptr(out), out.size))
+        return ModelOutput(list(self.output_shape), out)
+
+    def forward_image(self, image: GpuImage, preprocess: ImagePreprocess) -> ModelOutput:
+        corners = np.asarray(preprocess.corners, dtype=np.float32).reshape(8)
+        out = np.empty(self.output_elements, dtype=np.float32)
+        cw = preprocess.content_width if preprocess.content_width is not None else self.input_shape[3]
+        _check(library().ppocr_model_forward_image(self._h, image._h, _fptr(corners), int(cw), _fptr(out), out.size))
+        return ModelOutput(list(self.output_shape), out)
+
+    def benchmark(self, values, warmup: int, runs: int) -> List[float]:
+        """Device time of each run in seconds (the reference returns Durations)."""
+        x = self._input(values)
+        samples = (C.c_double * max(int(runs), 1))()
+        _check(library().ppocr_model_benchmark(self._h, _fptr(x), x.size, int(warmup), int(runs), samples))
+        return [samples[i] / 1000.0 for i in range(int(runs))]
+
+    # -- device-resident interface ------------------------------------------
+    def device_buffers(self):
+        i, o = C.c_void_p(), C.c_void_p()
+        _check(library().ppocr_model_device_buffers(self._h, C.byref(i), C.byref(o)))
+        return i.value, o.value
+
+    def run(self, stream: int = 0) -> None:
+        _check(library().ppocr_model_run(self._h, C.c_void_p(stream) if stream else None))
+
+    def forward_device(self, device_input: int, device_output: int, stream: int = 0) -> None:
+        _check(library().ppocr_model_forward_device(self._h, C.c_void_p(device_input), C.c_void_p(device_output),
+                                                    C.c_void_p(stream) if stream else None))
+
+    def ops(self) -> List[dict]:
+        """Plan ops: name, kernel family, algorithmic bytes and FLOPs."""
+        n = C.c_size_t()
+        _check(library().ppocr_model_op_count(self._h, C.byref(n)))
+        out = []
+        for i in range(n.value):
+            name, kind = C.create_string_buffer(256), C.create_string_buffer(64)
+            b, f = C.c_double(), C.c_double()
+            _check(library().ppocr_model_op_info(self._h, i, name, 256, kind, 64, C.byref(b), C.byref(f)))
+            out.append({"name": name.value.decode(), "kind": kind.value.decode(), "bytes": b.value, "flops": f.value})
+        return out
+
+    def profile(self, runs: int = 3) -> List[float]:
+        """Mean device milliseconds of every op, each bracketed by CUDA events."""
+        n = C.c_size_t()
+        _check(library().ppocr_model_op_count(self._h, C.byref(n)))
+        ms = (C.c_double * n.value)()
+        _check(library().ppocr_model_profile(self._h, int(runs), ms))
+        return list(ms)
+
+    def synchronize(self, timeout_ms: int = 0) -> None:
+        _check(library().ppocr_model_synchronize(self._h, int(timeout_ms)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            library().ppocr_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _options(precision, use_graph: bool) -> _LoadOptions:
+    o = _LoadOptions()
+    library().ppocr_load_options_default(C.byref(o))
+    o.precision = Precision.parse(precision)
+    o.use_graph = 1 if use_graph else 0
+    return o
+
+
+class Detector(_Model):
+    """gpu::Detector (src/gpu/model.rs:44-149)."""
+
+    @classmethod
+    def load(cls, gpu: Gpu, path: str, size, input_shape: Sequence[int], precision="fp32",
+             use_graph: bool = True) -> "Detector":
+        h = C.c_void_p()
+        o = _options(precision, use_graph)
+        _check(library().ppocr_detector_load_ex(gpu._h, str(path).encode(), ModelSize.parse(size),
+                                                _SIZE4(*input_shape), C.byref(o), C.byref(h)))
+        return cls(h, gpu, input_shape)
+
+    def forward_mask(self, values, threshold: float = 0.2):
+        """Probability map and DB binarisation mask (prob >= threshold), both [n, h, w]."""
+        x = self._input(values)
+        n, _, hh, ww = self.input_shape
+        prob = np.empty((n, hh, ww), dtype=np.float32)
+        mask = np.empty((n, hh, ww), dtype=np.uint8)
+        _check(library().ppocr_detector_forward_mask(self._h, _fptr(x), x.size, float(threshold), _fptr(prob),
+                                                     mask.ctypes.data_as(C.POINTER(C.c_uint8))))
+        return prob, mask
+
+
+class Recognizer(_Model):
+    """gpu::Recognizer (src/gpu/model.rs:150-266)."""
+
+    @classmethod
+    def load(cls, gpu: Gpu, path: str, size, input_shape: Sequence[int], precision="fp32",
+             use_graph: bool = True, shared_weights: Optional["Recognizer"] = None) -> "Recognizer":
+        h = C.c_void_p()
+        o = _options(precision, use_graph)
+        _check(library().ppocr_recognizer_load_ex(gpu._h, str(path).encode(), ModelSize.parse(size),
+                                                  _SIZE4(*input_shape), C.byref(o),
+                                                  shared_weights._h if shared_weights is not None else None,
+                                                  C.byref(h)))
+        return cls(h, gpu, input_shape, shared_weights)
+
+    def forward_logits(self, values) -> np.ndarray:
+        """Pre-softmax classifier logits [n, t, classes]."""
+        x = self._input(values)
+        out = np.empty(self.output_shape, dtype=np.float32)
+        _check(library().ppocr_recognizer_forward_logits(self._h, _fptr(x), x.size, _fptr(out), out.size))
+        return out
+
+    def forward_ctc(self, values):
+        """Greedy-CTC statistics per step: (arg-max index, its probability, top-2 logit margin), each [n, t]."""
+        x = self._input(values)
+        n, t = self.output_shape[0], self.output_shape[1]
+        idx = np.empty((n, t), dtype=np.int32)
+        prob = np.empty((n, t), dtype=np.float32)
+        margin = np.empty((n, t), dtype=np.float32)
+        _check(library().ppocr_recognizer_forward_ctc(self._h, _fptr(x), x.size,
+                                                      idx.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
+                                                      _fptr(margin)))
+        return idx, prob, margin
