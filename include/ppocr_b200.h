@@ -189,6 +189,14 @@ int ppocr_model_op_info(const ppocr_model* model, size_t index, char* name, size
                         char* kind, size_t kind_capacity, double* bytes, double* flops);
 int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms);
 
+/* Diagnostic (new): C[m, n] = act(A[m, k] W[n, k]^T + bias) through the
+ * BF16 GEMM path of this library on `gpu`.  A and W are host F32 arrays
+ * rounded to BF16 on upload; C is returned in F32.  used_tensor_cores is set
+ * to 1 when the tcgen05 kernel ran (k % 8 == 0), wait_error to the kernel's
+ * wait-expiry code (0 = none).  act: 0 none, 1 ReLU, 2 SiLU, 3 GELU. */
+int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
+                        int act, float* c, int* used_tensor_cores, int* wait_error);
+
 /* Recognizer only: the classifier's pre-softmax logits [n, t, classes]
  * (new; the reference fuses the softmax, src/cpu/backend.rs:1288-1290, so it
  * never exposes them). */

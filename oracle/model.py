@@ -202,8 +202,34 @@ def fuse_intraclass(sym_w, sym_b, ver_w, ver_b, hor_w, hor_b):
 # ---------------------------------------------------------------------------
 
 
+_DTYPE = torch.float32
+
+
+class compute_dtype:
+    """Context manager: run the oracle's arithmetic in another dtype.
+
+    ``with compute_dtype(torch.float64): ...`` evaluates the same graph, with
+    the same (F32-folded) parameters, in double precision.  The distance
+    between the float32 and float64 evaluations is the FP32 rounding noise of
+    the network itself, which bounds how closely any FP32 implementation with
+    a different summation order can agree with the reference.
+    """
+
+    def __init__(self, dtype):
+        self.dtype = dtype
+
+    def __enter__(self):
+        global _DTYPE
+        self.prev, _DTYPE = _DTYPE, self.dtype
+        return self
+
+    def __exit__(self, *exc):
+        global _DTYPE
+        _DTYPE = self.prev
+
+
 def t(a: np.ndarray) -> Tensor:
-    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(_DTYPE)
 
 
 def conv2d(x: Tensor, weight: np.ndarray, bias: Optional[np.ndarray], stride=(1, 1),
@@ -216,6 +242,7 @@ def conv2d(x: Tensor, weight: np.ndarray, bias: Optional[np.ndarray], stride=(1,
 
 
 def max_pool_same_upper(x: Tensor) -> Tensor:
+    # Note: in float64 mode F.pad keeps the dtype; -inf padding never wins.
     """2x2 stride-1 max pool padded at bottom/right; pads never win (ops.rs:1520-1535)."""
     x = F.pad(x, (0, 1, 0, 1), value=float("-inf"))
     return F.max_pool2d(x, kernel_size=2, stride=1)

@@ -383,9 +383,10 @@ int ppocr_recognizer_load_ex(ppocr_gpu* gpu, const char* path, int size, const s
 void ppocr_model_destroy(ppocr_model* model) {
     if (!model) return;
     {
+        // Never throws: this also runs from finalizers at process exit, when
+        // the CUDA runtime may already be shutting down.
         std::lock_guard<std::mutex> lock(model->gpu->mu);
-        model->gpu->bind();
-        cudaStreamSynchronize(model->gpu->stream);
+        if (cudaSetDevice(model->gpu->device) == cudaSuccess) cudaStreamSynchronize(model->gpu->stream);
     }
     delete model;
 }
@@ -611,6 +612,54 @@ int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms) {
         }
         for (auto& e : ev) cudaEventDestroy(e);
         for (size_t i = 0; i < ops.size(); ++i) op_ms[i] = acc[i] / (double)runs;
+    });
+}
+
+int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias, int act,
+                        float* c, int* used_tensor_cores, int* wait_error) {
+    return guard([&] {
+        if (!gpu || !a || !w || !c) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (m <= 0 || n <= 0 || k <= 0 || k % 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: GEMM shape (k must be a multiple of 4)");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        const int kp = (k + 63) / 64 * 64, np = (n + 15) / 16 * 16;
+        ConvWeight cw;
+        cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
+        cw.w.assign(w, w + (size_t)n * k);
+        cw.b = bias ? std::vector<float>(bias, bias + n) : std::vector<float>(n, 0.f);
+        int n_pad4 = 0;
+        WeightBlob blob;
+        const size_t wf = blob.add_f32(pack_gemm_kn(cw, n_pad4));
+        const size_t bo = blob.add_f32(cw.b);
+        const size_t wt = blob.add_bf16(pack_gemm_nk(cw, np, kp));
+        std::vector<float> av(a, a + (size_t)m * k);
+        const size_t ao = blob.add_bf16(av);
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        char* d = nullptr;
+        const size_t cbytes = (size_t)m * n * 4;
+        cuda_check(cudaMalloc(&d, bytes.size() + cbytes + 256), "allocate GEMM test buffers");
+        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        GemmParams p;
+        p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad4; p.k_pad = kp;
+        p.a = d + ao; p.w = reinterpret_cast<const float*>(d + wf); p.w_tc = d + wt;
+        p.bias = reinterpret_cast<const float*>(d + bo); p.act = act;
+        p.c = d + ((bytes.size() + 255) & ~(size_t)255); p.ldc = n; p.c_f32 = 1; p.dtype = DT_BF16;
+        const bool tc = gemm_tc_supported(p);
+        if (e == cudaSuccess) e = launch_gemm(p, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "GEMM self-test");
+        if (used_tensor_cores) *used_tensor_cores = tc ? 1 : 0;
+        const int err = gemm_tc_error_and_clear();
+        if (wait_error) *wait_error = err;
     });
 }
 

@@ -89,7 +89,9 @@ class Builder {
 public:
     Builder(BuiltModel& m, const WeightReader& r, bool tc) : m_(m), r_(r), tc_(tc) {}
     const WeightReader& reader() const { return r_; }
-    Plan& plan() { return m_.plan; }
+    // BF16 storage with tcgen05 GEMMs: SE gates are applied by a gate kernel
+    // instead of in the GEMM's A load (the tensor-core path reads A by TMA).
+    bool tensor_core_gemms() const { return tc_ && m_.dtype == DT_BF16; }
 
     Act4 tensor(const std::string& name, int n, int h, int w, int c) {
         Act4 a;
@@ -211,23 +213,22 @@ public:
 
     // SE gate of `x` (channel_sum + se_mlp); returns an FP32 [n][c] tensor id.
     int se_gate(const std::string& name, const Act4& x, const ConvWeight& reduce, const ConvWeight& expand, float alpha) {
-        const int sum = m_.plan.add_raw(name + ".sum", (size_t)x.n * x.c * 4);
-        const int gate = m_.plan.add_raw(name + ".gate", (size_t)x.n * x.c * 4);
+        const int n = x.n, c = x.c, hw = x.h * x.w, r = reduce.cout, xt = x.tid;
+        const int chunks = channel_sum_chunks(hw, c);
+        const int sum = m_.plan.add_raw(name + ".sum", (size_t)n * chunks * c * 4);
+        const int gate = m_.plan.add_raw(name + ".gate", (size_t)n * c * 4);
         const size_t w1 = m_.blob.add_f32(reduce.w), b1 = m_.blob.add_f32(reduce.b);
         const size_t w2 = m_.blob.add_f32(expand.w), b2 = m_.blob.add_f32(expand.b);
-        const int n = x.n, c = x.c, hw = x.h * x.w, r = reduce.cout, xt = x.tid;
         const DType dt = m_.dtype;
-        m_.plan.add_op(name + ".pool", {xt}, {sum}, [n, c, hw, xt, sum, dt](const Ctx& ctx, cudaStream_t st) {
-            cudaError_t e = cudaMemsetAsync(ctx.act(sum), 0, (size_t)n * c * 4, st);
-            if (e != cudaSuccess) return e;
+        m_.plan.add_op(name + ".pool", {xt}, {sum}, [n, c, hw, chunks, xt, sum, dt](const Ctx& ctx, cudaStream_t st) {
             PoolParams p;
-            p.n = n; p.hw = hw; p.c = c; p.in = ctx.act(xt); p.in_cstride = c;
+            p.n = n; p.hw = hw; p.c = c; p.in = ctx.act(xt); p.in_cstride = c; p.chunks = chunks;
             p.sum = static_cast<float*>(ctx.act(sum)); p.dtype = dt;
             return launch_channel_sum(p, st);
         }, "se.pool", 0, (double)n * hw * c);
-        m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, sum, gate, w1, b1, w2, b2, alpha](const Ctx& ctx, cudaStream_t st) {
+        m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, chunks, sum, gate, w1, b1, w2, b2, alpha](const Ctx& ctx, cudaStream_t st) {
             SeMlpParams p;
-            p.n = n; p.c = c; p.r = r; p.hw = hw;
+            p.n = n; p.c = c; p.r = r; p.hw = hw; p.chunks = chunks;
             p.sum = static_cast<const float*>(ctx.act(sum));
             p.w1 = ctx.wf(w1); p.b1 = ctx.wf(b1); p.w2 = ctx.wf(w2); p.b2 = ctx.wf(b2);
             p.alpha = alpha;
@@ -304,6 +305,10 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
         const int c = blk.cin;
         gate = b.se_gate(prefix + ".se", y, r.conv(prefix + ".token_squeeze_excitation.convolutions.0", c / 4, c, 1, 1, true),
                          r.conv(prefix + ".token_squeeze_excitation.convolutions.2", c, c / 4, 1, 1, true), 1.f / 6.f);
+        if (b.tensor_core_gemms()) {
+            y = b.gate_apply(prefix + ".se.apply", y, gate, 0, nullptr, 1);
+            gate = -1;
+        }
     }
     GemmOpts o1;
     o1.act = ACT_GELU;

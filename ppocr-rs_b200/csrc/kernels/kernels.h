@@ -127,23 +127,29 @@ struct PairParams {
 
 // Tensor-core (tcgen05) GEMM availability: BF16 storage, k_pad % 64 == 0, n_pad % 16 == 0.
 bool gemm_tc_supported(const GemmParams& p);
+// Reads and clears the tensor-core kernel's wait-expiry code (0 = none; host sync).
+int gemm_tc_error_and_clear();
 
 // ---------------------------------------------------------------------------
 // Squeeze-excitation
 // ---------------------------------------------------------------------------
-// pool_sum[img][c] += sum over pixels of x[img, :, :, c]   (pool_sum zeroed first)
+// partial[img][chunk][c] = sum over the chunk's pixels of x[img, :, :, c].
+// Fixed chunking and fixed summation order: results are bit-reproducible.
 struct PoolParams {
     int n = 0, hw = 0, c = 0;
     const void* in = nullptr;
     int in_cstride = 0;
-    float* sum = nullptr;
+    int chunks = 1;
+    float* sum = nullptr;      // [n][chunks][c]
     DType dtype = DT_F32;
 };
+int channel_sum_chunks(int hw, int c);
 cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream);
 
-// gate[img][c] = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5)
+// gate[img][c] = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5),
+// mean = (sum of the chunk partials in chunk order) / hw.
 struct SeMlpParams {
-    int n = 0, c = 0, r = 0, hw = 0;
+    int n = 0, c = 0, r = 0, hw = 0, chunks = 1;
     const float* sum = nullptr;
     const float* w1 = nullptr;  // [r][c]
     const float* b1 = nullptr;  // [r]

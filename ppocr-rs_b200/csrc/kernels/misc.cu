@@ -11,8 +11,9 @@ namespace {
 // ---------------------------------------------------------------------------
 // SE: per-(image, channel) sums over pixels (global_avg_pool2d numerator,
 // src/cpu/model.rs:488).  grid = (chunks, images); each thread owns 4
-// channels of a pixel row slice; partials reduced in shared memory, then one
-// atomicAdd per channel per block.
+// channels of a strided pixel slice of its chunk; the slices are reduced in
+// shared memory in a fixed order and the block writes its chunk partial (no
+// atomics, so every run produces the same bits).
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
@@ -20,22 +21,19 @@ __global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
     const int cg = p.c / 4;
     const int rows = blockDim.x / cg;          // pixel lanes per block
     const int g = threadIdx.x % cg, r = threadIdx.x / cg;
-    const int img = blockIdx.y;
+    const int img = blockIdx.y, chunk = blockIdx.x;
+    const int per = (p.hw + p.chunks - 1) / p.chunks;
+    const int px0 = chunk * per, px1 = min(p.hw, px0 + per);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < rows) {
         const T* base = static_cast<const T*>(p.in) + (size_t)img * p.hw * p.in_cstride + g * 4;
-        for (int px = blockIdx.x * rows + r; px < p.hw; px += gridDim.x * rows)
-            acc = f4_add(acc, load4(base + (size_t)px * p.in_cstride));
+        for (int px = px0 + r; px < px1; px += rows) acc = f4_add(acc, load4(base + (size_t)px * p.in_cstride));
     }
     part[threadIdx.x] = acc;
     __syncthreads();
     if (r == 0) {
         for (int i = 1; i < rows; ++i) acc = f4_add(acc, part[i * cg + g]);
-        float* dst = p.sum + (size_t)img * p.c + g * 4;
-        atomicAdd(dst + 0, acc.x);
-        atomicAdd(dst + 1, acc.y);
-        atomicAdd(dst + 2, acc.z);
-        atomicAdd(dst + 3, acc.w);
+        *reinterpret_cast<float4*>(p.sum + ((size_t)img * p.chunks + chunk) * p.c + g * 4) = acc;
     }
 }
 
@@ -47,7 +45,11 @@ __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
     float* hid = sm + p.c;
     const int img = blockIdx.x;
     const float inv = 1.f / (float)p.hw;
-    for (int i = threadIdx.x; i < p.c; i += blockDim.x) mean[i] = p.sum[(size_t)img * p.c + i] * inv;
+    for (int i = threadIdx.x; i < p.c; i += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < p.chunks; ++k) s += p.sum[((size_t)img * p.chunks + k) * p.c + i];
+        mean[i] = s * inv;
+    }
     __syncthreads();
     for (int j = threadIdx.x; j < p.r; j += blockDim.x) {
         float a = p.b1[j];
@@ -413,13 +415,18 @@ inline unsigned grid_for(long long total, int threads) {
 
 }  // namespace
 
-cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream) {
-    if (p.c % 4 || p.c / 4 > 256) return cudaErrorInvalidValue;
-    const int rows = 256 / (p.c / 4);
-    int chunks = (p.hw + rows * 8 - 1) / (rows * 8);
+int channel_sum_chunks(int hw, int c) {
+    const int cg = c / 4 > 0 ? c / 4 : 1;
+    const int rows = 256 / cg > 0 ? 256 / cg : 1;
+    int chunks = (hw + rows * 8 - 1) / (rows * 8);
     if (chunks > 64) chunks = 64;
     if (chunks < 1) chunks = 1;
-    dim3 grid(chunks, p.n);
+    return chunks;
+}
+
+cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream) {
+    if (p.c % 4 || p.c / 4 > 256 || p.chunks < 1) return cudaErrorInvalidValue;
+    dim3 grid(p.chunks, p.n);
     if (p.dtype == DT_F32) channel_sum_kernel<float><<<grid, 256, 0, stream>>>(p);
     else channel_sum_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
     return cudaGetLastError();

@@ -162,6 +162,7 @@ def library() -> C.CDLL:
         "ppocr_model_op_count": (I, [P, C.POINTER(S)]),
         "ppocr_model_op_info": (I, [P, S, C.c_char_p, S, C.c_char_p, S, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_model_profile": (I, [P, S, C.POINTER(C.c_double)]),
+        "ppocr_selftest_gemm": (I, [P, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
     }
     for name, (res, args) in sig.items():
@@ -234,6 +235,19 @@ class Gpu:
         _check(library().ppocr_preprocess(self._h, image._h, _fptr(c), int(content_width), int(out_h), int(out_w),
                                           0 if kind == "det" else 1, _fptr(out)))
         return out
+
+    def selftest_gemm(self, a, w, bias=None, act: int = 0):
+        """BF16 GEMM diagnostic: returns (C float32 [m, n], used_tensor_cores, wait_error)."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        m, k = a.shape
+        n = w.shape[0]
+        c = np.empty((m, n), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        used, err = C.c_int(), C.c_int()
+        _check(library().ppocr_selftest_gemm(self._h, m, n, k, _fptr(a), _fptr(w), None if b is None else _fptr(b),
+                                             int(act), _fptr(c), C.byref(used), C.byref(err)))
+        return c, bool(used.value), err.value
 
     def close(self) -> None:
         if getattr(self, "_h", None):
