@@ -211,6 +211,21 @@ int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size
 int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
                      size_t out_h, size_t out_w, int kind, float* output);
 
+/* ppocr_preprocess without any device allocation.  This entry point has no
+ * counterpart in the reference.  It is for callers that cannot call
+ * cudaMalloc: code under a fixed device-memory budget or an allocator that
+ * owns all device memory, and servers that forbid allocation calls (which
+ * synchronise the device) while serving.  Same arguments and results as
+ * ppocr_preprocess, but the output is staged in a fixed 4 MiB device array
+ * built into the library (present on every GPU that loads it, until exit),
+ * so 3 * out_h * out_w must not exceed 1048576 floats (InvalidInput beyond).
+ * The first call on a device looks up that array's device address (once per
+ * device); make that first call before any stream capture.  All calls on a
+ * device share the array: calls whose GPU work overlaps race and must be
+ * serialised by the caller. */
+int ppocr_preprocess_noalloc(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
+                             size_t out_h, size_t out_w, int kind, float* output);
+
 /* Detector only: probability map plus the DB binarisation mask
  * (prob >= threshold, src/ocr.rs:745,1047) as bytes of n*h*w. Either output
  * may be NULL. */

@@ -18,41 +18,18 @@
 #include <vector>
 
 #include "common.hpp"
+#include "handles.hpp"
 #include "models.hpp"
 #include "ppocr_b200.h"
 #include "safetensors.hpp"
 
 using namespace ppocr;
 
-namespace {
-thread_local std::string g_last_error;
-
-template <typename F>
-int guard(F&& f) {
-    try {
-        f();
-        g_last_error.clear();
-        return PPOCR_OK;
-    } catch (const Error& e) {
-        g_last_error = e.what();
-        return e.code;
-    } catch (const std::bad_alloc&) {
-        g_last_error = "out of host memory";
-        return PPOCR_ERR_GPU;
-    } catch (const std::exception& e) {
-        g_last_error = e.what();
-        return PPOCR_ERR_GPU;
-    }
+namespace ppocr {
+std::string& last_error() {
+    thread_local std::string message;
+    return message;
 }
-
-struct DeviceWeights {
-    void* ptr = nullptr;
-    size_t bytes = 0;
-    std::vector<uint8_t> host;   // kept for sharing checks
-    ~DeviceWeights() {
-        if (ptr) cudaFree(ptr);
-    }
-};
 
 void wait_stream(cudaStream_t s, int timeout_ms) {
     if (timeout_ms <= 0) timeout_ms = 60000;
@@ -66,35 +43,18 @@ void wait_stream(cudaStream_t s, int timeout_ms) {
         if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
-}  // namespace
+}  // namespace ppocr
 
-struct ppocr_gpu {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    std::mutex mu;
-    void* arena = nullptr;
-    size_t arena_bytes = 0;
-    uint64_t arena_gen = 0;
-    std::string name;
-
-    void bind() const { cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
-    void ensure_arena(size_t bytes) {
-        if (bytes <= arena_bytes) return;
-        cuda_check(cudaStreamSynchronize(stream), "synchronize before arena growth");
-        if (arena) cudaFree(arena);
-        arena = nullptr;
-        arena_bytes = 0;
-        cuda_check(cudaMalloc(&arena, bytes), "allocate activation arena");
-        arena_bytes = bytes;
-        ++arena_gen;
+namespace {
+struct DeviceWeights {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    std::vector<uint8_t> host;   // kept for sharing checks
+    ~DeviceWeights() {
+        if (ptr) cudaFree(ptr);
     }
 };
-
-struct ppocr_image {
-    ppocr_gpu* gpu = nullptr;
-    uint8_t* rgb = nullptr;
-    uint32_t width = 0, height = 0;
-};
+}  // namespace
 
 struct ppocr_model {
     ppocr_gpu* gpu = nullptr;
@@ -195,8 +155,10 @@ void finish(ppocr_model* model, int checked_tid, size_t checked_count) {
     if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
 }
 
-PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
-                                 size_t out_w, bool detector) {
+}  // namespace
+
+PreprocessParams ppocr::make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
+                                        size_t out_w, bool detector) {
     PreprocessParams p;
     p.rgb = image->rgb;
     p.src_w = (int)image->width;
@@ -214,6 +176,8 @@ PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8
     }
     return p;
 }
+
+namespace {
 
 void download(ppocr_model* model, int tid, void* dst, size_t bytes) {
     cuda_check(cudaMemcpyAsync(dst, model->tensor(tid), bytes, cudaMemcpyDeviceToHost, model->gpu->stream), "read output");
@@ -264,7 +228,7 @@ void ppocr_load_options_default(ppocr_load_options* options) {
     options->use_graph = 1;
 }
 
-const char* ppocr_last_error(void) { return g_last_error.c_str(); }
+const char* ppocr_last_error(void) { return last_error().c_str(); }
 
 int ppocr_gpu_count(int* count) {
     return guard([&] {

@@ -1,0 +1,77 @@
+// Internal definitions shared by the C-ABI translation units: the device and
+// image handles, the status/last-error plumbing and the bounded stream wait.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "../kernels/kernels.h"
+#include "common.hpp"
+#include "ppocr_b200.h"
+
+namespace ppocr {
+
+// Message of the last failure on the calling thread (ppocr_last_error()).
+std::string& last_error();
+
+// Runs `f`, turning an Error into its status code and recording the message.
+template <typename F>
+int guard(F&& f) {
+    try {
+        f();
+        last_error().clear();
+        return PPOCR_OK;
+    } catch (const Error& e) {
+        last_error() = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        last_error() = "out of host memory";
+        return PPOCR_ERR_GPU;
+    } catch (const std::exception& e) {
+        last_error() = e.what();
+        return PPOCR_ERR_GPU;
+    }
+}
+
+// Waits for `s` with a deadline (<= 0: 60 s); Error::Gpu on expiry or a device error.
+void wait_stream(cudaStream_t s, int timeout_ms);
+
+}  // namespace ppocr
+
+struct ppocr_gpu {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    uint64_t arena_gen = 0;
+    std::string name;
+
+    void bind() const { ppocr::cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
+    void ensure_arena(size_t bytes) {
+        if (bytes <= arena_bytes) return;
+        ppocr::cuda_check(cudaStreamSynchronize(stream), "synchronize before arena growth");
+        if (arena) cudaFree(arena);
+        arena = nullptr;
+        arena_bytes = 0;
+        ppocr::cuda_check(cudaMalloc(&arena, bytes), "allocate activation arena");
+        arena_bytes = bytes;
+        ++arena_gen;
+    }
+};
+
+struct ppocr_image {
+    ppocr_gpu* gpu = nullptr;
+    uint8_t* rgb = nullptr;
+    uint32_t width = 0, height = 0;
+};
+
+namespace ppocr {
+// Quad-resample parameters for `image` (Normalization::new, src/preprocess/kernels.rs:9-18).
+PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
+                                 size_t out_w, bool detector);
+}  // namespace ppocr

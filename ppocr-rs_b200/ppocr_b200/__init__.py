@@ -163,6 +163,7 @@ def library() -> C.CDLL:
         "ppocr_model_op_info": (I, [P, S, C.c_char_p, S, C.c_char_p, S, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_model_profile": (I, [P, S, C.POINTER(C.c_double)]),
         "ppocr_selftest_gemm": (I, [P, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
     }
     for name, (res, args) in sig.items():
@@ -234,6 +235,17 @@ class Gpu:
         out = np.empty((1, 3, int(out_h), int(out_w)), dtype=np.float32)
         _check(library().ppocr_preprocess(self._h, image._h, _fptr(c), int(content_width), int(out_h), int(out_w),
                                           0 if kind == "det" else 1, _fptr(out)))
+        return out
+
+    def preprocess_noalloc(self, image: "GpuImage", corners, content_width: int, out_h: int, out_w: int,
+                           kind: str = "det") -> np.ndarray:
+        """preprocess() for callers that cannot allocate device memory: the result is
+        staged in a fixed 4 MiB device array inside the library (3 * out_h * out_w
+        <= 1048576 floats); overlapping calls on one device must be serialised."""
+        c = np.asarray(corners, dtype=np.float32).reshape(8)
+        out = np.empty((1, 3, int(out_h), int(out_w)), dtype=np.float32)
+        _check(library().ppocr_preprocess_noalloc(self._h, image._h, _fptr(c), int(content_width), int(out_h),
+                                                  int(out_w), 0 if kind == "det" else 1, _fptr(out)))
         return out
 
     def selftest_gemm(self, a, w, bias=None, act: int = 0):
