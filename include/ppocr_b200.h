@@ -45,11 +45,14 @@ enum ppocr_status {
 enum ppocr_model_size { PPOCR_MEDIUM = 0, PPOCR_SMALL = 1, PPOCR_TINY = 2 };
 
 /* Activation storage / GEMM precision of a loaded model.
- * FP32: FP32 activations, FP32 arithmetic throughout (the reference's own
- *       arithmetic; the parity mode).
- * BF16: BF16 activations in HBM, tcgen05 BF16 tensor-core GEMMs with FP32
- *       accumulation; all other arithmetic FP32 in registers. */
-enum ppocr_precision { PPOCR_PRECISION_FP32 = 0, PPOCR_PRECISION_BF16 = 1 };
+ * FP32:   FP32 activations, FP32 FMA arithmetic throughout on the CUDA cores
+ *         (the reference's own arithmetic; the parity mode).
+ * BF16:   BF16 activations in HBM, tcgen05 BF16 tensor-core GEMMs with FP32
+ *         accumulation; all other arithmetic FP32 in registers.
+ * TF32X3: FP32 activations; pointwise and dense convs on tcgen05 as
+ *         A_hi W_hi + A_hi W_lo + A_lo W_hi with TF32 halves (FP32-class
+ *         products, tensor-core accumulation). */
+enum ppocr_precision { PPOCR_PRECISION_FP32 = 0, PPOCR_PRECISION_BF16 = 1, PPOCR_PRECISION_TF32X3 = 2 };
 
 typedef struct ppocr_gpu ppocr_gpu;
 typedef struct ppocr_image ppocr_image;
@@ -59,7 +62,8 @@ typedef struct ppocr_model ppocr_model;
 typedef struct ppocr_load_options {
     int precision;   /* enum ppocr_precision; default FP32 */
     int use_graph;   /* 1: replay each forward as one captured CUDA graph */
-    int reserved[6];
+    int simt_only;   /* 1: CUDA-core kernels only (no tcgen05); for A/B checks */
+    int reserved[5];
 } ppocr_load_options;
 
 /* Fills `options` with the defaults (FP32, CUDA graphs on). */
@@ -210,6 +214,16 @@ int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size
  * past `content_width` are zero. */
 int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
                      size_t out_h, size_t out_w, int kind, float* output);
+
+/* Diagnostic (new): one FP32 convolution through the FP32 tensor-core path
+ * (3xTF32 tcgen05): NHWC input [n, hi, wi, cin] (cin % 4 == 0), OIHW weight
+ * [cout, cin, kh, kw], symmetric padding, output NHWC [n, ho, wo, cout].
+ * 1x1 / stride 1 / pad 0 runs the dense-rows GEMM mode, anything else the
+ * implicit-GEMM gather mode.  used_tensor_cores and wait_error as for
+ * ppocr_selftest_gemm. */
+int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
+                        const float* x, const float* w, const float* bias, int act, float* out,
+                        int* used_tensor_cores, int* wait_error);
 
 /* ppocr_preprocess without any device allocation.  This entry point has no
  * counterpart in the reference.  It is for callers that cannot call

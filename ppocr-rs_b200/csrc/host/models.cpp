@@ -92,6 +92,47 @@ public:
     // BF16 storage with tcgen05 GEMMs: SE gates are applied by a gate kernel
     // instead of in the GEMM's A load (the tensor-core path reads A by TMA).
     bool tensor_core_gemms() const { return tc_ && m_.dtype == DT_BF16; }
+    // FP32 storage with 3xTF32 tcgen05 GEMMs and implicit-GEMM convs.
+    bool tensor_core_f32() const { return tc_ && m_.dtype == DT_F32; }
+
+    // Emits a tc_conv op (FP32 mode).  srcs empty: dense rows of `a_tid`.
+    void tc_f32_op(const std::string& name, const ConvWeight& cw, TcConvParams p, const std::vector<Src>& srcs, int a_tid,
+                   int gate, int res_gate, int residual, int out_tid, double flops) {
+        const int taps = cw.kh * cw.kw;
+        int cin4 = 0;
+        for (auto& s : srcs) cin4 += (s.channels + 3) / 4 * 4;
+        if (srcs.empty()) cin4 = cw.cin;
+        const int bn = tc_conv_tile_n(cw.cout);
+        p.n = cw.cout;
+        p.k = taps * cin4;
+        p.k_pad = (p.k + 31) / 32 * 32;
+        p.n_pad = (cw.cout + bn - 1) / bn * bn;
+        p.cin4 = cin4;
+        int acc = 0;
+        for (size_t i = 0; i < srcs.size(); ++i) {
+            p.src_start[i] = acc;
+            acc += (srcs[i].channels + 3) / 4 * 4;
+        }
+        p.src_start[srcs.size()] = acc;
+        const size_t woff = m_.blob.add_f32(pack_tf32_split(cw, cin4, p.n_pad, p.k_pad));
+        const size_t boff = m_.blob.add_f32(cw.b);
+        std::vector<int> reads = {a_tid, gate, res_gate, residual};
+        for (auto& s : srcs) reads.push_back(s.tid);
+        std::vector<Src> s2 = srcs;
+        m_.plan.add_op(name, reads, {out_tid},
+                       [p, s2, woff, boff, a_tid, gate, res_gate, residual, out_tid](const Ctx& c, cudaStream_t st) mutable {
+                           for (size_t i = 0; i < s2.size(); ++i) p.conv.src[i].ptr = c.act(s2[i].tid);
+                           p.w2 = c.wf(woff);
+                           p.bias = c.wf(boff);
+                           p.a = static_cast<const float*>(c.act(a_tid));
+                           p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
+                           p.res_gate = res_gate >= 0 ? static_cast<const float*>(c.act(res_gate)) : nullptr;
+                           p.residual = static_cast<const float*>(c.act(residual));
+                           p.c = static_cast<float*>(c.act(out_tid));
+                           return launch_tc_conv(p, st);
+                       },
+                       srcs.empty() ? "gemm" : "conv", (double)p.n_pad * p.k_pad * 8, flops);
+    }
 
     Act4 tensor(const std::string& name, int n, int h, int w, int c) {
         Act4 a;
@@ -108,6 +149,26 @@ public:
         if (cin != cw.cin) fail(PPOCR_ERR_INVALID_MODEL, name + ": conv input channels do not match the weight");
         const int ho = out_size(hi, cw.kh, sh, pt, pb), wo = out_size(wi, cw.kw, sw, pl, pr);
         Act4 out = tensor(name, n, ho, wo, cw.cout);
+        if (tensor_core_f32()) {
+            TcConvParams tp;
+            tp.mode = 1;
+            tp.m = n * ho * wo;
+            ConvParams& g = tp.conv;
+            g.n = n; g.hi = hi; g.wi = wi; g.cin = cin; g.nsrc = (int)srcs.size();
+            g.ho = ho; g.wo = wo; g.cout = cw.cout; g.kh = cw.kh; g.kw = cw.kw; g.sh = sh; g.sw = sw; g.pt = pt; g.pl = pl;
+            for (size_t i = 0; i < srcs.size(); ++i) {
+                g.src[i].channels = srcs[i].channels; g.src[i].cstride = srcs[i].cstride; g.src[i].coff = srcs[i].coff;
+                g.src[i].scale = srcs[i].scale; g.src[i].mode = srcs[i].mode;
+            }
+            tp.act = act;
+            tp.ldr = cw.cout;
+            tp.res_scale = res_scale;
+            tp.out_h = ho; tp.out_w = wo;
+            tp.rows_per_image = ho * wo;
+            tp.ldc = cw.cout;
+            tc_f32_op(name, cw, tp, srcs, -1, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
+            return out;
+        }
         const size_t woff = m_.blob.add_f32(pack_conv_tiles(cw));
         std::vector<float> bias = cw.b;
         bias.resize((cw.cout + 7) / 8 * 8, 0.f);
@@ -170,6 +231,23 @@ public:
     // Pointwise conv / linear over `rows` rows of `in` (gemm_simt.cu / tcgen05 GEMM).
     void gemm_rows(const std::string& name, const ConvWeight& cw, int in_tid, int rows, const GemmOpts& o, int out_tid) {
         const int k = cw.cin * cw.kh * cw.kw;
+        if (tensor_core_f32() && k % 4 == 0) {
+            TcConvParams tp;
+            tp.mode = 0;
+            tp.m = rows;
+            tp.lda = k;
+            tp.rows_per_image = o.rows_per_image;
+            tp.act = o.act;
+            tp.ldr = cw.cout;
+            tp.res_scale = o.res_scale;
+            tp.out_h = o.h; tp.out_w = o.w;
+            tp.ldc = cw.cout;
+            ConvWeight flat = cw;
+            flat.cin = k; flat.kh = 1; flat.kw = 1;
+            if (!o.has_bias) flat.b.assign(cw.cout, 0.f);
+            tc_f32_op(name, flat, tp, {}, in_tid, o.gate, o.res_gate, o.residual, out_tid, 2.0 * rows * cw.cout * k);
+            return;
+        }
         int n_pad = 0;
         const size_t woff = m_.blob.add_f32(pack_gemm_kn(cw, n_pad));
         const size_t boff = m_.blob.add_f32(cw.b);

@@ -217,6 +217,29 @@ std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad) {
     return out;
 }
 
+static inline float tf32_round(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+std::vector<float> pack_tf32_split(const ConvWeight& cw, int cin4, int n_pad, int k_pad) {
+    const int taps = cw.kh * cw.kw;
+    std::vector<float> out((size_t)2 * n_pad * k_pad, 0.f);
+    for (int o = 0; o < cw.cout; ++o)
+        for (int t = 0; t < taps; ++t)
+            for (int i = 0; i < cw.cin; ++i) {
+                const float v = cw.w[((size_t)o * cw.cin + i) * taps + t];
+                const float hi = tf32_round(v);
+                const size_t at = (size_t)o * k_pad + (size_t)t * cin4 + i;
+                out[at] = hi;
+                out[(size_t)n_pad * k_pad + at] = tf32_round(v - hi);
+            }
+    return out;
+}
+
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad) {
     const int k = cw.cin * cw.kh * cw.kw;
     std::vector<float> out((size_t)n_pad * k_pad, 0.f);

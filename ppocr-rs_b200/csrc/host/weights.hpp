@@ -65,5 +65,9 @@ std::vector<float> pack_conv_tiles(const ConvWeight& cw);                 // [ce
 std::vector<float> pack_depthwise(const ConvWeight& cw);                  // [kh*kw][C]
 std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad);        // [K][N_pad4]
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad);  // [N_pad][K_pad] (BF16 source)
+// 3xTF32 operand: [2][n_pad][k_pad], K index = tap * cin4 + channel (cin4 =
+// cin rounded up to 4); the first half TF32-rounded weights, the second the
+// TF32-rounded remainders.
+std::vector<float> pack_tf32_split(const ConvWeight& cw, int cin4, int n_pad, int k_pad);
 
 }  // namespace ppocr

@@ -131,6 +131,42 @@ bool gemm_tc_supported(const GemmParams& p);
 int gemm_tc_error_and_clear();
 
 // ---------------------------------------------------------------------------
+// FP32-accurate tensor-core GEMM / implicit-GEMM conv (3xTF32 on tcgen05),
+// the FP32 mode's kernel for pointwise and dense convs (tc_conv.cu).
+//   mode 0: A rows are dense FP32 [m][lda] (optional SE gate on A);
+//   mode 1: A is the conv window gathered from conv.src[] (conv.kh/kw/sh/sw/
+//           pt/pl/hi/wi, output grid out_h x out_w); K = taps * cin4 with each
+//           source's channels padded to a multiple of 4 (NCHW input: 3 -> 4).
+// W2 holds [2][n_pad][k_pad] FP32: TF32-rounded weights, then the TF32-rounded
+// remainders, K-major; n_pad = a multiple of tc_conv_tile_n(n).
+// ---------------------------------------------------------------------------
+struct TcConvParams {
+    int mode = 0;
+    int m = 0, n = 0, k = 0;
+    int n_pad = 0, k_pad = 0;
+    const float* w2 = nullptr;
+    const float* a = nullptr;
+    int lda = 0;
+    const float* gate = nullptr;
+    int rows_per_image = 1;
+    ConvParams conv;
+    int cin4 = 0;
+    int src_start[5] = {0, 0, 0, 0, 0};
+    const float* bias = nullptr;
+    int act = 0;
+    const float* residual = nullptr;
+    int ldr = 0;
+    const float* res_gate = nullptr;
+    int res_scale = 1;
+    int out_h = 1, out_w = 1;
+    float* c = nullptr;
+    int ldc = 0, coff = 0;
+};
+int tc_conv_tile_n(int n);
+cudaError_t launch_tc_conv(const TcConvParams& p, cudaStream_t stream);
+int tc_conv_error_and_clear();
+
+// ---------------------------------------------------------------------------
 // Squeeze-excitation
 // ---------------------------------------------------------------------------
 // partial[img][chunk][c] = sum over the chunk's pixels of x[img, :, :, c].

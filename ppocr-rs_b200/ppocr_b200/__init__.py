@@ -103,18 +103,21 @@ class ModelSize:
 
 
 class Precision:
+    """FP32: CUDA-core FP32 (parity mode); BF16: BF16 storage + tcgen05 BF16 GEMMs;
+    TF32X3: FP32 storage + 3xTF32 tcgen05 GEMMs / convs."""
     FP32 = 0
     BF16 = 1
+    TF32X3 = 2
 
     @staticmethod
     def parse(value) -> int:
         if isinstance(value, int):
             return value
-        return {"fp32": 0, "bf16": 1}[str(value).lower()]
+        return {"fp32": 0, "bf16": 1, "tf32x3": 2}[str(value).lower()]
 
 
 class _LoadOptions(C.Structure):
-    _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("reserved", C.c_int * 6)]
+    _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("simt_only", C.c_int), ("reserved", C.c_int * 5)]
 
 
 _SIZE4 = C.c_size_t * 4
@@ -164,6 +167,8 @@ def library() -> C.CDLL:
         "ppocr_model_profile": (I, [P, S, C.POINTER(C.c_double)]),
         "ppocr_selftest_gemm": (I, [P, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
+        "ppocr_selftest_conv": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int),
+                                    C.POINTER(C.c_int)]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
     }
     for name, (res, args) in sig.items():
@@ -247,6 +252,21 @@ class Gpu:
         _check(library().ppocr_preprocess_noalloc(self._h, image._h, _fptr(c), int(content_width), int(out_h),
                                                   int(out_w), 0 if kind == "det" else 1, _fptr(out)))
         return out
+
+    def selftest_conv(self, x_nhwc, w_oihw, bias=None, stride: int = 1, pad: int = 0, act: int = 0):
+        """FP32 3xTF32 tensor-core conv diagnostic: returns (out NHWC float32, wait_error)."""
+        x = np.ascontiguousarray(x_nhwc, dtype=np.float32)
+        w = np.ascontiguousarray(w_oihw, dtype=np.float32)
+        n, hi, wi, cin = x.shape
+        cout, _, kh, kw = w.shape
+        ho, wo = (hi + 2 * pad - kh) // stride + 1, (wi + 2 * pad - kw) // stride + 1
+        out = np.empty((n, ho, wo, cout), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        used, err = C.c_int(), C.c_int()
+        _check(library().ppocr_selftest_conv(self._h, n, hi, wi, cin, cout, kh, kw, int(stride), int(pad), _fptr(x),
+                                             _fptr(w), None if b is None else _fptr(b), int(act), _fptr(out),
+                                             C.byref(used), C.byref(err)))
+        return out, err.value
 
     def selftest_gemm(self, a, w, bias=None, act: int = 0):
         """BF16 GEMM diagnostic: returns (C float32 [m, n], used_tensor_cores, wait_error)."""
@@ -393,11 +413,12 @@ class _Model:
             pass
 
 
-def _options(precision, use_graph: bool) -> _LoadOptions:
+def _options(precision, use_graph: bool, simt_only: bool = False) -> _LoadOptions:
     o = _LoadOptions()
     library().ppocr_load_options_default(C.byref(o))
     o.precision = Precision.parse(precision)
     o.use_graph = 1 if use_graph else 0
+    o.simt_only = 1 if simt_only else 0
     return o
 
 
@@ -406,9 +427,9 @@ class Detector(_Model):
 
     @classmethod
     def load(cls, gpu: Gpu, path: str, size, input_shape: Sequence[int], precision="fp32",
-             use_graph: bool = True) -> "Detector":
+             use_graph: bool = True, simt_only: bool = False) -> "Detector":
         h = C.c_void_p()
-        o = _options(precision, use_graph)
+        o = _options(precision, use_graph, simt_only)
         _check(library().ppocr_detector_load_ex(gpu._h, str(path).encode(), ModelSize.parse(size),
                                                 _SIZE4(*input_shape), C.byref(o), C.byref(h)))
         return cls(h, gpu, input_shape)
@@ -429,9 +450,10 @@ class Recognizer(_Model):
 
     @classmethod
     def load(cls, gpu: Gpu, path: str, size, input_shape: Sequence[int], precision="fp32",
-             use_graph: bool = True, shared_weights: Optional["Recognizer"] = None) -> "Recognizer":
+             use_graph: bool = True, shared_weights: Optional["Recognizer"] = None,
+             simt_only: bool = False) -> "Recognizer":
         h = C.c_void_p()
-        o = _options(precision, use_graph)
+        o = _options(precision, use_graph, simt_only)
         _check(library().ppocr_recognizer_load_ex(gpu._h, str(path).encode(), ModelSize.parse(size),
                                                   _SIZE4(*input_shape), C.byref(o),
                                                   shared_weights._h if shared_weights is not None else None,

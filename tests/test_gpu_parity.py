@@ -129,6 +129,30 @@ def test_recognizer(gpu, weights_file, size, profile, precision, shape):
     _rec_check(gpu, weights_file("rec", size, profile), size, shape, precision)
 
 
+@pytest.mark.parametrize("kind,size,shape", [
+    ("det", "tiny", (2, 3, 96, 128)),
+    ("det", "medium", (1, 3, 128, 160)),
+    ("rec", "medium", (2, 3, 48, 160)),
+])
+def test_tf32x3_tensor_core_path_matches_fp32(gpu, weights_file, kind, size, shape):
+    """TF32X3 mode (3xTF32 tcgen05 GEMMs / convs) agrees with the FP32 CUDA-core mode."""
+    path = weights_file(kind, size, "conditioned")
+    if kind == "det":
+        x = seeded.det_batch(shape[0], shape[2], shape[3], seed=6, text=True)
+        a = P.Detector.load(gpu, path, size, shape, precision="tf32x3").forward(x).values
+        b = P.Detector.load(gpu, path, size, shape, precision="fp32").forward(x).values
+        want = oracle(kind, size, path).forward(x).reshape(-1)
+        assert np.abs(a - want).max() <= DET_MAX_ABS
+        assert np.abs(a - b).max() <= 1e-3
+    else:
+        x = seeded.rec_batch(shape[0], shape[3], seed=6)
+        a = P.Recognizer.load(gpu, path, size, shape, precision="tf32x3").forward_logits(x)
+        b = P.Recognizer.load(gpu, path, size, shape, precision="fp32").forward_logits(x)
+        want = oracle(kind, size, path).logits(x)
+        assert np.abs(a - want).max() <= REC_LOGIT_MAX_ABS
+        assert np.abs(a - b).max() <= 1e-3
+
+
 def test_preprocess_bit_exact(gpu):
     rng = np.random.default_rng(3)
     rgb = rng.integers(0, 256, size=(57, 83, 3), dtype=np.uint8)
