@@ -294,6 +294,10 @@ def run_b200(args):
         achieved = dom["bytes"] / launches / (per_launch_ms / 1000.0) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4)}
+    top = sorted(zip(ops, prof), key=lambda t: -t[1])[:8]
+    roof["top_ops"] = [{"op": o["name"], "kind": o["kind"], "ms": round(ms, 4),
+                        "GBps": round(o["bytes"] / (ms / 1000.0) / 1e9, 1),
+                        "TFLOPs": round(o["flops"] / (ms / 1000.0) / 1e12, 2)} for o, ms in top]
     roof.update({"kernel": dom_kind, "launches_per_step": launches, "time_share": round(dom["ms"] / sum(prof), 4),
                  "peak_source": peak_src, "traffic": None,
                  "algorithmic_bytes_per_launch": round(dom["bytes"] / launches),

@@ -169,15 +169,19 @@ public:
             tc_f32_op(name, cw, tp, srcs, -1, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
             return out;
         }
-        const size_t woff = m_.blob.add_f32(pack_conv_tiles(cw));
+        // 16 output channels per thread when cout >= 16 (the head's and stems' input
+        // windows are then read once per 16 channels instead of once per 8).
+        const int co_tile = cw.cout >= 16 ? 16 : 8;
+        const size_t woff = m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
         std::vector<float> bias = cw.b;
-        bias.resize((cw.cout + 7) / 8 * 8, 0.f);
+        bias.resize((cw.cout + co_tile - 1) / co_tile * co_tile, 0.f);
         const size_t boff = m_.blob.add_f32(bias);
         ConvParams p;
         p.n = n; p.hi = hi; p.wi = wi; p.cin = cin; p.nsrc = (int)srcs.size();
         p.ho = ho; p.wo = wo; p.cout = cw.cout;
         p.kh = cw.kh; p.kw = cw.kw; p.sh = sh; p.sw = sw; p.pt = pt; p.pl = pl;
         p.act = act; p.res_scale = res_scale; p.out_cstride = cw.cout; p.out_coff = 0; p.dtype = m_.dtype;
+        p.co_tile = co_tile;
         std::vector<int> reads;
         for (size_t i = 0; i < srcs.size(); ++i) {
             p.src[i].channels = srcs[i].channels; p.src[i].cstride = srcs[i].cstride; p.src[i].coff = srcs[i].coff;

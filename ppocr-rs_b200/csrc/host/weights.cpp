@@ -189,14 +189,15 @@ size_t WeightBlob::add_bf16(const std::vector<float>& v) {
     return off;
 }
 
-std::vector<float> pack_conv_tiles(const ConvWeight& cw) {
-    const int tiles = (cw.cout + 7) / 8;
+std::vector<float> pack_conv_tiles(const ConvWeight& cw, int tile) {
+    const int tiles = (cw.cout + tile - 1) / tile;
     const int taps = cw.kh * cw.kw;
-    std::vector<float> out((size_t)tiles * taps * cw.cin * 8, 0.f);
+    std::vector<float> out((size_t)tiles * taps * cw.cin * tile, 0.f);
     for (int o = 0; o < cw.cout; ++o)
         for (int i = 0; i < cw.cin; ++i)
             for (int t = 0; t < taps; ++t)
-                out[(((size_t)(o / 8) * taps + t) * cw.cin + i) * 8 + (o % 8)] = cw.w[((size_t)o * cw.cin + i) * taps + t];
+                out[(((size_t)(o / tile) * taps + t) * cw.cin + i) * tile + (o % tile)] =
+                    cw.w[((size_t)o * cw.cin + i) * taps + t];
     return out;
 }
 

@@ -7,9 +7,10 @@
 // conv_down over the upsample-concat of the four neck outputs
 // (src/cpu/model.rs:626-693, 1022-1066, 1479-1521).
 //
-// One thread computes one output pixel for a tile of 8 output channels; the
-// block's weight tile [kh][kw][cin][8] sits in shared memory and is read by
-// broadcast.  Input channels are read four at a time.
+// One thread computes one output pixel for a tile of CO output channels
+// (16 when cout >= 16, else 8), so the input window is read once per
+// 16 channels; the block's weight tile [kh][kw][cin][CO] sits in shared
+// memory and is read by broadcast.  Input channels are read four at a time.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -17,7 +18,6 @@ namespace ppocr {
 namespace {
 
 constexpr int kConvThreads = 128;
-constexpr int kCoTile = 8;
 
 template <typename T>
 __device__ __forceinline__ float4 read_source4(const ConvSource& s, int img, int iy, int ix, int hi, int wi, int c) {
@@ -45,12 +45,12 @@ __device__ __forceinline__ float4 read_source4(const ConvSource& s, int img, int
     return load4(base + ((size_t)(img * hs + sy) * ws + sx) * s.cstride + s.coff + c);
 }
 
-template <typename T>
+template <typename T, int CO>
 __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
     extern __shared__ float wsm[];
     const int tile = blockIdx.y;
     const int taps = p.kh * p.kw;
-    const int wcount = taps * p.cin * kCoTile;
+    const int wcount = taps * p.cin * CO;
     const float* wsrc = p.weight + (size_t)tile * wcount;
     for (int i = threadIdx.x * 4; i < wcount; i += kConvThreads * 4) {
         *reinterpret_cast<float4*>(wsm + i) = *reinterpret_cast<const float4*>(wsrc + i);
@@ -64,9 +64,9 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
     const int oy = (int)((pix / p.wo) % p.ho);
     const int img = (int)(pix / ((long long)p.wo * p.ho));
 
-    float acc[kCoTile];
+    float acc[CO];
 #pragma unroll
-    for (int o = 0; o < kCoTile; ++o) acc[o] = 0.f;
+    for (int o = 0; o < CO; ++o) acc[o] = 0.f;
 
     for (int ky = 0; ky < p.kh; ++ky) {
         const int iy = oy * p.sh - p.pt + ky;
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
         for (int kx = 0; kx < p.kw; ++kx) {
             const int ix = ox * p.sw - p.pl + kx;
             if (ix < 0 || ix >= p.wi) continue;
-            const float* wt = wsm + (size_t)(ky * p.kw + kx) * p.cin * kCoTile;
+            const float* wt = wsm + (size_t)(ky * p.kw + kx) * p.cin * CO;
             int cbase = 0;
             for (int s = 0; s < p.nsrc; ++s) {
                 const ConvSource& src = p.src[s];
@@ -82,22 +82,36 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
                     const float* base = static_cast<const float*>(src.ptr);
                     for (int c = 0; c < src.channels; ++c) {
                         const float v = base[((size_t)(img * src.channels + c) * p.hi + iy) * p.wi + ix];
-                        const float* wr = wt + (cbase + c) * kCoTile;
+                        const float* wr = wt + (cbase + c) * CO;
 #pragma unroll
-                        for (int o = 0; o < kCoTile; ++o) acc[o] = fmaf(v, wr[o], acc[o]);
+                        for (int o = 0; o < CO; ++o) acc[o] = fmaf(v, wr[o], acc[o]);
                     }
                 } else {
                     for (int c = 0; c < src.channels; c += 4) {
                         const float4 v = read_source4<T>(src, img, iy, ix, p.hi, p.wi, c);
-                        const float* wr = wt + (cbase + c) * kCoTile;
+                        const float* wr = wt + (cbase + c) * CO;
 #pragma unroll
-                        for (int o = 0; o < kCoTile; ++o) {
-                            float a = acc[o];
-                            a = fmaf(v.x, wr[o], a);
-                            a = fmaf(v.y, wr[kCoTile + o], a);
-                            a = fmaf(v.z, wr[2 * kCoTile + o], a);
-                            a = fmaf(v.w, wr[3 * kCoTile + o], a);
-                            acc[o] = a;
+                        for (int o = 0; o < CO; o += 4) {
+                            const float4 w0 = *reinterpret_cast<const float4*>(wr + o);
+                            const float4 w1 = *reinterpret_cast<const float4*>(wr + CO + o);
+                            const float4 w2 = *reinterpret_cast<const float4*>(wr + 2 * CO + o);
+                            const float4 w3 = *reinterpret_cast<const float4*>(wr + 3 * CO + o);
+                            acc[o] = fmaf(v.x, w0.x, acc[o]);
+                            acc[o + 1] = fmaf(v.x, w0.y, acc[o + 1]);
+                            acc[o + 2] = fmaf(v.x, w0.z, acc[o + 2]);
+                            acc[o + 3] = fmaf(v.x, w0.w, acc[o + 3]);
+                            acc[o] = fmaf(v.y, w1.x, acc[o]);
+                            acc[o + 1] = fmaf(v.y, w1.y, acc[o + 1]);
+                            acc[o + 2] = fmaf(v.y, w1.z, acc[o + 2]);
+                            acc[o + 3] = fmaf(v.y, w1.w, acc[o + 3]);
+                            acc[o] = fmaf(v.z, w2.x, acc[o]);
+                            acc[o + 1] = fmaf(v.z, w2.y, acc[o + 1]);
+                            acc[o + 2] = fmaf(v.z, w2.z, acc[o + 2]);
+                            acc[o + 3] = fmaf(v.z, w2.w, acc[o + 3]);
+                            acc[o] = fmaf(v.w, w3.x, acc[o]);
+                            acc[o + 1] = fmaf(v.w, w3.y, acc[o + 1]);
+                            acc[o + 2] = fmaf(v.w, w3.z, acc[o + 2]);
+                            acc[o + 3] = fmaf(v.w, w3.w, acc[o + 3]);
                         }
                     }
                 }
@@ -106,7 +120,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
         }
     }
 
-    const int co0 = tile * kCoTile;
+    const int co0 = tile * CO;
     T* out = static_cast<T*>(p.out) + (size_t)pix * p.out_cstride + p.out_coff + co0;
     const T* res = nullptr;
     if (p.residual) {
@@ -115,7 +129,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
               ((size_t)(img * rh + oy / p.res_scale) * rw + ox / p.res_scale) * p.cout + co0;
     }
 #pragma unroll
-    for (int g = 0; g < kCoTile; g += 4) {
+    for (int g = 0; g < CO; g += 4) {
         if (co0 + g >= p.cout) break;
         float4 v = make_float4(acc[g], acc[g + 1], acc[g + 2], acc[g + 3]);
         if (p.bias) v = f4_add(v, *reinterpret_cast<const float4*>(p.bias + co0 + g));
@@ -125,27 +139,30 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
     }
 }
 
-template <typename T>
+template <typename T, int CO>
 cudaError_t launch_conv_t(const ConvParams& p, cudaStream_t stream) {
-    const int tiles = (p.cout + kCoTile - 1) / kCoTile;
-    const size_t smem = (size_t)p.kh * p.kw * p.cin * kCoTile * sizeof(float);
+    const int tiles = (p.cout + CO - 1) / CO;
+    const size_t smem = (size_t)p.kh * p.kw * p.cin * CO * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(conv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(conv_kernel<T, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     if (smem > 200 * 1024) return cudaErrorInvalidConfiguration;
     const long long total = (long long)p.n * p.ho * p.wo;
     dim3 grid((unsigned)((total + kConvThreads - 1) / kConvThreads), (unsigned)tiles);
-    conv_kernel<T><<<grid, kConvThreads, smem, stream>>>(p);
+    conv_kernel<T, CO><<<grid, kConvThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream) {
-    return p.dtype == DT_F32 ? launch_conv_t<float>(p, stream) : launch_conv_t<__nv_bfloat16>(p, stream);
+    if (p.co_tile == 16)
+        return p.dtype == DT_F32 ? launch_conv_t<float, 16>(p, stream) : launch_conv_t<__nv_bfloat16, 16>(p, stream);
+    if (p.co_tile != 8) return cudaErrorInvalidValue;
+    return p.dtype == DT_F32 ? launch_conv_t<float, 8>(p, stream) : launch_conv_t<__nv_bfloat16, 8>(p, stream);
 }
 
 }  // namespace ppocr

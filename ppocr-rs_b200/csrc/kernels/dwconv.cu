@@ -6,65 +6,103 @@
 // halves (src/cpu/model.rs:165-219), the SVTR local 1x7 conv + SiLU + residual
 // (src/cpu/model.rs:1825-1830) and the tiny recognizer's 1x5 head conv.
 //
-// NHWC: a thread owns 4 consecutive channels of one output pixel, so a warp
-// reads contiguous channel runs of neighbouring pixels (coalesced 16- or
-// 8-byte accesses); the k x k window re-reads hit L1/L2.  Bandwidth-bound:
-// algorithmic bytes = input + output (+ residual) + weights.
+// Bandwidth-bound (algorithmic bytes = input + output (+ residual) +
+// weights).  A block owns a TH x TW output tile of CG channel quads: it
+// stages the input tile plus halo in shared memory once (coalesced 16-byte
+// loads, CG quads of a pixel contiguous), so every input element is read from
+// HBM about once instead of k^2 times, then each thread computes its
+// channel quad for a strided set of tile pixels from shared memory.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace ppocr {
 namespace {
 
-template <typename T>
-__global__ void __launch_bounds__(256) dwconv_kernel(DwParams p) {
-    const int cg = p.c >> 2;
-    const long long total = (long long)p.n * p.ho * p.wo * cg;
-    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
-        const int c = (int)(idx % cg) * 4;
-        const long long pix = idx / cg;
-        const int ox = (int)(pix % p.wo);
-        const int oy = (int)((pix / p.wo) % p.ho);
-        const int img = (int)(pix / ((long long)p.wo * p.ho));
-        const T* in = static_cast<const T*>(p.in) + p.in_coff + c;
+constexpr int kThreads = 256;
+
+template <typename T, int CG>
+__global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, int th, int tw, int ih, int iw) {
+    extern __shared__ float4 sm4[];
+    float4* tile = sm4;                       // [ih][iw][CG]
+    float4* wts = sm4 + (size_t)ih * iw * CG;  // [taps][CG]
+    const int taps = p.kh * p.kw;
+    const int groups = p.c / (4 * CG);
+    const int img = blockIdx.z / groups, grp = blockIdx.z % groups;
+    const int c0 = grp * CG * 4;
+    const int oy0 = blockIdx.y * th, ox0 = blockIdx.x * tw;
+    const int iy0 = oy0 * p.sh - p.pt, ix0 = ox0 * p.sw - p.pl;
+    const T* in = static_cast<const T*>(p.in);
+
+    for (int i = threadIdx.x; i < taps * CG; i += kThreads) {
+        const int t = i / CG, q = i % CG;
+        wts[i] = *reinterpret_cast<const float4*>(p.weight + (size_t)t * p.c + c0 + q * 4);
+    }
+    const int n_in = ih * iw * CG;
+    for (int i = threadIdx.x; i < n_in; i += kThreads) {
+        const int q = i % CG, pix = i / CG;
+        const int y = iy0 + pix / iw, x = ix0 + pix % iw;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (y >= 0 && y < p.hi && x >= 0 && x < p.wi)
+            v = load4(in + ((size_t)(img * p.hi + y) * p.wi + x) * p.in_cstride + p.in_coff + c0 + q * 4);
+        tile[i] = v;
+    }
+    __syncthreads();
+
+    const int q = threadIdx.x % CG;
+    const int c = c0 + q * 4;
+    const float4 bias = p.bias ? *reinterpret_cast<const float4*>(p.bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int PX = kThreads / CG;
+    for (int pp = threadIdx.x / CG; pp < th * tw; pp += PX) {
+        const int ty = pp / tw, tx = pp % tw;
+        const int oy = oy0 + ty, ox = ox0 + tx;
+        if (oy >= p.ho || ox >= p.wo) continue;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int ky = 0; ky < p.kh; ++ky) {
-            const int iy = oy * p.sh - p.pt + ky;
-            if (iy < 0 || iy >= p.hi) continue;
-            const T* row = in + (size_t)(img * p.hi + iy) * p.wi * p.in_cstride;
-            const float* wrow = p.weight + (size_t)ky * p.kw * p.c + c;
-            for (int kx = 0; kx < p.kw; ++kx) {
-                const int ix = ox * p.sw - p.pl + kx;
-                if (ix < 0 || ix >= p.wi) continue;
-                const float4 v = load4(row + (size_t)ix * p.in_cstride);
-                const float4 w = *reinterpret_cast<const float4*>(wrow + (size_t)kx * p.c);
-                acc = f4_vfma(v, w, acc);
-            }
+            const float4* row = tile + ((size_t)(ty * p.sh + ky) * iw + tx * p.sw) * CG + q;
+            const float4* wr = wts + (size_t)ky * p.kw * CG + q;
+            for (int kx = 0; kx < p.kw; ++kx) acc = f4_vfma(row[kx * CG], wr[kx * CG], acc);
         }
-        if (p.bias) acc = f4_add(acc, *reinterpret_cast<const float4*>(p.bias + c));
-        acc = f4_act(acc, p.act);
-        const size_t o = (size_t)pix * p.c + c;
+        acc = f4_act(f4_add(acc, bias), p.act);
+        const size_t o = ((size_t)(img * p.ho + oy) * p.wo + ox) * p.c + c;
         if (p.residual) acc = f4_add(acc, load4(static_cast<const T*>(p.residual) + o));
         store4(static_cast<T*>(p.out) + o, acc);
     }
 }
 
+template <typename T, int CG>
+cudaError_t launch_tiled(const DwParams& p, cudaStream_t stream) {
+    // Output tile: 8 rows x 32 columns at stride 1; halve along a strided axis.
+    const int th = p.sh == 1 ? 8 : 4;
+    const int tw = p.sw == 1 ? 32 : 16;
+    const int ih = (th - 1) * p.sh + p.kh, iw = (tw - 1) * p.sw + p.kw;
+    const size_t smem = ((size_t)ih * iw * CG + (size_t)p.kh * p.kw * CG) * sizeof(float4);
+    if (smem > 200 * 1024) return cudaErrorInvalidConfiguration;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(dwconv_tiled_kernel<T, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const long long z = (long long)p.n * (p.c / (4 * CG));
+    if (z > 65535 || (p.ho + th - 1) / th > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((p.wo + tw - 1) / tw, (p.ho + th - 1) / th, (unsigned)z);
+    dwconv_tiled_kernel<T, CG><<<grid, kThreads, smem, stream>>>(p, th, tw, ih, iw);
+    return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_dw_t(const DwParams& p, cudaStream_t stream) {
-    const long long total = (long long)p.n * p.ho * p.wo * (p.c / 4);
-    long long blocks = (total + 255) / 256;
-    const long long cap = 148LL * 16;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    dwconv_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(p);
-    return cudaGetLastError();
+    const int quads = p.c / 4;
+    if (quads % 8 == 0) return launch_tiled<T, 8>(p, stream);
+    if (quads % 4 == 0) return launch_tiled<T, 4>(p, stream);
+    if (quads % 2 == 0) return launch_tiled<T, 2>(p, stream);
+    return launch_tiled<T, 1>(p, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_dwconv(const DwParams& p, cudaStream_t stream) {
-    if (p.c % 4) return cudaErrorInvalidValue;
+    if (p.c % 4 || p.in_coff % 4 || p.in_cstride % 4) return cudaErrorInvalidValue;
     return p.dtype == DT_F32 ? launch_dw_t<float>(p, stream) : launch_dw_t<__nv_bfloat16>(p, stream);
 }
 

@@ -50,7 +50,8 @@ struct ConvParams {
     int nsrc = 0;
     int ho = 0, wo = 0, cout = 0;
     int kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
-    const float* weight = nullptr;        // [ceil(cout/8)][kh][kw][cin][8]
+    int co_tile = 8;                      // output channels per thread: 8 or 16
+    const float* weight = nullptr;        // [ceil(cout/co_tile)][kh][kw][cin][co_tile]
     const float* bias = nullptr;          // [cout]
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
