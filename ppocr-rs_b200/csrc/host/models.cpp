@@ -293,6 +293,32 @@ public:
         return out;
     }
 
+    // Fused LCNet channel pair (rowgemm.cu) where its register tile fits.
+    bool pair_rows_ok(int c_in, int c_out) const { return !tensor_core_f32() && pair_rows_supported(c_in, c_out); }
+
+    Act4 pair(const std::string& name, const ConvWeight& pw1, const ConvWeight& pw2, const Act4& x, int gate, bool residual) {
+        const int c = pw1.cin, h = pw1.cout, co = pw2.cout;
+        if (pw2.cin != h || x.c != c || (residual && co != c)) fail(PPOCR_ERR_INVALID_MODEL, name + ": pair weights do not match");
+        Act4 out = tensor(name, x.n, x.h, x.w, co);
+        std::vector<float> w2t((size_t)h * co);
+        for (int o = 0; o < co; ++o)
+            for (int j = 0; j < h; ++j) w2t[(size_t)j * co + o] = pw2.w[(size_t)o * h + j];
+        const size_t o1 = m_.blob.add_f32(pw1.w), o2 = m_.blob.add_f32(w2t);
+        const size_t ob1 = m_.blob.add_f32(pw1.b), ob2 = m_.blob.add_f32(pw2.b);
+        PairRowsParams p;
+        p.m = (long long)x.n * x.h * x.w;
+        p.c_in = c; p.c_out = co; p.rows_per_image = x.h * x.w; p.residual = residual ? 1 : 0; p.dtype = m_.dtype;
+        const int xt = x.tid, ot = out.tid;
+        m_.plan.add_op(name, {xt, gate}, {ot}, [p, o1, o2, ob1, ob2, xt, gate, ot](const Ctx& ctx, cudaStream_t st) mutable {
+            p.a = ctx.act(xt);
+            p.gate = gate >= 0 ? static_cast<const float*>(ctx.act(gate)) : nullptr;
+            p.w1t = ctx.wf(o1); p.w2 = ctx.wf(o2); p.b1 = ctx.wf(ob1); p.b2 = ctx.wf(ob2);
+            p.c = ctx.act(ot);
+            return launch_pair_rows(p, st);
+        }, "gemm", (double)(pw1.w.size() + w2t.size()) * 4, 2.0 * p.m * ((double)c * h + (double)h * co));
+        return out;
+    }
+
     // SE gate of `x` (channel_sum + se_mlp); returns an FP32 [n][c] tensor id.
     int se_gate(const std::string& name, const Act4& x, const ConvWeight& reduce, const ConvWeight& expand, float alpha) {
         const int n = x.n, c = x.c, hw = x.h * x.w, r = reduce.cout, xt = x.tid;
@@ -387,6 +413,12 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
         const int c = blk.cin;
         gate = b.se_gate(prefix + ".se", y, r.conv(prefix + ".token_squeeze_excitation.convolutions.0", c / 4, c, 1, 1, true),
                          r.conv(prefix + ".token_squeeze_excitation.convolutions.2", c, c / 4, 1, 1, true), 1.f / 6.f);
+    }
+    if (b.pair_rows_ok(blk.cin, blk.cout)) {
+        return b.pair(prefix + ".pair", r.conv_bn(prefix + ".channel_conv1", blk.cin * 2, blk.cin, 1, 1, false),
+                      r.conv_bn(prefix + ".channel_conv2", blk.cout, blk.cin * 2, 1, 1, false), y, gate, blk.residual());
+    }
+    if (gate >= 0) {
         if (b.tensor_core_gemms()) {
             y = b.gate_apply(prefix + ".se.apply", y, gate, 0, nullptr, 1);
             gate = -1;

@@ -9,6 +9,7 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
 
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
     if (p.w_tc && gemm_tc_supported(p)) return launch_gemm_tc(p, stream);
+    if (rows_gemm_supported(p)) return launch_rows_gemm(p, stream);
     return launch_gemm_simt(p, stream);
 }
 

@@ -110,21 +110,28 @@ struct GemmParams {
 };
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream);
 
-// Pointwise pair C = W2 * GELU(W1 * A + b1) + b2 (+ A), the hidden 2C tile
-// kept on chip (LCNet channel_conv1 / channel_conv2, src/cpu/backend.rs:443-695).
-struct PairParams {
-    int m = 0, cin = 0, hidden = 0, cout = 0;
-    const void* a = nullptr;
-    const float* gate = nullptr;
+// Pointwise pair out = W2 GELU(W1 (A*gate) + b1) + b2 (+ A*gate), one pixel
+// row per thread with the 2C hidden units kept in registers (LCNet
+// channel_conv1 / channel_conv2, src/cpu/backend.rs:443-695).  rowgemm.cu.
+struct PairRowsParams {
+    long long m = 0;
+    int c_in = 0, c_out = 0;
+    const void* a = nullptr;          // [m][c_in]
+    const float* gate = nullptr;      // [images][c_in] or null
     int rows_per_image = 1;
-    const void* w1_tc = nullptr;      // BF16 [hidden][cin]
-    const void* w2_tc = nullptr;      // BF16 [cout][hidden]
-    const float* b1 = nullptr;
-    const float* b2 = nullptr;
-    int residual = 0;
-    void* c = nullptr;
-    DType dtype = DT_BF16;
+    const float* w1t = nullptr;       // [2 c_in][c_in]
+    const float* w2 = nullptr;        // [2 c_in][c_out]
+    const float* b1 = nullptr;        // [2 c_in]
+    const float* b2 = nullptr;        // [c_out]
+    int residual = 0;                 // add the gated input (c_out == c_in)
+    void* c = nullptr;                // [m][c_out]
+    DType dtype = DT_F32;
 };
+bool pair_rows_supported(int c_in, int c_out);
+cudaError_t launch_pair_rows(const PairRowsParams& p, cudaStream_t stream);
+// Row-per-thread pointwise GEMM for N <= 128 (rowgemm.cu).
+bool rows_gemm_supported(const GemmParams& p);
+cudaError_t launch_rows_gemm(const GemmParams& p, cudaStream_t stream);
 
 // Tensor-core (tcgen05) GEMM availability: BF16 storage, k_pad % 64 == 0, n_pad % 16 == 0.
 bool gemm_tc_supported(const GemmParams& p);
