@@ -142,13 +142,19 @@ public:
     }
 
     // Dense conv over up to four concatenated sources (conv.cu).
+    // `into` (optional): write into channels [into_coff, into_coff + cout) of an
+    // existing wider tensor instead of a new one (a concatenation slice).
     Act4 conv(const std::string& name, const ConvWeight& cw, const std::vector<Src>& srcs, int n, int hi, int wi, int sh,
-              int sw, int pt, int pl, int pb, int pr, int act, int residual = -1, int res_scale = 1) {
+              int sw, int pt, int pl, int pb, int pr, int act, int residual = -1, int res_scale = 1,
+              const Act4* into = nullptr, int into_coff = 0) {
         int cin = 0;
         for (auto& s : srcs) cin += s.channels;
         if (cin != cw.cin) fail(PPOCR_ERR_INVALID_MODEL, name + ": conv input channels do not match the weight");
         const int ho = out_size(hi, cw.kh, sh, pt, pb), wo = out_size(wi, cw.kw, sw, pl, pr);
-        Act4 out = tensor(name, n, ho, wo, cw.cout);
+        if (into && (into->n != n || into->h != ho || into->w != wo || into_coff % 4 || into_coff + cw.cout > into->c))
+            fail(PPOCR_ERR_INVALID_MODEL, name + ": concatenation slice does not fit");
+        Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
+        const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
         if (tensor_core_f32()) {
             TcConvParams tp;
             tp.mode = 1;
@@ -165,7 +171,8 @@ public:
             tp.res_scale = res_scale;
             tp.out_h = ho; tp.out_w = wo;
             tp.rows_per_image = ho * wo;
-            tp.ldc = cw.cout;
+            tp.ldc = out_cstride;
+            tp.coff = out_coff;
             tc_f32_op(name, cw, tp, srcs, -1, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
             return out;
         }
@@ -180,7 +187,7 @@ public:
         p.n = n; p.hi = hi; p.wi = wi; p.cin = cin; p.nsrc = (int)srcs.size();
         p.ho = ho; p.wo = wo; p.cout = cw.cout;
         p.kh = cw.kh; p.kw = cw.kw; p.sh = sh; p.sw = sw; p.pt = pt; p.pl = pl;
-        p.act = act; p.res_scale = res_scale; p.out_cstride = cw.cout; p.out_coff = 0; p.dtype = m_.dtype;
+        p.act = act; p.res_scale = res_scale; p.out_cstride = out_cstride; p.out_coff = out_coff; p.dtype = m_.dtype;
         p.co_tile = co_tile;
         std::vector<int> reads;
         for (size_t i = 0; i < srcs.size(); ++i) {
@@ -203,9 +210,21 @@ public:
     }
 
     Act4 conv1(const std::string& name, const ConvWeight& cw, const Act4& in, int sh, int sw, int pt, int pl, int pb, int pr,
-               int act, int residual = -1, int res_scale = 1) {
+               int act, int residual = -1, int res_scale = 1, const Act4* into = nullptr, int into_coff = 0) {
         return conv(name, cw, {{in.tid, in.c, in.c, 0, 1, SRC_NHWC}}, in.n, in.h, in.w, sh, sw, pt, pl, pb, pr, act, residual,
-                    res_scale);
+                    res_scale, into, into_coff);
+    }
+
+    // 2x2 stride-1 "same-upper" max pool of `x` into channels [coff, coff + x.c) of `into`.
+    void maxpool_into(const std::string& name, const Act4& x, const Act4& into, int coff) {
+        MaxPoolParams p;
+        p.n = x.n; p.h = x.h; p.w = x.w; p.c = x.c; p.out_cstride = into.c; p.out_coff = coff; p.dtype = m_.dtype;
+        const int xt = x.tid, ot = into.tid;
+        m_.plan.add_op(name, {xt}, {ot}, [p, xt, ot](const Ctx& c, cudaStream_t st) mutable {
+            p.in = c.act(xt);
+            p.out = c.act(ot);
+            return launch_maxpool_same_upper(p, st);
+        }, "pool", 0, 3.0 * x.n * x.h * x.w * x.c);
     }
 
     // Depthwise conv (dwconv.cu).  cw is [C, 1, kh, kw].
@@ -383,11 +402,13 @@ Act4 large_stem(Builder& b, int in_tid, int n, int h, int w, int mid, int out) {
     Act4 e = b.conv("stem1", r.conv_bn(p + "stem1", mid, 3, 3, 3, false), {{in_tid, 3, 3, 0, 1, SRC_NCHW_F32}}, n, h, w, 2, 2,
                     1, 1, 1, 1, ACT_RELU);
     Act4 br = b.conv1("stem2a", r.conv_bn(p + "stem2a", mid / 2, mid, 2, 2, false), e, 1, 1, 0, 0, 1, 1, ACT_RELU);
-    br = b.conv1("stem2b", r.conv_bn(p + "stem2b", mid, mid / 2, 2, 2, false), br, 1, 1, 0, 0, 1, 1, ACT_RELU);
-    // cat(max_pool_same_upper(stem1), stem2b) is read in place by stem3.
-    Act4 x = b.conv("stem3", r.conv_bn(p + "stem3", mid, mid * 2, 3, 3, false),
-                    {{e.tid, mid, mid, 0, 1, SRC_NHWC_MAXPOOL}, {br.tid, mid, mid, 0, 1, SRC_NHWC}}, n, e.h, e.w, 2, 2, 1, 1, 1, 1,
-                    ACT_RELU);
+    // cat(max_pool_same_upper(stem1), stem2b) is materialised once: the pool
+    // writes channels [0, mid) and stem2b channels [mid, 2 mid) of one tensor,
+    // so stem3's 3x3 window reads plain pixels instead of re-pooling per tap.
+    Act4 cat = b.tensor("stem.cat", n, e.h, e.w, 2 * mid);
+    b.maxpool_into("stem.pool", e, cat, 0);
+    b.conv1("stem2b", r.conv_bn(p + "stem2b", mid, mid / 2, 2, 2, false), br, 1, 1, 0, 0, 1, 1, ACT_RELU, -1, 1, &cat, mid);
+    Act4 x = b.conv1("stem3", r.conv_bn(p + "stem3", mid, mid * 2, 3, 3, false), cat, 2, 2, 1, 1, 1, 1, ACT_RELU);
     GemmOpts o;
     o.act = ACT_RELU;
     return b.pointwise("stem4", r.conv_bn(p + "stem4", out, mid, 1, 1, false), x, o);

@@ -42,16 +42,23 @@ struct TcArgs {
     int ldc, coff, c_f32;
 };
 
-template <typename T>
+template <typename T, int ACT>
 __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, const float (&v)[16]) {
     float o[16];
     const bool full = col0 + 16 <= p.n;
+    if (p.bias && full) {
+        // 16 consecutive biases as four 16-byte loads (col0 is a multiple of 16).
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        float a = v[j];
-        if (p.bias && (full || col0 + j < p.n)) a += p.bias[col0 + j];
-        o[j] = apply_act(a, p.act);
+        for (int j = 0; j < 16; j += 4) {
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+            o[j] = v[j] + b.x; o[j + 1] = v[j + 1] + b.y; o[j + 2] = v[j + 2] + b.z; o[j + 3] = v[j + 3] + b.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = v[j] + ((p.bias && col0 + j < p.n) ? p.bias[col0 + j] : 0.f);
     }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = apply_act_fast<ACT>(o[j]);
     if (p.residual) {
         size_t rrow = (size_t)row;
         if (p.res_scale > 1) {
@@ -91,6 +98,7 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
     }
 }
 
+template <int ACT>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
                                                              const __grid_constant__ CUtensorMap tma_b, TcArgs p) {
     extern __shared__ uint8_t smem_raw[];
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                 const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * p.bn;
                 for (int kt = 0; kt < p.kt; ++kt, ++it) {
                     const int s = it % S;
-                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1)) {
+                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false)) {
                         atomicExch(&g_tc_error, 1);
                         abort_flag = 1;
                         break;
@@ -148,7 +156,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x, ++ti) {
                 const int b = ti & 1;
-                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1)) {
+                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false)) {
                     atomicExch(&g_tc_error, 2);
                     abort_flag = 1;
                     break;
@@ -158,7 +166,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                 bool ok = true;
                 for (int kt = 0; kt < p.kt; ++kt, ++it) {
                     const int s = it % S;
-                    if (!tc::mbar_wait(&full_bar[s], (it / S) & 1)) {
+                    if (!tc::mbar_wait(&full_bar[s], (it / S) & 1, false)) {
                         atomicExch(&g_tc_error, 3);
                         abort_flag = 1;
                         ok = false;
@@ -203,7 +211,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    epilogue16<__nv_bfloat16>(p, row, col, v);
+                    epilogue16<__nv_bfloat16, ACT>(p, row, col, v);
                 }
             }
             tc::fence_before();
@@ -251,6 +259,19 @@ int pick_bn(int n) {
     return (bn + 31) / 32 * 32;
 }
 
+template <int ACT>
+cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, int grid, size_t smem,
+                       cudaStream_t stream) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    gemm_tc_kernel<ACT><<<grid, THREADS, smem, stream>>>(ma, mb, a);
+    return cudaGetLastError();
+}
+
 int sm_count() {
     static int n = 0;
     if (!n) {
@@ -291,16 +312,17 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
     a.residual = p.residual; a.ldr = p.ldr; a.res_scale = p.res_scale; a.h = p.h; a.w_px = p.w_px;
     a.c = p.c; a.ldc = p.ldc; a.coff = p.coff; a.c_f32 = p.c_f32;
     const size_t smem = (size_t)a.stages * stage_bytes + 1024;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_tc_kernel<<<grid, THREADS, smem, stream>>>(ma, mb, a);
-    return cudaGetLastError();
+    switch (p.act) {
+        case ACT_NONE: return launch_act<ACT_NONE>(ma, mb, a, grid, smem, stream);
+        case ACT_RELU: return launch_act<ACT_RELU>(ma, mb, a, grid, smem, stream);
+        case ACT_SILU: return launch_act<ACT_SILU>(ma, mb, a, grid, smem, stream);
+        case ACT_GELU: return launch_act<ACT_GELU>(ma, mb, a, grid, smem, stream);
+        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mb, a, grid, smem, stream);
+        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mb, a, grid, smem, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 int gemm_tc_error_and_clear() {

@@ -238,6 +238,17 @@ struct HeadParams {
 };
 cudaError_t launch_det_head(const HeadParams& p, cudaStream_t stream);
 
+// 2x2 stride-1 max pool padded at the bottom / right (pads never win;
+// src/cpu/ops.rs:1520-1535), written into a channel slice of `out`.
+struct MaxPoolParams {
+    int n = 0, h = 0, w = 0, c = 0;
+    const void* in = nullptr;       // [n, h, w, c] tight
+    void* out = nullptr;
+    int out_cstride = 0, out_coff = 0;
+    DType dtype = DT_F32;
+};
+cudaError_t launch_maxpool_same_upper(const MaxPoolParams& p, cudaStream_t stream);
+
 // ---------------------------------------------------------------------------
 // Recognizer ops
 // ---------------------------------------------------------------------------

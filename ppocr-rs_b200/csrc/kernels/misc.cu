@@ -164,6 +164,30 @@ __global__ void __launch_bounds__(128) det_head_kernel(HeadParams p) {
     }
 }
 
+template <typename T>
+__global__ void __launch_bounds__(256) maxpool_su_kernel(MaxPoolParams p) {
+    const int cg = p.c / 4;
+    const long long total = (long long)p.n * p.h * p.w * cg;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(idx % cg) * 4;
+        const long long pix = idx / cg;
+        const int x = (int)(pix % p.w), y = (int)((pix / p.w) % p.h);
+        const T* in = static_cast<const T*>(p.in);
+        const size_t base = (size_t)pix * p.c + c;
+        float4 m = load4(in + base);
+        auto mx = [](float4 a, float4 b) {
+            return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+        };
+        if (x + 1 < p.w) m = mx(m, load4(in + base + p.c));
+        if (y + 1 < p.h) {
+            m = mx(m, load4(in + base + (size_t)p.w * p.c));
+            if (x + 1 < p.w) m = mx(m, load4(in + base + (size_t)p.w * p.c + p.c));
+        }
+        store4(static_cast<T*>(p.out) + (size_t)pix * p.out_cstride + p.out_coff + c, m);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Recognizer ops
 // ---------------------------------------------------------------------------
@@ -471,6 +495,14 @@ static cudaError_t launch_head_t(const HeadParams& p, cudaStream_t stream) {
 
 cudaError_t launch_det_head(const HeadParams& p, cudaStream_t stream) {
     return p.dtype == DT_F32 ? launch_head_t<float>(p, stream) : launch_head_t<__nv_bfloat16>(p, stream);
+}
+
+cudaError_t launch_maxpool_same_upper(const MaxPoolParams& p, cudaStream_t stream) {
+    if (p.c % 4 || p.out_cstride % 4 || p.out_coff % 4) return cudaErrorInvalidValue;
+    const unsigned g = grid_for((long long)p.n * p.h * p.w * (p.c / 4), 256);
+    if (p.dtype == DT_F32) maxpool_su_kernel<float><<<g, 256, 0, stream>>>(p);
+    else maxpool_su_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_avgpool_3x2(const AvgPoolParams& p, cudaStream_t stream) {

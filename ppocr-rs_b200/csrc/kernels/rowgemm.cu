@@ -22,7 +22,8 @@ namespace {
 
 constexpr int kRows = 128;   // threads (= rows) per block
 
-template <typename T, int C, int CO>
+// R pixel rows per thread: every shared-memory weight load feeds R rows.
+template <typename T, int C, int CO, int R>
 __global__ void __launch_bounds__(kRows) pair_rows_kernel(PairRowsParams p) {
     constexpr int H = 2 * C;
     extern __shared__ float4 psm[];
@@ -37,52 +38,73 @@ __global__ void __launch_bounds__(kRows) pair_rows_kernel(PairRowsParams p) {
     for (int i = threadIdx.x; i < H; i += kRows) b1[i] = p.b1[i];
     for (int i = threadIdx.x; i < CO; i += kRows) b2[i] = p.b2[i];
     __syncthreads();
-    const long long row = (long long)blockIdx.x * kRows + threadIdx.x;
-    if (row >= p.m) return;
-    float a[C];
-    const T* src = static_cast<const T*>(p.a) + (size_t)row * C;
-    const float* g = p.gate ? p.gate + (size_t)(row / p.rows_per_image) * C : nullptr;
+    const long long row0 = (long long)blockIdx.x * kRows * R + threadIdx.x;   // rows row0 + r * kRows
+    if (row0 >= p.m) return;
+    float a[R][C];
 #pragma unroll
-    for (int k = 0; k < C; k += 4) {
-        float4 v = load4(src + k);
-        if (g) v = f4_mul(v, *reinterpret_cast<const float4*>(g + k));
-        a[k] = v.x; a[k + 1] = v.y; a[k + 2] = v.z; a[k + 3] = v.w;
+    for (int r = 0; r < R; ++r) {
+        const long long row = row0 + (long long)r * kRows < p.m ? row0 + (long long)r * kRows : row0;
+        const T* src = static_cast<const T*>(p.a) + (size_t)row * C;
+        const float* g = p.gate ? p.gate + (size_t)(row / p.rows_per_image) * C : nullptr;
+#pragma unroll
+        for (int k = 0; k < C; k += 4) {
+            float4 v = load4(src + k);
+            if (g) v = f4_mul(v, *reinterpret_cast<const float4*>(g + k));
+            a[r][k] = v.x; a[r][k + 1] = v.y; a[r][k + 2] = v.z; a[r][k + 3] = v.w;
+        }
     }
-    float out[CO];
+    float out[R][CO];
 #pragma unroll
-    for (int o = 0; o < CO; ++o) out[o] = 0.f;
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int o = 0; o < CO; ++o) out[r][o] = 0.f;
 #pragma unroll 2
     for (int j = 0; j < H; ++j) {
         const float* wj = w1t + j * C;
-        float h = 0.f;
+        float h[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) h[r] = 0.f;
 #pragma unroll
         for (int k = 0; k < C; k += 4) {
             const float4 w = *reinterpret_cast<const float4*>(wj + k);
-            h = fmaf(a[k], w.x, h);
-            h = fmaf(a[k + 1], w.y, h);
-            h = fmaf(a[k + 2], w.z, h);
-            h = fmaf(a[k + 3], w.w, h);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                h[r] = fmaf(a[r][k], w.x, h[r]);
+                h[r] = fmaf(a[r][k + 1], w.y, h[r]);
+                h[r] = fmaf(a[r][k + 2], w.z, h[r]);
+                h[r] = fmaf(a[r][k + 3], w.w, h[r]);
+            }
         }
-        h = apply_act(h + b1[j], ACT_GELU);
+#pragma unroll
+        for (int r = 0; r < R; ++r) h[r] = apply_act(h[r] + b1[j], ACT_GELU);
         const float* w2j = w2 + j * CO;
 #pragma unroll
         for (int o = 0; o < CO; o += 4) {
             const float4 w = *reinterpret_cast<const float4*>(w2j + o);
-            out[o] = fmaf(h, w.x, out[o]);
-            out[o + 1] = fmaf(h, w.y, out[o + 1]);
-            out[o + 2] = fmaf(h, w.z, out[o + 2]);
-            out[o + 3] = fmaf(h, w.w, out[o + 3]);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                out[r][o] = fmaf(h[r], w.x, out[r][o]);
+                out[r][o + 1] = fmaf(h[r], w.y, out[r][o + 1]);
+                out[r][o + 2] = fmaf(h[r], w.z, out[r][o + 2]);
+                out[r][o + 3] = fmaf(h[r], w.w, out[r][o + 3]);
+            }
         }
     }
-    T* dst = static_cast<T*>(p.c) + (size_t)row * CO;
 #pragma unroll
-    for (int o = 0; o < CO; o += 4) {
-        float4 v = make_float4(out[o] + b2[o], out[o + 1] + b2[o + 1], out[o + 2] + b2[o + 2], out[o + 3] + b2[o + 3]);
-        if (p.residual) {
-            // CO == C: the residual is the gated input row (src/cpu/backend.rs:504-521).
-            v.x += a[o % C]; v.y += a[(o + 1) % C]; v.z += a[(o + 2) % C]; v.w += a[(o + 3) % C];
+    for (int r = 0; r < R; ++r) {
+        const long long row = row0 + (long long)r * kRows;
+        if (row >= p.m) break;
+        T* dst = static_cast<T*>(p.c) + (size_t)row * CO;
+#pragma unroll
+        for (int o = 0; o < CO; o += 4) {
+            float4 v = make_float4(out[r][o] + b2[o], out[r][o + 1] + b2[o + 1], out[r][o + 2] + b2[o + 2],
+                                   out[r][o + 3] + b2[o + 3]);
+            if (p.residual) {
+                // CO == C: the residual is the gated input row (src/cpu/backend.rs:504-521).
+                v.x += a[r][o % C]; v.y += a[r][(o + 1) % C]; v.z += a[r][(o + 2) % C]; v.w += a[r][(o + 3) % C];
+            }
+            store4(dst + o, v);
         }
-        store4(dst + o, v);
     }
 }
 
@@ -150,14 +172,15 @@ __global__ void __launch_bounds__(kRows) rows_gemm_kernel(GemmParams p) {
 
 template <typename T, int C, int CO>
 cudaError_t launch_pair(const PairRowsParams& p, cudaStream_t stream) {
+    constexpr int R = (C + CO <= 64) ? 2 : 1;
     const size_t smem = ((size_t)2 * C * C + (size_t)2 * C * CO + 2 * C + CO) * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(pair_rows_kernel<T, C, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(pair_rows_kernel<T, C, CO, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    pair_rows_kernel<T, C, CO><<<(unsigned)((p.m + kRows - 1) / kRows), kRows, smem, stream>>>(p);
+    pair_rows_kernel<T, C, CO, R><<<(unsigned)((p.m + kRows * R - 1) / (kRows * R)), kRows, smem, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -30,9 +30,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // Bounded parity wait: true when the phase completed, false on expiry.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// `backoff` threads (epilogue warps) sleep between polls; the single TMA and
+// MMA issuing threads poll without sleeping so the pipeline is not delayed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, bool backoff = true) {
     const uint32_t addr = smem_u32(bar);
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    const uint32_t limit = backoff ? kWaitLimit : kWaitLimit * 8;
+    for (uint32_t i = 0; i < limit; ++i) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -42,7 +45,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if (i > 32) __nanosleep(64);
+        if (backoff && i > 32) __nanosleep(64);
     }
     return false;
 }
