@@ -204,7 +204,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     import ppocr_b200 as P
-    from ppocr_b200 import seeded
+    from ppocr_b200 import seeded, sharding
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -259,10 +259,7 @@ def run_b200(args):
         barrier()
         wall = time.perf_counter() - w0
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
-    total_ms = float(total_ms.item())
+    total_ms = sharding.max_over_ranks(sum(step_ms))
     units = shape[0] * world * args.steps
     value = units / (total_ms / 1000.0)
 

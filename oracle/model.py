@@ -6,10 +6,11 @@ src/cpu/backend.rs, src/cpu/ops.rs, src/cpu/kernels/mod.rs).  It is the
 checker for the CUDA path: only tests/, __graft_entry__.smoke() and bench.py's
 CPU-baseline leg import it.  The product never calls into it.
 
-Parity status: the reference cannot be compiled or run here (Rust toolchain
-absent, wgpu GPU path needs a graphics API), so model-level parity is pinned
-by this restatement plus the reference's own known-answer tests, which
-tests/test_oracle.py re-expresses against these functions.
+Parity status: unpinned against execution of the reference.  The reference
+cannot be compiled or run here (Rust toolchain absent, wgpu GPU path needs a
+graphics API), so model-level parity rests on this restatement plus the
+reference's own known-answer tests, which tests/test_oracle.py re-expresses
+against these functions.
 
 Convolutions use torch's CPU FP32 conv (exact FP32 products and sums, only
 the summation order differs from the reference's packed AVX2 GEMMs); every
