@@ -201,6 +201,18 @@ int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms);
 int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                         int act, float* c, int* used_tensor_cores, int* wait_error);
 
+/* Diagnostic (new): ppocr_selftest_gemm writing into a channel slice of a
+ * wider output, with an optional residual, as the model's concat and
+ * residual epilogues do.  C is [m][ldc] (ldc >= coff + n); its initial
+ * contents come from `c` and columns outside [coff, coff + n) must come back
+ * unchanged.  residual (may be NULL) is [m][n], added after the activation.
+ * out_bf16 = 1 stores C (and reads the residual) as BF16, 0 as F32 output
+ * with a BF16 residual.  act as for ppocr_selftest_gemm, plus 4 HardSwish,
+ * 5 sigmoid. */
+int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
+                           int act, const float* residual, int out_bf16, int ldc, int coff, float* c,
+                           int* used_tensor_cores, int* wait_error);
+
 /* Recognizer only: the classifier's pre-softmax logits [n, t, classes]
  * (new; the reference fuses the softmax, src/cpu/backend.rs:1288-1290, so it
  * never exposes them). */

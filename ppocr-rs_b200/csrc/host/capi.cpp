@@ -144,16 +144,21 @@ void upload_and_run(ppocr_model* model, const float* input, size_t len) {
 // Enqueues the output scan and the flag readback, waits, and raises the
 // reference's errors: InvalidInput for a non-finite input, Error::Gpu for a
 // non-finite output (src/gpu/runtime.rs:2217-2219).
-void finish(ppocr_model* model, int checked_tid, size_t checked_count) {
+// Reads the device flags after a forward; `checked_tid` (if any) is checked
+// for non-finite values first, as `rows` rows of `cols` floats at stride `ld`.
+void finish(ppocr_model* model, int checked_tid, size_t rows, size_t cols, size_t ld) {
     cudaStream_t s = model->gpu->stream;
     if (checked_tid >= 0)
-        cuda_check(launch_check_finite(static_cast<const float*>(model->tensor(checked_tid)), checked_count, model->dflags + 1, s),
+        cuda_check(launch_check_finite_rows(static_cast<const float*>(model->tensor(checked_tid)), rows, cols, ld,
+                                            model->dflags + 1, s),
                    "check output");
     cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
     wait_stream(s, 0);
     if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
     if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
 }
+
+void finish(ppocr_model* model, int checked_tid, size_t checked_count) { finish(model, checked_tid, 1, checked_count, checked_count); }
 
 }  // namespace
 
@@ -632,6 +637,68 @@ int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, con
     });
 }
 
+int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias, int act,
+                           const float* residual, int out_bf16, int ldc, int coff, float* c, int* used_tensor_cores,
+                           int* wait_error) {
+    return guard([&] {
+        if (!gpu || !a || !w || !c) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (m <= 0 || n <= 0 || k <= 0 || k % 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: GEMM shape (k must be a multiple of 4)");
+        if (coff < 0 || ldc < coff + n) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: ldc must cover coff + n");
+        if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        const int kp = (k + 63) / 64 * 64, np = (n + 15) / 16 * 16;
+        ConvWeight cw;
+        cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
+        cw.w.assign(w, w + (size_t)n * k);
+        cw.b = bias ? std::vector<float>(bias, bias + n) : std::vector<float>(n, 0.f);
+        int n_pad4 = 0;
+        WeightBlob blob;
+        const size_t wf = blob.add_f32(pack_gemm_kn(cw, n_pad4));
+        const size_t bo = blob.add_f32(cw.b);
+        const size_t wt = blob.add_bf16(pack_gemm_nk(cw, np, kp));
+        const size_t ao = blob.add_bf16(std::vector<float>(a, a + (size_t)m * k));
+        const size_t ro = residual ? blob.add_bf16(std::vector<float>(residual, residual + (size_t)m * n)) : 0;
+        const size_t celems = (size_t)m * ldc;
+        const std::vector<float> cinit(c, c + celems);
+        const size_t co = out_bf16 ? blob.add_bf16(cinit) : blob.add_f32(cinit);
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate GEMM test buffers");
+        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        GemmParams p;
+        p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad4; p.k_pad = kp;
+        p.a = d + ao; p.w = reinterpret_cast<const float*>(d + wf); p.w_tc = d + wt;
+        p.bias = reinterpret_cast<const float*>(d + bo); p.act = act;
+        p.residual = residual ? d + ro : nullptr; p.ldr = n;
+        p.c = d + co; p.ldc = ldc; p.coff = coff; p.c_f32 = out_bf16 ? 0 : 1; p.dtype = DT_BF16;
+        const bool tc = gemm_tc_supported(p);
+        std::vector<uint16_t> hb(out_bf16 ? celems : 0);
+        if (e == cudaSuccess) e = launch_gemm(p, gpu->stream);
+        if (e == cudaSuccess)
+            e = out_bf16 ? cudaMemcpyAsync(hb.data(), p.c, celems * 2, cudaMemcpyDeviceToHost, gpu->stream)
+                         : cudaMemcpyAsync(c, p.c, celems * 4, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "GEMM self-test");
+        if (out_bf16)
+            for (size_t i = 0; i < celems; ++i) {
+                const uint32_t u = (uint32_t)hb[i] << 16;
+                std::memcpy(c + i, &u, 4);
+            }
+        if (used_tensor_cores) *used_tensor_cores = tc ? 1 : 0;
+        const int err = gemm_tc_error_and_clear();
+        if (wait_error) *wait_error = err;
+    });
+}
+
 int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
                         const float* x, const float* w, const float* bias, int act, float* out, int* used_tensor_cores,
                         int* wait_error) {
@@ -709,8 +776,12 @@ int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size
         std::lock_guard<std::mutex> lock(model->gpu->mu);
         model->gpu->bind();
         upload_and_run(model, input, input_len);
-        download(model, model->m.logits, logits, model->m.output_elements * 4);
-        finish(model, model->m.logits, model->m.output_elements);
+        const size_t classes = (size_t)model->m.classes, ld = (size_t)model->m.logits_ld;
+        const size_t rows = model->m.output_elements / classes;
+        cuda_check(cudaMemcpy2DAsync(logits, classes * 4, model->tensor(model->m.logits), ld * 4, classes * 4, rows,
+                                     cudaMemcpyDeviceToHost, model->gpu->stream),
+                   "read logits");
+        finish(model, model->m.logits, rows, classes, ld);
     });
 }
 

@@ -83,6 +83,7 @@ struct GemmOpts {
     int res_scale = 1, h = 1, w = 1;
     bool c_f32 = false;
     bool has_bias = true;
+    int ldc = 0;              // output row stride (0: cout)
 };
 
 class Builder {
@@ -176,19 +177,11 @@ public:
             tc_f32_op(name, cw, tp, srcs, -1, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
             return out;
         }
-        // 16 output channels per thread when cout >= 16 (the head's and stems' input
-        // windows are then read once per 16 channels instead of once per 8).
-        const int co_tile = cw.cout >= 16 ? 16 : 8;
-        const size_t woff = m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
-        std::vector<float> bias = cw.b;
-        bias.resize((cw.cout + co_tile - 1) / co_tile * co_tile, 0.f);
-        const size_t boff = m_.blob.add_f32(bias);
         ConvParams p;
         p.n = n; p.hi = hi; p.wi = wi; p.cin = cin; p.nsrc = (int)srcs.size();
         p.ho = ho; p.wo = wo; p.cout = cw.cout;
         p.kh = cw.kh; p.kw = cw.kw; p.sh = sh; p.sw = sw; p.pt = pt; p.pl = pl;
         p.act = act; p.res_scale = res_scale; p.out_cstride = out_cstride; p.out_coff = out_coff; p.dtype = m_.dtype;
-        p.co_tile = co_tile;
         std::vector<int> reads;
         for (size_t i = 0; i < srcs.size(); ++i) {
             p.src[i].channels = srcs[i].channels; p.src[i].cstride = srcs[i].cstride; p.src[i].coff = srcs[i].coff;
@@ -196,11 +189,26 @@ public:
             reads.push_back(srcs[i].tid);
         }
         reads.push_back(residual);
+        // BF16 storage: NHWC sources run as a register-tiled implicit GEMM
+        // (gemm_simt.cu).  FP32 storage and the NCHW image input take the direct
+        // kernel (measured faster for the detector's 16-channel FP32 convs), 16
+        // output channels per thread when cout >= 16 (8 otherwise).  Both
+        // accumulate each output in (ky, kx, channel) order.
+        const bool gemm = m_.dtype == DT_BF16 && conv_gemm_supported(p);
+        const int co_tile = cw.cout >= 16 ? 16 : 8;
+        int n_pad = 0;
+        const size_t woff = gemm ? m_.blob.add_f32(pack_conv_kn(cw, n_pad)) : m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
+        std::vector<float> bias = cw.b;
+        bias.resize((cw.cout + co_tile - 1) / co_tile * co_tile, 0.f);
+        const size_t boff = m_.blob.add_f32(bias);
+        p.co_tile = co_tile;
+        p.n_pad = n_pad;
         const int otid = out.tid;
         std::vector<Src> s2 = srcs;
-        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid](const Ctx& c, cudaStream_t st) mutable {
+        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid, gemm](const Ctx& c, cudaStream_t st) mutable {
             for (size_t i = 0; i < s2.size(); ++i) p.src[i].ptr = c.act(s2[i].tid);
-            p.weight = c.wf(woff);
+            p.weight = gemm ? nullptr : c.wf(woff);
+            p.weight_kn = gemm ? c.wf(woff) : nullptr;
             p.bias = c.wf(boff);
             p.residual = c.act(residual);
             p.out = c.act(otid);
@@ -264,7 +272,7 @@ public:
             tp.ldr = cw.cout;
             tp.res_scale = o.res_scale;
             tp.out_h = o.h; tp.out_w = o.w;
-            tp.ldc = cw.cout;
+            tp.ldc = o.ldc ? o.ldc : cw.cout;
             ConvWeight flat = cw;
             flat.cin = k; flat.kh = 1; flat.kw = 1;
             if (!o.has_bias) flat.b.assign(cw.cout, 0.f);
@@ -277,7 +285,7 @@ public:
         GemmParams p;
         p.m = rows; p.n = cw.cout; p.k = k; p.lda = k; p.n_pad = n_pad;
         p.rows_per_image = o.rows_per_image; p.act = o.act; p.ldr = cw.cout;
-        p.res_scale = o.res_scale; p.h = o.h; p.w_px = o.w; p.ldc = cw.cout; p.coff = 0; p.dtype = m_.dtype;
+        p.res_scale = o.res_scale; p.h = o.h; p.w_px = o.w; p.ldc = o.ldc ? o.ldc : cw.cout; p.coff = 0; p.dtype = m_.dtype;
         p.c_f32 = o.c_f32 ? 1 : 0;
         const bool tc = tc_ && m_.dtype == DT_BF16;
         size_t tcoff = 0;
@@ -341,7 +349,7 @@ public:
     // SE gate of `x` (channel_sum + se_mlp); returns an FP32 [n][c] tensor id.
     int se_gate(const std::string& name, const Act4& x, const ConvWeight& reduce, const ConvWeight& expand, float alpha) {
         const int n = x.n, c = x.c, hw = x.h * x.w, r = reduce.cout, xt = x.tid;
-        const int chunks = channel_sum_chunks(hw, c);
+        const int chunks = channel_sum_chunks(n, hw, c);
         const int sum = m_.plan.add_raw(name + ".sum", (size_t)n * chunks * c * 4);
         const int gate = m_.plan.add_raw(name + ".gate", (size_t)n * c * 4);
         const size_t w1 = m_.blob.add_f32(reduce.w), b1 = m_.blob.add_f32(reduce.b);
@@ -625,16 +633,25 @@ void detector_head(Builder& b, const std::vector<Act4>& feats, int channels) {
 // Recognizer heads
 // ---------------------------------------------------------------------------
 
+// Classifier logits with rows padded to a 16-byte pitch (whole-line TMA stores
+// from the GEMM epilogue, 16-byte loads in the softmax).
+int logits_tensor(BuiltModel& m, int rows) {
+    m.logits_ld = (m.classes + 3) / 4 * 4;
+    m.logits = m.plan.add_raw("logits", (size_t)rows * m.logits_ld * 4, true);
+    return m.logits;
+}
+
 void ctc_outputs(Builder& b, int logits_tid, int rows, int classes) {
     BuiltModel& m = b.model();
+    const int ld = m.logits_ld;
     m.probs = m.plan.add_raw("probs", (size_t)rows * classes * 4, true);
     m.index = m.plan.add_raw("index", (size_t)rows * 4, true);
     m.max_prob = m.plan.add_raw("max_prob", (size_t)rows * 4, true);
     m.margin = m.plan.add_raw("margin", (size_t)rows * 4, true);
     const int lt = logits_tid, pt = m.probs, it = m.index, mt = m.max_prob, gt = m.margin;
-    m.plan.add_op("ctc.softmax", {lt}, {pt, it, mt, gt}, [rows, classes, lt, pt, it, mt, gt](const Ctx& c, cudaStream_t st) {
+    m.plan.add_op("ctc.softmax", {lt}, {pt, it, mt, gt}, [rows, classes, ld, lt, pt, it, mt, gt](const Ctx& c, cudaStream_t st) {
         SoftmaxParams p;
-        p.rows = rows; p.classes = classes;
+        p.rows = rows; p.classes = classes; p.ld = ld;
         p.logits = static_cast<const float*>(c.act(lt));
         p.prob = static_cast<float*>(c.act(pt));
         p.index = static_cast<int32_t*>(c.act(it));
@@ -664,9 +681,10 @@ void tiny_rec_head(Builder& b, const Act4& x) {
     h = b.pointwise("head.conv2", c2, h, o);
     h = b.pointwise("head.fc1", r.linear("head.fc1", 160, 80), h, GemmOpts{});
     const int rows = h.n * h.h * h.w;
-    m.logits = m.plan.add_raw("logits", (size_t)rows * m.classes * 4, true);
+    logits_tensor(m, rows);
     GemmOpts of;
     of.c_f32 = true;
+    of.ldc = m.logits_ld;
     of.rows_per_image = h.h * h.w;
     b.gemm_rows("head.fc2", r.linear("head.fc2", 80, m.classes), h.tid, rows, of, m.logits);
     ctc_outputs(b, m.logits, rows, m.classes);
@@ -723,9 +741,10 @@ void svtr_head(Builder& b, const Act4& x, int cin, int hidden, int mlp) {
         seq = b.pointwise(p + ".fc2", r.linear(p + ".mlp.fc2", mlp, hidden), h1, of2);
     }
     Act4 fin = layer_norm(e + ".norm", e + ".norm", seq, skip.tid);
-    m.logits = m.plan.add_raw("logits", (size_t)rows * m.classes * 4, true);
+    logits_tensor(m, rows);
     GemmOpts oc;
     oc.c_f32 = true;
+    oc.ldc = m.logits_ld;
     oc.rows_per_image = seq.h * seq.w;
     b.gemm_rows("head.head", r.linear("head.head", hidden, m.classes), fin.tid, rows, oc, m.logits);
     ctc_outputs(b, m.logits, rows, m.classes);

@@ -24,7 +24,9 @@ struct BuiltModel {
     // detector
     int prob = -1, mask = -1;         // FP32 [n, h, w]; u8 [n, h, w]
     // recognizer
-    int probs = -1, logits = -1;      // FP32 [n, t, classes]
+    int probs = -1;                   // FP32 [n, t, classes]
+    int logits = -1;                  // FP32 [n, t, logits_ld]: rows padded to 16 bytes
+    int logits_ld = 0;
     int index = -1, max_prob = -1, margin = -1;   // [n, t]
     int t = 0, classes = 0;
     std::shared_ptr<float> mask_threshold = std::make_shared<float>(0.2f);   // DB binarisation threshold

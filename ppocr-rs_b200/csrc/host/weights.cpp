@@ -201,6 +201,17 @@ std::vector<float> pack_conv_tiles(const ConvWeight& cw, int tile) {
     return out;
 }
 
+std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad) {
+    n_pad = (cw.cout + 3) / 4 * 4;
+    const int taps = cw.kh * cw.kw;
+    std::vector<float> out((size_t)taps * cw.cin * n_pad, 0.f);
+    for (int o = 0; o < cw.cout; ++o)
+        for (int i = 0; i < cw.cin; ++i)
+            for (int t = 0; t < taps; ++t)
+                out[((size_t)t * cw.cin + i) * n_pad + o] = cw.w[((size_t)o * cw.cin + i) * taps + t];
+    return out;
+}
+
 std::vector<float> pack_depthwise(const ConvWeight& cw) {
     const int taps = cw.kh * cw.kw;
     std::vector<float> out((size_t)taps * cw.cout);

@@ -62,6 +62,7 @@ private:
 
 // Packers (all from OIHW / [out][in] sources)
 std::vector<float> pack_conv_tiles(const ConvWeight& cw, int tile);       // [ceil(O/tile)][kh][kw][I][tile]
+std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad);        // [kh][kw][I][O_pad4] (implicit GEMM)
 std::vector<float> pack_depthwise(const ConvWeight& cw);                  // [kh*kw][C]
 std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad);        // [K][N_pad4]
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad);  // [N_pad][K_pad] (BF16 source)

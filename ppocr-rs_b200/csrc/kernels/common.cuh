@@ -30,22 +30,23 @@ __device__ __forceinline__ float erf_as(float x) {
 }
 
 // Same formulas with hardware-approximate exp (ex2-based, ~2 ulp) and
-// reciprocal: for epilogues whose results are rounded to BF16 (8-bit
-// mantissa), where the difference to apply_act is far below one BF16 ulp.
+// approximate reciprocal / division: for epilogues whose results are rounded
+// to BF16 (8-bit mantissa), where the difference to apply_act is far below
+// one BF16 ulp.
 template <int ACT>
 __device__ __forceinline__ float apply_act_fast(float v) {
     if (ACT == ACT_RELU) return fmaxf(v, 0.f);
-    if (ACT == ACT_SILU) return v * __frcp_rn(1.f + __expf(-v));
+    if (ACT == ACT_SILU) return __fdividef(v, 1.f + __expf(-v));
     if (ACT == ACT_GELU) {
         const float x = v * 0.70710678118654752f;
         const float a = fabsf(x);
-        const float t = __frcp_rn(fmaf(a, 0.3275911f, 1.f));
+        const float t = __fdividef(1.f, fmaf(a, 0.3275911f, 1.f));
         const float p = t * (0.2548296f + t * (-0.28449672f + t * (1.4214138f + t * (-1.4531521f + t * 1.0614054f))));
         const float e = 1.f - p * __expf(-a * a);
         return 0.5f * v * (1.f + copysignf(e, x));
     }
-    if (ACT == ACT_HSWISH) return v * fminf(fmaxf(v / 6.f + 0.5f, 0.f), 1.f);
-    if (ACT == ACT_SIGMOID) return __frcp_rn(1.f + __expf(-v));
+    if (ACT == ACT_HSWISH) return v * fminf(fmaxf(v * (1.f / 6.f) + 0.5f, 0.f), 1.f);
+    if (ACT == ACT_SIGMOID) return __fdividef(1.f, 1.f + __expf(-v));
     return v;
 }
 
@@ -85,6 +86,9 @@ __device__ __forceinline__ float4 f4_fma(float a, float4 b, float4 c) {
 }
 __device__ __forceinline__ float4 f4_mul(float4 a, float4 b) { return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); }
 __device__ __forceinline__ float4 f4_add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float4 f4_max(float4 a, float4 b) {
+    return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+}
 __device__ __forceinline__ float4 f4_vfma(float4 a, float4 b, float4 c) {
     return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
 }

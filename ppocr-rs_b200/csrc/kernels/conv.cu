@@ -7,10 +7,12 @@
 // conv_down over the upsample-concat of the four neck outputs
 // (src/cpu/model.rs:626-693, 1022-1066, 1479-1521).
 //
-// One thread computes one output pixel for a tile of CO output channels
-// (16 when cout >= 16, else 8), so the input window is read once per
-// 16 channels; the block's weight tile [kh][kw][cin][CO] sits in shared
-// memory and is read by broadcast.  Input channels are read four at a time.
+// One thread computes PIX output pixels (one in the launched configuration)
+// for a tile of CO output channels (16 when cout >= 16, else 8), so the input
+// window is read once per 16 channels; the block's weight tile
+// [kh][kw][cin][CO] sits in shared memory and is read by broadcast.
+// Input channels are read four at a time; source addresses are computed
+// once per (tap, source).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -19,34 +21,73 @@ namespace {
 
 constexpr int kConvThreads = 128;
 
-template <typename T>
-__device__ __forceinline__ float4 read_source4(const ConvSource& s, int img, int iy, int ix, int hi, int wi, int c) {
-    const int hs = hi / s.scale, ws = wi / s.scale;
-    const T* base = static_cast<const T*>(s.ptr);
-    if (s.mode == SRC_NHWC_MAXPOOL) {
-        // 2x2 window anchored at (iy, ix); positions past the bottom/right edge
-        // are padding and never win (pads [0, 0, 1, 1]).
-        float4 m = load4(base + ((size_t)(img * hs + iy) * ws + ix) * s.cstride + s.coff + c);
-        if (ix + 1 < ws) {
-            float4 v = load4(base + ((size_t)(img * hs + iy) * ws + ix + 1) * s.cstride + s.coff + c);
-            m = make_float4(fmaxf(m.x, v.x), fmaxf(m.y, v.y), fmaxf(m.z, v.z), fmaxf(m.w, v.w));
-        }
-        if (iy + 1 < hs) {
-            float4 v = load4(base + ((size_t)(img * hs + iy + 1) * ws + ix) * s.cstride + s.coff + c);
-            m = make_float4(fmaxf(m.x, v.x), fmaxf(m.y, v.y), fmaxf(m.z, v.z), fmaxf(m.w, v.w));
-            if (ix + 1 < ws) {
-                v = load4(base + ((size_t)(img * hs + iy + 1) * ws + ix + 1) * s.cstride + s.coff + c);
-                m = make_float4(fmaxf(m.x, v.x), fmaxf(m.y, v.y), fmaxf(m.z, v.z), fmaxf(m.w, v.w));
-            }
-        }
-        return m;
-    }
-    const int sy = iy / s.scale, sx = ix / s.scale;
-    return load4(base + ((size_t)(img * hs + sy) * ws + sx) * s.cstride + s.coff + c);
+// Address of one NHWC source pixel for the logical (upsampled) position
+// (iy, ix); `shift` = log2 of the source's upsampling factor (a power of two,
+// checked on the host).  For max-pool sources the window's right / bottom
+// neighbours are flagged when they exist.
+struct SrcPix {
+    int off;        // element offset of the pixel's channel 0 of the view
+    bool right, down;
+};
+
+__device__ __forceinline__ SrcPix source_pixel(const ConvSource& s, int shift, int img, int iy, int ix, int hi, int wi) {
+    const int hs = hi >> shift, ws = wi >> shift;
+    const int sy = iy >> shift, sx = ix >> shift;
+    SrcPix r;
+    r.off = ((img * hs + sy) * ws + sx) * s.cstride + s.coff;
+    r.right = sx + 1 < ws;
+    r.down = sy + 1 < hs;
+    return r;
 }
 
-template <typename T, int CO>
-__global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
+template <typename T>
+__device__ __forceinline__ float4 read_pixel4(const ConvSource& s, const T* base, const SrcPix& px, int ws, int c) {
+    float4 m = load4(base + px.off + c);
+    if (s.mode == SRC_NHWC_MAXPOOL) {
+        // 2x2 window anchored at the pixel; positions past the bottom/right
+        // edge are padding and never win (pads [0, 0, 1, 1]).
+        if (px.right) m = f4_max(m, load4(base + px.off + s.cstride + c));
+        if (px.down) {
+            m = f4_max(m, load4(base + px.off + ws * s.cstride + c));
+            if (px.right) m = f4_max(m, load4(base + px.off + (ws + 1) * s.cstride + c));
+        }
+    }
+    return m;
+}
+
+template <int CO>
+__device__ __forceinline__ void fma_quad(float (&acc)[CO], const float4 v, const float* wr) {
+#pragma unroll
+    for (int o = 0; o < CO; o += 4) {
+        const float4 w0 = *reinterpret_cast<const float4*>(wr + o);
+        const float4 w1 = *reinterpret_cast<const float4*>(wr + CO + o);
+        const float4 w2 = *reinterpret_cast<const float4*>(wr + 2 * CO + o);
+        const float4 w3 = *reinterpret_cast<const float4*>(wr + 3 * CO + o);
+        acc[o] = fmaf(v.x, w0.x, acc[o]);
+        acc[o + 1] = fmaf(v.x, w0.y, acc[o + 1]);
+        acc[o + 2] = fmaf(v.x, w0.z, acc[o + 2]);
+        acc[o + 3] = fmaf(v.x, w0.w, acc[o + 3]);
+        acc[o] = fmaf(v.y, w1.x, acc[o]);
+        acc[o + 1] = fmaf(v.y, w1.y, acc[o + 1]);
+        acc[o + 2] = fmaf(v.y, w1.z, acc[o + 2]);
+        acc[o + 3] = fmaf(v.y, w1.w, acc[o + 3]);
+        acc[o] = fmaf(v.z, w2.x, acc[o]);
+        acc[o + 1] = fmaf(v.z, w2.y, acc[o + 1]);
+        acc[o + 2] = fmaf(v.z, w2.z, acc[o + 2]);
+        acc[o + 3] = fmaf(v.z, w2.w, acc[o + 3]);
+        acc[o] = fmaf(v.w, w3.x, acc[o]);
+        acc[o + 1] = fmaf(v.w, w3.y, acc[o + 1]);
+        acc[o + 2] = fmaf(v.w, w3.z, acc[o + 2]);
+        acc[o + 3] = fmaf(v.w, w3.w, acc[o + 3]);
+    }
+}
+
+// One thread computes PIX horizontally adjacent output pixels (of the
+// flattened pixel index) for CO output channels; the weight reads from
+// shared memory are shared by the PIX pixels.  Per output, the FMAs run in
+// the order (ky, kx, source, channel), the same for every PIX.
+template <typename T, int CO, int PIX>
+__global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p, int4 shifts) {
     extern __shared__ float wsm[];
     const int tile = blockIdx.y;
     const int taps = p.kh * p.kw;
@@ -58,60 +99,75 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
     __syncthreads();
 
     const long long total = (long long)p.n * p.ho * p.wo;
-    const long long pix = (long long)blockIdx.x * kConvThreads + threadIdx.x;
-    if (pix >= total) return;
-    const int ox = (int)(pix % p.wo);
-    const int oy = (int)((pix / p.wo) % p.ho);
-    const int img = (int)(pix / ((long long)p.wo * p.ho));
-
-    float acc[CO];
+    const long long pix0 = ((long long)blockIdx.x * kConvThreads + threadIdx.x) * PIX;
+    if (pix0 >= total) return;
+    int ox[PIX], oy[PIX], img[PIX];
+    bool live[PIX];
 #pragma unroll
-    for (int o = 0; o < CO; ++o) acc[o] = 0.f;
+    for (int q = 0; q < PIX; ++q) {
+        const long long pix = pix0 + q;
+        live[q] = pix < total;
+        const long long pc = live[q] ? pix : pix0;
+        ox[q] = (int)(pc % p.wo);
+        oy[q] = (int)((pc / p.wo) % p.ho);
+        img[q] = (int)(pc / ((long long)p.wo * p.ho));
+    }
+    const int shift[4] = {shifts.x, shifts.y, shifts.z, shifts.w};
+
+    float acc[PIX][CO];
+#pragma unroll
+    for (int q = 0; q < PIX; ++q)
+#pragma unroll
+        for (int o = 0; o < CO; ++o) acc[q][o] = 0.f;
 
     for (int ky = 0; ky < p.kh; ++ky) {
-        const int iy = oy * p.sh - p.pt + ky;
-        if (iy < 0 || iy >= p.hi) continue;
         for (int kx = 0; kx < p.kw; ++kx) {
-            const int ix = ox * p.sw - p.pl + kx;
-            if (ix < 0 || ix >= p.wi) continue;
+            bool in[PIX];
+            int iy[PIX], ix[PIX];
+            bool any = false;
+#pragma unroll
+            for (int q = 0; q < PIX; ++q) {
+                iy[q] = oy[q] * p.sh - p.pt + ky;
+                ix[q] = ox[q] * p.sw - p.pl + kx;
+                in[q] = live[q] && iy[q] >= 0 && iy[q] < p.hi && ix[q] >= 0 && ix[q] < p.wi;
+                any |= in[q];
+            }
+            if (!any) continue;
             const float* wt = wsm + (size_t)(ky * p.kw + kx) * p.cin * CO;
             int cbase = 0;
             for (int s = 0; s < p.nsrc; ++s) {
                 const ConvSource& src = p.src[s];
                 if (src.mode == SRC_NCHW_F32) {
                     const float* base = static_cast<const float*>(src.ptr);
+                    const size_t plane = (size_t)p.hi * p.wi;
+                    size_t off[PIX];
+#pragma unroll
+                    for (int q = 0; q < PIX; ++q)
+                        off[q] = in[q] ? ((size_t)img[q] * src.channels * p.hi + iy[q]) * p.wi + ix[q] : 0;
                     for (int c = 0; c < src.channels; ++c) {
-                        const float v = base[((size_t)(img * src.channels + c) * p.hi + iy) * p.wi + ix];
                         const float* wr = wt + (cbase + c) * CO;
 #pragma unroll
-                        for (int o = 0; o < CO; ++o) acc[o] = fmaf(v, wr[o], acc[o]);
+                        for (int q = 0; q < PIX; ++q) {
+                            if (!in[q]) continue;
+                            const float v = base[off[q] + (size_t)c * plane];
+#pragma unroll
+                            for (int o = 0; o < CO; ++o) acc[q][o] = fmaf(v, wr[o], acc[q][o]);
+                        }
                     }
                 } else {
+                    const T* base = static_cast<const T*>(src.ptr);
+                    const int sh = shift[s];
+                    const int ws = p.wi >> sh;
+                    SrcPix px[PIX];
+#pragma unroll
+                    for (int q = 0; q < PIX; ++q)
+                        px[q] = in[q] ? source_pixel(src, sh, img[q], iy[q], ix[q], p.hi, p.wi) : SrcPix{0, false, false};
                     for (int c = 0; c < src.channels; c += 4) {
-                        const float4 v = read_source4<T>(src, img, iy, ix, p.hi, p.wi, c);
                         const float* wr = wt + (cbase + c) * CO;
 #pragma unroll
-                        for (int o = 0; o < CO; o += 4) {
-                            const float4 w0 = *reinterpret_cast<const float4*>(wr + o);
-                            const float4 w1 = *reinterpret_cast<const float4*>(wr + CO + o);
-                            const float4 w2 = *reinterpret_cast<const float4*>(wr + 2 * CO + o);
-                            const float4 w3 = *reinterpret_cast<const float4*>(wr + 3 * CO + o);
-                            acc[o] = fmaf(v.x, w0.x, acc[o]);
-                            acc[o + 1] = fmaf(v.x, w0.y, acc[o + 1]);
-                            acc[o + 2] = fmaf(v.x, w0.z, acc[o + 2]);
-                            acc[o + 3] = fmaf(v.x, w0.w, acc[o + 3]);
-                            acc[o] = fmaf(v.y, w1.x, acc[o]);
-                            acc[o + 1] = fmaf(v.y, w1.y, acc[o + 1]);
-                            acc[o + 2] = fmaf(v.y, w1.z, acc[o + 2]);
-                            acc[o + 3] = fmaf(v.y, w1.w, acc[o + 3]);
-                            acc[o] = fmaf(v.z, w2.x, acc[o]);
-                            acc[o + 1] = fmaf(v.z, w2.y, acc[o + 1]);
-                            acc[o + 2] = fmaf(v.z, w2.z, acc[o + 2]);
-                            acc[o + 3] = fmaf(v.z, w2.w, acc[o + 3]);
-                            acc[o] = fmaf(v.w, w3.x, acc[o]);
-                            acc[o + 1] = fmaf(v.w, w3.y, acc[o + 1]);
-                            acc[o + 2] = fmaf(v.w, w3.z, acc[o + 2]);
-                            acc[o + 3] = fmaf(v.w, w3.w, acc[o + 3]);
+                        for (int q = 0; q < PIX; ++q) {
+                            if (!in[q]) continue;
+                            fma_quad<CO>(acc[q], read_pixel4<T>(src, base, px[q], ws, c), wr);
                         }
                     }
                 }
@@ -121,44 +177,59 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p) {
     }
 
     const int co0 = tile * CO;
-    T* out = static_cast<T*>(p.out) + (size_t)pix * p.out_cstride + p.out_coff + co0;
-    const T* res = nullptr;
-    if (p.residual) {
-        const int rh = p.ho / p.res_scale, rw = p.wo / p.res_scale;
-        res = static_cast<const T*>(p.residual) +
-              ((size_t)(img * rh + oy / p.res_scale) * rw + ox / p.res_scale) * p.cout + co0;
-    }
 #pragma unroll
-    for (int g = 0; g < CO; g += 4) {
-        if (co0 + g >= p.cout) break;
-        float4 v = make_float4(acc[g], acc[g + 1], acc[g + 2], acc[g + 3]);
-        if (p.bias) v = f4_add(v, *reinterpret_cast<const float4*>(p.bias + co0 + g));
-        v = f4_act(v, p.act);
-        if (res) v = f4_add(v, load4(res + g));
-        store4(out + g, v);
+    for (int q = 0; q < PIX; ++q) {
+        if (!live[q]) break;
+        T* out = static_cast<T*>(p.out) + (size_t)(pix0 + q) * p.out_cstride + p.out_coff + co0;
+        const T* res = nullptr;
+        if (p.residual) {
+            const int rh = p.ho / p.res_scale, rw = p.wo / p.res_scale;
+            res = static_cast<const T*>(p.residual) +
+                  ((size_t)(img[q] * rh + oy[q] / p.res_scale) * rw + ox[q] / p.res_scale) * p.cout + co0;
+        }
+#pragma unroll
+        for (int g = 0; g < CO; g += 4) {
+            if (co0 + g >= p.cout) break;
+            float4 v = make_float4(acc[q][g], acc[q][g + 1], acc[q][g + 2], acc[q][g + 3]);
+            if (p.bias) v = f4_add(v, *reinterpret_cast<const float4*>(p.bias + co0 + g));
+            v = f4_act(v, p.act);
+            if (res) v = f4_add(v, load4(res + g));
+            store4(out + g, v);
+        }
     }
 }
 
 template <typename T, int CO>
 cudaError_t launch_conv_t(const ConvParams& p, cudaStream_t stream) {
+    constexpr int PIX = 1;
     const int tiles = (p.cout + CO - 1) / CO;
     const size_t smem = (size_t)p.kh * p.kw * p.cin * CO * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(conv_kernel<T, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(conv_kernel<T, CO, PIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    if (smem > 200 * 1024) return cudaErrorInvalidConfiguration;
+    if (smem > 200 * 1024 || p.nsrc < 1 || p.nsrc > 4) return cudaErrorInvalidConfiguration;
+    // Upsampling factors are powers of two (nearest x2/x4/x8 in the necks);
+    // the kernel divides by shifting.
+    int sh[4] = {0, 0, 0, 0};
+    for (int s = 0; s < p.nsrc; ++s) {
+        const int sc = p.src[s].scale;
+        if (sc < 1 || (sc & (sc - 1)) || p.hi % sc || p.wi % sc) return cudaErrorInvalidValue;
+        while ((1 << sh[s]) < sc) ++sh[s];
+    }
     const long long total = (long long)p.n * p.ho * p.wo;
-    dim3 grid((unsigned)((total + kConvThreads - 1) / kConvThreads), (unsigned)tiles);
-    conv_kernel<T, CO><<<grid, kConvThreads, smem, stream>>>(p);
+    const long long threads = (total + PIX - 1) / PIX;
+    dim3 grid((unsigned)((threads + kConvThreads - 1) / kConvThreads), (unsigned)tiles);
+    conv_kernel<T, CO, PIX><<<grid, kConvThreads, smem, stream>>>(p, make_int4(sh[0], sh[1], sh[2], sh[3]));
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream) {
+    if (p.weight_kn) return launch_conv_gemm(p, stream);
     if (p.co_tile == 16)
         return p.dtype == DT_F32 ? launch_conv_t<float, 16>(p, stream) : launch_conv_t<__nv_bfloat16, 16>(p, stream);
     if (p.co_tile != 8) return cudaErrorInvalidValue;

@@ -11,6 +11,17 @@
 // thread's 8 rows are one 32-byte shared load).  The tile shape follows N:
 // 128 x 64 for wide outputs, 256 x 32 and 512 x 16 for the thin pointwise
 // layers of the detector, so no thread computes padding columns.
+//
+// A is loaded with four consecutive threads per row (64 contiguous bytes of
+// FP32), and stored transposed with the row index XOR-swizzled by the K
+// quad, so both the shared stores and the 16-byte shared reads are free of
+// bank conflicts.
+//
+// The same kernel runs dense convolutions as implicit GEMMs (CONV = true):
+// row = output pixel, k = (ky, kx, c) over the virtual concatenation of NHWC
+// sources (nearest-upsampled or 2x2 max-pooled views), gathered while A is
+// staged; out-of-image taps contribute zeros.  Per output the FMAs run in k
+// order, i.e. (ky, kx, channel), as in the direct convolution.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -22,8 +33,11 @@ constexpr int BK = 16, TM = 8, TN = 4, THREADS = 256;
 template <typename T>
 __device__ __forceinline__ float load1(const T* p) { return to_f(*p); }
 
-template <typename T, int BM, int BN>
-__global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p) {
+// Row index of A element (k, r) in the transposed shared tile: r XOR 8 * (k / 4 % 4).
+__device__ __forceinline__ int a_swz(int k, int r) { return r ^ (((k >> 2) & 3) << 3); }
+
+template <typename T, int BM, int BN, bool CONV>
+__global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p, ConvGather g) {
     static_assert((BM / TM) * (BN / TN) == THREADS, "tile shape");
     constexpr int TX = BN / TN;   // threads along N
     __shared__ __align__(16) float As[BK][BM];
@@ -38,24 +52,79 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p) {
 #pragma unroll
         for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
-    // A tile: BM rows x BK columns = BM * 4 float4; each thread loads A_LOADS of them.
+    // A tile: BM rows x BK columns = BM * 4 float4; thread t loads quad t % 4 of
+    // rows t / 4 + 64 l (four threads per row: 64 contiguous bytes).
     constexpr int A_LOADS = BM * (BK / 4) / THREADS;
     constexpr int B_LOADS = BK * (BN / 4) / THREADS;   // may be 0 for BN < 64 -> handled below
-    for (int k0 = 0; k0 < p.k; k0 += BK) {
+    const int kq = t & 3;
+    // Implicit GEMM: each loaded row's output pixel, as (oy * sh - pt, ox * sw - pl, image).
+    int iyb[CONV ? A_LOADS : 1], ixb[CONV ? A_LOADS : 1], pim[CONV ? A_LOADS : 1];
+    int ky = 0, kx = 0, c = kq * 4;   // this thread's quad position in k = (ky, kx, c)
+    if (CONV) {
 #pragma unroll
         for (int l = 0; l < A_LOADS; ++l) {
-            const int idx = t + l * THREADS;
-            const int r = idx % BM, kq = idx / BM;   // consecutive threads -> consecutive rows
-            const int row = m0 + r, kk = k0 + kq * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (row < p.m && kk < p.k) {
-                v = load4(A + (size_t)row * p.lda + kk);
-                if (p.gate) v = f4_mul(v, *reinterpret_cast<const float4*>(p.gate + (size_t)(row / p.rows_per_image) * p.k + kk));
+            const int row = m0 + (t >> 2) + l * (THREADS / 4);
+            const int rr = row < p.m ? row : 0;
+            const int ox = rr % g.wo, rest = rr / g.wo;
+            iyb[l] = (rest % g.ho) * g.sh - g.pt;
+            ixb[l] = ox * g.sw - g.pl;
+            pim[l] = row < p.m ? rest / g.ho : -1;
+        }
+        while (c >= g.cin) { c -= g.cin; if (++kx == g.kw) { kx = 0; ++ky; } }
+    }
+    for (int k0 = 0; k0 < p.k; k0 += BK) {
+        if (CONV) {
+            // The source view holding channel c (NHWC sources hold whole quads).
+            int s = 0, cs = c;
+            while (s + 1 < g.nsrc && cs >= g.src[s].channels) { cs -= g.src[s].channels; ++s; }
+            const ConvSource& src = g.src[s];
+            const T* base = static_cast<const T*>(src.ptr);
+            const int shift = g.shift[s];
+            const int hs = g.hi >> shift, ws = g.wi >> shift;
+            const bool kin = ky < g.kh;
+#pragma unroll
+            for (int l = 0; l < A_LOADS; ++l) {
+                const int r = (t >> 2) + l * (THREADS / 4);
+                const int iy = iyb[l] + ky, ix = ixb[l] + kx;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (kin && pim[l] >= 0 && iy >= 0 && iy < g.hi && ix >= 0 && ix < g.wi) {
+                    const int sy = iy >> shift, sx = ix >> shift;
+                    const T* px = base + ((size_t)(pim[l] * hs + sy) * ws + sx) * src.cstride + src.coff + cs;
+                    v = load4(px);
+                    if (src.mode == SRC_NHWC_MAXPOOL) {
+                        // 2x2 window anchored at the pixel; positions past the bottom /
+                        // right edge are padding and never win (pads [0, 0, 1, 1]).
+                        const bool right = sx + 1 < ws, down = sy + 1 < hs;
+                        if (right) v = f4_max(v, load4(px + src.cstride));
+                        if (down) {
+                            v = f4_max(v, load4(px + (size_t)ws * src.cstride));
+                            if (right) v = f4_max(v, load4(px + (size_t)(ws + 1) * src.cstride));
+                        }
+                    }
+                }
+                As[kq * 4 + 0][a_swz(kq * 4, r)] = v.x;
+                As[kq * 4 + 1][a_swz(kq * 4, r)] = v.y;
+                As[kq * 4 + 2][a_swz(kq * 4, r)] = v.z;
+                As[kq * 4 + 3][a_swz(kq * 4, r)] = v.w;
             }
-            As[kq * 4 + 0][r] = v.x;
-            As[kq * 4 + 1][r] = v.y;
-            As[kq * 4 + 2][r] = v.z;
-            As[kq * 4 + 3][r] = v.w;
+            // Advance this thread's quad by BK channels of k.
+            c += BK;
+            while (c >= g.cin && ky < g.kh) { c -= g.cin; if (++kx == g.kw) { kx = 0; ++ky; } }
+        } else {
+#pragma unroll
+            for (int l = 0; l < A_LOADS; ++l) {
+                const int r = (t >> 2) + l * (THREADS / 4);
+                const int row = m0 + r, kk = k0 + kq * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (row < p.m && kk < p.k) {
+                    v = load4(A + (size_t)row * p.lda + kk);
+                    if (p.gate) v = f4_mul(v, *reinterpret_cast<const float4*>(p.gate + (size_t)(row / p.rows_per_image) * p.k + kk));
+                }
+                As[kq * 4 + 0][a_swz(kq * 4, r)] = v.x;
+                As[kq * 4 + 1][a_swz(kq * 4, r)] = v.y;
+                As[kq * 4 + 2][a_swz(kq * 4, r)] = v.z;
+                As[kq * 4 + 3][a_swz(kq * 4, r)] = v.w;
+            }
         }
         if (B_LOADS >= 1) {
 #pragma unroll
@@ -77,8 +146,9 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p) {
         __syncthreads();
 #pragma unroll
         for (int kk = 0; kk < BK; ++kk) {
-            const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * TM]);
-            const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * TM + 4]);
+            const int ar0 = a_swz(kk, ty * TM);   // TM = 8: the swizzle keeps the 8 rows contiguous
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ar0]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ar0 + 4]);
             const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * TN]);
             const float ar[TM] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const float br[TN] = {b.x, b.y, b.z, b.w};
@@ -135,25 +205,61 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p) {
     }
 }
 
-template <typename T, int BM, int BN>
-cudaError_t launch_cfg(const GemmParams& p, cudaStream_t stream) {
-    dim3 grid((p.m + BM - 1) / BM, (p.n + BN - 1) / BN);
-    gemm_simt_kernel<T, BM, BN><<<grid, THREADS, 0, stream>>>(p);
+template <typename T, int BM, int BN, bool CONV>
+cudaError_t launch_cfg(const GemmParams& p, const ConvGather& g, cudaStream_t stream) {
+    const long long mt = ((long long)p.m + BM - 1) / BM;
+    if (mt > 0x7fffffffLL || (p.n + BN - 1) / BN > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)mt, (p.n + BN - 1) / BN);
+    gemm_simt_kernel<T, BM, BN, CONV><<<grid, THREADS, 0, stream>>>(p, g);
     return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
-    if (p.n <= 16) return launch_cfg<T, 512, 16>(p, stream);
-    if (p.n <= 32) return launch_cfg<T, 256, 32>(p, stream);
-    return launch_cfg<T, 128, 64>(p, stream);
+template <typename T, bool CONV>
+cudaError_t launch_t(const GemmParams& p, const ConvGather& g, cudaStream_t stream) {
+    if (p.n <= 16) return launch_cfg<T, 512, 16, CONV>(p, g, stream);
+    if (p.n <= 32) return launch_cfg<T, 256, 32, CONV>(p, g, stream);
+    return launch_cfg<T, 128, 64, CONV>(p, g, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_gemm_simt(const GemmParams& p, cudaStream_t stream) {
     if (p.k % 4 || p.lda % 4 || p.n_pad % 4 || p.n_pad < p.n) return cudaErrorInvalidValue;
-    return p.dtype == DT_F32 ? launch_t<float>(p, stream) : launch_t<__nv_bfloat16>(p, stream);
+    const ConvGather g{};
+    return p.dtype == DT_F32 ? launch_t<float, false>(p, g, stream) : launch_t<__nv_bfloat16, false>(p, g, stream);
+}
+
+bool conv_gemm_supported(const ConvParams& p) {
+    if (p.cin % 4 || p.cout < 16 || p.nsrc < 1 || p.nsrc > 4) return false;
+    for (int s = 0; s < p.nsrc; ++s) {
+        const ConvSource& src = p.src[s];
+        if (src.mode == SRC_NCHW_F32 || src.channels % 4 || src.cstride % 4 || src.coff % 4) return false;
+        if (src.scale < 1 || (src.scale & (src.scale - 1)) || p.hi % src.scale || p.wi % src.scale) return false;
+        if (src.mode == SRC_NHWC_MAXPOOL && src.scale != 1) return false;
+    }
+    return true;
+}
+
+cudaError_t launch_conv_gemm(const ConvParams& p, cudaStream_t stream) {
+    if (!conv_gemm_supported(p) || !p.weight_kn || p.n_pad % 4 || p.n_pad < p.cout) return cudaErrorInvalidValue;
+    ConvGather g{};
+    g.hi = p.hi; g.wi = p.wi; g.ho = p.ho; g.wo = p.wo; g.cin = p.cin; g.kh = p.kh; g.kw = p.kw;
+    g.sh = p.sh; g.sw = p.sw; g.pt = p.pt; g.pl = p.pl; g.nsrc = p.nsrc;
+    for (int s = 0; s < p.nsrc; ++s) {
+        g.src[s] = p.src[s];
+        while ((1 << g.shift[s]) < p.src[s].scale) ++g.shift[s];
+    }
+    GemmParams q;
+    const long long m = (long long)p.n * p.ho * p.wo;
+    if (m > 0x7fffffffLL) return cudaErrorInvalidValue;
+    q.m = (int)m; q.n = p.cout; q.k = p.kh * p.kw * p.cin;
+    q.w = p.weight_kn; q.n_pad = p.n_pad;
+    q.bias = p.bias; q.act = p.act;
+    q.residual = p.residual; q.ldr = p.cout;
+    q.res_scale = p.res_scale; q.h = p.ho; q.w_px = p.wo;
+    q.c = p.out; q.ldc = p.out_cstride; q.coff = p.out_coff; q.dtype = p.dtype;
+    q.k_pad = q.k; q.lda = 4;   // unused in CONV mode (A is gathered)
+    return p.dtype == DT_F32 ? launch_t<float, true>(q, g, stream) : launch_t<__nv_bfloat16, true>(q, g, stream);
 }
 
 }  // namespace ppocr

@@ -3,7 +3,7 @@
 //   C[m, n] = act(A[m, k] * W[n, k]^T + bias) (+ residual, optionally through
 //   nearest upsampling of the pixel grid), FP32 accumulation in TMEM.
 //
-// Persistent CTAs walk 128 x BN output tiles (BN a multiple of 16, <= 256).
+// Persistent CTAs walk 128 x BN output tiles (BN a multiple of 64, <= 256).
 // Roles (320 threads):
 //   warp 0 / lane 0   TMA producer: A and W tiles (128 x 64 and BN x 64 BF16,
 //                     128-byte swizzled, K-major) into a SMEM ring;
@@ -11,14 +11,22 @@
 //                     stage into one of two TMEM accumulators (2 x BN columns),
 //                     so the next tile's MMAs run while the previous tile's
 //                     epilogue drains the other accumulator;
-//   warps 2-9         epilogue: tcgen05.ld of their TMEM lane quarter (warp % 4)
-//                     and column half, bias, activation, residual, BF16/FP32
-//                     store, then release the accumulator.
+//   warps 2-9         epilogue: tcgen05.ld of their TMEM lane quarter (warp % 4),
+//                     bias, activation, residual, then release the accumulator.
+//                     Each warp owns every other 128-byte column group of the
+//                     tile (64 BF16 / 32 FP32 columns): it packs 32 rows of a
+//                     group into its own 4 KB 128-byte-swizzled staging tile and
+//                     one lane issues a TMA store of it, so the output leaves as
+//                     whole lines instead of 32 scattered row fragments per
+//                     store instruction.  Outputs whose row pitch or base is not
+//                     16-byte aligned take a direct-store epilogue instead.
 // Every mbarrier wait is bounded: on expiry the kernel records an error code
 // in g_tc_error, stops, frees its TMEM and returns.  No cluster launch and no
 // multicast: each CTA loads its own tiles from this GPU's memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -31,6 +39,8 @@ __device__ int g_tc_error = 0;
 namespace {
 
 constexpr int BM = 128, BK = 64, MAX_STAGES = 4, THREADS = 320, EPI_WARPS = 8;
+constexpr int STAGE_OUT_BYTES = 32 * 128;                 // one epilogue warp's staging tile
+constexpr int SMEM_LIMIT = 227 * 1024;                    // opt-in shared memory per block
 
 struct TcArgs {
     int m, n, k, kt, bn, tmem_cols, stages, m_tiles, n_tiles;
@@ -40,6 +50,7 @@ struct TcArgs {
     int ldr, res_scale, h, w_px;
     void* c;
     int ldc, coff, c_f32;
+    int tma_store;
 };
 
 template <typename T, int ACT>
@@ -76,7 +87,9 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
                 o[j] += rv.x; o[j + 1] += rv.y; o[j + 2] += rv.z; o[j + 3] += rv.w;
             }
         } else {
-            for (int j = 0; j < 16 && col0 + j < p.n; ++j) o[j] += to_f(r[j]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (col0 + j < p.n) o[j] += to_f(r[j]);
         }
     }
     if (p.c_f32) {
@@ -85,7 +98,9 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
 #pragma unroll
             for (int j = 0; j < 16; j += 4) store4(c + j, make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]));
         } else {
-            for (int j = 0; j < 16 && col0 + j < p.n; ++j) c[j] = o[j];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (col0 + j < p.n) c[j] = o[j];
         }
     } else {
         T* c = static_cast<T*>(p.c) + (size_t)row * p.ldc + p.coff + col0;
@@ -93,14 +108,103 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
 #pragma unroll
             for (int j = 0; j < 16; j += 4) store4(c + j, make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]));
         } else {
-            for (int j = 0; j < 16 && col0 + j < p.n; ++j) c[j] = from_f<T>(o[j]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (col0 + j < p.n) c[j] = from_f<T>(o[j]);
         }
     }
 }
 
-template <int ACT>
+// One 128-byte column group (64 BF16 or 32 FP32 outputs) of one row: all its
+// TMEM loads, bias loads and residual loads are issued before the first wait,
+// then bias, activation and residual are applied and the row's 128-byte line
+// of the warp's 128-byte-swizzled staging tile is written (the swizzle XORs
+// the 16-byte chunk with row % 8, so the warp's 32 row writes are free of bank
+// conflicts).  Lane 0 waits for the previous TMA store to have read the tile
+// only after the math, so that wait overlaps it.
+template <int ACT, bool F32>
+__device__ __forceinline__ void epilogue_group(const TcArgs& p, uint32_t taddr, int row, int col0, uint8_t* stage,
+                                               int lane) {
+    constexpr int GW = F32 ? 32 : 64;
+    uint32_t r[GW];
+#pragma unroll
+    for (int j = 0; j < GW; j += 16) tc::tmem_ld16_async(taddr + (uint32_t)j, r + j);
+    const bool full = col0 + GW <= p.n;
+    const bool res = p.residual != nullptr && row < p.m;
+    const __nv_bfloat16* rp = nullptr;
+    if (res) {
+        size_t rrow = (size_t)row;
+        if (p.res_scale > 1) {
+            const int img_hw = p.h * p.w_px;
+            const int pimg = row / img_hw, rem = row % img_hw;
+            const int y = rem / p.w_px, x = rem % p.w_px;
+            const int rh = p.h / p.res_scale, rw = p.w_px / p.res_scale;
+            rrow = ((size_t)pimg * rh + y / p.res_scale) * rw + x / p.res_scale;
+        }
+        rp = static_cast<const __nv_bfloat16*>(p.residual) + rrow * p.ldr + col0;
+    }
+    const bool res_vec = res && full && (p.ldr % 8) == 0;
+    uint4 rv[GW / 8];
+    if (res_vec) {
+#pragma unroll
+        for (int j = 0; j < GW / 8; ++j) rv[j] = __ldg(reinterpret_cast<const uint4*>(rp) + j);
+    }
+    tc::tmem_wait_ld_regs(r);
+    float o[GW];
+    if (p.bias && full) {
+#pragma unroll
+        for (int j = 0; j < GW; j += 4) {   // 16-byte bias loads (L1-resident)
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+            o[j] = __uint_as_float(r[j]) + b.x; o[j + 1] = __uint_as_float(r[j + 1]) + b.y;
+            o[j + 2] = __uint_as_float(r[j + 2]) + b.z; o[j + 3] = __uint_as_float(r[j + 3]) + b.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < GW; ++j)
+            o[j] = __uint_as_float(r[j]) + ((p.bias && col0 + j < p.n) ? __ldg(p.bias + col0 + j) : 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < GW; ++j) o[j] = apply_act_fast<ACT>(o[j]);
+    if (res_vec) {
+#pragma unroll
+        for (int j = 0; j < GW / 8; ++j) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&rv[j]);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = __bfloat1622float2(h[t]);
+                o[8 * j + 2 * t] += f.x;
+                o[8 * j + 2 * t + 1] += f.y;
+            }
+        }
+    } else if (res) {
+#pragma unroll
+        for (int j = 0; j < GW; ++j)
+            if (col0 + j < p.n) o[j] += __bfloat162float(rp[j]);
+    }
+    uint32_t w[GW / 2 * (F32 ? 2 : 1)];
+    if (F32) {
+#pragma unroll
+        for (int j = 0; j < GW; ++j) w[j] = __float_as_uint(o[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < GW / 2; ++j) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+            w[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    }
+    if (lane == 0) tc::bulk_wait_read();   // the previous store has left the staging tile
+    __syncwarp();
+    uint8_t* line = stage + lane * 128;
+    const int swz = lane & 7;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(line + ((c ^ swz) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
+template <int ACT, bool F32>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
-                                                             const __grid_constant__ CUtensorMap tma_b, TcArgs p) {
+                                                             const __grid_constant__ CUtensorMap tma_b,
+                                                             const __grid_constant__ CUtensorMap tma_c, TcArgs p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
@@ -111,6 +215,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     const int S = p.stages;
     uint8_t* sa = smem;
     uint8_t* sb = smem + S * a_bytes;
+    uint8_t* sout = sb + S * b_bytes;   // 8 x 4 KB staging tiles, 1024-byte aligned
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = p.m_tiles * p.n_tiles;
 
@@ -185,9 +290,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             }
         }
     } else {
-        // Epilogue warps 2..9: TMEM lane quarter = warp % 4, column half = (warp - 2) / 4.
+        // Epilogue warps 2..9: TMEM lane quarter q = warp % 4 (rows q*32 .. q*32+31);
+        // `half` picks every other column group of the tile.
         const int q = warp & 3, half = (warp - 2) >> 2;
-        const int cols = p.bn / 2;   // multiple of 8; processed 16 at a time with a masked tail
+        uint8_t* stage = sout + (warp - 2) * STAGE_OUT_BYTES;
+        constexpr int GW = F32 ? 32 : 64;                 // columns per 128-byte group
         int ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
             if (abort_flag) break;
@@ -202,21 +309,36 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             }
             tc::fence_after();
             const int row = m0 + q * 32 + lane;
-            const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * p.bn + half * cols);
-            for (int c0 = 0; c0 < cols; c0 += 16) {
-                uint32_t r[16];
-                tc::tmem_ld16(base + (uint32_t)c0, r);
-                const int col = n0 + half * cols + c0;
-                if (row < p.m && col < p.n && c0 < cols) {
-                    float v[16];
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * p.bn);
+            if (p.tma_store) {
+                for (int cb = half * GW; cb < p.bn && n0 + cb < p.n; cb += 2 * GW) {
+                    epilogue_group<ACT, F32>(p, tbase + (uint32_t)cb, row, n0 + cb, stage, lane);
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc::tma_store_2d(&tma_c, stage, n0 + cb, m0 + q * 32);
+                        tc::bulk_commit();
+                    }
+                }
+            } else {
+                const int cols = p.bn / 2;   // multiple of 32, processed 16 at a time
+                const uint32_t base = tbase + (uint32_t)(half * cols);
+                for (int c0 = 0; c0 < cols; c0 += 16) {
+                    uint32_t r[16];
+                    tc::tmem_ld16(base + (uint32_t)c0, r);
+                    const int col = n0 + half * cols + c0;
+                    if (row < p.m && col < p.n) {
+                        float v[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    epilogue16<__nv_bfloat16, ACT>(p, row, col, v);
+                        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+                        epilogue16<__nv_bfloat16, ACT>(p, row, col, v);
+                    }
                 }
             }
             tc::fence_before();
             tc::mbar_arrive(&acc_empty[b]);
         }
+        if (lane == 0) tc::bulk_wait_all();
     }
     __syncthreads();
     if (warp == 0) {
@@ -238,38 +360,46 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
-              uint32_t box_outer) {
+              uint32_t box_outer, CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tile width: N split into <= 256-wide tiles of equal width, a multiple of 32
-// (each epilogue warp pair takes half the columns, 16 per TMEM load).
+// Tile width: N split into <= 256-wide tiles of equal width, a multiple of 64
+// (whole 128-byte BF16 column groups for the staged epilogue).
 int pick_bn(int n) {
-    const int n32 = (n + 31) / 32 * 32;
-    const int tiles = (n32 + 255) / 256;
-    int bn = (n32 + tiles - 1) / tiles;
-    return (bn + 31) / 32 * 32;
+    const int n64 = (n + 63) / 64 * 64;
+    const int tiles = (n64 + 255) / 256;
+    const int bn = (n64 + tiles - 1) / tiles;
+    return (bn + 63) / 64 * 64;
 }
 
-template <int ACT>
-cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, int grid, size_t smem,
-                       cudaStream_t stream) {
+template <int ACT, bool F32>
+cudaError_t launch_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const TcArgs& a, int grid,
+                       size_t smem, cudaStream_t stream) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<ACT, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_LIMIT - 1024);   // headroom for the static barriers
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    gemm_tc_kernel<ACT><<<grid, THREADS, smem, stream>>>(ma, mb, a);
+    gemm_tc_kernel<ACT, F32><<<grid, THREADS, smem, stream>>>(ma, mb, mc, a);
     return cudaGetLastError();
+}
+
+template <int ACT>
+cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const TcArgs& a, int grid,
+                       size_t smem, cudaStream_t stream) {
+    return a.c_f32 ? launch_out<ACT, true>(ma, mb, mc, a, grid, smem, stream)
+                   : launch_out<ACT, false>(ma, mb, mc, a, grid, smem, stream);
 }
 
 int sm_count() {
@@ -304,23 +434,33 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
     while (cols < 2 * bn) cols <<= 1;
     a.tmem_cols = cols;
     const int stage_bytes = BM * BK * 2 + bn * BK * 2;
-    a.stages = (200 * 1024 - 1024) / stage_bytes;
+    const int out_bytes = EPI_WARPS * STAGE_OUT_BYTES;
+    a.stages = (SMEM_LIMIT - 2048 - out_bytes) / stage_bytes;
     if (a.stages > MAX_STAGES) a.stages = MAX_STAGES;
     a.m_tiles = (p.m + BM - 1) / BM;
     a.n_tiles = (p.n + bn - 1) / bn;
     a.bias = p.bias; a.act = p.act;
     a.residual = p.residual; a.ldr = p.ldr; a.res_scale = p.res_scale; a.h = p.h; a.w_px = p.w_px;
     a.c = p.c; a.ldc = p.ldc; a.coff = p.coff; a.c_f32 = p.c_f32;
-    const size_t smem = (size_t)a.stages * stage_bytes + 1024;
+    // TMA store: the output base and row pitch must be 16-byte aligned.
+    const size_t esize = p.c_f32 ? 4 : 2;
+    char* cbase = static_cast<char*>(p.c) + (size_t)p.coff * esize;
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    a.tma_store = ((reinterpret_cast<uintptr_t>(cbase) % 16) == 0 && ((size_t)p.ldc * esize) % 16 == 0 &&
+                   make_map(&mc, cbase, (uint64_t)p.n, (uint64_t)p.m, (uint64_t)p.ldc * esize, p.c_f32 ? 32 : 64, 32,
+                            p.c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
+                      ? 1 : 0;
+    const size_t smem = (size_t)a.stages * stage_bytes + out_bytes + 1024;
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
     switch (p.act) {
-        case ACT_NONE: return launch_act<ACT_NONE>(ma, mb, a, grid, smem, stream);
-        case ACT_RELU: return launch_act<ACT_RELU>(ma, mb, a, grid, smem, stream);
-        case ACT_SILU: return launch_act<ACT_SILU>(ma, mb, a, grid, smem, stream);
-        case ACT_GELU: return launch_act<ACT_GELU>(ma, mb, a, grid, smem, stream);
-        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mb, a, grid, smem, stream);
-        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mb, a, grid, smem, stream);
+        case ACT_NONE: return launch_act<ACT_NONE>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_RELU: return launch_act<ACT_RELU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_SILU: return launch_act<ACT_SILU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_GELU: return launch_act<ACT_GELU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mb, mc, a, grid, smem, stream);
         default: return cudaErrorInvalidValue;
     }
 }

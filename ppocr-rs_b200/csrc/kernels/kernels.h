@@ -52,6 +52,8 @@ struct ConvParams {
     int kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
     int co_tile = 8;                      // output channels per thread: 8 or 16
     const float* weight = nullptr;        // [ceil(cout/co_tile)][kh][kw][cin][co_tile]
+    const float* weight_kn = nullptr;     // implicit-GEMM layout [kh][kw][cin][n_pad] (or null)
+    int n_pad = 0;
     const float* bias = nullptr;          // [cout]
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
@@ -61,6 +63,19 @@ struct ConvParams {
     DType dtype = DT_F32;
 };
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
+
+// Implicit-GEMM view of a dense conv for the SIMT GEMM kernel (gemm_simt.cu).
+struct ConvGather {
+    int hi = 0, wi = 0, ho = 0, wo = 0, cin = 0, kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
+    int nsrc = 0;
+    ConvSource src[4];
+    int shift[4] = {0, 0, 0, 0};          // log2 of each source's upsampling factor
+};
+// True when the conv can run as a SIMT implicit GEMM: NHWC sources with whole
+// channel quads, power-of-two upsampling, cout >= 16.
+bool conv_gemm_supported(const ConvParams& p);
+// Runs the conv through the implicit-GEMM SIMT kernel (needs weight_kn).
+cudaError_t launch_conv_gemm(const ConvParams& p, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Depthwise convolution, any k x k / stride, fused bias + activation +
@@ -187,7 +202,7 @@ struct PoolParams {
     float* sum = nullptr;      // [n][chunks][c]
     DType dtype = DT_F32;
 };
-int channel_sum_chunks(int hw, int c);
+int channel_sum_chunks(int n, int hw, int c);
 cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream);
 
 // gate[img][c] = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5),
@@ -291,6 +306,7 @@ cudaError_t launch_attention(const AttentionParams& p, cudaStream_t stream);
 // the top-2 logit margin.  Any output may be null.
 struct SoftmaxParams {
     int rows = 0, classes = 0;
+    int ld = 0;                       // logits row stride in floats (0: classes)
     const float* logits = nullptr;
     float* prob = nullptr;
     int32_t* index = nullptr;
@@ -318,5 +334,7 @@ cudaError_t launch_preprocess(const PreprocessParams& p, cudaStream_t stream);
 cudaError_t launch_nchw_to_nhwc(const float* in, void* out, int n, int c, int h, int w, DType dt, cudaStream_t stream);
 cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cudaStream_t stream);
 cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream);
+// Same over `rows` rows of `cols` values at row stride `ld`.
+cudaError_t launch_check_finite_rows(const float* in, size_t rows, size_t cols, size_t ld, int* flag, cudaStream_t stream);
 
 }  // namespace ppocr

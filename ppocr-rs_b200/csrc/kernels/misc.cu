@@ -39,31 +39,70 @@ __global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
 
 // gate = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5)
 // (SqueezeExcitation src/cpu/model.rs:486-492, VariantSqueezeExcitation 1098-1104)
+// A block serves IMG images so every weight row it streams feeds IMG dot
+// products.  Each output unit is one thread's sequential FMA chain over its
+// weight row, starting from the bias, in input order (the order of the
+// reference's scalar dot products); rows are streamed with 16-byte loads.
+// GATE = false: hid = relu(.); GATE = true: gate = hard_sigmoid(.; alpha, 0.5).
+template <int IMG, bool GATE>
+__device__ __forceinline__ void se_dot_rows(const float* __restrict__ w, const float* __restrict__ bias, const float* in,
+                                            int in_len, int out_len, float alpha, float* out, size_t out_stride, int nimg) {
+    const bool vec = (in_len % 4) == 0;
+    for (int j = threadIdx.x; j < out_len; j += blockDim.x) {
+        float a[IMG];
+#pragma unroll
+        for (int k = 0; k < IMG; ++k) a[k] = bias[j];
+        const float* row = w + (size_t)j * in_len;
+        if (vec) {
+            const float4* row4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 8
+            for (int i4 = 0; i4 < in_len / 4; ++i4) {
+                const float4 wv = __ldg(row4 + i4);
+#pragma unroll
+                for (int k = 0; k < IMG; ++k) {
+                    const float4 x = *reinterpret_cast<const float4*>(in + k * in_len + 4 * i4);
+                    a[k] = fmaf(wv.x, x.x, a[k]);
+                    a[k] = fmaf(wv.y, x.y, a[k]);
+                    a[k] = fmaf(wv.z, x.z, a[k]);
+                    a[k] = fmaf(wv.w, x.w, a[k]);
+                }
+            }
+        } else {
+#pragma unroll 4
+            for (int i = 0; i < in_len; ++i) {
+                const float wv = __ldg(row + i);
+#pragma unroll
+                for (int k = 0; k < IMG; ++k) a[k] = fmaf(wv, in[k * in_len + i], a[k]);
+            }
+        }
+        for (int k = 0; k < nimg; ++k)
+            out[k * out_stride + j] = GATE ? fminf(fmaxf(fmaf(a[k], alpha, 0.5f), 0.f), 1.f) : fmaxf(a[k], 0.f);
+    }
+}
+
+template <int IMG>
 __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
-    extern __shared__ float sm[];
-    float* mean = sm;
-    float* hid = sm + p.c;
-    const int img = blockIdx.x;
+    extern __shared__ float4 sm4[];
+    float* mean = reinterpret_cast<float*>(sm4);   // [IMG][c]
+    float* hid = mean + IMG * p.c;                 // [IMG][r]
+    const int img0 = blockIdx.x * IMG;
+    const int nimg = min(IMG, p.n - img0);
     const float inv = 1.f / (float)p.hw;
-    for (int i = threadIdx.x; i < p.c; i += blockDim.x) {
+    for (int t = threadIdx.x; t < IMG * p.c; t += blockDim.x) {
+        const int k = t / p.c, i = t % p.c;
         float s = 0.f;
-        for (int k = 0; k < p.chunks; ++k) s += p.sum[((size_t)img * p.chunks + k) * p.c + i];
-        mean[i] = s * inv;
+        if (k < nimg) {
+            const float* src = p.sum + (size_t)(img0 + k) * p.chunks * p.c + i;
+#pragma unroll 8
+            for (int ch = 0; ch < p.chunks; ++ch) s += __ldg(src + (size_t)ch * p.c);
+        }
+        mean[t] = s * inv;
     }
+    for (int t = threadIdx.x; t < IMG * p.r; t += blockDim.x) hid[t] = 0.f;
     __syncthreads();
-    for (int j = threadIdx.x; j < p.r; j += blockDim.x) {
-        float a = p.b1[j];
-        const float* w = p.w1 + (size_t)j * p.c;
-        for (int i = 0; i < p.c; ++i) a = fmaf(w[i], mean[i], a);
-        hid[j] = fmaxf(a, 0.f);
-    }
+    se_dot_rows<IMG, false>(p.w1, p.b1, mean, p.c, p.r, 0.f, hid, (size_t)p.r, nimg);
     __syncthreads();
-    for (int i = threadIdx.x; i < p.c; i += blockDim.x) {
-        float a = p.b2[i];
-        const float* w = p.w2 + (size_t)i * p.r;
-        for (int j = 0; j < p.r; ++j) a = fmaf(w[j], hid[j], a);
-        p.gate[(size_t)img * p.c + i] = fminf(fmaxf(fmaf(a, p.alpha, 0.5f), 0.f), 1.f);
-    }
+    se_dot_rows<IMG, true>(p.w2, p.b2, hid, p.r, p.c, p.alpha, p.gate + (size_t)img0 * p.c, (size_t)p.c, nimg);
 }
 
 // out = x*g or x + x*g (residual_mul_in_place, src/cpu/kernels/mod.rs:777-796),
@@ -306,7 +345,7 @@ __global__ void __launch_bounds__(256) softmax_ctc_kernel(SoftmaxParams p) {
     __shared__ float r1[8], r2[8];
     __shared__ ArgMax ra[8];
     const int row = blockIdx.x;
-    const float* x = p.logits + (size_t)row * p.classes;
+    const float* x = p.logits + (size_t)row * p.ld;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float m1 = -FLT_MAX, m2 = -FLT_MAX;   // top-2 logits
     for (int i = threadIdx.x; i < p.classes; i += blockDim.x) {
@@ -352,6 +391,86 @@ __global__ void __launch_bounds__(256) softmax_ctc_kernel(SoftmaxParams p) {
     if (threadIdx.x == 0) {
         ArgMax b = ra[0];
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w) b = better(b, ra[w]);
+        if (p.index) p.index[row] = b.i;
+        if (p.max_prob) p.max_prob[row] = b.v;
+        if (p.margin) p.margin[row] = m1 - m2;
+    }
+}
+
+__device__ __forceinline__ void top2_push(float v, float& m1, float& m2) {
+    if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+}
+
+// The same statistics with the row staged in shared memory: the logits are
+// read from HBM once (16-byte loads) and the probabilities written once; the
+// exponentials are kept in the staged row between the sum and the write.
+__global__ void __launch_bounds__(512) softmax_ctc_staged_kernel(SoftmaxParams p) {
+    extern __shared__ float4 srow4[];
+    float* srow = reinterpret_cast<float*>(srow4);
+    __shared__ float r1[16], r2[16];
+    __shared__ ArgMax ra[16];
+    const int row = blockIdx.x;
+    const float* x = p.logits + (size_t)row * p.ld;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float m1 = -FLT_MAX, m2 = -FLT_MAX;
+    int head = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        head = p.classes & ~3;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (int i = threadIdx.x; i < (head >> 2); i += blockDim.x) {
+            const float4 v = __ldcs(x4 + i);
+            srow4[i] = v;
+            top2_push(v.x, m1, m2); top2_push(v.y, m1, m2); top2_push(v.z, m1, m2); top2_push(v.w, m1, m2);
+        }
+    }
+    for (int i = head + threadIdx.x; i < p.classes; i += blockDim.x) {
+        const float v = x[i];
+        srow[i] = v;
+        top2_push(v, m1, m2);
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float a1 = __shfl_xor_sync(0xffffffffu, m1, o), a2 = __shfl_xor_sync(0xffffffffu, m2, o);
+        const float n1 = fmaxf(m1, a1);
+        const float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
+        m1 = n1; m2 = n2;
+    }
+    if (lane == 0) { r1[warp] = m1; r2[warp] = m2; }
+    __syncthreads();
+    m1 = r1[0]; m2 = r2[0];
+    for (int w = 1; w < nw; ++w) {
+        const float a1 = r1[w], a2 = r2[w];
+        const float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
+        m1 = fmaxf(m1, a1); m2 = n2;
+    }
+    __syncthreads();
+    float sum = 0.f;
+    for (int i = threadIdx.x; i < p.classes; i += blockDim.x) {
+        const float e = expf(srow[i] - m1);
+        srow[i] = e;
+        sum += e;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) r1[warp] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int w = 0; w < nw; ++w) sum += r1[w];
+    const float rcp = 1.f / sum;
+    ArgMax best{-FLT_MAX, -1};
+    float* prob = p.prob ? p.prob + (size_t)row * p.classes : nullptr;
+    for (int i = threadIdx.x; i < p.classes; i += blockDim.x) {
+        const float pr = srow[i] * rcp;
+        if (prob) __stcs(prob + i, pr);
+        best = better(best, ArgMax{pr, i});
+    }
+    for (int o = 16; o; o >>= 1) {
+        ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+        best = better(best, other);
+    }
+    if (lane == 0) ra[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ArgMax b = ra[0];
+        for (int w = 1; w < nw; ++w) b = better(b, ra[w]);
         if (p.index) p.index[row] = b.i;
         if (p.max_prob) p.max_prob[row] = b.v;
         if (p.margin) p.margin[row] = m1 - m2;
@@ -426,9 +545,10 @@ __global__ void to_f32_kernel(const T* in, float* out, size_t count) {
         out[i] = to_f(in[i]);
 }
 
-__global__ void check_finite_kernel(const float* in, size_t count, int* flag) {
+__global__ void check_finite_kernel(const float* in, size_t rows, size_t cols, size_t ld, int* flag) {
+    const size_t count = rows * cols;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
-        if (!isfinite(in[i])) { *flag = 1; return; }
+        if (!isfinite(in[(i / cols) * ld + i % cols])) { *flag = 1; return; }
 }
 
 inline unsigned grid_for(long long total, int threads) {
@@ -439,10 +559,14 @@ inline unsigned grid_for(long long total, int threads) {
 
 }  // namespace
 
-int channel_sum_chunks(int hw, int c) {
+int channel_sum_chunks(int n, int hw, int c) {
+    // Enough (chunk, image) blocks for ~4 per SM, each summing at least 8
+    // pixel rows per thread; fewer chunks keep the MLP's partial reads short.
     const int cg = c / 4 > 0 ? c / 4 : 1;
     const int rows = 256 / cg > 0 ? 256 / cg : 1;
     int chunks = (hw + rows * 8 - 1) / (rows * 8);
+    const int want = (4 * 148 + n - 1) / (n > 0 ? n : 1);
+    if (chunks > want) chunks = want;
     if (chunks > 64) chunks = 64;
     if (chunks < 1) chunks = 1;
     return chunks;
@@ -457,8 +581,15 @@ cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
-    const size_t smem = (size_t)(p.c + p.r) * sizeof(float);
-    se_mlp_kernel<<<p.n, 256, smem, stream>>>(p);
+    if (p.c % 4 || p.n <= 0 || p.r <= 0) return cudaErrorInvalidValue;
+    // Images per block: enough blocks to cover the SMs, each weight row reused IMG times.
+    const int img = p.n <= 148 ? 1 : (p.n <= 296 ? 2 : 4);
+    const size_t smem = (size_t)img * (p.c + p.r) * sizeof(float);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)((p.n + img - 1) / img);
+    if (img == 1) se_mlp_kernel<1><<<grid, 256, smem, stream>>>(p);
+    else if (img == 2) se_mlp_kernel<2><<<grid, 256, smem, stream>>>(p);
+    else se_mlp_kernel<4><<<grid, 256, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -538,8 +669,24 @@ cudaError_t launch_attention(const AttentionParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_softmax_ctc(const SoftmaxParams& p, cudaStream_t stream) {
-    softmax_ctc_kernel<<<p.rows, 256, 0, stream>>>(p);
+cudaError_t launch_softmax_ctc(const SoftmaxParams& in, cudaStream_t stream) {
+    SoftmaxParams p = in;
+    if (p.ld == 0) p.ld = p.classes;
+    if (p.ld < p.classes || p.rows <= 0 || p.classes <= 0) return cudaErrorInvalidValue;
+    const size_t smem = ((size_t)p.classes * sizeof(float) + 15) / 16 * 16;
+    constexpr size_t kStagedMax = 200 * 1024;
+    if (smem <= kStagedMax) {
+        static bool configured = false;
+        if (!configured) {
+            cudaError_t e = cudaFuncSetAttribute(softmax_ctc_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)kStagedMax);
+            if (e != cudaSuccess) return e;
+            configured = true;
+        }
+        softmax_ctc_staged_kernel<<<p.rows, 512, smem, stream>>>(p);
+    } else {
+        softmax_ctc_kernel<<<p.rows, 256, 0, stream>>>(p);
+    }
     return cudaGetLastError();
 }
 
@@ -563,10 +710,15 @@ cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cu
     return cudaGetLastError();
 }
 
-cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream) {
-    const unsigned g = grid_for((long long)count, 256);
-    check_finite_kernel<<<g, 256, 0, stream>>>(in, count, flag);
+cudaError_t launch_check_finite_rows(const float* in, size_t rows, size_t cols, size_t ld, int* flag, cudaStream_t stream) {
+    if (rows == 0 || cols == 0) return cudaSuccess;
+    const unsigned g = grid_for((long long)(rows * cols), 256);
+    check_finite_kernel<<<g, 256, 0, stream>>>(in, rows, cols, ld, flag);
     return cudaGetLastError();
+}
+
+cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream) {
+    return launch_check_finite_rows(in, 1, count, count, flag, stream);
 }
 
 }  // namespace ppocr

@@ -166,6 +166,8 @@ def library() -> C.CDLL:
         "ppocr_model_op_info": (I, [P, S, C.c_char_p, S, C.c_char_p, S, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_model_profile": (I, [P, S, C.POINTER(C.c_double)]),
         "ppocr_selftest_gemm": (I, [P, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "ppocr_selftest_gemm_ex": (I, [P, I, I, I, FP, FP, FP, I, FP, I, I, I, FP, C.POINTER(C.c_int),
+                                       C.POINTER(C.c_int)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_selftest_conv": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int),
                                     C.POINTER(C.c_int)]),
@@ -279,6 +281,23 @@ class Gpu:
         used, err = C.c_int(), C.c_int()
         _check(library().ppocr_selftest_gemm(self._h, m, n, k, _fptr(a), _fptr(w), None if b is None else _fptr(b),
                                              int(act), _fptr(c), C.byref(used), C.byref(err)))
+        return c, bool(used.value), err.value
+
+    def selftest_gemm_ex(self, a, w, c_init, coff: int, bias=None, act: int = 0, residual=None, out_bf16: bool = True):
+        """GEMM diagnostic into columns [coff, coff + n) of c_init [m, ldc] (other columns must survive);
+        returns (C float32 [m, ldc], used_tensor_cores, wait_error)."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        m, k = a.shape
+        n = w.shape[0]
+        c = np.array(c_init, dtype=np.float32, copy=True, order="C")
+        ldc = c.shape[1]
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        used, err = C.c_int(), C.c_int()
+        _check(library().ppocr_selftest_gemm_ex(self._h, m, n, k, _fptr(a), _fptr(w), None if b is None else _fptr(b),
+                                                int(act), None if r is None else _fptr(r), int(bool(out_bf16)),
+                                                int(ldc), int(coff), _fptr(c), C.byref(used), C.byref(err)))
         return c, bool(used.value), err.value
 
     def close(self) -> None:
