@@ -258,6 +258,96 @@ int ppocr_preprocess_noalloc(ppocr_gpu* gpu, const ppocr_image* image, const flo
 int ppocr_detector_forward_mask(ppocr_model* model, const float* input, size_t input_len,
                                 float threshold, float* probabilities, uint8_t* mask);
 
+/* ------------------------------------------------------------------------
+ * End-to-end pipeline (src/ocr.rs): the host steps around the two models
+ * and an engine that runs them with device preprocessing / rectification.
+ * ---------------------------------------------------------------------- */
+
+/* Recognizer only: device rectification of `count` (== batch) crops of
+ * `image` straight into the model input -- crop i is the quad corners[8 i ..
+ * 8 i + 8] resampled to 48 x content_widths[i] on the model's canvas, as
+ * ImagePreprocess::recognizer (src/gpu/runtime.rs:58-69) prepares one crop
+ * and prepare_recognizer (src/preprocess.rs:49-76) stacks a batch -- then the
+ * forward and the greedy-CTC statistics of ppocr_recognizer_forward_ctc,
+ * each [count, t] (any output may be NULL). Only these statistics cross to
+ * the host. */
+int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image, size_t count, const float* corners,
+                                   const size_t* content_widths, int32_t* indices, float* probabilities,
+                                   float* margins);
+
+/* DetectorPostprocessOptions (src/ocr.rs:231-271). */
+typedef struct ppocr_postprocess_options {
+    float binary_threshold; /* 0.2 */
+    float box_threshold;    /* 0.4 */
+    size_t min_area;        /* 3 */
+    float unclip_ratio;     /* 1.4 */
+    size_t max_boxes;       /* 1000 */
+} ppocr_postprocess_options;
+void ppocr_postprocess_options_default(ppocr_postprocess_options* options);
+
+/* Detection (src/ocr.rs:225-229): quadrilateral x0 y0 .. x3 y3 in source pixels. */
+typedef struct ppocr_detection {
+    float polygon[8];
+    float score;
+} ppocr_detection;
+
+/* extract_detections (src/ocr.rs:723-782), host only: components of the
+ * [height, width] probability map's content area, boxes mapped to a source
+ * image of source_w x source_h. Writes min(count, capacity) detections and
+ * sets *count to the number found. */
+int ppocr_db_postprocess(const float* probabilities, size_t height, size_t width, uint32_t source_w,
+                         uint32_t source_h, uint32_t content_w, uint32_t content_h,
+                         const ppocr_postprocess_options* options, ppocr_detection* detections, size_t capacity,
+                         size_t* count);
+
+/* Recognition dictionary (load_dictionary / parse_dictionary, src/ocr.rs:785-790, 892-965). */
+typedef struct ppocr_dictionary ppocr_dictionary;
+int ppocr_dictionary_parse(const char* contents, size_t length, ppocr_dictionary** out);
+int ppocr_dictionary_load(const char* path, ppocr_dictionary** out);
+int ppocr_dictionary_size(const ppocr_dictionary* dictionary, size_t* size);
+/* UTF-8 entry `index`; *length = its byte length (copied when it fits `capacity`). */
+int ppocr_dictionary_entry(const ppocr_dictionary* dictionary, size_t index, char* text, size_t capacity,
+                           size_t* length);
+void ppocr_dictionary_destroy(ppocr_dictionary* dictionary);
+
+/* decode_ctc_greedy_for_input (src/ocr.rs:800-853), host only, from
+ * probability rows [steps, classes]. The UTF-8 text is written to `text`
+ * (NUL-terminated when it fits; *text_length = its byte length, InvalidInput
+ * when capacity is too small). */
+int ppocr_ctc_decode(const ppocr_dictionary* dictionary, const float* probabilities, size_t steps, size_t classes,
+                     size_t content_width, size_t input_width, char* text, size_t text_capacity,
+                     size_t* text_length, float* score);
+/* The same from per-step arg-max classes and their probabilities, the
+ * statistics ppocr_recognizer_forward_crops returns. */
+int ppocr_ctc_decode_steps(const ppocr_dictionary* dictionary, const int32_t* indices, const float* probabilities,
+                           size_t steps, size_t classes, size_t content_width, size_t input_width, char* text,
+                           size_t text_capacity, size_t* text_length, float* score);
+
+/* OcrEngine / OcrOptions (src/ocr.rs:276-326, 364-540) on this library's GPU
+ * backend. detector_max_side 0 selects the released model's resize policy. */
+typedef struct ppocr_engine ppocr_engine;
+typedef struct ppocr_engine_options {
+    int detector_size;            /* ppocr_model_size, PPOCR_TINY */
+    int recognizer_size;          /* PPOCR_TINY */
+    int precision;                /* ppocr_precision of both models, PPOCR_PRECISION_FP32 */
+    uint32_t detector_max_side;   /* 736 */
+    ppocr_postprocess_options postprocess;
+    int reserved[8];
+} ppocr_engine_options;
+void ppocr_engine_options_default(ppocr_engine_options* options);
+/* OcrEngine::load: the dictionary is parsed and checked against the
+ * recognizer's classes; models are loaded per input shape on first use. */
+int ppocr_engine_create(ppocr_gpu* gpu, const char* detector_model, const char* recognizer_model,
+                        const char* dictionary, const ppocr_engine_options* options, ppocr_engine** out);
+void ppocr_engine_destroy(ppocr_engine* engine);
+/* OcrEngine::recognize on packed RGB8 pixels: format 0 writes the pretty JSON
+ * of OcrResult (README.md:34-49), 1 its text() (non-empty lines joined by
+ * newlines). *result is allocated by the library (free with
+ * ppocr_string_free). */
+int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_length, uint32_t width,
+                           uint32_t height, int format, char** result, size_t* result_length);
+void ppocr_string_free(char* text);
+
 #ifdef __cplusplus
 }
 #endif

@@ -527,6 +527,50 @@ int ppocr_recognizer_forward_ctc(ppocr_model* model, const float* input, size_t 
     });
 }
 
+int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image, size_t count, const float* corners,
+                                   const size_t* content_widths, int32_t* indices, float* probabilities,
+                                   float* margins) {
+    return guard([&] {
+        if (!model || !image || !corners || !content_widths) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "crop forward needs a recognizer");
+        if (image->gpu != model->gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        if (count != (size_t)model->m.n)
+            fail(PPOCR_ERR_INVALID_INPUT, "crop count " + std::to_string(count) + " does not match the batch " +
+                                              std::to_string(model->m.n));
+        for (size_t i = 0; i < count * 8; ++i)
+            if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
+        for (size_t i = 0; i < count; ++i)
+            if (content_widths[i] == 0 || content_widths[i] > (size_t)model->m.w)
+                fail(PPOCR_ERR_INVALID_INPUT, "invalid input: content width outside 1..=input width");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        cudaStream_t s = model->gpu->stream;
+        float* in = static_cast<float*>(model->tensor(model->m.input));
+        const size_t per = (size_t)3 * model->m.h * model->m.w;
+        for (size_t i = 0; i < count; ++i) {
+            PreprocessParams p = make_preprocess(image, corners + 8 * i, content_widths[i], (size_t)model->m.h,
+                                                 (size_t)model->m.w, false);
+            p.out = in + i * per;
+            cuda_check(launch_preprocess(p, s), "launch crop rectification");
+        }
+        model->run(s);
+        const size_t rows = (size_t)model->m.n * model->m.t;
+        std::vector<int32_t> idx(rows);
+        std::vector<float> prob(rows);
+        download(model, model->m.index, idx.data(), rows * 4);
+        download(model, model->m.max_prob, prob.data(), rows * 4);
+        if (margins) download(model, model->m.margin, margins, rows * 4);
+        wait_stream(s, 0);
+        // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
+        for (size_t r = 0; r < rows; ++r)
+            if (idx[r] < 0 || idx[r] >= model->m.classes || !std::isfinite(prob[r]))
+                fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+        if (indices) std::memcpy(indices, idx.data(), rows * 4);
+        if (probabilities) std::memcpy(probabilities, prob.data(), rows * 4);
+    });
+}
+
 int ppocr_model_op_count(const ppocr_model* model, size_t* count) {
     return guard([&] {
         if (!model || !count) fail(PPOCR_ERR_INVALID_INPUT, "null argument");

@@ -1,0 +1,328 @@
+// C ABI of the end-to-end pipeline: the host steps of pipeline.cpp and an
+// OcrEngine (src/ocr.rs:364-540) over this library's models.
+//
+// The engine follows recognize_with (src/ocr.rs:573-621): the page is
+// uploaded once; the detector runs on it with device preprocessing; the
+// probability map comes back to the host for the DB postprocess; crops are
+// ordered by aspect ratio and recognized six at a time on a canvas of the
+// chunk's width, each chunk rectified on the device straight into the
+// recognizer's input; only the per-step arg-max classes and probabilities
+// come back for the CTC text assembly.  Models are cached per input shape
+// (two detector and four recognizer shapes, the reference's limits, with
+// the recognizer's packed weights shared between shapes).
+#include <array>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "common.hpp"
+#include "handles.hpp"
+#include "pipeline.hpp"
+#include "ppocr_b200.h"
+
+using namespace ppocr;
+
+struct ppocr_dictionary {
+    std::vector<std::string> entries;
+};
+
+namespace {
+
+void check(int status) {
+    if (status != PPOCR_OK) fail(status, last_error());
+}
+
+PostOptions post_options(const ppocr_postprocess_options* o) {
+    PostOptions p;
+    if (o) {
+        p.binary_threshold = o->binary_threshold;
+        p.box_threshold = o->box_threshold;
+        p.min_area = o->min_area;
+        p.unclip_ratio = o->unclip_ratio;
+        p.max_boxes = o->max_boxes;
+    }
+    return p;
+}
+
+void write_text(const Decoded& d, char* text, size_t capacity, size_t* length, float* score) {
+    if (length) *length = d.text.size();
+    if (score) *score = d.score;
+    if (text) {
+        if (capacity < d.text.size() + 1) fail(PPOCR_ERR_INVALID_INPUT, "text buffer is too small");
+        std::memcpy(text, d.text.c_str(), d.text.size() + 1);
+    }
+}
+
+std::string read_file(const char* path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) fail(PPOCR_ERR_READ_FILE, std::string("read recognition dictionary ") + path);
+    std::ostringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+using Shape = std::array<size_t, 4>;
+
+}  // namespace
+
+struct ppocr_engine {
+    ppocr_gpu* gpu = nullptr;
+    std::string det_path, rec_path;
+    int det_size = PPOCR_TINY, rec_size = PPOCR_TINY;
+    ppocr_load_options load{};
+    PostOptions post;
+    uint32_t max_side = 736;
+    std::vector<std::string> dict;
+    size_t classes = 0;
+    std::vector<std::pair<Shape, ppocr_model*>> det_cache, rec_cache;
+    ppocr_model* rec_weights = nullptr;   // keeps the shared packed recognizer weights alive
+
+    ~ppocr_engine() {
+        for (auto& e : det_cache) ppocr_model_destroy(e.second);
+        for (auto& e : rec_cache) ppocr_model_destroy(e.second);
+        if (rec_weights) ppocr_model_destroy(rec_weights);
+    }
+
+    ppocr_model* detector(const Shape& shape) {
+        for (auto& e : det_cache)
+            if (e.first == shape) return e.second;
+        if (det_cache.size() == 2) {
+            ppocr_model_destroy(det_cache.front().second);
+            det_cache.erase(det_cache.begin());
+        }
+        ppocr_model* m = nullptr;
+        check(ppocr_detector_load_ex(gpu, det_path.c_str(), det_size, shape.data(), &load, &m));
+        det_cache.emplace_back(shape, m);
+        return m;
+    }
+
+    ppocr_model* recognizer(const Shape& shape) {
+        for (auto& e : rec_cache)
+            if (e.first == shape) return e.second;
+        if (rec_cache.size() == 4) {
+            ppocr_model_destroy(rec_cache.front().second);
+            rec_cache.erase(rec_cache.begin());
+        }
+        ppocr_model* m = nullptr;
+        check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &load, rec_weights, &m));
+        if (!rec_weights) {
+            // A second session on the same weights owns nothing but keeps them loaded.
+            check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &load, m, &rec_weights));
+        }
+        rec_cache.emplace_back(shape, m);
+        return m;
+    }
+
+    OcrResult recognize(const uint8_t* rgb, size_t len, uint32_t width, uint32_t height) {
+        if (!rgb) fail(PPOCR_ERR_INVALID_INPUT, "image pixels are null");
+        OcrResult r;
+        r.source_w = width;
+        r.source_h = height;
+        detector_input_size(width, height, max_side, &r.input_w, &r.input_h);
+        ppocr_image* img = nullptr;
+        check(ppocr_upload_rgb(gpu, width, height, rgb, len, &img));
+        struct ImageGuard {
+            ppocr_image* p;
+            ~ImageGuard() { ppocr_image_destroy(p); }
+        } guard_img{img};
+
+        ppocr_model* det = detector(Shape{1, 3, r.input_h, r.input_w});
+        std::vector<float> prob((size_t)r.input_h * r.input_w);
+        const float full[8] = {0.f, 0.f, (float)width, 0.f, (float)width, (float)height, 0.f, (float)height};
+        check(ppocr_model_forward_image(det, img, full, r.input_w, prob.data(), prob.size()));
+        const std::vector<Detection> dets =
+            extract_detections(prob.data(), r.input_h, r.input_w, width, height, r.input_w, r.input_h, post);
+
+        std::vector<Decoded> decoded(dets.size());
+        for (const RecBatch& b : recognition_batches(dets)) {
+            const size_t n = b.index.size();
+            ppocr_model* rec = recognizer(Shape{n, 3, 48, b.width});
+            size_t out_shape[4] = {0, 0, 0, 0};
+            check(ppocr_model_output_shape(rec, out_shape, nullptr, nullptr));
+            const size_t steps = out_shape[1];
+            std::vector<float> corners(n * 8);
+            for (size_t k = 0; k < n; ++k)
+                for (int c = 0; c < 4; ++c) {
+                    corners[k * 8 + 2 * c] = dets[b.index[k]].poly[c].x;
+                    corners[k * 8 + 2 * c + 1] = dets[b.index[k]].poly[c].y;
+                }
+            std::vector<int32_t> idx(n * steps);
+            std::vector<float> p(n * steps);
+            check(ppocr_recognizer_forward_crops(rec, img, n, corners.data(), b.content.data(), idx.data(), p.data(),
+                                                 nullptr));
+            for (size_t k = 0; k < n; ++k)
+                decoded[b.index[k]] = decode_ctc_steps(idx.data() + k * steps, p.data() + k * steps, steps, classes, dict,
+                                                       b.content[k], b.width);
+        }
+        for (size_t i = 0; i < dets.size(); ++i) {
+            OcrLine l;
+            std::copy(dets[i].poly, dets[i].poly + 4, l.poly);
+            l.detection_score = dets[i].score;
+            l.text = decoded[i].text;
+            l.recognition_score = decoded[i].score;
+            r.lines.push_back(std::move(l));
+        }
+        return r;
+    }
+};
+
+extern "C" {
+
+void ppocr_postprocess_options_default(ppocr_postprocess_options* o) {
+    if (!o) return;
+    const PostOptions d;
+    o->binary_threshold = d.binary_threshold;
+    o->box_threshold = d.box_threshold;
+    o->min_area = d.min_area;
+    o->unclip_ratio = d.unclip_ratio;
+    o->max_boxes = d.max_boxes;
+}
+
+int ppocr_db_postprocess(const float* probabilities, size_t height, size_t width, uint32_t source_w, uint32_t source_h,
+                         uint32_t content_w, uint32_t content_h, const ppocr_postprocess_options* options,
+                         ppocr_detection* detections, size_t capacity, size_t* count) {
+    return guard([&] {
+        if (!probabilities) fail(PPOCR_ERR_INVALID_INPUT, "probability map is null");
+        if (capacity && !detections) fail(PPOCR_ERR_INVALID_INPUT, "detection buffer is null");
+        const std::vector<Detection> d =
+            extract_detections(probabilities, height, width, source_w, source_h, content_w, content_h, post_options(options));
+        if (count) *count = d.size();
+        for (size_t i = 0; i < d.size() && i < capacity; ++i) {
+            for (int c = 0; c < 4; ++c) {
+                detections[i].polygon[2 * c] = d[i].poly[c].x;
+                detections[i].polygon[2 * c + 1] = d[i].poly[c].y;
+            }
+            detections[i].score = d[i].score;
+        }
+    });
+}
+
+int ppocr_dictionary_parse(const char* contents, size_t length, ppocr_dictionary** out) {
+    return guard([&] {
+        if (!contents || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        auto d = std::make_unique<ppocr_dictionary>();
+        d->entries = parse_dictionary(std::string(contents, length));
+        *out = d.release();
+    });
+}
+
+int ppocr_dictionary_load(const char* path, ppocr_dictionary** out) {
+    return guard([&] {
+        if (!path || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        auto d = std::make_unique<ppocr_dictionary>();
+        d->entries = parse_dictionary(read_file(path));
+        *out = d.release();
+    });
+}
+
+int ppocr_dictionary_size(const ppocr_dictionary* dictionary, size_t* size) {
+    return guard([&] {
+        if (!dictionary || !size) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        *size = dictionary->entries.size();
+    });
+}
+
+int ppocr_dictionary_entry(const ppocr_dictionary* dictionary, size_t index, char* text, size_t capacity, size_t* length) {
+    return guard([&] {
+        if (!dictionary) fail(PPOCR_ERR_INVALID_INPUT, "dictionary is null");
+        if (index >= dictionary->entries.size()) fail(PPOCR_ERR_INVALID_INPUT, "dictionary index out of range");
+        const std::string& e = dictionary->entries[index];
+        if (length) *length = e.size();
+        if (text && capacity > e.size()) std::memcpy(text, e.c_str(), e.size() + 1);
+    });
+}
+
+void ppocr_dictionary_destroy(ppocr_dictionary* dictionary) { delete dictionary; }
+
+int ppocr_ctc_decode(const ppocr_dictionary* dictionary, const float* probabilities, size_t steps, size_t classes,
+                     size_t content_width, size_t input_width, char* text, size_t text_capacity, size_t* text_length,
+                     float* score) {
+    return guard([&] {
+        if (!dictionary || !probabilities) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        write_text(decode_ctc_rows(probabilities, steps, classes, dictionary->entries, content_width, input_width), text,
+                   text_capacity, text_length, score);
+    });
+}
+
+int ppocr_ctc_decode_steps(const ppocr_dictionary* dictionary, const int32_t* indices, const float* probabilities,
+                           size_t steps, size_t classes, size_t content_width, size_t input_width, char* text,
+                           size_t text_capacity, size_t* text_length, float* score) {
+    return guard([&] {
+        if (!dictionary || !indices || !probabilities) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        write_text(decode_ctc_steps(indices, probabilities, steps, classes, dictionary->entries, content_width, input_width),
+                   text, text_capacity, text_length, score);
+    });
+}
+
+void ppocr_engine_options_default(ppocr_engine_options* o) {
+    if (!o) return;
+    std::memset(o, 0, sizeof(*o));
+    o->detector_size = PPOCR_TINY;
+    o->recognizer_size = PPOCR_TINY;
+    o->precision = PPOCR_PRECISION_FP32;
+    o->detector_max_side = 736;
+    ppocr_postprocess_options_default(&o->postprocess);
+}
+
+int ppocr_engine_create(ppocr_gpu* gpu, const char* detector_model, const char* recognizer_model, const char* dictionary,
+                        const ppocr_engine_options* options, ppocr_engine** out) {
+    return guard([&] {
+        if (!gpu || !detector_model || !recognizer_model || !dictionary || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        ppocr_engine_options o;
+        ppocr_engine_options_default(&o);
+        if (options) o = *options;
+        auto e = std::make_unique<ppocr_engine>();
+        e->gpu = gpu;
+        e->det_path = detector_model;
+        e->rec_path = recognizer_model;
+        e->det_size = o.detector_size;
+        e->rec_size = o.recognizer_size;
+        e->post = post_options(&o.postprocess);
+        e->post.validate();
+        e->max_side = o.detector_max_side;
+        ppocr_load_options_default(&e->load);
+        e->load.precision = o.precision;
+        e->dict = parse_dictionary(read_file(dictionary));
+        // validate_recognizer_dictionary (src/ocr.rs:689-700), against the file's classifier.
+        const size_t shape[4] = {1, 3, 48, 320};
+        size_t out_shape[4] = {0, 0, 0, 0};
+        check(ppocr_inspect_model(recognizer_model, 1, o.recognizer_size, shape, o.precision, nullptr, nullptr, nullptr,
+                                  out_shape));
+        e->classes = out_shape[2];
+        if (e->classes != e->dict.size() + 1 && e->classes != e->dict.size() + 2)
+            fail(PPOCR_ERR_INVALID_INPUT, "recognizer has " + std::to_string(e->classes) +
+                                              " output classes, but the dictionary has " + std::to_string(e->dict.size()) +
+                                              " entries");
+        *out = e.release();
+    });
+}
+
+void ppocr_engine_destroy(ppocr_engine* engine) {
+    try {
+        delete engine;
+    } catch (...) {
+    }
+}
+
+int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_length, uint32_t width, uint32_t height,
+                           int format, char** result, size_t* result_length) {
+    return guard([&] {
+        if (!engine || !result) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (format != 0 && format != 1) fail(PPOCR_ERR_INVALID_INPUT, "format must be 0 (JSON) or 1 (text)");
+        const OcrResult r = engine->recognize(rgb, rgb_length, width, height);
+        const std::string s = format == 0 ? result_json(r) : result_text(r);
+        char* buf = static_cast<char*>(std::malloc(s.size() + 1));
+        if (!buf) fail(PPOCR_ERR_GPU, "out of host memory");
+        std::memcpy(buf, s.c_str(), s.size() + 1);
+        *result = buf;
+        if (result_length) *result_length = s.size();
+    });
+}
+
+void ppocr_string_free(char* text) { std::free(text); }
+
+}  // extern "C"

@@ -116,6 +116,20 @@ class Precision:
         return {"fp32": 0, "bf16": 1, "tf32x3": 2}[str(value).lower()]
 
 
+class _PostOptions(C.Structure):
+    _fields_ = [("binary_threshold", C.c_float), ("box_threshold", C.c_float), ("min_area", C.c_size_t),
+                ("unclip_ratio", C.c_float), ("max_boxes", C.c_size_t)]
+
+
+class _Detection(C.Structure):
+    _fields_ = [("polygon", C.c_float * 8), ("score", C.c_float)]
+
+
+class _EngineOptions(C.Structure):
+    _fields_ = [("detector_size", C.c_int), ("recognizer_size", C.c_int), ("precision", C.c_int),
+                ("detector_max_side", C.c_uint32), ("postprocess", _PostOptions), ("reserved", C.c_int * 8)]
+
+
 class _LoadOptions(C.Structure):
     _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("simt_only", C.c_int), ("reserved", C.c_int * 5)]
 
@@ -172,6 +186,23 @@ def library() -> C.CDLL:
         "ppocr_selftest_conv": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int),
                                     C.POINTER(C.c_int)]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
+        "ppocr_recognizer_forward_crops": (I, [P, P, S, FP, C.POINTER(S), C.POINTER(C.c_int32), FP, FP]),
+        "ppocr_postprocess_options_default": (None, [C.POINTER(_PostOptions)]),
+        "ppocr_db_postprocess": (I, [FP, S, S, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                     C.POINTER(_PostOptions), C.POINTER(_Detection), S, C.POINTER(S)]),
+        "ppocr_dictionary_parse": (I, [C.c_char_p, S, C.POINTER(P)]),
+        "ppocr_dictionary_load": (I, [C.c_char_p, C.POINTER(P)]),
+        "ppocr_dictionary_size": (I, [P, C.POINTER(S)]),
+        "ppocr_dictionary_entry": (I, [P, S, C.c_char_p, S, C.POINTER(S)]),
+        "ppocr_dictionary_destroy": (None, [P]),
+        "ppocr_ctc_decode": (I, [P, FP, S, S, S, S, C.c_char_p, S, C.POINTER(S), FP]),
+        "ppocr_ctc_decode_steps": (I, [P, C.POINTER(C.c_int32), FP, S, S, S, S, C.c_char_p, S, C.POINTER(S), FP]),
+        "ppocr_engine_options_default": (None, [C.POINTER(_EngineOptions)]),
+        "ppocr_engine_create": (I, [P, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(_EngineOptions), C.POINTER(P)]),
+        "ppocr_engine_destroy": (None, [P]),
+        "ppocr_engine_recognize": (I, [P, C.POINTER(C.c_uint8), S, C.c_uint32, C.c_uint32, I,
+                                       C.POINTER(C.c_void_p), C.POINTER(S)]),
+        "ppocr_string_free": (None, [C.c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -479,6 +510,21 @@ class Recognizer(_Model):
                                                   C.byref(h)))
         return cls(h, gpu, input_shape, shared_weights)
 
+    def forward_crops(self, image: "GpuImage", corners, content_widths):
+        """Device rectification of each crop (corners [n, 4, 2], content widths [n]) into the
+        input canvas, forward, and greedy-CTC statistics: (arg-max index, its probability,
+        top-2 logit margin), each [n, t]."""
+        n, t = self.output_shape[0], self.output_shape[1]
+        c = np.ascontiguousarray(corners, dtype=np.float32).reshape(-1)
+        cw = (C.c_size_t * n)(*[int(v) for v in content_widths])
+        idx = np.empty((n, t), dtype=np.int32)
+        prob = np.empty((n, t), dtype=np.float32)
+        margin = np.empty((n, t), dtype=np.float32)
+        _check(library().ppocr_recognizer_forward_crops(self._h, image._h, n, _fptr(c), cw,
+                                                        idx.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
+                                                        _fptr(margin)))
+        return idx, prob, margin
+
     def forward_logits(self, values) -> np.ndarray:
         """Pre-softmax classifier logits [n, t, classes]."""
         x = self._input(values)
@@ -497,3 +543,148 @@ class Recognizer(_Model):
                                                       idx.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
                                                       _fptr(margin)))
         return idx, prob, margin
+
+
+# ---------------------------------------------------------------------------
+# End-to-end pipeline (src/ocr.rs): host postprocess, dictionary, CTC, engine
+# ---------------------------------------------------------------------------
+
+
+class PostprocessOptions:
+    """DetectorPostprocessOptions (src/ocr.rs:231-271)."""
+
+    def __init__(self, binary_threshold=0.2, box_threshold=0.4, min_area=3, unclip_ratio=1.4, max_boxes=1000):
+        self.binary_threshold, self.box_threshold = binary_threshold, box_threshold
+        self.min_area, self.unclip_ratio, self.max_boxes = min_area, unclip_ratio, max_boxes
+
+    def _c(self) -> _PostOptions:
+        return _PostOptions(float(self.binary_threshold), float(self.box_threshold), int(self.min_area),
+                            float(self.unclip_ratio), int(self.max_boxes))
+
+
+def db_postprocess(prob, source_size, content_size=None, options: PostprocessOptions = None):
+    """extract_detections on a [h, w] probability map: [(polygon float32 [4, 2], score)]."""
+    prob = np.ascontiguousarray(prob, dtype=np.float32)
+    h, w = prob.shape[-2:]
+    cw, ch = content_size if content_size is not None else (w, h)
+    opts = (options or PostprocessOptions())._c()
+    count = C.c_size_t()
+    _check(library().ppocr_db_postprocess(_fptr(prob), h, w, int(source_size[0]), int(source_size[1]), int(cw), int(ch),
+                                          C.byref(opts), None, 0, C.byref(count)))
+    buf = (_Detection * max(count.value, 1))()
+    _check(library().ppocr_db_postprocess(_fptr(prob), h, w, int(source_size[0]), int(source_size[1]), int(cw), int(ch),
+                                          C.byref(opts), buf, count.value, C.byref(count)))
+    return [(np.array(buf[i].polygon, dtype=np.float32).reshape(4, 2), np.float32(buf[i].score))
+            for i in range(count.value)]
+
+
+class Dictionary:
+    """Recognition dictionary (parse_dictionary, src/ocr.rs:892-965)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @classmethod
+    def parse(cls, contents: str) -> "Dictionary":
+        raw = contents.encode("utf-8")
+        h = C.c_void_p()
+        _check(library().ppocr_dictionary_parse(raw, len(raw), C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def load(cls, path: str) -> "Dictionary":
+        h = C.c_void_p()
+        _check(library().ppocr_dictionary_load(str(path).encode(), C.byref(h)))
+        return cls(h)
+
+    def __len__(self) -> int:
+        n = C.c_size_t()
+        _check(library().ppocr_dictionary_size(self._h, C.byref(n)))
+        return n.value
+
+    def entries(self):
+        out = []
+        for i in range(len(self)):
+            n = C.c_size_t()
+            _check(library().ppocr_dictionary_entry(self._h, i, None, 0, C.byref(n)))
+            buf = C.create_string_buffer(n.value + 1)
+            _check(library().ppocr_dictionary_entry(self._h, i, buf, n.value + 1, C.byref(n)))
+            out.append(buf.raw[:n.value].decode("utf-8", "replace"))
+        return out
+
+    def _text(self, fn, *args):
+        n, score = C.c_size_t(), C.c_float()
+        _check(fn(self._h, *args, None, 0, C.byref(n), C.byref(score)))
+        buf = C.create_string_buffer(n.value + 1)
+        _check(fn(self._h, *args, buf, n.value + 1, C.byref(n), C.byref(score)))
+        return buf.raw[:n.value].decode("utf-8", "replace"), score.value
+
+    def decode(self, probs, content_width: int, input_width: int):
+        """decode_ctc_greedy_for_input on probability rows [t, classes] -> (text, score)."""
+        probs = np.ascontiguousarray(probs, dtype=np.float32)
+        t, c = probs.shape
+        return self._text(library().ppocr_ctc_decode, _fptr(probs), t, c, int(content_width), int(input_width))
+
+    def decode_steps(self, index, prob, classes: int, content_width: int, input_width: int):
+        """The same from per-step arg-max classes and probabilities."""
+        index = np.ascontiguousarray(index, dtype=np.int32)
+        prob = np.ascontiguousarray(prob, dtype=np.float32)
+        return self._text(library().ppocr_ctc_decode_steps, index.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
+                          index.size, int(classes), int(content_width), int(input_width))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            library().ppocr_dictionary_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Engine:
+    """OcrEngine (src/ocr.rs:364-540) on this library's GPU backend."""
+
+    def __init__(self, gpu: Gpu, detector_model: str, recognizer_model: str, dictionary: str,
+                 detector_size="tiny", recognizer_size="tiny", precision="fp32", detector_max_side: int = 736,
+                 postprocess: PostprocessOptions = None):
+        o = _EngineOptions()
+        library().ppocr_engine_options_default(C.byref(o))
+        o.detector_size = ModelSize.parse(detector_size)
+        o.recognizer_size = ModelSize.parse(recognizer_size)
+        o.precision = Precision.parse(precision)
+        o.detector_max_side = int(detector_max_side or 0)
+        if postprocess is not None:
+            o.postprocess = postprocess._c()
+        h = C.c_void_p()
+        _check(library().ppocr_engine_create(gpu._h, str(detector_model).encode(), str(recognizer_model).encode(),
+                                             str(dictionary).encode(), C.byref(o), C.byref(h)))
+        self._h, self.gpu = h, gpu
+
+    def recognize(self, rgb, fmt: str = "json"):
+        """OcrEngine::recognize on an RGB8 [h, w, 3] array -> parsed JSON dict (fmt="json") or text."""
+        import json
+
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        h, w = rgb.shape[:2]
+        out, n = C.c_void_p(), C.c_size_t()
+        _check(library().ppocr_engine_recognize(self._h, rgb.ctypes.data_as(C.POINTER(C.c_uint8)), rgb.size, w, h,
+                                                0 if fmt == "json" else 1, C.byref(out), C.byref(n)))
+        try:
+            text = C.string_at(out, n.value).decode("utf-8")
+        finally:
+            library().ppocr_string_free(out)
+        return json.loads(text) if fmt == "json" else text
+
+    def close(self):
+        if getattr(self, "_h", None):
+            library().ppocr_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
