@@ -7,7 +7,7 @@ GPU), seeded uniform-RGB8 inputs, seeded random-init weights in the exact
 reference checkpoint layout, FP32 (the parity mode).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--kind det|rec] [--size tiny|small|medium] [--batch B]
+                  [--kind det|rec|e2e] [--size tiny|small|medium] [--batch B]
 
 One process per GPU (torchrun for N > 1); images shard across ranks with no
 collective on the data path (weak scaling).  A step is one forward of the
@@ -15,6 +15,13 @@ rank's batch.  `value` is device-timed throughput with inputs resident in HBM
 (the model's own input slot), each step bracketed by CUDA events on the
 launching stream with an L2 flush between steps; `e2e` is the same metric
 through the C ABI's host-buffer forward (pinned H2D input, D2H output).
+
+The default line also carries two secondary figures of the same run
+(`secondary`): the medium recognizer in BF16 (config 4, crops/s, device-timed)
+and end-to-end pages (config 5: 1920x1080 synthetic pages through the OCR
+engine -- detector, DB postprocess, rectification, recognizer, CTC text --
+pages/s by wall clock around the public batch call).  `--kind e2e` makes the
+page pipeline the headline.
 """
 
 from __future__ import annotations
@@ -164,9 +171,21 @@ def cpu_baseline(args, shape, seconds=12.0):
 def run_reference(args):
     """--impl reference: the reference's CPU algorithm (the oracle port; the Rust crate cannot be built here)."""
     rank = int(os.environ.get("RANK", "0"))
-    shape, name, unit, metric = _workload(args)
     if rank != 0:
         return
+    if args.kind == "e2e":
+        tmp = tempfile.mkdtemp(prefix="ppocr_e2e_ref_")
+        cpu = cpu_baseline_e2e(tmp, seconds=20.0)
+        line = {"impl": "reference", "metric": "e2e pages/s @1920x1080 (tiny det + DB postprocess + tiny rec + CTC)",
+                "value": cpu["value"], "unit": "pages/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(1000.0 / cpu["value"], 3) if cpu["value"] else None, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "config 5 pages through the CPU restatement of the reference pipeline"},
+                "cpu_baseline": cpu,
+                "e2e": {"value": cpu["value"], "unit": "pages/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    shape, name, unit, metric = _workload(args)
     import torch
 
     from oracle import model as om
@@ -197,6 +216,178 @@ def run_reference(args):
         "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+E2E_SIZE = (1080, 1920)
+
+
+def _e2e_pages(count, rank, world):
+    """Config 5 pages for this rank (page ids dealt round-robin): 30-80 dark stroke blocks,
+    height 16-40, width 40-600, +-15 degrees, on a light noisy background."""
+    from ppocr_b200 import seeded, sharding
+
+    ids = sharding.round_robin(count * world, world, rank)
+    return [seeded.text_page_rgb8(E2E_SIZE[0], E2E_SIZE[1], seed=5000 + i, blocks=(30, 80), block_h=(16, 40),
+                                  block_w=(40, 600), max_angle=15.0, background=(180, 250)) for i in ids]
+
+
+def _e2e_models(tmp):
+    from ppocr_b200 import seeded
+
+    det = seeded.write_weights(os.path.join(tmp, "e2e_det_tiny.safetensors"), "det", "tiny", 0, "spec")
+    rec = seeded.write_weights(os.path.join(tmp, "e2e_rec_tiny.safetensors"), "rec", "tiny", 0, "spec")
+    d = os.path.join(tmp, "e2e_dict.txt")
+    with open(d, "w", encoding="utf-8") as f:
+        f.write("\n".join(seeded.synthetic_dictionary("tiny")) + "\n")
+    return det, rec, d
+
+
+def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp):
+    """Pages/s of the OCR engine's batch call over this rank's pages (max over ranks of the wall time)."""
+    import ppocr_b200 as P
+    from ppocr_b200 import sharding
+
+    det, rec, d = _e2e_models(tmp)
+    pages = _e2e_pages(pages_per_rank, rank, world)
+    eng = P.Engine(gpu, det, rec, d)
+    for _ in range(max(1, warmup)):
+        res = eng.recognize_batch(pages)
+    lines = sum(len(r["lines"]) for r in res)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        eng.recognize_batch(pages)
+    dt = sharding.max_over_ranks(time.perf_counter() - t0)
+    eng.close()
+    value = pages_per_rank * world * steps / dt
+    return {"metric": "e2e pages/s @1920x1080 (tiny det + DB postprocess + tiny rec + CTC)", "value": round(value, 2),
+            "unit": "pages/s", "ms_per_page": round(1000 * dt / (pages_per_rank * steps), 3),
+            "pages_per_step_per_gpu": pages_per_rank, "steps": steps, "lines_per_page": round(lines / len(pages), 1),
+            "api": "ppocr_engine_recognize_batch (host RGB8 pages in, JSON out)",
+            "h2d_bytes_per_step": int(sum(p.size for p in pages)),
+            "data": "synthetic config-5 pages, seeded random-init (spec) weights"}
+
+
+def cpu_baseline_e2e(tmp, seconds=12.0):
+    """The oracle pipeline (torch-CPU detector + restated DB postprocess + recognizer + CTC) on pages."""
+    import torch
+
+    from oracle import model as om
+    from oracle import pipeline as opl
+    from oracle import postprocess as opost
+    from oracle import preprocess as opre
+    from ppocr_b200 import seeded
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    det, rec, _ = _e2e_models(tmp)
+    odet, orec = om.load_detector(det, "tiny"), om.load_recognizer(rec, "tiny")
+    words = seeded.synthetic_dictionary("tiny")
+    pages = _e2e_pages(2, 0, 1)
+    n, t0 = 0, time.perf_counter()
+    for page in pages:
+        h, w = page.shape[:2]
+        iw, ih = opre.detector_input_size(w, h, 736)
+        prob = odet.forward(opre.prepare_detector(page, iw, ih))[0, 0]
+        dets = opl.extract_detections(prob, ih, iw, (w, h), (iw, ih))
+        for idx, width, contents in opl.recognition_batches(dets):
+            x = np.concatenate([opre.prepare_recognizer_crop(page, dets[i].polygon, width, c)
+                                for i, c in zip(idx, contents)])
+            probs = orec.forward(x)
+            for k, c in enumerate(contents):
+                opost.decode_ctc_greedy(probs[k], words, c, width)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "pages/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} config-5 pages through the torch-CPU oracle pipeline"}
+
+
+def measure_rec(gpu, world, barrier, tmp, steps=10, warmup=3, batch=256):
+    """Config 4 secondary figure: medium recognizer BF16, crops/s device-timed (max over ranks)."""
+    import torch
+
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded, sharding
+
+    wpath = os.path.join(tmp, "rec_medium.safetensors")
+    seeded.write_weights(wpath, "rec", "medium", 0, "spec")
+    shape = (batch, 3, 48, 320)
+    model = P.Recognizer.load(gpu, wpath, "medium", shape, precision="bf16")
+    x = seeded.rec_batch(batch, 320, seed=2000 + int(os.environ.get("RANK", "0")))
+    din, _ = model.device_buffers()
+    _device_view(din, x.size, torch).copy_(torch.from_numpy(x.reshape(-1)))
+    stream = torch.cuda.Stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        model.run(stream.cuda_stream)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            model.run(stream.cuda_stream)
+            ends[i].record(stream)
+    torch.cuda.synchronize()
+    total = sharding.max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    ops, prof = model.ops(), model.profile(runs=3)
+    gemm = [(o, ms) for o, ms in zip(ops, prof) if o["kind"] == "gemm"]
+    g_ms = sum(ms for _, ms in gemm)
+    g_tf = sum(o["flops"] for o, _ in gemm) / (g_ms / 1000.0) / 1e12 if g_ms else 0.0
+    _, tflops, src = _peaks()
+    model.close()
+    del flush
+    return {"metric": "rec crops/s @48x320 (medium recognizer, batch 256/GPU)", "value": round(batch * world * steps / (total / 1000.0), 2),
+            "unit": "crops/s", "ms_per_step": round(total / steps, 4), "dtype": "bf16",
+            "gemm_roofline": {"bound": "tensor", "achieved": round(g_tf, 2), "peak": tflops, "unit": "TFLOP/s",
+                              "frac": round(g_tf / tflops, 4), "time_share": round(g_ms / sum(prof), 4),
+                              "peak_source": src}}
+
+
+def run_e2e(args):
+    import torch
+    import torch.distributed as dist
+
+    import ppocr_b200 as P
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    tmp = tempfile.mkdtemp(prefix=f"ppocr_e2e_{rank}_")
+    gpu = P.Gpu(local)
+    with _Clocks(local) as clocks:
+        r = measure_e2e(gpu, args.batch, args.steps, args.warmup, world, rank, barrier, tmp)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_e2e(tmp)
+    if rank == 0:
+        line = {"metric": r["metric"], "value": r["value"], "unit": "pages/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(r["ms_per_page"] * args.batch, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": r["data"],
+                "config": {"workload": "config 5: 1920x1080 pages -> tiny det -> DB -> rectify -> tiny rec -> CTC",
+                           "pages_per_step_per_gpu": args.batch, "parallelism": f"dp{world} (pages sharded, no collective)",
+                           "lines_per_page": r["lines_per_page"]},
+                "roofline": None, "cpu_baseline": cpu,
+                "e2e": {"value": r["value"], "unit": "pages/s", "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                        "d2h_bytes_per_step": None, "api": r["api"]},
+                "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    gpu.close()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_b200(args):
@@ -338,6 +529,12 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args, shape)
 
+    secondary = None
+    if args.kind == "det" and not args.no_secondary:
+        model.close()
+        secondary = {"rec": measure_rec(gpu, world, barrier, tmp),
+                     "e2e_pages": measure_e2e(gpu, 8, 3, 1, world, rank, barrier, tmp)}
+
     launches_per_step = sum(1 for op in ops)
     if rank == 0:
         line = {
@@ -351,6 +548,7 @@ def run_b200(args):
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(), "wall_s": round(wall, 3), "output_finite": finite,
             "step_ms_min_max": [round(min(step_ms), 4), round(max(step_ms), 4)],
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     model.close()
@@ -365,19 +563,22 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--kind", default="det", choices=["det", "rec"])
+    ap.add_argument("--kind", default="det", choices=["det", "rec", "e2e"])
     ap.add_argument("--size", default="tiny", choices=["tiny", "small", "medium"])
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--precision", default=None, choices=[None, "fp32", "bf16"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.batch is None:
-        args.batch = 32 if args.kind == "det" else 256
+        args.batch = {"det": 32, "rec": 256, "e2e": 16}[args.kind]
     if args.impl == "reference":
         run_reference(args)
+    elif args.kind == "e2e":
+        run_e2e(args)
     else:
         run_b200(args)
 

@@ -275,6 +275,19 @@ int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image,
                                    const size_t* content_widths, int32_t* indices, float* probabilities,
                                    float* margins);
 
+/* ppocr_recognizer_forward_crops over crops of several images (crop i from
+ * images[i]) filling the first `count` <= batch slots; unused slots are
+ * zero-filled and the statistics are returned for the first `count` rows.
+ * Each crop's result does not depend on the other slots. */
+int ppocr_recognizer_forward_crops_ex(ppocr_model* model, const ppocr_image* const* images, size_t count,
+                                      const float* corners, const size_t* content_widths, int32_t* indices,
+                                      float* probabilities, float* margins);
+
+/* Detector only: forward_image (full-image corners) of `count` == batch
+ * images at once; probability maps [count, h, w]. */
+int ppocr_detector_forward_images(ppocr_model* model, const ppocr_image* const* images, size_t count,
+                                  float* probabilities);
+
 /* DetectorPostprocessOptions (src/ocr.rs:231-271). */
 typedef struct ppocr_postprocess_options {
     float binary_threshold; /* 0.2 */
@@ -347,6 +360,14 @@ void ppocr_engine_destroy(ppocr_engine* engine);
 int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_length, uint32_t width,
                            uint32_t height, int format, char** result, size_t* result_length);
 void ppocr_string_free(char* text);
+/* OcrEngine::recognize over `count` pages at once (same results per page as
+ * ppocr_engine_recognize): pages of one detector input size run through the
+ * detector together, the DB postprocess runs on host threads, and crops of
+ * all pages that share a canvas width are recognized in shared batches.
+ * results[i] / result_lengths[i] as for ppocr_engine_recognize. */
+int ppocr_engine_recognize_batch(ppocr_engine* engine, size_t count, const uint8_t* const* rgb,
+                                 const size_t* rgb_lengths, const uint32_t* widths, const uint32_t* heights,
+                                 int format, char** results, size_t* result_lengths);
 
 #ifdef __cplusplus
 }

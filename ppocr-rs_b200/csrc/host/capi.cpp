@@ -527,21 +527,89 @@ int ppocr_recognizer_forward_ctc(ppocr_model* model, const float* input, size_t 
     });
 }
 
+namespace {
+
+// Rectifies crops of (possibly different) images into the recognizer's input
+// slots 0..count-1, zero-fills the unused slots, runs the forward and returns
+// the greedy-CTC statistics of the first `count` rows.
+void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+                   const size_t* content_widths, int32_t* indices, float* probabilities, float* margins) {
+    if (!model || !images || !corners || !content_widths) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+    if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "crop forward needs a recognizer");
+    if (count == 0 || count > (size_t)model->m.n)
+        fail(PPOCR_ERR_INVALID_INPUT, "crop count " + std::to_string(count) + " is outside 1..=" + std::to_string(model->m.n));
+    for (size_t i = 0; i < count; ++i) {
+        if (!images[i]) fail(PPOCR_ERR_INVALID_INPUT, "null image");
+        if (images[i]->gpu != model->gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        if (content_widths[i] == 0 || content_widths[i] > (size_t)model->m.w)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: content width outside 1..=input width");
+    }
+    for (size_t i = 0; i < count * 8; ++i)
+        if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
+    std::lock_guard<std::mutex> lock(model->gpu->mu);
+    model->gpu->bind();
+    model->gpu->ensure_arena(model->m.plan.arena_bytes);
+    cudaStream_t s = model->gpu->stream;
+    float* in = static_cast<float*>(model->tensor(model->m.input));
+    const size_t per = (size_t)3 * model->m.h * model->m.w;
+    for (size_t i = 0; i < count; ++i) {
+        PreprocessParams p = make_preprocess(images[i], corners + 8 * i, content_widths[i], (size_t)model->m.h,
+                                             (size_t)model->m.w, false);
+        p.out = in + i * per;
+        cuda_check(launch_preprocess(p, s), "launch crop rectification");
+    }
+    if (count < (size_t)model->m.n)
+        cuda_check(cudaMemsetAsync(in + count * per, 0, ((size_t)model->m.n - count) * per * sizeof(float), s),
+                   "clear unused crop slots");
+    model->run(s);
+    const size_t rows = count * model->m.t;
+    std::vector<int32_t> idx(rows);
+    std::vector<float> prob(rows);
+    download(model, model->m.index, idx.data(), rows * 4);
+    download(model, model->m.max_prob, prob.data(), rows * 4);
+    if (margins) download(model, model->m.margin, margins, rows * 4);
+    wait_stream(s, 0);
+    // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
+    for (size_t r = 0; r < rows; ++r)
+        if (idx[r] < 0 || idx[r] >= model->m.classes || !std::isfinite(prob[r]))
+            fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+    if (indices) std::memcpy(indices, idx.data(), rows * 4);
+    if (probabilities) std::memcpy(probabilities, prob.data(), rows * 4);
+}
+
+}  // namespace
+
 int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image, size_t count, const float* corners,
                                    const size_t* content_widths, int32_t* indices, float* probabilities,
                                    float* margins) {
     return guard([&] {
-        if (!model || !image || !corners || !content_widths) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
-        if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "crop forward needs a recognizer");
-        if (image->gpu != model->gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
         if (count != (size_t)model->m.n)
             fail(PPOCR_ERR_INVALID_INPUT, "crop count " + std::to_string(count) + " does not match the batch " +
                                               std::to_string(model->m.n));
-        for (size_t i = 0; i < count * 8; ++i)
-            if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
-        for (size_t i = 0; i < count; ++i)
-            if (content_widths[i] == 0 || content_widths[i] > (size_t)model->m.w)
-                fail(PPOCR_ERR_INVALID_INPUT, "invalid input: content width outside 1..=input width");
+        std::vector<const ppocr_image*> images(count, image);
+        forward_crops(model, images.data(), count, corners, content_widths, indices, probabilities, margins);
+    });
+}
+
+int ppocr_recognizer_forward_crops_ex(ppocr_model* model, const ppocr_image* const* images, size_t count,
+                                      const float* corners, const size_t* content_widths, int32_t* indices,
+                                      float* probabilities, float* margins) {
+    return guard([&] { forward_crops(model, images, count, corners, content_widths, indices, probabilities, margins); });
+}
+
+int ppocr_detector_forward_images(ppocr_model* model, const ppocr_image* const* images, size_t count,
+                                  float* probabilities) {
+    return guard([&] {
+        if (!model || !images || !probabilities) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (model->m.kind != Kind::Detector) fail(PPOCR_ERR_INVALID_INPUT, "image batch forward needs a detector");
+        if (count != (size_t)model->m.n)
+            fail(PPOCR_ERR_INVALID_INPUT, "image count " + std::to_string(count) + " does not match the batch " +
+                                              std::to_string(model->m.n));
+        for (size_t i = 0; i < count; ++i) {
+            if (!images[i]) fail(PPOCR_ERR_INVALID_INPUT, "null image");
+            if (images[i]->gpu != model->gpu) fail(PPOCR_ERR_INVALID_INPUT, "image was uploaded to a different GPU");
+        }
         std::lock_guard<std::mutex> lock(model->gpu->mu);
         model->gpu->bind();
         model->gpu->ensure_arena(model->m.plan.arena_bytes);
@@ -549,25 +617,17 @@ int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image,
         float* in = static_cast<float*>(model->tensor(model->m.input));
         const size_t per = (size_t)3 * model->m.h * model->m.w;
         for (size_t i = 0; i < count; ++i) {
-            PreprocessParams p = make_preprocess(image, corners + 8 * i, content_widths[i], (size_t)model->m.h,
-                                                 (size_t)model->m.w, false);
+            const float w = (float)images[i]->width, h = (float)images[i]->height;
+            const float corners[8] = {0.f, 0.f, w, 0.f, w, h, 0.f, h};
+            PreprocessParams p = make_preprocess(images[i], corners, (size_t)model->m.w, (size_t)model->m.h,
+                                                 (size_t)model->m.w, true);
             p.out = in + i * per;
-            cuda_check(launch_preprocess(p, s), "launch crop rectification");
+            cuda_check(launch_preprocess(p, s), "launch preprocess");
         }
+        cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), s), "reset flags");
         model->run(s);
-        const size_t rows = (size_t)model->m.n * model->m.t;
-        std::vector<int32_t> idx(rows);
-        std::vector<float> prob(rows);
-        download(model, model->m.index, idx.data(), rows * 4);
-        download(model, model->m.max_prob, prob.data(), rows * 4);
-        if (margins) download(model, model->m.margin, margins, rows * 4);
-        wait_stream(s, 0);
-        // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
-        for (size_t r = 0; r < rows; ++r)
-            if (idx[r] < 0 || idx[r] >= model->m.classes || !std::isfinite(prob[r]))
-                fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
-        if (indices) std::memcpy(indices, idx.data(), rows * 4);
-        if (probabilities) std::memcpy(probabilities, prob.data(), rows * 4);
+        download(model, model->output_tid(), probabilities, model->m.output_elements * 4);
+        finish(model, model->output_tid(), model->m.output_elements);
     });
 }
 

@@ -7,16 +7,25 @@
 // ordered by aspect ratio and recognized six at a time on a canvas of the
 // chunk's width, each chunk rectified on the device straight into the
 // recognizer's input; only the per-step arg-max classes and probabilities
-// come back for the CTC text assembly.  Models are cached per input shape
-// (two detector and four recognizer shapes, the reference's limits, with
-// the recognizer's packed weights shared between shapes).
+// come back for the CTC text assembly.  Models are cached per input shape,
+// the recognizer's packed weights shared between shapes.
+//
+// The batch entry point gives every page the same result as the one-page
+// call: a crop's recognizer output depends only on its own canvas width and
+// pixels (every kernel treats batch entries independently and chooses its
+// configuration from per-image shapes), so crops of all pages that share a
+// canvas width run in shared batches, with unused slots zero-filled.
+#include <algorithm>
 #include <array>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <memory>
 #include <sstream>
+#include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.hpp"
@@ -67,6 +76,27 @@ std::string read_file(const char* path) {
 
 using Shape = std::array<size_t, 4>;
 
+// Cached model shapes: a few detector page sizes and batch sizes, and one
+// recognizer per (batch, canvas width) in use.
+constexpr size_t kDetectorCache = 4, kRecognizerCache = 16;
+constexpr size_t kDetectorBatch = 8;     // pages per detector forward
+constexpr size_t kRecognizerBatch = 64;  // crops per recognizer forward
+
+struct ImageHandle {
+    ppocr_image* p = nullptr;
+    ImageHandle() = default;
+    ImageHandle(const ImageHandle&) = delete;
+    ImageHandle& operator=(const ImageHandle&) = delete;
+    ImageHandle(ImageHandle&& o) noexcept : p(o.p) { o.p = nullptr; }
+    ~ImageHandle() { ppocr_image_destroy(p); }
+};
+
+size_t pow2_at_least(size_t n) {
+    size_t b = 1;
+    while (b < n) b <<= 1;
+    return b;
+}
+
 }  // namespace
 
 struct ppocr_engine {
@@ -90,7 +120,7 @@ struct ppocr_engine {
     ppocr_model* detector(const Shape& shape) {
         for (auto& e : det_cache)
             if (e.first == shape) return e.second;
-        if (det_cache.size() == 2) {
+        if (det_cache.size() == kDetectorCache) {
             ppocr_model_destroy(det_cache.front().second);
             det_cache.erase(det_cache.begin());
         }
@@ -103,7 +133,7 @@ struct ppocr_engine {
     ppocr_model* recognizer(const Shape& shape) {
         for (auto& e : rec_cache)
             if (e.first == shape) return e.second;
-        if (rec_cache.size() == 4) {
+        if (rec_cache.size() == kRecognizerCache) {
             ppocr_model_destroy(rec_cache.front().second);
             rec_cache.erase(rec_cache.begin());
         }
@@ -115,6 +145,112 @@ struct ppocr_engine {
         }
         rec_cache.emplace_back(shape, m);
         return m;
+    }
+
+    struct Page {
+        const uint8_t* rgb;
+        size_t len;
+        uint32_t width, height;
+    };
+
+    std::vector<OcrResult> recognize_batch(const std::vector<Page>& pages) {
+        const size_t np = pages.size();
+        std::vector<OcrResult> res(np);
+        std::vector<ImageHandle> imgs(np);
+        for (size_t i = 0; i < np; ++i) {
+            if (!pages[i].rgb) fail(PPOCR_ERR_INVALID_INPUT, "image pixels are null");
+            res[i].source_w = pages[i].width;
+            res[i].source_h = pages[i].height;
+            detector_input_size(pages[i].width, pages[i].height, max_side, &res[i].input_w, &res[i].input_h);
+            check(ppocr_upload_rgb(gpu, pages[i].width, pages[i].height, pages[i].rgb, pages[i].len, &imgs[i].p));
+        }
+        // Detector: pages of one input size, kDetectorBatch per forward.
+        std::vector<std::vector<float>> probs(np);
+        std::map<std::pair<uint32_t, uint32_t>, std::vector<size_t>> by_size;
+        for (size_t i = 0; i < np; ++i) by_size[{res[i].input_h, res[i].input_w}].push_back(i);
+        for (const auto& [hw, idx] : by_size) {
+            for (size_t s = 0; s < idx.size(); s += kDetectorBatch) {
+                const size_t n = std::min(kDetectorBatch, idx.size() - s);
+                ppocr_model* det = detector(Shape{n, 3, hw.first, hw.second});
+                std::vector<const ppocr_image*> batch(n);
+                for (size_t k = 0; k < n; ++k) batch[k] = imgs[idx[s + k]].p;
+                const size_t per = (size_t)hw.first * hw.second;
+                std::vector<float> out(n * per);
+                check(ppocr_detector_forward_images(det, batch.data(), n, out.data()));
+                for (size_t k = 0; k < n; ++k) probs[idx[s + k]].assign(out.begin() + k * per, out.begin() + (k + 1) * per);
+            }
+        }
+        // DB postprocess on host threads.
+        std::vector<std::vector<Detection>> dets(np);
+        std::vector<std::string> errors(np);
+        std::atomic<size_t> next{0};
+        const size_t workers = std::max<size_t>(1, std::min<size_t>(np, std::thread::hardware_concurrency()));
+        std::vector<std::thread> pool;
+        for (size_t t = 0; t < workers; ++t)
+            pool.emplace_back([&] {
+                for (size_t i = next++; i < np; i = next++) {
+                    try {
+                        dets[i] = extract_detections(probs[i].data(), res[i].input_h, res[i].input_w, pages[i].width,
+                                                     pages[i].height, res[i].input_w, res[i].input_h, post);
+                    } catch (const std::exception& e) {
+                        errors[i] = e.what();
+                    }
+                }
+            });
+        for (auto& t : pool) t.join();
+        for (size_t i = 0; i < np; ++i)
+            if (!errors[i].empty()) fail(PPOCR_ERR_INVALID_INPUT, errors[i]);
+        // Crops of every page, grouped by their chunk's canvas width.
+        struct Crop {
+            size_t page, det, content;
+        };
+        std::map<size_t, std::vector<Crop>> by_width;
+        std::vector<std::vector<Decoded>> decoded(np);
+        for (size_t i = 0; i < np; ++i) {
+            decoded[i].resize(dets[i].size());
+            for (const RecBatch& b : recognition_batches(dets[i]))
+                for (size_t k = 0; k < b.index.size(); ++k) by_width[b.width].push_back(Crop{i, b.index[k], b.content[k]});
+        }
+        for (const auto& [width, crops] : by_width) {
+            for (size_t s = 0; s < crops.size(); s += kRecognizerBatch) {
+                const size_t n = std::min(kRecognizerBatch, crops.size() - s);
+                ppocr_model* rec = recognizer(Shape{pow2_at_least(n), 3, 48, width});
+                size_t out_shape[4] = {0, 0, 0, 0};
+                check(ppocr_model_output_shape(rec, out_shape, nullptr, nullptr));
+                const size_t steps = out_shape[1];
+                std::vector<const ppocr_image*> ims(n);
+                std::vector<float> corners(n * 8);
+                std::vector<size_t> contents(n);
+                for (size_t k = 0; k < n; ++k) {
+                    const Crop& c = crops[s + k];
+                    ims[k] = imgs[c.page].p;
+                    contents[k] = c.content;
+                    for (int q = 0; q < 4; ++q) {
+                        corners[k * 8 + 2 * q] = dets[c.page][c.det].poly[q].x;
+                        corners[k * 8 + 2 * q + 1] = dets[c.page][c.det].poly[q].y;
+                    }
+                }
+                std::vector<int32_t> idx(n * steps);
+                std::vector<float> p(n * steps);
+                check(ppocr_recognizer_forward_crops_ex(rec, ims.data(), n, corners.data(), contents.data(), idx.data(),
+                                                        p.data(), nullptr));
+                for (size_t k = 0; k < n; ++k) {
+                    const Crop& c = crops[s + k];
+                    decoded[c.page][c.det] = decode_ctc_steps(idx.data() + k * steps, p.data() + k * steps, steps, classes,
+                                                              dict, c.content, width);
+                }
+            }
+        }
+        for (size_t i = 0; i < np; ++i)
+            for (size_t d = 0; d < dets[i].size(); ++d) {
+                OcrLine l;
+                std::copy(dets[i][d].poly, dets[i][d].poly + 4, l.poly);
+                l.detection_score = dets[i][d].score;
+                l.text = decoded[i][d].text;
+                l.recognition_score = decoded[i][d].score;
+                res[i].lines.push_back(std::move(l));
+            }
+        return res;
     }
 
     OcrResult recognize(const uint8_t* rgb, size_t len, uint32_t width, uint32_t height) {
@@ -320,6 +456,32 @@ int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_
         std::memcpy(buf, s.c_str(), s.size() + 1);
         *result = buf;
         if (result_length) *result_length = s.size();
+    });
+}
+
+int ppocr_engine_recognize_batch(ppocr_engine* engine, size_t count, const uint8_t* const* rgb, const size_t* rgb_lengths,
+                                 const uint32_t* widths, const uint32_t* heights, int format, char** results,
+                                 size_t* result_lengths) {
+    return guard([&] {
+        if (!engine || !rgb || !rgb_lengths || !widths || !heights || !results) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (format != 0 && format != 1) fail(PPOCR_ERR_INVALID_INPUT, "format must be 0 (JSON) or 1 (text)");
+        std::vector<ppocr_engine::Page> pages(count);
+        for (size_t i = 0; i < count; ++i) pages[i] = ppocr_engine::Page{rgb[i], rgb_lengths[i], widths[i], heights[i]};
+        const std::vector<OcrResult> r = engine->recognize_batch(pages);
+        std::vector<char*> out(count, nullptr);
+        try {
+            for (size_t i = 0; i < count; ++i) {
+                const std::string s = format == 0 ? result_json(r[i]) : result_text(r[i]);
+                out[i] = static_cast<char*>(std::malloc(s.size() + 1));
+                if (!out[i]) fail(PPOCR_ERR_GPU, "out of host memory");
+                std::memcpy(out[i], s.c_str(), s.size() + 1);
+                if (result_lengths) result_lengths[i] = s.size();
+            }
+        } catch (...) {
+            for (char* p : out) std::free(p);
+            throw;
+        }
+        for (size_t i = 0; i < count; ++i) results[i] = out[i];
     });
 }
 

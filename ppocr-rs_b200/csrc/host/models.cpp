@@ -349,7 +349,7 @@ public:
     // SE gate of `x` (channel_sum + se_mlp); returns an FP32 [n][c] tensor id.
     int se_gate(const std::string& name, const Act4& x, const ConvWeight& reduce, const ConvWeight& expand, float alpha) {
         const int n = x.n, c = x.c, hw = x.h * x.w, r = reduce.cout, xt = x.tid;
-        const int chunks = channel_sum_chunks(n, hw, c);
+        const int chunks = channel_sum_chunks(hw, c);
         const int sum = m_.plan.add_raw(name + ".sum", (size_t)n * chunks * c * 4);
         const int gate = m_.plan.add_raw(name + ".gate", (size_t)n * c * 4);
         const size_t w1 = m_.blob.add_f32(reduce.w), b1 = m_.blob.add_f32(reduce.b);

@@ -202,7 +202,7 @@ struct PoolParams {
     float* sum = nullptr;      // [n][chunks][c]
     DType dtype = DT_F32;
 };
-int channel_sum_chunks(int n, int hw, int c);
+int channel_sum_chunks(int hw, int c);
 cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream);
 
 // gate[img][c] = hard_sigmoid(W2 relu(W1 mean + b1) + b2; alpha, 0.5),

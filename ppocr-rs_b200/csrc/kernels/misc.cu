@@ -559,14 +559,13 @@ inline unsigned grid_for(long long total, int threads) {
 
 }  // namespace
 
-int channel_sum_chunks(int n, int hw, int c) {
-    // Enough (chunk, image) blocks for ~4 per SM, each summing at least 8
-    // pixel rows per thread; fewer chunks keep the MLP's partial reads short.
+int channel_sum_chunks(int hw, int c) {
+    // Pixel chunks of one image: each thread sums at least 8 pixel rows.  The
+    // count depends on the image's shape only, so an image's pooled sums (and
+    // everything after them) are the same bits whatever batch it runs in.
     const int cg = c / 4 > 0 ? c / 4 : 1;
     const int rows = 256 / cg > 0 ? 256 / cg : 1;
     int chunks = (hw + rows * 8 - 1) / (rows * 8);
-    const int want = (4 * 148 + n - 1) / (n > 0 ? n : 1);
-    if (chunks > want) chunks = want;
     if (chunks > 64) chunks = 64;
     if (chunks < 1) chunks = 1;
     return chunks;

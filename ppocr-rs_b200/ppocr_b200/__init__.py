@@ -203,6 +203,11 @@ def library() -> C.CDLL:
         "ppocr_engine_recognize": (I, [P, C.POINTER(C.c_uint8), S, C.c_uint32, C.c_uint32, I,
                                        C.POINTER(C.c_void_p), C.POINTER(S)]),
         "ppocr_string_free": (None, [C.c_void_p]),
+        "ppocr_engine_recognize_batch": (I, [P, S, C.POINTER(C.c_void_p), C.POINTER(S), C.POINTER(C.c_uint32),
+                                             C.POINTER(C.c_uint32), I, C.POINTER(C.c_void_p), C.POINTER(S)]),
+        "ppocr_recognizer_forward_crops_ex": (I, [P, C.POINTER(C.c_void_p), S, FP, C.POINTER(S),
+                                                  C.POINTER(C.c_int32), FP, FP]),
+        "ppocr_detector_forward_images": (I, [P, C.POINTER(C.c_void_p), S, FP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -677,6 +682,30 @@ class Engine:
         finally:
             library().ppocr_string_free(out)
         return json.loads(text) if fmt == "json" else text
+
+    def recognize_batch(self, pages, fmt: str = "json"):
+        """OcrEngine::recognize over several RGB8 pages at once (same per-page results)."""
+        import json
+
+        pages = [np.ascontiguousarray(p, dtype=np.uint8) for p in pages]
+        n = len(pages)
+        ptrs = (C.c_void_p * n)(*[p.ctypes.data for p in pages])
+        lens = (C.c_size_t * n)(*[p.size for p in pages])
+        ws = (C.c_uint32 * n)(*[p.shape[1] for p in pages])
+        hs = (C.c_uint32 * n)(*[p.shape[0] for p in pages])
+        outs = (C.c_void_p * n)()
+        olens = (C.c_size_t * n)()
+        _check(library().ppocr_engine_recognize_batch(self._h, n, ptrs, lens, ws, hs, 0 if fmt == "json" else 1,
+                                                      outs, olens))
+        res = []
+        try:
+            for i in range(n):
+                text = C.string_at(outs[i], olens[i]).decode("utf-8")
+                res.append(json.loads(text) if fmt == "json" else text)
+        finally:
+            for i in range(n):
+                library().ppocr_string_free(outs[i])
+        return res
 
     def close(self):
         if getattr(self, "_h", None):

@@ -121,3 +121,19 @@ def test_engine_rejects_mismatched_dictionary(gpu, setup, tmp_path):
     d.write_text("a\nb\n")
     with pytest.raises(P.InvalidInput):
         P.Engine(gpu, det_path, rec_path, str(d))
+
+
+def test_engine_batch_matches_single_pages(gpu, setup):
+    # Pages of two sizes; every page's result from the batched call must equal
+    # its own single-page result exactly (crops of all pages share batches).
+    det_path, rec_path, dict_path, _, rgb = setup
+    pages = [rgb,
+             seeded.text_page_rgb8(180, 320, seed=33, blocks=(6, 10), block_h=(12, 28), block_w=(40, 200),
+                                   max_angle=15.0, background=(170, 250)),
+             seeded.text_page_rgb8(240, 200, seed=34, blocks=(4, 8), block_h=(12, 28), block_w=(40, 150),
+                                   max_angle=15.0, background=(170, 250))]
+    eng = P.Engine(gpu, det_path, rec_path, dict_path)
+    batch = eng.recognize_batch(pages)
+    single = [P.Engine(gpu, det_path, rec_path, dict_path).recognize(p) for p in pages]
+    assert batch == single
+    assert sum(len(r["lines"]) for r in batch) > 0
