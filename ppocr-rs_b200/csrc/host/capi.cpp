@@ -46,6 +46,43 @@ void wait_stream(cudaStream_t s, int timeout_ms) {
 }  // namespace ppocr
 
 namespace {
+
+// Process-wide pool of pinned host flag pairs: a model load takes one pair
+// instead of pinning a fresh page (cudaMallocHost costs milliseconds), and the
+// pool outlives every device handle.
+class PinnedFlags {
+public:
+    static int* acquire() {
+        std::lock_guard<std::mutex> lock(mu());
+        auto& f = free_list();
+        if (f.empty()) {
+            constexpr size_t kPairs = 1024;
+            int* slab = nullptr;
+            cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&slab), kPairs * 2 * sizeof(int), cudaHostAllocPortable),
+                       "allocate host flags");
+            for (size_t i = 0; i < kPairs; ++i) f.push_back(slab + 2 * i);
+        }
+        int* p = f.back();
+        f.pop_back();
+        return p;
+    }
+    static void release(int* p) {
+        if (!p) return;
+        std::lock_guard<std::mutex> lock(mu());
+        free_list().push_back(p);
+    }
+
+private:
+    static std::mutex& mu() {
+        static std::mutex m;
+        return m;
+    }
+    static std::vector<int*>& free_list() {
+        static std::vector<int*> f;
+        return f;
+    }
+};
+
 struct DeviceWeights {
     void* ptr = nullptr;
     size_t bytes = 0;
@@ -71,7 +108,7 @@ struct ppocr_model {
     ~ppocr_model() {
         if (exec) cudaGraphExecDestroy(exec);
         if (dflags) cudaFree(dflags);
-        if (hflags) cudaFreeHost(hflags);
+        PinnedFlags::release(hflags);
     }
 
     Ctx ctx() const {
@@ -221,7 +258,7 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     }
     gpu->ensure_arena(model->m.plan.arena_bytes);
     cuda_check(cudaMalloc(&model->dflags, 2 * sizeof(int)), "allocate flags");
-    cuda_check(cudaMallocHost(&model->hflags, 2 * sizeof(int)), "allocate host flags");
+    model->hflags = PinnedFlags::acquire();
     return model.release();
 }
 

@@ -78,9 +78,10 @@ using Shape = std::array<size_t, 4>;
 
 // Cached model shapes: a few detector page sizes and batch sizes, and one
 // recognizer per (batch, canvas width) in use.
-constexpr size_t kDetectorCache = 4, kRecognizerCache = 16;
+constexpr size_t kDetectorCache = 4, kRecognizerCache = 32;
 constexpr size_t kDetectorBatch = 8;     // pages per detector forward
 constexpr size_t kRecognizerBatch = 64;  // crops per recognizer forward
+constexpr size_t kSmallBatch = 8;        // the batch of a width's last few crops
 
 struct ImageHandle {
     ppocr_image* p = nullptr;
@@ -91,11 +92,6 @@ struct ImageHandle {
     ~ImageHandle() { ppocr_image_destroy(p); }
 };
 
-size_t pow2_at_least(size_t n) {
-    size_t b = 1;
-    while (b < n) b <<= 1;
-    return b;
-}
 
 }  // namespace
 
@@ -214,7 +210,8 @@ struct ppocr_engine {
         for (const auto& [width, crops] : by_width) {
             for (size_t s = 0; s < crops.size(); s += kRecognizerBatch) {
                 const size_t n = std::min(kRecognizerBatch, crops.size() - s);
-                ppocr_model* rec = recognizer(Shape{pow2_at_least(n), 3, 48, width});
+                // Two batch shapes per canvas width keep the model cache small.
+                ppocr_model* rec = recognizer(Shape{n <= kSmallBatch ? kSmallBatch : kRecognizerBatch, 3, 48, width});
                 size_t out_shape[4] = {0, 0, 0, 0};
                 check(ppocr_model_output_shape(rec, out_shape, nullptr, nullptr));
                 const size_t steps = out_shape[1];
