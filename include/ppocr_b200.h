@@ -49,10 +49,11 @@ enum ppocr_model_size { PPOCR_MEDIUM = 0, PPOCR_SMALL = 1, PPOCR_TINY = 2 };
  *         (the reference's own arithmetic; the parity mode).
  * BF16:   BF16 activations in HBM, tcgen05 BF16 tensor-core GEMMs with FP32
  *         accumulation; all other arithmetic FP32 in registers.
- * TF32X3: FP32 activations; pointwise and dense convs on tcgen05 as
- *         A_hi W_hi + A_hi W_lo + A_lo W_hi with TF32 halves (FP32-class
- *         products, tensor-core accumulation). */
-enum ppocr_precision { PPOCR_PRECISION_FP32 = 0, PPOCR_PRECISION_BF16 = 1, PPOCR_PRECISION_TF32X3 = 2 };
+ * FP32_TC: FP32 activations; pointwise and dense convs on tcgen05 with each
+ *         FP32 operand split into three BF16 pieces (x = x0 + x1 + x2) and
+ *         the six leading products accumulated in FP32 (FP32-class products,
+ *         tensor-core accumulation order). */
+enum ppocr_precision { PPOCR_PRECISION_FP32 = 0, PPOCR_PRECISION_BF16 = 1, PPOCR_PRECISION_FP32_TC = 2 };
 
 typedef struct ppocr_gpu ppocr_gpu;
 typedef struct ppocr_image ppocr_image;
@@ -213,6 +214,21 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
                            int act, const float* residual, int out_bf16, int ldc, int coff, float* c,
                            int* used_tensor_cores, int* wait_error);
 
+/* Diagnostic (new): one convolution through the tcgen05 engine of the BF16
+ * and FP32-class modes.  planes 1: input rounded to BF16, BF16 weights and
+ * output; planes 3: FP32 input / weights split into three BF16 pieces each,
+ * FP32 output.  NHWC input [n, hi, wi, cin] (cin a multiple of 8 / 4), OIHW
+ * weight, symmetric padding, output NHWC [n, ho, wo, cout] in F32.  When
+ * `second` is 1 the input's channels are split into two sources: the first
+ * half direct, the second half read through a 2x2 same-upper max pool
+ * (second == 2: through a x2 nearest upsampling of a half-size tensor given
+ * as x2 [n, hi/2, wi/2, cin/2]).  1x1 / stride 1 / pad 0 with one source runs
+ * the dense-rows mode.  used_tensor_cores / wait_error as for
+ * ppocr_selftest_gemm. */
+int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int cin, int cout, int kh, int kw,
+                          int stride, int pad, int second, const float* x, const float* x2, const float* w,
+                          const float* bias, int act, float* out, int* used_tensor_cores, int* wait_error);
+
 /* Recognizer only: the classifier's pre-softmax logits [n, t, classes]
  * (new; the reference fuses the softmax, src/cpu/backend.rs:1288-1290, so it
  * never exposes them). */
@@ -226,16 +242,6 @@ int ppocr_recognizer_forward_logits(ppocr_model* model, const float* input, size
  * past `content_width` are zero. */
 int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
                      size_t out_h, size_t out_w, int kind, float* output);
-
-/* Diagnostic (new): one FP32 convolution through the FP32 tensor-core path
- * (3xTF32 tcgen05): NHWC input [n, hi, wi, cin] (cin % 4 == 0), OIHW weight
- * [cout, cin, kh, kw], symmetric padding, output NHWC [n, ho, wo, cout].
- * 1x1 / stride 1 / pad 0 runs the dense-rows GEMM mode, anything else the
- * implicit-GEMM gather mode.  used_tensor_cores and wait_error as for
- * ppocr_selftest_gemm. */
-int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
-                        const float* x, const float* w, const float* bias, int act, float* out,
-                        int* used_tensor_cores, int* wait_error);
 
 /* ppocr_preprocess without any device allocation.  This entry point has no
  * counterpart in the reference.  It is for callers that cannot call

@@ -116,7 +116,7 @@ int main(int argc, char** argv) {
     check(ppocr_gpu_create(0, &gpu), "create GPU");
     ppocr_load_options o;
     ppocr_load_options_default(&o);
-    o.precision = a.precision == "bf16" ? PPOCR_PRECISION_BF16 : a.precision == "tf32x3" ? PPOCR_PRECISION_TF32X3 : PPOCR_PRECISION_FP32;
+    o.precision = a.precision == "bf16" ? PPOCR_PRECISION_BF16 : a.precision == "fp32tc" ? PPOCR_PRECISION_FP32_TC : PPOCR_PRECISION_FP32;
     o.use_graph = a.graph ? 1 : 0;
     ppocr_model* model = nullptr;
     if (det) check(ppocr_detector_load_ex(gpu, a.model.c_str(), size, shape, &o, &model), "load detector");

@@ -73,13 +73,15 @@ public:
     }
 
 private:
+    // Never destroyed: models may be released by finalizers after static
+    // destruction has begun at process exit.
     static std::mutex& mu() {
-        static std::mutex m;
-        return m;
+        static std::mutex* m = new std::mutex;
+        return *m;
     }
     static std::vector<int*>& free_list() {
-        static std::vector<int*> f;
-        return f;
+        static std::vector<int*>* f = new std::vector<int*>;
+        return *f;
     }
 };
 
@@ -233,14 +235,14 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     ppocr_load_options o;
     if (options) o = *options;
     else ppocr_load_options_default(&o);
-    if (o.precision != PPOCR_PRECISION_FP32 && o.precision != PPOCR_PRECISION_BF16 && o.precision != PPOCR_PRECISION_TF32X3)
+    if (o.precision != PPOCR_PRECISION_FP32 && o.precision != PPOCR_PRECISION_BF16 && o.precision != PPOCR_PRECISION_FP32_TC)
         fail(PPOCR_ERR_INVALID_INPUT, "unknown precision");
     const DType dt = o.precision == PPOCR_PRECISION_BF16 ? DT_BF16 : DT_F32;
     SafeTensors st = SafeTensors::load(path);
     std::unique_ptr<ppocr_model> model(new ppocr_model());
     model->gpu = gpu;
     model->opts = o;
-    // FP32 runs on the CUDA cores (exact FP32 FMA); BF16 and TF32X3 use tcgen05 unless simt_only.
+    // FP32 runs on the CUDA cores (exact FP32 FMA); BF16 and FP32_TC use tcgen05 unless simt_only.
     const bool tensor_cores = o.simt_only == 0 && o.precision != PPOCR_PRECISION_FP32;
     model->m = detector ? build_detector(st, size, shape, dt, tensor_cores) : build_recognizer(st, size, shape, dt, tensor_cores);
     std::lock_guard<std::mutex> lock(gpu->mu);
@@ -405,7 +407,7 @@ int ppocr_inspect_model(const char* path, int kind, int size, const size_t input
     return guard([&] {
         if (!path || !input_shape) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
         if (kind != 0 && kind != 1) fail(PPOCR_ERR_INVALID_INPUT, "kind must be 0 (detector) or 1 (recognizer)");
-        if (precision != PPOCR_PRECISION_FP32 && precision != PPOCR_PRECISION_BF16 && precision != PPOCR_PRECISION_TF32X3)
+        if (precision != PPOCR_PRECISION_FP32 && precision != PPOCR_PRECISION_BF16 && precision != PPOCR_PRECISION_FP32_TC)
             fail(PPOCR_ERR_INVALID_INPUT, "unknown precision");
         const DType dt = precision == PPOCR_PRECISION_BF16 ? DT_BF16 : DT_F32;
         const bool tc = precision != PPOCR_PRECISION_FP32;
@@ -840,13 +842,16 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
     });
 }
 
-int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
-                        const float* x, const float* w, const float* bias, int act, float* out, int* used_tensor_cores,
-                        int* wait_error) {
+int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride,
+                          int pad, int second, const float* x, const float* x2, const float* w, const float* bias, int act,
+                          float* out, int* used_tensor_cores, int* wait_error) {
     return guard([&] {
         if (!gpu || !x || !w || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
-        if (n <= 0 || hi <= 0 || wi <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0 || cin % 4)
-            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: conv shape (cin must be a multiple of 4)");
+        if (planes != 1 && planes != 3) fail(PPOCR_ERR_INVALID_INPUT, "planes must be 1 or 3");
+        const int ch = planes == 1 ? 8 : 4;
+        if (n <= 0 || hi <= 0 || wi <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0 ||
+            cin % (second ? 2 * ch : ch) || second < 0 || second > 2 || (second == 2 && (!x2 || hi % 2 || wi % 2)))
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: engine test shape");
         const int ho = (hi + 2 * pad - kh) / stride + 1, wo = (wi + 2 * pad - kw) / stride + 1;
         if (ho <= 0 || wo <= 0) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: empty output");
         std::lock_guard<std::mutex> lock(gpu->mu);
@@ -855,43 +860,58 @@ int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout
         cw.cout = cout; cw.cin = cin; cw.kh = kh; cw.kw = kw;
         cw.w.assign(w, w + (size_t)cout * cin * kh * kw);
         cw.b = bias ? std::vector<float>(bias, bias + cout) : std::vector<float>(cout, 0.f);
-        const bool dense = kh == 1 && kw == 1 && stride == 1 && pad == 0;
-        TcConvParams p;
-        p.mode = dense ? 0 : 1;
-        p.m = n * ho * wo;
-        p.n = cout;
-        p.k = kh * kw * cin;
-        const int bn = tc_conv_tile_n(cout);
+        TcEngineParams p;
+        p.planes = planes;
+        p.mode = (kh == 1 && kw == 1 && stride == 1 && pad == 0 && !second) ? 0 : 1;
+        p.m = n * ho * wo; p.n = cout; p.k = kh * kw * cin;
+        const int bn = tc_engine_tile_n(cout, planes);
         p.n_pad = (cout + bn - 1) / bn * bn;
-        p.k_pad = (p.k + 31) / 32 * 32;
-        p.cin4 = cin;
-        p.src_start[0] = 0;
-        p.src_start[1] = cin;
-        p.lda = cin;
-        p.rows_per_image = ho * wo;
-        p.act = act;
-        p.out_h = ho; p.out_w = wo;
-        p.ldc = cout;
-        ConvParams& g = p.conv;
-        g.n = n; g.hi = hi; g.wi = wi; g.cin = cin; g.nsrc = 1; g.ho = ho; g.wo = wo; g.cout = cout;
-        g.kh = kh; g.kw = kw; g.sh = stride; g.sw = stride; g.pt = pad; g.pl = pad;
-        g.src[0].channels = cin; g.src[0].cstride = cin; g.src[0].coff = 0; g.src[0].scale = 1; g.src[0].mode = SRC_NHWC;
+        p.k_pad = (p.k + 63) / 64 * 64;
+        p.lda = cin; p.act = act; p.out_h = ho; p.out_w = wo; p.ldc = cout;
+        ConvGather& g = p.conv;
+        g.hi = hi; g.wi = wi; g.ho = ho; g.wo = wo; g.cin = cin; g.kh = kh; g.kw = kw; g.sh = stride; g.sw = stride;
+        g.pt = pad; g.pl = pad;
         WeightBlob blob;
-        const size_t wo2 = blob.add_f32(pack_tf32_split(cw, cin, p.n_pad, p.k_pad));
+        const size_t wof = blob.add_bf16(pack_engine_kn(cw, planes, p.n_pad, p.k_pad));
         const size_t bo = blob.add_f32(cw.b);
-        const size_t xo = blob.add_f32(std::vector<float>(x, x + (size_t)n * hi * wi * cin));
+        const size_t xn = (size_t)n * hi * wi * cin;
+        std::vector<float> xv(x, x + xn);
+        const size_t xo = planes == 1 ? blob.add_bf16(xv) : blob.add_f32(xv);
+        size_t x2o = 0;
+        if (second == 2) {
+            std::vector<float> v2(x2, x2 + (size_t)n * (hi / 2) * (wi / 2) * (cin / 2));
+            x2o = planes == 1 ? blob.add_bf16(v2) : blob.add_f32(v2);
+        }
         const std::vector<uint8_t>& bytes = blob.bytes();
-        const size_t cbytes = (size_t)p.m * cout * 4;
+        const size_t esize = planes == 1 ? 2 : 4;
+        const size_t cbytes = (size_t)p.m * cout * esize;
         char* d = nullptr;
-        cuda_check(cudaMalloc(&d, bytes.size() + cbytes + 256), "allocate conv test buffers");
+        cuda_check(cudaMalloc(&d, bytes.size() + cbytes + 256), "allocate engine test buffers");
         cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
-        p.w2 = reinterpret_cast<const float*>(d + wo2);
+        p.w = d + wof;
         p.bias = reinterpret_cast<const float*>(d + bo);
-        p.a = reinterpret_cast<const float*>(d + xo);
-        g.src[0].ptr = d + xo;
-        p.c = reinterpret_cast<float*>(d + ((bytes.size() + 255) & ~(size_t)255));
-        if (e == cudaSuccess) e = launch_tc_conv(p, gpu->stream);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(out, p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream);
+        p.a = d + xo;
+        if (!second) {
+            g.nsrc = 1;
+            g.src[0] = ConvSource{d + xo, cin, cin, 0, 1, SRC_NHWC};
+        } else if (second == 1) {
+            // Both halves are views of the one [n, hi, wi, cin] tensor: channels
+            // [0, cin/2) direct, [cin/2, cin) max-pooled.
+            g.nsrc = 2;
+            g.src[0] = ConvSource{d + xo, cin / 2, cin, 0, 1, SRC_NHWC};
+            g.src[1] = ConvSource{d + xo, cin / 2, cin, cin / 2, 1, SRC_NHWC_MAXPOOL};
+        } else {
+            g.nsrc = 2;
+            g.src[0] = ConvSource{d + xo, cin / 2, cin, 0, 1, SRC_NHWC};
+            g.src[1] = ConvSource{d + x2o, cin / 2, cin / 2, 0, 2, SRC_NHWC};
+        }
+        p.c = d + ((bytes.size() + 255) & ~(size_t)255);
+        const bool tc = tc_engine_supported(p);
+        std::vector<uint16_t> hb(planes == 1 ? (size_t)p.m * cout : 0);
+        if (e == cudaSuccess) e = launch_tc_engine(p, gpu->stream);
+        if (e == cudaSuccess)
+            e = planes == 1 ? cudaMemcpyAsync(hb.data(), p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream)
+                            : cudaMemcpyAsync(out, p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
                 wait_stream(gpu->stream, 0);
@@ -901,9 +921,14 @@ int ppocr_selftest_conv(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout
             }
         }
         cudaFree(d);
-        cuda_check(e, "conv self-test");
-        if (used_tensor_cores) *used_tensor_cores = 1;
-        const int err = tc_conv_error_and_clear();
+        cuda_check(e, "engine self-test");
+        if (planes == 1)
+            for (size_t i = 0; i < hb.size(); ++i) {
+                const uint32_t u = (uint32_t)hb[i] << 16;
+                std::memcpy(out + i, &u, 4);
+            }
+        if (used_tensor_cores) *used_tensor_cores = tc ? 1 : 0;
+        const int err = tc_engine_error_and_clear();
         if (wait_error) *wait_error = err;
     });
 }

@@ -93,46 +93,39 @@ public:
     // BF16 storage with tcgen05 GEMMs: SE gates are applied by a gate kernel
     // instead of in the GEMM's A load (the tensor-core path reads A by TMA).
     bool tensor_core_gemms() const { return tc_ && m_.dtype == DT_BF16; }
-    // FP32 storage with 3xTF32 tcgen05 GEMMs and implicit-GEMM convs.
+    // FP32 storage with tcgen05 GEMMs and implicit-GEMM convs on three-way
+    // BF16-split operands (tc_engine.cu, planes 3).
     bool tensor_core_f32() const { return tc_ && m_.dtype == DT_F32; }
+    int engine_planes() const { return m_.dtype == DT_BF16 ? 1 : 3; }
 
-    // Emits a tc_conv op (FP32 mode).  srcs empty: dense rows of `a_tid`.
-    void tc_f32_op(const std::string& name, const ConvWeight& cw, TcConvParams p, const std::vector<Src>& srcs, int a_tid,
-                   int gate, int res_gate, int residual, int out_tid, double flops) {
-        const int taps = cw.kh * cw.kw;
-        int cin4 = 0;
-        for (auto& s : srcs) cin4 += (s.channels + 3) / 4 * 4;
-        if (srcs.empty()) cin4 = cw.cin;
-        const int bn = tc_conv_tile_n(cw.cout);
+    // Emits a tc_engine op.  srcs empty: dense rows of `a_tid` (mode 0);
+    // otherwise the conv window over the sources (mode 1, geometry in `g`).
+    void engine_op(const std::string& name, const ConvWeight& cw, TcEngineParams p, const std::vector<Src>& srcs,
+                   int a_tid, int gate, int residual, int out_tid, double flops) {
+        const int planes = engine_planes();
+        const int bn = tc_engine_tile_n(cw.cout, planes);
+        p.planes = planes;
         p.n = cw.cout;
-        p.k = taps * cin4;
-        p.k_pad = (p.k + 31) / 32 * 32;
+        p.k = cw.kh * cw.kw * cw.cin;
         p.n_pad = (cw.cout + bn - 1) / bn * bn;
-        p.cin4 = cin4;
-        int acc = 0;
-        for (size_t i = 0; i < srcs.size(); ++i) {
-            p.src_start[i] = acc;
-            acc += (srcs[i].channels + 3) / 4 * 4;
-        }
-        p.src_start[srcs.size()] = acc;
-        const size_t woff = m_.blob.add_f32(pack_tf32_split(cw, cin4, p.n_pad, p.k_pad));
+        p.k_pad = (p.k + 63) / 64 * 64;
+        const size_t woff = m_.blob.add_bf16(pack_engine_kn(cw, planes, p.n_pad, p.k_pad));
         const size_t boff = m_.blob.add_f32(cw.b);
-        std::vector<int> reads = {a_tid, gate, res_gate, residual};
+        std::vector<int> reads = {a_tid, gate, residual};
         for (auto& s : srcs) reads.push_back(s.tid);
         std::vector<Src> s2 = srcs;
         m_.plan.add_op(name, reads, {out_tid},
-                       [p, s2, woff, boff, a_tid, gate, res_gate, residual, out_tid](const Ctx& c, cudaStream_t st) mutable {
+                       [p, s2, woff, boff, a_tid, gate, residual, out_tid](const Ctx& c, cudaStream_t st) mutable {
                            for (size_t i = 0; i < s2.size(); ++i) p.conv.src[i].ptr = c.act(s2[i].tid);
-                           p.w2 = c.wf(woff);
+                           p.w = c.wb(woff);
                            p.bias = c.wf(boff);
-                           p.a = static_cast<const float*>(c.act(a_tid));
+                           p.a = c.act(a_tid);
                            p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
-                           p.res_gate = res_gate >= 0 ? static_cast<const float*>(c.act(res_gate)) : nullptr;
-                           p.residual = static_cast<const float*>(c.act(residual));
-                           p.c = static_cast<float*>(c.act(out_tid));
-                           return launch_tc_conv(p, st);
+                           p.residual = c.act(residual);
+                           p.c = c.act(out_tid);
+                           return launch_tc_engine(p, st);
                        },
-                       srcs.empty() ? "gemm" : "conv", (double)p.n_pad * p.k_pad * 8, flops);
+                       srcs.empty() ? "gemm" : "conv", (double)planes * p.n_pad * p.k_pad * 2, flops);
     }
 
     Act4 tensor(const std::string& name, int n, int h, int w, int c) {
@@ -157,12 +150,16 @@ public:
         Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
         if (tensor_core_f32()) {
-            TcConvParams tp;
+            // FP32_TC: the tensor-core engine for NHWC sources whose channels split
+            // into 16-byte chunks.  (BF16 convs stay on the register-tiled SIMT
+            // implicit GEMM, which measured faster than the engine's gather.)
+            TcEngineParams tp;
             tp.mode = 1;
+            tp.planes = engine_planes();
             tp.m = n * ho * wo;
-            ConvParams& g = tp.conv;
-            g.n = n; g.hi = hi; g.wi = wi; g.cin = cin; g.nsrc = (int)srcs.size();
-            g.ho = ho; g.wo = wo; g.cout = cw.cout; g.kh = cw.kh; g.kw = cw.kw; g.sh = sh; g.sw = sw; g.pt = pt; g.pl = pl;
+            ConvGather& g = tp.conv;
+            g.hi = hi; g.wi = wi; g.ho = ho; g.wo = wo; g.cin = cin; g.kh = cw.kh; g.kw = cw.kw;
+            g.sh = sh; g.sw = sw; g.pt = pt; g.pl = pl; g.nsrc = (int)srcs.size();
             for (size_t i = 0; i < srcs.size(); ++i) {
                 g.src[i].channels = srcs[i].channels; g.src[i].cstride = srcs[i].cstride; g.src[i].coff = srcs[i].coff;
                 g.src[i].scale = srcs[i].scale; g.src[i].mode = srcs[i].mode;
@@ -171,11 +168,16 @@ public:
             tp.ldr = cw.cout;
             tp.res_scale = res_scale;
             tp.out_h = ho; tp.out_w = wo;
-            tp.rows_per_image = ho * wo;
             tp.ldc = out_cstride;
             tp.coff = out_coff;
-            tc_f32_op(name, cw, tp, srcs, -1, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
-            return out;
+            tp.k = cw.kh * cw.kw * cin;
+            tp.k_pad = (tp.k + 63) / 64 * 64;
+            tp.n = cw.cout;
+            tp.w = tp.c = reinterpret_cast<void*>(1);   // placeholders for the support check
+            if (tc_engine_supported(tp)) {
+                engine_op(name, cw, tp, srcs, -1, -1, residual, out.tid, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
+                return out;
+            }
         }
         ConvParams p;
         p.n = n; p.hi = hi; p.wi = wi; p.cin = cin; p.nsrc = (int)srcs.size();
@@ -262,8 +264,8 @@ public:
     // Pointwise conv / linear over `rows` rows of `in` (gemm_simt.cu / tcgen05 GEMM).
     void gemm_rows(const std::string& name, const ConvWeight& cw, int in_tid, int rows, const GemmOpts& o, int out_tid) {
         const int k = cw.cin * cw.kh * cw.kw;
-        if (tensor_core_f32() && k % 4 == 0) {
-            TcConvParams tp;
+        if (tensor_core_f32() && k % 4 == 0 && o.res_gate < 0) {
+            TcEngineParams tp;
             tp.mode = 0;
             tp.m = rows;
             tp.lda = k;
@@ -276,7 +278,7 @@ public:
             ConvWeight flat = cw;
             flat.cin = k; flat.kh = 1; flat.kw = 1;
             if (!o.has_bias) flat.b.assign(cw.cout, 0.f);
-            tc_f32_op(name, flat, tp, {}, in_tid, o.gate, o.res_gate, o.residual, out_tid, 2.0 * rows * cw.cout * k);
+            engine_op(name, flat, tp, {}, in_tid, o.gate, o.residual, out_tid, 2.0 * rows * cw.cout * k);
             return;
         }
         int n_pad = 0;
@@ -448,7 +450,8 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
                       r.conv_bn(prefix + ".channel_conv2", blk.cout, blk.cin * 2, 1, 1, false), y, gate, blk.residual());
     }
     if (gate >= 0) {
-        if (b.tensor_core_gemms()) {
+        // The tensor-core GEMMs take no residual gate: apply the SE gate once.
+        if (b.tensor_core_gemms() || b.tensor_core_f32()) {
             y = b.gate_apply(prefix + ".se.apply", y, gate, 0, nullptr, 1);
             gate = -1;
         }

@@ -212,6 +212,31 @@ std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad) {
     return out;
 }
 
+float bf16_round(float f) {
+    const uint16_t h = to_bf16(f);
+    const uint32_t u = (uint32_t)h << 16;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad) {
+    const int taps = cw.kh * cw.kw;
+    std::vector<float> out((size_t)planes * n_pad * k_pad, 0.f);
+    for (int o = 0; o < cw.cout; ++o)
+        for (int t = 0; t < taps; ++t)
+            for (int i = 0; i < cw.cin; ++i) {
+                float v = cw.w[((size_t)o * cw.cin + i) * taps + t];
+                const size_t col = (size_t)t * cw.cin + i;
+                for (int pl = 0; pl < planes; ++pl) {
+                    const float piece = bf16_round(v);   // x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1)
+                    out[((size_t)pl * n_pad + o) * k_pad + col] = piece;
+                    v = v - piece;
+                }
+            }
+    return out;
+}
+
 std::vector<float> pack_depthwise(const ConvWeight& cw) {
     const int taps = cw.kh * cw.kw;
     std::vector<float> out((size_t)taps * cw.cout);
@@ -229,28 +254,6 @@ std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad) {
     return out;
 }
 
-static inline float tf32_round(float f) {
-    uint32_t u;
-    std::memcpy(&u, &f, 4);
-    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
-    std::memcpy(&f, &u, 4);
-    return f;
-}
-
-std::vector<float> pack_tf32_split(const ConvWeight& cw, int cin4, int n_pad, int k_pad) {
-    const int taps = cw.kh * cw.kw;
-    std::vector<float> out((size_t)2 * n_pad * k_pad, 0.f);
-    for (int o = 0; o < cw.cout; ++o)
-        for (int t = 0; t < taps; ++t)
-            for (int i = 0; i < cw.cin; ++i) {
-                const float v = cw.w[((size_t)o * cw.cin + i) * taps + t];
-                const float hi = tf32_round(v);
-                const size_t at = (size_t)o * k_pad + (size_t)t * cin4 + i;
-                out[at] = hi;
-                out[(size_t)n_pad * k_pad + at] = tf32_round(v - hi);
-            }
-    return out;
-}
 
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad) {
     const int k = cw.cin * cw.kh * cw.kw;

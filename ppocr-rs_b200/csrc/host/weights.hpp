@@ -63,12 +63,12 @@ private:
 // Packers (all from OIHW / [out][in] sources)
 std::vector<float> pack_conv_tiles(const ConvWeight& cw, int tile);       // [ceil(O/tile)][kh][kw][I][tile]
 std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad);        // [kh][kw][I][O_pad4] (implicit GEMM)
+// Tensor-core engine weights: [planes][n_pad][k_pad] with k = (ky, kx, i); plane
+// p holds the p-th BF16 piece of each value (planes 1: bf16(w); planes 3: the
+// three-way split w = w0 + w1 + w2), every value exactly representable in BF16.
+std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad);
+float bf16_round(float f);                                                // round to nearest even
 std::vector<float> pack_depthwise(const ConvWeight& cw);                  // [kh*kw][C]
 std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad);        // [K][N_pad4]
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad);  // [N_pad][K_pad] (BF16 source)
-// 3xTF32 operand: [2][n_pad][k_pad], K index = tap * cin4 + channel (cin4 =
-// cin rounded up to 4); the first half TF32-rounded weights, the second the
-// TF32-rounded remainders.
-std::vector<float> pack_tf32_split(const ConvWeight& cw, int cin4, int n_pad, int k_pad);
-
 }  // namespace ppocr

@@ -154,40 +154,32 @@ bool gemm_tc_supported(const GemmParams& p);
 int gemm_tc_error_and_clear();
 
 // ---------------------------------------------------------------------------
-// FP32-accurate tensor-core GEMM / implicit-GEMM conv (3xTF32 on tcgen05),
-// the FP32 mode's kernel for pointwise and dense convs (tc_conv.cu).
-//   mode 0: A rows are dense FP32 [m][lda] (optional SE gate on A);
-//   mode 1: A is the conv window gathered from conv.src[] (conv.kh/kw/sh/sw/
-//           pt/pl/hi/wi, output grid out_h x out_w); K = taps * cin4 with each
-//           source's channels padded to a multiple of 4 (NCHW input: 3 -> 4).
-// W2 holds [2][n_pad][k_pad] FP32: TF32-rounded weights, then the TF32-rounded
-// remainders, K-major; n_pad = a multiple of tc_conv_tile_n(n).
-// ---------------------------------------------------------------------------
-struct TcConvParams {
-    int mode = 0;
+// tcgen05 GEMM / implicit-GEMM conv over BF16 operands (tc_engine.cu).
+// planes 1: BF16 A (activations), W and C; planes 3: FP32 A, W and C, each
+// operand split into three BF16 pieces and the six leading products
+// accumulated (FP32-class products).  K order of a conv: (ky, kx, channel).
+struct TcEngineParams {
+    int mode = 0;                     // 0: dense A rows; 1: conv window gather (conv)
+    int planes = 1;
     int m = 0, n = 0, k = 0;
-    int n_pad = 0, k_pad = 0;
-    const float* w2 = nullptr;
-    const float* a = nullptr;
+    int n_pad = 0, k_pad = 0;         // W is BF16 [planes][n_pad][k_pad], k_pad % 64 == 0
+    const void* w = nullptr;
+    const void* a = nullptr;          // mode 0: [m][lda]
     int lda = 0;
-    const float* gate = nullptr;
+    const float* gate = nullptr;      // mode 0: A *= gate[row / rows_per_image][k]
     int rows_per_image = 1;
-    ConvParams conv;
-    int cin4 = 0;
-    int src_start[5] = {0, 0, 0, 0, 0};
-    const float* bias = nullptr;
+    ConvGather conv;                  // mode 1: geometry, sources (channel counts per source)
+    const float* bias = nullptr;      // [n]
     int act = 0;
-    const float* residual = nullptr;
-    int ldr = 0;
-    const float* res_gate = nullptr;
-    int res_scale = 1;
-    int out_h = 1, out_w = 1;
-    float* c = nullptr;
+    const void* residual = nullptr;   // same dtype as C, [rows][ldr], nearest-upsampled by res_scale
+    int ldr = 0, res_scale = 1, out_h = 1, out_w = 1;
+    void* c = nullptr;                // BF16 (planes 1) or FP32 (planes 3) [m][ldc] at column coff
     int ldc = 0, coff = 0;
 };
-int tc_conv_tile_n(int n);
-cudaError_t launch_tc_conv(const TcConvParams& p, cudaStream_t stream);
-int tc_conv_error_and_clear();
+int tc_engine_tile_n(int n, int planes);
+bool tc_engine_supported(const TcEngineParams& p);
+cudaError_t launch_tc_engine(const TcEngineParams& p, cudaStream_t stream);
+int tc_engine_error_and_clear();
 
 // ---------------------------------------------------------------------------
 // Squeeze-excitation

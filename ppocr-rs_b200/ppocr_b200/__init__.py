@@ -104,16 +104,17 @@ class ModelSize:
 
 class Precision:
     """FP32: CUDA-core FP32 (parity mode); BF16: BF16 storage + tcgen05 BF16 GEMMs;
-    TF32X3: FP32 storage + 3xTF32 tcgen05 GEMMs / convs."""
+    FP32_TC: FP32 storage; tcgen05 GEMMs / convs on three-way BF16-split operands
+    (FP32-class products)."""
     FP32 = 0
     BF16 = 1
-    TF32X3 = 2
+    FP32_TC = 2
 
     @staticmethod
     def parse(value) -> int:
         if isinstance(value, int):
             return value
-        return {"fp32": 0, "bf16": 1, "tf32x3": 2}[str(value).lower()]
+        return {"fp32": 0, "bf16": 1, "fp32tc": 2}[str(value).lower()]
 
 
 class _PostOptions(C.Structure):
@@ -183,9 +184,9 @@ def library() -> C.CDLL:
         "ppocr_selftest_gemm_ex": (I, [P, I, I, I, FP, FP, FP, I, FP, I, I, I, FP, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
-        "ppocr_selftest_conv": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int),
-                                    C.POINTER(C.c_int)]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
+        "ppocr_selftest_engine": (I, [P, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, FP, I, FP, C.POINTER(C.c_int),
+                                      C.POINTER(C.c_int)]),
         "ppocr_recognizer_forward_crops": (I, [P, P, S, FP, C.POINTER(S), C.POINTER(C.c_int32), FP, FP]),
         "ppocr_postprocess_options_default": (None, [C.POINTER(_PostOptions)]),
         "ppocr_db_postprocess": (I, [FP, S, S, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
@@ -291,21 +292,6 @@ class Gpu:
                                                   int(out_w), 0 if kind == "det" else 1, _fptr(out)))
         return out
 
-    def selftest_conv(self, x_nhwc, w_oihw, bias=None, stride: int = 1, pad: int = 0, act: int = 0):
-        """FP32 3xTF32 tensor-core conv diagnostic: returns (out NHWC float32, wait_error)."""
-        x = np.ascontiguousarray(x_nhwc, dtype=np.float32)
-        w = np.ascontiguousarray(w_oihw, dtype=np.float32)
-        n, hi, wi, cin = x.shape
-        cout, _, kh, kw = w.shape
-        ho, wo = (hi + 2 * pad - kh) // stride + 1, (wi + 2 * pad - kw) // stride + 1
-        out = np.empty((n, ho, wo, cout), dtype=np.float32)
-        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-        used, err = C.c_int(), C.c_int()
-        _check(library().ppocr_selftest_conv(self._h, n, hi, wi, cin, cout, kh, kw, int(stride), int(pad), _fptr(x),
-                                             _fptr(w), None if b is None else _fptr(b), int(act), _fptr(out),
-                                             C.byref(used), C.byref(err)))
-        return out, err.value
-
     def selftest_gemm(self, a, w, bias=None, act: int = 0):
         """BF16 GEMM diagnostic: returns (C float32 [m, n], used_tensor_cores, wait_error)."""
         a = np.ascontiguousarray(a, dtype=np.float32)
@@ -318,6 +304,24 @@ class Gpu:
         _check(library().ppocr_selftest_gemm(self._h, m, n, k, _fptr(a), _fptr(w), None if b is None else _fptr(b),
                                              int(act), _fptr(c), C.byref(used), C.byref(err)))
         return c, bool(used.value), err.value
+
+    def selftest_engine(self, planes, x, w, bias=None, act=0, stride=1, pad=0, second=0, x2=None):
+        """Tensor-core engine conv diagnostic: x NHWC [n, h, w, cin], w OIHW; returns
+        (out NHWC float32, used_tensor_cores, wait_error)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        n, hi, wi, cin = x.shape
+        cout, _, kh, kw = w.shape
+        ho, wo = (hi + 2 * pad - kh) // stride + 1, (wi + 2 * pad - kw) // stride + 1
+        out = np.empty((n, ho, wo, cout), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        x2a = None if x2 is None else np.ascontiguousarray(x2, dtype=np.float32)
+        used, err = C.c_int(), C.c_int()
+        _check(library().ppocr_selftest_engine(self._h, int(planes), n, hi, wi, cin, cout, kh, kw, int(stride), int(pad),
+                                               int(second), _fptr(x), None if x2a is None else _fptr(x2a), _fptr(w),
+                                               None if b is None else _fptr(b), int(act), _fptr(out), C.byref(used),
+                                               C.byref(err)))
+        return out, bool(used.value), err.value
 
     def selftest_gemm_ex(self, a, w, c_init, coff: int, bias=None, act: int = 0, residual=None, out_bf16: bool = True):
         """GEMM diagnostic into columns [coff, coff + n) of c_init [m, ldc] (other columns must survive);

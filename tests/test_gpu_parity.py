@@ -62,17 +62,20 @@ def test_detector_conditioned(gpu, weights_file, size, profile, precision, shape
     assert d.mean() <= DET_MEAN_ABS, f"mean-abs {d.mean()}"
 
 
+@pytest.mark.parametrize("precision", ["fp32"])
 @pytest.mark.parametrize("size,shape", [
     ("tiny", (1, 3, 416, 736)),      # benchmark config 1
     ("small", (1, 3, 416, 736)),
     ("medium", (1, 3, 416, 736)),
 ])
-def test_detector_spec_weights(gpu, weights_file, size, shape):
+def test_detector_spec_weights(gpu, weights_file, size, shape, precision):
+    """Spec weights make the detector chaotic: any FP32 arithmetic is held to the
+    float64 answer within a few times the reference arithmetic's own FP32 error."""
     import torch
 
     path = weights_file("det", size, "spec")
     x = seeded.det_batch(shape[0], shape[2], shape[3], seed=1)
-    det = P.Detector.load(gpu, path, size, shape, precision="fp32")
+    det = P.Detector.load(gpu, path, size, shape, precision=precision)
     got = det.forward(x).values.reshape(shape[0], 1, shape[2], shape[3])
     orc = oracle("det", size, path)
     want = orc.forward(x)
@@ -83,7 +86,7 @@ def test_detector_spec_weights(gpu, weights_file, size, shape):
     d_exact = np.abs(got - exact)           # this build's FP32 error
     flips = int(((got >= 0.5) != (exact >= 0.5)).sum())
     ref_flips = int(((want >= 0.5) != (exact >= 0.5)).sum())
-    print(f"{size}: vs oracle max {d.max():.3g} mean {d.mean():.3g}; vs float64 max {d_exact.max():.3g} "
+    print(f"{size} {precision}: vs oracle max {d.max():.3g} mean {d.mean():.3g}; vs float64 max {d_exact.max():.3g} "
           f"mean {d_exact.mean():.3g}; oracle vs float64 max {noise.max():.3g}; flips {flips} (oracle {ref_flips})")
     assert d.mean() <= DET_MEAN_ABS, f"mean-abs {d.mean()}"
     assert d_exact.max() <= max(DET_MAX_ABS, 4 * float(noise.max())), \
@@ -134,19 +137,19 @@ def test_recognizer(gpu, weights_file, size, profile, precision, shape):
     ("det", "medium", (1, 3, 128, 160)),
     ("rec", "medium", (2, 3, 48, 160)),
 ])
-def test_tf32x3_tensor_core_path_matches_fp32(gpu, weights_file, kind, size, shape):
-    """TF32X3 mode (3xTF32 tcgen05 GEMMs / convs) agrees with the FP32 CUDA-core mode."""
+def test_fp32_tensor_core_path_matches_fp32(gpu, weights_file, kind, size, shape):
+    """FP32_TC mode (tcgen05 on three-way BF16-split operands) agrees with the FP32 CUDA-core mode."""
     path = weights_file(kind, size, "conditioned")
     if kind == "det":
         x = seeded.det_batch(shape[0], shape[2], shape[3], seed=6, text=True)
-        a = P.Detector.load(gpu, path, size, shape, precision="tf32x3").forward(x).values
+        a = P.Detector.load(gpu, path, size, shape, precision="fp32tc").forward(x).values
         b = P.Detector.load(gpu, path, size, shape, precision="fp32").forward(x).values
         want = oracle(kind, size, path).forward(x).reshape(-1)
         assert np.abs(a - want).max() <= DET_MAX_ABS
         assert np.abs(a - b).max() <= 1e-3
     else:
         x = seeded.rec_batch(shape[0], shape[3], seed=6)
-        a = P.Recognizer.load(gpu, path, size, shape, precision="tf32x3").forward_logits(x)
+        a = P.Recognizer.load(gpu, path, size, shape, precision="fp32tc").forward_logits(x)
         b = P.Recognizer.load(gpu, path, size, shape, precision="fp32").forward_logits(x)
         want = oracle(kind, size, path).logits(x)
         assert np.abs(a - want).max() <= REC_LOGIT_MAX_ABS
