@@ -4,22 +4,26 @@
 //   nearest upsampling of the pixel grid), FP32 accumulation in TMEM.
 //
 // Persistent CTAs walk 128 x BN output tiles (BN a multiple of 64, <= 256).
-// Roles (320 threads):
+// Roles (576 threads):
 //   warp 0 / lane 0   TMA producer: A and W tiles (128 x 64 and BN x 64 BF16,
 //                     128-byte swizzled, K-major) into a SMEM ring;
 //   warp 1 / lane 0   MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per
 //                     stage into one of two TMEM accumulators (2 x BN columns),
 //                     so the next tile's MMAs run while the previous tile's
 //                     epilogue drains the other accumulator;
-//   warps 2-9         epilogue: tcgen05.ld of their TMEM lane quarter (warp % 4),
+//   warps 2-17        epilogue: tcgen05.ld of their TMEM lane quarter (warp % 4),
 //                     bias, activation, residual, then release the accumulator.
-//                     Each warp owns every other 128-byte column group of the
-//                     tile (64 BF16 / 32 FP32 columns): it packs 32 rows of a
-//                     group into its own 4 KB 128-byte-swizzled staging tile and
-//                     one lane issues a TMA store of it, so the output leaves as
-//                     whole lines instead of 32 scattered row fragments per
-//                     store instruction.  Outputs whose row pitch or base is not
-//                     16-byte aligned take a direct-store epilogue instead.
+//                     Four warps share a lane quarter, each owning every fourth
+//                     128-byte column group of the tile (64 BF16 / 32 FP32
+//                     columns), processed 32 columns at a time to stay within
+//                     the register budget of 576 threads; sixteen warps give
+//                     the activation math (GELU: two MUFU ops per element)
+//                     enough issue slots and latency hiding to keep up with
+//                     the MMAs.  A warp packs 32 rows of a group into its own
+//                     4 KB 128-byte-swizzled staging tile and one lane issues
+//                     a TMA store of it, so the output leaves as whole lines.
+//                     Outputs whose row pitch or base is not 16-byte aligned
+//                     take a direct-store epilogue instead.
 // Every mbarrier wait is bounded: on expiry the kernel records an error code
 // in g_tc_error, stops, frees its TMEM and returns.  No cluster launch and no
 // multicast: each CTA loads its own tiles from this GPU's memory.
@@ -38,7 +42,7 @@ __device__ int g_tc_error = 0;
 
 namespace {
 
-constexpr int BM = 128, BK = 64, MAX_STAGES = 4, THREADS = 320, EPI_WARPS = 8;
+constexpr int BM = 128, BK = 64, MAX_STAGES = 4, THREADS = 576, EPI_WARPS = 16;
 constexpr int STAGE_OUT_BYTES = 32 * 128;                 // one epilogue warp's staging tile
 constexpr int SMEM_LIMIT = 227 * 1024;                    // opt-in shared memory per block
 
@@ -123,13 +127,13 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
 // conflicts).  Lane 0 waits for the previous TMA store to have read the tile
 // only after the math, so that wait overlaps it.
 template <int ACT, bool F32>
-__device__ __forceinline__ void epilogue_group(const TcArgs& p, uint32_t taddr, int row, int col0, uint8_t* stage,
-                                               int lane) {
-    constexpr int GW = F32 ? 32 : 64;
-    uint32_t r[GW];
+__device__ __forceinline__ void epilogue_half(const TcArgs& p, uint32_t taddr, int row, int col0, uint8_t* line, int chunk0,
+                                              int swz) {
+    constexpr int HW = 32;   // columns per half
+    uint32_t r[HW];
 #pragma unroll
-    for (int j = 0; j < GW; j += 16) tc::tmem_ld16_async(taddr + (uint32_t)j, r + j);
-    const bool full = col0 + GW <= p.n;
+    for (int j = 0; j < HW; j += 16) tc::tmem_ld16_async(taddr + (uint32_t)j, r + j);
+    const bool full = col0 + HW <= p.n;
     const bool res = p.residual != nullptr && row < p.m;
     const __nv_bfloat16* rp = nullptr;
     if (res) {
@@ -144,30 +148,30 @@ __device__ __forceinline__ void epilogue_group(const TcArgs& p, uint32_t taddr, 
         rp = static_cast<const __nv_bfloat16*>(p.residual) + rrow * p.ldr + col0;
     }
     const bool res_vec = res && full && (p.ldr % 8) == 0;
-    uint4 rv[GW / 8];
+    uint4 rv[HW / 8];
     if (res_vec) {
 #pragma unroll
-        for (int j = 0; j < GW / 8; ++j) rv[j] = __ldg(reinterpret_cast<const uint4*>(rp) + j);
+        for (int j = 0; j < HW / 8; ++j) rv[j] = __ldg(reinterpret_cast<const uint4*>(rp) + j);
     }
     tc::tmem_wait_ld_regs(r);
-    float o[GW];
+    float o[HW];
     if (p.bias && full) {
 #pragma unroll
-        for (int j = 0; j < GW; j += 4) {   // 16-byte bias loads (L1-resident)
+        for (int j = 0; j < HW; j += 4) {
             const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
             o[j] = __uint_as_float(r[j]) + b.x; o[j + 1] = __uint_as_float(r[j + 1]) + b.y;
             o[j + 2] = __uint_as_float(r[j + 2]) + b.z; o[j + 3] = __uint_as_float(r[j + 3]) + b.w;
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < GW; ++j)
+        for (int j = 0; j < HW; ++j)
             o[j] = __uint_as_float(r[j]) + ((p.bias && col0 + j < p.n) ? __ldg(p.bias + col0 + j) : 0.f);
     }
 #pragma unroll
-    for (int j = 0; j < GW; ++j) o[j] = apply_act_fast<ACT>(o[j]);
+    for (int j = 0; j < HW; ++j) o[j] = apply_act_fast<ACT>(o[j]);
     if (res_vec) {
 #pragma unroll
-        for (int j = 0; j < GW / 8; ++j) {
+        for (int j = 0; j < HW / 8; ++j) {
             const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&rv[j]);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -178,27 +182,24 @@ __device__ __forceinline__ void epilogue_group(const TcArgs& p, uint32_t taddr, 
         }
     } else if (res) {
 #pragma unroll
-        for (int j = 0; j < GW; ++j)
+        for (int j = 0; j < HW; ++j)
             if (col0 + j < p.n) o[j] += __bfloat162float(rp[j]);
     }
-    uint32_t w[GW / 2 * (F32 ? 2 : 1)];
-    if (F32) {
+    if constexpr (F32) {
 #pragma unroll
-        for (int j = 0; j < GW; ++j) w[j] = __float_as_uint(o[j]);
+        for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4*>(line + (((chunk0 + c) ^ swz) << 4)) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
     } else {
+        uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < GW / 2; ++j) {
+        for (int j = 0; j < 16; ++j) {
             const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
             w[j] = *reinterpret_cast<const uint32_t*>(&h);
         }
-    }
-    if (lane == 0) tc::bulk_wait_read();   // the previous store has left the staging tile
-    __syncwarp();
-    uint8_t* line = stage + lane * 128;
-    const int swz = lane & 7;
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(line + ((c ^ swz) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(line + (((chunk0 + c) ^ swz) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    }
 }
 
 template <int ACT, bool F32>
@@ -290,11 +291,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             }
         }
     } else {
-        // Epilogue warps 2..9: TMEM lane quarter q = warp % 4 (rows q*32 .. q*32+31);
-        // `half` picks every other column group of the tile.
-        const int q = warp & 3, half = (warp - 2) >> 2;
+        // Epilogue warps 2..17: TMEM lane quarter q = warp % 4, column slot (warp - 2) / 4.
+        const int q = warp & 3, slot = (warp - 2) >> 2;
         uint8_t* stage = sout + (warp - 2) * STAGE_OUT_BYTES;
-        constexpr int GW = F32 ? 32 : 64;                 // columns per 128-byte group
+        uint8_t* line = stage + lane * 128;
+        const int swz = lane & 7;
+        constexpr int GW = F32 ? 32 : 64;
         int ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
             if (abort_flag) break;
@@ -311,8 +313,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             const int row = m0 + q * 32 + lane;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * p.bn);
             if (p.tma_store) {
-                for (int cb = half * GW; cb < p.bn && n0 + cb < p.n; cb += 2 * GW) {
-                    epilogue_group<ACT, F32>(p, tbase + (uint32_t)cb, row, n0 + cb, stage, lane);
+                for (int cb = slot * GW; cb < p.bn && n0 + cb < p.n; cb += 4 * GW) {
+                    if (lane == 0) tc::bulk_wait_read();
+                    __syncwarp();
+                    for (int hf = 0; hf < GW; hf += 32)
+                        epilogue_half<ACT, F32>(p, tbase + (uint32_t)(cb + hf), row, n0 + cb + hf, line, hf / (F32 ? 4 : 8), swz);
                     tc::fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) {
@@ -321,7 +326,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                     }
                 }
             } else {
-                const int cols = p.bn / 2;   // multiple of 32, processed 16 at a time
+                const int cols = p.bn / 4;   // multiple of 16, processed 16 at a time
+                const int half = slot;
                 const uint32_t base = tbase + (uint32_t)(half * cols);
                 for (int c0 = 0; c0 < cols; c0 += 16) {
                     uint32_t r[16];
