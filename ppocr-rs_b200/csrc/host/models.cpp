@@ -196,10 +196,20 @@ public:
         // kernel (measured faster for the detector's 16-channel FP32 convs), 16
         // output channels per thread when cout >= 16 (8 otherwise).  Both
         // accumulate each output in (ky, kx, channel) order.
-        const bool gemm = m_.dtype == DT_BF16 && conv_gemm_supported(p);
+        // BF16 with tensor cores: one plain NHWC source -> tcgen05 implicit GEMM
+        // (TMA boxes per tap); otherwise the SIMT implicit GEMM.
+        const bool tcconv = tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
+        const bool gemm = !tcconv && m_.dtype == DT_BF16 && conv_gemm_supported(p);
         const int co_tile = cw.cout >= 16 ? 16 : 8;
         int n_pad = 0;
-        const size_t woff = gemm ? m_.blob.add_f32(pack_conv_kn(cw, n_pad)) : m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
+        size_t woff;
+        if (tcconv) {
+            p.tc_n_pad = (cw.cout + 15) / 16 * 16;
+            p.tc_cin_pad = (cin + 63) / 64 * 64;
+            woff = m_.blob.add_bf16(pack_conv_tc(cw, p.tc_n_pad, p.tc_cin_pad));
+        } else {
+            woff = gemm ? m_.blob.add_f32(pack_conv_kn(cw, n_pad)) : m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
+        }
         std::vector<float> bias = cw.b;
         bias.resize((cw.cout + co_tile - 1) / co_tile * co_tile, 0.f);
         const size_t boff = m_.blob.add_f32(bias);
@@ -207,10 +217,11 @@ public:
         p.n_pad = n_pad;
         const int otid = out.tid;
         std::vector<Src> s2 = srcs;
-        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid, gemm](const Ctx& c, cudaStream_t st) mutable {
+        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid, gemm, tcconv](const Ctx& c, cudaStream_t st) mutable {
             for (size_t i = 0; i < s2.size(); ++i) p.src[i].ptr = c.act(s2[i].tid);
-            p.weight = gemm ? nullptr : c.wf(woff);
+            p.weight = (gemm || tcconv) ? nullptr : c.wf(woff);
             p.weight_kn = gemm ? c.wf(woff) : nullptr;
+            p.w_tc = tcconv ? c.wb(woff) : nullptr;
             p.bias = c.wf(boff);
             p.residual = c.act(residual);
             p.out = c.act(otid);

@@ -237,6 +237,16 @@ std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, i
     return out;
 }
 
+std::vector<float> pack_conv_tc(const ConvWeight& cw, int n_pad, int cin_pad) {
+    const int taps = cw.kh * cw.kw;
+    const size_t k = (size_t)taps * cin_pad;
+    std::vector<float> out((size_t)n_pad * k, 0.f);
+    for (int o = 0; o < cw.cout; ++o)
+        for (int t = 0; t < taps; ++t)
+            for (int i = 0; i < cw.cin; ++i) out[(size_t)o * k + (size_t)t * cin_pad + i] = cw.w[((size_t)o * cw.cin + i) * taps + t];
+    return out;
+}
+
 std::vector<float> pack_depthwise(const ConvWeight& cw) {
     const int taps = cw.kh * cw.kw;
     std::vector<float> out((size_t)taps * cw.cout);

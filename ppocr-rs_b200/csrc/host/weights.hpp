@@ -68,6 +68,8 @@ std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad);        // [kh
 // three-way split w = w0 + w1 + w2), every value exactly representable in BF16.
 std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad);
 float bf16_round(float f);                                                // round to nearest even
+// tcgen05 conv weights: [n_pad][kh][kw][cin_pad], channels past cin zero.
+std::vector<float> pack_conv_tc(const ConvWeight& cw, int n_pad, int cin_pad);
 std::vector<float> pack_depthwise(const ConvWeight& cw);                  // [kh*kw][C]
 std::vector<float> pack_gemm_kn(const ConvWeight& cw, int& n_pad);        // [K][N_pad4]
 std::vector<float> pack_gemm_nk(const ConvWeight& cw, int n_pad, int k_pad);  // [N_pad][K_pad] (BF16 source)

@@ -229,6 +229,7 @@ cudaError_t launch_conv_t(const ConvParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream) {
+    if (p.w_tc) return launch_conv_tc(p, stream);
     if (p.weight_kn) return launch_conv_gemm(p, stream);
     if (p.co_tile == 16)
         return p.dtype == DT_F32 ? launch_conv_t<float, 16>(p, stream) : launch_conv_t<__nv_bfloat16, 16>(p, stream);

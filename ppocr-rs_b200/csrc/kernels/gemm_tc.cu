@@ -55,6 +55,9 @@ struct TcArgs {
     void* c;
     int ldc, coff, c_f32;
     int tma_store;
+    // Implicit-GEMM conv (conv = 1): a tile is 8 x 16 output pixels of one image,
+    // a K step one (tap, 64-channel block) loaded as a strided 4D TMA box.
+    int conv, tiles_y, tiles_x, cblocks, kw, stride, pt, pl;
 };
 
 template <typename T, int ACT>
@@ -242,7 +245,16 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         if (lane == 0) {
             int it = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
-                const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * p.bn;
+                const int mt = tile / p.n_tiles;
+                const int m0 = mt * BM, n0 = (tile % p.n_tiles) * p.bn;
+                int img = 0, x0 = 0, y0 = 0;
+                if (p.conv) {
+                    const int per = p.tiles_y * p.tiles_x;
+                    img = mt / per;
+                    const int r = mt - img * per;
+                    y0 = (r / p.tiles_x) * 8 * p.stride - p.pt;
+                    x0 = (r % p.tiles_x) * 16 * p.stride - p.pl;
+                }
                 for (int kt = 0; kt < p.kt; ++kt, ++it) {
                     const int s = it % S;
                     if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false)) {
@@ -251,7 +263,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                         break;
                     }
                     tc::mbar_expect_tx(&full_bar[s], (uint32_t)(a_bytes + b_bytes));
-                    tc::tma_load_2d(sa + s * a_bytes, &tma_a, &full_bar[s], kt * BK, m0);
+                    if (p.conv) {
+                        const int tap = kt / p.cblocks, cb = kt - tap * p.cblocks;
+                        const int ky = tap / p.kw, kx = tap - ky * p.kw;
+                        tc::tma_load_4d(sa + s * a_bytes, &tma_a, &full_bar[s], cb * BK, x0 + kx, y0 + ky, img);
+                    } else {
+                        tc::tma_load_2d(sa + s * a_bytes, &tma_a, &full_bar[s], kt * BK, m0);
+                    }
                     tc::tma_load_2d(sb + s * b_bytes, &tma_b, &full_bar[s], kt * BK, n0);
                 }
             }
@@ -321,7 +339,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                     tc::fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) {
-                        tc::tma_store_2d(&tma_c, stage, n0 + cb, m0 + q * 32);
+                        if (p.conv) {
+                            // The warp's 32 rows are two 16-pixel output rows of the tile.
+                            const int mt = tile / p.n_tiles, per = p.tiles_y * p.tiles_x;
+                            const int img = mt / per, r = mt - img * per;
+                            tc::tma_store_4d(&tma_c, stage, n0 + cb, (r % p.tiles_x) * 16, (r / p.tiles_x) * 8 + q * 2, img);
+                        } else {
+                            tc::tma_store_2d(&tma_c, stage, n0 + cb, m0 + q * 32);
+                        }
                         tc::bulk_commit();
                     }
                 }
@@ -374,6 +399,22 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 4D NHWC map: dims (channels, width, height, images) of a view with pixel
+// pitch `cstride` elements, box (box_c, box_x, box_y, 1) traversed with
+// element strides (1, stride, stride, 1).
+bool make_map4(CUtensorMap* map, const void* base, uint64_t channels, uint64_t w, uint64_t h, uint64_t n, uint64_t cstride,
+               uint32_t box_c, uint32_t box_x, uint32_t box_y, uint32_t stride) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {channels, w, h, n};
+    cuuint64_t strides[3] = {cstride * 2, w * cstride * 2, h * w * cstride * 2};
+    cuuint32_t box[4] = {box_c, box_x, box_y, 1};
+    cuuint32_t estr[4] = {1, stride, stride, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -434,7 +475,7 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
     if (!make_map(&ma, p.a, (uint64_t)p.k, (uint64_t)p.m, (uint64_t)p.lda * 2, BK, BM)) return cudaErrorInvalidValue;
     if (!make_map(&mb, p.w_tc, (uint64_t)p.k_pad, (uint64_t)n_rows, (uint64_t)p.k_pad * 2, BK, (uint32_t)bn))
         return cudaErrorInvalidValue;
-    TcArgs a;
+    TcArgs a{};
     a.m = p.m; a.n = p.n; a.k = p.k; a.kt = (p.k + BK - 1) / BK; a.bn = bn;
     int cols = 32;
     while (cols < 2 * bn) cols <<= 1;
@@ -457,6 +498,82 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
                    make_map(&mc, cbase, (uint64_t)p.n, (uint64_t)p.m, (uint64_t)p.ldc * esize, p.c_f32 ? 32 : 64, 32,
                             p.c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
                       ? 1 : 0;
+    const size_t smem = (size_t)a.stages * stage_bytes + out_bytes + 1024;
+    const int tiles = a.m_tiles * a.n_tiles;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    switch (p.act) {
+        case ACT_NONE: return launch_act<ACT_NONE>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_RELU: return launch_act<ACT_RELU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_SILU: return launch_act<ACT_SILU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_GELU: return launch_act<ACT_GELU>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mb, mc, a, grid, smem, stream);
+        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mb, mc, a, grid, smem, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+bool conv_tc_supported(const ConvParams& p) {
+    if (p.dtype != DT_BF16 || p.nsrc != 1 || p.residual) return false;
+    const ConvSource& s = p.src[0];
+    if (s.mode != SRC_NHWC || s.scale != 1 || s.cstride % 8 || s.coff % 8) return false;
+    if (p.sh != p.sw || (p.sh != 1 && p.sh != 2)) return false;
+    if (p.out_cstride % 8 || p.out_coff % 8 || p.cout < 1) return false;
+    return p.n > 0 && p.ho > 0 && p.wo > 0;
+}
+
+cudaError_t launch_conv_tc(const ConvParams& p, cudaStream_t stream) {
+    if (!conv_tc_supported(p) || !p.w_tc) return cudaErrorInvalidValue;
+    const ConvSource& src = p.src[0];
+    const int cblocks = (src.channels + BK - 1) / BK;
+    if (p.tc_cin_pad != cblocks * BK) return cudaErrorInvalidValue;
+    const int bn = pick_bn(p.cout);
+    const int taps = p.kh * p.kw;
+    const int n_rows = (p.cout + 15) / 16 * 16;
+    if (p.tc_n_pad != n_rows) return cudaErrorInvalidValue;
+    const int s = p.sh;
+    CUtensorMap ma, mb, mc;
+    memset(&mc, 0, sizeof(mc));
+    const char* abase = static_cast<const char*>(src.ptr) + (size_t)src.coff * 2;
+    char* cbase = static_cast<char*>(p.out) + (size_t)p.out_coff * 2;
+    if ((reinterpret_cast<uintptr_t>(abase) % 16) || (reinterpret_cast<uintptr_t>(cbase) % 16)) return cudaErrorInvalidValue;
+    if (!make_map4(&ma, abase, (uint64_t)src.channels, (uint64_t)p.wi, (uint64_t)p.hi, (uint64_t)p.n, (uint64_t)src.cstride, BK,
+                   16 * s, 8 * s, s))
+        return cudaErrorInvalidValue;
+    if (!make_map(&mb, p.w_tc, (uint64_t)taps * cblocks * BK, (uint64_t)n_rows, (uint64_t)taps * cblocks * BK * 2, BK,
+                  (uint32_t)bn))
+        return cudaErrorInvalidValue;
+    if (!make_map4(&mc, cbase, (uint64_t)p.cout, (uint64_t)p.wo, (uint64_t)p.ho, (uint64_t)p.n, (uint64_t)p.out_cstride, 64,
+                   16, 2, 1))
+        return cudaErrorInvalidValue;
+    TcArgs a{};
+    a.conv = 1;
+    a.tiles_y = (p.ho + 7) / 8;
+    a.tiles_x = (p.wo + 15) / 16;
+    a.cblocks = cblocks;
+    a.kw = p.kw;
+    a.stride = s;
+    a.pt = p.pt;
+    a.pl = p.pl;
+    a.m_tiles = p.n * a.tiles_y * a.tiles_x;
+    a.m = a.m_tiles * BM;
+    a.n = p.cout;
+    a.k = taps * cblocks * BK;
+    a.kt = taps * cblocks;
+    a.bn = bn;
+    int cols = 32;
+    while (cols < 2 * bn) cols <<= 1;
+    a.tmem_cols = cols;
+    const int stage_bytes = BM * BK * 2 + bn * BK * 2;
+    const int out_bytes = EPI_WARPS * STAGE_OUT_BYTES;
+    a.stages = (SMEM_LIMIT - 2048 - out_bytes) / stage_bytes;
+    if (a.stages > MAX_STAGES) a.stages = MAX_STAGES;
+    a.n_tiles = (p.cout + bn - 1) / bn;
+    a.bias = p.bias;
+    a.act = p.act;
+    a.c = p.out;
+    a.ldc = p.out_cstride;
+    a.coff = p.out_coff;
+    a.tma_store = 1;
     const size_t smem = (size_t)a.stages * stage_bytes + out_bytes + 1024;
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();

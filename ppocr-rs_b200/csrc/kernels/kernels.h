@@ -54,6 +54,8 @@ struct ConvParams {
     const float* weight = nullptr;        // [ceil(cout/co_tile)][kh][kw][cin][co_tile]
     const float* weight_kn = nullptr;     // implicit-GEMM layout [kh][kw][cin][n_pad] (or null)
     int n_pad = 0;
+    const void* w_tc = nullptr;           // tcgen05 conv: BF16 [tc_n_pad][kh*kw*tc_cin_pad] (or null)
+    int tc_n_pad = 0, tc_cin_pad = 0;
     const float* bias = nullptr;          // [cout]
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
@@ -63,6 +65,12 @@ struct ConvParams {
     DType dtype = DT_F32;
 };
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
+
+// tcgen05 implicit-GEMM conv of one NHWC BF16 source (gemm_tc.cu): 8 x 16
+// output-pixel tiles, each K step a strided 4D TMA box of 64 channels at one
+// tap, TMA stores of the output tile.  Needs w_tc.
+bool conv_tc_supported(const ConvParams& p);
+cudaError_t launch_conv_tc(const ConvParams& p, cudaStream_t stream);
 
 // Implicit-GEMM view of a dense conv for the SIMT GEMM kernel (gemm_simt.cu).
 struct ConvGather {
