@@ -214,6 +214,18 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
                            int act, const float* residual, int out_bf16, int ldc, int coff, float* c,
                            int* used_tensor_cores, int* wait_error);
 
+/* Diagnostic (new): the FP32 pointwise GEMM of the FP32 mode,
+ * C[m, n] = act((A * gate) W[n, k]^T + bias) + residual, all in F32, through
+ * one chosen kernel: kernel 0 = the model's dispatch, 1 = the register-tiled
+ * SIMT kernel, 2 = the row kernel (n <= 128), 3 = the streaming kernel
+ * (k <= 128, n <= 128).  gate (may be NULL) is [m / rows_per_image][k] and
+ * scales A; residual (may be NULL) is [m][n].  kernel_used returns the kernel
+ * that ran (1..3).  k must be a multiple of 4; a kernel that does not
+ * support the shape fails with PPOCR_ERR_INVALID_INPUT. */
+int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
+                            int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
+                            int* kernel_used);
+
 /* Diagnostic (new): one convolution through the tcgen05 engine of the BF16
  * and FP32-class modes.  planes 1: input rounded to BF16, BF16 weights and
  * output; planes 3: FP32 input / weights split into three BF16 pieces each,

@@ -842,6 +842,67 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
     });
 }
 
+int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
+                            int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
+                            int* kernel_used) {
+    return guard([&] {
+        if (!gpu || !a || !w || !c) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (m <= 0 || n <= 0 || k <= 0 || k % 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: GEMM shape (k must be a multiple of 4)");
+        if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
+        if (kernel < 0 || kernel > 3) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..3");
+        if (gate && (rows_per_image <= 0 || m % rows_per_image)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: rows_per_image must divide m");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        ConvWeight cw;
+        cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
+        cw.w.assign(w, w + (size_t)n * k);
+        cw.b = bias ? std::vector<float>(bias, bias + n) : std::vector<float>(n, 0.f);
+        int n_pad4 = 0;
+        WeightBlob blob;
+        const size_t wf = blob.add_f32(pack_gemm_kn(cw, n_pad4));
+        const size_t bo = blob.add_f32(cw.b);
+        const size_t ao = blob.add_f32(std::vector<float>(a, a + (size_t)m * k));
+        const size_t go = gate ? blob.add_f32(std::vector<float>(gate, gate + (size_t)(m / rows_per_image) * k)) : 0;
+        const size_t ro = residual ? blob.add_f32(std::vector<float>(residual, residual + (size_t)m * n)) : 0;
+        const size_t co = blob.add_f32(std::vector<float>((size_t)m * n, 0.f));
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        GemmParams p;
+        p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad4;
+        p.act = act; p.ldr = n; p.ldc = n; p.coff = 0; p.c_f32 = 0; p.dtype = DT_F32;
+        p.rows_per_image = gate ? rows_per_image : 1;
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate GEMM test buffers");
+        p.a = d + ao; p.w = reinterpret_cast<const float*>(d + wf);
+        p.bias = reinterpret_cast<const float*>(d + bo);
+        p.gate = gate ? reinterpret_cast<const float*>(d + go) : nullptr;
+        p.residual = residual ? d + ro : nullptr;
+        p.c = d + co;
+        int used = kernel;
+        if (kernel == 0) used = p.n <= 32 && gemm_stream_supported(p) ? 3 : 1;   // launch_gemm's FP32 choice
+        const bool ok = used == 1 || (used == 2 && rows_gemm_supported(p)) || (used == 3 && gemm_stream_supported(p));
+        if (!ok) {
+            cudaFree(d);
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the chosen GEMM kernel does not support this shape");
+        }
+        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = used == 3 ? launch_gemm_stream(p, gpu->stream) : used == 2 ? launch_rows_gemm(p, gpu->stream)
+                                                                 : launch_gemm_simt(p, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, (size_t)m * n * 4, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "FP32 GEMM self-test");
+        if (kernel_used) *kernel_used = used;
+    });
+}
+
 int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride,
                           int pad, int second, const float* x, const float* x2, const float* w, const float* bias, int act,
                           float* out, int* used_tensor_cores, int* wait_error) {

@@ -5,6 +5,7 @@
 // neck concatenations read in place by the head conv.
 #include "models.hpp"
 
+#include <algorithm>
 #include <sstream>
 
 #include "common.hpp"
@@ -138,9 +139,12 @@ public:
     // Dense conv over up to four concatenated sources (conv.cu).
     // `into` (optional): write into channels [into_coff, into_coff + cout) of an
     // existing wider tensor instead of a new one (a concatenation slice).
+    // `any_order`: the conv may sum its products input quad by quad (the
+    // halo-tiled kernel) rather than tap by tap.  Kept to convs whose rounding
+    // differences reach the output unamplified (the detector head).
     Act4 conv(const std::string& name, const ConvWeight& cw, const std::vector<Src>& srcs, int n, int hi, int wi, int sh,
               int sw, int pt, int pl, int pb, int pr, int act, int residual = -1, int res_scale = 1,
-              const Act4* into = nullptr, int into_coff = 0) {
+              const Act4* into = nullptr, int into_coff = 0, bool any_order = false) {
         int cin = 0;
         for (auto& s : srcs) cin += s.channels;
         if (cin != cw.cin) fail(PPOCR_ERR_INVALID_MODEL, name + ": conv input channels do not match the weight");
@@ -191,27 +195,39 @@ public:
             reads.push_back(srcs[i].tid);
         }
         reads.push_back(residual);
-        // BF16 storage: NHWC sources run as a register-tiled implicit GEMM
-        // (gemm_simt.cu).  FP32 storage and the NCHW image input take the direct
-        // kernel (measured faster for the detector's 16-channel FP32 convs), 16
-        // output channels per thread when cout >= 16 (8 otherwise).  Both
-        // accumulate each output in (ky, kx, channel) order.
         // BF16 with tensor cores: one plain NHWC source -> tcgen05 implicit GEMM
-        // (TMA boxes per tap); otherwise the SIMT implicit GEMM.
+        // (TMA boxes per tap); other BF16 convs with NHWC sources -> the
+        // register-tiled SIMT implicit GEMM (gemm_simt.cu).
+        // FP32: the halo-tiled kernel (conv_halo.cu) where its geometries apply
+        // and its blocked (quad, tap, channel) sum is the plain (tap, channel)
+        // sum (one input quad: the image stem) or any order is allowed (the
+        // detector head); elsewhere the direct kernel (conv.cu), 16 output
+        // channels per thread when cout >= 16 (8 otherwise).  The direct and
+        // implicit-GEMM kernels accumulate each output in (ky, kx, channel)
+        // order.  The detector's chaotic spec-weight parity check flipped a
+        // pixel when the stem and neck convs were re-associated, so those keep
+        // the tap-major order.
         const bool tcconv = tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
-        const bool gemm = !tcconv && m_.dtype == DT_BF16 && conv_gemm_supported(p);
-        const int co_tile = cw.cout >= 16 ? 16 : 8;
+        const bool halo = !tcconv && m_.dtype == DT_F32 && (any_order || cin <= 4) && conv_halo_supported(p);
+        const bool gemm = !tcconv && !halo && m_.dtype == DT_BF16 && conv_gemm_supported(p);
+        // The NCHW image input has 3 channels: one thread covers up to 64 output
+        // channels so each loaded input feeds 64 FMAs.
+        const bool image_src = srcs.size() == 1 && srcs[0].mode == SRC_NCHW_F32;
+        const int co_tile = image_src && cw.cout % 64 == 0 ? 64 : image_src && cw.cout % 32 == 0 ? 32 : cw.cout >= 16 ? 16 : 8;
         int n_pad = 0;
         size_t woff;
         if (tcconv) {
             p.tc_n_pad = (cw.cout + 15) / 16 * 16;
             p.tc_cin_pad = (cin + 63) / 64 * 64;
             woff = m_.blob.add_bf16(pack_conv_tc(cw, p.tc_n_pad, p.tc_cin_pad));
+        } else if (halo) {
+            woff = m_.blob.add_f32(pack_conv_halo(cw, conv_halo_bn(cw.cout)));
+            p.halo = 1;
         } else {
             woff = gemm ? m_.blob.add_f32(pack_conv_kn(cw, n_pad)) : m_.blob.add_f32(pack_conv_tiles(cw, co_tile));
         }
         std::vector<float> bias = cw.b;
-        bias.resize((cw.cout + co_tile - 1) / co_tile * co_tile, 0.f);
+        bias.resize(std::max((cw.cout + co_tile - 1) / co_tile * co_tile, conv_halo_bn(cw.cout)), 0.f);
         const size_t boff = m_.blob.add_f32(bias);
         p.co_tile = co_tile;
         p.n_pad = n_pad;
@@ -456,7 +472,10 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
         gate = b.se_gate(prefix + ".se", y, r.conv(prefix + ".token_squeeze_excitation.convolutions.0", c / 4, c, 1, 1, true),
                          r.conv(prefix + ".token_squeeze_excitation.convolutions.2", c, c / 4, 1, 1, true), 1.f / 6.f);
     }
-    if (b.pair_rows_ok(blk.cin, blk.cout)) {
+    // The fused pair saves the hidden tensor's round trip, which pays on large
+    // maps; on small ones (fewer than ~100k pixel rows) its one-row-per-thread
+    // grid is too small and the two tiled GEMMs (same sums, same order) win.
+    if (b.pair_rows_ok(blk.cin, blk.cout) && (long long)y.n * y.h * y.w >= 98304) {
         return b.pair(prefix + ".pair", r.conv_bn(prefix + ".channel_conv1", blk.cin * 2, blk.cin, 1, 1, false),
                       r.conv_bn(prefix + ".channel_conv2", blk.cout, blk.cin * 2, 1, 1, false), y, gate, blk.residual());
     }
@@ -611,7 +630,7 @@ void detector_head(Builder& b, const std::vector<Act4>& feats, int channels) {
     if (total != channels) fail(PPOCR_ERR_INVALID_MODEL, "detector neck produced the wrong channel count");
     const Act4& base = feats[0];
     Act4 down = b.conv("head.conv_down", r.conv_bn("head.conv_down", hidden, channels, 3, 3, false, "norm"), srcs, base.n, base.h,
-                       base.w, 1, 1, 1, 1, 1, 1, ACT_RELU);
+                       base.w, 1, 1, 1, 1, 1, 1, ACT_RELU, -1, 1, nullptr, 0, true);
     std::vector<float> up_w = r.get("head.conv_up.convolution.weight", {(size_t)hidden, (size_t)hidden, 2, 2});
     std::vector<float> up_b = r.get("head.conv_up.convolution.bias", {(size_t)hidden});
     fold_transpose_bn(up_w, up_b, hidden, hidden, r, "head.conv_up.norm");

@@ -212,6 +212,16 @@ std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad) {
     return out;
 }
 
+std::vector<float> pack_conv_halo(const ConvWeight& cw, int bn) {
+    const int taps = cw.kh * cw.kw, quads = (cw.cin + 3) / 4;
+    std::vector<float> out((size_t)quads * taps * 4 * bn, 0.f);
+    for (int o = 0; o < cw.cout; ++o)
+        for (int i = 0; i < cw.cin; ++i)
+            for (int t = 0; t < taps; ++t)
+                out[(((size_t)(i / 4) * taps + t) * 4 + i % 4) * bn + o] = cw.w[((size_t)o * cw.cin + i) * taps + t];
+    return out;
+}
+
 float bf16_round(float f) {
     const uint16_t h = to_bf16(f);
     const uint32_t u = (uint32_t)h << 16;

@@ -63,6 +63,7 @@ private:
 // Packers (all from OIHW / [out][in] sources)
 std::vector<float> pack_conv_tiles(const ConvWeight& cw, int tile);       // [ceil(O/tile)][kh][kw][I][tile]
 std::vector<float> pack_conv_kn(const ConvWeight& cw, int& n_pad);        // [kh][kw][I][O_pad4] (implicit GEMM)
+std::vector<float> pack_conv_halo(const ConvWeight& cw, int bn);          // [ceil(I/4)][kh*kw][4][bn], zero padded
 // Tensor-core engine weights: [planes][n_pad][k_pad] with k = (ky, kx, i); plane
 // p holds the p-th BF16 piece of each value (planes 1: bf16(w); planes 3: the
 // three-way split w = w0 + w1 + w2), every value exactly representable in BF16.

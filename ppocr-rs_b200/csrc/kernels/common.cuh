@@ -89,8 +89,18 @@ __device__ __forceinline__ float4 f4_add(float4 a, float4 b) { return make_float
 __device__ __forceinline__ float4 f4_max(float4 a, float4 b) {
     return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
 }
+// Two FP32 FMAs in one packed sm_100 instruction: (c0, c1) += (a0, a1) * (b0, b1),
+// each lane rounded once, exactly as fmaf.  Halves the issue slots FP32 FMA
+// loops spend on arithmetic.
+__device__ __forceinline__ void fma2(float& c0, float& c1, float a0, float a1, float b0, float b1) {
+    const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(c0, c1));
+    c0 = r.x;
+    c1 = r.y;
+}
 __device__ __forceinline__ float4 f4_vfma(float4 a, float4 b, float4 c) {
-    return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
+    fma2(c.x, c.y, a.x, a.y, b.x, b.y);
+    fma2(c.z, c.w, a.z, a.w, b.z, b.w);
+    return c;
 }
 __device__ __forceinline__ float4 f4_act(float4 v, int act) {
     return make_float4(apply_act(v.x, act), apply_act(v.y, act), apply_act(v.z, act), apply_act(v.w, act));

@@ -8,8 +8,10 @@
 // (src/cpu/model.rs:626-693, 1022-1066, 1479-1521).
 //
 // One thread computes PIX output pixels (one in the launched configuration)
-// for a tile of CO output channels (16 when cout >= 16, else 8), so the input
-// window is read once per 16 channels; the block's weight tile
+// for a tile of CO output channels (16 when cout >= 16, else 8; 32 or 64 for
+// the 3-channel image input, whose few inputs per pixel would otherwise be
+// re-read once per 16 output channels), so the input window is read once per
+// CO channels; the block's weight tile
 // [kh][kw][cin][CO] sits in shared memory and is read by broadcast.
 // Input channels are read four at a time; source addresses are computed
 // once per (tap, source).
@@ -63,22 +65,14 @@ __device__ __forceinline__ void fma_quad(float (&acc)[CO], const float4 v, const
         const float4 w1 = *reinterpret_cast<const float4*>(wr + CO + o);
         const float4 w2 = *reinterpret_cast<const float4*>(wr + 2 * CO + o);
         const float4 w3 = *reinterpret_cast<const float4*>(wr + 3 * CO + o);
-        acc[o] = fmaf(v.x, w0.x, acc[o]);
-        acc[o + 1] = fmaf(v.x, w0.y, acc[o + 1]);
-        acc[o + 2] = fmaf(v.x, w0.z, acc[o + 2]);
-        acc[o + 3] = fmaf(v.x, w0.w, acc[o + 3]);
-        acc[o] = fmaf(v.y, w1.x, acc[o]);
-        acc[o + 1] = fmaf(v.y, w1.y, acc[o + 1]);
-        acc[o + 2] = fmaf(v.y, w1.z, acc[o + 2]);
-        acc[o + 3] = fmaf(v.y, w1.w, acc[o + 3]);
-        acc[o] = fmaf(v.z, w2.x, acc[o]);
-        acc[o + 1] = fmaf(v.z, w2.y, acc[o + 1]);
-        acc[o + 2] = fmaf(v.z, w2.z, acc[o + 2]);
-        acc[o + 3] = fmaf(v.z, w2.w, acc[o + 3]);
-        acc[o] = fmaf(v.w, w3.x, acc[o]);
-        acc[o + 1] = fmaf(v.w, w3.y, acc[o + 1]);
-        acc[o + 2] = fmaf(v.w, w3.z, acc[o + 2]);
-        acc[o + 3] = fmaf(v.w, w3.w, acc[o + 3]);
+        fma2(acc[o], acc[o + 1], v.x, v.x, w0.x, w0.y);
+        fma2(acc[o + 2], acc[o + 3], v.x, v.x, w0.z, w0.w);
+        fma2(acc[o], acc[o + 1], v.y, v.y, w1.x, w1.y);
+        fma2(acc[o + 2], acc[o + 3], v.y, v.y, w1.z, w1.w);
+        fma2(acc[o], acc[o + 1], v.z, v.z, w2.x, w2.y);
+        fma2(acc[o + 2], acc[o + 3], v.z, v.z, w2.z, w2.w);
+        fma2(acc[o], acc[o + 1], v.w, v.w, w3.x, w3.y);
+        fma2(acc[o + 2], acc[o + 3], v.w, v.w, w3.z, w3.w);
     }
 }
 
@@ -151,7 +145,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvParams p, int4 s
                             if (!in[q]) continue;
                             const float v = base[off[q] + (size_t)c * plane];
 #pragma unroll
-                            for (int o = 0; o < CO; ++o) acc[q][o] = fmaf(v, wr[o], acc[q][o]);
+                            for (int o = 0; o < CO; o += 2) fma2(acc[q][o], acc[q][o + 1], v, v, wr[o], wr[o + 1]);
                         }
                     }
                 } else {
@@ -230,7 +224,12 @@ cudaError_t launch_conv_t(const ConvParams& p, cudaStream_t stream) {
 
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream) {
     if (p.w_tc) return launch_conv_tc(p, stream);
+    if (p.halo) return launch_conv_halo(p, stream);
     if (p.weight_kn) return launch_conv_gemm(p, stream);
+    if (p.co_tile == 64)
+        return p.dtype == DT_F32 ? launch_conv_t<float, 64>(p, stream) : launch_conv_t<__nv_bfloat16, 64>(p, stream);
+    if (p.co_tile == 32)
+        return p.dtype == DT_F32 ? launch_conv_t<float, 32>(p, stream) : launch_conv_t<__nv_bfloat16, 32>(p, stream);
     if (p.co_tile == 16)
         return p.dtype == DT_F32 ? launch_conv_t<float, 16>(p, stream) : launch_conv_t<__nv_bfloat16, 16>(p, stream);
     if (p.co_tile != 8) return cudaErrorInvalidValue;

@@ -153,9 +153,9 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmParams p, ConvGa
             const float ar[TM] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const float br[TN] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int i = 0; i < TM; ++i)
+            for (int i = 0; i < TM; i += 2)
 #pragma unroll
-                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+                for (int j = 0; j < TN; ++j) fma2(acc[i][j], acc[i + 1][j], ar[i], ar[i + 1], br[j], br[j]);
         }
         __syncthreads();
     }

@@ -50,13 +50,14 @@ struct ConvParams {
     int nsrc = 0;
     int ho = 0, wo = 0, cout = 0;
     int kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0;
-    int co_tile = 8;                      // output channels per thread: 8 or 16
+    int co_tile = 8;                      // output channels per thread: 8, 16, 32 or 64
     const float* weight = nullptr;        // [ceil(cout/co_tile)][kh][kw][cin][co_tile]
     const float* weight_kn = nullptr;     // implicit-GEMM layout [kh][kw][cin][n_pad] (or null)
     int n_pad = 0;
     const void* w_tc = nullptr;           // tcgen05 conv: BF16 [tc_n_pad][kh*kw*tc_cin_pad] (or null)
     int tc_n_pad = 0, tc_cin_pad = 0;
-    const float* bias = nullptr;          // [cout]
+    int halo = 0;                         // 1: `weight` is the halo-tiled layout [ceil(cin/4)][kh*kw][4][conv_halo_bn(cout)]
+    const float* bias = nullptr;          // [cout] (padded to conv_halo_bn(cout) for the halo kernel)
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
     int res_scale = 1;
@@ -71,6 +72,14 @@ cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
 // tap, TMA stores of the output tile.  Needs w_tc.
 bool conv_tc_supported(const ConvParams& p);
 cudaError_t launch_conv_tc(const ConvParams& p, cudaStream_t stream);
+
+// Halo-tiled SIMT conv (conv_halo.cu): 3x3 at stride 1 or 2 and 2x2 at
+// stride 1, cout a multiple of 8 up to 64, NHWC sources (power-of-two
+// upsampled views) or the 3-channel NCHW FP32 image at stride 2.  Sums each
+// output in (input quad, ky, kx, channel) order.
+bool conv_halo_supported(const ConvParams& p);
+int conv_halo_bn(int cout);   // output channels the packed weights and bias are padded to
+cudaError_t launch_conv_halo(const ConvParams& p, cudaStream_t stream);
 
 // Implicit-GEMM view of a dense conv for the SIMT GEMM kernel (gemm_simt.cu).
 struct ConvGather {
@@ -155,6 +164,13 @@ cudaError_t launch_pair_rows(const PairRowsParams& p, cudaStream_t stream);
 // Row-per-thread pointwise GEMM for N <= 128 (rowgemm.cu).
 bool rows_gemm_supported(const GemmParams& p);
 cudaError_t launch_rows_gemm(const GemmParams& p, cudaStream_t stream);
+// FP32 SIMT GEMMs (gemm_simt.cu: any shape; gemm_stream.cu: persistent,
+// double-buffered, K <= 128 and N <= 128).  All FP32 GEMM kernels sum each
+// output in k order and add bias, activation and residual in the same order,
+// so they give bit-identical results.
+cudaError_t launch_gemm_simt(const GemmParams& p, cudaStream_t stream);
+bool gemm_stream_supported(const GemmParams& p);
+cudaError_t launch_gemm_stream(const GemmParams& p, cudaStream_t stream);
 
 // Tensor-core (tcgen05) GEMM availability: BF16 storage, k_pad % 64 == 0, n_pad % 16 == 0.
 bool gemm_tc_supported(const GemmParams& p);

@@ -83,10 +83,8 @@ __global__ void __launch_bounds__(kRows) pair_rows_kernel(PairRowsParams p) {
             const float4 w = *reinterpret_cast<const float4*>(w2j + o);
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                out[r][o] = fmaf(h[r], w.x, out[r][o]);
-                out[r][o + 1] = fmaf(h[r], w.y, out[r][o + 1]);
-                out[r][o + 2] = fmaf(h[r], w.z, out[r][o + 2]);
-                out[r][o + 3] = fmaf(h[r], w.w, out[r][o + 3]);
+                fma2(out[r][o], out[r][o + 1], h[r], h[r], w.x, w.y);
+                fma2(out[r][o + 2], out[r][o + 3], h[r], h[r], w.z, w.w);
             }
         }
     }
@@ -138,10 +136,8 @@ __global__ void __launch_bounds__(kRows) rows_gemm_kernel(GemmParams p) {
 #pragma unroll
             for (int o = 0; o < N; o += 4) {
                 const float4 ww = *reinterpret_cast<const float4*>(wk + o);
-                acc[o] = fmaf(av[q], ww.x, acc[o]);
-                acc[o + 1] = fmaf(av[q], ww.y, acc[o + 1]);
-                acc[o + 2] = fmaf(av[q], ww.z, acc[o + 2]);
-                acc[o + 3] = fmaf(av[q], ww.w, acc[o + 3]);
+                fma2(acc[o], acc[o + 1], av[q], av[q], ww.x, ww.y);
+                fma2(acc[o + 2], acc[o + 3], av[q], av[q], ww.z, ww.w);
             }
         }
     }

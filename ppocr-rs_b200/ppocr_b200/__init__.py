@@ -183,6 +183,7 @@ def library() -> C.CDLL:
         "ppocr_selftest_gemm": (I, [P, I, I, I, FP, FP, FP, I, FP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "ppocr_selftest_gemm_ex": (I, [P, I, I, I, FP, FP, FP, I, FP, I, I, I, FP, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]),
+        "ppocr_selftest_gemm_f32": (I, [P, I, I, I, FP, FP, FP, I, FP, I, FP, I, FP, C.POINTER(C.c_int)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_selftest_engine": (I, [P, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, FP, I, FP, C.POINTER(C.c_int),
@@ -339,6 +340,24 @@ class Gpu:
                                                 int(act), None if r is None else _fptr(r), int(bool(out_bf16)),
                                                 int(ldc), int(coff), _fptr(c), C.byref(used), C.byref(err)))
         return c, bool(used.value), err.value
+
+    def selftest_gemm_f32(self, a, w, bias=None, act: int = 0, gate=None, rows_per_image: int = 1, residual=None,
+                          kernel: int = 0):
+        """FP32 GEMM diagnostic through one kernel (0 dispatch, 1 SIMT, 2 rows, 3 streaming);
+        returns (C float32 [m, n], kernel that ran)."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        m, k = a.shape
+        n = w.shape[0]
+        c = np.zeros((m, n), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        used = C.c_int()
+        _check(library().ppocr_selftest_gemm_f32(self._h, m, n, k, _fptr(a), _fptr(w), None if b is None else _fptr(b),
+                                                 int(act), None if g is None else _fptr(g), int(rows_per_image),
+                                                 None if r is None else _fptr(r), int(kernel), _fptr(c), C.byref(used)))
+        return c, used.value
 
     def close(self) -> None:
         if getattr(self, "_h", None):
