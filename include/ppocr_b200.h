@@ -136,6 +136,17 @@ int ppocr_model_input_shape(const ppocr_model* model, size_t shape[4]);
 int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len,
                         float* output, size_t output_capacity);
 
+/* New: the host-buffer forward of `images` inputs (a multiple of the model's
+ * batch), run as images / batch chunks of the model's batch with each chunk's
+ * host-to-device copy, forward and device-to-host copy on their own streams,
+ * so copies of one chunk overlap the forward of the next.  `input` holds
+ * images x 3 x H x W values and `output` receives images x (per-image output)
+ * values, exactly what ppocr_model_forward returns chunk by chunk (the
+ * kernels are batch-invariant).  Page-locked host buffers let the copies run
+ * asynchronously; pageable ones still work.  Errors as ppocr_model_forward. */
+int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t images, float* output,
+                                  size_t output_capacity);
+
 /* forward_image(&GpuImage, ImagePreprocess) (src/gpu/model.rs:116-138,
  * 240-259; ImagePreprocess::{detector, recognizer} src/gpu/runtime.rs:50-69):
  * device-side quad resample, BGR swap, normalisation and right zero-padding
@@ -237,6 +248,11 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
  * as x2 [n, hi/2, wi/2, cin/2]).  1x1 / stride 1 / pad 0 with one source runs
  * the dense-rows mode.  used_tensor_cores / wait_error as for
  * ppocr_selftest_gemm. */
+/* Diagnostic (new): the measured FP32 CUDA-core throughput of `gpu` in
+ * TFLOP/s (independent FMA chains, no memory traffic), with plain and packed
+ * two-lane FMAs: the roofline denominator for the FP32 mode's SIMT kernels. */
+int ppocr_measure_fp32_peak(ppocr_gpu* gpu, double* tflops_fma, double* tflops_fma2);
+
 int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int cin, int cout, int kh, int kw,
                           int stride, int pad, int second, const float* x, const float* x2, const float* w,
                           const float* bias, int act, float* out, int* used_tensor_cores, int* wait_error);

@@ -8,6 +8,7 @@
 // arena moves.  Every wait is bounded: a stuck stream surfaces as Error::Gpu.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -95,8 +96,31 @@ struct DeviceWeights {
 };
 }  // namespace
 
+// Staging buffers, copy streams and events of ppocr_model_forward_pipelined:
+// two slots, so chunk s + 1 uploads while chunk s computes and chunk s - 1
+// downloads.
+struct ForwardPipe {
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    void* in_stage[2] = {nullptr, nullptr};
+    void* out_stage[2] = {nullptr, nullptr};
+    cudaEvent_t arrived[2] = {}, consumed[2] = {}, computed[2] = {}, downloaded[2] = {};
+    ~ForwardPipe() {
+        if (h2d) cudaStreamSynchronize(h2d);
+        if (d2h) cudaStreamSynchronize(d2h);
+        for (int i = 0; i < 2; ++i) {
+            if (in_stage[i]) cudaFree(in_stage[i]);
+            if (out_stage[i]) cudaFree(out_stage[i]);
+            for (cudaEvent_t e : {arrived[i], consumed[i], computed[i], downloaded[i]})
+                if (e) cudaEventDestroy(e);
+        }
+        if (h2d) cudaStreamDestroy(h2d);
+        if (d2h) cudaStreamDestroy(d2h);
+    }
+};
+
 struct ppocr_model {
     ppocr_gpu* gpu = nullptr;
+    std::unique_ptr<ForwardPipe> pipe;
     BuiltModel m;
     std::shared_ptr<DeviceWeights> weights;
     ppocr_load_options opts{};
@@ -254,7 +278,11 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
         auto w = std::make_shared<DeviceWeights>();
         w->bytes = blob.size();
         cuda_check(cudaMalloc(&w->ptr, std::max<size_t>(w->bytes, 256)), "allocate weights");
-        cuda_check(cudaMemcpy(w->ptr, blob.data(), w->bytes, cudaMemcpyHostToDevice), "upload weights");
+        // Ordered on the model's (non-blocking) stream and completed before
+        // returning: a plain cudaMemcpy from pageable memory may return before
+        // its DMA lands, and the stream would not wait for it.
+        cuda_check(cudaMemcpyAsync(w->ptr, blob.data(), w->bytes, cudaMemcpyHostToDevice, gpu->stream), "upload weights");
+        cuda_check(cudaStreamSynchronize(gpu->stream), "upload weights");
         w->host = blob;
         model->weights = w;
     }
@@ -349,7 +377,8 @@ int ppocr_upload_rgb(ppocr_gpu* gpu, uint32_t width, uint32_t height, const uint
         img->width = width;
         img->height = height;
         cuda_check(cudaMalloc(&img->rgb, expected), "allocate source image");
-        cuda_check(cudaMemcpy(img->rgb, pixels, expected, cudaMemcpyHostToDevice), "upload source image");
+        cuda_check(cudaMemcpyAsync(img->rgb, pixels, expected, cudaMemcpyHostToDevice, gpu->stream), "upload source image");
+        cuda_check(cudaStreamSynchronize(gpu->stream), "upload source image");
         *out = img.release();
     });
 }
@@ -450,6 +479,82 @@ int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len
         upload_and_run(model, input, input_len);
         download(model, model->output_tid(), output, model->m.output_elements * 4);
         finish(model, model->output_tid(), model->m.output_elements);
+    });
+}
+
+int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t images, float* output,
+                                  size_t output_capacity) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (!input || !output) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        const size_t batch = (size_t)model->m.n;
+        if (images == 0 || images % batch)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: image count " + std::to_string(images) + " is not a multiple of the model batch " +
+                                              std::to_string(batch));
+        const size_t chunks = images / batch;
+        const size_t in_elems = model->input_elements(), out_elems = model->m.output_elements;
+        if (output_capacity < chunks * out_elems)
+            fail(PPOCR_ERR_INVALID_INPUT, "output buffer holds " + std::to_string(output_capacity) + " values; " +
+                                              std::to_string(chunks * out_elems) + " required");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        if (!model->pipe) {
+            std::unique_ptr<ForwardPipe> p(new ForwardPipe());
+            cuda_check(cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking), "create upload stream");
+            cuda_check(cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking), "create download stream");
+            for (int i = 0; i < 2; ++i) {
+                cuda_check(cudaMalloc(&p->in_stage[i], in_elems * 4), "allocate input staging");
+                cuda_check(cudaMalloc(&p->out_stage[i], out_elems * 4), "allocate output staging");
+                for (cudaEvent_t* e : {&p->arrived[i], &p->consumed[i], &p->computed[i], &p->downloaded[i]})
+                    cuda_check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "create pipeline event");
+            }
+            model->pipe = std::move(p);
+        }
+        ForwardPipe& pp = *model->pipe;
+        cudaStream_t cs = model->gpu->stream;
+        float* dinput = static_cast<float*>(model->tensor(model->m.input));
+        const int otid = model->output_tid();
+        try {
+            cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), cs), "reset flags");
+            for (size_t c = 0; c < chunks; ++c) {
+                const int slot = (int)(c & 1);
+                // Upload chunk c once the forward of chunk c - 2 has taken its copy of the slot.
+                cuda_check(cudaStreamWaitEvent(pp.h2d, pp.consumed[slot], 0), "order upload");
+                cuda_check(cudaMemcpyAsync(pp.in_stage[slot], input + c * in_elems, in_elems * 4, cudaMemcpyHostToDevice, pp.h2d),
+                           "upload input");
+                cuda_check(cudaEventRecord(pp.arrived[slot], pp.h2d), "record upload");
+                // Forward chunk c on the model stream.
+                cuda_check(cudaStreamWaitEvent(cs, pp.arrived[slot], 0), "order forward");
+                // Staging copies run as kernels (with the finiteness checks folded
+                // in): a copy-engine copy here would queue behind the next chunk's upload.
+                cuda_check(launch_copy_check(static_cast<const float*>(pp.in_stage[slot]), dinput, in_elems, model->dflags, cs),
+                           "stage input");
+                cuda_check(cudaEventRecord(pp.consumed[slot], cs), "record staging");
+                model->run(cs);
+                // Hand the output to the download slot once chunk c - 2 has left it.
+                cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[slot], 0), "order output staging");
+                cuda_check(launch_copy_check(static_cast<const float*>(model->tensor(otid)), static_cast<float*>(pp.out_stage[slot]),
+                                             out_elems, model->dflags + 1, cs),
+                           "stage output");
+                cuda_check(cudaEventRecord(pp.computed[slot], cs), "record forward");
+                cuda_check(cudaStreamWaitEvent(pp.d2h, pp.computed[slot], 0), "order download");
+                cuda_check(cudaMemcpyAsync(output + c * out_elems, pp.out_stage[slot], out_elems * 4, cudaMemcpyDeviceToHost, pp.d2h),
+                           "read output");
+                cuda_check(cudaEventRecord(pp.downloaded[slot], pp.d2h), "record download");
+            }
+            cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[(chunks - 1) & 1], 0), "join download");
+            cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
+            wait_stream(cs, 0);
+        } catch (...) {
+            // The caller's buffers must not be touched after return.
+            cudaStreamSynchronize(pp.h2d);
+            cudaStreamSynchronize(cs);
+            cudaStreamSynchronize(pp.d2h);
+            throw;
+        }
+        if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
+        if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
     });
 }
 
@@ -755,7 +860,8 @@ int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, con
         char* d = nullptr;
         const size_t cbytes = (size_t)m * n * 4;
         cuda_check(cudaMalloc(&d, bytes.size() + cbytes + 256), "allocate GEMM test buffers");
-        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
         GemmParams p;
         p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad4; p.k_pad = kp;
         p.a = d + ao; p.w = reinterpret_cast<const float*>(d + wf); p.w_tc = d + wt;
@@ -808,7 +914,8 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
         const std::vector<uint8_t>& bytes = blob.bytes();
         char* d = nullptr;
         cuda_check(cudaMalloc(&d, bytes.size()), "allocate GEMM test buffers");
-        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
         GemmParams p;
         p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad4; p.k_pad = kp;
         p.a = d + ao; p.w = reinterpret_cast<const float*>(d + wf); p.w_tc = d + wt;
@@ -884,7 +991,8 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             cudaFree(d);
             fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the chosen GEMM kernel does not support this shape");
         }
-        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
         if (e == cudaSuccess)
             e = used == 3 ? launch_gemm_stream(p, gpu->stream) : used == 2 ? launch_rows_gemm(p, gpu->stream)
                                                                  : launch_gemm_simt(p, gpu->stream);
@@ -900,6 +1008,41 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
         cudaFree(d);
         cuda_check(e, "FP32 GEMM self-test");
         if (kernel_used) *kernel_used = used;
+    });
+}
+
+int ppocr_measure_fp32_peak(ppocr_gpu* gpu, double* tflops_fma, double* tflops_fma2) {
+    return guard([&] {
+        if (!gpu || !tflops_fma || !tflops_fma2) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        int dev = 0, sms = 0;
+        cuda_check(cudaGetDevice(&dev), "query device");
+        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "query SM count");
+        float* sink = nullptr;
+        cuda_check(cudaMalloc(&sink, sizeof(float)), "allocate probe sink");
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        cudaError_t e = cudaEventCreate(&e0);
+        if (e == cudaSuccess) e = cudaEventCreate(&e1);
+        const int blocks = sms * 4, iters = 20000;
+        const double flops = 2.0 * 16 * iters * 512.0 * blocks;
+        double best[2] = {0.0, 0.0};
+        for (int packed = 0; packed < 2 && e == cudaSuccess; ++packed)
+            for (int rep = 0; rep < 3 && e == cudaSuccess; ++rep) {
+                e = cudaEventRecord(e0, gpu->stream);
+                if (e == cudaSuccess) e = launch_fp32_peak(sink, blocks, iters, packed != 0, gpu->stream);
+                if (e == cudaSuccess) e = cudaEventRecord(e1, gpu->stream);
+                if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+                float ms = 0.f;
+                if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+                if (e == cudaSuccess && ms > 0.f) best[packed] = std::max(best[packed], flops / (ms * 1e-3) / 1e12);
+            }
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        cudaFree(sink);
+        cuda_check(e, "FP32 throughput probe");
+        *tflops_fma = best[0];
+        *tflops_fma2 = best[1];
     });
 }
 
@@ -948,7 +1091,8 @@ int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int
         const size_t cbytes = (size_t)p.m * cout * esize;
         char* d = nullptr;
         cuda_check(cudaMalloc(&d, bytes.size() + cbytes + 256), "allocate engine test buffers");
-        cudaError_t e = cudaMemcpy(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
         p.w = d + wof;
         p.bias = reinterpret_cast<const float*>(d + bo);
         p.a = d + xo;

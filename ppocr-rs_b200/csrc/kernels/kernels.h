@@ -350,7 +350,12 @@ cudaError_t launch_preprocess(const PreprocessParams& p, cudaStream_t stream);
 cudaError_t launch_nchw_to_nhwc(const float* in, void* out, int n, int c, int h, int w, DType dt, cudaStream_t stream);
 cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cudaStream_t stream);
 cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream);
+// dst[0, count) = src[0, count), *flag = 1 if any value is not finite (16-byte aligned buffers).
+cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* flag, cudaStream_t stream);
 // Same over `rows` rows of `cols` values at row stride `ld`.
 cudaError_t launch_check_finite_rows(const float* in, size_t rows, size_t cols, size_t ld, int* flag, cudaStream_t stream);
+// FP32 CUDA-core throughput probe (fp32_peak.cu): blocks x 512 threads, each
+// 16 FMA chains x iters steps (2 * 16 * iters * 512 * blocks flops).
+cudaError_t launch_fp32_peak(float* sink, int blocks, int iters, bool packed, cudaStream_t stream);
 
 }  // namespace ppocr

@@ -551,6 +551,26 @@ __global__ void check_finite_kernel(const float* in, size_t rows, size_t cols, s
         if (!isfinite(in[(i / cols) * ld + i % cols])) { *flag = 1; return; }
 }
 
+// Copies `count` floats and raises *flag if any is not finite: the staging
+// copy of the pipelined host-buffer forward, done by the SMs so it never
+// queues behind the other chunks' host copies on a copy engine.
+__global__ void copy_check_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t count, int* flag) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t n4 = count / 4;
+    bool bad = false;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(src) + i);
+        bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+        reinterpret_cast<float4*>(dst)[i] = v;
+    }
+    for (size_t i = n4 * 4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const float v = src[i];
+        bad |= !isfinite(v);
+        dst[i] = v;
+    }
+    if (bad) *flag = 1;
+}
+
 inline unsigned grid_for(long long total, int threads) {
     long long b = (total + threads - 1) / threads;
     if (b > 148LL * 32) b = 148LL * 32;
@@ -713,6 +733,13 @@ cudaError_t launch_check_finite_rows(const float* in, size_t rows, size_t cols, 
     if (rows == 0 || cols == 0) return cudaSuccess;
     const unsigned g = grid_for((long long)(rows * cols), 256);
     check_finite_kernel<<<g, 256, 0, stream>>>(in, rows, cols, ld, flag);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* flag, cudaStream_t stream) {
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return cudaErrorInvalidValue;
+    if (count == 0) return cudaSuccess;
+    copy_check_kernel<<<grid_for((long long)(count / 4 + 1), 256), 256, 0, stream>>>(src, dst, count, flag);
     return cudaGetLastError();
 }
 

@@ -168,6 +168,7 @@ def library() -> C.CDLL:
         "ppocr_model_output_shape": (I, [P, _SIZE4, C.POINTER(S), C.POINTER(S)]),
         "ppocr_model_input_shape": (I, [P, _SIZE4]),
         "ppocr_model_forward": (I, [P, FP, S, FP, S]),
+        "ppocr_model_forward_pipelined": (I, [P, FP, S, FP, S]),
         "ppocr_model_forward_image": (I, [P, P, FP, S, FP, S]),
         "ppocr_model_benchmark": (I, [P, FP, S, S, S, C.POINTER(C.c_double)]),
         "ppocr_model_forward_device": (I, [P, P, P, P]),
@@ -184,6 +185,7 @@ def library() -> C.CDLL:
         "ppocr_selftest_gemm_ex": (I, [P, I, I, I, FP, FP, FP, I, FP, I, I, I, FP, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]),
         "ppocr_selftest_gemm_f32": (I, [P, I, I, I, FP, FP, FP, I, FP, I, FP, I, FP, C.POINTER(C.c_int)]),
+        "ppocr_measure_fp32_peak": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_selftest_engine": (I, [P, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, FP, I, FP, C.POINTER(C.c_int),
@@ -341,6 +343,12 @@ class Gpu:
                                                 int(ldc), int(coff), _fptr(c), C.byref(used), C.byref(err)))
         return c, bool(used.value), err.value
 
+    def measure_fp32_peak(self):
+        """Measured FP32 CUDA-core throughput (TFLOP/s) with plain and packed FMAs."""
+        a, b = C.c_double(), C.c_double()
+        _check(library().ppocr_measure_fp32_peak(self._h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
     def selftest_gemm_f32(self, a, w, bias=None, act: int = 0, gate=None, rows_per_image: int = 1, residual=None,
                           kernel: int = 0):
         """FP32 GEMM diagnostic through one kernel (0 dispatch, 1 SIMT, 2 rows, 3 streaming);
@@ -428,6 +436,20 @@ class _Model:
         out = np.empty(self.output_elements, dtype=np.float32)
         _check(library().ppocr_model_forward(self._h, _fptr(x), x.size, _fptr(out), out.size))
         return ModelOutput(list(self.output_shape), out)
+
+    def forward_pipelined(self, values) -> np.ndarray:
+        """Forward of any multiple of the model batch from host memory, chunk by chunk with
+        the copies overlapped (ppocr_model_forward_pipelined); returns [images, ...] outputs
+        as a flat float32 array of images x per-image output values."""
+        x = np.ascontiguousarray(values, dtype=np.float32)
+        per_in = int(np.prod(self.input_shape[1:]))
+        if x.size % per_in:
+            raise InvalidInput(f"invalid input: {x.size} values are not whole {self.input_shape[1:]} images")
+        images = x.size // per_in
+        per_out = self.output_elements // self.input_shape[0]
+        out = np.empty(images * per_out, dtype=np.float32)
+        _check(library().ppocr_model_forward_pipelined(self._h, _fptr(x), images, _fptr(out), out.size))
+        return out
 
     def forward_image(self, image: GpuImage, preprocess: ImagePreprocess) -> ModelOutput:
         corners = np.asarray(preprocess.corners, dtype=np.float32).reshape(8)
