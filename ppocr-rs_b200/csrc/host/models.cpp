@@ -198,17 +198,18 @@ public:
         // BF16 with tensor cores: one plain NHWC source -> tcgen05 implicit GEMM
         // (TMA boxes per tap); other BF16 convs with NHWC sources -> the
         // register-tiled SIMT implicit GEMM (gemm_simt.cu).
-        // FP32: the halo-tiled kernel (conv_halo.cu) where its geometries apply
-        // and its blocked (quad, tap, channel) sum is the plain (tap, channel)
-        // sum (one input quad: the image stem) or any order is allowed (the
-        // detector head); elsewhere the direct kernel (conv.cu), 16 output
-        // channels per thread when cout >= 16 (8 otherwise).  The direct and
-        // implicit-GEMM kernels accumulate each output in (ky, kx, channel)
-        // order.  The detector's chaotic spec-weight parity check flipped a
-        // pixel when the stem and neck convs were re-associated, so those keep
-        // the tap-major order.
+        // FP32: the halo-tiled kernel (conv_halo.cu) where its geometries apply:
+        // blocked per-quad sums where any order is allowed (the detector head),
+        // else its tap-major mode, which keeps the direct kernel's (ky, kx,
+        // channel) order and needs the tile's whole input in one stage (the
+        // image stem, stem2a/2b).  Elsewhere the direct kernel (conv.cu), 16
+        // output channels per thread when cout >= 16 (8 otherwise).  The
+        // detector's chaotic spec-weight parity check flipped a pixel when the
+        // stem and neck convs were re-associated, so those keep the tap-major
+        // order.
         const bool tcconv = tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
-        const bool halo = !tcconv && m_.dtype == DT_F32 && (any_order || cin <= 4) && conv_halo_supported(p);
+        p.halo_order = any_order ? 0 : 1;
+        const bool halo = !tcconv && m_.dtype == DT_F32 && conv_halo_supported(p);
         const bool gemm = !tcconv && !halo && m_.dtype == DT_BF16 && conv_gemm_supported(p);
         // The NCHW image input has 3 channels: one thread covers up to 64 output
         // channels so each loaded input feeds 64 FMAs.

@@ -20,12 +20,16 @@
 // issues TM * TN packed two-lane FMAs (fma.rn.f32x2, each lane rounded as
 // fmaf).
 //
-// Per output the products of one input quad are summed in (ky, kx, channel)
+// Two summation orders.  Blocked (the default): per output the products of
+// one input quad are summed in (ky, kx, channel)
 // order into a fresh partial sum, each with one FMA, and the quads' partial
 // sums are added in quad order (a blocked summation: its rounding error grows
 // with the number of quads plus the products per quad, not with their
 // product); then the bias, activation and residual are applied.  With one
 // input quad (the 3-channel image) this is the plain (ky, kx, channel) sum.
+// Tap-major (ConvParams::halo_order = 1): a stage holds the tile's input for
+// every quad and each output is one running sum in (ky, kx, channel) order,
+// exactly the direct kernel's, for convs whose rounding must not change.
 // At stride 2 the halo tile keeps even and odd columns in separate halves, so
 // the 32 lanes of a warp, reading every second input column, still read 32
 // consecutive pixel quads.
@@ -78,14 +82,16 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 __device__ __forceinline__ float4 quad_at(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float4 quad_at(const __nv_bfloat16* p) { return load4(p); }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW>
+template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, bool TAPQ>
 __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, HaloArgs a) {
     constexpr int TAPS = KH * KW;
     extern __shared__ float4 hsm[];
     char* smem = reinterpret_cast<char*>(hsm);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int wy = warp % a.ty, g = warp / a.ty;
-    const int steps_per_tile = a.quads;
+    // Blocked mode: one step per input quad.  Tap-major mode: one step per tile,
+    // every quad of the tile resident in the stage.
+    const int steps_per_tile = TAPQ ? 1 : a.quads;
     int my_tiles = 0;
     if ((int)blockIdx.x < a.total) my_tiles = (a.total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
     const int steps = my_tiles * steps_per_tile;
@@ -118,31 +124,38 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
                 cp_async4(dst + d * 4 + 3, base, false);
             }
         } else {
-            // The source holding quad q (unrolled selects keep the parameter
-            // block out of local memory).
-            const void* sptr = p.src[0].ptr;
-            int cstride = p.src[0].cstride, coff = p.src[0].coff, q0 = a.qstart[0], sh = a.shift[0];
+            auto copy_quad = [&](int qq, T* dst) {
+                // The source holding quad qq (unrolled selects keep the parameter
+                // block out of local memory).
+                const void* sptr = p.src[0].ptr;
+                int cstride = p.src[0].cstride, coff = p.src[0].coff, q0 = a.qstart[0], sh = a.shift[0];
 #pragma unroll
-            for (int k = 1; k < 4; ++k)
-                if (k < p.nsrc && q >= a.qstart[k]) {
-                    sptr = p.src[k].ptr; cstride = p.src[k].cstride; coff = p.src[k].coff; q0 = a.qstart[k]; sh = a.shift[k];
+                for (int k = 1; k < 4; ++k)
+                    if (k < p.nsrc && qq >= a.qstart[k]) {
+                        sptr = p.src[k].ptr; cstride = p.src[k].cstride; coff = p.src[k].coff; q0 = a.qstart[k]; sh = a.shift[k];
+                    }
+                const int hs = p.hi >> sh, ws = p.wi >> sh;
+                const T* base = static_cast<const T*>(sptr) + (size_t)img * hs * ws * cstride + coff + (qq - q0) * 4;
+                for (int i = t; i < npx; i += kThreads) {
+                    const int ry = (int)(((float)i + 0.5f) * a.inv_iw), rx = i - ry * a.iw;
+                    const int y = iy0 + ry, x = ix0 + rx;
+                    const bool ok = y >= 0 && y < p.hi && x >= 0 && x < p.wi;
+                    const T* px = ok ? base + ((size_t)(y >> sh) * ws + (x >> sh)) * cstride : base;
+                    const int d = slot(ry, rx);
+                    if constexpr (sizeof(T) == 4) cp_async16(dst + d * 4, px, ok);
+                    else cp_async8(dst + d * 4, px, ok);
                 }
-            const int hs = p.hi >> sh, ws = p.wi >> sh;
-            const T* base = static_cast<const T*>(sptr) + (size_t)img * hs * ws * cstride + coff + (q - q0) * 4;
+            };
             T* dst = reinterpret_cast<T*>(st);
-            for (int i = t; i < npx; i += kThreads) {
-                const int ry = (int)(((float)i + 0.5f) * a.inv_iw), rx = i - ry * a.iw;
-                const int y = iy0 + ry, x = ix0 + rx;
-                const bool ok = y >= 0 && y < p.hi && x >= 0 && x < p.wi;
-                const T* px = ok ? base + ((size_t)(y >> sh) * ws + (x >> sh)) * cstride : base;
-                const int d = slot(ry, rx);
-                if constexpr (sizeof(T) == 4) cp_async16(dst + d * 4, px, ok);
-                else cp_async8(dst + d * 4, px, ok);
+            if constexpr (TAPQ) {
+                for (int qq = 0; qq < a.quads; ++qq) copy_quad(qq, dst + (size_t)qq * npx * 4);
+            } else {
+                copy_quad(q, dst);
             }
         }
-        const float* wsrc = p.weight + (size_t)q * TAPS * 4 * a.bn;
+        const float* wsrc = p.weight + (TAPQ ? 0 : (size_t)q * TAPS * 4 * a.bn);
         float* wdst = reinterpret_cast<float*>(st + a.halo_bytes);
-        const int wq = TAPS * a.bn;   // 16-byte chunks: TAPS * 4 * bn floats / 4
+        const int wq = (TAPQ ? a.quads : 1) * TAPS * a.bn;   // 16-byte chunks of [quads][TAPS][4][bn] floats
         for (int i = t; i < wq; i += kThreads) cp_async16(wdst + i * 4, wsrc + i * 4, true);
     };
 
@@ -161,6 +174,45 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
         const char* st = smem + (size_t)(step % NST) * a.stage_bytes;
         const T* halo = reinterpret_cast<const T*>(st);
         const float* wt = reinterpret_cast<const float*>(st + a.halo_bytes) + g * TN;
+        if constexpr (TAPQ) {
+            // The direct kernel's order: per output, taps outer, every input
+            // channel (quad by quad) inner, one running sum.
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+            const int plane = a.ih * a.iw * 4;
+#pragma unroll
+            for (int ky = 0; ky < KH; ++ky) {
+#pragma unroll
+                for (int kx = 0; kx < KW; ++kx) {
+                    const int col = SW == 2 ? (kx & 1) * half_w + lane + (kx >> 1) : lane + kx;
+                    const T* hx0 = halo + (size_t)((wy * SH + ky) * a.iw + col) * 4;
+                    for (int qq = 0; qq < a.quads; ++qq) {
+                        const T* hx = hx0 + (size_t)qq * plane;
+                        float4 av[TM];
+#pragma unroll
+                        for (int i = 0; i < TM; ++i) av[i] = quad_at(hx + (size_t)(i * 32) * 4);
+                        const float* wk = wt + (size_t)((qq * TAPS + ky * KW + kx) * 4) * a.bn;
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            float b[TN];
+#pragma unroll
+                            for (int j = 0; j < TN; j += 4) {
+                                const float4 v = *reinterpret_cast<const float4*>(wk + c * a.bn + j);
+                                b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+                            }
+#pragma unroll
+                            for (int i = 0; i < TM; ++i) {
+                                const float x = c == 0 ? av[i].x : c == 1 ? av[i].y : c == 2 ? av[i].z : av[i].w;
+#pragma unroll
+                                for (int j = 0; j < TN; j += 2) fma2(acc[i][j], acc[i][j + 1], x, x, b[j], b[j + 1]);
+                            }
+                        }
+                    }
+                }
+            }
+        } else {
         float part[TM][TN];
 #pragma unroll
         for (int i = 0; i < TM; ++i)
@@ -200,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
         for (int i = 0; i < TM; ++i)
 #pragma unroll
             for (int j = 0; j < TN; ++j) acc[i][j] = q == 0 ? part[i][j] : acc[i][j] + part[i][j];
+        }
         if (q == steps_per_tile - 1) {
             const int tile = (int)blockIdx.x + (step / steps_per_tile) * (int)gridDim.x;
             const int img = tile / per_img, rem = tile - img * per_img;
@@ -244,20 +297,26 @@ struct HaloPlan {
     size_t smem = 0;
 };
 
+// Tap-major mode (the direct kernel's summation order) when the conv asks for
+// it and has more than one input quad: every quad of a tile shares one stage.
+inline bool halo_tapq(const ConvParams& p) { return p.halo_order == 1 && p.src[0].mode != SRC_NCHW_F32 && p.cin > 4; }
+
 inline HaloPlan plan_halo(const ConvParams& p, int tn, int elem_bytes) {
+    const bool tapq = halo_tapq(p);
+    const int stage_quads = tapq ? p.cin / 4 : 1;
     HaloPlan best;
     const int groups = (p.cout + tn - 1) / tn;
     const int ty = 8 / groups;
     long long best_waste = -1;
     for (int tm = 4; tm >= 2; --tm) {
-        if (2 * tm * tn > 64) continue;   // running and partial sums stay in registers
+        if ((tapq ? 1 : 2) * tm * tn > 64) continue;   // the running (and partial) sums stay in registers
         HaloArgs a{};
         a.groups = groups; a.ty = ty; a.tw = 32 * tm;
         a.ih = (ty - 1) * p.sh + p.kh;
         a.iw = (a.tw - 1) * p.sw + p.kw;
         a.bn = groups * tn;
-        a.halo_bytes = (a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
-        a.stage_bytes = a.halo_bytes + p.kh * p.kw * 4 * a.bn * 4;
+        a.halo_bytes = (stage_quads * a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
+        a.stage_bytes = a.halo_bytes + stage_quads * p.kh * p.kw * 4 * a.bn * 4;
         int nst = 3;
         if ((size_t)nst * a.stage_bytes > 110 * 1024) nst = 2;
         if ((size_t)nst * a.stage_bytes > 110 * 1024) continue;
@@ -272,9 +331,9 @@ inline HaloPlan plan_halo(const ConvParams& p, int tn, int elem_bytes) {
     return best;
 }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW>
+template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, bool TAPQ>
 cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream_t stream) {
-    auto kernel = conv_halo_kernel<T, KH, KW, SH, SW, TN, TM, NST, NCHW>;
+    auto kernel = conv_halo_kernel<T, KH, KW, SH, SW, TN, TM, NST, NCHW, TAPQ>;
     static std::atomic<int> regs{0};
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
@@ -304,11 +363,11 @@ cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream
     return cudaGetLastError();
 }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, bool NCHW>
+template <typename T, int KH, int KW, int SH, int SW, int TN, bool NCHW, bool TAPQ>
 cudaError_t launch_tm(const ConvParams& p, const HaloPlan& pl, cudaStream_t stream) {
 #define HALO_TM(TM_, NST_)                                                                                   \
-    if constexpr (2 * TM_ * TN <= 64)                                                                          \
-        if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW>(p, pl.a, pl.smem, stream);
+    if constexpr ((TAPQ ? 1 : 2) * TM_ * TN <= 64)                                                             \
+        if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW, TAPQ>(p, pl.a, pl.smem, stream);
     HALO_TM(4, 3) HALO_TM(4, 2) HALO_TM(3, 3) HALO_TM(3, 2) HALO_TM(2, 3) HALO_TM(2, 2)
 #undef HALO_TM
     return cudaErrorInvalidConfiguration;
@@ -336,7 +395,11 @@ cudaError_t launch_tn(const ConvParams& p, cudaStream_t stream) {
     a.total = (int)total;
     a.inv_iw = 1.0f / (float)a.iw;
     if (a.total == 0) return cudaSuccess;
-    return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW>(p, pl, stream) : launch_tm<T, KH, KW, SH, SW, 8, NCHW>(p, pl, stream);
+    if (!NCHW && halo_tapq(p))
+        return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, true>(p, pl, stream)
+                        : launch_tm<T, KH, KW, SH, SW, 8, NCHW, true>(p, pl, stream);
+    return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, false>(p, pl, stream)
+                    : launch_tm<T, KH, KW, SH, SW, 8, NCHW, false>(p, pl, stream);
 }
 
 template <typename T>

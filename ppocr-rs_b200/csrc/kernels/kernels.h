@@ -57,6 +57,7 @@ struct ConvParams {
     const void* w_tc = nullptr;           // tcgen05 conv: BF16 [tc_n_pad][kh*kw*tc_cin_pad] (or null)
     int tc_n_pad = 0, tc_cin_pad = 0;
     int halo = 0;                         // 1: `weight` is the halo-tiled layout [ceil(cin/4)][kh*kw][4][conv_halo_bn(cout)]
+    int halo_order = 0;                   // halo kernel: 0 blocked per-quad sums, 1 the direct kernel's (tap, channel) order
     const float* bias = nullptr;          // [cout] (padded to conv_halo_bn(cout) for the halo kernel)
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
@@ -76,7 +77,8 @@ cudaError_t launch_conv_tc(const ConvParams& p, cudaStream_t stream);
 // Halo-tiled SIMT conv (conv_halo.cu): 3x3 at stride 1 or 2 and 2x2 at
 // stride 1, cout a multiple of 8 up to 64, NHWC sources (power-of-two
 // upsampled views) or the 3-channel NCHW FP32 image at stride 2.  Sums each
-// output in (input quad, ky, kx, channel) order.
+// output per input quad (blocked) or, with halo_order = 1, in the direct
+// kernel's (ky, kx, channel) order when the tile's whole input fits a stage.
 bool conv_halo_supported(const ConvParams& p);
 int conv_halo_bn(int cout);   // output channels the packed weights and bias are padded to
 cudaError_t launch_conv_halo(const ConvParams& p, cudaStream_t stream);

@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < rows) {
         const T* base = static_cast<const T*>(p.in) + (size_t)img * p.hw * p.in_cstride + g * 4;
+        // Unrolled so several loads are in flight; the adds stay in pixel order.
+#pragma unroll 4
         for (int px = px0 + r; px < px1; px += rows) acc = f4_add(acc, load4(base + (size_t)px * p.in_cstride));
     }
     part[threadIdx.x] = acc;
@@ -107,15 +109,17 @@ __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
 
 // out = x*g or x + x*g (residual_mul_in_place, src/cpu/kernels/mod.rs:777-796),
 // then + nearest-upsampled addend (upsample_add_nchw, src/cpu/model.rs:1265-1320).
-template <typename T>
+// I: the index type, 32-bit when the element count fits (64-bit division
+// costs several times the arithmetic of this bandwidth-bound loop).
+template <typename T, typename I>
 __global__ void __launch_bounds__(256) gate_apply_kernel(GateApplyParams p) {
-    const int cg = p.c / 4;
-    const long long total = (long long)p.n * p.h * p.w * cg;
-    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
+    const I cg = (I)(p.c / 4);
+    const I total = (I)p.n * (I)p.h * (I)p.w * cg;
+    const I hw = (I)p.h * (I)p.w;
+    for (I idx = (I)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (I)gridDim.x * blockDim.x) {
         const int c = (int)(idx % cg) * 4;
-        const long long pix = idx / cg;
-        const int img = (int)(pix / ((long long)p.h * p.w));
+        const I pix = idx / cg;
+        const int img = (int)(pix / hw);
         float4 v = load4(static_cast<const T*>(p.x) + (size_t)pix * p.c + c);
         if (p.gate) {
             const float4 g = *reinterpret_cast<const float4*>(p.gate + (size_t)img * p.c + c);
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(256) gate_apply_kernel(GateApplyParams p) {
             v = p.mode ? f4_add(s, v) : s;
         }
         if (p.addend) {
-            const int x = (int)(pix % p.w), y = (int)((pix / p.w) % p.h);
+            const int x = (int)(pix % (I)p.w), y = (int)((pix / (I)p.w) % (I)p.h);
             const int ah = p.h / p.add_scale, aw = p.w / p.add_scale;
             const size_t ai = ((size_t)(img * ah + y / p.add_scale) * aw + x / p.add_scale) * p.c + c;
             v = f4_add(v, load4(static_cast<const T*>(p.addend) + ai));
@@ -601,7 +605,9 @@ cudaError_t launch_channel_sum(const PoolParams& p, cudaStream_t stream) {
 
 cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
     if (p.c % 4 || p.n <= 0 || p.r <= 0) return cudaErrorInvalidValue;
-    // Images per block: enough blocks to cover the SMs, each weight row reused IMG times.
+    // Images per block: enough blocks to cover the SMs, each weight row reused IMG
+    // times.  (Eight images per block, to share the recognizer's large weight
+    // reads, measured twice as slow: the blocks' serial FMA chains dominate.)
     const int img = p.n <= 148 ? 1 : (p.n <= 296 ? 2 : 4);
     const size_t smem = (size_t)img * (p.c + p.r) * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
@@ -614,9 +620,16 @@ cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
 
 cudaError_t launch_gate_apply(const GateApplyParams& p, cudaStream_t stream) {
     if (p.c % 4 || p.out_cstride % 4 || p.out_coff % 4) return cudaErrorInvalidValue;
-    const unsigned g = grid_for((long long)p.n * p.h * p.w * (p.c / 4), 256);
-    if (p.dtype == DT_F32) gate_apply_kernel<float><<<g, 256, 0, stream>>>(p);
-    else gate_apply_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(p);
+    const long long total = (long long)p.n * p.h * p.w * (p.c / 4);
+    const unsigned g = grid_for(total, 256);
+    const bool narrow = total + (long long)g * 256 < 0x7fffffffLL;
+    if (p.dtype == DT_F32) {
+        if (narrow) gate_apply_kernel<float, uint32_t><<<g, 256, 0, stream>>>(p);
+        else gate_apply_kernel<float, unsigned long long><<<g, 256, 0, stream>>>(p);
+    } else {
+        if (narrow) gate_apply_kernel<__nv_bfloat16, uint32_t><<<g, 256, 0, stream>>>(p);
+        else gate_apply_kernel<__nv_bfloat16, unsigned long long><<<g, 256, 0, stream>>>(p);
+    }
     return cudaGetLastError();
 }
 
