@@ -34,8 +34,8 @@
 // the 32 lanes of a warp, reading every second input column, still read 32
 // consecutive pixel quads.
 // Sources: up to four NHWC views (nearest-upsampled by a power of two),
-// concatenated along channels, or the NCHW FP32 image (three channels padded
-// to one quad with a zero channel and zero weights).
+// concatenated along channels, or the NCHW FP32 image (three channel planes,
+// copied row by row in 16-byte chunks into a planar tile).
 #include <algorithm>
 #include <atomic>
 
@@ -51,6 +51,7 @@ constexpr size_t kSmemLimit = 200 * 1024;
 struct HaloArgs {
     int groups, ty, tw;              // channel groups, tile rows, tile columns
     int ih, iw;                      // input tile (pixels)
+    int iwp;                         // NCHW image: planar row pitch in floats (iw + 3 rounded up to 4)
     int tiles_x, tiles_y, total;     // tiles per image row / column, all tiles
     int quads;                       // input channel quads (steps per tile)
     int bn;                          // padded output channels (groups * TN)
@@ -68,11 +69,6 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
 __device__ __forceinline__ void cp_async8(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                  "l"(src), "r"(valid ? 8 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src), "r"(valid ? 4 : 0)
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -110,18 +106,22 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
         const int iy0 = tyi * a.ty * SH - p.pt, ix0 = txi * a.tw * SW - p.pl;
         const int npx = a.ih * a.iw;
         if constexpr (NCHW) {
+            // Planar [3][ih][iwp]: each tile row of each channel plane is copied as
+            // 16-byte chunks starting at the 4-aligned column xa <= ix0 (the image
+            // width is a multiple of 4, so no chunk straddles an image edge).
             const float* base = static_cast<const float*>(p.src[0].ptr) + (size_t)img * 3 * p.hi * p.wi;
             const size_t plane = (size_t)p.hi * p.wi;
             float* dst = reinterpret_cast<float*>(st);
-            for (int i = t; i < npx; i += kThreads) {
-                const int ry = (int)(((float)i + 0.5f) * a.inv_iw), rx = i - ry * a.iw;
-                const int y = iy0 + ry, x = ix0 + rx;
+            const int xa = ix0 >= 0 ? ix0 & ~3 : -((-ix0 + 3) & ~3);
+            const int nch = a.iwp / 4;                 // chunks per row
+            const int rows = 3 * a.ih;
+            for (int i = t; i < rows * nch; i += kThreads) {
+                const int row = i / nch, ch = i - row * nch;
+                const int c = row / a.ih, ry = row - c * a.ih;
+                const int y = iy0 + ry, x = xa + ch * 4;
                 const bool ok = y >= 0 && y < p.hi && x >= 0 && x < p.wi;
-                const float* src = ok ? base + (size_t)y * p.wi + x : base;
-                const int d = slot(ry, rx);
-#pragma unroll
-                for (int c = 0; c < 3; ++c) cp_async4(dst + d * 4 + c, src + c * plane, ok);
-                cp_async4(dst + d * 4 + 3, base, false);
+                const float* src = ok ? base + c * plane + (size_t)y * p.wi + x : base;
+                cp_async16(dst + (size_t)row * a.iwp + ch * 4, src, ok);
             }
         } else {
             auto copy_quad = [&](int qq, T* dst) {
@@ -174,7 +174,42 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
         const char* st = smem + (size_t)(step % NST) * a.stage_bytes;
         const T* halo = reinterpret_cast<const T*>(st);
         const float* wt = reinterpret_cast<const float*>(st + a.halo_bytes) + g * TN;
-        if constexpr (TAPQ) {
+        if constexpr (NCHW) {
+            // Planar image tile: per tap, channel by channel, (ky, kx, channel) order.
+            const float* pl = reinterpret_cast<const float*>(st);
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+            const int tile = (int)blockIdx.x + (step / steps_per_tile) * (int)gridDim.x;
+            const int rem = tile % per_img;
+            const int txi = rem % a.tiles_x;
+            const int ix0 = txi * a.tw * SW - p.pl;
+            const int xoff = ix0 - (ix0 >= 0 ? ix0 & ~3 : -((-ix0 + 3) & ~3));
+#pragma unroll
+            for (int ky = 0; ky < KH; ++ky) {
+#pragma unroll
+                for (int kx = 0; kx < KW; ++kx) {
+                    const float* wk = wt + (size_t)((ky * KW + kx) * 4) * a.bn;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        const float* prow = pl + (size_t)(c * a.ih + wy * SH + ky) * a.iwp + xoff + kx + lane * SW;
+                        float b[TN];
+#pragma unroll
+                        for (int j = 0; j < TN; j += 4) {
+                            const float4 v = *reinterpret_cast<const float4*>(wk + c * a.bn + j);
+                            b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+                        }
+#pragma unroll
+                        for (int i = 0; i < TM; ++i) {
+                            const float x = prow[i * 32 * SW];
+#pragma unroll
+                            for (int j = 0; j < TN; j += 2) fma2(acc[i][j], acc[i][j + 1], x, x, b[j], b[j + 1]);
+                        }
+                    }
+                }
+            }
+        } else if constexpr (TAPQ) {
             // The direct kernel's order: per output, taps outer, every input
             // channel (quad by quad) inner, one running sum.
 #pragma unroll
@@ -309,13 +344,19 @@ inline HaloPlan plan_halo(const ConvParams& p, int tn, int elem_bytes) {
     const int ty = 8 / groups;
     long long best_waste = -1;
     for (int tm = 4; tm >= 2; --tm) {
-        if ((tapq ? 1 : 2) * tm * tn > 64) continue;   // the running (and partial) sums stay in registers
+        const bool single = tapq || p.src[0].mode == SRC_NCHW_F32;   // one running sum, no partials
+        if ((single ? 1 : 2) * tm * tn > 64) continue;   // the running (and partial) sums stay in registers
         HaloArgs a{};
         a.groups = groups; a.ty = ty; a.tw = 32 * tm;
         a.ih = (ty - 1) * p.sh + p.kh;
         a.iw = (a.tw - 1) * p.sw + p.kw;
         a.bn = groups * tn;
-        a.halo_bytes = (stage_quads * a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
+        if (p.src[0].mode == SRC_NCHW_F32) {
+            a.iwp = (a.iw + 3 + 3) / 4 * 4;          // room for the 0..3-column alignment offset
+            a.halo_bytes = 3 * a.ih * a.iwp * 4;
+        } else {
+            a.halo_bytes = (stage_quads * a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
+        }
         a.stage_bytes = a.halo_bytes + stage_quads * p.kh * p.kw * 4 * a.bn * 4;
         int nst = 3;
         if ((size_t)nst * a.stage_bytes > 110 * 1024) nst = 2;
@@ -366,7 +407,7 @@ cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream
 template <typename T, int KH, int KW, int SH, int SW, int TN, bool NCHW, bool TAPQ>
 cudaError_t launch_tm(const ConvParams& p, const HaloPlan& pl, cudaStream_t stream) {
 #define HALO_TM(TM_, NST_)                                                                                   \
-    if constexpr ((TAPQ ? 1 : 2) * TM_ * TN <= 64)                                                             \
+    if constexpr ((TAPQ || NCHW ? 1 : 2) * TM_ * TN <= 64)                                                     \
         if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW, TAPQ>(p, pl.a, pl.smem, stream);
     HALO_TM(4, 3) HALO_TM(4, 2) HALO_TM(3, 3) HALO_TM(3, 2) HALO_TM(2, 3) HALO_TM(2, 2)
 #undef HALO_TM
@@ -434,7 +475,13 @@ bool conv_halo_supported(const ConvParams& p) {
     if (!geom) return false;
     if (p.out_cstride % 4 || p.out_coff % 4) return false;
     if (p.dtype == DT_BF16 && (p.out_cstride % 4 || p.out_coff % 4)) return false;
-    if (p.src[0].mode == SRC_NCHW_F32) return p.nsrc == 1 && p.cin == 3 && p.src[0].channels == 3 && p.sh == 2 && p.dtype == DT_F32;
+    if (p.src[0].mode == SRC_NCHW_F32) {
+        // 16-byte row chunks: the image width must keep every row 16-byte aligned.
+        if (!(p.nsrc == 1 && p.cin == 3 && p.src[0].channels == 3 && p.sh == 2 && p.dtype == DT_F32 && p.wi % 4 == 0))
+            return false;
+        HaloPlan pl = plan_halo(p, tn, 4);
+        return pl.tm != 0;
+    }
     int cin = 0;
     for (int s = 0; s < p.nsrc; ++s) {
         const ConvSource& src = p.src[s];
