@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
 // {2, 3, 4} whose tiles waste the fewest columns, among those whose stages
 // leave room for two resident blocks per SM.
 struct HaloPlan {
-    int tm = 0, nst = 0;
+    int tm = 0, tn = 0, nst = 0;
     HaloArgs a{};
     size_t smem = 0;
 };
@@ -336,38 +336,61 @@ struct HaloPlan {
 // it and has more than one input quad: every quad of a tile shares one stage.
 inline bool halo_tapq(const ConvParams& p) { return p.halo_order == 1 && p.src[0].mode != SRC_NCHW_F32 && p.cin > 4; }
 
-inline HaloPlan plan_halo(const ConvParams& p, int tn, int elem_bytes) {
+// Output channels the packed weights and the bias are padded to.
+inline int halo_bn(int cout) { return (cout + 7) / 8 * 8; }
+
+// Tile shape and pipeline depth for one launch.  Candidates: TN in {16, 8}
+// channels per thread (G = bn / TN channel groups, TY = 8 / G rows), TM in
+// {4, 3, 2, 1} pixels per thread, 3 or 2 stages.  Preferred: stages that
+// leave room for two resident blocks per SM, then the least tile padding,
+// then the most outputs per thread, then the deeper pipeline.
+inline HaloPlan plan_halo(const ConvParams& p, int elem_bytes) {
     const bool tapq = halo_tapq(p);
+    const bool nchw = p.src[0].mode == SRC_NCHW_F32;
     const int stage_quads = tapq ? p.cin / 4 : 1;
+    const bool single = tapq || nchw;   // one running sum, no partial sums
+    const int bn = halo_bn(p.cout);
     HaloPlan best;
-    const int groups = (p.cout + tn - 1) / tn;
-    const int ty = 8 / groups;
-    long long best_waste = -1;
-    for (int tm = 4; tm >= 2; --tm) {
-        const bool single = tapq || p.src[0].mode == SRC_NCHW_F32;   // one running sum, no partials
-        if ((single ? 1 : 2) * tm * tn > 64) continue;   // the running (and partial) sums stay in registers
-        HaloArgs a{};
-        a.groups = groups; a.ty = ty; a.tw = 32 * tm;
-        a.ih = (ty - 1) * p.sh + p.kh;
-        a.iw = (a.tw - 1) * p.sw + p.kw;
-        a.bn = groups * tn;
-        if (p.src[0].mode == SRC_NCHW_F32) {
-            a.iwp = (a.iw + 3 + 3) / 4 * 4;          // room for the 0..3-column alignment offset
-            a.halo_bytes = 3 * a.ih * a.iwp * 4;
-        } else {
-            a.halo_bytes = (stage_quads * a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
+    long long best_key[4] = {0, 0, 0, 0};
+    for (int tn : {16, 8}) {
+        if (bn % tn) continue;
+        const int groups = bn / tn;
+        if (groups > 8 || 8 % groups) continue;
+        const int ty = 8 / groups;
+        for (int tm = 4; tm >= 1; --tm) {
+            if ((single ? 1 : 2) * tm * tn > 64) continue;   // the sums stay in registers
+            HaloArgs a{};
+            a.groups = groups; a.ty = ty; a.tw = 32 * tm;
+            a.ih = (ty - 1) * p.sh + p.kh;
+            a.iw = (a.tw - 1) * p.sw + p.kw;
+            a.bn = bn;
+            if (nchw) {
+                a.iwp = (a.iw + 3 + 3) / 4 * 4;          // room for the 0..3-column alignment offset
+                a.halo_bytes = 3 * a.ih * a.iwp * 4;
+            } else {
+                a.halo_bytes = (stage_quads * a.ih * a.iw * 4 * elem_bytes + 15) / 16 * 16;
+            }
+            a.stage_bytes = a.halo_bytes + stage_quads * p.kh * p.kw * 4 * a.bn * 4;
+            a.tiles_x = (p.wo + a.tw - 1) / a.tw;
+            a.tiles_y = (p.ho + ty - 1) / ty;
+            for (int nst = 3; nst >= 2; --nst) {
+                const size_t smem = (size_t)nst * a.stage_bytes;
+                if (smem > kSmemLimit) continue;
+                // Tap-major with one resident block per SM measured slower than the
+                // direct kernel (stem3: 384 vs 343 us): it must keep two.
+                if (tapq && smem > 110 * 1024) continue;
+                const long long covered = (long long)a.tiles_x * a.tw * a.tiles_y * ty;
+                const long long waste_pct = (covered * 50 / ((long long)p.wo * p.ho) - 50);   // 2 % buckets
+                const long long key[4] = {smem <= 110 * 1024 ? 1 : 0, -waste_pct, (long long)tm * tn, nst};
+                bool better = best.tm == 0;
+                for (int k = 0; k < 4 && !better; ++k) {
+                    if (key[k] != best_key[k]) { better = key[k] > best_key[k]; break; }
+                }
+                if (!better) continue;
+                for (int k = 0; k < 4; ++k) best_key[k] = key[k];
+                best.tm = tm; best.tn = tn; best.nst = nst; best.a = a; best.smem = smem;
+            }
         }
-        a.stage_bytes = a.halo_bytes + stage_quads * p.kh * p.kw * 4 * a.bn * 4;
-        int nst = 3;
-        if ((size_t)nst * a.stage_bytes > 110 * 1024) nst = 2;
-        if ((size_t)nst * a.stage_bytes > 110 * 1024) continue;
-        a.tiles_x = (p.wo + a.tw - 1) / a.tw;
-        a.tiles_y = (p.ho + ty - 1) / ty;
-        const long long waste = (long long)a.tiles_x * a.tw - p.wo;
-        if (best_waste >= 0 && waste >= best_waste) continue;
-        best_waste = waste;
-        best.tm = tm; best.nst = nst; best.a = a;
-        best.smem = (size_t)nst * a.stage_bytes;
     }
     return best;
 }
@@ -409,16 +432,16 @@ cudaError_t launch_tm(const ConvParams& p, const HaloPlan& pl, cudaStream_t stre
 #define HALO_TM(TM_, NST_)                                                                                   \
     if constexpr ((TAPQ || NCHW ? 1 : 2) * TM_ * TN <= 64)                                                     \
         if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW, TAPQ>(p, pl.a, pl.smem, stream);
-    HALO_TM(4, 3) HALO_TM(4, 2) HALO_TM(3, 3) HALO_TM(3, 2) HALO_TM(2, 3) HALO_TM(2, 2)
+    HALO_TM(4, 3) HALO_TM(4, 2) HALO_TM(3, 3) HALO_TM(3, 2) HALO_TM(2, 3) HALO_TM(2, 2) HALO_TM(1, 3) HALO_TM(1, 2)
 #undef HALO_TM
     return cudaErrorInvalidConfiguration;
 }
 
 template <typename T, int KH, int KW, int SH, int SW, bool NCHW>
 cudaError_t launch_tn(const ConvParams& p, cudaStream_t stream) {
-    const int tn = p.cout % 16 == 0 || p.cout > 8 ? 16 : 8;
-    HaloPlan pl = plan_halo(p, tn, (int)sizeof(T));
+    HaloPlan pl = plan_halo(p, NCHW ? 4 : (int)sizeof(T));
     if (!pl.tm) return cudaErrorInvalidConfiguration;
+    const int tn = pl.tn;
     HaloArgs& a = pl.a;
     a.quads = NCHW ? 1 : p.cin / 4;
     int q = 0;
@@ -460,16 +483,10 @@ cudaError_t launch_geom(const ConvParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-int conv_halo_bn(int cout) {
-    const int tn = cout % 16 == 0 || cout > 8 ? 16 : 8;
-    return (cout + tn - 1) / tn * tn;
-}
+int conv_halo_bn(int cout) { return halo_bn(cout); }
 
 bool conv_halo_supported(const ConvParams& p) {
     if (p.cout < 8 || p.cout % 8 || p.cout > 64 || p.nsrc < 1 || p.nsrc > 4) return false;
-    const int tn = p.cout % 16 == 0 || p.cout > 8 ? 16 : 8;
-    const int groups = (p.cout + tn - 1) / tn;
-    if (8 % groups) return false;
     const bool geom = (p.kh == 3 && p.kw == 3 && ((p.sh == 1 && p.sw == 1) || (p.sh == 2 && p.sw == 2))) ||
                       (p.kh == 2 && p.kw == 2 && p.sh == 1 && p.sw == 1);
     if (!geom) return false;
@@ -479,7 +496,7 @@ bool conv_halo_supported(const ConvParams& p) {
         // 16-byte row chunks: the image width must keep every row 16-byte aligned.
         if (!(p.nsrc == 1 && p.cin == 3 && p.src[0].channels == 3 && p.sh == 2 && p.dtype == DT_F32 && p.wi % 4 == 0))
             return false;
-        HaloPlan pl = plan_halo(p, tn, 4);
+        HaloPlan pl = plan_halo(p, 4);
         return pl.tm != 0;
     }
     int cin = 0;
@@ -491,7 +508,7 @@ bool conv_halo_supported(const ConvParams& p) {
         cin += src.channels;
     }
     if (cin != p.cin) return false;
-    HaloPlan pl = plan_halo(p, tn, p.dtype == DT_F32 ? 4 : 2);
+    HaloPlan pl = plan_halo(p, p.dtype == DT_F32 ? 4 : 2);
     // The float-reciprocal row division in the tile loader is exact below these.
     return pl.tm != 0 && pl.a.ih * pl.a.iw < (1 << 14) && pl.a.iw < (1 << 10);
 }
