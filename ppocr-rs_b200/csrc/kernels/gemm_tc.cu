@@ -75,8 +75,7 @@ __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, c
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = v[j] + ((p.bias && col0 + j < p.n) ? p.bias[col0 + j] : 0.f);
     }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = apply_act_fast<ACT>(o[j]);
+    apply_act_fast_array<ACT>(o);
     if (p.residual) {
         size_t rrow = (size_t)row;
         if (p.res_scale > 1) {
@@ -170,8 +169,7 @@ __device__ __forceinline__ void epilogue_half(const TcArgs& p, uint32_t taddr, i
         for (int j = 0; j < HW; ++j)
             o[j] = __uint_as_float(r[j]) + ((p.bias && col0 + j < p.n) ? __ldg(p.bias + col0 + j) : 0.f);
     }
-#pragma unroll
-    for (int j = 0; j < HW; ++j) o[j] = apply_act_fast<ACT>(o[j]);
+    apply_act_fast_array<ACT>(o);
     if (res_vec) {
 #pragma unroll
         for (int j = 0; j < HW / 8; ++j) {
