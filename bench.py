@@ -242,14 +242,16 @@ def _e2e_models(tmp):
     return det, rec, d
 
 
-def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp):
-    """Pages/s of the OCR engine's batch call over this rank's pages (max over ranks of the wall time)."""
+def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp, rec_precision=None):
+    """Pages/s of the OCR engine's batch call over this rank's pages (max over ranks of the wall time).
+    rec_precision: None runs both models in FP32 (the reference's arithmetic); "bf16" runs the
+    recognizer on the tcgen05 BF16 path."""
     import ppocr_b200 as P
     from ppocr_b200 import sharding
 
     det, rec, d = _e2e_models(tmp)
     pages = _e2e_pages(pages_per_rank, rank, world)
-    eng = P.Engine(gpu, det, rec, d)
+    eng = P.Engine(gpu, det, rec, d, recognizer_precision=rec_precision)
     for _ in range(max(1, warmup)):
         res = eng.recognize_batch(pages)
     lines = sum(len(r["lines"]) for r in res)
@@ -258,9 +260,13 @@ def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp):
     for _ in range(steps):
         eng.recognize_batch(pages)
     dt = sharding.max_over_ranks(time.perf_counter() - t0)
+    stages = eng.stage_times()
     eng.close()
     value = pages_per_rank * world * steps / dt
-    return {"metric": "e2e pages/s @1920x1080 (tiny det + DB postprocess + tiny rec + CTC)", "value": round(value, 2),
+    name = "e2e pages/s @1920x1080 (tiny det + DB postprocess + tiny rec + CTC)"
+    if rec_precision:
+        name += f", recognizer {rec_precision}"
+    return {"metric": name, "value": round(value, 2), "last_call_stage_ms": {k: round(v, 2) for k, v in stages.items()},
             "unit": "pages/s", "ms_per_page": round(1000 * dt / (pages_per_rank * steps), 3),
             "pages_per_step_per_gpu": pages_per_rank, "steps": steps, "lines_per_page": round(lines / len(pages), 1),
             "api": "ppocr_engine_recognize_batch (host RGB8 pages in, JSON out)",
@@ -551,7 +557,8 @@ def run_b200(args):
     if args.kind == "det" and not args.no_secondary:
         model.close()
         secondary = {"rec": measure_rec(gpu, world, barrier, tmp),
-                     "e2e_pages": measure_e2e(gpu, 8, 4, 2, world, rank, barrier, tmp)}
+                     "e2e_pages": measure_e2e(gpu, 8, 4, 2, world, rank, barrier, tmp),
+                     "e2e_pages_rec_bf16": measure_e2e(gpu, 8, 4, 2, world, rank, barrier, tmp, rec_precision="bf16")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

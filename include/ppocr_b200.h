@@ -379,7 +379,8 @@ typedef struct ppocr_engine_options {
     int precision;                /* ppocr_precision of both models, PPOCR_PRECISION_FP32 */
     uint32_t detector_max_side;   /* 736 */
     ppocr_postprocess_options postprocess;
-    int reserved[8];
+    int recognizer_precision;     /* new: 0 = as `precision`; 1 + ppocr_precision for the recognizer alone */
+    int reserved[7];
 } ppocr_engine_options;
 void ppocr_engine_options_default(ppocr_engine_options* options);
 /* OcrEngine::load: the dictionary is parsed and checked against the
@@ -402,6 +403,12 @@ void ppocr_string_free(char* text);
 int ppocr_engine_recognize_batch(ppocr_engine* engine, size_t count, const uint8_t* const* rgb,
                                  const size_t* rgb_lengths, const uint32_t* widths, const uint32_t* heights,
                                  int format, char** results, size_t* result_lengths);
+
+/* New: wall time in ms of each stage of the last ppocr_engine_recognize_batch
+ * call: [0] page uploads, [1] detector forwards, [2] DB postprocess, [3]
+ * recognizer forwards with crop rectification (and any model loads), [4]
+ * result assembly.  Writes min(count, 5) values. */
+int ppocr_engine_stage_times(const ppocr_engine* engine, double* ms, size_t count);
 
 #ifdef __cplusplus
 }

@@ -286,6 +286,10 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
         w->host = blob;
         model->weights = w;
     }
+    // The packed host copy is no longer needed (the device weights hold one
+    // host copy for sharing checks): an engine caching hundreds of recognizer
+    // shapes would otherwise keep one per shape.
+    model->m.blob = WeightBlob();
     gpu->ensure_arena(model->m.plan.arena_bytes);
     cuda_check(cudaMalloc(&model->dflags, 2 * sizeof(int)), "allocate flags");
     model->hflags = PinnedFlags::acquire();

@@ -16,6 +16,7 @@
 // configuration from per-image shapes), so crops of all pages that share a
 // canvas width run in shared batches, with unused slots zero-filled.
 #include <algorithm>
+#include <chrono>
 #include <array>
 #include <atomic>
 #include <cstdlib>
@@ -77,11 +78,16 @@ std::string read_file(const char* path) {
 using Shape = std::array<size_t, 4>;
 
 // Cached model shapes: a few detector page sizes and batch sizes, and one
-// recognizer per (batch, canvas width) in use.
-constexpr size_t kDetectorCache = 4, kRecognizerCache = 32;
+// recognizer per (batch, canvas width) in use.  A page's text chunks span
+// hundreds of canvas widths, each a model shape (plan, graph); the recognizer
+// cache holds them all so repeated calls rebuild nothing (a cached shape keeps
+// its plan and graph on the host and 8 bytes of flags on the device; the
+// weights are shared).
+constexpr size_t kDetectorCache = 4, kRecognizerCache = 1024;
 constexpr size_t kDetectorBatch = 8;     // pages per detector forward
 constexpr size_t kRecognizerBatch = 64;  // crops per recognizer forward
-constexpr size_t kSmallBatch = 8;        // the batch of a width's last few crops
+// Batch shapes for a width's remaining crops: the smallest that holds them.
+constexpr size_t kTailBatches[] = {8, 16, 32};
 
 struct ImageHandle {
     ppocr_image* p = nullptr;
@@ -99,13 +105,16 @@ struct ppocr_engine {
     ppocr_gpu* gpu = nullptr;
     std::string det_path, rec_path;
     int det_size = PPOCR_TINY, rec_size = PPOCR_TINY;
-    ppocr_load_options load{};
+    ppocr_load_options load{}, rec_load{};
     PostOptions post;
     uint32_t max_side = 736;
     std::vector<std::string> dict;
     size_t classes = 0;
     std::vector<std::pair<Shape, ppocr_model*>> det_cache, rec_cache;
     ppocr_model* rec_weights = nullptr;   // keeps the shared packed recognizer weights alive
+    // Wall time of the last batch call per stage (ms): upload, detector,
+    // DB postprocess, recognizer forwards (model loads included), assembly.
+    double stage_ms[5] = {0, 0, 0, 0, 0};
 
     ~ppocr_engine() {
         for (auto& e : det_cache) ppocr_model_destroy(e.second);
@@ -134,10 +143,10 @@ struct ppocr_engine {
             rec_cache.erase(rec_cache.begin());
         }
         ppocr_model* m = nullptr;
-        check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &load, rec_weights, &m));
+        check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &rec_load, rec_weights, &m));
         if (!rec_weights) {
             // A second session on the same weights owns nothing but keeps them loaded.
-            check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &load, m, &rec_weights));
+            check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &rec_load, m, &rec_weights));
         }
         rec_cache.emplace_back(shape, m);
         return m;
@@ -150,6 +159,13 @@ struct ppocr_engine {
     };
 
     std::vector<OcrResult> recognize_batch(const std::vector<Page>& pages) {
+        using clock = std::chrono::steady_clock;
+        auto t_prev = clock::now();
+        auto lap = [&](int stage) {
+            const auto t = clock::now();
+            stage_ms[stage] = std::chrono::duration<double, std::milli>(t - t_prev).count();
+            t_prev = t;
+        };
         const size_t np = pages.size();
         std::vector<OcrResult> res(np);
         std::vector<ImageHandle> imgs(np);
@@ -160,6 +176,7 @@ struct ppocr_engine {
             detector_input_size(pages[i].width, pages[i].height, max_side, &res[i].input_w, &res[i].input_h);
             check(ppocr_upload_rgb(gpu, pages[i].width, pages[i].height, pages[i].rgb, pages[i].len, &imgs[i].p));
         }
+        lap(0);
         // Detector: pages of one input size, kDetectorBatch per forward.
         std::vector<std::vector<float>> probs(np);
         std::map<std::pair<uint32_t, uint32_t>, std::vector<size_t>> by_size;
@@ -176,6 +193,7 @@ struct ppocr_engine {
                 for (size_t k = 0; k < n; ++k) probs[idx[s + k]].assign(out.begin() + k * per, out.begin() + (k + 1) * per);
             }
         }
+        lap(1);
         // DB postprocess on host threads.
         std::vector<std::vector<Detection>> dets(np);
         std::vector<std::string> errors(np);
@@ -196,6 +214,7 @@ struct ppocr_engine {
         for (auto& t : pool) t.join();
         for (size_t i = 0; i < np; ++i)
             if (!errors[i].empty()) fail(PPOCR_ERR_INVALID_INPUT, errors[i]);
+        lap(2);
         // Crops of every page, grouped by their chunk's canvas width.
         struct Crop {
             size_t page, det, content;
@@ -210,8 +229,10 @@ struct ppocr_engine {
         for (const auto& [width, crops] : by_width) {
             for (size_t s = 0; s < crops.size(); s += kRecognizerBatch) {
                 const size_t n = std::min(kRecognizerBatch, crops.size() - s);
-                // Two batch shapes per canvas width keep the model cache small.
-                ppocr_model* rec = recognizer(Shape{n <= kSmallBatch ? kSmallBatch : kRecognizerBatch, 3, 48, width});
+                size_t shape_n = kRecognizerBatch;
+                for (size_t b : kTailBatches)
+                    if (n <= b) { shape_n = b; break; }
+                ppocr_model* rec = recognizer(Shape{shape_n, 3, 48, width});
                 size_t out_shape[4] = {0, 0, 0, 0};
                 check(ppocr_model_output_shape(rec, out_shape, nullptr, nullptr));
                 const size_t steps = out_shape[1];
@@ -238,6 +259,7 @@ struct ppocr_engine {
                 }
             }
         }
+        lap(3);
         for (size_t i = 0; i < np; ++i)
             for (size_t d = 0; d < dets[i].size(); ++d) {
                 OcrLine l;
@@ -247,6 +269,7 @@ struct ppocr_engine {
                 l.recognition_score = decoded[i][d].score;
                 res[i].lines.push_back(std::move(l));
             }
+        lap(4);
         return res;
     }
 
@@ -419,12 +442,17 @@ int ppocr_engine_create(ppocr_gpu* gpu, const char* detector_model, const char* 
         e->max_side = o.detector_max_side;
         ppocr_load_options_default(&e->load);
         e->load.precision = o.precision;
+        e->rec_load = e->load;
+        if (o.recognizer_precision) e->rec_load.precision = o.recognizer_precision - 1;
+        if (e->rec_load.precision != PPOCR_PRECISION_FP32 && e->rec_load.precision != PPOCR_PRECISION_BF16 &&
+            e->rec_load.precision != PPOCR_PRECISION_FP32_TC)
+            fail(PPOCR_ERR_INVALID_INPUT, "unknown recognizer precision");
         e->dict = parse_dictionary(read_file(dictionary));
         // validate_recognizer_dictionary (src/ocr.rs:689-700), against the file's classifier.
         const size_t shape[4] = {1, 3, 48, 320};
         size_t out_shape[4] = {0, 0, 0, 0};
-        check(ppocr_inspect_model(recognizer_model, 1, o.recognizer_size, shape, o.precision, nullptr, nullptr, nullptr,
-                                  out_shape));
+        check(ppocr_inspect_model(recognizer_model, 1, o.recognizer_size, shape, e->rec_load.precision, nullptr, nullptr,
+                                  nullptr, out_shape));
         e->classes = out_shape[2];
         if (e->classes != e->dict.size() + 1 && e->classes != e->dict.size() + 2)
             fail(PPOCR_ERR_INVALID_INPUT, "recognizer has " + std::to_string(e->classes) +
@@ -453,6 +481,13 @@ int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_
         std::memcpy(buf, s.c_str(), s.size() + 1);
         *result = buf;
         if (result_length) *result_length = s.size();
+    });
+}
+
+int ppocr_engine_stage_times(const ppocr_engine* engine, double* ms, size_t count) {
+    return guard([&] {
+        if (!engine || !ms) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        for (size_t i = 0; i < count && i < 5; ++i) ms[i] = engine->stage_ms[i];
     });
 }
 

@@ -128,7 +128,8 @@ class _Detection(C.Structure):
 
 class _EngineOptions(C.Structure):
     _fields_ = [("detector_size", C.c_int), ("recognizer_size", C.c_int), ("precision", C.c_int),
-                ("detector_max_side", C.c_uint32), ("postprocess", _PostOptions), ("reserved", C.c_int * 8)]
+                ("detector_max_side", C.c_uint32), ("postprocess", _PostOptions), ("recognizer_precision", C.c_int),
+                ("reserved", C.c_int * 7)]
 
 
 class _LoadOptions(C.Structure):
@@ -207,6 +208,7 @@ def library() -> C.CDLL:
         "ppocr_engine_recognize": (I, [P, C.POINTER(C.c_uint8), S, C.c_uint32, C.c_uint32, I,
                                        C.POINTER(C.c_void_p), C.POINTER(S)]),
         "ppocr_string_free": (None, [C.c_void_p]),
+        "ppocr_engine_stage_times": (I, [P, C.POINTER(C.c_double), S]),
         "ppocr_engine_recognize_batch": (I, [P, S, C.POINTER(C.c_void_p), C.POINTER(S), C.POINTER(C.c_uint32),
                                              C.POINTER(C.c_uint32), I, C.POINTER(C.c_void_p), C.POINTER(S)]),
         "ppocr_recognizer_forward_crops_ex": (I, [P, C.POINTER(C.c_void_p), S, FP, C.POINTER(S),
@@ -699,12 +701,14 @@ class Engine:
 
     def __init__(self, gpu: Gpu, detector_model: str, recognizer_model: str, dictionary: str,
                  detector_size="tiny", recognizer_size="tiny", precision="fp32", detector_max_side: int = 736,
-                 postprocess: PostprocessOptions = None):
+                 postprocess: PostprocessOptions = None, recognizer_precision=None):
         o = _EngineOptions()
         library().ppocr_engine_options_default(C.byref(o))
         o.detector_size = ModelSize.parse(detector_size)
         o.recognizer_size = ModelSize.parse(recognizer_size)
         o.precision = Precision.parse(precision)
+        if recognizer_precision is not None:
+            o.recognizer_precision = 1 + Precision.parse(recognizer_precision)
         o.detector_max_side = int(detector_max_side or 0)
         if postprocess is not None:
             o.postprocess = postprocess._c()
@@ -727,6 +731,12 @@ class Engine:
         finally:
             library().ppocr_string_free(out)
         return json.loads(text) if fmt == "json" else text
+
+    def stage_times(self) -> dict:
+        """Wall ms of each stage of the last recognize_batch call."""
+        ms = (C.c_double * 5)()
+        _check(library().ppocr_engine_stage_times(self._h, ms, 5))
+        return dict(zip(["upload", "detector", "postprocess", "recognizer", "assembly"], list(ms)))
 
     def recognize_batch(self, pages, fmt: str = "json"):
         """OcrEngine::recognize over several RGB8 pages at once (same per-page results)."""
