@@ -142,6 +142,9 @@ struct ppocr_model {
         c.arena = static_cast<char*>(gpu->arena);
         c.weights = static_cast<const char*>(weights->ptr);
         c.tensors = &m.plan.tensors;
+        c.side = gpu->side;
+        c.fork = gpu->fork;
+        c.join = gpu->join;
         return c;
     }
     void* tensor(int tid) const { return tid < 0 ? nullptr : static_cast<char*>(gpu->arena) + m.plan.tensors[tid].offset; }
@@ -343,6 +346,9 @@ int ppocr_gpu_create(int device, ppocr_gpu** out) {
         if (prop.major < 10) fail(PPOCR_ERR_GPU, std::string("device ") + prop.name + " is not sm_100 class; this build targets sm_100a");
         g->name = prop.name;
         cuda_check(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "create stream");
+        cuda_check(cudaStreamCreateWithFlags(&g->side, cudaStreamNonBlocking), "create side stream");
+        cuda_check(cudaEventCreateWithFlags(&g->fork, cudaEventDisableTiming), "create fork event");
+        cuda_check(cudaEventCreateWithFlags(&g->join, cudaEventDisableTiming), "create join event");
         *out = g.release();
     });
 }
@@ -352,7 +358,11 @@ void ppocr_gpu_destroy(ppocr_gpu* gpu) {
     cudaSetDevice(gpu->device);
     if (gpu->stream) cudaStreamSynchronize(gpu->stream);
     if (gpu->arena) cudaFree(gpu->arena);
+    if (gpu->side) cudaStreamSynchronize(gpu->side);
     if (gpu->stream) cudaStreamDestroy(gpu->stream);
+    if (gpu->side) cudaStreamDestroy(gpu->side);
+    if (gpu->fork) cudaEventDestroy(gpu->fork);
+    if (gpu->join) cudaEventDestroy(gpu->join);
     delete gpu;
 }
 

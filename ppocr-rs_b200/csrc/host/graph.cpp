@@ -41,6 +41,7 @@ void Plan::add_op(const std::string& name, std::vector<int> reads, std::vector<i
     writes.erase(std::remove(writes.begin(), writes.end(), -1), writes.end());
     r.reads = std::move(reads);
     r.writes = std::move(writes);
+    r.lane = lane;
     ops.push_back(std::move(r));
 }
 
@@ -59,6 +60,12 @@ size_t Plan::finalize() {
             t.last = std::max(t.last, i);
         }
     }
+    for (const Region& g : regions)
+        for (auto& t : tensors)
+            if (t.first >= 0 && t.first < g.end && t.last >= g.begin) {
+                t.first = std::min(t.first, g.begin);
+                t.last = std::max(t.last, g.end - 1);
+            }
     for (auto& t : tensors)
         if (t.pinned || t.first < 0) { t.first = -1; t.last = nops; }
 
@@ -89,9 +96,22 @@ size_t Plan::finalize() {
 }
 
 void Plan::run(const Ctx& ctx, cudaStream_t stream) const {
-    for (const auto& op : ops) {
-        cudaError_t e = op.fn(ctx, stream);
+    const bool conc = ctx.side && ctx.fork && ctx.join;
+    size_t r = 0;
+    for (int i = 0; i < (int)ops.size(); ++i) {
+        const OpRec& op = ops[i];
+        const bool in_region = conc && r < regions.size() && i >= regions[r].begin && i < regions[r].end;
+        if (in_region && i == regions[r].begin) {
+            cuda_check(cudaEventRecord(ctx.fork, stream), "fork concurrent region");
+            cuda_check(cudaStreamWaitEvent(ctx.side, ctx.fork, 0), "fork concurrent region");
+        }
+        cudaError_t e = op.fn(ctx, in_region && op.lane == 1 ? ctx.side : stream);
         if (e != cudaSuccess) fail(PPOCR_ERR_GPU, "launch " + op.name + ": " + cudaGetErrorString(e));
+        if (in_region && i + 1 == regions[r].end) {
+            cuda_check(cudaEventRecord(ctx.join, ctx.side), "join concurrent region");
+            cuda_check(cudaStreamWaitEvent(stream, ctx.join, 0), "join concurrent region");
+            ++r;
+        }
     }
 }
 

@@ -5,6 +5,8 @@
 // greedy interval colouring over op-index lifetimes (largest first, lowest
 // offset that does not overlap a tensor alive at the same time), the same
 // job as ppocr-rs's ArenaAllocator / compact_layout (src/gpu/runtime.rs:414-557).
+// A tensor touched inside a concurrent region is live for the whole region,
+// so ops that may run at the same time never share memory.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -32,6 +34,10 @@ struct Ctx {
     char* arena = nullptr;
     const char* weights = nullptr;
     const std::vector<TensorDesc>* tensors = nullptr;
+    // Second stream and the fork / join events of concurrent regions (null:
+    // every op on the launch stream).
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
     void* act(int tid) const { return tid < 0 ? nullptr : arena + (*tensors)[tid].offset; }
     const float* wf(size_t off) const { return reinterpret_cast<const float*>(weights + off); }
     const void* wb(size_t off) const { return weights + off; }
@@ -46,12 +52,29 @@ struct OpRec {
     std::string kind;          // kernel family: conv, dwconv, gemm, se, gate, head, ...
     double weight_bytes = 0;   // parameter bytes the kernel reads
     double flops = 0;          // algorithmic multiply-adds x 2
+    int lane = 0;              // inside a concurrent region: 0 the launch stream, 1 the side stream
+};
+
+// Ops [begin, end) whose lane-1 ops run on a second stream, concurrently with
+// the region's lane-0 ops: the side stream waits for everything enqueued
+// before the region, and the launch stream waits for the side stream at its
+// end.  Lane-1 ops must not depend on the region's lane-0 ops or vice versa.
+struct Region {
+    int begin = 0, end = 0;
 };
 
 struct Plan {
     std::vector<TensorDesc> tensors;
     std::vector<OpRec> ops;
+    std::vector<Region> regions;
+    int lane = 0;               // lane of the ops added next
     size_t arena_bytes = 0;
+
+    // Concurrent regions: ops added between begin_region and end_region with
+    // set_lane(1) form the side lane.  Regions do not nest.
+    void begin_region() { regions.push_back({(int)ops.size(), -1}); }
+    void end_region() { regions.back().end = (int)ops.size(); lane = 0; }
+    void set_lane(int l) { lane = l; }
 
     int add_tensor(const std::string& name, int n, int h, int w, int c, DType dt, bool pinned = false);
     int add_raw(const std::string& name, size_t bytes, bool pinned = false);

@@ -45,6 +45,8 @@ void wait_stream(cudaStream_t s, int timeout_ms);
 struct ppocr_gpu {
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;                            // concurrent regions' second stream
+    cudaEvent_t fork = nullptr, join = nullptr;             // their fork / join events
     std::mutex mu;
     void* arena = nullptr;
     size_t arena_bytes = 0;

@@ -129,6 +129,12 @@ public:
                        srcs.empty() ? "gemm" : "conv", (double)planes * p.n_pad * p.k_pad * 2, flops);
     }
 
+    // Concurrent regions of the plan (graph.hpp): ops added in lane 1 between
+    // begin_region and end_region run on the side stream beside the lane-0 ops.
+    void begin_region() { m_.plan.begin_region(); }
+    void lane(int l) { m_.plan.set_lane(l); }
+    void end_region() { m_.plan.end_region(); }
+
     Act4 tensor(const std::string& name, int n, int h, int w, int c) {
         Act4 a;
         a.tid = m_.plan.add_tensor(name, n, h, w, c, m_.dtype);
@@ -439,13 +445,18 @@ Act4 large_stem(Builder& b, int in_tid, int n, int h, int w, int mid, int out) {
     const std::string p = "model.backbone.encoder.convolution.";
     Act4 e = b.conv("stem1", r.conv_bn(p + "stem1", mid, 3, 3, 3, false), {{in_tid, 3, 3, 0, 1, SRC_NCHW_F32}}, n, h, w, 2, 2,
                     1, 1, 1, 1, ACT_RELU);
-    Act4 br = b.conv1("stem2a", r.conv_bn(p + "stem2a", mid / 2, mid, 2, 2, false), e, 1, 1, 0, 0, 1, 1, ACT_RELU);
     // cat(max_pool_same_upper(stem1), stem2b) is materialised once: the pool
     // writes channels [0, mid) and stem2b channels [mid, 2 mid) of one tensor,
     // so stem3's 3x3 window reads plain pixels instead of re-pooling per tap.
+    // The bandwidth-bound pool runs on the side stream beside stem2a/2b.
     Act4 cat = b.tensor("stem.cat", n, e.h, e.w, 2 * mid);
+    b.begin_region();
+    b.lane(1);
     b.maxpool_into("stem.pool", e, cat, 0);
+    b.lane(0);
+    Act4 br = b.conv1("stem2a", r.conv_bn(p + "stem2a", mid / 2, mid, 2, 2, false), e, 1, 1, 0, 0, 1, 1, ACT_RELU);
     b.conv1("stem2b", r.conv_bn(p + "stem2b", mid, mid / 2, 2, 2, false), br, 1, 1, 0, 0, 1, 1, ACT_RELU, -1, 1, &cat, mid);
+    b.end_region();
     Act4 x = b.conv1("stem3", r.conv_bn(p + "stem3", mid, mid * 2, 3, 3, false), cat, 2, 2, 1, 1, 1, 1, ACT_RELU);
     GemmOpts o;
     o.act = ACT_RELU;
@@ -523,7 +534,11 @@ std::vector<Act4> rep_lk_fpn(Builder& b, const std::vector<Act4>& stages, int ne
     const WeightReader& r = b.reader();
     std::vector<Act4> hid(4);
     std::vector<int> gates(4);
+    // The pyramid levels are independent until the top-down adds: level 0
+    // (the largest map) on the launch stream, levels 1-3 on the side stream.
+    b.begin_region();
     for (int i = 0; i < 4; ++i) {
+        b.lane(i == 0 ? 0 : 1);
         const std::string p = "model.neck.insert_conv." + std::to_string(i);
         GemmOpts o;
         o.has_bias = false;
@@ -531,6 +546,7 @@ std::vector<Act4> rep_lk_fpn(Builder& b, const std::vector<Act4>& stages, int ne
         gates[i] = b.se_gate(p + ".se", hid[i], r.conv(p + ".squeeze_excitation_block.conv1", neck / 4, neck, 1, 1, true),
                              r.conv(p + ".squeeze_excitation_block.conv2", neck, neck / 4, 1, 1, true), 0.2f);
     }
+    b.end_region();
     // Residual SE (x + x g) then the top-down nearest x2 upsample-add, deepest first.
     std::vector<Act4> fused(4);
     fused[3] = b.gate_apply("model.neck.fused.3", hid[3], gates[3], 1, nullptr, 1);
@@ -538,7 +554,9 @@ std::vector<Act4> rep_lk_fpn(Builder& b, const std::vector<Act4>& stages, int ne
         fused[i] = b.gate_apply("model.neck.fused." + std::to_string(i), hid[i], gates[i], 1, &fused[i + 1], 2);
     std::vector<Act4> feats(4);
     const int pad = kernel / 2;
+    b.begin_region();
     for (int i = 0; i < 4; ++i) {
+        b.lane(i == 0 ? 0 : 1);
         const std::string p = "model.neck.input_conv." + std::to_string(i);
         Act4 d = b.dwconv(p + ".dw", r.conv(p + ".depthwise_convolution", neck, 1, kernel, kernel, true), fused[i], 1, 1, pad, pad,
                           pad, pad, ACT_NONE, true);
@@ -549,6 +567,7 @@ std::vector<Act4> rep_lk_fpn(Builder& b, const std::vector<Act4>& stages, int ne
                           r.conv(p + ".squeeze_excitation_module.conv2", neck / 4, neck / 16, 1, 1, true), 0.2f);
         feats[i] = b.gate_apply(p + ".out", pw, g, 1, nullptr, 1);
     }
+    b.end_region();
     return feats;
 }
 
