@@ -357,7 +357,9 @@ public:
     }
 
     // Fused LCNet channel pair (rowgemm.cu) where its register tile fits.
-    bool pair_rows_ok(int c_in, int c_out) const { return !tensor_core_f32() && pair_rows_supported(c_in, c_out); }
+    // The fused SIMT pair serves the CUDA-core mode only: with tcgen05 GEMMs
+    // (BF16, FP32_TC) the pair runs as two tensor-core GEMMs.
+    bool pair_rows_ok(int c_in, int c_out) const { return !tc_ && pair_rows_supported(c_in, c_out); }
 
     Act4 pair(const std::string& name, const ConvWeight& pw1, const ConvWeight& pw2, const Act4& x, int gate, bool residual) {
         const int c = pw1.cin, h = pw1.cout, co = pw2.cout;
