@@ -214,7 +214,7 @@ public:
         // stem and neck convs were re-associated, so those keep the tap-major
         // order.
         const bool tcconv = tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
-        p.halo_order = any_order ? 0 : 1;
+        p.halo_order = any_order ? 2 : 1;
         const bool halo = !tcconv && m_.dtype == DT_F32 && conv_halo_supported(p);
         const bool gemm = !tcconv && !halo && m_.dtype == DT_BF16 && conv_gemm_supported(p);
         // The NCHW image input has 3 channels: one thread covers up to 64 output

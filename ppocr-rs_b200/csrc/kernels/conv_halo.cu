@@ -27,6 +27,9 @@
 // with the number of quads plus the products per quad, not with their
 // product); then the bias, activation and residual are applied.  With one
 // input quad (the 3-channel image) this is the plain (ky, kx, channel) sum.
+// Plain (halo_order = 2): one running sum in (quad, ky, kx, channel) order,
+// for convs whose rounding is not amplified downstream (fewer registers than
+// blocked, so more pixels per thread).
 // Tap-major (ConvParams::halo_order = 1): a stage holds the tile's input for
 // every quad and each output is one running sum in (ky, kx, channel) order,
 // exactly the direct kernel's, for convs whose rounding must not change.
@@ -46,6 +49,13 @@ namespace ppocr {
 namespace {
 
 constexpr int kThreads = 256;
+// Summation orders (ConvParams::halo_order): per-quad partial sums, the direct
+// kernel's tap-major order, or one running sum quad by quad.
+constexpr int kBlocked = 0, kTapMajor = 1, kPlain = 2;
+// The sums stay in registers: one running sum holds up to 48 per thread (64
+// spilled under the two-blocks-per-SM register cap), partial plus running
+// sums 2 x 32.
+constexpr bool halo_fits(bool single, int tm, int tn) { return single ? tm * tn <= 48 : 2 * tm * tn <= 64; }
 constexpr size_t kSmemLimit = 200 * 1024;
 
 struct HaloArgs {
@@ -78,7 +88,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 __device__ __forceinline__ float4 quad_at(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float4 quad_at(const __nv_bfloat16* p) { return load4(p); }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, bool TAPQ>
+template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, int MODE>
 __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, HaloArgs a) {
     constexpr int TAPS = KH * KW;
     extern __shared__ float4 hsm[];
@@ -87,6 +97,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
     const int wy = warp % a.ty, g = warp / a.ty;
     // Blocked mode: one step per input quad.  Tap-major mode: one step per tile,
     // every quad of the tile resident in the stage.
+    constexpr bool TAPQ = MODE == kTapMajor;
     const int steps_per_tile = TAPQ ? 1 : a.quads;
     int my_tiles = 0;
     if ((int)blockIdx.x < a.total) my_tiles = (a.total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
@@ -248,11 +259,21 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
                 }
             }
         } else {
-        float part[TM][TN];
+        // Blocked: this quad's products go to a fresh partial sum, added to the
+        // running sum below.  Plain: straight into the running sum.
+        constexpr int PM = MODE == kBlocked ? TM : 1, PN = MODE == kBlocked ? TN : 2;
+        float part[PM][PN];
+        if constexpr (MODE == kBlocked) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i)
+            for (int i = 0; i < TM; ++i)
 #pragma unroll
-            for (int j = 0; j < TN; ++j) part[i][j] = 0.f;
+                for (int j = 0; j < TN; ++j) part[i][j] = 0.f;
+        } else if (q == 0) {
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+        }
 #pragma unroll
         for (int ky = 0; ky < KH; ++ky) {
             const T* hrow = halo + (size_t)((wy * SH + ky) * a.iw) * 4;
@@ -277,16 +298,21 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
 #pragma unroll
                     for (int i = 0; i < TM; ++i) {
                         const float x = c == 0 ? av[i].x : c == 1 ? av[i].y : c == 2 ? av[i].z : av[i].w;
+                        float* d;
+                        if constexpr (MODE == kBlocked) d = part[i];
+                        else d = acc[i];
 #pragma unroll
-                        for (int j = 0; j < TN; j += 2) fma2(part[i][j], part[i][j + 1], x, x, b[j], b[j + 1]);
+                        for (int j = 0; j < TN; j += 2) fma2(d[j], d[j + 1], x, x, b[j], b[j + 1]);
                     }
                 }
             }
         }
+        if constexpr (MODE == kBlocked) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i)
+            for (int i = 0; i < TM; ++i)
 #pragma unroll
-            for (int j = 0; j < TN; ++j) acc[i][j] = q == 0 ? part[i][j] : acc[i][j] + part[i][j];
+                for (int j = 0; j < TN; ++j) acc[i][j] = q == 0 ? part[i][j] : acc[i][j] + part[i][j];
+        }
         }
         if (q == steps_per_tile - 1) {
             const int tile = (int)blockIdx.x + (step / steps_per_tile) * (int)gridDim.x;
@@ -348,7 +374,7 @@ inline HaloPlan plan_halo(const ConvParams& p, int elem_bytes) {
     const bool tapq = halo_tapq(p);
     const bool nchw = p.src[0].mode == SRC_NCHW_F32;
     const int stage_quads = tapq ? p.cin / 4 : 1;
-    const bool single = tapq || nchw;   // one running sum, no partial sums
+    const bool single = tapq || nchw || p.halo_order == kPlain;   // one running sum, no partial sums
     const int bn = halo_bn(p.cout);
     HaloPlan best;
     long long best_key[4] = {0, 0, 0, 0};
@@ -358,7 +384,7 @@ inline HaloPlan plan_halo(const ConvParams& p, int elem_bytes) {
         if (groups > 8 || 8 % groups) continue;
         const int ty = 8 / groups;
         for (int tm = 4; tm >= 1; --tm) {
-            if ((single ? 1 : 2) * tm * tn > 64) continue;   // the sums stay in registers
+            if (!halo_fits(single, tm, tn)) continue;
             HaloArgs a{};
             a.groups = groups; a.ty = ty; a.tw = 32 * tm;
             a.ih = (ty - 1) * p.sh + p.kh;
@@ -395,9 +421,9 @@ inline HaloPlan plan_halo(const ConvParams& p, int elem_bytes) {
     return best;
 }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, bool TAPQ>
+template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, bool NCHW, int MODE>
 cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream_t stream) {
-    auto kernel = conv_halo_kernel<T, KH, KW, SH, SW, TN, TM, NST, NCHW, TAPQ>;
+    auto kernel = conv_halo_kernel<T, KH, KW, SH, SW, TN, TM, NST, NCHW, MODE>;
     static std::atomic<int> regs{0};
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
@@ -427,11 +453,11 @@ cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream
     return cudaGetLastError();
 }
 
-template <typename T, int KH, int KW, int SH, int SW, int TN, bool NCHW, bool TAPQ>
+template <typename T, int KH, int KW, int SH, int SW, int TN, bool NCHW, int MODE>
 cudaError_t launch_tm(const ConvParams& p, const HaloPlan& pl, cudaStream_t stream) {
 #define HALO_TM(TM_, NST_)                                                                                   \
-    if constexpr ((TAPQ || NCHW ? 1 : 2) * TM_ * TN <= 64)                                                     \
-        if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW, TAPQ>(p, pl.a, pl.smem, stream);
+    if constexpr (halo_fits(MODE != kBlocked || NCHW, TM_, TN))                                                 \
+        if (pl.tm == TM_ && pl.nst == NST_) return launch_halo<T, KH, KW, SH, SW, TN, TM_, NST_, NCHW, MODE>(p, pl.a, pl.smem, stream);
     HALO_TM(4, 3) HALO_TM(4, 2) HALO_TM(3, 3) HALO_TM(3, 2) HALO_TM(2, 3) HALO_TM(2, 2) HALO_TM(1, 3) HALO_TM(1, 2)
 #undef HALO_TM
     return cudaErrorInvalidConfiguration;
@@ -459,11 +485,16 @@ cudaError_t launch_tn(const ConvParams& p, cudaStream_t stream) {
     a.total = (int)total;
     a.inv_iw = 1.0f / (float)a.iw;
     if (a.total == 0) return cudaSuccess;
-    if (!NCHW && halo_tapq(p))
-        return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, true>(p, pl, stream)
-                        : launch_tm<T, KH, KW, SH, SW, 8, NCHW, true>(p, pl, stream);
-    return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, false>(p, pl, stream)
-                    : launch_tm<T, KH, KW, SH, SW, 8, NCHW, false>(p, pl, stream);
+    if constexpr (!NCHW) {
+        if (halo_tapq(p))
+            return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, kTapMajor>(p, pl, stream)
+                            : launch_tm<T, KH, KW, SH, SW, 8, NCHW, kTapMajor>(p, pl, stream);
+        if (p.halo_order == kPlain)
+            return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, kPlain>(p, pl, stream)
+                            : launch_tm<T, KH, KW, SH, SW, 8, NCHW, kPlain>(p, pl, stream);
+    }
+    return tn == 16 ? launch_tm<T, KH, KW, SH, SW, 16, NCHW, kBlocked>(p, pl, stream)
+                    : launch_tm<T, KH, KW, SH, SW, 8, NCHW, kBlocked>(p, pl, stream);
 }
 
 template <typename T>

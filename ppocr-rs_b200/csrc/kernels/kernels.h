@@ -57,7 +57,8 @@ struct ConvParams {
     const void* w_tc = nullptr;           // tcgen05 conv: BF16 [tc_n_pad][kh*kw*tc_cin_pad] (or null)
     int tc_n_pad = 0, tc_cin_pad = 0;
     int halo = 0;                         // 1: `weight` is the halo-tiled layout [ceil(cin/4)][kh*kw][4][conv_halo_bn(cout)]
-    int halo_order = 0;                   // halo kernel: 0 blocked per-quad sums, 1 the direct kernel's (tap, channel) order
+    int halo_order = 0;                   // halo kernel: 0 blocked per-quad sums, 1 the direct kernel's (tap, channel) order,
+                                          // 2 one running sum quad by quad
     const float* bias = nullptr;          // [cout] (padded to conv_halo_bn(cout) for the halo kernel)
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
