@@ -237,6 +237,19 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used);
 
+/* Diagnostic (new): one depthwise convolution (the models' LCNet token convs,
+ * RepLkFpn / rank-one depthwise, recognizer head convs) through one chosen
+ * kernel: kernel 0 = the models' dispatch, 1 = the tiled kernel (every
+ * geometry), 2 = the rolling-row kernel (3x3 only).  x is NHWC [n, hi, wi, c],
+ * w is [c][kh * kw], bias (may be NULL) [c], residual (may be NULL) and out
+ * NHWC [n, ho, wo, c] with ho = (hi + pt + pb - kh) / sh + 1 and wo likewise.
+ * act as for ppocr_selftest_gemm_ex.  bf16 = 1 runs the BF16 mode: x and
+ * residual are rounded to BF16 and out holds the BF16 results widened to F32.
+ * c must be a multiple of 4 (8 with bf16).  kernel_used returns 1 or 2. */
+int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, int kw, int sh, int sw, int pt, int pl,
+                          int pb, int pr, const float* x, const float* w, const float* bias, int act,
+                          const float* residual, int bf16, int kernel, float* out, int* kernel_used);
+
 /* Diagnostic (new): one convolution through the tcgen05 engine of the BF16
  * and FP32-class modes.  planes 1: input rounded to BF16, BF16 weights and
  * output; planes 3: FP32 input / weights split into three BF16 pieces each,

@@ -963,6 +963,75 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
     });
 }
 
+int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, int kw, int sh, int sw, int pt, int pl,
+                          int pb, int pr, const float* x, const float* w, const float* bias, int act,
+                          const float* residual, int bf16, int kernel, float* out, int* kernel_used) {
+    return guard([&] {
+        if (!gpu || !x || !w || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (n <= 0 || hi <= 0 || wi <= 0 || c <= 0 || c % (bf16 ? 8 : 4) || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
+            pt < 0 || pl < 0 || pb < 0 || pr < 0)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: depthwise shape");
+        if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
+        if (kernel < 0 || kernel > 2) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..2");
+        const int ho = (hi + pt + pb - kh) / sh + 1, wo = (wi + pl + pr - kw) / sw + 1;
+        if (hi + pt + pb < kh || wi + pl + pr < kw) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel larger than the padded input");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        ConvWeight cw;
+        cw.cout = c; cw.cin = 1; cw.kh = kh; cw.kw = kw;
+        cw.w.assign(w, w + (size_t)c * kh * kw);
+        const size_t in_elems = (size_t)n * hi * wi * c, out_elems = (size_t)n * ho * wo * c;
+        WeightBlob blob;
+        const size_t wf = blob.add_f32(pack_depthwise(cw));
+        const size_t bo = blob.add_f32(bias ? std::vector<float>(bias, bias + c) : std::vector<float>(c, 0.f));
+        const std::vector<float> xin(x, x + in_elems);
+        const size_t xo = bf16 ? blob.add_bf16(xin) : blob.add_f32(xin);
+        size_t ro = 0;
+        if (residual) {
+            const std::vector<float> rin(residual, residual + out_elems);
+            ro = bf16 ? blob.add_bf16(rin) : blob.add_f32(rin);
+        }
+        const size_t oo = blob.add_f32(std::vector<float>(out_elems, 0.f));   // room for either type
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        DwParams p;
+        p.n = n; p.hi = hi; p.wi = wi; p.c = c; p.in_cstride = c; p.in_coff = 0;
+        p.ho = ho; p.wo = wo; p.kh = kh; p.kw = kw; p.sh = sh; p.sw = sw; p.pt = pt; p.pl = pl;
+        p.act = act; p.dtype = bf16 ? DT_BF16 : DT_F32;
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate depthwise test buffers");
+        p.in = d + xo;
+        p.weight = reinterpret_cast<const float*>(d + wf);
+        p.bias = bias ? reinterpret_cast<const float*>(d + bo) : nullptr;
+        p.residual = residual ? d + ro : nullptr;
+        p.out = d + oo;
+        const int used = kernel != 0 ? kernel : (kh == 3 && kw == 3 ? 2 : 1);
+        std::vector<uint16_t> ob(bf16 ? out_elems : 0);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
+        if (e == cudaSuccess) e = launch_dwconv_kernel(p, gpu->stream, kernel);
+        if (e == cudaSuccess)
+            e = bf16 ? cudaMemcpyAsync(ob.data(), p.out, out_elems * 2, cudaMemcpyDeviceToHost, gpu->stream)
+                     : cudaMemcpyAsync(out, p.out, out_elems * 4, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        if (e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the chosen depthwise kernel does not support this shape");
+        cuda_check(e, "depthwise self-test");
+        for (size_t i = 0; i < ob.size(); ++i) {
+            const uint32_t u = (uint32_t)ob[i] << 16;
+            std::memcpy(out + i, &u, 4);
+        }
+        if (kernel_used) *kernel_used = used;
+    });
+}
+
 int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used) {

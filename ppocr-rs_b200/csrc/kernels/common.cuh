@@ -115,11 +115,11 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 // (bf16) access.  Callers guarantee 4-element alignment.
 __device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
-    uint2 u = *reinterpret_cast<const uint2*>(p);
-    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&u.x);
-    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&u.y);
-    float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
-    return make_float4(fa.x, fa.y, fb.x, fb.y);
+    // A BF16 value is the upper half of the FP32 with the same value: widening
+    // is a shift (even channel, low half) or a mask (odd channel, high half).
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
 }
 __device__ __forceinline__ void store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 __device__ __forceinline__ void store4(__nv_bfloat16* p, float4 v) {

@@ -47,6 +47,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                  "l"(src), "r"(valid ? 16 : 0)
                  : "memory");
 }
+__device__ __forceinline__ void cp_async16_u32(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -62,7 +65,10 @@ __device__ __forceinline__ float4 to4(const __nv_bfloat16* p) { return load4(p);
 // from an integer, far outside its rounding error, so the floor is exact.
 __device__ __forceinline__ int div_small(int i, float inv_d) { return (int)(((float)i + 0.5f) * inv_d); }
 
-template <typename T, int CG, int KH, int KW, int SH, int SW>
+// PLAIN: no activation and no residual, so the epilogue is the bias add and
+// the store (the per-element activation switch is a large share of the
+// instructions of a depthwise conv).
+template <typename T, int CG, int KH, int KW, int SH, int SW, bool PLAIN>
 __global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, DwGeom g) {
     constexpr int QPC = 16 / (4 * sizeof(T));          // channel quads per 16-byte copy
     constexpr int CPP = CG / QPC;                      // 16-byte copies per pixel
@@ -146,9 +152,12 @@ __global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, DwGe
             for (int r = 0; r < kRun; ++r) {
                 const int ox = ox0 + tx0 + r;
                 if (ox >= p.wo) break;
-                float4 v = f4_act(f4_add(acc[r], bias), p.act);
+                float4 v = f4_add(acc[r], bias);
                 const size_t o = ((size_t)(img * p.ho + oy) * p.wo + ox) * p.c + c;
-                if (p.residual) v = f4_add(v, load4(static_cast<const T*>(p.residual) + o));
+                if constexpr (!PLAIN) {
+                    v = f4_act(v, p.act);
+                    if (p.residual) v = f4_add(v, load4(static_cast<const T*>(p.residual) + o));
+                }
                 store4(static_cast<T*>(p.out) + o, v);
             }
         }
@@ -158,6 +167,24 @@ __global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, DwGe
 }
 
 constexpr size_t kSmemLimit = 200 * 1024;
+
+// Resident blocks per SM from a kernel's registers (queried once per kernel)
+// and a launch's threads and shared memory: the occupancy API is far too slow
+// to call for every tile shape the recognizer's varying widths produce.
+inline int resident_blocks(int nregs, int threads, size_t smem) {
+    int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 65536, threads_sm = 2048;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+    const int warps = (threads + 31) / 32;
+    const int warp_regs = (nregs + 7) / 8 * 8 * 32;   // registers are allocated per warp in 256-register units
+    int blocks = threads_sm / (warps * 32);
+    blocks = std::min(blocks, regs_sm / (warp_regs * warps));
+    blocks = std::min(blocks, (int)(smem_sm / (smem + (size_t)reserved)));
+    return blocks < 1 ? 1 : blocks;
+}
 
 // Splits the output into tiles of about th0 x tw0 outputs that divide it
 // evenly, then fits the double-buffered input tile into shared memory.
@@ -194,10 +221,249 @@ cudaError_t launch_tiled(const DwParams& p, cudaStream_t stream) {
     if (g.total < 0 || smem > kSmemLimit || g.ih * g.iw >= (1 << 14) || g.iw >= (1 << 10) || g.runs >= (1 << 10))
         return cudaErrorInvalidConfiguration;
     if (g.total == 0) return cudaSuccess;
-    auto kernel = dwconv_tiled_kernel<T, CG, KH, KW, SH, SW>;
-    // Resident blocks per SM, from the kernel's registers (queried once) and
-    // this launch's shared memory: the occupancy API is far too slow to call
-    // for every tile shape the recognizer's varying widths produce.
+    const bool plain = p.act == ACT_NONE && !p.residual;
+    auto kernel = plain ? dwconv_tiled_kernel<T, CG, KH, KW, SH, SW, true> : dwconv_tiled_kernel<T, CG, KH, KW, SH, SW, false>;
+    static std::atomic<int> regs_by_plain[2] = {0, 0};   // each kernel's registers, queried once
+    std::atomic<int>& regs = regs_by_plain[plain ? 1 : 0];
+    int nregs = regs.load(std::memory_order_acquire);
+    if (!nregs) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        if (e != cudaSuccess) return e;
+        cudaFuncAttributes fa{};
+        e = cudaFuncGetAttributes(&fa, kernel);
+        if (e != cudaSuccess) return e;
+        nregs = fa.numRegs > 0 ? fa.numRegs : 1;
+        regs.store(nregs, std::memory_order_release);
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long cap = (long long)sms * resident_blocks(nregs, kThreads, smem);
+    const int grid = (int)(g.total < cap ? g.total : cap);
+    kernel<<<grid, kThreads, smem, stream>>>(p, g);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// 3x3 depthwise conv over rolling rows.
+//
+// A unit is one image x one segment of bh output rows x one band of bw output
+// columns x one channel group of CG quads (units numbered with the group
+// fastest, so blocks running side by side read all channels of the same
+// pixels).  Each thread owns one channel quad and RUN adjacent output columns
+// of the band and walks down the segment's input rows: each input row is read
+// from shared memory once and feeds every output row it belongs to (three at
+// stride 1, up to two at stride 2), whose partial sums stay in registers until
+// their last tap.  The taps of each output are still summed in (ky, kx) order,
+// so the results are bit-identical to the tiled kernel's.  Input rows arrive
+// through an NR-slot cp.async ring, NR - 1 rows ahead and continuous across a
+// persistent block's units; a unit's weights and bias ride with its first row
+// (the weights are read from shared memory by broadcast, which leaves the
+// registers to the three rows of partial sums).
+// ---------------------------------------------------------------------------
+struct DwBand {
+    int bw, bh, sx, iw;          // outputs per band row, output rows per segment, runs per band, input columns per row
+    int bands, segs, groups;     // units: ((img * segs + seg) * bands + bx) * groups + grp
+    int ni, total;               // input rows per segment, units
+};
+
+constexpr int kBandRun = 4;
+
+__device__ __forceinline__ void band_decode(const DwBand& g, int u, int& img, int& seg, int& bx, int& grp) {
+    grp = u % g.groups;
+    int r = u / g.groups;
+    bx = r % g.bands;
+    r /= g.bands;
+    seg = r % g.segs;
+    img = r / g.segs;
+}
+
+// Positive remainder and floor division for the static set bookkeeping.
+__host__ __device__ constexpr int pmod(int a, int m) { return ((a % m) + m) % m; }
+__host__ __device__ constexpr int fdiv(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+// PLAIN: no activation and no residual (the token convs), so the epilogue is
+// the bias add and the store.
+template <typename T, int CG, int SH, int SW, int NR, bool PLAIN>
+__global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand g) {
+    constexpr int RUN = kBandRun;
+    constexpr int D = NR - 1;                  // rows in flight ahead of the one being computed
+    constexpr int QPC = 16 / (4 * sizeof(T));  // channel quads per 16-byte copy
+    constexpr int CPP = CG / QPC;              // 16-byte copies per pixel
+    constexpr int SPAN = (RUN - 1) * SW + 3;   // window columns of one run
+    constexpr int NS = SH == 1 ? 3 : 2;        // output rows whose sums are in flight
+    constexpr int U = SH == 1 ? 3 : 4;         // steps per unrolled group: set indices stay static
+    constexpr int WQ = 10 * CG;                // float4 per weight slot: 9 taps + bias
+    extern __shared__ float4 sm4[];
+    float4* const wslot = sm4;                                  // [2][10][CG]
+    T* const ring = reinterpret_cast<T*>(sm4 + 2 * WQ);         // [NR][iw][CG * 4]
+    const int row_elems = g.iw * CG * 4;
+    const int nt = blockDim.x, tid = threadIdx.x;
+    if ((int)blockIdx.x >= g.total) return;
+
+    // Issue side: the next row to copy is row `it` of unit `iu` (this block's
+    // ik-th unit).  Thread tid copies the 16-byte chunk cq of pixels p0,
+    // p0 + pstep, ... of each row, so its source and destination addresses
+    // advance by fixed steps and only the row start changes per row.
+    const int cq = tid % CPP, p0 = tid / CPP, pstep = nt / CPP;
+    const size_t row_pitch = (size_t)p.wi * p.in_cstride;           // elements between input rows
+    const size_t src_step = (size_t)pstep * p.in_cstride;
+    const uint32_t dst_step = (uint32_t)(pstep * CG * 4 * sizeof(T));
+    const uint32_t ring_u32 = (uint32_t)__cvta_generic_to_shared(ring) + (uint32_t)((p0 * CG + cq * QPC) * 4 * sizeof(T));
+    const T* const in_base = static_cast<const T*>(p.in) + p.in_coff + cq * QPC * 4;
+    int iu = blockIdx.x, it = 0, ik = 0, islot = 0;
+    int i_y0 = 0, i_x0 = 0, i_grp = 0;   // unit's first input row, this thread's first column, channel group
+    const T* i_img = nullptr;            // unit's image at this thread's channels
+    auto start_unit = [&]() {
+        int img, seg, bx;
+        band_decode(g, iu, img, seg, bx, i_grp);
+        i_y0 = seg * g.bh * SH - p.pt;
+        i_x0 = bx * g.bw * SW - p.pl + p0;
+        i_img = in_base + (size_t)img * p.hi * row_pitch + i_grp * CG * 4;
+    };
+    start_unit();
+    auto issue_row = [&]() {
+        if (iu < g.total) {
+            const int y = i_y0 + it;
+            if (y >= 0 && y < p.hi) {
+                const T* src = i_img + (size_t)y * row_pitch + (ptrdiff_t)i_x0 * p.in_cstride;
+                uint32_t dst = ring_u32 + (uint32_t)(islot * row_elems * sizeof(T));
+                for (int pix = p0, x = i_x0; pix < g.iw; pix += pstep, x += pstep, src += src_step, dst += dst_step) {
+                    const bool ok = (unsigned)x < (unsigned)p.wi;
+                    cp_async16_u32(dst, ok ? src : i_img, ok);
+                }
+            } else {   // a padding row: zero-fill
+                uint32_t dst = ring_u32 + (uint32_t)(islot * row_elems * sizeof(T));
+                for (int pix = p0; pix < g.iw; pix += pstep, dst += dst_step) cp_async16_u32(dst, i_img, false);
+            }
+            if (it == 0) {
+                float4* wd = wslot + (ik & 1) * WQ;
+                const int c0 = i_grp * CG * 4;
+                for (int i = tid; i < WQ; i += nt) {
+                    const int t = i / CG, q = i - t * CG;
+                    if (t < 9) cp_async16(wd + i, p.weight + (size_t)t * p.c + c0 + q * 4, true);
+                    else cp_async16(wd + i, p.bias ? p.bias + c0 + q * 4 : p.weight, p.bias != nullptr);
+                }
+            }
+            if (++it == g.ni) {
+                it = 0;
+                ++ik;
+                iu += gridDim.x;
+                if (iu < g.total) start_unit();
+            }
+        }
+        cp_async_commit();   // one group per row, empty past the last unit
+        islot = islot == NR - 1 ? 0 : islot + 1;
+    };
+
+    for (int k = 0; k < D; ++k) issue_row();
+
+    const int q = tid % CG, rx = tid / CG;
+    const bool active = rx < g.sx;
+    int cslot = 0, kord = 0;
+    for (int u = blockIdx.x; u < g.total; u += gridDim.x, ++kord) {
+        int img, seg, bx, grp;
+        band_decode(g, u, img, seg, bx, grp);
+        const int oy0 = seg * g.bh, ox0 = bx * g.bw + rx * RUN;
+        const int rows = min(g.bh, p.ho - oy0);
+        const int c = grp * CG * 4 + q * 4;
+        const size_t obase = ((size_t)img * p.ho + oy0) * p.wo * p.c + c;   // + (j * wo + ox) * c
+        float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4* const w = wslot + (kord & 1) * WQ + q;   // [tap * CG]: broadcast reads
+        float4 acc[NS][RUN];
+#pragma unroll
+        for (int s = 0; s < NS; ++s)
+#pragma unroll
+            for (int r = 0; r < RUN; ++r) acc[s][r] = bias;
+        for (int t0 = 0; t0 < g.ni; t0 += U) {
+#pragma unroll
+            for (int r = 0; r < U; ++r) {
+                const int t = t0 + r;
+                if (t >= g.ni) break;   // block-uniform
+                cp_async_wait<D - 1>();  // row t (and, at t == 0, the unit's weights) has landed
+                __syncthreads();         // ... for every thread; the slot of row t - 1 is free
+                issue_row();
+                if (r == 0 && t0 == 0) bias = w[9 * CG];
+                if (active) {
+                    const T* row = ring + cslot * row_elems + (rx * RUN * SW * CG + q) * 4;
+                    float4 win[SPAN];
+#pragma unroll
+                    for (int i = 0; i < SPAN; ++i) win[i] = to4(row + i * CG * 4);
+#pragma unroll
+                    for (int ky = 2; ky >= 0; --ky) {
+                        if (pmod(r - ky, SH) != 0) continue;          // static: row t is not tap row ky of any output
+                        const int j = (t - ky) / SH;                   // output row (in the segment) this tap row feeds
+                        if (t < ky || j >= rows) continue;
+                        float4* a = acc[pmod(fdiv(r - ky, SH), NS)];
+                        if (ky == 0) {
+#pragma unroll
+                            for (int rr = 0; rr < RUN; ++rr) a[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int kx = 0; kx < 3; ++kx) {
+                            const float4 wv = w[(ky * 3 + kx) * CG];
+#pragma unroll
+                            for (int rr = 0; rr < RUN; ++rr) a[rr] = f4_vfma(win[rr * SW + kx], wv, a[rr]);
+                        }
+                        if (ky == 2) {   // output row j is complete
+                            const size_t orow = obase + ((size_t)j * p.wo + ox0) * p.c;
+                            T* o = static_cast<T*>(p.out) + orow;
+#pragma unroll
+                            for (int rr = 0; rr < RUN; ++rr) {
+                                if (ox0 + rr >= p.wo) break;
+                                float4 v = f4_add(a[rr], bias);
+                                if constexpr (!PLAIN) {
+                                    v = f4_act(v, p.act);
+                                    if (p.residual)
+                                        v = f4_add(v, load4(static_cast<const T*>(p.residual) + orow + (size_t)rr * p.c));
+                                }
+                                store4(o + (size_t)rr * p.c, v);
+                            }
+                        }
+                    }
+                }
+                cslot = cslot == NR - 1 ? 0 : cslot + 1;
+            }
+        }
+    }
+    cp_async_wait<0>();
+}
+
+// Units, bands and the ring depth for one launch.  Bands are at most 32 runs
+// (128 outputs) wide so a block is at most 8 quads x 32 runs = 256 threads;
+// tall maps are cut into segments of at least 8 rows until there are a few
+// units per resident block.
+template <typename T, int CG, int SH, int SW>
+DwBand band_geometry(const DwParams& p, int resident) {
+    DwBand g{};
+    const int runs = (p.wo + kBandRun - 1) / kBandRun;
+    const int sx_max = 256 / CG < 32 ? 256 / CG : 32;
+    g.bands = (runs + sx_max - 1) / sx_max;
+    g.sx = (runs + g.bands - 1) / g.bands;
+    g.bw = g.sx * kBandRun;
+    g.iw = (g.bw - 1) * SW + 3;
+    g.groups = p.c / (4 * CG);
+    const long long base = (long long)p.n * g.groups * g.bands;
+    const long long want = 4LL * resident;
+    int segs = 1;
+    if (base < want) {
+        const long long need = (want + base - 1) / base;
+        const int max_segs = (p.ho + 7) / 8;
+        segs = (int)(need < max_segs ? need : max_segs);
+        if (segs < 1) segs = 1;
+    }
+    g.bh = (p.ho + segs - 1) / segs;
+    g.segs = (p.ho + g.bh - 1) / g.bh;
+    g.ni = (g.bh - 1) * SH + 3;
+    const long long total = base * g.segs;
+    g.total = total > 0x7fffffffLL ? -1 : (int)total;
+    return g;
+}
+
+template <typename T, int CG, int SH, int SW, int NR, bool PLAIN>
+cudaError_t launch_band_nr(const DwParams& p, const DwBand& g, int nt, cudaStream_t stream) {
+    auto kernel = dwconv_band_kernel<T, CG, SH, SW, NR, PLAIN>;
+    const size_t smem = 2 * 10 * CG * sizeof(float4) + (size_t)NR * g.iw * CG * 4 * sizeof(T);
     static std::atomic<int> regs{0};
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
@@ -209,22 +475,46 @@ cudaError_t launch_tiled(const DwParams& p, cudaStream_t stream) {
         nregs = fa.numRegs > 0 ? fa.numRegs : 1;
         regs.store(nregs, std::memory_order_release);
     }
-    int dev = 0, sms = 148, smem_sm = 0, reserved = 0, regs_sm = 65536, threads_sm = 2048;
+    if (smem > kSmemLimit) return cudaErrorInvalidConfiguration;
+    const int blocks_per_sm = resident_blocks(nregs, nt, smem);
+    int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
-    cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
-    cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
-    const int warp_regs = (nregs + 7) / 8 * 8 * 32;   // registers are allocated per warp in 256-register units
-    int blocks_per_sm = threads_sm / kThreads;
-    blocks_per_sm = std::min(blocks_per_sm, regs_sm / (warp_regs * (kThreads / 32)));
-    blocks_per_sm = std::min(blocks_per_sm, (int)(smem_sm / (smem + (size_t)reserved)));
-    if (blocks_per_sm < 1) blocks_per_sm = 1;
     const long long cap = (long long)sms * blocks_per_sm;
     const int grid = (int)(g.total < cap ? g.total : cap);
-    kernel<<<grid, kThreads, smem, stream>>>(p, g);
+    kernel<<<grid, nt, smem, stream>>>(p, g);
     return cudaGetLastError();
+}
+
+template <typename T, int CG, int SH, int SW>
+cudaError_t launch_band(const DwParams& p, cudaStream_t stream) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const DwBand g = band_geometry<T, CG, SH, SW>(p, 2 * sms);
+    if (g.total < 0) return cudaErrorInvalidConfiguration;
+    if (g.total == 0) return cudaSuccess;
+    const int nt = (CG * g.sx + 31) / 32 * 32;
+    const size_t row_bytes = (size_t)g.iw * CG * 4 * sizeof(T);
+    // The weight slot of a block's unit k + 2 is refilled D rows before that
+    // unit starts while unit k still reads its own: a unit must span at least
+    // D rows.
+    const bool plain = p.act == ACT_NONE && !p.residual;
+    if (row_bytes <= 6 * 1024 && g.ni >= 7)
+        return plain ? launch_band_nr<T, CG, SH, SW, 8, true>(p, g, nt, stream)
+                     : launch_band_nr<T, CG, SH, SW, 8, false>(p, g, nt, stream);
+    return plain ? launch_band_nr<T, CG, SH, SW, 4, true>(p, g, nt, stream)
+                 : launch_band_nr<T, CG, SH, SW, 4, false>(p, g, nt, stream);
+}
+
+template <typename T, int SH, int SW>
+cudaError_t launch_band_cg(const DwParams& p, cudaStream_t stream) {
+    const int quads = p.c / 4;
+    if (quads % 8 == 0) return launch_band<T, 8, SH, SW>(p, stream);
+    if (quads % 4 == 0) return launch_band<T, 4, SH, SW>(p, stream);
+    if (quads % 2 == 0) return launch_band<T, 2, SH, SW>(p, stream);
+    if constexpr (sizeof(T) == 4) return launch_band<T, 1, SH, SW>(p, stream);
+    return cudaErrorInvalidValue;
 }
 
 template <typename T, int KH, int KW, int SH, int SW>
@@ -240,14 +530,18 @@ cudaError_t launch_cg(const DwParams& p, cudaStream_t stream) {
 
 // The geometries of the PP-OCRv6 graphs: 3x3 at strides (1,1), (2,2), (2,1);
 // square 5x5 / 7x7 / 9x9 at stride 1; 1x5 / 1x7 (recognizer heads).
+// 3x3 convs run on the rolling-row kernel unless `kernel` asks for the tiled
+// one (1); every other geometry on the tiled kernel.
 template <typename T>
-cudaError_t launch_dw_t(const DwParams& p, cudaStream_t stream) {
+cudaError_t launch_dw_t(const DwParams& p, cudaStream_t stream, int kernel) {
     if (p.kh == 3 && p.kw == 3) {
-        if (p.sh == 1 && p.sw == 1) return launch_cg<T, 3, 3, 1, 1>(p, stream);
-        if (p.sh == 2 && p.sw == 2) return launch_cg<T, 3, 3, 2, 2>(p, stream);
-        if (p.sh == 2 && p.sw == 1) return launch_cg<T, 3, 3, 2, 1>(p, stream);
+        const bool band = kernel != 1;
+        if (p.sh == 1 && p.sw == 1) return band ? launch_band_cg<T, 1, 1>(p, stream) : launch_cg<T, 3, 3, 1, 1>(p, stream);
+        if (p.sh == 2 && p.sw == 2) return band ? launch_band_cg<T, 2, 2>(p, stream) : launch_cg<T, 3, 3, 2, 2>(p, stream);
+        if (p.sh == 2 && p.sw == 1) return band ? launch_band_cg<T, 2, 1>(p, stream) : launch_cg<T, 3, 3, 2, 1>(p, stream);
         return cudaErrorInvalidValue;
     }
+    if (kernel == 2) return cudaErrorInvalidValue;
     if (p.sh != 1 || p.sw != 1) return cudaErrorInvalidValue;
     if (p.kh == p.kw) {
         switch (p.kh) {
@@ -264,11 +558,14 @@ cudaError_t launch_dw_t(const DwParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-cudaError_t launch_dwconv(const DwParams& p, cudaStream_t stream) {
+cudaError_t launch_dwconv_kernel(const DwParams& p, cudaStream_t stream, int kernel) {
     if (p.c % 4 || p.in_coff % 4 || p.in_cstride % 4) return cudaErrorInvalidValue;
     // 16-byte copies: BF16 views need 8-channel alignment.
     if (p.dtype == DT_BF16 && (p.c % 8 || p.in_coff % 8 || p.in_cstride % 8)) return cudaErrorInvalidValue;
-    return p.dtype == DT_F32 ? launch_dw_t<float>(p, stream) : launch_dw_t<__nv_bfloat16>(p, stream);
+    if (kernel < 0 || kernel > 2) return cudaErrorInvalidValue;
+    return p.dtype == DT_F32 ? launch_dw_t<float>(p, stream, kernel) : launch_dw_t<__nv_bfloat16>(p, stream, kernel);
 }
+
+cudaError_t launch_dwconv(const DwParams& p, cudaStream_t stream) { return launch_dwconv_kernel(p, stream, 0); }
 
 }  // namespace ppocr

@@ -115,6 +115,8 @@ struct DwParams {
     DType dtype = DT_F32;
 };
 cudaError_t launch_dwconv(const DwParams& p, cudaStream_t stream);
+// kernel: 0 the default choice, 1 the tiled kernel, 2 the rolling-row 3x3 kernel.
+cudaError_t launch_dwconv_kernel(const DwParams& p, cudaStream_t stream, int kernel);
 
 // ---------------------------------------------------------------------------
 // Pointwise GEMM  C[m, n] = act(A[m, k] * W + bias) (+ residual)

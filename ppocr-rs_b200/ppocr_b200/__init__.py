@@ -187,6 +187,8 @@ def library() -> C.CDLL:
                                        C.POINTER(C.c_int)]),
         "ppocr_selftest_gemm_f32": (I, [P, I, I, I, FP, FP, FP, I, FP, I, FP, I, FP, C.POINTER(C.c_int)]),
         "ppocr_measure_fp32_peak": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+        "ppocr_selftest_dwconv": (I, [P, I, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, I, I, FP,
+                                      C.POINTER(C.c_int)]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_selftest_engine": (I, [P, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, FP, I, FP, C.POINTER(C.c_int),
@@ -350,6 +352,27 @@ class Gpu:
         a, b = C.c_double(), C.c_double()
         _check(library().ppocr_measure_fp32_peak(self._h, C.byref(a), C.byref(b)))
         return a.value, b.value
+
+    def selftest_dwconv(self, x, w, bias=None, stride=(1, 1), pad=(0, 0, 0, 0), act: int = 0, residual=None,
+                        bf16: bool = False, kernel: int = 0):
+        """Depthwise conv diagnostic: x NHWC [n, hi, wi, c], w [c, kh, kw], pad (top, left, bottom, right);
+        kernel 0 dispatch, 1 tiled, 2 rolling rows (3x3).  Returns (out float32 NHWC, kernel that ran)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        n, hi, wi, c = x.shape
+        kh, kw = w.shape[1], w.shape[2]
+        sh, sw = stride
+        pt, pl, pb, pr = pad
+        ho, wo = (hi + pt + pb - kh) // sh + 1, (wi + pl + pr - kw) // sw + 1
+        out = np.zeros((n, ho, wo, c), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        used = C.c_int()
+        _check(library().ppocr_selftest_dwconv(self._h, n, hi, wi, c, kh, kw, sh, sw, pt, pl, pb, pr, _fptr(x), _fptr(w),
+                                               None if b is None else _fptr(b), int(act),
+                                               None if r is None else _fptr(r), int(bool(bf16)), int(kernel),
+                                               _fptr(out), C.byref(used)))
+        return out, used.value
 
     def selftest_gemm_f32(self, a, w, bias=None, act: int = 0, gate=None, rows_per_image: int = 1, residual=None,
                           kernel: int = 0):
