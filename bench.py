@@ -257,8 +257,11 @@ def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp, r
     lines = sum(len(r["lines"]) for r in res)
     barrier()
     t0 = time.perf_counter()
+    step_ms = []
     for _ in range(steps):
+        ts = time.perf_counter()
         eng.recognize_batch(pages)
+        step_ms.append(round(1000 * (time.perf_counter() - ts), 2))
     dt = sharding.max_over_ranks(time.perf_counter() - t0)
     stages = eng.stage_times()
     eng.close()
@@ -268,7 +271,8 @@ def measure_e2e(gpu, pages_per_rank, steps, warmup, world, rank, barrier, tmp, r
         name += f", recognizer {rec_precision}"
     return {"metric": name, "value": round(value, 2), "last_call_stage_ms": {k: round(v, 2) for k, v in stages.items()},
             "unit": "pages/s", "ms_per_page": round(1000 * dt / (pages_per_rank * steps), 3),
-            "pages_per_step_per_gpu": pages_per_rank, "steps": steps, "lines_per_page": round(lines / len(pages), 1),
+            "pages_per_step_per_gpu": pages_per_rank, "steps": steps, "step_ms": step_ms,
+            "lines_per_page": round(lines / len(pages), 1),
             "api": "ppocr_engine_recognize_batch (host RGB8 pages in, JSON out)",
             "h2d_bytes_per_step": int(sum(p.size for p in pages)),
             "data": "synthetic config-5 pages, seeded random-init (spec) weights"}

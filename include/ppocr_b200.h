@@ -237,6 +237,17 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used);
 
+/* Diagnostic (new): the fused FP32 LCNet channel pair of the FP32 mode,
+ * out = W2 GELU(W1 (a * gate) + b1) + b2 (+ a * gate when residual is 1),
+ * a [m][c_in], w1 [2 c_in][c_in], w2 [c_out][2 c_in], b1 [2 c_in], b2 [c_out],
+ * gate (may be NULL) [m / rows_per_image][c_in], out [m][c_out].  The model
+ * runs it on maps of at least 98,304 pixel rows; on the same inputs it must
+ * equal two ppocr_selftest_gemm_f32 calls (GELU, then the residual) bit for
+ * bit.  (c_in, c_out) must be one of the LCNet pairs the kernel covers. */
+int ppocr_selftest_pair_f32(ppocr_gpu* gpu, int m, int c_in, int c_out, const float* a, const float* w1,
+                            const float* b1, const float* w2, const float* b2, const float* gate, int rows_per_image,
+                            int residual, float* out);
+
 /* Diagnostic (new): one depthwise convolution (the models' LCNet token convs,
  * RepLkFpn / rank-one depthwise, recognizer head convs) through one chosen
  * kernel: kernel 0 = the models' dispatch, 1 = the tiled kernel (every

@@ -963,6 +963,58 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
     });
 }
 
+int ppocr_selftest_pair_f32(ppocr_gpu* gpu, int m, int c_in, int c_out, const float* a, const float* w1,
+                            const float* b1, const float* w2, const float* b2, const float* gate, int rows_per_image,
+                            int residual, float* out) {
+    return guard([&] {
+        if (!gpu || !a || !w1 || !b1 || !w2 || !b2 || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (m <= 0 || !pair_rows_supported(c_in, c_out)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: pair shape not covered");
+        if (residual && c_out != c_in) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the residual needs c_out == c_in");
+        if (gate && (rows_per_image <= 0 || m % rows_per_image)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: rows_per_image must divide m");
+        const int h = 2 * c_in;
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        std::vector<float> w2t((size_t)h * c_out);   // [2 c_in][c_out], as the model packs it
+        for (int o = 0; o < c_out; ++o)
+            for (int j = 0; j < h; ++j) w2t[(size_t)j * c_out + o] = w2[(size_t)o * h + j];
+        WeightBlob blob;
+        const size_t o1 = blob.add_f32(std::vector<float>(w1, w1 + (size_t)h * c_in));
+        const size_t o2 = blob.add_f32(w2t);
+        const size_t ob1 = blob.add_f32(std::vector<float>(b1, b1 + h));
+        const size_t ob2 = blob.add_f32(std::vector<float>(b2, b2 + c_out));
+        const size_t ao = blob.add_f32(std::vector<float>(a, a + (size_t)m * c_in));
+        const size_t go = gate ? blob.add_f32(std::vector<float>(gate, gate + (size_t)(m / rows_per_image) * c_in)) : 0;
+        const size_t co = blob.add_f32(std::vector<float>((size_t)m * c_out, 0.f));
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate pair test buffers");
+        PairRowsParams p;
+        p.m = m; p.c_in = c_in; p.c_out = c_out; p.rows_per_image = gate ? rows_per_image : 1;
+        p.residual = residual ? 1 : 0; p.dtype = DT_F32;
+        p.a = d + ao;
+        p.gate = gate ? reinterpret_cast<const float*>(d + go) : nullptr;
+        p.w1t = reinterpret_cast<const float*>(d + o1);
+        p.w2 = reinterpret_cast<const float*>(d + o2);
+        p.b1 = reinterpret_cast<const float*>(d + ob1);
+        p.b2 = reinterpret_cast<const float*>(d + ob2);
+        p.c = d + co;
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(gpu->stream);
+        if (e == cudaSuccess) e = launch_pair_rows(p, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(out, p.c, (size_t)m * c_out * 4, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "pair self-test");
+    });
+}
+
 int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, int kw, int sh, int sw, int pt, int pl,
                           int pb, int pr, const float* x, const float* w, const float* bias, int act,
                           const float* residual, int bf16, int kernel, float* out, int* kernel_used) {

@@ -27,12 +27,14 @@ template <typename T, int C, int CO, int R>
 __global__ void __launch_bounds__(kRows) pair_rows_kernel(PairRowsParams p) {
     constexpr int H = 2 * C;
     extern __shared__ float4 psm[];
-    float* w1t = reinterpret_cast<float*>(psm);          // [H][C]   (hidden-major)
-    float* w2 = w1t + H * C;                             // [H][CO]
+    float* w1p = reinterpret_cast<float*>(psm);          // [H / 2][C][2]: hidden units 2jp, 2jp + 1 side by side
+    float* w2 = w1p + H * C;                             // [H][CO]
     float* b1 = w2 + H * CO;                             // [H]
     float* b2 = b1 + H;                                  // [CO]
-    for (int i = threadIdx.x * 4; i < H * C; i += kRows * 4)
-        *reinterpret_cast<float4*>(w1t + i) = *reinterpret_cast<const float4*>(p.w1t + i);
+    for (int i = threadIdx.x; i < H * C / 2; i += kRows) {   // i = jp * C + k
+        const int jp = i / C, k = i - jp * C;
+        *reinterpret_cast<float2*>(w1p + 2 * i) = make_float2(p.w1t[(2 * jp) * C + k], p.w1t[(2 * jp + 1) * C + k]);
+    }
     for (int i = threadIdx.x * 4; i < H * CO; i += kRows * 4)
         *reinterpret_cast<float4*>(w2 + i) = *reinterpret_cast<const float4*>(p.w2 + i);
     for (int i = threadIdx.x; i < H; i += kRows) b1[i] = p.b1[i];
@@ -58,33 +60,39 @@ __global__ void __launch_bounds__(kRows) pair_rows_kernel(PairRowsParams p) {
     for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int o = 0; o < CO; ++o) out[r][o] = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < H; ++j) {
-        const float* wj = w1t + j * C;
-        float h[R];
+    // Hidden units in pairs: each packed FMA advances the k-ordered sums of two
+    // hidden units (each lane rounded as fmaf), so every hidden value is the
+    // same chain of FMAs as one scalar sum.
+#pragma unroll 2
+    for (int jp = 0; jp < H / 2; ++jp) {
+        const float* wj = w1p + jp * C * 2;
+        float h0[R], h1[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) h[r] = 0.f;
+        for (int r = 0; r < R; ++r) h0[r] = h1[r] = 0.f;
 #pragma unroll
-        for (int k = 0; k < C; k += 4) {
-            const float4 w = *reinterpret_cast<const float4*>(wj + k);
+        for (int k = 0; k < C; k += 2) {
+            const float4 w = *reinterpret_cast<const float4*>(wj + 2 * k);   // (j, k) (j + 1, k) (j, k + 1) (j + 1, k + 1)
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                h[r] = fmaf(a[r][k], w.x, h[r]);
-                h[r] = fmaf(a[r][k + 1], w.y, h[r]);
-                h[r] = fmaf(a[r][k + 2], w.z, h[r]);
-                h[r] = fmaf(a[r][k + 3], w.w, h[r]);
+                fma2(h0[r], h1[r], a[r][k], a[r][k], w.x, w.y);
+                fma2(h0[r], h1[r], a[r][k + 1], a[r][k + 1], w.z, w.w);
             }
         }
 #pragma unroll
-        for (int r = 0; r < R; ++r) h[r] = apply_act(h[r] + b1[j], ACT_GELU);
-        const float* w2j = w2 + j * CO;
+        for (int half = 0; half < 2; ++half) {
+            const int j = 2 * jp + half;
+            float h[R];
 #pragma unroll
-        for (int o = 0; o < CO; o += 4) {
-            const float4 w = *reinterpret_cast<const float4*>(w2j + o);
+            for (int r = 0; r < R; ++r) h[r] = apply_act((half ? h1[r] : h0[r]) + b1[j], ACT_GELU);
+            const float* w2j = w2 + j * CO;
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                fma2(out[r][o], out[r][o + 1], h[r], h[r], w.x, w.y);
-                fma2(out[r][o + 2], out[r][o + 3], h[r], h[r], w.z, w.w);
+            for (int o = 0; o < CO; o += 4) {
+                const float4 w = *reinterpret_cast<const float4*>(w2j + o);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    fma2(out[r][o], out[r][o + 1], h[r], h[r], w.x, w.y);
+                    fma2(out[r][o + 2], out[r][o + 3], h[r], h[r], w.z, w.w);
+                }
             }
         }
     }

@@ -189,6 +189,7 @@ def library() -> C.CDLL:
         "ppocr_measure_fp32_peak": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_selftest_dwconv": (I, [P, I, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, I, I, FP,
                                       C.POINTER(C.c_int)]),
+        "ppocr_selftest_pair_f32": (I, [P, I, I, I, FP, FP, FP, FP, FP, FP, I, I, FP]),
         "ppocr_preprocess_noalloc": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_preprocess": (I, [P, P, FP, S, S, S, I, FP]),
         "ppocr_selftest_engine": (I, [P, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, FP, I, FP, C.POINTER(C.c_int),
@@ -352,6 +353,22 @@ class Gpu:
         a, b = C.c_double(), C.c_double()
         _check(library().ppocr_measure_fp32_peak(self._h, C.byref(a), C.byref(b)))
         return a.value, b.value
+
+    def selftest_pair_f32(self, a, w1, b1, w2, b2, gate=None, rows_per_image: int = 1, residual: bool = False):
+        """Fused FP32 LCNet pair: a [m, c], w1 [2c, c], w2 [c', 2c]; returns out float32 [m, c']."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        w1 = np.ascontiguousarray(w1, dtype=np.float32)
+        w2 = np.ascontiguousarray(w2, dtype=np.float32)
+        b1 = np.ascontiguousarray(b1, dtype=np.float32)
+        b2 = np.ascontiguousarray(b2, dtype=np.float32)
+        m, c = a.shape
+        co = w2.shape[0]
+        out = np.zeros((m, co), np.float32)
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        _check(library().ppocr_selftest_pair_f32(self._h, m, c, co, _fptr(a), _fptr(w1), _fptr(b1), _fptr(w2), _fptr(b2),
+                                                 None if g is None else _fptr(g), int(rows_per_image), int(bool(residual)),
+                                                 _fptr(out)))
+        return out
 
     def selftest_dwconv(self, x, w, bias=None, stride=(1, 1), pad=(0, 0, 0, 0), act: int = 0, residual=None,
                         bf16: bool = False, kernel: int = 0):

@@ -87,3 +87,31 @@ def test_dispatch_choice(gpu):
     w = rng.normal(0, 0.1, (16, 256)).astype(np.float32)
     _, used = gpu.selftest_gemm_f32(a, w, None, 0, None, 1, None, 0)
     assert used == 1   # k = 256 is past the streaming kernel's shared-memory tile
+
+
+PAIRS = [
+    # m, c, c', gated, residual, rows_per_image
+    (1000, 32, 32, True, True, 250),     # detector stage-0 pair: gated, token residual
+    (777, 32, 48, False, False, 1),      # stage transition pair (no residual)
+    (513, 48, 48, True, True, 171),
+    (300, 64, 64, False, True, 1),
+    (129, 16, 16, True, False, 43),
+]
+
+
+@pytest.mark.parametrize("m,c,co,gated,res,rpi", PAIRS)
+def test_fused_pair_matches_two_gemms(gpu, m, c, co, gated, res, rpi):
+    """The fused pair kernel (used on maps of >= 98,304 rows, which the model tests
+    never reach) equals the two-GEMM form bit for bit: the same k-ordered FMA chains."""
+    rng = np.random.default_rng(m + 17 * c + co)
+    a = rng.normal(0, 1, (m, c)).astype(np.float32)
+    w1 = rng.normal(0, 1 / np.sqrt(c), (2 * c, c)).astype(np.float32)
+    b1 = rng.normal(0, 0.1, 2 * c).astype(np.float32)
+    w2 = rng.normal(0, 1 / np.sqrt(2 * c), (co, 2 * c)).astype(np.float32)
+    b2 = rng.normal(0, 0.1, co).astype(np.float32)
+    g = rng.uniform(0, 1, (m // rpi, c)).astype(np.float32) if gated else None
+    fused = gpu.selftest_pair_f32(a, w1, b1, w2, b2, g, rpi, res)
+    h, _ = gpu.selftest_gemm_f32(a, w1, b1, 3, g, rpi, None, 1)
+    ga = (a * np.repeat(g, rpi, axis=0)).astype(np.float32) if gated else a
+    two, _ = gpu.selftest_gemm_f32(h, w2, b2, 0, None, 1, ga if res else None, 1)
+    np.testing.assert_array_equal(fused, two)
