@@ -251,7 +251,8 @@ int ppocr_selftest_pair_f32(ppocr_gpu* gpu, int m, int c_in, int c_out, const fl
 /* Diagnostic (new): one depthwise convolution (the models' LCNet token convs,
  * RepLkFpn / rank-one depthwise, recognizer head convs) through one chosen
  * kernel: kernel 0 = the models' dispatch, 1 = the tiled kernel (every
- * geometry), 2 = the rolling-row kernel (3x3 only).  x is NHWC [n, hi, wi, c],
+ * geometry), 2 = the rolling-row kernel (3x3 and 5x5; the dispatch uses it
+ * for 3x3).  x is NHWC [n, hi, wi, c],
  * w is [c][kh * kw], bias (may be NULL) [c], residual (may be NULL) and out
  * NHWC [n, ho, wo, c] with ho = (hi + pt + pb - kh) / sh + 1 and wo likewise.
  * act as for ppocr_selftest_gemm_ex.  bf16 = 1 runs the BF16 mode: x and

@@ -267,7 +267,10 @@ struct DwBand {
     int ni, total;               // input rows per segment, units
 };
 
-constexpr int kBandRun = 4;
+// Outputs per thread along a row: 4 for 3x3; 2 for 5x5, whose five rows of
+// partial sums in flight would otherwise not fit the registers (the models
+// run their 5x5 convs on the tiled kernel, which is faster there).
+__host__ __device__ constexpr int band_run(int k) { return k == 3 ? 4 : 2; }
 
 __device__ __forceinline__ void band_decode(const DwBand& g, int u, int& img, int& seg, int& bx, int& grp) {
     grp = u % g.groups;
@@ -284,16 +287,17 @@ __host__ __device__ constexpr int fdiv(int a, int b) { return a >= 0 ? a / b : -
 
 // PLAIN: no activation and no residual (the token convs), so the epilogue is
 // the bias add and the store.
-template <typename T, int CG, int SH, int SW, int NR, bool PLAIN>
+template <typename T, int CG, int K, int SH, int SW, int NR, bool PLAIN>
 __global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand g) {
-    constexpr int RUN = kBandRun;
+    constexpr int RUN = band_run(K);
     constexpr int D = NR - 1;                  // rows in flight ahead of the one being computed
     constexpr int QPC = 16 / (4 * sizeof(T));  // channel quads per 16-byte copy
     constexpr int CPP = CG / QPC;              // 16-byte copies per pixel
-    constexpr int SPAN = (RUN - 1) * SW + 3;   // window columns of one run
-    constexpr int NS = SH == 1 ? 3 : 2;        // output rows whose sums are in flight
-    constexpr int U = SH == 1 ? 3 : 4;         // steps per unrolled group: set indices stay static
-    constexpr int WQ = 10 * CG;                // float4 per weight slot: 9 taps + bias
+    constexpr int SPAN = (RUN - 1) * SW + K;   // window columns of one run
+    constexpr int NS = SH == 1 ? K : 2;        // output rows whose sums are in flight (stride 2: 3x3 only)
+    constexpr int U = SH == 1 ? K : 4;         // steps per unrolled group: set indices stay static
+    constexpr int TAPS = K * K;
+    constexpr int WQ = (TAPS + 1) * CG;        // float4 per weight slot: taps + bias
     extern __shared__ float4 sm4[];
     float4* const wslot = sm4;                                  // [2][10][CG]
     T* const ring = reinterpret_cast<T*>(sm4 + 2 * WQ);         // [NR][iw][CG * 4]
@@ -341,7 +345,7 @@ __global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand 
                 const int c0 = i_grp * CG * 4;
                 for (int i = tid; i < WQ; i += nt) {
                     const int t = i / CG, q = i - t * CG;
-                    if (t < 9) cp_async16(wd + i, p.weight + (size_t)t * p.c + c0 + q * 4, true);
+                    if (t < TAPS) cp_async16(wd + i, p.weight + (size_t)t * p.c + c0 + q * 4, true);
                     else cp_async16(wd + i, p.bias ? p.bias + c0 + q * 4 : p.weight, p.bias != nullptr);
                 }
             }
@@ -383,14 +387,14 @@ __global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand 
                 cp_async_wait<D - 1>();  // row t (and, at t == 0, the unit's weights) has landed
                 __syncthreads();         // ... for every thread; the slot of row t - 1 is free
                 issue_row();
-                if (r == 0 && t0 == 0) bias = w[9 * CG];
+                if (r == 0 && t0 == 0) bias = w[TAPS * CG];
                 if (active) {
                     const T* row = ring + cslot * row_elems + (rx * RUN * SW * CG + q) * 4;
                     float4 win[SPAN];
 #pragma unroll
                     for (int i = 0; i < SPAN; ++i) win[i] = to4(row + i * CG * 4);
 #pragma unroll
-                    for (int ky = 2; ky >= 0; --ky) {
+                    for (int ky = K - 1; ky >= 0; --ky) {
                         if (pmod(r - ky, SH) != 0) continue;          // static: row t is not tap row ky of any output
                         const int j = (t - ky) / SH;                   // output row (in the segment) this tap row feeds
                         if (t < ky || j >= rows) continue;
@@ -400,12 +404,12 @@ __global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand 
                             for (int rr = 0; rr < RUN; ++rr) a[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
                         }
 #pragma unroll
-                        for (int kx = 0; kx < 3; ++kx) {
-                            const float4 wv = w[(ky * 3 + kx) * CG];
+                        for (int kx = 0; kx < K; ++kx) {
+                            const float4 wv = w[(ky * K + kx) * CG];
 #pragma unroll
                             for (int rr = 0; rr < RUN; ++rr) a[rr] = f4_vfma(win[rr * SW + kx], wv, a[rr]);
                         }
-                        if (ky == 2) {   // output row j is complete
+                        if (ky == K - 1) {   // output row j is complete
                             const size_t orow = obase + ((size_t)j * p.wo + ox0) * p.c;
                             T* o = static_cast<T*>(p.out) + orow;
 #pragma unroll
@@ -433,15 +437,16 @@ __global__ void __launch_bounds__(256, 2) dwconv_band_kernel(DwParams p, DwBand 
 // (128 outputs) wide so a block is at most 8 quads x 32 runs = 256 threads;
 // tall maps are cut into segments of at least 8 rows until there are a few
 // units per resident block.
-template <typename T, int CG, int SH, int SW>
+template <typename T, int CG, int K, int SH, int SW>
 DwBand band_geometry(const DwParams& p, int resident) {
+    constexpr int RUN = band_run(K);
     DwBand g{};
-    const int runs = (p.wo + kBandRun - 1) / kBandRun;
+    const int runs = (p.wo + RUN - 1) / RUN;
     const int sx_max = 256 / CG < 32 ? 256 / CG : 32;
     g.bands = (runs + sx_max - 1) / sx_max;
     g.sx = (runs + g.bands - 1) / g.bands;
-    g.bw = g.sx * kBandRun;
-    g.iw = (g.bw - 1) * SW + 3;
+    g.bw = g.sx * RUN;
+    g.iw = (g.bw - 1) * SW + K;
     g.groups = p.c / (4 * CG);
     const long long base = (long long)p.n * g.groups * g.bands;
     const long long want = 4LL * resident;
@@ -454,16 +459,16 @@ DwBand band_geometry(const DwParams& p, int resident) {
     }
     g.bh = (p.ho + segs - 1) / segs;
     g.segs = (p.ho + g.bh - 1) / g.bh;
-    g.ni = (g.bh - 1) * SH + 3;
+    g.ni = (g.bh - 1) * SH + K;
     const long long total = base * g.segs;
     g.total = total > 0x7fffffffLL ? -1 : (int)total;
     return g;
 }
 
-template <typename T, int CG, int SH, int SW, int NR, bool PLAIN>
+template <typename T, int CG, int K, int SH, int SW, int NR, bool PLAIN>
 cudaError_t launch_band_nr(const DwParams& p, const DwBand& g, int nt, cudaStream_t stream) {
-    auto kernel = dwconv_band_kernel<T, CG, SH, SW, NR, PLAIN>;
-    const size_t smem = 2 * 10 * CG * sizeof(float4) + (size_t)NR * g.iw * CG * 4 * sizeof(T);
+    auto kernel = dwconv_band_kernel<T, CG, K, SH, SW, NR, PLAIN>;
+    const size_t smem = 2 * (K * K + 1) * CG * sizeof(float4) + (size_t)NR * g.iw * CG * 4 * sizeof(T);
     static std::atomic<int> regs{0};
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
@@ -486,12 +491,12 @@ cudaError_t launch_band_nr(const DwParams& p, const DwBand& g, int nt, cudaStrea
     return cudaGetLastError();
 }
 
-template <typename T, int CG, int SH, int SW>
+template <typename T, int CG, int K, int SH, int SW>
 cudaError_t launch_band(const DwParams& p, cudaStream_t stream) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const DwBand g = band_geometry<T, CG, SH, SW>(p, 2 * sms);
+    const DwBand g = band_geometry<T, CG, K, SH, SW>(p, 2 * sms);
     if (g.total < 0) return cudaErrorInvalidConfiguration;
     if (g.total == 0) return cudaSuccess;
     const int nt = (CG * g.sx + 31) / 32 * 32;
@@ -501,19 +506,19 @@ cudaError_t launch_band(const DwParams& p, cudaStream_t stream) {
     // D rows.
     const bool plain = p.act == ACT_NONE && !p.residual;
     if (row_bytes <= 6 * 1024 && g.ni >= 7)
-        return plain ? launch_band_nr<T, CG, SH, SW, 8, true>(p, g, nt, stream)
-                     : launch_band_nr<T, CG, SH, SW, 8, false>(p, g, nt, stream);
-    return plain ? launch_band_nr<T, CG, SH, SW, 4, true>(p, g, nt, stream)
-                 : launch_band_nr<T, CG, SH, SW, 4, false>(p, g, nt, stream);
+        return plain ? launch_band_nr<T, CG, K, SH, SW, 8, true>(p, g, nt, stream)
+                     : launch_band_nr<T, CG, K, SH, SW, 8, false>(p, g, nt, stream);
+    return plain ? launch_band_nr<T, CG, K, SH, SW, 4, true>(p, g, nt, stream)
+                 : launch_band_nr<T, CG, K, SH, SW, 4, false>(p, g, nt, stream);
 }
 
-template <typename T, int SH, int SW>
+template <typename T, int K, int SH, int SW>
 cudaError_t launch_band_cg(const DwParams& p, cudaStream_t stream) {
     const int quads = p.c / 4;
-    if (quads % 8 == 0) return launch_band<T, 8, SH, SW>(p, stream);
-    if (quads % 4 == 0) return launch_band<T, 4, SH, SW>(p, stream);
-    if (quads % 2 == 0) return launch_band<T, 2, SH, SW>(p, stream);
-    if constexpr (sizeof(T) == 4) return launch_band<T, 1, SH, SW>(p, stream);
+    if (quads % 8 == 0) return launch_band<T, 8, K, SH, SW>(p, stream);
+    if (quads % 4 == 0) return launch_band<T, 4, K, SH, SW>(p, stream);
+    if (quads % 2 == 0) return launch_band<T, 2, K, SH, SW>(p, stream);
+    if constexpr (sizeof(T) == 4) return launch_band<T, 1, K, SH, SW>(p, stream);
     return cudaErrorInvalidValue;
 }
 
@@ -531,18 +536,22 @@ cudaError_t launch_cg(const DwParams& p, cudaStream_t stream) {
 // The geometries of the PP-OCRv6 graphs: 3x3 at strides (1,1), (2,2), (2,1);
 // square 5x5 / 7x7 / 9x9 at stride 1; 1x5 / 1x7 (recognizer heads).
 // 3x3 convs run on the rolling-row kernel unless `kernel` asks for the tiled
-// one (1); every other geometry on the tiled kernel.
+// one (1); every other geometry on the tiled kernel.  The rolling-row kernel
+// also covers 5x5 (kernel 2 only): with the two-column runs that five rows of
+// sums in flight leave room for, it is slower there than the tiled kernel
+// (detector neck 5x5: 123 -> 131 us).
 template <typename T>
 cudaError_t launch_dw_t(const DwParams& p, cudaStream_t stream, int kernel) {
     if (p.kh == 3 && p.kw == 3) {
         const bool band = kernel != 1;
-        if (p.sh == 1 && p.sw == 1) return band ? launch_band_cg<T, 1, 1>(p, stream) : launch_cg<T, 3, 3, 1, 1>(p, stream);
-        if (p.sh == 2 && p.sw == 2) return band ? launch_band_cg<T, 2, 2>(p, stream) : launch_cg<T, 3, 3, 2, 2>(p, stream);
-        if (p.sh == 2 && p.sw == 1) return band ? launch_band_cg<T, 2, 1>(p, stream) : launch_cg<T, 3, 3, 2, 1>(p, stream);
+        if (p.sh == 1 && p.sw == 1) return band ? launch_band_cg<T, 3, 1, 1>(p, stream) : launch_cg<T, 3, 3, 1, 1>(p, stream);
+        if (p.sh == 2 && p.sw == 2) return band ? launch_band_cg<T, 3, 2, 2>(p, stream) : launch_cg<T, 3, 3, 2, 2>(p, stream);
+        if (p.sh == 2 && p.sw == 1) return band ? launch_band_cg<T, 3, 2, 1>(p, stream) : launch_cg<T, 3, 3, 2, 1>(p, stream);
         return cudaErrorInvalidValue;
     }
-    if (kernel == 2) return cudaErrorInvalidValue;
     if (p.sh != 1 || p.sw != 1) return cudaErrorInvalidValue;
+    if (p.kh == 5 && p.kw == 5 && kernel == 2) return launch_band_cg<T, 5, 1, 1>(p, stream);
+    if (kernel == 2) return cudaErrorInvalidValue;
     if (p.kh == p.kw) {
         switch (p.kh) {
             case 5: return launch_cg<T, 5, 5, 1, 1>(p, stream);

@@ -373,7 +373,7 @@ class Gpu:
     def selftest_dwconv(self, x, w, bias=None, stride=(1, 1), pad=(0, 0, 0, 0), act: int = 0, residual=None,
                         bf16: bool = False, kernel: int = 0):
         """Depthwise conv diagnostic: x NHWC [n, hi, wi, c], w [c, kh, kw], pad (top, left, bottom, right);
-        kernel 0 dispatch, 1 tiled, 2 rolling rows (3x3).  Returns (out float32 NHWC, kernel that ran)."""
+        kernel 0 dispatch, 1 tiled, 2 rolling rows (3x3, 5x5).  Returns (out float32 NHWC, kernel that ran)."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         w = np.ascontiguousarray(w, dtype=np.float32)
         n, hi, wi, c = x.shape

@@ -1,6 +1,6 @@
 """Depthwise conv kernels against each other and float64.
 
-The rolling-row 3x3 kernel and the tiled kernel sum each output's taps in
+The rolling-row kernel (3x3, 5x5) and the tiled kernel sum each output's taps in
 (ky, kx) order with the same packed FMAs and apply bias, activation and
 residual in the same order, so on the same inputs they must agree bit for
 bit.  Both must stay within a few FP32 ulps of the float64 result (scaled by
@@ -74,7 +74,10 @@ CASES = [
     (2, 9, 130, 16, 3, (1, 1), (1, 1, 1, 1), 1, True, False),     # 16 channels, 33 runs over two bands
     (1, 7, 9, 8, 3, (2, 2), (1, 1, 1, 1), 5, True, False),        # tiny map, one channel group of two quads
     (2, 20, 36, 4, 3, (1, 1), (1, 1, 1, 1), 3, True, True),       # one channel quad
-    (1, 14, 30, 24, 5, (1, 1), (2, 2, 2, 2), 0, True, False),     # 5x5 (tiled kernel only)
+    (1, 14, 30, 24, 5, (1, 1), (2, 2, 2, 2), 0, True, False),     # 5x5: RepLkFpn depthwise
+    (2, 52, 92, 64, 5, (1, 1), (2, 2, 2, 2), 0, True, False),     # 5x5 detector neck shape, two bands, segments
+    (1, 9, 40, 32, 5, (1, 1), (2, 2, 2, 2), 4, False, True),      # 5x5 with activation and residual
+    (1, 12, 30, 16, 7, (1, 1), (3, 3, 3, 3), 0, True, False),     # 7x7 (tiled kernel only)
     (1, 3, 40, 32, (1, 7), (1, 1), (0, 3, 0, 3), 2, True, True),  # SVTR 1x7 + SiLU + residual (tiled)
 ]
 
@@ -85,6 +88,7 @@ def test_dwconv_kernels(gpu, n, hi, wi, c, k, stride, pad, act, has_bias, has_re
     if bf16 and c % 8:
         pytest.skip("BF16 views need 8-channel alignment")
     kh, kw = (k, k) if isinstance(k, int) else k
+    band = (kh, kw) in ((3, 3), (5, 5))
     rng = np.random.default_rng(n * 1000 + hi * 37 + wi * 11 + c + kh)
     x = rng.normal(0, 1, (n, hi, wi, c)).astype(np.float32)
     w = rng.normal(0, 1 / math.sqrt(kh * kw), (c, kh, kw)).astype(np.float32)
@@ -96,12 +100,12 @@ def test_dwconv_kernels(gpu, n, hi, wi, c, k, stride, pad, act, has_bias, has_re
     for kernel in (1, 2):
         try:
             out, used = gpu.selftest_dwconv(x, w, b, stride, pad, act, r, bf16, kernel)
-        except Exception as e:  # the rolling-row kernel covers 3x3 only
-            assert "does not support" in str(e) and (kh, kw) != (3, 3), e
+        except Exception as e:  # the rolling-row kernel covers 3x3 and 5x5
+            assert "does not support" in str(e) and not band, e
             continue
         assert used == kernel
         outs[kernel] = out
-    assert 1 in outs and ((kh, kw) != (3, 3) or 2 in outs)
+    assert 1 in outs and (not band or 2 in outs)
     xs = _bf16(x) if bf16 else x
     rs = (_bf16(r) if bf16 else r) if r is not None else None
     ref, mag = _reference(xs.astype(np.float64), w.astype(np.float64), b, stride, pad, act, rs)
