@@ -173,25 +173,24 @@ __global__ void __launch_bounds__(128) det_head_kernel(HeadParams p) {
 #pragma unroll
             for (int co = 0; co < CH; ++co) h[co] = bup[co];
             const float* w0 = wup + (a * 2 + b) * CH * CH;
+            // Packed pairs of output channels: each lane is rounded as fmaf, and
+            // every channel still sums its inputs in ci order.
 #pragma unroll 2
             for (int ci = 0; ci < CH; ++ci) {
                 const float v = in[ci];
 #pragma unroll
-                for (int co = 0; co < CH; ++co) h[co] = fmaf(v, w0[ci * CH + co], h[co]);
+                for (int co = 0; co < CH; co += 2) fma2(h[co], h[co + 1], v, v, w0[ci * CH + co], w0[ci * CH + co + 1]);
             }
 #pragma unroll
             for (int co = 0; co < CH; ++co) h[co] = fmaxf(h[co], 0.f);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                float l[2];
+                // The two columns d = 0, 1 as one packed pair of co-ordered sums.
+                float l[2] = {p.b_fin, p.b_fin};
+                const float* wf0 = wfin + (c * 2) * CH;
+                const float* wf1 = wf0 + CH;
 #pragma unroll
-                for (int d = 0; d < 2; ++d) {
-                    const float* wf = wfin + (c * 2 + d) * CH;
-                    float s = p.b_fin;
-#pragma unroll
-                    for (int co = 0; co < CH; ++co) s = fmaf(h[co], wf[co], s);
-                    l[d] = s;
-                }
+                for (int co = 0; co < CH; ++co) fma2(l[0], l[1], h[co], h[co], wf0[co], wf1[co]);
                 const size_t o = ((size_t)img * p.h * 4 + (size_t)(4 * y + 2 * a + c)) * W + 4 * x + 2 * b;
                 if (p.logits) *reinterpret_cast<float2*>(p.logits + o) = make_float2(l[0], l[1]);
                 const float2 pr = make_float2(1.f / (1.f + expf(-l[0])), 1.f / (1.f + expf(-l[1])));
