@@ -64,7 +64,10 @@ typedef struct ppocr_load_options {
     int precision;   /* enum ppocr_precision; default FP32 */
     int use_graph;   /* 1: replay each forward as one captured CUDA graph */
     int simt_only;   /* 1: CUDA-core kernels only (no tcgen05); for A/B checks */
-    int reserved[5];
+    int keep_tensors; /* 1: every activation keeps its own arena range, so
+                         ppocr_model_read_tensor sees each op's output after a
+                         forward (diagnostics; the arena grows to their sum) */
+    int reserved[4];
 } ppocr_load_options;
 
 /* Fills `options` with the defaults (FP32, CUDA graphs on). */
@@ -205,6 +208,19 @@ int ppocr_model_op_info(const ppocr_model* model, size_t index, char* name, size
                         char* kind, size_t kind_capacity, double* bytes, double* flops);
 int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms);
 
+/* Diagnostic (new): the plan's activation tensors.  tensor_info gives the
+ * name of tensor `index` (the op or weight prefix that writes it), its NHWC
+ * shape (n, h, w, c; raw buffers report n = h = w = 1 and c = their element
+ * count) and its storage type (0 F32, 1 BF16).  read_tensor copies the
+ * tensor's current arena contents to `out` as F32 (BF16 widened).  An
+ * intermediate tensor holds its op's output after a forward only when the
+ * model was loaded with keep_tensors = 1; otherwise later ops may reuse its
+ * memory. */
+int ppocr_model_tensor_count(const ppocr_model* model, size_t* count);
+int ppocr_model_tensor_info(const ppocr_model* model, size_t index, char* name, size_t name_capacity, size_t shape[4],
+                            int* dtype);
+int ppocr_model_read_tensor(ppocr_model* model, size_t index, float* out, size_t capacity);
+
 /* Diagnostic (new): C[m, n] = act(A[m, k] W[n, k]^T + bias) through the
  * BF16 GEMM path of this library on `gpu`.  A and W are host F32 arrays
  * rounded to BF16 on upload; C is returned in F32.  used_tensor_cores is set
@@ -281,6 +297,19 @@ int ppocr_measure_fp32_peak(ppocr_gpu* gpu, double* tflops_fma, double* tflops_f
 int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int cin, int cout, int kh, int kw,
                           int stride, int pad, int second, const float* x, const float* x2, const float* w,
                           const float* bias, int act, float* out, int* used_tensor_cores, int* wait_error);
+
+/* Diagnostic (new; the reference's wgpu path has no device-side waits):
+ * failure detection of the tensor-core kernels.  Runs one small GEMM whose
+ * first CTA never issues the loads of its first pipeline stage, so its waits
+ * on that stage run out after wait_ms (1..2000) milliseconds, as a wait on an
+ * arrive that never comes would in a forward.  kernel 0 = the BF16 tcgen05
+ * GEMM, 1 = the engine with BF16 operands, 2 = the engine with FP32 operands
+ * in three BF16 pieces.  The kernel drains its copies and MMAs in flight,
+ * frees its TMEM and returns; the call then fails with PPOCR_ERR_GPU and
+ * *code holds the kernel's wait-expiry code (nonzero).  The device stays
+ * usable.  In a model forward the same expiry fails the forward with
+ * PPOCR_ERR_GPU (src/gpu/error.rs:8-45, Error::Gpu). */
+int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* code);
 
 /* Recognizer only: the classifier's pre-softmax logits [n, t, classes]
  * (new; the reference fuses the softmax, src/cpu/backend.rs:1288-1290, so it

@@ -229,6 +229,18 @@ class compute_dtype:
         _DTYPE = self.prev
 
 
+# Optional capture of intermediate activations (test diagnostics only): while
+# TRACE is a dict, the detector's modules store their outputs in it (NCHW)
+# under the names the CUDA plan gives the same tensors.
+TRACE: Optional[Dict[str, Tensor]] = None
+
+
+def _trace(name: str, x: Tensor) -> Tensor:
+    if TRACE is not None:
+        TRACE[name] = x.detach().clone()
+    return x
+
+
 def t(a: np.ndarray) -> Tensor:
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(_DTYPE)
 
@@ -355,6 +367,7 @@ class LcNetBlock:
     def __init__(self, w: Weights, prefix: str, blk):
         pad = blk.kernel // 2
         pads = (pad,) * 4
+        self.prefix = prefix
         self.residual = blk.residual
         if blk.residual:
             self.token = load_conv(w, f"{prefix}.token_conv", blk.cin, blk.cout, (blk.kernel,) * 2,
@@ -372,12 +385,12 @@ class LcNetBlock:
         self.pw2 = load_conv_bn(w, f"{prefix}.channel_conv2", blk.cin * 2, blk.cout, (1, 1), (1, 1), (0,) * 4, False, 1)
 
     def __call__(self, x: Tensor) -> Tensor:
-        y = self.token(x)
+        y = _trace(f"{self.prefix}.token", self.token(x))
         if self.se is not None:
             y = self.se(y)
         out = self.pw2(gelu(self.pw1(y)))
         # The residual is the token/SE output (backend.rs:504-521, cpu/model.rs:591-602).
-        return y + out if self.residual else out
+        return _trace(f"{self.prefix}.out", y + out if self.residual else out)
 
 
 class LargeStem:
@@ -390,10 +403,11 @@ class LargeStem:
         self.stem4 = c("stem4", mid, out, (1, 1), (1, 1), (0, 0, 0, 0))
 
     def __call__(self, x: Tensor) -> Tensor:
-        e = self.stem1(x)
+        e = _trace("stem1", self.stem1(x))
         branch = self.stem2b(self.stem2a(e))
         pooled = max_pool_same_upper(e)
-        return self.stem4(self.stem3(torch.cat([pooled, branch], dim=1)))
+        s3 = _trace("stem3", self.stem3(torch.cat([pooled, branch], dim=1)))
+        return _trace("stem4", self.stem4(s3))
 
 
 class SmallStem:
@@ -452,7 +466,8 @@ class RepLkFpn:
         fused = [se(conv(f)) for (conv, se), f in zip(self.insert, stages)]
         for i in (2, 1, 0):
             fused[i] = fused[i] + upsample(fused[i + 1], 2)
-        feats = [se(pw(dw(f))) for (dw, pw, se), f in zip(self.input, fused)]
+        feats = [_trace(f"model.neck.input_conv.{i}.out", se(pw(dw(f))))
+                 for i, ((dw, pw, se), f) in enumerate(zip(self.input, fused))]
         feats.reverse()
         return torch.cat([upsample(f, s) for f, s in zip(feats, (8, 4, 2, 1))], dim=1)
 
@@ -537,7 +552,7 @@ class DetectorHead:
         self.final_b = w.get("head.conv_final.bias", (1,))
 
     def logits(self, x: Tensor) -> Tensor:
-        h = self.down(x)
+        h = _trace("head.conv_down", self.down(x))
         h = relu(conv_transpose_2x2(h, self.up_w, self.up_b))
         return conv_transpose_2x2(h, self.final_w, self.final_b)
 

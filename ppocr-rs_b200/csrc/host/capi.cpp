@@ -48,7 +48,12 @@ void wait_stream(cudaStream_t s, int timeout_ms) {
 
 namespace {
 
-// Process-wide pool of pinned host flag pairs: a model load takes one pair
+// Per-model device flags, reset before and read back after every forward:
+// [0] non-finite input, [1] non-finite output, [2] the code of a tensor-core
+// pipeline wait that ran out (0: none), [3] unused.
+constexpr size_t kFlags = 4;
+
+// Process-wide pool of pinned host flag sets (kFlags ints): a model load takes one set
 // instead of pinning a fresh page (cudaMallocHost costs milliseconds), and the
 // pool outlives every device handle.
 class PinnedFlags {
@@ -57,11 +62,11 @@ public:
         std::lock_guard<std::mutex> lock(mu());
         auto& f = free_list();
         if (f.empty()) {
-            constexpr size_t kPairs = 1024;
+            constexpr size_t kSets = 1024;
             int* slab = nullptr;
-            cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&slab), kPairs * 2 * sizeof(int), cudaHostAllocPortable),
+            cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&slab), kSets * kFlags * sizeof(int), cudaHostAllocPortable),
                        "allocate host flags");
-            for (size_t i = 0; i < kPairs; ++i) f.push_back(slab + 2 * i);
+            for (size_t i = 0; i < kSets; ++i) f.push_back(slab + kFlags * i);
         }
         int* p = f.back();
         f.pop_back();
@@ -128,7 +133,7 @@ struct ppocr_model {
     uint64_t exec_gen = 0;
     float exec_threshold = 0.f;
     bool warmed = false;
-    int* dflags = nullptr;   // device: [0] non-finite input, [1] non-finite output
+    int* dflags = nullptr;   // device flags (kFlags ints, see above)
     int* hflags = nullptr;   // pinned host copy
 
     ~ppocr_model() {
@@ -145,6 +150,7 @@ struct ppocr_model {
         c.side = gpu->side;
         c.fork = gpu->fork;
         c.join = gpu->join;
+        c.err = dflags + 2;
         return c;
     }
     void* tensor(int tid) const { return tid < 0 ? nullptr : static_cast<char*>(gpu->arena) + m.plan.tensors[tid].offset; }
@@ -191,6 +197,18 @@ struct ppocr_model {
 
 namespace {
 
+// Raises the reference's error for the flags read back after a forward:
+// InvalidInput for a non-finite input (src/gpu/runtime.rs:1979-1983),
+// Error::Gpu for a non-finite output (2217-2219) or a tensor-core pipeline
+// wait that ran out (the forward's results are then incomplete).
+void raise_flags(const ppocr_model* model) {
+    if (model->hflags[2])
+        fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(model->hflags[2]) +
+                                "); the forward's results are incomplete");
+    if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
+    if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+}
+
 void upload_and_run(ppocr_model* model, const float* input, size_t len) {
     if (!input) fail(PPOCR_ERR_INVALID_INPUT, "input pointer is null");
     if (len != model->input_elements()) {
@@ -199,7 +217,7 @@ void upload_and_run(ppocr_model* model, const float* input, size_t len) {
     }
     ppocr_gpu* g = model->gpu;
     g->ensure_arena(model->m.plan.arena_bytes);
-    cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), g->stream), "reset flags");
+    cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), g->stream), "reset flags");
     cuda_check(cudaMemcpyAsync(model->tensor(model->m.input), input, len * 4, cudaMemcpyHostToDevice, g->stream), "upload input");
     // Non-finite inputs are an InvalidInput (src/gpu/runtime.rs:1979-1983); the scan runs on the device.
     cuda_check(launch_check_finite(static_cast<const float*>(model->tensor(model->m.input)), len, model->dflags, g->stream),
@@ -218,10 +236,9 @@ void finish(ppocr_model* model, int checked_tid, size_t rows, size_t cols, size_
         cuda_check(launch_check_finite_rows(static_cast<const float*>(model->tensor(checked_tid)), rows, cols, ld,
                                             model->dflags + 1, s),
                    "check output");
-    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
+    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
     wait_stream(s, 0);
-    if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
-    if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+    raise_flags(model);
 }
 
 void finish(ppocr_model* model, int checked_tid, size_t checked_count) { finish(model, checked_tid, 1, checked_count, checked_count); }
@@ -293,8 +310,14 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     // host copy for sharing checks): an engine caching hundreds of recognizer
     // shapes would otherwise keep one per shape.
     model->m.blob = WeightBlob();
+    if (o.keep_tensors) {
+        // Diagnostics: no two tensors share memory, so every op's output
+        // survives the forward for ppocr_model_read_tensor.
+        for (auto& t : model->m.plan.tensors) t.pinned = true;
+        model->m.plan.finalize();
+    }
     gpu->ensure_arena(model->m.plan.arena_bytes);
-    cuda_check(cudaMalloc(&model->dflags, 2 * sizeof(int)), "allocate flags");
+    cuda_check(cudaMalloc(&model->dflags, kFlags * sizeof(int)), "allocate flags");
     model->hflags = PinnedFlags::acquire();
     return model.release();
 }
@@ -530,7 +553,7 @@ int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t
         float* dinput = static_cast<float*>(model->tensor(model->m.input));
         const int otid = model->output_tid();
         try {
-            cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), cs), "reset flags");
+            cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), cs), "reset flags");
             for (size_t c = 0; c < chunks; ++c) {
                 const int slot = (int)(c & 1);
                 // Upload chunk c once the forward of chunk c - 2 has taken its copy of the slot.
@@ -558,7 +581,7 @@ int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t
                 cuda_check(cudaEventRecord(pp.downloaded[slot], pp.d2h), "record download");
             }
             cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[(chunks - 1) & 1], 0), "join download");
-            cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
+            cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
             wait_stream(cs, 0);
         } catch (...) {
             // The caller's buffers must not be touched after return.
@@ -567,8 +590,7 @@ int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t
             cudaStreamSynchronize(pp.d2h);
             throw;
         }
-        if (model->hflags[0]) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: model input contains non-finite values");
-        if (model->hflags[1]) fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+        raise_flags(model);
     });
 }
 
@@ -589,7 +611,7 @@ int ppocr_model_forward_image(ppocr_model* model, const ppocr_image* image, cons
         model->gpu->ensure_arena(model->m.plan.arena_bytes);
         PreprocessParams p = make_preprocess(image, corners, cw, (size_t)model->m.h, (size_t)model->m.w, det);
         p.out = static_cast<float*>(model->tensor(model->m.input));
-        cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), model->gpu->stream), "reset flags");
+        cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), model->gpu->stream), "reset flags");
         cuda_check(launch_preprocess(p, model->gpu->stream), "launch preprocess");
         model->run(model->gpu->stream);
         download(model, model->output_tid(), output, model->m.output_elements * 4);
@@ -623,6 +645,7 @@ int ppocr_model_benchmark(ppocr_model* model, const float* input, size_t input_l
         }
         cudaEventDestroy(a);
         cudaEventDestroy(b);
+        finish(model, -1, 0);   // a pipeline wait that ran out in any run fails the call
     });
 }
 
@@ -633,6 +656,7 @@ int ppocr_model_forward_device(ppocr_model* model, const float* device_input, fl
         model->gpu->bind();
         model->gpu->ensure_arena(model->m.plan.arena_bytes);
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : model->gpu->stream;
+        cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
         cuda_check(cudaMemcpyAsync(model->tensor(model->m.input), device_input, model->input_elements() * 4,
                                    cudaMemcpyDeviceToDevice, s), "copy input");
         model->run(s);
@@ -657,7 +681,9 @@ int ppocr_model_run(ppocr_model* model, void* stream) {
         if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
         std::lock_guard<std::mutex> lock(model->gpu->mu);
         model->gpu->bind();
-        model->run(stream ? static_cast<cudaStream_t>(stream) : model->gpu->stream);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : model->gpu->stream;
+        cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
+        model->run(s);
     });
 }
 
@@ -666,6 +692,14 @@ int ppocr_model_synchronize(ppocr_model* model, int timeout_ms) {
         if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
         model->gpu->bind();
         wait_stream(model->gpu->stream, timeout_ms);
+        // Device-resident runs on a caller stream report a tensor-core wait that
+        // ran out here, once the caller's stream has completed.
+        cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost,
+                                   model->gpu->stream), "read flags");
+        wait_stream(model->gpu->stream, timeout_ms);
+        if (model->hflags[2])
+            fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(model->hflags[2]) +
+                                    "); the forward's results are incomplete");
     });
 }
 
@@ -719,6 +753,7 @@ void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t 
     if (count < (size_t)model->m.n)
         cuda_check(cudaMemsetAsync(in + count * per, 0, ((size_t)model->m.n - count) * per * sizeof(float), s),
                    "clear unused crop slots");
+    cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
     model->run(s);
     const size_t rows = count * model->m.t;
     std::vector<int32_t> idx(rows);
@@ -726,7 +761,9 @@ void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t 
     download(model, model->m.index, idx.data(), rows * 4);
     download(model, model->m.max_prob, prob.data(), rows * 4);
     if (margins) download(model, model->m.margin, margins, rows * 4);
+    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
     wait_stream(s, 0);
+    raise_flags(model);
     // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
     for (size_t r = 0; r < rows; ++r)
         if (idx[r] < 0 || idx[r] >= model->m.classes || !std::isfinite(prob[r]))
@@ -782,7 +819,7 @@ int ppocr_detector_forward_images(ppocr_model* model, const ppocr_image* const* 
             p.out = in + i * per;
             cuda_check(launch_preprocess(p, s), "launch preprocess");
         }
-        cuda_check(cudaMemsetAsync(model->dflags, 0, 2 * sizeof(int), s), "reset flags");
+        cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
         model->run(s);
         download(model, model->output_tid(), probabilities, model->m.output_elements * 4);
         finish(model, model->output_tid(), model->m.output_elements);
@@ -812,6 +849,62 @@ int ppocr_model_op_info(const ppocr_model* model, size_t index, char* name, size
         }
         if (bytes) *bytes = model->m.plan.op_bytes(index);
         if (flops) *flops = op.flops;
+    });
+}
+
+int ppocr_model_tensor_count(const ppocr_model* model, size_t* count) {
+    return guard([&] {
+        if (!model || !count) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        *count = model->m.plan.tensors.size();
+    });
+}
+
+int ppocr_model_tensor_info(const ppocr_model* model, size_t index, char* name, size_t name_capacity, size_t shape[4],
+                            int* dtype) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (index >= model->m.plan.tensors.size()) fail(PPOCR_ERR_INVALID_INPUT, "tensor index out of range");
+        const TensorDesc& t = model->m.plan.tensors[index];
+        if (name && name_capacity) {
+            std::strncpy(name, t.name.c_str(), name_capacity - 1);
+            name[name_capacity - 1] = 0;
+        }
+        const bool raw = t.n == 0;
+        if (shape) {
+            shape[0] = raw ? 1 : (size_t)t.n;
+            shape[1] = raw ? 1 : (size_t)t.h;
+            shape[2] = raw ? 1 : (size_t)t.w;
+            shape[3] = raw ? t.bytes / dtype_size(t.dt) : (size_t)t.c;
+        }
+        if (dtype) *dtype = (int)t.dt;
+    });
+}
+
+int ppocr_model_read_tensor(ppocr_model* model, size_t index, float* out, size_t capacity) {
+    return guard([&] {
+        if (!model || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (index >= model->m.plan.tensors.size()) fail(PPOCR_ERR_INVALID_INPUT, "tensor index out of range");
+        const TensorDesc& t = model->m.plan.tensors[index];
+        const size_t count = t.bytes / dtype_size(t.dt);
+        if (capacity < count)
+            fail(PPOCR_ERR_INVALID_INPUT, "output buffer holds " + std::to_string(capacity) + " values; " +
+                                              std::to_string(count) + " required");
+        std::lock_guard<std::mutex> lock(model->gpu->mu);
+        model->gpu->bind();
+        model->gpu->ensure_arena(model->m.plan.arena_bytes);
+        cudaStream_t s = model->gpu->stream;
+        if (t.dt == DT_F32) {
+            download(model, (int)index, out, count * 4);
+        } else {
+            std::vector<uint16_t> h(count);
+            download(model, (int)index, h.data(), count * 2);
+            wait_stream(s, 0);
+            for (size_t i = 0; i < count; ++i) {
+                const uint32_t u = (uint32_t)h[i] << 16;
+                std::memcpy(out + i, &u, 4);
+            }
+        }
+        wait_stream(s, 0);
     });
 }
 
@@ -848,6 +941,67 @@ int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms) {
         }
         for (auto& e : ev) cudaEventDestroy(e);
         for (size_t i = 0; i < ops.size(); ++i) op_ms[i] = acc[i] / (double)runs;
+    });
+}
+
+int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* code) {
+    return guard([&] {
+        if (!gpu || !code) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (kernel < 0 || kernel > 2) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0, 1 or 2");
+        if (wait_ms < 1 || wait_ms > 2000) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: wait_ms outside 1..=2000");
+        *code = 0;
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        // A 256 x 64 x 128 GEMM: two 128-row tiles, so CTA 1 runs normally while
+        // CTA 0 waits for the first stage that its producer never loads.
+        const int m = 256, n = 64, k = 128, planes = kernel == 2 ? 3 : 1;
+        ConvWeight cw;
+        cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
+        cw.w.assign((size_t)n * k, 0.5f);
+        cw.b.assign(n, 0.f);
+        WeightBlob blob;
+        const int bn = tc_engine_tile_n(n, planes);
+        const int n_pad = kernel == 0 ? (n + 15) / 16 * 16 : (n + bn - 1) / bn * bn, k_pad = (k + 63) / 64 * 64;
+        const size_t wo = kernel == 0 ? blob.add_bf16(pack_gemm_nk(cw, n_pad, k_pad)) : blob.add_bf16(pack_engine_kn(cw, planes, n_pad, k_pad));
+        const std::vector<float> av((size_t)m * k, 0.25f);
+        const size_t ao = planes == 1 ? blob.add_bf16(av) : blob.add_f32(av);
+        const size_t co = blob.add_f32(std::vector<float>((size_t)m * n, 0.f));
+        const size_t fo = blob.add_f32(std::vector<float>(64, 0.f));   // the wait-expiry flag
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate wait test buffers");
+        int* flag = reinterpret_cast<int*>(d + fo);
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        const uint64_t limit = (uint64_t)wait_ms * 1000000ull;
+        if (e == cudaSuccess) {
+            if (kernel == 0) {
+                GemmParams p;
+                p.m = m; p.n = n; p.k = k; p.lda = k; p.k_pad = k_pad; p.n_pad = n_pad;
+                p.a = d + ao; p.w_tc = d + wo; p.c = d + co; p.ldc = n; p.c_f32 = 1; p.dtype = DT_BF16;
+                p.err = flag; p.wait_ns = limit; p.skip_load = 1;
+                e = launch_gemm_tc(p, gpu->stream);
+            } else {
+                TcEngineParams p;
+                p.mode = 0; p.planes = planes; p.m = m; p.n = n; p.k = k; p.n_pad = n_pad; p.k_pad = k_pad;
+                p.w = d + wo; p.a = d + ao; p.lda = k; p.c = d + co; p.ldc = n;
+                p.err = flag; p.wait_ns = limit; p.skip_load = 1;
+                e = launch_tc_engine(p, gpu->stream);
+            }
+        }
+        int h = 0;
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "wait-expiry self-test");
+        *code = h;
+        if (h) fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(h) + ")");
     });
 }
 

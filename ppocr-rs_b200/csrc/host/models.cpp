@@ -124,6 +124,7 @@ public:
                            p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
                            p.residual = c.act(residual);
                            p.c = c.act(out_tid);
+                           p.err = c.err;
                            return launch_tc_engine(p, st);
                        },
                        srcs.empty() ? "gemm" : "conv", (double)planes * p.n_pad * p.k_pad * 2, flops);
@@ -248,6 +249,7 @@ public:
             p.bias = c.wf(boff);
             p.residual = c.act(residual);
             p.out = c.act(otid);
+            p.err = c.err;
             return launch_conv(p, st);
         }, "conv", (double)cw.w.size() * 4, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
         return out;
@@ -342,6 +344,7 @@ public:
                            p.res_gate = res_gate >= 0 ? static_cast<const float*>(c.act(res_gate)) : nullptr;
                            p.residual = c.act(residual);
                            p.c = c.act(out_tid);
+                           p.err = c.err;
                            return launch_gemm(p, st);
                        },
                        "gemm", (double)k * cw.cout * (tc ? 2 : 4), 2.0 * rows * cw.cout * k);

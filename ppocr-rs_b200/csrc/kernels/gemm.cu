@@ -7,8 +7,6 @@
 
 namespace ppocr {
 
-cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
-
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
     if (p.w_tc && gemm_tc_supported(p)) return launch_gemm_tc(p, stream);
     if (p.dtype == DT_F32) {

@@ -58,7 +58,15 @@ struct TcArgs {
     // Implicit-GEMM conv (conv = 1): a tile is 8 x 16 output pixels of one image,
     // a K step one (tap, 64-channel block) loaded as a strided 4D TMA box.
     int conv, tiles_y, tiles_x, cblocks, kw, stride, pt, pl;
+    // Wait-expiry reporting: the code lands in *err (null: g_tc_error); each
+    // pipeline wait gives up after wait_ns.  skip_load (self-test only): CTA 0
+    // never issues its first stage's loads, so the waits on it run out.
+    int* err;
+    uint64_t wait_ns;
+    int skip_load;
 };
+
+__device__ __forceinline__ void report(const TcArgs& p, int code) { atomicExch(p.err ? p.err : &g_tc_error, code); }
 
 template <typename T, int ACT>
 __device__ __forceinline__ void epilogue16(const TcArgs& p, int row, int col0, const float (&v)[16]) {
@@ -208,12 +216,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tma_b,
                                                              const __grid_constant__ CUtensorMap tma_c, TcArgs p) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], acc_full[2], acc_empty[2];
+    __shared__ __align__(8) uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int a_bytes = BM * BK * 2;
     const int b_bytes = p.bn * BK * 2;
+    const uint64_t wait_ns = p.wait_ns;
     const int S = p.stages;
     uint8_t* sa = smem;
     uint8_t* sb = smem + S * a_bytes;
@@ -230,6 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             tc::mbar_init(&acc_full[b], 1);
             tc::mbar_init(&acc_empty[b], EPI_WARPS * 32);
         }
+        tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -241,6 +251,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
     if (warp == 0) {
         if (lane == 0) {
+            // last_it[s]: the last iteration whose loads were issued into stage s
+            // (-1: none), so an aborting CTA can wait for its copies in flight.
+            int last_it[MAX_STAGES];
+            for (int s = 0; s < MAX_STAGES; ++s) last_it[s] = -1;
             int it = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
                 const int mt = tile / p.n_tiles;
@@ -255,11 +269,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                 }
                 for (int kt = 0; kt < p.kt; ++kt, ++it) {
                     const int s = it % S;
-                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false)) {
-                        atomicExch(&g_tc_error, 1);
+                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false, wait_ns, &abort_flag)) {
+                        report(p, 1);
                         abort_flag = 1;
                         break;
                     }
+                    if (p.skip_load && it == 0 && blockIdx.x == 0) continue;
                     tc::mbar_expect_tx(&full_bar[s], (uint32_t)(a_bytes + b_bytes));
                     if (p.conv) {
                         const int tap = kt / p.cblocks, cb = kt - tap * p.cblocks;
@@ -269,7 +284,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                         tc::tma_load_2d(sa + s * a_bytes, &tma_a, &full_bar[s], kt * BK, m0);
                     }
                     tc::tma_load_2d(sb + s * b_bytes, &tma_b, &full_bar[s], kt * BK, n0);
+                    last_it[s] = it;
                 }
+            }
+            if (abort_flag) {
+                // Let the copies already issued land before the CTA exits.
+                for (int s = 0; s < S; ++s)
+                    if (last_it[s] >= 0) tc::mbar_wait(&full_bar[s], (last_it[s] / S) & 1, false, wait_ns);
             }
         }
     } else if (warp == 1) {
@@ -278,8 +299,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x, ++ti) {
                 const int b = ti & 1;
-                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false)) {
-                    atomicExch(&g_tc_error, 2);
+                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false, wait_ns, &abort_flag)) {
+                    report(p, 2);
                     abort_flag = 1;
                     break;
                 }
@@ -288,8 +309,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                 bool ok = true;
                 for (int kt = 0; kt < p.kt; ++kt, ++it) {
                     const int s = it % S;
-                    if (!tc::mbar_wait(&full_bar[s], (it / S) & 1, false)) {
-                        atomicExch(&g_tc_error, 3);
+                    if (!tc::mbar_wait(&full_bar[s], (it / S) & 1, false, wait_ns, &abort_flag)) {
+                        report(p, 3);
                         abort_flag = 1;
                         ok = false;
                         break;
@@ -305,6 +326,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                 if (!ok) break;
                 tc::commit(&acc_full[b]);
             }
+            // Every MMA this thread issued completes before the CTA goes on to
+            // free TMEM (on the normal path they already have).
+            tc::commit(&drain_bar);
+            tc::mbar_wait(&drain_bar, 0, false, wait_ns);
         }
     } else {
         // Epilogue warps 2..17: TMEM lane quarter q = warp % 4, column slot (warp - 2) / 4.
@@ -318,10 +343,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             if (abort_flag) break;
             const int b = ti & 1;
             const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * p.bn;
-            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1);
+            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1, true, wait_ns, &abort_flag);
             got = __all_sync(0xffffffffu, got);
             if (!got) {
-                if (lane == 0) atomicExch(&g_tc_error, 4);
+                if (lane == 0) report(p, 4);
                 abort_flag = 1;
                 break;
             }
@@ -485,6 +510,7 @@ cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
     a.m_tiles = (p.m + BM - 1) / BM;
     a.n_tiles = (p.n + bn - 1) / bn;
     a.bias = p.bias; a.act = p.act;
+    a.err = p.err; a.wait_ns = p.wait_ns ? p.wait_ns : tc::kWaitNs; a.skip_load = p.skip_load;
     a.residual = p.residual; a.ldr = p.ldr; a.res_scale = p.res_scale; a.h = p.h; a.w_px = p.w_px;
     a.c = p.c; a.ldc = p.ldc; a.coff = p.coff; a.c_f32 = p.c_f32;
     // TMA store: the output base and row pitch must be 16-byte aligned.
@@ -572,6 +598,8 @@ cudaError_t launch_conv_tc(const ConvParams& p, cudaStream_t stream) {
     a.ldc = p.out_cstride;
     a.coff = p.out_coff;
     a.tma_store = 1;
+    a.err = p.err;
+    a.wait_ns = p.wait_ns ? p.wait_ns : tc::kWaitNs;
     const size_t smem = (size_t)a.stages * stage_bytes + out_bytes + 1024;
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();

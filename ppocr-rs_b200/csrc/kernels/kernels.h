@@ -66,6 +66,10 @@ struct ConvParams {
     void* out = nullptr;
     int out_cstride = 0, out_coff = 0;
     DType dtype = DT_F32;
+    // tcgen05 kernels: a pipeline wait that runs out stores its code here
+    // (null: the kernel file's own flag) and gives up after wait_ns (0: 2 s).
+    int* err = nullptr;
+    uint64_t wait_ns = 0;
 };
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
 
@@ -144,6 +148,12 @@ struct GemmParams {
     int ldc = 0, coff = 0;
     DType dtype = DT_F32;             // storage of A, residual and C
     int c_f32 = 0;                    // 1: C is FP32 regardless of dtype
+    // tcgen05 GEMM: wait-expiry flag (null: g_tc_error) and bound (0: 2 s);
+    // skip_load = 1 (self-test only) leaves CTA 0's first stage unloaded so
+    // that the waits on it run out.
+    int* err = nullptr;
+    uint64_t wait_ns = 0;
+    int skip_load = 0;
 };
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream);
 
@@ -179,6 +189,7 @@ cudaError_t launch_gemm_stream(const GemmParams& p, cudaStream_t stream);
 
 // Tensor-core (tcgen05) GEMM availability: BF16 storage, k_pad % 64 == 0, n_pad % 16 == 0.
 bool gemm_tc_supported(const GemmParams& p);
+cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
 // Reads and clears the tensor-core kernel's wait-expiry code (0 = none; host sync).
 int gemm_tc_error_and_clear();
 
@@ -204,6 +215,9 @@ struct TcEngineParams {
     int ldr = 0, res_scale = 1, out_h = 1, out_w = 1;
     void* c = nullptr;                // BF16 (planes 1) or FP32 (planes 3) [m][ldc] at column coff
     int ldc = 0, coff = 0;
+    int* err = nullptr;               // wait-expiry flag (null: g_tce_error)
+    uint64_t wait_ns = 0;             // pipeline wait bound (0: 2 s)
+    int skip_load = 0;                // self-test only: CTA 0's first W load is never issued
 };
 int tc_engine_tile_n(int n, int planes);
 bool tc_engine_supported(const TcEngineParams& p);

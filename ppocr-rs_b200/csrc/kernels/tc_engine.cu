@@ -49,7 +49,11 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 struct EngArgs {
     TcEngineParams p;
     int kt, bn, stages, tmem_cols, m_tiles, n_tiles, tma_store;
+    uint64_t wait_ns;
 };
+
+// Wait-expiry code into the caller's flag (null: g_tce_error).
+__device__ __forceinline__ void report(const TcEngineParams& p, int code) { atomicExch(p.err ? p.err : &g_tce_error, code); }
 
 // 8 BF16 / 4 FP32 consecutive elements as floats.
 __device__ __forceinline__ void load8(const __nv_bfloat16* src, float (&v)[8]) {
@@ -238,7 +242,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
     const TcEngineParams& p = args.p;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t w_full[MAX_STAGES], a_full[MAX_STAGES], empty_bar[MAX_STAGES], acc_full[2],
-        acc_empty[2];
+        acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -249,6 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
     uint8_t* sout = smem + (size_t)S * stage_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = args.m_tiles * args.n_tiles;
+    const uint64_t wait_ns = args.wait_ns;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -260,6 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
             tc::mbar_init(&acc_full[b], 1);
             tc::mbar_init(&acc_empty[b], EPI_WARPS * 32);
         }
+        tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -271,22 +277,32 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
 
     if (warp == 0) {
         if (lane == 0) {
+            // last_it[s]: the last iteration whose W loads went into stage s (-1:
+            // none), so an aborting CTA can wait for its copies in flight.
+            int last_it[MAX_STAGES];
+            for (int s = 0; s < MAX_STAGES; ++s) last_it[s] = -1;
             int it = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
                 const int n0 = (tile % args.n_tiles) * args.bn;
                 for (int kt = 0; kt < args.kt; ++kt, ++it) {
                     const int s = it % S;
-                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false)) {
-                        atomicExch(&g_tce_error, 1);
+                    if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, false, wait_ns, &abort_flag)) {
+                        report(p, 1);
                         abort_flag = 1;
                         break;
                     }
+                    if (p.skip_load && it == 0 && blockIdx.x == 0) continue;
                     uint8_t* st = smem + (size_t)s * stage_bytes + PLANES * a_bytes;
                     tc::mbar_expect_tx(&w_full[s], (uint32_t)(PLANES * b_bytes));
 #pragma unroll
                     for (int j = 0; j < PLANES; ++j)
                         tc::tma_load_2d(st + j * b_bytes, &tma_w, &w_full[s], kt * BK, j * p.n_pad + n0);
+                    last_it[s] = it;
                 }
+            }
+            if (abort_flag) {
+                for (int s = 0; s < S; ++s)
+                    if (last_it[s] >= 0) tc::mbar_wait(&w_full[s], (last_it[s] / S) & 1, false, wait_ns);
             }
         }
     } else if (warp == 1) {
@@ -295,8 +311,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x, ++ti) {
                 const int b = ti & 1;
-                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false)) {
-                    atomicExch(&g_tce_error, 2);
+                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false, wait_ns, &abort_flag)) {
+                    report(p, 2);
                     abort_flag = 1;
                     break;
                 }
@@ -306,8 +322,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
                 for (int kt = 0; kt < args.kt; ++kt, ++it) {
                     const int s = it % S;
                     const uint32_t par = (it / S) & 1;
-                    if (!tc::mbar_wait(&a_full[s], par, false) || !tc::mbar_wait(&w_full[s], par, false)) {
-                        atomicExch(&g_tce_error, 3);
+                    if (!tc::mbar_wait(&a_full[s], par, false, wait_ns, &abort_flag) ||
+                        !tc::mbar_wait(&w_full[s], par, false, wait_ns, &abort_flag)) {
+                        report(p, 3);
                         abort_flag = 1;
                         ok = false;
                         break;
@@ -335,6 +352,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
                 if (!ok) break;
                 tc::commit(&acc_full[b]);
             }
+            // Every MMA this thread issued completes before TMEM is freed.
+            tc::commit(&drain_bar);
+            tc::mbar_wait(&drain_bar, 0, false, wait_ns);
         }
     } else if (warp < 6) {
         // A producers: thread pt owns rows rb + 16 i (i < 8) and chunk(s) ch + 8 j (j < CPT).
@@ -366,8 +386,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
             bool ok = true;
             for (int kt = 0; kt < args.kt; ++kt, ++it) {
                 const int s = it % S;
-                if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1)) {
-                    atomicExch(&g_tce_error, 4);
+                if (it >= S && !tc::mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, true, wait_ns, &abort_flag)) {
+                    report(p, 4);
                     abort_flag = 1;
                     ok = false;
                     break;
@@ -457,10 +477,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_engine_kernel(const __grid_cons
             if (abort_flag) break;
             const int b = ti & 1;
             const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * args.bn;
-            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1);
+            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1, true, wait_ns, &abort_flag);
             got = __all_sync(0xffffffffu, got);
             if (!got) {
-                if (lane == 0) atomicExch(&g_tce_error, 5);
+                if (lane == 0) report(p, 5);
                 abort_flag = 1;
                 break;
             }
@@ -581,6 +601,7 @@ cudaError_t launch_tc_engine(const TcEngineParams& in, cudaStream_t stream) {
     while (cols < 2 * a.bn || cols < a.bn + gw) cols <<= 1;
     if (cols > 512) return cudaErrorInvalidConfiguration;
     a.tmem_cols = cols;
+    a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
     const int stage_bytes = planes * (BM * BK * 2 + a.bn * BK * 2);
     const int out_bytes = EPI_WARPS * STAGE_OUT_BYTES;
     a.stages = (SMEM_LIMIT - 2048 - out_bytes) / stage_bytes;

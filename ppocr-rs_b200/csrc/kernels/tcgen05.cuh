@@ -11,7 +11,16 @@
 namespace ppocr {
 namespace tc {
 
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Default bound of one pipeline wait.  Every wait inside these kernels is
+// on another role of the same CTA and normally ends within microseconds; the
+// bound only has to end a wait whose arrive never comes.
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -29,13 +38,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded parity wait: true when the phase completed, false on expiry.
+// Bounded parity wait: true when the phase completed, false when `limit_ns`
+// of wall time (the GPU's global timer) passed first or, polled every 64
+// tries, another role of the CTA has raised `*abort` (null: never).
 // `backoff` threads (epilogue warps) sleep between polls; the single TMA and
 // MMA issuing threads poll without sleeping so the pipeline is not delayed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, bool backoff = true) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, bool backoff = true, uint64_t limit_ns = kWaitNs,
+                                          const volatile int* abort = nullptr) {
     const uint32_t addr = smem_u32(bar);
-    const uint32_t limit = backoff ? kWaitLimit : kWaitLimit * 8;
-    for (uint32_t i = 0; i < limit; ++i) {
+    uint64_t start = 0;
+    for (uint32_t i = 0;; ++i) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -45,9 +57,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, bool b
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
+        if ((i & 63) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (i == 0) start = now;
+            else if (now - start > limit_ns || (abort && *abort)) return false;
+        }
         if (backoff && i > 32) __nanosleep(64);
     }
-    return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {

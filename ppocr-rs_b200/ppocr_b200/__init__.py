@@ -133,7 +133,8 @@ class _EngineOptions(C.Structure):
 
 
 class _LoadOptions(C.Structure):
-    _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("simt_only", C.c_int), ("reserved", C.c_int * 5)]
+    _fields_ = [("precision", C.c_int), ("use_graph", C.c_int), ("simt_only", C.c_int), ("keep_tensors", C.c_int),
+                ("reserved", C.c_int * 4)]
 
 
 _SIZE4 = C.c_size_t * 4
@@ -217,6 +218,10 @@ def library() -> C.CDLL:
         "ppocr_recognizer_forward_crops_ex": (I, [P, C.POINTER(C.c_void_p), S, FP, C.POINTER(S),
                                                   C.POINTER(C.c_int32), FP, FP]),
         "ppocr_detector_forward_images": (I, [P, C.POINTER(C.c_void_p), S, FP]),
+        "ppocr_selftest_wait_expiry": (I, [P, I, I, C.POINTER(C.c_int)]),
+        "ppocr_model_tensor_count": (I, [P, C.POINTER(S)]),
+        "ppocr_model_tensor_info": (I, [P, S, C.c_char_p, S, _SIZE4, C.POINTER(C.c_int)]),
+        "ppocr_model_read_tensor": (I, [P, S, FP, S]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -330,6 +335,19 @@ class Gpu:
                                                None if b is None else _fptr(b), int(act), _fptr(out), C.byref(used),
                                                C.byref(err)))
         return out, bool(used.value), err.value
+
+    def selftest_wait_expiry(self, kernel: int, wait_ms: int = 20) -> int:
+        """Makes one tensor-core pipeline wait run out (kernel 0: BF16 GEMM, 1 / 2:
+        the engine with 1 / 3 operand planes); raises GpuError carrying the
+        kernel's wait-expiry code as `.wait_code`."""
+        code = C.c_int()
+        status = library().ppocr_selftest_wait_expiry(self._h, int(kernel), int(wait_ms), C.byref(code))
+        try:
+            _check(status)
+        except Error as e:
+            e.wait_code = code.value
+            raise
+        return code.value
 
     def selftest_gemm_ex(self, a, w, c_init, coff: int, bias=None, act: int = 0, residual=None, out_bf16: bool = True):
         """GEMM diagnostic into columns [coff, coff + n) of c_init [m, ldc] (other columns must survive);
@@ -543,6 +561,28 @@ class _Model:
     def synchronize(self, timeout_ms: int = 0) -> None:
         _check(library().ppocr_model_synchronize(self._h, int(timeout_ms)))
 
+    def tensors(self) -> List[dict]:
+        """The plan's activation tensors: name, NHWC shape and storage type."""
+        n = C.c_size_t()
+        _check(library().ppocr_model_tensor_count(self._h, C.byref(n)))
+        out = []
+        for i in range(n.value):
+            name = C.create_string_buffer(256)
+            shape = _SIZE4()
+            dt = C.c_int()
+            _check(library().ppocr_model_tensor_info(self._h, i, name, 256, shape, C.byref(dt)))
+            out.append({"index": i, "name": name.value.decode(), "shape": tuple(shape), "dtype": "bf16" if dt.value else "f32"})
+        return out
+
+    def read_tensor(self, name: str) -> np.ndarray:
+        """Current contents of the named tensor as float32 NHWC (needs keep_tensors for intermediates)."""
+        for t in self.tensors():
+            if t["name"] == name:
+                out = np.empty(t["shape"], dtype=np.float32)
+                _check(library().ppocr_model_read_tensor(self._h, t["index"], _fptr(out), out.size))
+                return out
+        raise KeyError(name)
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             library().ppocr_model_destroy(self._h)
@@ -555,12 +595,13 @@ class _Model:
             pass
 
 
-def _options(precision, use_graph: bool, simt_only: bool = False) -> _LoadOptions:
+def _options(precision, use_graph: bool, simt_only: bool = False, keep_tensors: bool = False) -> _LoadOptions:
     o = _LoadOptions()
     library().ppocr_load_options_default(C.byref(o))
     o.precision = Precision.parse(precision)
     o.use_graph = 1 if use_graph else 0
     o.simt_only = 1 if simt_only else 0
+    o.keep_tensors = 1 if keep_tensors else 0
     return o
 
 
@@ -569,9 +610,9 @@ class Detector(_Model):
 
     @classmethod
     def load(cls, gpu: Gpu, path: str, size, input_shape: Sequence[int], precision="fp32",
-             use_graph: bool = True, simt_only: bool = False) -> "Detector":
+             use_graph: bool = True, simt_only: bool = False, keep_tensors: bool = False) -> "Detector":
         h = C.c_void_p()
-        o = _options(precision, use_graph, simt_only)
+        o = _options(precision, use_graph, simt_only, keep_tensors)
         _check(library().ppocr_detector_load_ex(gpu._h, str(path).encode(), ModelSize.parse(size),
                                                 _SIZE4(*input_shape), C.byref(o), C.byref(h)))
         return cls(h, gpu, input_shape)

@@ -1,0 +1,82 @@
+"""Where the FP32 detector's rounding leaves the reference arithmetic's own
+FP32 noise band (benchmark config 1: tiny detector, spec weights,
+1x3x416x736).
+
+The spec weights make the detector numerically chaotic (logits of 1e4-1e6),
+so the final probability map of any FP32 evaluation differs from the float64
+evaluation of the same graph at a few pixels.  This test loads the CUDA model
+with keep_tensors (every op's output kept), traces the same activations in
+the oracle at FP32 and float64, and prints per layer the normwise relative
+error of the CUDA path and of the FP32 oracle against float64, plus the map
+statistics.  It asserts the per-layer errors stay within FP32 rounding
+(relative error < 1e-4 before the head) and that the map's mean-abs error is
+within the 2e-3 bound.
+"""
+
+import numpy as np
+import pytest
+
+import ppocr_b200 as P
+from ppocr_b200 import seeded
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, ref):
+    scale = float(np.abs(ref).max()) or 1.0
+    return float(np.abs(a - ref).max()) / scale, float(np.abs(a - ref).mean()) / (float(np.abs(ref).mean()) or 1.0)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "fp32tc"])
+def test_detector_spec_layer_divergence(gpu, weights_file, precision):
+    import torch
+
+    path = weights_file("det", "tiny", "spec")
+    x = seeded.det_batch(1, 416, 736, seed=1)
+    det = P.Detector.load(gpu, path, "tiny", x.shape, precision=precision, keep_tensors=True)
+    got = det.forward(x).values.reshape(1, 1, 416, 736)
+    names = {t["name"] for t in det.tensors()}
+    orc = om.Detector(om.Weights.load(path), "tiny")
+    try:
+        om.TRACE = {}
+        want = orc.forward(x)
+        t32 = om.TRACE
+        om.TRACE = {}
+        with om.compute_dtype(torch.float64):
+            exact = orc.forward(x)
+        t64 = om.TRACE
+    finally:
+        om.TRACE = None
+    lines = [f"{precision}: layer | CUDA max-rel mean-rel | oracle-f32 max-rel mean-rel (both vs float64)"]
+    first_out = None
+    found = 0
+    for key, ref in t64.items():
+        cands = [key]
+        if key.endswith(".out") and key.startswith("model.backbone"):
+            stem = key[: -len(".out")]
+            cands = [stem + ".pair", stem + ".pw2"]
+        cname = next((c for c in cands if c in names), None)
+        if cname is None:
+            continue
+        found += 1
+        g = det.read_tensor(cname).transpose(0, 3, 1, 2)
+        e = ref.numpy()
+        o = t32[key].numpy()
+        cr, cm = _rel(g, e)
+        orr, om_ = _rel(o, e)
+        lines.append(f"  {key:48s} {cr:9.2e} {cm:9.2e} | {orr:9.2e} {om_:9.2e}")
+        if first_out is None and cm > 3 * om_ and cm > 1e-6:
+            first_out = key
+        if key != "head.conv_down":
+            assert cr < 1e-4, f"{key}: relative error {cr} is beyond FP32 rounding"
+    d = np.abs(got - want)
+    de = np.abs(got - exact)
+    dn = np.abs(want - exact)
+    lines.append(f"  map vs FP32 oracle: max {d.max():.3g} mean {d.mean():.3g} n>2e-2 {int((d > 2e-2).sum())}")
+    lines.append(f"  map vs float64:     max {de.max():.3g} mean {de.mean():.3g} n>2e-2 {int((de > 2e-2).sum())}")
+    lines.append(f"  oracle vs float64:  max {dn.max():.3g} mean {dn.mean():.3g} n>2e-2 {int((dn > 2e-2).sum())}")
+    lines.append(f"  first layer whose mean relative error exceeds 3x the oracle's: {first_out}")
+    print("\n".join(lines))
+    assert found >= 10, f"only {found} traced layers matched plan tensors"
+    assert d.mean() <= 2e-3
