@@ -4,7 +4,7 @@
 Default workload: the tiny detector forward at 416x736 (benchmark configs 1
 and 3: the reference's ppocr-gpu-bench --kind det shape, batched 32 images per
 GPU), seeded uniform-RGB8 inputs, seeded random-init weights in the exact
-reference checkpoint layout, FP32 (the parity mode).
+reference checkpoint layout, FP32.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                   [--kind det|rec|e2e] [--size tiny|small|medium] [--batch B]
@@ -599,7 +599,7 @@ def main():
     ap.add_argument("--kind", default="det", choices=["det", "rec", "e2e"])
     ap.add_argument("--size", default="tiny", choices=["tiny", "small", "medium"])
     ap.add_argument("--batch", type=int, default=None)
-    ap.add_argument("--precision", default=None, choices=[None, "fp32", "bf16"])
+    ap.add_argument("--precision", default=None, choices=[None, "fp32", "bf16", "fp32tc"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")

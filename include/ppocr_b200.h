@@ -124,6 +124,18 @@ void ppocr_model_destroy(ppocr_model* model);
 int ppocr_inspect_model(const char* path, int kind, int size, const size_t input_shape[4], int precision,
                         size_t* ops, size_t* arena_bytes, size_t* weight_bytes, size_t output_shape[4]);
 
+/* Seeded random-init checkpoint (new; the reference downloads the released
+ * weights, src/models.rs:200-222, which needs a network): writes a
+ * safetensors file holding every tensor of the kind (0 detector,
+ * 1 recognizer) / size tier in the reference's names and shapes, drawn from
+ * the benchmark configs' distributions (detector conv weights
+ * N(0, sqrt(2 / fan_in)), recognizer conv / linear weights N(0, 0.02), batch
+ * norm gamma 1 / beta 0 / mean 0 / var 1, layer norm weight 1 / bias 0,
+ * biases 0).  Each tensor has its own generator seeded by (seed, name), so the
+ * file depends only on (kind, size, seed).  Needs no GPU.  Backs
+ * ppocr-gpu-bench --seed-weights. */
+int ppocr_write_seeded_weights(const char* path, int kind, int size, uint64_t seed);
+
 /* ModelOutput::shape: writes the output shape (rank 4 for the detector,
  * rank 3 for the recognizer) and the element count. */
 int ppocr_model_output_shape(const ppocr_model* model, size_t shape[4],
@@ -248,7 +260,10 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
  * (k <= 128, n <= 128).  gate (may be NULL) is [m / rows_per_image][k] and
  * scales A; residual (may be NULL) is [m][n].  kernel_used returns the kernel
  * that ran (1..3).  k must be a multiple of 4; a kernel that does not
- * support the shape fails with PPOCR_ERR_INVALID_INPUT. */
+ * support the shape fails with PPOCR_ERR_INVALID_INPUT.  kernel 4 = the
+ * tcgen05 split GEMM of the FP32_TC mode (k a multiple of 16): A and W carried
+ * as three BF16 pieces each, the six leading products accumulated in FP32 in
+ * TMEM (FP32-class rounding, not bit-identical to the CUDA-core kernels). */
 int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used);
@@ -304,7 +319,8 @@ int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int
  * on that stage run out after wait_ms (1..2000) milliseconds, as a wait on an
  * arrive that never comes would in a forward.  kernel 0 = the BF16 tcgen05
  * GEMM, 1 = the engine with BF16 operands, 2 = the engine with FP32 operands
- * in three BF16 pieces.  The kernel drains its copies and MMAs in flight,
+ * in three BF16 pieces, 3 = the split GEMM (FP32 activations split in shared
+ * memory).  The kernel drains its copies and MMAs in flight,
  * frees its TMEM and returns; the call then fails with PPOCR_ERR_GPU and
  * *code holds the kernel's wait-expiry code (nonzero).  The device stays
  * usable.  In a model forward the same expiry fails the forward with

@@ -1,7 +1,9 @@
 // ppocr-gpu-bench: the reference's benchmark CLI contract
 // (ppocr-rs src/bin/ppocr-gpu-bench.rs:45-88, src/bin/benchmark.rs:13-320)
 // over the C ABI.  Same flags, deterministic input, F32 reference / dump files
-// and report keys; adds --batch, --precision and --no-graph.
+// and report keys; adds --batch, --precision, --no-graph, --gpus (the same
+// benchmark on N devices at once, one host thread and model per device) and
+// --seed-weights (a seeded random-init checkpoint instead of --model).
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -9,6 +11,7 @@
 #include <cstring>
 #include <fstream>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "ppocr_b200.h"
@@ -26,7 +29,8 @@ void check(int status, const char* what) {
 
 struct Args {
     std::string kind, model_size = "tiny", model, input, reference, dump, precision = "fp32";
-    long height = -1, width = -1, warmup = 5, runs = 30, batch = 1;
+    long height = -1, width = -1, warmup = 5, runs = 30, batch = 1, gpus = 1;
+    long long seed = -1;
     bool graph = true;
 };
 
@@ -53,16 +57,22 @@ Args parse(int argc, char** argv) {
         else if (k == "--batch") a.batch = std::stol(val());
         else if (k == "--precision") a.precision = val();
         else if (k == "--no-graph") a.graph = false;
+        else if (k == "--gpus") a.gpus = std::stol(val());
+        else if (k == "--seed-weights") a.seed = std::stoll(val());
         else if (k == "-h" || k == "--help") {
             std::printf("usage: ppocr-gpu-bench --kind det|rec --model FILE [--model-size tiny|small|medium] [--height H] "
                         "[--width W] [--input F32] [--reference F32] [--dump F32] [--warmup 5] [--runs 30] [--batch 1] "
-                        "[--precision fp32|bf16] [--no-graph]\n");
+                        "[--precision fp32|bf16|fp32tc] [--no-graph] [--gpus N] [--seed-weights SEED]\n");
             std::exit(0);
         } else die("unknown argument " + k);
     }
     if (a.kind != "det" && a.kind != "rec") die("--kind must be det or rec");
-    if (a.model.empty()) die("the pinned model store is not part of this build; pass --model FILE");
+    if (a.seed >= 0 && !a.model.empty()) die("--model and --seed-weights are mutually exclusive");
+    if (a.model.empty() && a.seed < 0)
+        die("the pinned model store is not part of this build; pass --model FILE or --seed-weights SEED");
     if (a.runs <= 0) die("--runs must be positive");
+    if (a.gpus <= 0) die("--gpus must be positive");
+    if (a.batch <= 0) die("--batch must be positive");
     return a;
 }
 
@@ -112,24 +122,72 @@ int main(int argc, char** argv) {
     int size = a.model_size == "medium" ? PPOCR_MEDIUM : a.model_size == "small" ? PPOCR_SMALL : a.model_size == "tiny" ? PPOCR_TINY : -1;
     if (size < 0) die("unknown --model-size " + a.model_size);
 
-    ppocr_gpu* gpu = nullptr;
-    check(ppocr_gpu_create(0, &gpu), "create GPU");
-    ppocr_load_options o;
-    ppocr_load_options_default(&o);
-    o.precision = a.precision == "bf16" ? PPOCR_PRECISION_BF16 : a.precision == "fp32tc" ? PPOCR_PRECISION_FP32_TC : PPOCR_PRECISION_FP32;
-    o.use_graph = a.graph ? 1 : 0;
-    ppocr_model* model = nullptr;
-    if (det) check(ppocr_detector_load_ex(gpu, a.model.c_str(), size, shape, &o, &model), "load detector");
-    else check(ppocr_recognizer_load_ex(gpu, a.model.c_str(), size, shape, &o, nullptr, &model), "load recognizer");
-    size_t out_shape[4], rank = 0, elements = 0;
-    check(ppocr_model_output_shape(model, out_shape, &rank, &elements), "output shape");
-    std::vector<float> out(elements);
-    check(ppocr_model_forward(model, input.data(), input.size(), out.data(), out.size()), "forward");
+    if (a.seed >= 0) {
+        // A seeded checkpoint in the reference layout, written next to the
+        // system's temporary files.
+        const char* tmp = std::getenv("TMPDIR");
+        a.model = std::string(tmp && *tmp ? tmp : "/tmp") + "/ppocr-seeded-" + a.kind + "-" + a.model_size + "-" +
+                  std::to_string(a.seed) + ".safetensors";
+        check(ppocr_write_seeded_weights(a.model.c_str(), det ? 0 : 1, size, (uint64_t)a.seed), "write seeded weights");
+    }
+    int devices = 0;
+    check(ppocr_gpu_count(&devices), "count GPUs");
+    if (a.gpus > devices) die("--gpus " + std::to_string(a.gpus) + " exceeds the " + std::to_string(devices) + " visible devices");
+
+    // One worker per device: its own handle, model, output and samples.
+    struct Worker {
+        ppocr_gpu* gpu = nullptr;
+        ppocr_model* model = nullptr;
+        std::vector<float> out;
+        std::vector<double> samples;
+        size_t out_shape[4] = {0, 0, 0, 0}, rank = 0;
+        int status = PPOCR_OK;
+        std::string error;
+    };
+    std::vector<Worker> workers((size_t)a.gpus);
+    auto run = [&](int dev) {
+        Worker& wk = workers[(size_t)dev];
+        auto ok = [&](int st, const char* what) {
+            if (st != PPOCR_OK && wk.status == PPOCR_OK) {
+                wk.status = st;
+                wk.error = std::string(what) + ": " + ppocr_last_error();
+            }
+            return st == PPOCR_OK;
+        };
+        if (!ok(ppocr_gpu_create(dev, &wk.gpu), "create GPU")) return;
+        ppocr_load_options o;
+        ppocr_load_options_default(&o);
+        o.precision = a.precision == "bf16" ? PPOCR_PRECISION_BF16 : a.precision == "fp32tc" ? PPOCR_PRECISION_FP32_TC : PPOCR_PRECISION_FP32;
+        o.use_graph = a.graph ? 1 : 0;
+        if (!ok(det ? ppocr_detector_load_ex(wk.gpu, a.model.c_str(), size, shape, &o, &wk.model)
+                    : ppocr_recognizer_load_ex(wk.gpu, a.model.c_str(), size, shape, &o, nullptr, &wk.model),
+                det ? "load detector" : "load recognizer"))
+            return;
+        size_t elements = 0;
+        if (!ok(ppocr_model_output_shape(wk.model, wk.out_shape, &wk.rank, &elements), "output shape")) return;
+        wk.out.resize(elements);
+        if (!ok(ppocr_model_forward(wk.model, input.data(), input.size(), wk.out.data(), wk.out.size()), "forward")) return;
+        wk.samples.resize((size_t)a.runs);
+        ok(ppocr_model_benchmark(wk.model, input.data(), input.size(), (size_t)a.warmup, (size_t)a.runs, wk.samples.data()),
+           "benchmark");
+    };
+    if (a.gpus == 1) {
+        run(0);
+    } else {
+        std::vector<std::thread> threads;
+        for (int d = 0; d < (int)a.gpus; ++d) threads.emplace_back(run, d);
+        for (auto& t : threads) t.join();
+    }
+    for (size_t d = 0; d < workers.size(); ++d)
+        if (workers[d].status != PPOCR_OK) die("GPU " + std::to_string(d) + ": " + workers[d].error);
+    const Worker& w0 = workers[0];
+    const std::vector<float>& out = w0.out;
+    const size_t* out_shape = w0.out_shape;
+    const size_t rank = w0.rank;
     float mn = INFINITY, mx = -INFINITY;
     double sum = 0.0;
     for (float v : out) { mn = std::min(mn, v); mx = std::max(mx, v); sum += v; }
-    std::vector<double> samples((size_t)a.runs);
-    check(ppocr_model_benchmark(model, input.data(), input.size(), (size_t)a.warmup, (size_t)a.runs, samples.data()), "benchmark");
+    const std::vector<double>& samples = w0.samples;
     double avg = 0.0;
     for (double s : samples) avg += s;
     avg /= samples.size();
@@ -149,6 +207,21 @@ int main(int argc, char** argv) {
                 percentile(sorted, 0.9), percentile(sorted, 0.95));
     std::printf("throughput: %.2f\n", 1000.0 / avg);
     std::printf("batch: %ld\n%s: %.2f\n", a.batch, det ? "images_per_s" : "crops_per_s", 1000.0 * a.batch / avg);
+    if (a.gpus > 1) {
+        // Every device ran the same batch concurrently (weak scaling): the
+        // aggregate is the sum of the per-device rates.
+        double agg = 0.0;
+        std::printf("gpus: %ld\n", a.gpus);
+        for (size_t d = 0; d < workers.size(); ++d) {
+            double m = 0.0;
+            for (double s : workers[d].samples) m += s;
+            m /= workers[d].samples.size();
+            std::printf("gpu%zu_average_ms: %.3f\n", d, m);
+            agg += 1000.0 * a.batch / m;
+        }
+        std::printf("aggregate_%s: %.2f\n", det ? "images_per_s" : "crops_per_s", agg);
+    }
+    if (a.seed >= 0) std::printf("seed_weights: %lld\n", a.seed);
 
     if (!a.reference.empty()) {
         // report_reference (benchmark.rs:229-285)
@@ -178,7 +251,9 @@ int main(int argc, char** argv) {
         f.write(reinterpret_cast<const char*>(out.data()), out.size() * 4);
         std::printf("dump: %s\n", a.dump.c_str());
     }
-    ppocr_model_destroy(model);
-    ppocr_gpu_destroy(gpu);
+    for (auto& wk : workers) {
+        ppocr_model_destroy(wk.model);
+        ppocr_gpu_destroy(wk.gpu);
+    }
     return 0;
 }

@@ -468,6 +468,15 @@ void ppocr_model_destroy(ppocr_model* model) {
     delete model;
 }
 
+int ppocr_write_seeded_weights(const char* path, int kind, int size, uint64_t seed) {
+    return guard([&] {
+        if (!path) fail(PPOCR_ERR_INVALID_INPUT, "path is null");
+        if (kind != 0 && kind != 1) fail(PPOCR_ERR_INVALID_INPUT, "kind must be 0 (detector) or 1 (recognizer)");
+        if (size != PPOCR_MEDIUM && size != PPOCR_SMALL && size != PPOCR_TINY) fail(PPOCR_ERR_INVALID_INPUT, "unknown model size");
+        write_seeded_weights(path, kind == 0, size, seed);
+    });
+}
+
 int ppocr_inspect_model(const char* path, int kind, int size, const size_t input_shape[4], int precision, size_t* ops,
                         size_t* arena_bytes, size_t* weight_bytes, size_t output_shape[4]) {
     return guard([&] {
@@ -947,20 +956,20 @@ int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms) {
 int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* code) {
     return guard([&] {
         if (!gpu || !code) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
-        if (kernel < 0 || kernel > 2) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0, 1 or 2");
+        if (kernel < 0 || kernel > 3) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..3");
         if (wait_ms < 1 || wait_ms > 2000) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: wait_ms outside 1..=2000");
         *code = 0;
         std::lock_guard<std::mutex> lock(gpu->mu);
         gpu->bind();
         // A 256 x 64 x 128 GEMM: two 128-row tiles, so CTA 1 runs normally while
         // CTA 0 waits for the first stage that its producer never loads.
-        const int m = 256, n = 64, k = 128, planes = kernel == 2 ? 3 : 1;
+        const int m = 256, n = 64, k = 128, planes = kernel >= 2 ? 3 : 1;
         ConvWeight cw;
         cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
         cw.w.assign((size_t)n * k, 0.5f);
         cw.b.assign(n, 0.f);
         WeightBlob blob;
-        const int bn = tc_engine_tile_n(n, planes);
+        const int bn = kernel == 3 ? gemm_split_tile_n(n) : tc_engine_tile_n(n, planes);
         const int n_pad = kernel == 0 ? (n + 15) / 16 * 16 : (n + bn - 1) / bn * bn, k_pad = (k + 63) / 64 * 64;
         const size_t wo = kernel == 0 ? blob.add_bf16(pack_gemm_nk(cw, n_pad, k_pad)) : blob.add_bf16(pack_engine_kn(cw, planes, n_pad, k_pad));
         const std::vector<float> av((size_t)m * k, 0.25f);
@@ -980,6 +989,12 @@ int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* cod
                 p.a = d + ao; p.w_tc = d + wo; p.c = d + co; p.ldc = n; p.c_f32 = 1; p.dtype = DT_BF16;
                 p.err = flag; p.wait_ns = limit; p.skip_load = 1;
                 e = launch_gemm_tc(p, gpu->stream);
+            } else if (kernel == 3) {
+                SplitGemmParams p;
+                p.m = m; p.n = n; p.k = k; p.lda = k; p.n_pad = n_pad; p.k_pad = k_pad;
+                p.a = reinterpret_cast<const float*>(d + ao); p.w = d + wo; p.c = reinterpret_cast<float*>(d + co); p.ldc = n;
+                p.err = flag; p.wait_ns = limit; p.skip_load = 1;
+                e = launch_gemm_split(p, gpu->stream);
             } else {
                 TcEngineParams p;
                 p.mode = 0; p.planes = planes; p.m = m; p.n = n; p.k = k; p.n_pad = n_pad; p.k_pad = k_pad;
@@ -1245,8 +1260,58 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
         if (!gpu || !a || !w || !c) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
         if (m <= 0 || n <= 0 || k <= 0 || k % 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: GEMM shape (k must be a multiple of 4)");
         if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
-        if (kernel < 0 || kernel > 3) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..3");
+        if (kernel < 0 || kernel > 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..4");
         if (gate && (rows_per_image <= 0 || m % rows_per_image)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: rows_per_image must divide m");
+        if (kernel == 4) {
+            // The FP32-class tcgen05 split GEMM.
+            SplitGemmParams p;
+            p.m = m; p.n = n; p.k = k; p.lda = k; p.ldc = n; p.ldr = n; p.act = act;
+            p.rows_per_image = gate ? rows_per_image : 1;
+            const int bn = gemm_split_tile_n(n);
+            p.n_pad = (n + bn - 1) / bn * bn;
+            p.k_pad = (k + 63) / 64 * 64;
+            if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split GEMM needs k % 16 == 0");
+            std::lock_guard<std::mutex> lock(gpu->mu);
+            gpu->bind();
+            ConvWeight cw;
+            cw.cout = n; cw.cin = k; cw.kh = 1; cw.kw = 1;
+            cw.w.assign(w, w + (size_t)n * k);
+            cw.b = bias ? std::vector<float>(bias, bias + n) : std::vector<float>(n, 0.f);
+            WeightBlob blob;
+            const size_t wo = blob.add_bf16(pack_engine_kn(cw, 3, p.n_pad, p.k_pad));
+            const size_t bo = blob.add_f32(cw.b);
+            const size_t ao = blob.add_f32(std::vector<float>(a, a + (size_t)m * k));
+            const size_t go = gate ? blob.add_f32(std::vector<float>(gate, gate + (size_t)(m / rows_per_image) * k)) : 0;
+            const size_t ro = residual ? blob.add_f32(std::vector<float>(residual, residual + (size_t)m * n)) : 0;
+            const size_t co = blob.add_f32(std::vector<float>((size_t)m * n, 0.f));
+            const size_t fo = blob.add_f32(std::vector<float>(64, 0.f));
+            const std::vector<uint8_t>& bytes = blob.bytes();
+            char* d = nullptr;
+            cuda_check(cudaMalloc(&d, bytes.size()), "allocate GEMM test buffers");
+            p.a = reinterpret_cast<const float*>(d + ao); p.w = d + wo; p.bias = reinterpret_cast<const float*>(d + bo);
+            p.gate = gate ? reinterpret_cast<const float*>(d + go) : nullptr;
+            p.residual = residual ? reinterpret_cast<const float*>(d + ro) : nullptr;
+            p.c = reinterpret_cast<float*>(d + co);
+            p.err = reinterpret_cast<int*>(d + fo);
+            int flag = 0;
+            cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+            if (e == cudaSuccess) e = launch_gemm_split(p, gpu->stream);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, (size_t)m * n * 4, cudaMemcpyDeviceToHost, gpu->stream);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(&flag, p.err, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
+            if (e == cudaSuccess) {
+                try {
+                    wait_stream(gpu->stream, 0);
+                } catch (...) {
+                    cudaFree(d);
+                    throw;
+                }
+            }
+            cudaFree(d);
+            cuda_check(e, "split GEMM self-test");
+            if (flag) fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(flag) + ")");
+            if (kernel_used) *kernel_used = 4;
+            return;
+        }
         std::lock_guard<std::mutex> lock(gpu->mu);
         gpu->bind();
         ConvWeight cw;

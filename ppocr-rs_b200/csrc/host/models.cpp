@@ -297,9 +297,58 @@ public:
         return out;
     }
 
+    // FP32 operands on tcgen05 through the split GEMM (gemm_split.cu): A split
+    // into three BF16 pieces in shared memory, the SE gate applied there.
+    bool split_gemm_ok(int k, int n) const {
+        if (!tensor_core_f32()) return false;
+        SplitGemmParams p;
+        p.m = 1; p.n = n; p.k = k; p.lda = k; p.ldc = n;
+        const int bn = gemm_split_tile_n(n);
+        p.n_pad = (n + bn - 1) / bn * bn;
+        p.k_pad = (k + 63) / 64 * 64;
+        return gemm_split_supported(p);
+    }
+
+    void split_gemm(const std::string& name, const ConvWeight& cw, int in_tid, int rows, const GemmOpts& o, int out_tid) {
+        const int k = cw.cin * cw.kh * cw.kw;
+        ConvWeight flat = cw;
+        flat.cin = k; flat.kh = 1; flat.kw = 1;
+        SplitGemmParams p;
+        p.m = rows; p.n = cw.cout; p.k = k; p.lda = k;
+        const int bn = gemm_split_tile_n(cw.cout);
+        p.n_pad = (cw.cout + bn - 1) / bn * bn;
+        p.k_pad = (k + 63) / 64 * 64;
+        p.rows_per_image = o.rows_per_image;
+        p.act = o.act;
+        p.ldr = cw.cout;
+        p.res_scale = o.res_scale; p.out_h = o.h; p.out_w = o.w;
+        p.ldc = o.ldc ? o.ldc : cw.cout;
+        const size_t woff = m_.blob.add_bf16(pack_engine_kn(flat, 3, p.n_pad, p.k_pad));
+        const size_t boff = m_.blob.add_f32(cw.b);
+        const bool has_bias = o.has_bias;
+        const int gate = o.gate, res_gate = o.res_gate, residual = o.residual;
+        m_.plan.add_op(name, {in_tid, gate, res_gate, residual}, {out_tid},
+                       [p, woff, boff, has_bias, in_tid, gate, res_gate, residual, out_tid](const Ctx& c, cudaStream_t st) mutable {
+                           p.a = static_cast<const float*>(c.act(in_tid));
+                           p.w = c.wb(woff);
+                           p.bias = has_bias ? c.wf(boff) : nullptr;
+                           p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
+                           p.res_gate = res_gate >= 0 ? static_cast<const float*>(c.act(res_gate)) : nullptr;
+                           p.residual = static_cast<const float*>(c.act(residual));
+                           p.c = static_cast<float*>(c.act(out_tid));
+                           p.err = c.err;
+                           return launch_gemm_split(p, st);
+                       },
+                       "gemm", (double)3 * p.n_pad * p.k_pad * 2, 2.0 * rows * cw.cout * k);
+    }
+
     // Pointwise conv / linear over `rows` rows of `in` (gemm_simt.cu / tcgen05 GEMM).
     void gemm_rows(const std::string& name, const ConvWeight& cw, int in_tid, int rows, const GemmOpts& o, int out_tid) {
         const int k = cw.cin * cw.kh * cw.kw;
+        if (split_gemm_ok(k, cw.cout)) {
+            split_gemm(name, cw, in_tid, rows, o, out_tid);
+            return;
+        }
         if (tensor_core_f32() && k % 4 == 0 && o.res_gate < 0) {
             TcEngineParams tp;
             tp.mode = 0;
@@ -497,8 +546,10 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
                       r.conv_bn(prefix + ".channel_conv2", blk.cout, blk.cin * 2, 1, 1, false), y, gate, blk.residual());
     }
     if (gate >= 0) {
-        // The tensor-core GEMMs take no residual gate: apply the SE gate once.
-        if (b.tensor_core_gemms() || b.tensor_core_f32()) {
+        // The BF16 and engine tensor-core GEMMs take no residual gate: apply the
+        // SE gate once.  (The FP32 split GEMM gates A and the residual itself.)
+        const bool split = b.split_gemm_ok(blk.cin, blk.cin * 2) && b.split_gemm_ok(blk.cin * 2, blk.cout);
+        if (b.tensor_core_gemms() || (b.tensor_core_f32() && !split)) {
             y = b.gate_apply(prefix + ".se.apply", y, gate, 0, nullptr, 1);
             gate = -1;
         }
@@ -809,7 +860,7 @@ void svtr_head(Builder& b, const Act4& x, int cin, int hidden, int mlp) {
 }
 
 void check_count(const SafeTensors& st, const char* what, int size, size_t expected) {
-    if (st.size() != expected) {
+    if (!st.recording() && st.size() != expected) {
         std::ostringstream o;
         o << size_name(size) << " " << what << " has " << st.size() << " tensors; expected " << expected;
         fail(PPOCR_ERR_INVALID_MODEL, o.str());

@@ -231,7 +231,19 @@ std::vector<float> SafeTensors::f32(const std::string& name) const {
     return out;
 }
 
+SafeTensors SafeTensors::recorder() {
+    SafeTensors st;
+    st.recording_ = true;
+    return st;
+}
+
 std::vector<float> SafeTensors::f32(const std::string& name, const std::vector<size_t>& shape) const {
+    if (recording_) {
+        requested_[name] = shape;
+        size_t count = 1;
+        for (size_t d : shape) count *= d;
+        return std::vector<float>(count, 1.f);
+    }
     const std::vector<size_t>& found = this->shape(name);
     if (found != shape)
         fail(PPOCR_ERR_SHAPE_MISMATCH, "tensor \"" + name + "\" has shape " + shape_str(found) + "; expected " + shape_str(shape));

@@ -198,11 +198,9 @@ cudaError_t launch_conv_t(const ConvParams& p, cudaStream_t stream) {
     constexpr int PIX = 1;
     const int tiles = (p.cout + CO - 1) / CO;
     const size_t smem = (size_t)p.kh * p.kw * p.cin * CO * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(conv_kernel<T, CO, PIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(conv_kernel<T, CO, PIX>), 200 * 1024);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     if (smem > 200 * 1024 || p.nsrc < 1 || p.nsrc > 4) return cudaErrorInvalidConfiguration;
     // Upsampling factors are powers of two (nearest x2/x4/x8 in the necks);

@@ -1,0 +1,446 @@
+// FP32-class tcgen05 GEMM over FP32 activations and weights ("split" GEMM).
+//
+//   C[m, n] = act(sum_k (A[m, k] g[img, k]) W[n, k] + bias) (+ residual r[m, n] h[img, n])
+//
+// Both operands are carried as three BF16 pieces, x = x0 + x1 + x2 with
+// x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1) (24 significand
+// bits: the FP32 value for normal ranges), and the six products with
+// i + j <= 2 are accumulated in FP32 in TMEM; the dropped x1 w2 + x2 w1 +
+// x2 w2 are ~2^-24 relative, so every product carries FP32-class error.
+// The weights are split once on the host; A is split on the fly:
+//
+//   warp 0 / lane 0   TMA: A as FP32 (two 128-row x 32-column 128-byte-swizzled
+//                     boxes per 64-wide K block) and the three W pieces of the
+//                     tile's BN output channels, into a two-stage ring;
+//   warps 2-5         converters: one A row per thread, FP32 tile from shared
+//                     memory, optional SE gate, split into the three BF16 planes
+//                     in the UMMA K-major 128-byte-swizzled layout;
+//   warp 1 / lane 0   MMA: per 16-wide K step three tcgen05.mma, plane-major:
+//                     a0 x [w0 w1 w2] (N = 3 BN), a1 x [w0 w1] (N = 2 BN) and
+//                     a2 x w0 (N = BN), so TMEM holds D0 = (a0 + a1 + a2) w0,
+//                     D1 = (a0 + a1) w1, D2 = a0 w2 side by side and each A
+//                     plane is read once per step; two accumulators, so a
+//                     tile's MMAs overlap the previous tile's epilogue;
+//   warps 6-9         epilogue: (D2 + D1) + D0, bias, activation, optional
+//                     gated / upsampled residual, 128-byte-swizzled staging
+//                     tile, TMA store.
+//
+// Every mbarrier wait is bounded by the GPU's global timer; on expiry the
+// kernel records a code in *err (or g_split_error), stops, lets its copies
+// and MMAs in flight land, frees its TMEM and returns.  No clusters, no
+// multicast: each CTA loads its own tiles from this GPU's memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace ppocr {
+
+__device__ int g_split_error = 0;
+
+namespace {
+
+constexpr int BM = 128, BK = 64, STAGES = 2, THREADS = 320, MAX_BN = 64;
+constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows x 32 columns
+constexpr int F32_STAGE = 2 * BOX_BYTES;               // 32 KB
+constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
+constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
+constexpr int W_STAGE = 3 * MAX_BN * BK * 2;           // 24 KB
+constexpr int EPI_WARPS = 4, STAGE_OUT = 32 * 128;
+constexpr int SMEM_BYTES = STAGES * (F32_STAGE + PLANES_STAGE + W_STAGE) + EPI_WARPS * STAGE_OUT + 1024;
+
+struct SplitArgs {
+    SplitGemmParams p;
+    int bn, kt, m_tiles, n_tiles, tmem_cols;
+    uint64_t wait_ns;
+};
+
+__device__ __forceinline__ void report(const SplitGemmParams& p, int code) { atomicExch(p.err ? p.err : &g_split_error, code); }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Eight consecutive values -> their three BF16 pieces, packed as 16-byte chunks.
+__device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& mid, uint4& lo) {
+    uint32_t h[4], m[4], l[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const float a = x[2 * t], b = x[2 * t + 1];
+        const float a0 = __bfloat162float(__float2bfloat16_rn(a)), b0 = __bfloat162float(__float2bfloat16_rn(b));
+        const float ar = a - a0, br = b - b0;   // exact
+        const float a1 = __bfloat162float(__float2bfloat16_rn(ar)), b1 = __bfloat162float(__float2bfloat16_rn(br));
+        h[t] = pack2(a0, b0);
+        m[t] = pack2(a1, b1);
+        l[t] = pack2(ar - a1, br - b1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    mid = make_uint4(m[0], m[1], m[2], m[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_constant__ CUtensorMap tma_a,
+                                                                const __grid_constant__ CUtensorMap tma_w,
+                                                                const __grid_constant__ CUtensorMap tma_c, SplitArgs args) {
+    const SplitGemmParams& p = args.p;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[STAGES], f32_empty[STAGES], mma_done[STAGES], planes_full[STAGES], acc_full[2],
+        acc_empty[2], drain_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sf32 = smem;
+    uint8_t* splanes = sf32 + STAGES * F32_STAGE;
+    uint8_t* sw = splanes + STAGES * PLANES_STAGE;
+    uint8_t* sout = sw + STAGES * W_STAGE;
+    const int bn = args.bn;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = args.m_tiles * args.n_tiles;
+    const uint64_t wait_ns = args.wait_ns;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&f32_empty[s], 128);
+            tc::mbar_init(&mma_done[s], 1);
+            tc::mbar_init(&planes_full[s], 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], EPI_WARPS * 32);
+        }
+        tc::mbar_init(&drain_bar, 1);
+        abort_flag = 0;
+        tc::mbar_fence_init();
+    }
+    if (warp == 0) tc::tmem_alloc(&tmem_slot, (uint32_t)args.tmem_cols);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int last_it[STAGES];
+            for (int s = 0; s < STAGES; ++s) last_it[s] = -1;
+            const uint32_t w_bytes = (uint32_t)(3 * bn * BK * 2);
+            int it = 0;
+            for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
+                const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
+                for (int kb = 0; kb < args.kt; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES) {
+                        const uint32_t par = ((it / STAGES) + 1) & 1;
+                        if (!tc::mbar_wait(&f32_empty[s], par, false, wait_ns, &abort_flag) ||
+                            !tc::mbar_wait(&mma_done[s], par, false, wait_ns, &abort_flag)) {
+                            report(p, 1);
+                            abort_flag = 1;
+                            break;
+                        }
+                    }
+                    if (p.skip_load && it == 0 && blockIdx.x == 0) continue;
+                    const int k0 = kb * BK;
+                    const bool two = k0 + 32 < p.k;
+                    tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + w_bytes);
+                    uint8_t* f = sf32 + s * F32_STAGE;
+                    tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
+                    if (two) tc::tma_load_2d(f + BOX_BYTES, &tma_a, &full[s], k0 + 32, m0);
+                    uint8_t* w = sw + s * W_STAGE;
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) tc::tma_load_2d(w + j * bn * 128, &tma_w, &full[s], k0, j * p.n_pad + n0);
+                    last_it[s] = it;
+                }
+            }
+            // Every copy issued has landed before the CTA can exit.
+            for (int s = 0; s < STAGES; ++s)
+                if (last_it[s] >= 0) tc::mbar_wait(&full[s], (last_it[s] / STAGES) & 1, false, wait_ns);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id3 = tc::idesc_bf16(BM, 3 * bn), id2 = tc::idesc_bf16(BM, 2 * bn), id1 = tc::idesc_bf16(BM, bn);
+            const uint64_t a_step = (uint64_t)(PLANE_BYTES >> 4);
+            int it = 0, ti = 0;
+            for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x, ++ti) {
+                const int b = ti & 1;
+                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false, wait_ns, &abort_flag)) {
+                    report(p, 2);
+                    abort_flag = 1;
+                    break;
+                }
+                tc::fence_after();
+                const uint32_t acc = tmem + (uint32_t)(b * 3 * bn);
+                bool ok = true;
+                for (int kb = 0; kb < args.kt; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t par = (it / STAGES) & 1;
+                    if (!tc::mbar_wait(&planes_full[s], par, false, wait_ns, &abort_flag) ||
+                        !tc::mbar_wait(&full[s], par, false, wait_ns, &abort_flag)) {
+                        report(p, 3);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after();
+                    const uint64_t ad = tc::sw128_desc(tc::smem_u32(splanes + s * PLANES_STAGE));
+                    const uint64_t bd = tc::sw128_desc(tc::smem_u32(sw + s * W_STAGE));
+                    const int rem = (p.k - kb * BK) / 16;
+                    const int nk = rem < 4 ? rem : 4;
+                    for (int kk = 0; kk < nk; ++kk) {   // +32 bytes per 16-element K step
+                        tc::mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, id3, (kb | kk) != 0 ? 1u : 0u);
+                        tc::mma_bf16(acc, ad + a_step + 2 * kk, bd + 2 * kk, id2, 1u);
+                        tc::mma_bf16(acc, ad + 2 * a_step + 2 * kk, bd + 2 * kk, id1, 1u);
+                    }
+                    tc::commit(&mma_done[s]);
+                }
+                if (!ok) break;
+                tc::commit(&acc_full[b]);
+            }
+            tc::commit(&drain_bar);
+            tc::mbar_wait(&drain_bar, 0, false, wait_ns);
+        }
+    } else if (warp < 6) {
+        // Converters: thread r owns row r of every tile.
+        const int r = threadIdx.x - 64;
+        const int swz = r & 7;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            if (abort_flag) break;
+            const int m0 = (tile / args.n_tiles) * BM;
+            const int row = m0 + r;
+            const float* grow = (p.gate && row < p.m) ? p.gate + (size_t)(row / p.rows_per_image) * p.k : nullptr;
+            bool ok = true;
+            for (int kb = 0; kb < args.kt; ++kb, ++it) {
+                const int s = it % STAGES;
+                if (!tc::mbar_wait(&full[s], (it / STAGES) & 1, true, wait_ns, &abort_flag) ||
+                    (it >= STAGES && !tc::mbar_wait(&mma_done[s], ((it / STAGES) + 1) & 1, true, wait_ns, &abort_flag))) {
+                    report(p, 4);
+                    abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const uint8_t* f = sf32 + s * F32_STAGE + r * 128;
+                uint8_t* pl = splanes + s * PLANES_STAGE + r * 128;
+                const int k0 = kb * BK;
+                const int rem = (p.k - k0) / 8;
+                const int nq = rem < 8 ? rem : 8;   // 8-value chunks that hold data
+                for (int q = 0; q < nq; ++q) {
+                    const uint8_t* fb = f + (q >> 2) * BOX_BYTES;
+                    const int c0 = (q & 3) * 2;
+                    const float4 u = *reinterpret_cast<const float4*>(fb + ((c0 ^ swz) << 4));
+                    const float4 v = *reinterpret_cast<const float4*>(fb + (((c0 + 1) ^ swz) << 4));
+                    float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+                    if (grow) {
+                        const float4 g0 = __ldg(reinterpret_cast<const float4*>(grow + k0 + q * 8));
+                        const float4 g1 = __ldg(reinterpret_cast<const float4*>(grow + k0 + q * 8 + 4));
+                        x[0] *= g0.x; x[1] *= g0.y; x[2] *= g0.z; x[3] *= g0.w;
+                        x[4] *= g1.x; x[5] *= g1.y; x[6] *= g1.z; x[7] *= g1.w;
+                    }
+                    uint4 hi, mid, lo;
+                    split8(x, hi, mid, lo);
+                    const uint32_t off = (uint32_t)((q ^ swz) << 4);
+                    *reinterpret_cast<uint4*>(pl + off) = hi;
+                    *reinterpret_cast<uint4*>(pl + PLANE_BYTES + off) = mid;
+                    *reinterpret_cast<uint4*>(pl + 2 * PLANE_BYTES + off) = lo;
+                }
+                tc::fence_proxy_async();
+                tc::mbar_arrive(&planes_full[s]);
+                tc::mbar_arrive(&f32_empty[s]);
+            }
+            if (!ok) break;
+        }
+    } else {
+        // Epilogue warps 6-9: TMEM lane quarter warp % 4.
+        const int q = warp & 3;
+        uint8_t* stage = sout + (warp - 6) * STAGE_OUT;
+        uint8_t* line = stage + lane * 128;
+        const int swz = lane & 7;
+        int ti = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+            if (abort_flag) break;
+            const int b = ti & 1;
+            const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
+            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1, true, wait_ns, &abort_flag);
+            got = __all_sync(0xffffffffu, got);
+            if (!got) {
+                if (lane == 0) report(p, 5);
+                abort_flag = 1;
+                break;
+            }
+            tc::fence_after();
+            const int row = m0 + q * 32 + lane;
+            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 3 * bn);
+            const bool live = row < p.m;
+            size_t rrow = (size_t)row;
+            const float* hrow = nullptr;
+            if (live && p.residual) {
+                if (p.res_scale > 1) {
+                    const int img_hw = p.out_h * p.out_w;
+                    const int pimg = row / img_hw, rem = row % img_hw;
+                    const int y = rem / p.out_w, x = rem % p.out_w;
+                    const int rh = p.out_h / p.res_scale, rw = p.out_w / p.res_scale;
+                    rrow = ((size_t)pimg * rh + y / p.res_scale) * rw + x / p.res_scale;
+                }
+                if (p.res_gate) hrow = p.res_gate + (size_t)(row / p.rows_per_image) * p.n;
+            }
+            for (int cb = 0; cb < bn && n0 + cb < p.n; cb += 32) {
+                const int col0 = n0 + cb;
+                uint32_t r0[32], r1[32], r2[32];
+                tc::tmem_ld16_async(tb + (uint32_t)cb, r0);
+                tc::tmem_ld16_async(tb + (uint32_t)(cb + 16), r0 + 16);
+                tc::tmem_ld16_async(tb + (uint32_t)(bn + cb), r1);
+                tc::tmem_ld16_async(tb + (uint32_t)(bn + cb + 16), r1 + 16);
+                tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb), r2);
+                tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb + 16), r2 + 16);
+                const bool full_cols = col0 + 32 <= p.n;
+                tc::tmem_wait_ld();
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float d = (__uint_as_float(r2[j]) + __uint_as_float(r1[j])) + __uint_as_float(r0[j]);
+                    const float bv = (p.bias && (full_cols || col0 + j < p.n)) ? __ldg(p.bias + col0 + j) : 0.f;
+                    o[j] = apply_act(d + bv, p.act);
+                }
+                if (live && p.residual) {
+                    const float* rp = p.residual + rrow * p.ldr + col0;
+                    if (full_cols && (p.ldr % 4) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 rv = __ldg(reinterpret_cast<const float4*>(rp + j));
+                            if (hrow) rv = f4_mul(rv, __ldg(reinterpret_cast<const float4*>(hrow + col0 + j)));
+                            o[j] += rv.x; o[j + 1] += rv.y; o[j + 2] += rv.z; o[j + 3] += rv.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j < p.n) {
+                                float rv = __ldg(rp + j);
+                                if (hrow) rv *= __ldg(hrow + col0 + j);
+                                o[j] += rv;
+                            }
+                        }
+                    }
+                }
+                if (lane == 0) tc::bulk_wait_read();
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<float4*>(line + ((c ^ swz) << 4)) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::tma_store_2d(&tma_c, stage, col0, m0 + q * 32);
+                    tc::bulk_commit();
+                }
+            }
+            tc::fence_before();
+            tc::mbar_arrive(&acc_empty[b]);
+        }
+        if (lane == 0) tc::bulk_wait_all();
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, (uint32_t)args.tmem_cols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+              uint32_t box_outer, CUtensorMapDataType type) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+
+int gemm_split_tile_n(int n) {
+    // One tile when it fits (any multiple of 16); otherwise equal tiles of whole
+    // 32-column output groups, so no TMA store box reaches the next tile.
+    const int n16 = (n + 15) / 16 * 16;
+    if (n16 <= MAX_BN) return n16;
+    const int tiles = (n16 + MAX_BN - 1) / MAX_BN;
+    const int bn = (n16 + tiles - 1) / tiles;
+    return (bn + 31) / 32 * 32;
+}
+
+bool gemm_split_supported(const SplitGemmParams& p) {
+    if (p.m <= 0 || p.n <= 0 || p.k <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k) return false;
+    if (p.k_pad % BK || p.k_pad < p.k) return false;
+    const int bn = gemm_split_tile_n(p.n);
+    if (p.n_pad < (p.n + bn - 1) / bn * bn) return false;
+    if (p.ldc % 4 || p.coff % 4 || p.ldc < p.coff + p.n) return false;
+    if (p.res_scale < 1 || (p.res_scale & (p.res_scale - 1))) return false;
+    if ((p.gate || p.res_gate) && p.rows_per_image < 1) return false;
+    return true;
+}
+
+cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
+    if (!gemm_split_supported(in) || !in.a || !in.w || !in.c) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(in.a) % 16) || (reinterpret_cast<uintptr_t>(in.w) % 16)) return cudaErrorInvalidValue;
+    float* cbase = in.c + in.coff;
+    if (reinterpret_cast<uintptr_t>(cbase) % 16) return cudaErrorInvalidValue;
+    SplitArgs a;
+    a.p = in;
+    a.bn = gemm_split_tile_n(in.n);
+    a.n_tiles = (in.n + a.bn - 1) / a.bn;
+    a.m_tiles = (in.m + BM - 1) / BM;
+    a.kt = (in.k + BK - 1) / BK;
+    // Two accumulators of 3 BN columns; an epilogue group reads up to 32
+    // columns past a D part's start, so the allocation covers 6 BN + 32.
+    int cols = 32;
+    while (cols < 6 * a.bn + 32) cols <<= 1;
+    if (cols > 512) return cudaErrorInvalidConfiguration;
+    a.tmem_cols = cols;
+    a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
+    CUtensorMap ma, mw, mc;
+    if (!make_map(&ma, in.a, (uint64_t)in.k, (uint64_t)in.m, (uint64_t)in.lda * 4, 32, BM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return cudaErrorInvalidValue;
+    if (!make_map(&mw, in.w, (uint64_t)in.k_pad, (uint64_t)3 * in.n_pad, (uint64_t)in.k_pad * 2, BK, (uint32_t)a.bn,
+                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
+        return cudaErrorInvalidValue;
+    if (!make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return cudaErrorInvalidValue;
+    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_split_kernel), SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    const int tiles = a.m_tiles * a.n_tiles;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    gemm_split_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mc, a);
+    return cudaGetLastError();
+}
+
+int gemm_split_smem_bytes() { return SMEM_BYTES; }
+
+}  // namespace ppocr

@@ -454,12 +454,9 @@ int pick_bn(int n) {
 template <int ACT, bool F32>
 cudaError_t launch_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const TcArgs& a, int grid,
                        size_t smem, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<ACT, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_LIMIT - 1024);   // headroom for the static barriers
+    {
+        cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_tc_kernel<ACT, F32>), SMEM_LIMIT - 1024);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     gemm_tc_kernel<ACT, F32><<<grid, THREADS, smem, stream>>>(ma, mb, mc, a);
     return cudaGetLastError();

@@ -219,6 +219,39 @@ struct TcEngineParams {
     uint64_t wait_ns = 0;             // pipeline wait bound (0: 2 s)
     int skip_load = 0;                // self-test only: CTA 0's first W load is never issued
 };
+// FP32-class tcgen05 GEMM over FP32 activations (gemm_split.cu): A is loaded
+// as FP32 by TMA and split into three BF16 pieces in shared memory, W comes
+// pre-split ([3][n_pad][k_pad] BF16, pack_engine_kn with planes 3), the six
+// leading products accumulate in FP32 in TMEM.  The SE gate scales A (and
+// res_gate the residual) inside the kernel.
+struct SplitGemmParams {
+    int m = 0, n = 0, k = 0;          // k % 16 == 0
+    const float* a = nullptr;         // [m][lda], lda % 4 == 0, 16-byte aligned
+    int lda = 0;
+    const float* gate = nullptr;      // A *= gate[row / rows_per_image][k] (or null)
+    int rows_per_image = 1;
+    const void* w = nullptr;          // BF16 [3][n_pad][k_pad], k_pad % 64 == 0
+    int n_pad = 0, k_pad = 0;
+    const float* bias = nullptr;      // [n] or null
+    int act = 0;
+    const float* residual = nullptr;  // [rows][ldr] FP32 added after act, nearest-upsampled by res_scale
+    int ldr = 0;
+    const float* res_gate = nullptr;  // residual *= res_gate[row / rows_per_image][col] (or null)
+    int res_scale = 1, out_h = 1, out_w = 1;
+    float* c = nullptr;               // [m][ldc] at column coff (16-byte aligned rows)
+    int ldc = 0, coff = 0;
+    int* err = nullptr;               // wait-expiry flag (null: g_split_error)
+    uint64_t wait_ns = 0;             // pipeline wait bound (0: 2 s)
+    int skip_load = 0;                // self-test only: CTA 0's first stage is never loaded
+};
+int gemm_split_tile_n(int n);         // output channels per tile (n_pad is a multiple of it)
+bool gemm_split_supported(const SplitGemmParams& p);
+cudaError_t launch_gemm_split(const SplitGemmParams& p, cudaStream_t stream);
+
+// Raises `func`'s dynamic shared memory limit to `bytes` on the current
+// device, once per device (the attribute is per device context).
+cudaError_t allow_dynamic_smem(const void* func, int bytes);
+
 int tc_engine_tile_n(int n, int planes);
 bool tc_engine_supported(const TcEngineParams& p);
 cudaError_t launch_tc_engine(const TcEngineParams& p, cudaStream_t stream);

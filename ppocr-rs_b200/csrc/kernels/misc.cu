@@ -641,11 +641,9 @@ static cudaError_t launch_head_t(const HeadParams& p, cudaStream_t stream) {
         case 16: det_head_kernel<T, 16><<<g, 128, smem, stream>>>(p); break;
         case 24: det_head_kernel<T, 24><<<g, 128, smem, stream>>>(p); break;
         case 64: {
-            static bool configured = false;
-            if (!configured) {
-                cudaError_t e = cudaFuncSetAttribute(det_head_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            {
+                cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(det_head_kernel<T, 64>), (int)smem);
                 if (e != cudaSuccess) return e;
-                configured = true;
             }
             det_head_kernel<T, 64><<<g, 128, smem, stream>>>(p);
             break;
@@ -686,14 +684,11 @@ cudaError_t launch_attention(const AttentionParams& p, cudaStream_t stream) {
     const int warps = 4;
     const size_t smem = (size_t)(2 * p.t * p.d + warps * p.d + warps * p.t) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    static bool configured[2] = {false, false};
-    const int key = p.dtype == DT_F32 ? 0 : 1;
-    if (!configured[key]) {
-        cudaError_t e = key == 0
-            ? cudaFuncSetAttribute(attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)
-            : cudaFuncSetAttribute(attention_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = p.dtype == DT_F32
+            ? allow_dynamic_smem(reinterpret_cast<const void*>(attention_kernel<float>), 200 * 1024)
+            : allow_dynamic_smem(reinterpret_cast<const void*>(attention_kernel<__nv_bfloat16>), 200 * 1024);
         if (e != cudaSuccess) return e;
-        configured[key] = true;
     }
     if (p.dtype == DT_F32) attention_kernel<float><<<p.n * p.heads, warps * 32, smem, stream>>>(p);
     else attention_kernel<__nv_bfloat16><<<p.n * p.heads, warps * 32, smem, stream>>>(p);
@@ -707,12 +702,9 @@ cudaError_t launch_softmax_ctc(const SoftmaxParams& in, cudaStream_t stream) {
     const size_t smem = ((size_t)p.classes * sizeof(float) + 15) / 16 * 16;
     constexpr size_t kStagedMax = 200 * 1024;
     if (smem <= kStagedMax) {
-        static bool configured = false;
-        if (!configured) {
-            cudaError_t e = cudaFuncSetAttribute(softmax_ctc_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)kStagedMax);
+        {
+            cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(softmax_ctc_staged_kernel), (int)kStagedMax);
             if (e != cudaSuccess) return e;
-            configured = true;
         }
         softmax_ctc_staged_kernel<<<p.rows, 512, smem, stream>>>(p);
     } else {

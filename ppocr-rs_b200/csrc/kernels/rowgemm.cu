@@ -181,11 +181,9 @@ cudaError_t launch_pair(const PairRowsParams& p, cudaStream_t stream) {
     // dependent FMA chains of each hidden unit).
     constexpr int R = 1;
     const size_t smem = ((size_t)2 * C * C + (size_t)2 * C * CO + 2 * C + CO) * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(pair_rows_kernel<T, C, CO, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(pair_rows_kernel<T, C, CO, R>), 200 * 1024);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     pair_rows_kernel<T, C, CO, R><<<(unsigned)((p.m + kRows * R - 1) / (kRows * R)), kRows, smem, stream>>>(p);
     return cudaGetLastError();
@@ -205,11 +203,9 @@ template <typename T, int N>
 cudaError_t launch_rows(const GemmParams& p, cudaStream_t stream) {
     const size_t smem = ((size_t)p.k * N + N) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidConfiguration;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(rows_gemm_kernel<T, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(rows_gemm_kernel<T, N>), 200 * 1024);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     rows_gemm_kernel<T, N><<<(unsigned)((p.m + kRows - 1) / kRows), kRows, smem, stream>>>(p);
     return cudaGetLastError();

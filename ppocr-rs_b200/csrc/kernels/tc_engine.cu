@@ -623,19 +623,15 @@ cudaError_t launch_tc_engine(const TcEngineParams& in, cudaStream_t stream) {
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
     if (planes == 1) {
-        static bool configured = false;
-        if (!configured) {
-            cudaError_t e = cudaFuncSetAttribute(tc_engine_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT - 1024);
+        {
+            cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(tc_engine_kernel<1>), SMEM_LIMIT - 1024);
             if (e != cudaSuccess) return e;
-            configured = true;
         }
         tc_engine_kernel<1><<<grid, THREADS, smem, stream>>>(mw, mc, a);
     } else {
-        static bool configured = false;
-        if (!configured) {
-            cudaError_t e = cudaFuncSetAttribute(tc_engine_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT - 1024);
+        {
+            cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(tc_engine_kernel<3>), SMEM_LIMIT - 1024);
             if (e != cudaSuccess) return e;
-            configured = true;
         }
         tc_engine_kernel<3><<<grid, THREADS, smem, stream>>>(mw, mc, a);
     }

@@ -222,6 +222,7 @@ def library() -> C.CDLL:
         "ppocr_model_tensor_count": (I, [P, C.POINTER(S)]),
         "ppocr_model_tensor_info": (I, [P, S, C.c_char_p, S, _SIZE4, C.POINTER(C.c_int)]),
         "ppocr_model_read_tensor": (I, [P, S, FP, S]),
+        "ppocr_write_seeded_weights": (I, [C.c_char_p, I, I, C.c_uint64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -245,6 +246,14 @@ def gpu_count() -> int:
     n = C.c_int(0)
     _check(library().ppocr_gpu_count(C.byref(n)))
     return n.value
+
+
+def write_seeded_weights(path: str, kind: str, size, seed: int = 0) -> str:
+    """The C++ seeded checkpoint writer (ppocr-gpu-bench --seed-weights): the
+    reference tensor layout with the benchmark configs' spec distributions."""
+    _check(library().ppocr_write_seeded_weights(str(path).encode(), 0 if kind == "det" else 1, ModelSize.parse(size),
+                                                int(seed)))
+    return str(path)
 
 
 def inspect_model(path: str, kind: str, size, input_shape: Sequence[int], precision="fp32") -> dict:

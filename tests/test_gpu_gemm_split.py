@@ -1,0 +1,67 @@
+"""The FP32-class tcgen05 split GEMM (gemm_split.cu) against float64.
+
+A and W are carried as three BF16 pieces each and the six leading products
+are accumulated in FP32 in TMEM, so the result must stay within a few FP32
+ulps of the sum of |products| of the float64 result (the same bound the
+CUDA-core FP32 kernels meet), and close to the CUDA-core kernel's output.
+Shapes cover the detector's pointwise layers (k 32..320, n 16..320), ragged
+last tiles, several N tiles, the SE gate on A and the residual.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _act(x, act):
+    if act == 1:
+        return np.maximum(x, 0)
+    if act == 3:
+        erf = np.vectorize(math.erf)
+        return 0.5 * x * (1 + erf(x / math.sqrt(2)))
+    return x
+
+
+SHAPES = [
+    # m, n, k, act, gated, residual, rows_per_image
+    (1, 16, 16, 0, False, False, 1),
+    (300, 16, 64, 0, False, False, 1),           # neck input_conv.pw: thin output
+    (1000, 64, 32, 3, True, False, 250),         # stage-0 pw1, gate spanning images within a tile
+    (2049, 32, 64, 0, False, True, 1),           # stage-0 pw2 with the residual, ragged last tile
+    (777, 96, 48, 3, True, False, 259),          # stage-1 pw1: two N tiles
+    (513, 48, 96, 0, False, True, 171),          # stage-1 pw2
+    (640, 128, 64, 1, False, False, 1),
+    (299, 320, 160, 3, False, False, 1),         # stage-3 pw1: five N tiles, three K blocks
+    (299, 160, 320, 0, False, True, 1),          # stage-3 pw2: K = 320
+    (4096, 64, 32, 0, False, False, 1),
+]
+
+
+@pytest.mark.parametrize("m,n,k,act,gated,res,rpi", SHAPES)
+def test_split_gemm_fp32_class(gpu, m, n, k, act, gated, res, rpi):
+    rng = np.random.default_rng(m * 5 + n * 3 + k)
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    w = rng.normal(0, 1 / np.sqrt(k), (n, k)).astype(np.float32)
+    b = rng.normal(0, 0.1, n).astype(np.float32)
+    g = rng.uniform(0, 1, (m // rpi, k)).astype(np.float32) if gated else None
+    r = rng.normal(0, 1, (m, n)).astype(np.float32) if res else None
+    c, used = gpu.selftest_gemm_f32(a, w, b, act, g, rpi, r, kernel=4)
+    assert used == 4
+    ag = a.astype(np.float64)
+    if gated:
+        ag = (a * np.repeat(g, rpi, axis=0)).astype(np.float64)   # the kernel gates in FP32
+    pre = ag @ w.astype(np.float64).T + b
+    ref = _act(pre, act)
+    if res:
+        ref = ref + r
+    mag = np.abs(ag) @ np.abs(w.astype(np.float64)).T + np.abs(b)
+    bound = 16 * 2.0 ** -24 * mag + (2.0 ** -24 * np.abs(r) if res else 0) + 1e-30
+    err = np.abs(c - ref)
+    assert np.all(err <= bound * 1.5 + 1e-6 * (act == 3)), f"worst {float((err / bound).max()):.2f}x the bound"
+    # Close to the CUDA-core FP32 kernel on the same inputs.
+    c2, _ = gpu.selftest_gemm_f32(a, w, b, act, g, rpi, r, kernel=1)
+    assert np.abs(c - c2).max() <= 1e-4 * max(1.0, float(np.abs(c2).max()))
+

@@ -23,7 +23,7 @@ def bf16(x):
     return (u.astype(np.uint32) << 16).view(np.float32)
 
 
-@pytest.mark.parametrize("kernel", [0, 1, 2])
+@pytest.mark.parametrize("kernel", [0, 1, 2, 3])
 def test_wait_expiry_fails_cleanly(gpu, kernel):
     with pytest.raises(P.GpuError) as info:
         gpu.selftest_wait_expiry(kernel, 20)
