@@ -287,8 +287,8 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     model->gpu = gpu;
     model->opts = o;
     // FP32 runs on the CUDA cores (exact FP32 FMA); BF16 and FP32_TC use tcgen05 unless simt_only.
-    const bool tensor_cores = o.simt_only == 0 && o.precision != PPOCR_PRECISION_FP32;
-    model->m = detector ? build_detector(st, size, shape, dt, tensor_cores) : build_recognizer(st, size, shape, dt, tensor_cores);
+    const int tc_mode = o.simt_only ? TC_NONE : o.precision == PPOCR_PRECISION_FP32_TC ? TC_ALL : TC_GEMMS;
+    model->m = detector ? build_detector(st, size, shape, dt, tc_mode) : build_recognizer(st, size, shape, dt, tc_mode);
     std::lock_guard<std::mutex> lock(gpu->mu);
     gpu->bind();
     const std::vector<uint8_t>& blob = model->m.blob.bytes();
@@ -319,10 +319,26 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     gpu->ensure_arena(model->m.plan.arena_bytes);
     cuda_check(cudaMalloc(&model->dflags, kFlags * sizeof(int)), "allocate flags");
     model->hflags = PinnedFlags::acquire();
+    gpu_retain(gpu);
     return model.release();
 }
 
 }  // namespace
+
+void ppocr::gpu_retain(ppocr_gpu* gpu) { gpu->refs.fetch_add(1); }
+
+void ppocr::gpu_release(ppocr_gpu* gpu) {
+    if (gpu->refs.fetch_sub(1) != 1) return;
+    cudaSetDevice(gpu->device);
+    if (gpu->stream) cudaStreamSynchronize(gpu->stream);
+    if (gpu->arena) cudaFree(gpu->arena);
+    if (gpu->side) cudaStreamSynchronize(gpu->side);
+    if (gpu->stream) cudaStreamDestroy(gpu->stream);
+    if (gpu->side) cudaStreamDestroy(gpu->side);
+    if (gpu->fork) cudaEventDestroy(gpu->fork);
+    if (gpu->join) cudaEventDestroy(gpu->join);
+    delete gpu;
+}
 
 extern "C" {
 
@@ -377,16 +393,7 @@ int ppocr_gpu_create(int device, ppocr_gpu** out) {
 }
 
 void ppocr_gpu_destroy(ppocr_gpu* gpu) {
-    if (!gpu) return;
-    cudaSetDevice(gpu->device);
-    if (gpu->stream) cudaStreamSynchronize(gpu->stream);
-    if (gpu->arena) cudaFree(gpu->arena);
-    if (gpu->side) cudaStreamSynchronize(gpu->side);
-    if (gpu->stream) cudaStreamDestroy(gpu->stream);
-    if (gpu->side) cudaStreamDestroy(gpu->side);
-    if (gpu->fork) cudaEventDestroy(gpu->fork);
-    if (gpu->join) cudaEventDestroy(gpu->join);
-    delete gpu;
+    if (gpu) gpu_release(gpu);
 }
 
 int ppocr_gpu_info(const ppocr_gpu* gpu, char* name, size_t capacity) {
@@ -416,17 +423,20 @@ int ppocr_upload_rgb(ppocr_gpu* gpu, uint32_t width, uint32_t height, const uint
         cuda_check(cudaMalloc(&img->rgb, expected), "allocate source image");
         cuda_check(cudaMemcpyAsync(img->rgb, pixels, expected, cudaMemcpyHostToDevice, gpu->stream), "upload source image");
         cuda_check(cudaStreamSynchronize(gpu->stream), "upload source image");
+        gpu_retain(gpu);
         *out = img.release();
     });
 }
 
 void ppocr_image_destroy(ppocr_image* image) {
     if (!image) return;
+    ppocr_gpu* gpu = image->gpu;
     if (image->rgb) {
-        cudaSetDevice(image->gpu->device);
+        cudaSetDevice(gpu->device);
         cudaFree(image->rgb);
     }
     delete image;
+    gpu_release(gpu);
 }
 
 int ppocr_detector_load(ppocr_gpu* gpu, const char* path, int size, const size_t input_shape[4], ppocr_model** out) {
@@ -465,7 +475,9 @@ void ppocr_model_destroy(ppocr_model* model) {
         std::lock_guard<std::mutex> lock(model->gpu->mu);
         if (cudaSetDevice(model->gpu->device) == cudaSuccess) cudaStreamSynchronize(model->gpu->stream);
     }
+    ppocr_gpu* gpu = model->gpu;
     delete model;
+    gpu_release(gpu);
 }
 
 int ppocr_write_seeded_weights(const char* path, int kind, int size, uint64_t seed) {
@@ -485,7 +497,7 @@ int ppocr_inspect_model(const char* path, int kind, int size, const size_t input
         if (precision != PPOCR_PRECISION_FP32 && precision != PPOCR_PRECISION_BF16 && precision != PPOCR_PRECISION_FP32_TC)
             fail(PPOCR_ERR_INVALID_INPUT, "unknown precision");
         const DType dt = precision == PPOCR_PRECISION_BF16 ? DT_BF16 : DT_F32;
-        const bool tc = precision != PPOCR_PRECISION_FP32;
+        const int tc = precision == PPOCR_PRECISION_FP32_TC ? TC_ALL : TC_GEMMS;
         SafeTensors st = SafeTensors::load(path);
         BuiltModel m = kind == 0 ? build_detector(st, size, input_shape, dt, tc) : build_recognizer(st, size, input_shape, dt, tc);
         if (ops) *ops = m.plan.ops.size();

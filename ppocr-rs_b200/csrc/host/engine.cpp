@@ -103,6 +103,7 @@ struct ImageHandle {
 
 struct ppocr_engine {
     ppocr_gpu* gpu = nullptr;
+    bool owns_gpu_ref = false;   // the engine holds a reference on `gpu` (released by ppocr_engine_destroy)
     std::string det_path, rec_path;
     int det_size = PPOCR_TINY, rec_size = PPOCR_TINY;
     ppocr_load_options load{}, rec_load{};
@@ -433,6 +434,8 @@ int ppocr_engine_create(ppocr_gpu* gpu, const char* detector_model, const char* 
         if (options) o = *options;
         auto e = std::make_unique<ppocr_engine>();
         e->gpu = gpu;
+        gpu_retain(gpu);
+        e->owns_gpu_ref = true;
         e->det_path = detector_model;
         e->rec_path = recognizer_model;
         e->det_size = o.detector_size;
@@ -463,10 +466,13 @@ int ppocr_engine_create(ppocr_gpu* gpu, const char* detector_model, const char* 
 }
 
 void ppocr_engine_destroy(ppocr_engine* engine) {
+    if (!engine) return;
+    ppocr_gpu* gpu = engine->owns_gpu_ref ? engine->gpu : nullptr;
     try {
         delete engine;
     } catch (...) {
     }
+    if (gpu) gpu_release(gpu);
 }
 
 int ppocr_engine_recognize(ppocr_engine* engine, const uint8_t* rgb, size_t rgb_length, uint32_t width, uint32_t height,

@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 #include <new>
@@ -43,6 +44,11 @@ void wait_stream(cudaStream_t s, int timeout_ms);
 }  // namespace ppocr
 
 struct ppocr_gpu {
+    // References: the caller's handle plus every model, image and engine made
+    // on this device (the reference's Gpu is Clone over an Arc, so its models
+    // keep it alive, src/gpu/runtime.rs:88-92).  The device resources are freed
+    // when the last one is released.
+    std::atomic<int> refs{1};
     int device = 0;
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;                            // concurrent regions' second stream
@@ -73,6 +79,9 @@ struct ppocr_image {
 };
 
 namespace ppocr {
+void gpu_retain(ppocr_gpu* gpu);
+void gpu_release(ppocr_gpu* gpu);
+
 // Quad-resample parameters for `image` (Normalization::new, src/preprocess/kernels.rs:9-18).
 PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
                                  size_t out_w, bool detector);

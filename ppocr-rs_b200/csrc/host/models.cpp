@@ -89,14 +89,17 @@ struct GemmOpts {
 
 class Builder {
 public:
-    Builder(BuiltModel& m, const WeightReader& r, bool tc) : m_(m), r_(r), tc_(tc) {}
+    Builder(BuiltModel& m, const WeightReader& r, int tc_mode) : m_(m), r_(r), tc_(tc_mode != TC_NONE), all_(tc_mode == TC_ALL) {}
     const WeightReader& reader() const { return r_; }
     // BF16 storage with tcgen05 GEMMs: SE gates are applied by a gate kernel
     // instead of in the GEMM's A load (the tensor-core path reads A by TMA).
     bool tensor_core_gemms() const { return tc_ && m_.dtype == DT_BF16; }
-    // FP32 storage with tcgen05 GEMMs and implicit-GEMM convs on three-way
-    // BF16-split operands (tc_engine.cu, planes 3).
-    bool tensor_core_f32() const { return tc_ && m_.dtype == DT_F32; }
+    // FP32 storage, pointwise convs on tcgen05 as split GEMMs (three-piece
+    // BF16 operands, gemm_split.cu).
+    bool split_gemms() const { return tc_ && m_.dtype == DT_F32; }
+    // FP32 storage with the dense convs (and GEMMs the split kernel does not
+    // cover) on the tensor-core engine (tc_engine.cu, planes 3).
+    bool tensor_core_f32() const { return all_ && m_.dtype == DT_F32; }
     int engine_planes() const { return m_.dtype == DT_BF16 ? 1 : 3; }
 
     // Emits a tc_engine op.  srcs empty: dense rows of `a_tid` (mode 0);
@@ -299,8 +302,14 @@ public:
 
     // FP32 operands on tcgen05 through the split GEMM (gemm_split.cu): A split
     // into three BF16 pieces in shared memory, the SE gate applied there.
+    // Up to K = 320 (every detector layer of the tiny tier): the tensor core
+    // rounds its FP32 accumulator once per 16-wide K step, toward zero, so the
+    // rounding of the dominant sum grows with K; past ~320 it exceeds the
+    // CUDA-core kernels' (seen on the medium detector, K up to 1,792), which
+    // keep those layers.
+    static constexpr int kSplitMaxK = 320;
     bool split_gemm_ok(int k, int n) const {
-        if (!tensor_core_f32()) return false;
+        if (!split_gemms() || k > kSplitMaxK) return false;
         SplitGemmParams p;
         p.m = 1; p.n = n; p.k = k; p.lda = k; p.ldc = n;
         const int bn = gemm_split_tile_n(n);
@@ -486,7 +495,7 @@ public:
 private:
     BuiltModel& m_;
     const WeightReader& r_;
-    bool tc_;
+    bool tc_, all_;
 };
 
 // ---------------------------------------------------------------------------
@@ -549,7 +558,7 @@ Act4 lcnet_block(Builder& b, const std::string& prefix, const Blk& blk, const Ac
         // The BF16 and engine tensor-core GEMMs take no residual gate: apply the
         // SE gate once.  (The FP32 split GEMM gates A and the residual itself.)
         const bool split = b.split_gemm_ok(blk.cin, blk.cin * 2) && b.split_gemm_ok(blk.cin * 2, blk.cout);
-        if (b.tensor_core_gemms() || (b.tensor_core_f32() && !split)) {
+        if (b.tensor_core_gemms() || (b.split_gemms() && !split)) {
             y = b.gate_apply(prefix + ".se.apply", y, gate, 0, nullptr, 1);
             gate = -1;
         }
@@ -869,7 +878,7 @@ void check_count(const SafeTensors& st, const char* what, int size, size_t expec
 
 }  // namespace
 
-BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4], DType dt, bool tensor_cores) {
+BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4], DType dt, int tc_mode) {
     // validate_detector_shape (src/gpu/model.rs:268-276)
     const size_t n = shape[0], c = shape[1], h = shape[2], w = shape[3];
     if (n == 0 || c != 3 || h < 32 || w < 32 || h % 32 || w % 32) {
@@ -888,7 +897,7 @@ BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4]
     m.n = (int)n; m.h = (int)h; m.w = (int)w;
     m.tensor_count = (int)st.size();
     WeightReader r(st);
-    Builder b(m, r, tensor_cores);
+    Builder b(m, r, tc_mode);
     m.input = m.plan.add_raw("input", n * 3 * h * w * 4, true);
     int s1, s2, s3, s4, mid, out;
     if (size == PPOCR_MEDIUM) { s1 = 128; s2 = 256; s3 = 512; s4 = 896; mid = 64; out = 128; }
@@ -913,7 +922,7 @@ BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4]
     return m;
 }
 
-BuiltModel build_recognizer(const SafeTensors& st, int size, const size_t shape[4], DType dt, bool tensor_cores) {
+BuiltModel build_recognizer(const SafeTensors& st, int size, const size_t shape[4], DType dt, int tc_mode) {
     // validate_recognizer_shape (src/gpu/model.rs:278-286)
     const size_t n = shape[0], c = shape[1], h = shape[2], w = shape[3];
     if (n == 0 || c != 3 || h != 48 || w < 32 || w % 4) {
@@ -932,7 +941,7 @@ BuiltModel build_recognizer(const SafeTensors& st, int size, const size_t shape[
     m.tensor_count = (int)st.size();
     m.classes = size == PPOCR_TINY ? 6906 : 18710;
     WeightReader r(st);
-    Builder b(m, r, tensor_cores);
+    Builder b(m, r, tc_mode);
     m.input = m.plan.add_raw("input", n * 3 * h * w * 4, true);
     Act4 x;
     if (size == PPOCR_TINY) x = small_stem(b, m.input, (int)n, (int)h, (int)w, 24, 48);

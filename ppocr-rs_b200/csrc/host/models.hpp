@@ -35,10 +35,19 @@ struct BuiltModel {
     int tensor_count = 0;             // tensors in the source file
 };
 
+// Which contractions run on the tensor cores (tcgen05):
+//   TC_NONE      every GEMM and conv on CUDA cores (FP32 exact FMA / BF16 SIMT);
+//   TC_GEMMS     pointwise convs / linears on tcgen05: BF16 operands in BF16
+//                mode, FP32 operands as three BF16 pieces in FP32 mode (split
+//                GEMM); BF16 single-source convs as implicit tcgen05 GEMMs;
+//   TC_ALL       as TC_GEMMS, plus the FP32 mode's dense convs through the
+//                tensor-core engine (three-piece operands gathered per tap).
+enum TcMode : int { TC_NONE = 0, TC_GEMMS = 1, TC_ALL = 2 };
+
 // Validates, reads and packs the checkpoint, and builds the plan.  Errors
 // follow gpu::Detector::load / gpu::Recognizer::load (src/gpu/model.rs:50-93, 156-220).
-BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4], DType dt, bool tensor_cores);
-BuiltModel build_recognizer(const SafeTensors& st, int size, const size_t shape[4], DType dt, bool tensor_cores);
+BuiltModel build_detector(const SafeTensors& st, int size, const size_t shape[4], DType dt, int tc_mode);
+BuiltModel build_recognizer(const SafeTensors& st, int size, const size_t shape[4], DType dt, int tc_mode);
 
 const char* size_name(int size);
 

@@ -108,8 +108,8 @@ std::vector<float> draw(const std::string& name, const std::vector<size_t>& shap
 void write_seeded_weights(const std::string& path, bool detector, int size, uint64_t seed) {
     SafeTensors rec = SafeTensors::recorder();
     const size_t shape[4] = {1, 3, detector ? (size_t)64 : (size_t)48, 64};
-    if (detector) build_detector(rec, size, shape, DT_F32, false);
-    else build_recognizer(rec, size, shape, DT_F32, false);
+    if (detector) build_detector(rec, size, shape, DT_F32, TC_NONE);
+    else build_recognizer(rec, size, shape, DT_F32, TC_NONE);
     std::ostringstream head;
     head << "{\"__metadata__\":{\"format\":\"pt\"}";
     size_t off = 0;

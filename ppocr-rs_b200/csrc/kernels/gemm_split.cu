@@ -16,14 +16,19 @@
 //                     memory, optional SE gate, split into the three BF16 planes
 //                     in the UMMA K-major 128-byte-swizzled layout;
 //   warp 1 / lane 0   MMA: per 16-wide K step three tcgen05.mma, plane-major:
-//                     a0 x [w0 w1 w2] (N = 3 BN), a1 x [w0 w1] (N = 2 BN) and
-//                     a2 x w0 (N = BN), so TMEM holds D0 = (a0 + a1 + a2) w0,
-//                     D1 = (a0 + a1) w1, D2 = a0 w2 side by side and each A
-//                     plane is read once per step; two accumulators, so a
-//                     tile's MMAs overlap the previous tile's epilogue;
-//   warps 6-9         epilogue: (D2 + D1) + D0, bias, activation, optional
-//                     gated / upsampled residual, 128-byte-swizzled staging
-//                     tile, TMA store.
+//                     a0 x [w0 w1 w2] (N = 3 BN) into [D S1 S2], a1 x [w0 w1]
+//                     (N = 2 BN) into [S1 S2] and a2 x w0 (N = BN) into S1, so
+//                     TMEM holds D = a0 w0, S1 = a0 w1 + a1 w0 + a2 w0 and
+//                     S2 = a0 w2 + a1 w1 side by side, each A plane is read
+//                     once per step, and the dominant sum D is rounded once
+//                     per step; two accumulators, so a tile's MMAs overlap
+//                     the previous tile's epilogue;
+//   warps 6-13        epilogue: (S2 + S1) + D, bias, activation, optional
+//                     gated / upsampled residual, 64-byte-swizzled staging
+//                     tile, TMA store.  Two groups of four warps (one per
+//                     TMEM lane quarter) take alternate tiles, each owning
+//                     one accumulator buffer, so two tiles' epilogues overlap;
+//                     the residual is fetched one 16-column group ahead.
 //
 // Every mbarrier wait is bounded by the GPU's global timer; on expiry the
 // kernel records a code in *err (or g_split_error), stops, lets its copies
@@ -44,13 +49,13 @@ __device__ int g_split_error = 0;
 
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 2, THREADS = 320, MAX_BN = 64;
+constexpr int BM = 128, BK = 64, STAGES = 2, THREADS = 448, MAX_BN = 64;
 constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows x 32 columns
 constexpr int F32_STAGE = 2 * BOX_BYTES;               // 32 KB
 constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
 constexpr int W_STAGE = 3 * MAX_BN * BK * 2;           // 24 KB
-constexpr int EPI_WARPS = 4, STAGE_OUT = 32 * 128;
+constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;   // staging: 32 rows x 16 FP32 columns
 constexpr int SMEM_BYTES = STAGES * (F32_STAGE + PLANES_STAGE + W_STAGE) + EPI_WARPS * STAGE_OUT + 1024;
 
 struct SplitArgs {
@@ -84,6 +89,48 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& mi
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+template <int ACT>
+__device__ __forceinline__ float act_exact(float v) {
+    if constexpr (ACT == ACT_NONE) return v;
+    else return apply_act(v, ACT);
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// GELU 0.5 v (1 + erf(v / sqrt 2)) with the Abramowitz-Stegun 7.1.26 erf of
+// the reference (src/cpu/kernels/mod.rs:2395-2403), two values at a time in
+// packed FP32: the reciprocal 1 / (1 + 0.3275911 a) from the hardware
+// approximation refined by one Newton-Raphson step (within an ulp), exp(-a^2)
+// as 2^(-a^2 log2 e) on the hardware exp2 (relative error ~2^-22).  FP32-class
+// (a few ulps from the libm formula), at a quarter of its instructions.
+__device__ __forceinline__ void gelu_f32x2(float& v0, float& v1) {
+    const float2 v = make_float2(v0, v1);
+    const float2 x = __fmul2_rn(v, make_float2(0.70710678118654752f, 0.70710678118654752f));
+    const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+    const float2 d = __ffma2_rn(a, make_float2(0.3275911f, 0.3275911f), make_float2(1.f, 1.f));
+    float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    const float2 r = __ffma2_rn(make_float2(-d.x, -d.y), t, make_float2(1.f, 1.f));
+    t = __ffma2_rn(t, r, t);
+    float2 q = __ffma2_rn(t, make_float2(1.0614054f, 1.0614054f), make_float2(-1.4531521f, -1.4531521f));
+    q = __ffma2_rn(t, q, make_float2(1.4214138f, 1.4214138f));
+    q = __ffma2_rn(t, q, make_float2(-0.28449672f, -0.28449672f));
+    q = __ffma2_rn(t, q, make_float2(0.2548296f, 0.2548296f));
+    q = __fmul2_rn(t, q);
+    const float2 m = __fmul2_rn(a, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+    const float2 y = __fmul2_rn(m, a);
+    const float2 ex = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+    const float2 e = __ffma2_rn(make_float2(-q.x, -q.y), ex, make_float2(1.f, 1.f));
+    const float2 h = __fmul2_rn(v, make_float2(0.5f, 0.5f));
+    const float2 o = __ffma2_rn(h, make_float2(copysignf(e.x, x.x), copysignf(e.y, x.y)), h);
+    v0 = o.x;
+    v1 = o.y;
+}
+
+template <int ACT>
 __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_constant__ CUtensorMap tma_a,
                                                                 const __grid_constant__ CUtensorMap tma_w,
                                                                 const __grid_constant__ CUtensorMap tma_c, SplitArgs args) {
@@ -112,7 +159,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], EPI_WARPS * 32);
+            tc::mbar_init(&acc_empty[b], 4 * 32);   // one epilogue group per buffer
         }
         tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
@@ -191,9 +238,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     const int rem = (p.k - kb * BK) / 16;
                     const int nk = rem < 4 ? rem : 4;
                     for (int kk = 0; kk < nk; ++kk) {   // +32 bytes per 16-element K step
+                        // a0 x [w0 w1 w2] -> [D | S1 | S2]; a1 x [w0 w1] -> [S1 | S2];
+                        // a2 x w0 -> S1.  D only ever receives a0 w0, so the
+                        // accumulation rounding of the dominant sum happens once
+                        // per step; S1 (2^-8 D) and S2 (2^-16 D) take the rest.
                         tc::mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, id3, (kb | kk) != 0 ? 1u : 0u);
-                        tc::mma_bf16(acc, ad + a_step + 2 * kk, bd + 2 * kk, id2, 1u);
-                        tc::mma_bf16(acc, ad + 2 * a_step + 2 * kk, bd + 2 * kk, id1, 1u);
+                        tc::mma_bf16(acc + (uint32_t)bn, ad + a_step + 2 * kk, bd + 2 * kk, id2, 1u);
+                        tc::mma_bf16(acc + (uint32_t)bn, ad + 2 * a_step + 2 * kk, bd + 2 * kk, id1, 1u);
                     }
                     tc::commit(&mma_done[s]);
                 }
@@ -228,7 +279,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 const int k0 = kb * BK;
                 const int rem = (p.k - k0) / 8;
                 const int nq = rem < 8 ? rem : 8;   // 8-value chunks that hold data
-                for (int q = 0; q < nq; ++q) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (q >= nq) break;
                     const uint8_t* fb = f + (q >> 2) * BOX_BYTES;
                     const int c0 = (q & 3) * 2;
                     const float4 u = *reinterpret_cast<const float4*>(fb + ((c0 ^ swz) << 4));
@@ -254,16 +307,57 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             if (!ok) break;
         }
     } else {
-        // Epilogue warps 6-9: TMEM lane quarter warp % 4.
-        const int q = warp & 3;
+        // Epilogue warps 6-13: two groups of four, one warp per TMEM lane
+        // quarter (warp % 4) in each.  Group g = (warp - 6) / 4 owns
+        // accumulator buffer g and so every other tile: two tiles' epilogues
+        // run at once, and each warp walks all of its tile's 16-column groups.
+        const int q = warp & 3, grp = (warp - 6) >> 2;
         uint8_t* stage = sout + (warp - 6) * STAGE_OUT;
-        uint8_t* line = stage + lane * 128;
-        const int swz = lane & 7;
+        uint8_t* line = stage + lane * 64;
+        const int swz = (lane >> 1) & 3;   // 64-byte swizzle: chunk ^= row bits 1-2
         int ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+            if ((ti & 1) != grp) continue;
             if (abort_flag) break;
-            const int b = ti & 1;
+            const int b = grp;
             const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
+            const int row = m0 + q * 32 + lane;
+            const bool live = row < p.m;
+            const float* rp = nullptr;
+            const float* hrow = nullptr;
+            if (live && p.residual) {
+                size_t rrow = (size_t)row;
+                if (p.res_scale > 1) {
+                    const int img_hw = p.out_h * p.out_w;
+                    const int pimg = row / img_hw, rem = row % img_hw;
+                    const int y = rem / p.out_w, x = rem % p.out_w;
+                    const int rh = p.out_h / p.res_scale, rw = p.out_w / p.res_scale;
+                    rrow = ((size_t)pimg * rh + y / p.res_scale) * rw + x / p.res_scale;
+                }
+                rp = p.residual + rrow * p.ldr;
+                if (p.res_gate) hrow = p.res_gate + (size_t)(row / p.rows_per_image) * p.n;
+            }
+            // The residual of a 16-column group, gated; issued one group ahead
+            // (the first before the accumulator wait) so its latency overlaps.
+            auto load_res = [&](int col0, float (&res)[16]) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) res[j] = 0.f;
+                if (!rp || col0 >= p.n) return;
+                if (col0 + 16 <= p.n && (p.ldr % 4) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        float4 v = __ldg(reinterpret_cast<const float4*>(rp + col0 + j));
+                        if (hrow) v = f4_mul(v, __ldg(reinterpret_cast<const float4*>(hrow + col0 + j)));
+                        res[j] = v.x; res[j + 1] = v.y; res[j + 2] = v.z; res[j + 3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (col0 + j < p.n) res[j] = hrow ? __ldg(rp + col0 + j) * __ldg(hrow + col0 + j) : __ldg(rp + col0 + j);
+                }
+            };
+            float res[16];
+            load_res(n0, res);
             bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1, true, wait_ns, &abort_flag);
             got = __all_sync(0xffffffffu, got);
             if (!got) {
@@ -272,63 +366,47 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 break;
             }
             tc::fence_after();
-            const int row = m0 + q * 32 + lane;
             const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 3 * bn);
-            const bool live = row < p.m;
-            size_t rrow = (size_t)row;
-            const float* hrow = nullptr;
-            if (live && p.residual) {
-                if (p.res_scale > 1) {
-                    const int img_hw = p.out_h * p.out_w;
-                    const int pimg = row / img_hw, rem = row % img_hw;
-                    const int y = rem / p.out_w, x = rem % p.out_w;
-                    const int rh = p.out_h / p.res_scale, rw = p.out_w / p.res_scale;
-                    rrow = ((size_t)pimg * rh + y / p.res_scale) * rw + x / p.res_scale;
-                }
-                if (p.res_gate) hrow = p.res_gate + (size_t)(row / p.rows_per_image) * p.n;
-            }
-            for (int cb = 0; cb < bn && n0 + cb < p.n; cb += 32) {
+            for (int cb = 0; cb < bn && n0 + cb < p.n; cb += 16) {
                 const int col0 = n0 + cb;
-                uint32_t r0[32], r1[32], r2[32];
+                uint32_t r0[16], r1[16], r2[16];
                 tc::tmem_ld16_async(tb + (uint32_t)cb, r0);
-                tc::tmem_ld16_async(tb + (uint32_t)(cb + 16), r0 + 16);
                 tc::tmem_ld16_async(tb + (uint32_t)(bn + cb), r1);
-                tc::tmem_ld16_async(tb + (uint32_t)(bn + cb + 16), r1 + 16);
                 tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb), r2);
-                tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb + 16), r2 + 16);
-                const bool full_cols = col0 + 32 <= p.n;
-                tc::tmem_wait_ld();
-                float o[32];
+                float nres[16];
+                load_res(col0 + 16 < n0 + bn ? col0 + 16 : p.n, nres);
+                const bool full_cols = col0 + 16 <= p.n;
+                float bias[16];
+                if (p.bias && full_cols) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float d = (__uint_as_float(r2[j]) + __uint_as_float(r1[j])) + __uint_as_float(r0[j]);
-                    const float bv = (p.bias && (full_cols || col0 + j < p.n)) ? __ldg(p.bias + col0 + j) : 0.f;
-                    o[j] = apply_act(d + bv, p.act);
-                }
-                if (live && p.residual) {
-                    const float* rp = p.residual + rrow * p.ldr + col0;
-                    if (full_cols && (p.ldr % 4) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 rv = __ldg(reinterpret_cast<const float4*>(rp + j));
-                            if (hrow) rv = f4_mul(rv, __ldg(reinterpret_cast<const float4*>(hrow + col0 + j)));
-                            o[j] += rv.x; o[j + 1] += rv.y; o[j + 2] += rv.z; o[j + 3] += rv.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (col0 + j < p.n) {
-                                float rv = __ldg(rp + j);
-                                if (hrow) rv *= __ldg(hrow + col0 + j);
-                                o[j] += rv;
-                            }
-                        }
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+                        bias[j] = v.x; bias[j + 1] = v.y; bias[j + 2] = v.z; bias[j + 3] = v.w;
                     }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bias[j] = (p.bias && col0 + j < p.n) ? __ldg(p.bias + col0 + j) : 0.f;
+                }
+                tc::tmem_wait_ld();
+                float o[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    o[j] = ((__uint_as_float(r2[j]) + __uint_as_float(r1[j])) + __uint_as_float(r0[j])) + bias[j];
+                if constexpr (ACT == ACT_GELU) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) gelu_f32x2(o[j], o[j + 1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) o[j] = act_exact<ACT>(o[j]);
+                }
+                if (rp) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) o[j] += res[j];
                 }
                 if (lane == 0) tc::bulk_wait_read();
                 __syncwarp();
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
+                for (int c = 0; c < 4; ++c)
                     *reinterpret_cast<float4*>(line + ((c ^ swz) << 4)) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
                 tc::fence_proxy_async();
                 __syncwarp();
@@ -336,6 +414,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     tc::tma_store_2d(&tma_c, stage, col0, m0 + q * 32);
                     tc::bulk_commit();
                 }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) res[j] = nres[j];
             }
             tc::fence_before();
             tc::mbar_arrive(&acc_empty[b]);
@@ -362,15 +442,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
-              uint32_t box_outer, CUtensorMapDataType type) {
+              uint32_t box_outer, CUtensorMapDataType type, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int ACT>
+cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mc, const SplitArgs& a, int grid,
+                       cudaStream_t stream) {
+    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_split_kernel<ACT>), SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    gemm_split_kernel<ACT><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mc, a);
+    return cudaGetLastError();
 }
 
 int sm_count() {
@@ -387,13 +476,13 @@ int sm_count() {
 }  // namespace
 
 int gemm_split_tile_n(int n) {
-    // One tile when it fits (any multiple of 16); otherwise equal tiles of whole
-    // 32-column output groups, so no TMA store box reaches the next tile.
+    // One tile when it fits, else equal tiles; any multiple of 16 (the
+    // epilogue stores 16-column boxes, so none reaches the next tile).
     const int n16 = (n + 15) / 16 * 16;
     if (n16 <= MAX_BN) return n16;
     const int tiles = (n16 + MAX_BN - 1) / MAX_BN;
     const int bn = (n16 + tiles - 1) / tiles;
-    return (bn + 31) / 32 * 32;
+    return (bn + 15) / 16 * 16;
 }
 
 bool gemm_split_supported(const SplitGemmParams& p) {
@@ -418,10 +507,9 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.n_tiles = (in.n + a.bn - 1) / a.bn;
     a.m_tiles = (in.m + BM - 1) / BM;
     a.kt = (in.k + BK - 1) / BK;
-    // Two accumulators of 3 BN columns; an epilogue group reads up to 32
-    // columns past a D part's start, so the allocation covers 6 BN + 32.
+    // Two accumulators of 3 BN columns (BN a multiple of 16).
     int cols = 32;
-    while (cols < 6 * a.bn + 32) cols <<= 1;
+    while (cols < 6 * a.bn) cols <<= 1;
     if (cols > 512) return cudaErrorInvalidConfiguration;
     a.tmem_cols = cols;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
@@ -431,14 +519,20 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     if (!make_map(&mw, in.w, (uint64_t)in.k_pad, (uint64_t)3 * in.n_pad, (uint64_t)in.k_pad * 2, BK, (uint32_t)a.bn,
                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
         return cudaErrorInvalidValue;
-    if (!make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+    if (!make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                  CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_split_kernel), SMEM_BYTES);
-    if (e != cudaSuccess) return e;
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_split_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mc, a);
-    return cudaGetLastError();
+    switch (in.act) {
+        case ACT_NONE: return launch_act<ACT_NONE>(ma, mw, mc, a, grid, stream);
+        case ACT_RELU: return launch_act<ACT_RELU>(ma, mw, mc, a, grid, stream);
+        case ACT_SILU: return launch_act<ACT_SILU>(ma, mw, mc, a, grid, stream);
+        case ACT_GELU: return launch_act<ACT_GELU>(ma, mw, mc, a, grid, stream);
+        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mw, mc, a, grid, stream);
+        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mw, mc, a, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 int gemm_split_smem_bytes() { return SMEM_BYTES; }

@@ -8,9 +8,10 @@ evaluation of the same graph at a few pixels.  This test loads the CUDA model
 with keep_tensors (every op's output kept), traces the same activations in
 the oracle at FP32 and float64, and prints per layer the normwise relative
 error of the CUDA path and of the FP32 oracle against float64, plus the map
-statistics.  It asserts the per-layer errors stay within FP32 rounding
-(relative error < 1e-4 before the head) and that the map's mean-abs error is
-within the 2e-3 bound.
+statistics.  It asserts that the rounding is FP32-class at every traced
+layer: the mean relative error (normwise, vs float64) within 3x the FP32
+oracle's own plus 1e-6, the max relative error below 1e-4, and the map's
+mean-abs error within the 2e-3 bound.
 """
 
 import numpy as np
@@ -28,16 +29,18 @@ def _rel(a, ref):
     return float(np.abs(a - ref).max()) / scale, float(np.abs(a - ref).mean()) / (float(np.abs(ref).mean()) or 1.0)
 
 
-@pytest.mark.parametrize("precision", ["fp32", "fp32tc"])
-def test_detector_spec_layer_divergence(gpu, weights_file, precision):
+@pytest.mark.parametrize("size,mode", [("tiny", "fp32"), ("tiny", "fp32simt"), ("medium", "fp32"), ("medium", "fp32simt")])
+def test_detector_spec_layer_divergence(gpu, weights_file, size, mode):
+    """mode fp32: the FP32 mode (pointwise convs on tcgen05 with three-piece
+    BF16 operands); fp32simt: the same with every contraction on CUDA cores."""
     import torch
 
-    path = weights_file("det", "tiny", "spec")
+    path = weights_file("det", size, "spec")
     x = seeded.det_batch(1, 416, 736, seed=1)
-    det = P.Detector.load(gpu, path, "tiny", x.shape, precision=precision, keep_tensors=True)
+    det = P.Detector.load(gpu, path, size, x.shape, precision="fp32", simt_only=mode == "fp32simt", keep_tensors=True)
     got = det.forward(x).values.reshape(1, 1, 416, 736)
     names = {t["name"] for t in det.tensors()}
-    orc = om.Detector(om.Weights.load(path), "tiny")
+    orc = om.Detector(om.Weights.load(path), size)
     try:
         om.TRACE = {}
         want = orc.forward(x)
@@ -48,9 +51,10 @@ def test_detector_spec_layer_divergence(gpu, weights_file, precision):
         t64 = om.TRACE
     finally:
         om.TRACE = None
-    lines = [f"{precision}: layer | CUDA max-rel mean-rel | oracle-f32 max-rel mean-rel (both vs float64)"]
+    lines = [f"{size} {mode}: layer | CUDA max-rel mean-rel | oracle-f32 max-rel mean-rel (both vs float64)"]
     first_out = None
     found = 0
+    worst = 0.0
     for key, ref in t64.items():
         cands = [key]
         if key.endswith(".out") and key.startswith("model.backbone"):
@@ -66,17 +70,24 @@ def test_detector_spec_layer_divergence(gpu, weights_file, precision):
         cr, cm = _rel(g, e)
         orr, om_ = _rel(o, e)
         lines.append(f"  {key:48s} {cr:9.2e} {cm:9.2e} | {orr:9.2e} {om_:9.2e}")
-        if first_out is None and cm > 3 * om_ and cm > 1e-6:
+        if first_out is None and cm > 3 * om_ + 1e-6:
             first_out = key
-        if key != "head.conv_down":
-            assert cr < 1e-4, f"{key}: relative error {cr} is beyond FP32 rounding"
+        worst = max(worst, cr) if key != "head.conv_down" else worst
     d = np.abs(got - want)
     de = np.abs(got - exact)
     dn = np.abs(want - exact)
     lines.append(f"  map vs FP32 oracle: max {d.max():.3g} mean {d.mean():.3g} n>2e-2 {int((d > 2e-2).sum())}")
     lines.append(f"  map vs float64:     max {de.max():.3g} mean {de.mean():.3g} n>2e-2 {int((de > 2e-2).sum())}")
     lines.append(f"  oracle vs float64:  max {dn.max():.3g} mean {dn.mean():.3g} n>2e-2 {int((dn > 2e-2).sum())}")
-    lines.append(f"  first layer whose mean relative error exceeds 3x the oracle's: {first_out}")
+    lines.append(f"  first layer whose mean relative error exceeds 3x the oracle's + 1e-6: {first_out}")
+    flips = int(((got >= 0.5) != (exact >= 0.5)).sum())
+    lines.append(f"  threshold-0.5 flips vs float64: {flips} (oracle {int(((want >= 0.5) != (exact >= 0.5)).sum())})")
     print("\n".join(lines))
     assert found >= 10, f"only {found} traced layers matched plan tensors"
+    assert worst < 1e-4, f"a layer's relative error {worst} is beyond FP32 rounding"
+    if mode == "fp32":
+        # The default FP32 mode is held to the band; the CUDA-core-only mode is
+        # printed for comparison (its sequential K=320 sums leave the band at
+        # the tiny detector's last stage).
+        assert first_out is None, f"{first_out}: mean relative error beyond 3x the FP32 oracle's"
     assert d.mean() <= 2e-3
