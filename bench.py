@@ -144,28 +144,60 @@ def _device_view(ptr, count, torch):
     return torch.as_tensor(_Ptr(), device="cuda")
 
 
-def cpu_baseline(args, shape, seconds=12.0):
-    """The oracle (CPU restatement of src/cpu/model.rs) on a bounded sample, all host threads."""
+def _cpu_forms(args, shape):
+    """The CPU restatements of the reference's CPU path for this workload, as
+    (name, forward(x), per-step sample, description) on all host threads:
+    the torch port (oracle/model.py, intra-op threads, one image per call) and,
+    for the tiny / small detector, the C++ restatement (oracle/cpu_detector.cpp,
+    -O3 -march=native -fopenmp, images spread over the threads)."""
     import torch
 
     from oracle import model as om
     from ppocr_b200 import seeded
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     w = om.Weights(seeded.make_weights(args.kind, args.size, 0, "spec"))
     m = om.Detector(w, args.size) if args.kind == "det" else om.Recognizer(w, args.size)
-    sample = 1 if args.kind == "det" else min(shape[0], 8)
-    x = _inputs(args.kind, (sample,) + tuple(shape[1:]), seed=99)
-    fwd = m.forward if args.kind == "det" else m.forward
+    forms = [("torch", m.forward, 1 if args.kind == "det" else min(shape[0], 8),
+              f"torch-CPU FP32 port of src/cpu/model.rs, {threads} intra-op threads")]
+    if args.kind == "det" and args.size in ("tiny", "small"):
+        from oracle.cpu_detector import CpuDetector
+
+        tmp = tempfile.mkdtemp(prefix="ppocr_cpu_")
+        path = os.path.join(tmp, "w.safetensors")
+        seeded.write_weights(path, args.kind, args.size, 0, "spec")
+        cpp = CpuDetector(path, args.size)
+        forms.append(("c++", lambda x: cpp.forward(x, threads), min(shape[0], max(threads, 2)),
+                      f"C++ restatement of src/cpu/model.rs (g++ -O3 -march=native -fopenmp), images over {threads} threads"))
+    return forms, threads
+
+
+def _time_form(fwd, x, seconds):
     fwd(x)
     n, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds or n < 2:
         fwd(x)
         n += 1
-    dt = time.perf_counter() - t0
-    return {"value": round(n * sample / dt, 3), "unit": "img/s" if args.kind == "det" else "crops/s",
-            "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} forwards of {sample}x{shape[1]}x{shape[2]}x{shape[3]} ({args.size}, FP32 torch-CPU oracle)"}
+    return n, time.perf_counter() - t0
+
+
+def cpu_baseline(args, shape, seconds=12.0):
+    """Both CPU restatements on a bounded sample of the workload, all host threads;
+    the faster one is the baseline (both rates are listed)."""
+    forms, threads = _cpu_forms(args, shape)
+    unit = "img/s" if args.kind == "det" else "crops/s"
+    rates = {}
+    best = None
+    for name, fwd, sample, desc in forms:
+        x = _inputs(args.kind, (sample,) + tuple(shape[1:]), seed=99)
+        n, dt = _time_form(fwd, x, seconds / len(forms))
+        rate = n * sample / dt
+        rates[name] = round(rate, 3)
+        if best is None or rate > best[0]:
+            best = (rate, f"{n} calls of {sample}x{shape[1]}x{shape[2]}x{shape[3]} ({args.size}): {desc}")
+    return {"value": round(best[0], 3), "unit": unit, "cores": threads, "kind": "port", "sample": best[1],
+            "rates": rates}
 
 
 def run_reference(args):
@@ -186,22 +218,22 @@ def run_reference(args):
         print(json.dumps(line), flush=True)
         return
     shape, name, unit, metric = _workload(args)
-    import torch
-
-    from oracle import model as om
-    from ppocr_b200 import seeded
-
-    torch.set_num_threads(os.cpu_count() or 1)
-    w = om.Weights(seeded.make_weights(args.kind, args.size, 0, "spec"))
-    m = om.Detector(w, args.size) if args.kind == "det" else om.Recognizer(w, args.size)
-    sample = min(shape[0], 2 if args.kind == "det" else 16)
-    x = _inputs(args.kind, (sample,) + tuple(shape[1:]), seed=99)
+    # The faster CPU restatement (a short probe of each), then K timed steps of it.
+    forms, threads = _cpu_forms(args, shape)
+    best = None
+    for form in forms:
+        name_f, fwd, sample_f, desc = form
+        x = _inputs(args.kind, (sample_f,) + tuple(shape[1:]), seed=99)
+        n, dt = _time_form(fwd, x, 3.0)
+        if best is None or n * sample_f / dt > best[0]:
+            best = (n * sample_f / dt, form, x)
+    _, (form_name, fwd, sample, desc), x = best
     for _ in range(max(args.warmup, 1)):
-        m.forward(x)
+        fwd(x)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        m.forward(x)
+        fwd(x)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = sample * args.steps / total
@@ -210,9 +242,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": name, "sample_per_step": sample},
-        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{sample} of the {shape[0]} inputs per step, torch-CPU FP32 restatement of "
-                                   f"src/cpu/model.rs (ppocr-cpu-bench needs a Rust toolchain, absent here)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
+                         "sample": f"{sample} of the {shape[0]} inputs per step: {desc} (the faster CPU restatement; "
+                                   f"ppocr-cpu-bench needs a Rust toolchain, absent here)"},
         "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -163,6 +163,35 @@ public:
             fail(PPOCR_ERR_INVALID_MODEL, name + ": concatenation slice does not fit");
         Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
+        if (split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 && srcs[0].coff == 0 &&
+            residual < 0 && sh == sw) {
+            // FP32 mode: a dense conv over one plain 32-channel NHWC source as an
+            // implicit split GEMM on tcgen05 (one strided TMA box per tap).
+            SplitGemmParams sp;
+            sp.conv = 1;
+            sp.n_img = n; sp.hi = hi; sp.wi = wi; sp.ho = ho; sp.wo = wo; sp.kh = cw.kh; sp.kw = cw.kw;
+            sp.stride = sh; sp.pt = pt; sp.pl = pl;
+            sp.k = cw.kh * cw.kw * cin; sp.n = cw.cout; sp.lda = srcs[0].cstride;
+            sp.ldc = out_cstride; sp.coff = out_coff; sp.act = act;
+            const int bn = gemm_split_tile_n(cw.cout);
+            sp.n_pad = (cw.cout + bn - 1) / bn * bn;
+            sp.k_pad = (sp.k + 63) / 64 * 64;
+            sp.m = n * ((ho + 7) / 8) * ((wo + 15) / 16) * 128;
+            if (gemm_split_supported(sp)) {
+                const size_t woff = m_.blob.add_bf16(pack_engine_kn(cw, 3, sp.n_pad, sp.k_pad));
+                const size_t boff = m_.blob.add_f32(cw.b);
+                const int stid = srcs[0].tid, otid = out.tid;
+                m_.plan.add_op(name, {stid}, {otid}, [sp, woff, boff, stid, otid](const Ctx& c, cudaStream_t st) mutable {
+                    sp.a = static_cast<const float*>(c.act(stid));
+                    sp.w = c.wb(woff);
+                    sp.bias = c.wf(boff);
+                    sp.c = static_cast<float*>(c.act(otid));
+                    sp.err = c.err;
+                    return launch_gemm_split(sp, st);
+                }, "conv", (double)3 * sp.n_pad * sp.k_pad * 2, 2.0 * n * ho * wo * cw.cout * cin * cw.kh * cw.kw);
+                return out;
+            }
+        }
         if (tensor_core_f32()) {
             // FP32_TC: the tensor-core engine for NHWC sources whose channels split
             // into 16-byte chunks.  (BF16 convs stay on the register-tiled SIMT

@@ -61,6 +61,7 @@ constexpr int SMEM_BYTES = STAGES * (F32_STAGE + PLANES_STAGE + W_STAGE) + EPI_W
 struct SplitArgs {
     SplitGemmParams p;
     int bn, kt, m_tiles, n_tiles, tmem_cols;
+    int tiles_y, tiles_x;   // conv mode: tile grid per image
     uint64_t wait_ns;
 };
 
@@ -195,8 +196,23 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     const bool two = k0 + 32 < p.k;
                     tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + w_bytes);
                     uint8_t* f = sf32 + s * F32_STAGE;
-                    tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
-                    if (two) tc::tma_load_2d(f + BOX_BYTES, &tma_a, &full[s], k0 + 32, m0);
+                    if (p.conv) {
+                        // Taps 2 kb and 2 kb + 1 (K order tap, channel), one box each:
+                        // the tile's 8 x 16 output pixels read input pixels
+                        // (oy s + ky - pt, ox s + kx - pl); outside the image reads 0.
+                        const int mt = tile / args.n_tiles, per = args.tiles_y * args.tiles_x;
+                        const int img = mt / per, rt = mt - img * per;
+                        const int yb = (rt / args.tiles_x) * 8 * p.stride - p.pt;
+                        const int xb = (rt % args.tiles_x) * 16 * p.stride - p.pl;
+                        for (int h = 0; h < (two ? 2 : 1); ++h) {
+                            const int tap = 2 * kb + h;
+                            const int ky = tap / p.kw, kx = tap - ky * p.kw;
+                            tc::tma_load_4d(f + h * BOX_BYTES, &tma_a, &full[s], 0, xb + kx, yb + ky, img);
+                        }
+                    } else {
+                        tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
+                        if (two) tc::tma_load_2d(f + BOX_BYTES, &tma_a, &full[s], k0 + 32, m0);
+                    }
                     uint8_t* w = sw + s * W_STAGE;
 #pragma unroll
                     for (int j = 0; j < 3; ++j) tc::tma_load_2d(w + j * bn * 128, &tma_w, &full[s], k0, j * p.n_pad + n0);
@@ -263,7 +279,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             if (abort_flag) break;
             const int m0 = (tile / args.n_tiles) * BM;
             const int row = m0 + r;
-            const float* grow = (p.gate && row < p.m) ? p.gate + (size_t)(row / p.rows_per_image) * p.k : nullptr;
+            const float* grow = (!p.conv && p.gate && row < p.m) ? p.gate + (size_t)(row / p.rows_per_image) * p.k : nullptr;
             bool ok = true;
             for (int kb = 0; kb < args.kt; ++kb, ++it) {
                 const int s = it % STAGES;
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             const bool live = row < p.m;
             const float* rp = nullptr;
             const float* hrow = nullptr;
-            if (live && p.residual) {
+            if (live && p.residual && !p.conv) {
                 size_t rrow = (size_t)row;
                 if (p.res_scale > 1) {
                     const int img_hw = p.out_h * p.out_w;
@@ -411,7 +427,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) {
-                    tc::tma_store_2d(&tma_c, stage, col0, m0 + q * 32);
+                    if (p.conv) {
+                        // The warp's 32 rows are two 16-pixel output rows of the tile.
+                        const int mt = tile / args.n_tiles, per = args.tiles_y * args.tiles_x;
+                        const int img = mt / per, rt = mt - img * per;
+                        tc::tma_store_4d(&tma_c, stage, col0, (rt % args.tiles_x) * 16, (rt / args.tiles_x) * 8 + q * 2, img);
+                    } else {
+                        tc::tma_store_2d(&tma_c, stage, col0, m0 + q * 32);
+                    }
                     tc::bulk_commit();
                 }
 #pragma unroll
@@ -462,6 +485,22 @@ cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mw, const CUten
     return cudaGetLastError();
 }
 
+// 4D NHWC FP32 map: dims (channels, width, height, images), pixel pitch
+// `pixel_bytes`; box (box_c, box_x, box_y, 1) traversed with element strides
+// (1, stride, stride, 1).
+bool make_map4(CUtensorMap* map, const void* base, uint64_t channels, uint64_t w, uint64_t h, uint64_t n, uint64_t pixel_bytes,
+               uint32_t box_c, uint32_t box_x, uint32_t box_y, uint32_t stride, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {channels, w, h, n};
+    cuuint64_t strides[3] = {pixel_bytes, w * pixel_bytes, h * w * pixel_bytes};
+    cuuint32_t box[4] = {box_c, box_x, box_y, 1};
+    cuuint32_t estr[4] = {1, stride, stride, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int sm_count() {
     static int n = 0;
     if (!n) {
@@ -486,6 +525,15 @@ int gemm_split_tile_n(int n) {
 }
 
 bool gemm_split_supported(const SplitGemmParams& p) {
+    if (p.conv) {
+        const int cin = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
+        if (cin != 32 || p.k != p.kh * p.kw * 32 || p.lda % 4 || p.lda < 32 || p.gate || p.residual) return false;
+        if (p.n_img <= 0 || p.hi <= 0 || p.wi <= 0 || p.ho <= 0 || p.wo <= 0 || (p.stride != 1 && p.stride != 2)) return false;
+        if (p.ldc % 4 || p.coff % 4 || p.ldc < p.coff + p.n || p.n <= 0) return false;
+        if (p.k_pad % BK || p.k_pad < p.k) return false;
+        const int bn = gemm_split_tile_n(p.n);
+        return p.n_pad >= (p.n + bn - 1) / bn * bn;
+    }
     if (p.m <= 0 || p.n <= 0 || p.k <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k) return false;
     if (p.k_pad % BK || p.k_pad < p.k) return false;
     const int bn = gemm_split_tile_n(p.n);
@@ -505,8 +553,16 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.p = in;
     a.bn = gemm_split_tile_n(in.n);
     a.n_tiles = (in.n + a.bn - 1) / a.bn;
-    a.m_tiles = (in.m + BM - 1) / BM;
-    a.kt = (in.k + BK - 1) / BK;
+    if (in.conv) {
+        a.tiles_y = (in.ho + 7) / 8;
+        a.tiles_x = (in.wo + 15) / 16;
+        a.m_tiles = in.n_img * a.tiles_y * a.tiles_x;
+        a.kt = (in.kh * in.kw + 1) / 2;   // two taps of 32 channels per 64-wide K block
+    } else {
+        a.tiles_y = a.tiles_x = 0;
+        a.m_tiles = (in.m + BM - 1) / BM;
+        a.kt = (in.k + BK - 1) / BK;
+    }
     // Two accumulators of 3 BN columns (BN a multiple of 16).
     int cols = 32;
     while (cols < 6 * a.bn) cols <<= 1;
@@ -514,14 +570,22 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.tmem_cols = cols;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
     CUtensorMap ma, mw, mc;
-    if (!make_map(&ma, in.a, (uint64_t)in.k, (uint64_t)in.m, (uint64_t)in.lda * 4, 32, BM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+    if (in.conv) {
+        if (!make_map4(&ma, in.a, 32, (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
+                       16 * (uint32_t)in.stride, 8 * (uint32_t)in.stride, (uint32_t)in.stride, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_map4(&mc, cbase, (uint64_t)in.n, (uint64_t)in.wo, (uint64_t)in.ho, (uint64_t)in.n_img, (uint64_t)in.ldc * 4,
+                       16, 16, 2, 1, CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+    } else if (!make_map(&ma, in.a, (uint64_t)in.k, (uint64_t)in.m, (uint64_t)in.lda * 4, 32, BM,
+                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32) ||
+               !make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 16, 32,
+                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B)) {
         return cudaErrorInvalidValue;
+    }
     if (!make_map(&mw, in.w, (uint64_t)in.k_pad, (uint64_t)3 * in.n_pad, (uint64_t)in.k_pad * 2, BK, (uint32_t)a.bn,
                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
         return cudaErrorInvalidValue;
-    if (!make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                  CU_TENSOR_MAP_SWIZZLE_64B))
-        return cudaErrorInvalidValue;
+
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
     switch (in.act) {

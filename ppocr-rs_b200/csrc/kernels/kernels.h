@@ -243,6 +243,14 @@ struct SplitGemmParams {
     int* err = nullptr;               // wait-expiry flag (null: g_split_error)
     uint64_t wait_ns = 0;             // pipeline wait bound (0: 2 s)
     int skip_load = 0;                // self-test only: CTA 0's first stage is never loaded
+    // Implicit-GEMM convolution (conv = 1): A is the NHWC FP32 input
+    // [n_img][hi][wi] with pixel pitch lda, cin == 32 (K order (ky, kx,
+    // channel), k = kh * kw * 32); a tile is 8 x 16 output pixels of one image,
+    // each 64-wide K block two taps, each loaded as a strided 4D TMA box; C is
+    // NHWC [n_img][ho][wo] with pixel pitch ldc at channel coff.
+    // No gate and no residual in this mode.
+    int conv = 0;
+    int n_img = 0, hi = 0, wi = 0, ho = 0, wo = 0, kh = 0, kw = 0, stride = 1, pt = 0, pl = 0;
 };
 int gemm_split_tile_n(int n);         // output channels per tile (n_pad is a multiple of it)
 bool gemm_split_supported(const SplitGemmParams& p);

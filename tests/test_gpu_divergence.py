@@ -8,10 +8,14 @@ evaluation of the same graph at a few pixels.  This test loads the CUDA model
 with keep_tensors (every op's output kept), traces the same activations in
 the oracle at FP32 and float64, and prints per layer the normwise relative
 error of the CUDA path and of the FP32 oracle against float64, plus the map
-statistics.  It asserts that the rounding is FP32-class at every traced
-layer: the mean relative error (normwise, vs float64) within 3x the FP32
-oracle's own plus 1e-6, the max relative error below 1e-4, and the map's
-mean-abs error within the 2e-3 bound.
+statistics.  The FP32 band of a layer is the largest error (vs the float64
+evaluation of the unperturbed input) among the FP32 oracle and three FP32
+oracle runs on the input moved by one ulp per element: at an ill-conditioned
+layer (an SE gate whose pre-activation cancels) any FP32 evaluation's error is
+of that size.  It asserts that the rounding is FP32-class at every traced
+layer: the mean relative error (normwise, vs float64) within 3x the band plus
+1e-6, the max relative error below 1e-4, and the map's mean-abs error within
+the 2e-3 bound.
 """
 
 import numpy as np
@@ -49,9 +53,17 @@ def test_detector_spec_layer_divergence(gpu, weights_file, size, mode):
         with om.compute_dtype(torch.float64):
             exact = orc.forward(x)
         t64 = om.TRACE
+        rng = np.random.default_rng(0)
+        variants = []
+        for _ in range(3):
+            sgn = rng.choice(np.array([-1.0, 1.0], np.float32), size=x.shape)
+            xp = np.nextafter(x, x + sgn * np.float32(1e30)).astype(np.float32)
+            om.TRACE = {}
+            orc.forward(xp)
+            variants.append(om.TRACE)
     finally:
         om.TRACE = None
-    lines = [f"{size} {mode}: layer | CUDA max-rel mean-rel | oracle-f32 max-rel mean-rel (both vs float64)"]
+    lines = [f"{size} {mode}: layer | CUDA max-rel mean-rel | oracle-f32 max-rel mean-rel | band mean-rel (all vs float64)"]
     first_out = None
     found = 0
     worst = 0.0
@@ -69,8 +81,9 @@ def test_detector_spec_layer_divergence(gpu, weights_file, size, mode):
         o = t32[key].numpy()
         cr, cm = _rel(g, e)
         orr, om_ = _rel(o, e)
-        lines.append(f"  {key:48s} {cr:9.2e} {cm:9.2e} | {orr:9.2e} {om_:9.2e}")
-        if first_out is None and cm > 3 * om_ + 1e-6:
+        band = max([om_] + [_rel(v[key].numpy(), e)[1] for v in variants])
+        lines.append(f"  {key:48s} {cr:9.2e} {cm:9.2e} | {orr:9.2e} {om_:9.2e} | {band:9.2e}")
+        if first_out is None and cm > 3 * band + 1e-6:
             first_out = key
         worst = max(worst, cr) if key != "head.conv_down" else worst
     d = np.abs(got - want)
@@ -79,7 +92,7 @@ def test_detector_spec_layer_divergence(gpu, weights_file, size, mode):
     lines.append(f"  map vs FP32 oracle: max {d.max():.3g} mean {d.mean():.3g} n>2e-2 {int((d > 2e-2).sum())}")
     lines.append(f"  map vs float64:     max {de.max():.3g} mean {de.mean():.3g} n>2e-2 {int((de > 2e-2).sum())}")
     lines.append(f"  oracle vs float64:  max {dn.max():.3g} mean {dn.mean():.3g} n>2e-2 {int((dn > 2e-2).sum())}")
-    lines.append(f"  first layer whose mean relative error exceeds 3x the oracle's + 1e-6: {first_out}")
+    lines.append(f"  first layer whose mean relative error exceeds 3x the band + 1e-6: {first_out}")
     flips = int(((got >= 0.5) != (exact >= 0.5)).sum())
     lines.append(f"  threshold-0.5 flips vs float64: {flips} (oracle {int(((want >= 0.5) != (exact >= 0.5)).sum())})")
     print("\n".join(lines))
@@ -89,5 +102,5 @@ def test_detector_spec_layer_divergence(gpu, weights_file, size, mode):
         # The default FP32 mode is held to the band; the CUDA-core-only mode is
         # printed for comparison (its sequential K=320 sums leave the band at
         # the tiny detector's last stage).
-        assert first_out is None, f"{first_out}: mean relative error beyond 3x the FP32 oracle's"
+        assert first_out is None, f"{first_out}: mean relative error beyond 3x the FP32 band"
     assert d.mean() <= 2e-3
