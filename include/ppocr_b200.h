@@ -197,7 +197,14 @@ int ppocr_model_device_buffers(ppocr_model* model, float** device_input, float**
 int ppocr_model_run(ppocr_model* model, void* stream);
 
 /* Waits (bounded by `timeout_ms`; <= 0 means 60 s) for the model's stream;
- * Error::Gpu on a timeout or an asynchronous device error. */
+ * Error::Gpu on a timeout or an asynchronous device error, and Error::Gpu
+ * when a tensor-core pipeline wait of the last device-resident run ran out.
+ *
+ * Every call that waits for the device does so for at most 60 s.  When that
+ * limit runs out the call fails with PPOCR_ERR_GPU while work it queued may
+ * still be running: that work may still write the call's output buffers
+ * afterwards, and the ppocr_gpu handle (with its models and images) refuses
+ * every further call with PPOCR_ERR_GPU.  Destroying the handles stays safe. */
 int ppocr_model_synchronize(ppocr_model* model, int timeout_ms);
 
 /* Recognizer only: greedy CTC on the device (replaces the argmax scan of
@@ -352,7 +359,10 @@ int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corne
  * The first call on a device looks up that array's device address (once per
  * device); make that first call before any stream capture.  All calls on a
  * device share the array: calls whose GPU work overlaps race and must be
- * serialised by the caller. */
+ * serialised by the caller.  A call that fails because the device did not
+ * finish within the wait limit may leave the kernel and the copy still
+ * writing the array and `output`; the gpu handle then refuses further calls
+ * (see ppocr_model_synchronize). */
 int ppocr_preprocess_noalloc(ppocr_gpu* gpu, const ppocr_image* image, const float corners[8], size_t content_width,
                              size_t out_h, size_t out_w, int kind, float* output);
 

@@ -32,7 +32,7 @@ std::string& last_error() {
     return message;
 }
 
-void wait_stream(cudaStream_t s, int timeout_ms) {
+void wait_stream(cudaStream_t s, int timeout_ms, ppocr_gpu* owner) {
     if (timeout_ms <= 0) timeout_ms = 60000;
     const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
     int spins = 0;
@@ -40,7 +40,12 @@ void wait_stream(cudaStream_t s, int timeout_ms) {
         cudaError_t e = cudaStreamQuery(s);
         if (e == cudaSuccess) return;
         if (e != cudaErrorNotReady) cuda_check(e, "device execution");
-        if (std::chrono::steady_clock::now() > deadline) fail(PPOCR_ERR_GPU, "device did not finish within the wait limit");
+        if (std::chrono::steady_clock::now() > deadline) {
+            // Work still queued on the device may write the caller's buffers
+            // later: the handle refuses every further call.
+            if (owner) owner->poisoned = true;
+            fail(PPOCR_ERR_GPU, "device did not finish within the wait limit");
+        }
         if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
@@ -237,7 +242,7 @@ void finish(ppocr_model* model, int checked_tid, size_t rows, size_t cols, size_
                                             model->dflags + 1, s),
                    "check output");
     cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
-    wait_stream(s, 0);
+    wait_stream(s, 0, model->gpu);
     raise_flags(model);
 }
 
@@ -603,7 +608,7 @@ int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t
             }
             cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[(chunks - 1) & 1], 0), "join download");
             cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
-            wait_stream(cs, 0);
+            wait_stream(cs, 0, model->gpu);
         } catch (...) {
             // The caller's buffers must not be touched after return.
             cudaStreamSynchronize(pp.h2d);
@@ -651,7 +656,7 @@ int ppocr_model_benchmark(ppocr_model* model, const float* input, size_t input_l
         finish(model, -1, 0);
         cudaStream_t s = model->gpu->stream;
         for (size_t i = 0; i < warmup; ++i) model->run(s);
-        wait_stream(s, 0);
+        wait_stream(s, 0, model->gpu);
         cudaEvent_t a, b;
         cuda_check(cudaEventCreate(&a), "event");
         cuda_check(cudaEventCreate(&b), "event");
@@ -659,7 +664,7 @@ int ppocr_model_benchmark(ppocr_model* model, const float* input, size_t input_l
             cuda_check(cudaEventRecord(a, s), "record");
             model->run(s);
             cuda_check(cudaEventRecord(b, s), "record");
-            wait_stream(s, 0);
+            wait_stream(s, 0, model->gpu);
             float ms = 0.f;
             cuda_check(cudaEventElapsedTime(&ms, a, b), "elapsed");
             samples_ms[i] = ms;
@@ -712,12 +717,12 @@ int ppocr_model_synchronize(ppocr_model* model, int timeout_ms) {
     return guard([&] {
         if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
         model->gpu->bind();
-        wait_stream(model->gpu->stream, timeout_ms);
+        wait_stream(model->gpu->stream, timeout_ms, model->gpu);
         // Device-resident runs on a caller stream report a tensor-core wait that
         // ran out here, once the caller's stream has completed.
         cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost,
                                    model->gpu->stream), "read flags");
-        wait_stream(model->gpu->stream, timeout_ms);
+        wait_stream(model->gpu->stream, timeout_ms, model->gpu);
         if (model->hflags[2])
             fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(model->hflags[2]) +
                                     "); the forward's results are incomplete");
@@ -783,7 +788,7 @@ void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t 
     download(model, model->m.max_prob, prob.data(), rows * 4);
     if (margins) download(model, model->m.margin, margins, rows * 4);
     cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
-    wait_stream(s, 0);
+    wait_stream(s, 0, model->gpu);
     raise_flags(model);
     // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
     for (size_t r = 0; r < rows; ++r)
@@ -919,13 +924,13 @@ int ppocr_model_read_tensor(ppocr_model* model, size_t index, float* out, size_t
         } else {
             std::vector<uint16_t> h(count);
             download(model, (int)index, h.data(), count * 2);
-            wait_stream(s, 0);
+            wait_stream(s, 0, model->gpu);
             for (size_t i = 0; i < count; ++i) {
                 const uint32_t u = (uint32_t)h[i] << 16;
                 std::memcpy(out + i, &u, 4);
             }
         }
-        wait_stream(s, 0);
+        wait_stream(s, 0, model->gpu);
     });
 }
 
@@ -949,7 +954,7 @@ int ppocr_model_profile(ppocr_model* model, size_t runs, double* op_ms) {
                     cuda_check(ops[i].fn(c, s), ops[i].name.c_str());
                     cuda_check(cudaEventRecord(ev[i + 1], s), "record");
                 }
-                wait_stream(s, 0);
+                wait_stream(s, 0, model->gpu);
                 for (size_t i = 0; i < ops.size(); ++i) {
                     float ms = 0.f;
                     cuda_check(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "elapsed");
@@ -1019,7 +1024,7 @@ int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* cod
         if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1067,7 +1072,7 @@ int ppocr_selftest_gemm(ppocr_gpu* gpu, int m, int n, int k, const float* a, con
         if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1125,7 +1130,7 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
                          : cudaMemcpyAsync(c, p.c, celems * 4, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1185,7 +1190,7 @@ int ppocr_selftest_pair_f32(ppocr_gpu* gpu, int m, int c_in, int c_out, const fl
         if (e == cudaSuccess) e = cudaMemcpyAsync(out, p.c, (size_t)m * c_out * 4, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1247,7 +1252,7 @@ int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, 
                      : cudaMemcpyAsync(out, p.out, out_elems * 4, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1312,7 +1317,7 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             if (e == cudaSuccess) e = cudaMemcpyAsync(&flag, p.err, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
             if (e == cudaSuccess) {
                 try {
-                    wait_stream(gpu->stream, 0);
+                    wait_stream(gpu->stream, 0, gpu);
                 } catch (...) {
                     cudaFree(d);
                     throw;
@@ -1365,7 +1370,7 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
         if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, (size_t)m * n * 4, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1485,7 +1490,7 @@ int ppocr_selftest_engine(ppocr_gpu* gpu, int planes, int n, int hi, int wi, int
                             : cudaMemcpyAsync(out, p.c, cbytes, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
                 cudaFree(d);
                 throw;
@@ -1543,9 +1548,11 @@ int ppocr_preprocess(ppocr_gpu* gpu, const ppocr_image* image, const float corne
         if (e == cudaSuccess) e = cudaMemcpyAsync(output, d, bytes, cudaMemcpyDeviceToHost, gpu->stream);
         if (e == cudaSuccess) {
             try {
-                wait_stream(gpu->stream, 0);
+                wait_stream(gpu->stream, 0, gpu);
             } catch (...) {
-                cudaFree(d);
+                // After a wait that ran out the kernel may still write `d`: it is
+                // left allocated rather than freed under it.
+                if (!gpu->poisoned) cudaFree(d);
                 throw;
             }
         }

@@ -38,8 +38,10 @@ int guard(F&& f) {
     }
 }
 
-// Waits for `s` with a deadline (<= 0: 60 s); Error::Gpu on expiry or a device error.
-void wait_stream(cudaStream_t s, int timeout_ms);
+// Waits for `s` with a deadline (<= 0: 60 s); Error::Gpu on expiry or a device
+// error.  On expiry `owner` (if given) is marked poisoned: its queued work may
+// still write the caller's buffers, so every later call on it fails at once.
+void wait_stream(cudaStream_t s, int timeout_ms, ppocr_gpu* owner = nullptr);
 
 }  // namespace ppocr
 
@@ -49,6 +51,7 @@ struct ppocr_gpu {
     // keep it alive, src/gpu/runtime.rs:88-92).  The device resources are freed
     // when the last one is released.
     std::atomic<int> refs{1};
+    std::atomic<bool> poisoned{false};   // a wait on this device ran out (see wait_stream)
     int device = 0;
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;                            // concurrent regions' second stream
@@ -59,7 +62,12 @@ struct ppocr_gpu {
     uint64_t arena_gen = 0;
     std::string name;
 
-    void bind() const { ppocr::cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
+    void bind() const {
+        if (poisoned)
+            ppocr::fail(PPOCR_ERR_GPU, "GPU error: an earlier call's device work did not finish within the wait limit; "
+                                       "this handle accepts no further work");
+        ppocr::cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    }
     void ensure_arena(size_t bytes) {
         if (bytes <= arena_bytes) return;
         ppocr::cuda_check(cudaStreamSynchronize(stream), "synchronize before arena growth");

@@ -489,13 +489,15 @@ public:
             p.sum = static_cast<float*>(ctx.act(sum)); p.dtype = dt;
             return launch_channel_sum(p, st);
         }, "se.pool", 0, (double)n * hw * c);
-        m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, chunks, sum, gate, w1, b1, w2, b2, alpha](const Ctx& ctx, cudaStream_t st) {
+        const int f64 = dt == DT_F32 ? 1 : 0;
+        m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, chunks, sum, gate, w1, b1, w2, b2, alpha, f64](const Ctx& ctx, cudaStream_t st) {
             SeMlpParams p;
             p.n = n; p.c = c; p.r = r; p.hw = hw; p.chunks = chunks;
             p.sum = static_cast<const float*>(ctx.act(sum));
             p.w1 = ctx.wf(w1); p.b1 = ctx.wf(b1); p.w2 = ctx.wf(w2); p.b2 = ctx.wf(b2);
             p.alpha = alpha;
             p.gate = static_cast<float*>(ctx.act(gate));
+            p.f64 = f64;
             return launch_se_mlp(p, st);
         }, "se.mlp", (double)(reduce.w.size() + expand.w.size()) * 4, 4.0 * n * c * r);
         return gate;

@@ -72,6 +72,6 @@ extern "C" int ppocr_preprocess_noalloc(ppocr_gpu* gpu, const ppocr_image* image
         cuda_check(launch_preprocess(p, gpu->stream), "preprocess");
         cuda_check(cudaMemcpyAsync(output, p.out, 3 * out_h * out_w * sizeof(float), cudaMemcpyDeviceToHost, gpu->stream),
                    "read preprocess output");
-        wait_stream(gpu->stream, 0);
+        wait_stream(gpu->stream, 0, gpu);
     });
 }

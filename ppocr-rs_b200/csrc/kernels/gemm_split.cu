@@ -49,19 +49,26 @@ __device__ int g_split_error = 0;
 
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 2, THREADS = 448, MAX_BN = 64;
+constexpr int BM = 128, BK = 64, THREADS = 448, MAX_BN = 64;
+constexpr int MAX_A = 6, PLANE_STAGES = 2;             // FP32 ring depth bound; BF16 plane ring
 constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows x 32 columns
-constexpr int F32_STAGE = 2 * BOX_BYTES;               // 32 KB
 constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
-constexpr int W_STAGE = 3 * MAX_BN * BK * 2;           // 24 KB
-constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;   // staging: 32 rows x 16 FP32 columns
-constexpr int SMEM_BYTES = STAGES * (F32_STAGE + PLANES_STAGE + W_STAGE) + EPI_WARPS * STAGE_OUT + 1024;
+constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 FP32 columns
+constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory per block
 
+// Shared memory, 1024-byte aligned pieces: [resident W] [plane ring]
+// [epilogue staging] [FP32 ring: per stage the A boxes, then (streamed) W].
 struct SplitArgs {
     SplitGemmParams p;
     int bn, kt, m_tiles, n_tiles, tmem_cols;
     int tiles_y, tiles_x;   // conv mode: tile grid per image
+    int w_resident;         // 1: one K block and one N tile, W loaded once per CTA
+    int stages;             // FP32 ring depth
+    int a_stage_bytes;      // one FP32 ring stage (A boxes + streamed W), 1024-aligned
+    int a_box_bytes;        // the A boxes of a stage (1 or 2 boxes of 16 KB)
+    int w_bytes;            // the three W pieces of one (K block, N tile)
+    int w_region;           // resident W bytes (0 when streamed), 1024-aligned
     uint64_t wait_ns;
 };
 
@@ -137,27 +144,36 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                                                                 const __grid_constant__ CUtensorMap tma_c, SplitArgs args) {
     const SplitGemmParams& p = args.p;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[STAGES], f32_empty[STAGES], mma_done[STAGES], planes_full[STAGES], acc_full[2],
-        acc_empty[2], drain_bar;
+    // full: TMA of a FP32 stage landed; f32_empty: its A rows converted;
+    // w_free: the MMAs are done with its streamed W; planes_full / planes_empty:
+    // the BF16 plane ring between converters and MMA.
+    __shared__ __align__(8) uint64_t full[MAX_A], f32_empty[MAX_A], w_free[MAX_A], planes_full[PLANE_STAGES],
+        planes_empty[PLANE_STAGES], w_ready, acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* sf32 = smem;
-    uint8_t* splanes = sf32 + STAGES * F32_STAGE;
-    uint8_t* sw = splanes + STAGES * PLANES_STAGE;
-    uint8_t* sout = sw + STAGES * W_STAGE;
+    uint8_t* sw_res = smem;
+    uint8_t* splanes = smem + args.w_region;
+    uint8_t* sout = splanes + PLANE_STAGES * PLANES_STAGE;
+    uint8_t* sring = sout + EPI_WARPS * STAGE_OUT;
+    const int S = args.stages;
     const int bn = args.bn;
+    const bool wres = args.w_resident != 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = args.m_tiles * args.n_tiles;
     const uint64_t wait_ns = args.wait_ns;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&f32_empty[s], 128);
-            tc::mbar_init(&mma_done[s], 1);
-            tc::mbar_init(&planes_full[s], 128);
+            tc::mbar_init(&w_free[s], 1);
         }
+        for (int s = 0; s < PLANE_STAGES; ++s) {
+            tc::mbar_init(&planes_full[s], 128);
+            tc::mbar_init(&planes_empty[s], 1);
+        }
+        tc::mbar_init(&w_ready, 1);
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
             tc::mbar_init(&acc_empty[b], 4 * 32);   // one epilogue group per buffer
@@ -174,18 +190,23 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
 
     if (warp == 0) {
         if (lane == 0) {
-            int last_it[STAGES];
-            for (int s = 0; s < STAGES; ++s) last_it[s] = -1;
-            const uint32_t w_bytes = (uint32_t)(3 * bn * BK * 2);
+            int last_it[MAX_A];
+            for (int s = 0; s < MAX_A; ++s) last_it[s] = -1;
+            if (wres) {
+                // One K block and one N tile: the CTA's W never changes.
+                tc::mbar_expect_tx(&w_ready, (uint32_t)args.w_bytes);
+#pragma unroll
+                for (int j = 0; j < 3; ++j) tc::tma_load_2d(sw_res + j * bn * 128, &tma_w, &w_ready, 0, j * p.n_pad);
+            }
             int it = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
                 const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    if (it >= STAGES) {
-                        const uint32_t par = ((it / STAGES) + 1) & 1;
+                    const int s = it % S;
+                    if (it >= S) {
+                        const uint32_t par = ((it / S) + 1) & 1;
                         if (!tc::mbar_wait(&f32_empty[s], par, false, wait_ns, &abort_flag) ||
-                            !tc::mbar_wait(&mma_done[s], par, false, wait_ns, &abort_flag)) {
+                            (!wres && !tc::mbar_wait(&w_free[s], par, false, wait_ns, &abort_flag))) {
                             report(p, 1);
                             abort_flag = 1;
                             break;
@@ -194,8 +215,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     if (p.skip_load && it == 0 && blockIdx.x == 0) continue;
                     const int k0 = kb * BK;
                     const bool two = k0 + 32 < p.k;
-                    tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + w_bytes);
-                    uint8_t* f = sf32 + s * F32_STAGE;
+                    uint8_t* f = sring + (size_t)s * args.a_stage_bytes;
+                    tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + (wres ? 0u : (uint32_t)args.w_bytes));
                     if (p.conv) {
                         // Taps 2 kb and 2 kb + 1 (K order tap, channel), one box each:
                         // the tile's 8 x 16 output pixels read input pixels
@@ -213,22 +234,31 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                         tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
                         if (two) tc::tma_load_2d(f + BOX_BYTES, &tma_a, &full[s], k0 + 32, m0);
                     }
-                    uint8_t* w = sw + s * W_STAGE;
+                    if (!wres) {
+                        uint8_t* w = f + args.a_box_bytes;   // after the boxes a stage can hold
 #pragma unroll
-                    for (int j = 0; j < 3; ++j) tc::tma_load_2d(w + j * bn * 128, &tma_w, &full[s], k0, j * p.n_pad + n0);
+                        for (int j = 0; j < 3; ++j) tc::tma_load_2d(w + j * bn * 128, &tma_w, &full[s], k0, j * p.n_pad + n0);
+                    }
                     last_it[s] = it;
                 }
             }
             // Every copy issued has landed before the CTA can exit.
-            for (int s = 0; s < STAGES; ++s)
-                if (last_it[s] >= 0) tc::mbar_wait(&full[s], (last_it[s] / STAGES) & 1, false, wait_ns);
+            for (int s = 0; s < S; ++s)
+                if (last_it[s] >= 0) tc::mbar_wait(&full[s], (last_it[s] / S) & 1, false, wait_ns);
+            if (wres) tc::mbar_wait(&w_ready, 0, false, wait_ns);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t id3 = tc::idesc_bf16(BM, 3 * bn), id2 = tc::idesc_bf16(BM, 2 * bn), id1 = tc::idesc_bf16(BM, bn);
             const uint64_t a_step = (uint64_t)(PLANE_BYTES >> 4);
+            const int w_off = args.a_box_bytes;
+            bool ok = !wres || tc::mbar_wait(&w_ready, 0, false, wait_ns, &abort_flag);
+            if (!ok) {
+                report(p, 6);
+                abort_flag = 1;
+            }
             int it = 0, ti = 0;
-            for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x, ++ti) {
+            for (int tile = blockIdx.x; ok && tile < total && !abort_flag; tile += gridDim.x, ++ti) {
                 const int b = ti & 1;
                 if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false, wait_ns, &abort_flag)) {
                     report(p, 2);
@@ -237,20 +267,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 }
                 tc::fence_after();
                 const uint32_t acc = tmem + (uint32_t)(b * 3 * bn);
-                bool ok = true;
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    const uint32_t par = (it / STAGES) & 1;
-                    if (!tc::mbar_wait(&planes_full[s], par, false, wait_ns, &abort_flag) ||
-                        !tc::mbar_wait(&full[s], par, false, wait_ns, &abort_flag)) {
+                    const int s = it % S, sp = it % PLANE_STAGES;
+                    if (!tc::mbar_wait(&planes_full[sp], (it / PLANE_STAGES) & 1, false, wait_ns, &abort_flag) ||
+                        (!wres && !tc::mbar_wait(&full[s], (it / S) & 1, false, wait_ns, &abort_flag))) {
                         report(p, 3);
                         abort_flag = 1;
                         ok = false;
                         break;
                     }
                     tc::fence_after();
-                    const uint64_t ad = tc::sw128_desc(tc::smem_u32(splanes + s * PLANES_STAGE));
-                    const uint64_t bd = tc::sw128_desc(tc::smem_u32(sw + s * W_STAGE));
+                    const uint64_t ad = tc::sw128_desc(tc::smem_u32(splanes + sp * PLANES_STAGE));
+                    const uint64_t bd = tc::sw128_desc(tc::smem_u32(wres ? sw_res : sring + (size_t)s * args.a_stage_bytes + w_off));
                     const int rem = (p.k - kb * BK) / 16;
                     const int nk = rem < 4 ? rem : 4;
                     for (int kk = 0; kk < nk; ++kk) {   // +32 bytes per 16-element K step
@@ -262,7 +290,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                         tc::mma_bf16(acc + (uint32_t)bn, ad + a_step + 2 * kk, bd + 2 * kk, id2, 1u);
                         tc::mma_bf16(acc + (uint32_t)bn, ad + 2 * a_step + 2 * kk, bd + 2 * kk, id1, 1u);
                     }
-                    tc::commit(&mma_done[s]);
+                    tc::commit(&planes_empty[sp]);
+                    if (!wres) tc::commit(&w_free[s]);
                 }
                 if (!ok) break;
                 tc::commit(&acc_full[b]);
@@ -282,16 +311,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             const float* grow = (!p.conv && p.gate && row < p.m) ? p.gate + (size_t)(row / p.rows_per_image) * p.k : nullptr;
             bool ok = true;
             for (int kb = 0; kb < args.kt; ++kb, ++it) {
-                const int s = it % STAGES;
-                if (!tc::mbar_wait(&full[s], (it / STAGES) & 1, true, wait_ns, &abort_flag) ||
-                    (it >= STAGES && !tc::mbar_wait(&mma_done[s], ((it / STAGES) + 1) & 1, true, wait_ns, &abort_flag))) {
+                const int s = it % S, sp = it % PLANE_STAGES;
+                if (!tc::mbar_wait(&full[s], (it / S) & 1, true, wait_ns, &abort_flag) ||
+                    (it >= PLANE_STAGES &&
+                     !tc::mbar_wait(&planes_empty[sp], ((it / PLANE_STAGES) + 1) & 1, true, wait_ns, &abort_flag))) {
                     report(p, 4);
                     abort_flag = 1;
                     ok = false;
                     break;
                 }
-                const uint8_t* f = sf32 + s * F32_STAGE + r * 128;
-                uint8_t* pl = splanes + s * PLANES_STAGE + r * 128;
+                const uint8_t* f = sring + (size_t)s * args.a_stage_bytes + r * 128;
+                uint8_t* pl = splanes + sp * PLANES_STAGE + r * 128;
                 const int k0 = kb * BK;
                 const int rem = (p.k - k0) / 8;
                 const int nq = rem < 8 ? rem : 8;   // 8-value chunks that hold data
@@ -317,7 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     *reinterpret_cast<uint4*>(pl + 2 * PLANE_BYTES + off) = lo;
                 }
                 tc::fence_proxy_async();
-                tc::mbar_arrive(&planes_full[s]);
+                tc::mbar_arrive(&planes_full[sp]);
                 tc::mbar_arrive(&f32_empty[s]);
             }
             if (!ok) break;
@@ -478,10 +508,10 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer
 
 template <int ACT>
 cudaError_t launch_act(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mc, const SplitArgs& a, int grid,
-                       cudaStream_t stream) {
-    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_split_kernel<ACT>), SMEM_BYTES);
+                       int smem, cudaStream_t stream) {
+    cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(gemm_split_kernel<ACT>), SMEM_MAX - 1024);
     if (e != cudaSuccess) return e;
-    gemm_split_kernel<ACT><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mc, a);
+    gemm_split_kernel<ACT><<<grid, THREADS, smem, stream>>>(ma, mw, mc, a);
     return cudaGetLastError();
 }
 
@@ -569,6 +599,21 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     if (cols > 512) return cudaErrorInvalidConfiguration;
     a.tmem_cols = cols;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
+    // Shared memory: the plane ring and the staging tiles are fixed; W is
+    // resident when one K block and one N tile cover the GEMM; the rest is
+    // the FP32 ring, as deep as fits (deeper rings keep more loads in flight).
+    const int align = 1024;
+    auto up = [&](int v) { return (v + align - 1) / align * align; };
+    a.w_bytes = 3 * a.bn * BK * 2;
+    a.w_resident = (a.kt == 1 && a.n_tiles == 1) ? 1 : 0;
+    a.w_region = a.w_resident ? up(a.w_bytes) : 0;
+    a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
+    a.a_stage_bytes = a.a_box_bytes + (a.w_resident ? 0 : up(a.w_bytes));
+    const int fixed = align + a.w_region + PLANE_STAGES * PLANES_STAGE + EPI_WARPS * STAGE_OUT;
+    a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
+    if (a.stages > MAX_A) a.stages = MAX_A;
+    if (a.stages < 2) return cudaErrorInvalidConfiguration;
+    const int smem = fixed + a.stages * a.a_stage_bytes;
     CUtensorMap ma, mw, mc;
     if (in.conv) {
         if (!make_map4(&ma, in.a, 32, (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
@@ -589,16 +634,15 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     const int tiles = a.m_tiles * a.n_tiles;
     const int grid = tiles < sm_count() ? tiles : sm_count();
     switch (in.act) {
-        case ACT_NONE: return launch_act<ACT_NONE>(ma, mw, mc, a, grid, stream);
-        case ACT_RELU: return launch_act<ACT_RELU>(ma, mw, mc, a, grid, stream);
-        case ACT_SILU: return launch_act<ACT_SILU>(ma, mw, mc, a, grid, stream);
-        case ACT_GELU: return launch_act<ACT_GELU>(ma, mw, mc, a, grid, stream);
-        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mw, mc, a, grid, stream);
-        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mw, mc, a, grid, stream);
+        case ACT_NONE: return launch_act<ACT_NONE>(ma, mw, mc, a, grid, smem, stream);
+        case ACT_RELU: return launch_act<ACT_RELU>(ma, mw, mc, a, grid, smem, stream);
+        case ACT_SILU: return launch_act<ACT_SILU>(ma, mw, mc, a, grid, smem, stream);
+        case ACT_GELU: return launch_act<ACT_GELU>(ma, mw, mc, a, grid, smem, stream);
+        case ACT_HSWISH: return launch_act<ACT_HSWISH>(ma, mw, mc, a, grid, smem, stream);
+        case ACT_SIGMOID: return launch_act<ACT_SIGMOID>(ma, mw, mc, a, grid, smem, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
-int gemm_split_smem_bytes() { return SMEM_BYTES; }
 
 }  // namespace ppocr

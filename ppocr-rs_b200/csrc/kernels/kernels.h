@@ -292,6 +292,7 @@ struct SeMlpParams {
     const float* b2 = nullptr;  // [c]
     float alpha = 1.f / 6.f;
     float* gate = nullptr;      // [n][c]
+    int f64 = 0;                // 1: mean and dot products accumulated in double (FP32 mode)
 };
 cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream);
 

@@ -43,17 +43,19 @@ __global__ void __launch_bounds__(256) channel_sum_kernel(PoolParams p) {
 // (SqueezeExcitation src/cpu/model.rs:486-492, VariantSqueezeExcitation 1098-1104)
 // A block serves IMG images so every weight row it streams feeds IMG dot
 // products.  Each output unit is one thread's sequential FMA chain over its
-// weight row, starting from the bias, in input order (the order of the
-// reference's scalar dot products); rows are streamed with 16-byte loads.
+// weight row, starting from the bias, in input order; rows are streamed with
+// 16-byte loads.  ACC is the accumulation type: double for the FP32 mode
+// (where a gate's pre-activation can be a near-cancelling sum of large terms,
+// so its rounding is amplified into the gated channel), float for BF16.
 // GATE = false: hid = relu(.); GATE = true: gate = hard_sigmoid(.; alpha, 0.5).
-template <int IMG, bool GATE>
-__device__ __forceinline__ void se_dot_rows(const float* __restrict__ w, const float* __restrict__ bias, const float* in,
-                                            int in_len, int out_len, float alpha, float* out, size_t out_stride, int nimg) {
+template <typename ACC, int IMG, bool GATE, typename OUT>
+__device__ __forceinline__ void se_dot_rows(const float* __restrict__ w, const float* __restrict__ bias, const ACC* in,
+                                            int in_len, int out_len, float alpha, OUT* out, size_t out_stride, int nimg) {
     const bool vec = (in_len % 4) == 0;
     for (int j = threadIdx.x; j < out_len; j += blockDim.x) {
-        float a[IMG];
+        ACC a[IMG];
 #pragma unroll
-        for (int k = 0; k < IMG; ++k) a[k] = bias[j];
+        for (int k = 0; k < IMG; ++k) a[k] = (ACC)bias[j];
         const float* row = w + (size_t)j * in_len;
         if (vec) {
             const float4* row4 = reinterpret_cast<const float4*>(row);
@@ -62,49 +64,55 @@ __device__ __forceinline__ void se_dot_rows(const float* __restrict__ w, const f
                 const float4 wv = __ldg(row4 + i4);
 #pragma unroll
                 for (int k = 0; k < IMG; ++k) {
-                    const float4 x = *reinterpret_cast<const float4*>(in + k * in_len + 4 * i4);
-                    a[k] = fmaf(wv.x, x.x, a[k]);
-                    a[k] = fmaf(wv.y, x.y, a[k]);
-                    a[k] = fmaf(wv.z, x.z, a[k]);
-                    a[k] = fmaf(wv.w, x.w, a[k]);
+                    const ACC* x = in + k * in_len + 4 * i4;
+                    a[k] = fma((ACC)wv.x, x[0], a[k]);
+                    a[k] = fma((ACC)wv.y, x[1], a[k]);
+                    a[k] = fma((ACC)wv.z, x[2], a[k]);
+                    a[k] = fma((ACC)wv.w, x[3], a[k]);
                 }
             }
         } else {
 #pragma unroll 4
             for (int i = 0; i < in_len; ++i) {
-                const float wv = __ldg(row + i);
+                const ACC wv = (ACC)__ldg(row + i);
 #pragma unroll
-                for (int k = 0; k < IMG; ++k) a[k] = fmaf(wv, in[k * in_len + i], a[k]);
+                for (int k = 0; k < IMG; ++k) a[k] = fma(wv, in[k * in_len + i], a[k]);
             }
         }
-        for (int k = 0; k < nimg; ++k)
-            out[k * out_stride + j] = GATE ? fminf(fmaxf(fmaf(a[k], alpha, 0.5f), 0.f), 1.f) : fmaxf(a[k], 0.f);
+        for (int k = 0; k < nimg; ++k) {
+            if (GATE) {
+                const float v = (float)a[k];
+                out[k * out_stride + j] = (OUT)fminf(fmaxf(fmaf(v, alpha, 0.5f), 0.f), 1.f);
+            } else {
+                out[k * out_stride + j] = (OUT)(a[k] > (ACC)0 ? a[k] : (ACC)0);
+            }
+        }
     }
 }
 
-template <int IMG>
+template <typename ACC, int IMG>
 __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
     extern __shared__ float4 sm4[];
-    float* mean = reinterpret_cast<float*>(sm4);   // [IMG][c]
-    float* hid = mean + IMG * p.c;                 // [IMG][r]
+    ACC* mean = reinterpret_cast<ACC*>(sm4);   // [IMG][c]
+    ACC* hid = mean + IMG * p.c;               // [IMG][r]
     const int img0 = blockIdx.x * IMG;
     const int nimg = min(IMG, p.n - img0);
-    const float inv = 1.f / (float)p.hw;
+    const ACC inv = (ACC)1 / (ACC)p.hw;
     for (int t = threadIdx.x; t < IMG * p.c; t += blockDim.x) {
         const int k = t / p.c, i = t % p.c;
-        float s = 0.f;
+        ACC s = 0;
         if (k < nimg) {
             const float* src = p.sum + (size_t)(img0 + k) * p.chunks * p.c + i;
 #pragma unroll 8
-            for (int ch = 0; ch < p.chunks; ++ch) s += __ldg(src + (size_t)ch * p.c);
+            for (int ch = 0; ch < p.chunks; ++ch) s += (ACC)__ldg(src + (size_t)ch * p.c);
         }
         mean[t] = s * inv;
     }
-    for (int t = threadIdx.x; t < IMG * p.r; t += blockDim.x) hid[t] = 0.f;
+    for (int t = threadIdx.x; t < IMG * p.r; t += blockDim.x) hid[t] = 0;
     __syncthreads();
-    se_dot_rows<IMG, false>(p.w1, p.b1, mean, p.c, p.r, 0.f, hid, (size_t)p.r, nimg);
+    se_dot_rows<ACC, IMG, false, ACC>(p.w1, p.b1, mean, p.c, p.r, 0.f, hid, (size_t)p.r, nimg);
     __syncthreads();
-    se_dot_rows<IMG, true>(p.w2, p.b2, hid, p.r, p.c, p.alpha, p.gate + (size_t)img0 * p.c, (size_t)p.c, nimg);
+    se_dot_rows<ACC, IMG, true, float>(p.w2, p.b2, hid, p.r, p.c, p.alpha, p.gate + (size_t)img0 * p.c, (size_t)p.c, nimg);
 }
 
 // out = x*g or x + x*g (residual_mul_in_place, src/cpu/kernels/mod.rs:777-796),
@@ -608,12 +616,18 @@ cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
     // times.  (Eight images per block, to share the recognizer's large weight
     // reads, measured twice as slow: the blocks' serial FMA chains dominate.)
     const int img = p.n <= 148 ? 1 : (p.n <= 296 ? 2 : 4);
-    const size_t smem = (size_t)img * (p.c + p.r) * sizeof(float);
+    const size_t smem = (size_t)img * (p.c + p.r) * (p.f64 ? sizeof(double) : sizeof(float));
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)((p.n + img - 1) / img);
-    if (img == 1) se_mlp_kernel<1><<<grid, 256, smem, stream>>>(p);
-    else if (img == 2) se_mlp_kernel<2><<<grid, 256, smem, stream>>>(p);
-    else se_mlp_kernel<4><<<grid, 256, smem, stream>>>(p);
+    if (p.f64) {
+        if (img == 1) se_mlp_kernel<double, 1><<<grid, 256, smem, stream>>>(p);
+        else if (img == 2) se_mlp_kernel<double, 2><<<grid, 256, smem, stream>>>(p);
+        else se_mlp_kernel<double, 4><<<grid, 256, smem, stream>>>(p);
+    } else {
+        if (img == 1) se_mlp_kernel<float, 1><<<grid, 256, smem, stream>>>(p);
+        else if (img == 2) se_mlp_kernel<float, 2><<<grid, 256, smem, stream>>>(p);
+        else se_mlp_kernel<float, 4><<<grid, 256, smem, stream>>>(p);
+    }
     return cudaGetLastError();
 }
 
