@@ -140,10 +140,12 @@ struct ppocr_model {
     bool warmed = false;
     int* dflags = nullptr;   // device flags (kFlags ints, see above)
     int* hflags = nullptr;   // pinned host copy
+    int* dcounters = nullptr;   // the plan's fused-SE arrival counters (zero between launches)
 
     ~ppocr_model() {
         if (exec) cudaGraphExecDestroy(exec);
         if (dflags) cudaFree(dflags);
+        if (dcounters) cudaFree(dcounters);
         PinnedFlags::release(hflags);
     }
 
@@ -156,6 +158,7 @@ struct ppocr_model {
         c.fork = gpu->fork;
         c.join = gpu->join;
         c.err = dflags + 2;
+        c.counters = dcounters;
         return c;
     }
     void* tensor(int tid) const { return tid < 0 ? nullptr : static_cast<char*>(gpu->arena) + m.plan.tensors[tid].offset; }
@@ -323,6 +326,11 @@ ppocr_model* load_model(ppocr_gpu* gpu, const char* path, int size, const size_t
     }
     gpu->ensure_arena(model->m.plan.arena_bytes);
     cuda_check(cudaMalloc(&model->dflags, kFlags * sizeof(int)), "allocate flags");
+    if (model->m.counter_slots > 0) {
+        cuda_check(cudaMalloc(&model->dcounters, (size_t)model->m.counter_slots * sizeof(int)), "allocate counters");
+        cuda_check(cudaMemsetAsync(model->dcounters, 0, (size_t)model->m.counter_slots * sizeof(int), gpu->stream), "clear counters");
+        cuda_check(cudaStreamSynchronize(gpu->stream), "clear counters");
+    }
     model->hflags = PinnedFlags::acquire();
     gpu_retain(gpu);
     return model.release();

@@ -41,6 +41,8 @@ struct Ctx {
     // Device flag the tensor-core kernels set when a pipeline wait runs out
     // (read back with the forward's other flags); null: their own globals.
     int* err = nullptr;
+    // Per-model arrival counters of the fused SE kernels (zero between launches).
+    int* counters = nullptr;
     void* act(int tid) const { return tid < 0 ? nullptr : arena + (*tensors)[tid].offset; }
     const float* wf(size_t off) const { return reinterpret_cast<const float*>(weights + off); }
     const void* wb(size_t off) const { return weights + off; }

@@ -483,23 +483,26 @@ public:
         const size_t w1 = m_.blob.add_f32(reduce.w), b1 = m_.blob.add_f32(reduce.b);
         const size_t w2 = m_.blob.add_f32(expand.w), b2 = m_.blob.add_f32(expand.b);
         const DType dt = m_.dtype;
-        m_.plan.add_op(name + ".pool", {xt}, {sum}, [n, c, hw, chunks, xt, sum, dt](const Ctx& ctx, cudaStream_t st) {
-            PoolParams p;
+        const int f64 = dt == DT_F32 ? 1 : 0;
+        // One launch: chunk sums, then the MLP in each image's last block.
+        const int slot = m_.counter_slots;
+        m_.counter_slots += n;
+        m_.plan.add_op(name + ".pool", {xt}, {sum, gate},
+                       [n, c, r, hw, chunks, xt, sum, gate, w1, b1, w2, b2, alpha, f64, dt, slot](const Ctx& ctx, cudaStream_t st) {
+            SePoolParams sp;
+            PoolParams& p = sp.pool;
             p.n = n; p.hw = hw; p.c = c; p.in = ctx.act(xt); p.in_cstride = c; p.chunks = chunks;
             p.sum = static_cast<float*>(ctx.act(sum)); p.dtype = dt;
-            return launch_channel_sum(p, st);
-        }, "se.pool", 0, (double)n * hw * c);
-        const int f64 = dt == DT_F32 ? 1 : 0;
-        m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, chunks, sum, gate, w1, b1, w2, b2, alpha, f64](const Ctx& ctx, cudaStream_t st) {
-            SeMlpParams p;
-            p.n = n; p.c = c; p.r = r; p.hw = hw; p.chunks = chunks;
-            p.sum = static_cast<const float*>(ctx.act(sum));
-            p.w1 = ctx.wf(w1); p.b1 = ctx.wf(b1); p.w2 = ctx.wf(w2); p.b2 = ctx.wf(b2);
-            p.alpha = alpha;
-            p.gate = static_cast<float*>(ctx.act(gate));
-            p.f64 = f64;
-            return launch_se_mlp(p, st);
-        }, "se.mlp", (double)(reduce.w.size() + expand.w.size()) * 4, 4.0 * n * c * r);
+            SeMlpParams& q = sp.mlp;
+            q.n = n; q.c = c; q.r = r; q.hw = hw; q.chunks = chunks;
+            q.sum = p.sum;
+            q.w1 = ctx.wf(w1); q.b1 = ctx.wf(b1); q.w2 = ctx.wf(w2); q.b2 = ctx.wf(b2);
+            q.alpha = alpha;
+            q.gate = static_cast<float*>(ctx.act(gate));
+            q.f64 = f64;
+            sp.counters = ctx.counters + slot;
+            return launch_se_pool_mlp(sp, st);
+        }, "se.pool", (double)(reduce.w.size() + expand.w.size()) * 4, (double)n * hw * c + 4.0 * n * c * r);
         return gate;
     }
 

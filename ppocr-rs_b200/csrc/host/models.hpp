@@ -21,6 +21,7 @@ struct BuiltModel {
     WeightBlob blob;
     int n = 0, h = 0, w = 0;          // input NCHW [n, 3, h, w]
     int input = -1;                   // FP32 NCHW input tensor
+    int counter_slots = 0;            // per-model device counters (fused SE pool + MLP), zeroed at load
     // detector
     int prob = -1, mask = -1;         // FP32 [n, h, w]; u8 [n, h, w]
     // recognizer

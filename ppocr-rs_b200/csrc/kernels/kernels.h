@@ -296,6 +296,17 @@ struct SeMlpParams {
 };
 cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream);
 
+// channel_sum and se_mlp in one launch: the last block to finish its chunk of
+// an image (a per-image arrival counter) runs that image's MLP from the chunk
+// partials, in chunk order, so the gate is the same as the two-launch form's.
+// counters: n ints, zero before the launch; the kernel leaves them zero.
+struct SePoolParams {
+    PoolParams pool;
+    SeMlpParams mlp;                  // n, c, r, hw, chunks, sum as in `pool`
+    int* counters = nullptr;
+};
+cudaError_t launch_se_pool_mlp(const SePoolParams& p, cudaStream_t stream);
+
 // out = x * g (mode 0) or x + x * g (mode 1), then + upsample(addend, add_scale)
 struct GateApplyParams {
     int n = 0, h = 0, w = 0, c = 0;

@@ -115,6 +115,58 @@ __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
     se_dot_rows<ACC, IMG, true, float>(p.w2, p.b2, hid, p.r, p.c, p.alpha, p.gate + (size_t)img0 * p.c, (size_t)p.c, nimg);
 }
 
+// channel_sum_kernel's chunk sums, then, in the last block to finish an
+// image, se_mlp_kernel's arithmetic for that image (IMG = 1).
+template <typename T, typename ACC>
+__global__ void __launch_bounds__(256) se_pool_mlp_kernel(SePoolParams sp) {
+    const PoolParams& p = sp.pool;
+    __shared__ float4 part[256];
+    __shared__ int last;
+    const int cg = p.c / 4;
+    const int rows = blockDim.x / cg;
+    const int g = threadIdx.x % cg, r = threadIdx.x / cg;
+    const int img = blockIdx.y, chunk = blockIdx.x;
+    const int per = (p.hw + p.chunks - 1) / p.chunks;
+    const int px0 = chunk * per, px1 = min(p.hw, px0 + per);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows) {
+        const T* base = static_cast<const T*>(p.in) + (size_t)img * p.hw * p.in_cstride + g * 4;
+#pragma unroll 4
+        for (int px = px0 + r; px < px1; px += rows) acc = f4_add(acc, load4(base + (size_t)px * p.in_cstride));
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (r == 0) {
+        for (int i = 1; i < rows; ++i) acc = f4_add(acc, part[i * cg + g]);
+        *reinterpret_cast<float4*>(p.sum + ((size_t)img * p.chunks + chunk) * p.c + g * 4) = acc;
+    }
+    // Publish this block's sums, then count it in; the image's last block
+    // (whichever it is) computes the gate from all chunk sums.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(sp.counters + img, 1) == p.chunks - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    extern __shared__ float4 sm4[];
+    const SeMlpParams& m = sp.mlp;
+    ACC* mean = reinterpret_cast<ACC*>(sm4);   // [c]
+    ACC* hid = mean + m.c;                     // [r]
+    const ACC inv = (ACC)1 / (ACC)m.hw;
+    for (int i = threadIdx.x; i < m.c; i += blockDim.x) {
+        ACC s = 0;
+        const float* src = p.sum + (size_t)img * p.chunks * p.c + i;
+        for (int ch = 0; ch < p.chunks; ++ch) s += (ACC)__ldcg(src + (size_t)ch * p.c);
+        mean[i] = s * inv;
+    }
+    for (int i = threadIdx.x; i < m.r; i += blockDim.x) hid[i] = 0;
+    __syncthreads();
+    se_dot_rows<ACC, 1, false, ACC>(m.w1, m.b1, mean, m.c, m.r, 0.f, hid, (size_t)m.r, 1);
+    __syncthreads();
+    se_dot_rows<ACC, 1, true, float>(m.w2, m.b2, hid, m.r, m.c, m.alpha, m.gate + (size_t)img * m.c, (size_t)m.c, 1);
+    if (threadIdx.x == 0) sp.counters[img] = 0;   // ready for the next launch
+}
+
 // out = x*g or x + x*g (residual_mul_in_place, src/cpu/kernels/mod.rs:777-796),
 // then + nearest-upsampled addend (upsample_add_nchw, src/cpu/model.rs:1265-1320).
 // I: the index type, 32-bit when the element count fits (64-bit division
@@ -627,6 +679,22 @@ cudaError_t launch_se_mlp(const SeMlpParams& p, cudaStream_t stream) {
         if (img == 1) se_mlp_kernel<float, 1><<<grid, 256, smem, stream>>>(p);
         else if (img == 2) se_mlp_kernel<float, 2><<<grid, 256, smem, stream>>>(p);
         else se_mlp_kernel<float, 4><<<grid, 256, smem, stream>>>(p);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_se_pool_mlp(const SePoolParams& p, cudaStream_t stream) {
+    const PoolParams& q = p.pool;
+    if (q.c % 4 || q.c / 4 > 256 || q.n <= 0 || q.chunks < 1 || p.mlp.r <= 0 || !p.counters) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(p.mlp.c + p.mlp.r) * (p.mlp.f64 ? sizeof(double) : sizeof(float));
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    dim3 grid((unsigned)q.chunks, (unsigned)q.n);
+    if (q.dtype == DT_F32) {
+        if (p.mlp.f64) se_pool_mlp_kernel<float, double><<<grid, 256, smem, stream>>>(p);
+        else se_pool_mlp_kernel<float, float><<<grid, 256, smem, stream>>>(p);
+    } else {
+        if (p.mlp.f64) se_pool_mlp_kernel<__nv_bfloat16, double><<<grid, 256, smem, stream>>>(p);
+        else se_pool_mlp_kernel<__nv_bfloat16, float><<<grid, 256, smem, stream>>>(p);
     }
     return cudaGetLastError();
 }
