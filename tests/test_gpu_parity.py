@@ -99,6 +99,12 @@ def test_detector_spec_weights(gpu, weights_file, size, shape, precision):
     assert flips <= 4 * (ref_flips + 1), f"{flips} threshold flips vs float64 (reference: {ref_flips})"
     beyond, ref_beyond = int((d_exact > DET_MAX_ABS).sum()), int((noise > DET_MAX_ABS).sum())
     assert beyond <= max(16, 8 * ref_beyond), f"{beyond} pixels beyond 2e-2 vs float64 (reference: {ref_beyond})"
+    if size == "tiny":
+        # Benchmark config 1 at the BASELINE bound against the float64
+        # evaluation of the reference graph (the FP32 oracle itself misses it:
+        # its own error is ~3e-2 at one pixel).  The SE gates' MLPs run in
+        # double in FP32 mode; they are where a pre-activation cancels.
+        assert d_exact.max() <= DET_MAX_ABS, f"config 1 max-abs vs float64 {d_exact.max()}"
 
 
 def _rec_check(gpu, path, size, shape, precision, seed=5):
