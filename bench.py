@@ -345,24 +345,59 @@ def cpu_baseline_e2e(tmp, seconds=12.0):
             "sample": f"{n} config-5 pages through the torch-CPU oracle pipeline"}
 
 
-def measure_rec(gpu, world, barrier, tmp, steps=10, warmup=3, batch=256):
-    """Config 4 secondary figure: medium recognizer BF16, crops/s device-timed (max over ranks)."""
+def family_roofline(model, precision, families=None):
+    """The dominant kernel family of a model's plan (per-op CUDA events, 3 runs)
+    against its roof: FLOP/s vs the BF16 tensor peak for the BF16 tcgen05 GEMMs,
+    algorithmic bytes/s vs HBM for everything else (the FP32 split GEMMs are
+    HBM-bound: three BF16 pieces per operand, six products, tensor pipe
+    ~5-10 %).  Returns (roofline dict, per-family table, ops, per-op ms)."""
+    ops = model.ops()
+    prof = model.profile(runs=3)
+    fam = {}
+    for op, ms in zip(ops, prof):
+        f = fam.setdefault(op["kind"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "launches": 0})
+        f["ms"] += ms
+        f["bytes"] += op["bytes"]
+        f["flops"] += op["flops"]
+        f["launches"] += 1
+    dom_kind = max(fam, key=lambda k: fam[k]["ms"]) if families is None else families
+    dom = fam[dom_kind]
+    hbm, tflops, peak_src = _peaks()
+    launches = dom["launches"]
+    per_launch_s = dom["ms"] / launches / 1000.0
+    if dom_kind == "gemm" and precision == "bf16":
+        achieved = dom["flops"] / launches / per_launch_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(achieved / tflops, 4)}
+    else:
+        achieved = dom["bytes"] / launches / per_launch_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4)}
+        if dom_kind == "gemm" and precision == "fp32":
+            # Tensor-pipe view of the split GEMMs: six BF16 products per FP32 MAC.
+            bf16_tf = 6 * dom["flops"] / launches / per_launch_s / 1e12
+            roof["tensor_view"] = {"achieved": round(bf16_tf, 2), "peak": tflops, "unit": "TFLOP/s (BF16, six products)",
+                                   "frac": round(bf16_tf / tflops, 4)}
+    roof.update({"kernel": dom_kind, "launches_per_step": launches, "time_share": round(dom["ms"] / sum(prof), 4),
+                 "peak_source": peak_src, "algorithmic_bytes_per_launch": round(dom["bytes"] / launches),
+                 "algorithmic_flops_per_launch": round(dom["flops"] / launches)})
+    table = {k: {"ms": round(v["ms"], 4), "launches": v["launches"],
+                 "GBps": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1),
+                 "TFLOPs": round(v["flops"] / (v["ms"] / 1000.0) / 1e12, 2)} for k, v in fam.items()}
+    return roof, table, ops, prof
+
+
+def _timed(models_inputs, steps, warmup, barrier):
+    """Device time (ms, summed over `steps`) of one step = one graph replay of
+    every model in order, each on its resident input slot, with a 256 MiB L2
+    flush before each step; CUDA events on the launching stream."""
     import torch
 
-    import ppocr_b200 as P
-    from ppocr_b200 import seeded, sharding
-
-    wpath = os.path.join(tmp, "rec_medium.safetensors")
-    seeded.write_weights(wpath, "rec", "medium", 0, "spec")
-    shape = (batch, 3, 48, 320)
-    model = P.Recognizer.load(gpu, wpath, "medium", shape, precision="bf16")
-    x = seeded.rec_batch(batch, 320, seed=2000 + int(os.environ.get("RANK", "0")))
-    din, _ = model.device_buffers()
-    _device_view(din, x.size, torch).copy_(torch.from_numpy(x.reshape(-1)))
     stream = torch.cuda.Stream()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     for _ in range(warmup):
-        model.run(stream.cuda_stream)
+        for m in models_inputs:
+            m.run(stream.cuda_stream)
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -371,22 +406,156 @@ def measure_rec(gpu, world, barrier, tmp, steps=10, warmup=3, batch=256):
         for i in range(steps):
             flush.fill_(i & 0xFF)
             starts[i].record(stream)
-            model.run(stream.cuda_stream)
+            for m in models_inputs:
+                m.run(stream.cuda_stream)
             ends[i].record(stream)
     torch.cuda.synchronize()
-    total = sharding.max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
-    ops, prof = model.ops(), model.profile(runs=3)
-    gemm = [(o, ms) for o, ms in zip(ops, prof) if o["kind"] == "gemm"]
-    g_ms = sum(ms for _, ms in gemm)
-    g_tf = sum(o["flops"] for o, _ in gemm) / (g_ms / 1000.0) / 1e12 if g_ms else 0.0
-    _, tflops, src = _peaks()
-    model.close()
     del flush
-    return {"metric": "rec crops/s @48x320 (medium recognizer, batch 256/GPU)", "value": round(batch * world * steps / (total / 1000.0), 2),
-            "unit": "crops/s", "ms_per_step": round(total / steps, 4), "dtype": "bf16",
-            "gemm_roofline": {"bound": "tensor", "achieved": round(g_tf, 2), "peak": tflops, "unit": "TFLOP/s",
-                              "frac": round(g_tf / tflops, 4), "time_share": round(g_ms / sum(prof), 4),
-                              "peak_source": src}}
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+
+def _load_resident(P, gpu, path, kind, size, shape, precision, x, shared=None):
+    import torch
+
+    M = P.Detector if kind == "det" else P.Recognizer
+    model = M.load(gpu, path, size, shape, precision=precision) if kind == "det" else \
+        M.load(gpu, path, size, shape, precision=precision, shared_weights=shared)
+    din, _ = model.device_buffers()
+    _device_view(din, x.size, torch).copy_(torch.from_numpy(np.ascontiguousarray(x).reshape(-1)))
+    return model
+
+
+def _cpu_rate(kind, size, shape, seconds=3.0):
+    """The faster CPU restatement (torch port, C++ for tiny / small detectors)
+    on a small sample of this configuration, all host threads."""
+    class A:
+        pass
+
+    a = A()
+    a.kind, a.size = kind, size
+    forms, threads = _cpu_forms(a, shape)
+    best = None
+    for name, fwd, sample, desc in forms:
+        x = _inputs(kind, (sample,) + tuple(shape[1:]), seed=99)
+        n, dt = _time_form(fwd, x, seconds / len(forms))
+        rate = n * sample / dt
+        if best is None or rate > best["value"]:
+            best = {"value": round(rate, 3), "unit": "img/s" if kind == "det" else "crops/s", "cores": threads,
+                    "kind": "port", "sample": f"{n} calls of {sample}x{shape[1]}x{shape[2]}x{shape[3]}: {desc}"}
+    return best
+
+
+def measure_config(gpu, world, rank, barrier, tmp, kind, size, batch, precision, text, steps=10, warmup=3, cpu=False):
+    """Configs 3 (small / medium detector, batch 32 per GPU, text-like pages)
+    and the like: device throughput with inputs resident (max over ranks), the
+    dominant family's roofline, and (rank 0 of a 1-GPU run) the CPU rate."""
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded, sharding
+
+    path = os.path.join(tmp, f"{kind}_{size}.safetensors")
+    if not os.path.exists(path):
+        seeded.write_weights(path, kind, size, 0, "spec")
+    shape = (batch, 3, 416, 736) if kind == "det" else (batch, 3, 48, 320)
+    x = seeded.det_batch(batch, 416, 736, seed=3000 + rank, text=text) if kind == "det" else \
+        seeded.rec_batch(batch, 320, seed=3000 + rank)
+    model = _load_resident(P, gpu, path, kind, size, shape, precision, x)
+    total = sharding.max_over_ranks(_timed([model], steps, warmup, barrier))
+    roof, table, _, _ = family_roofline(model, precision)
+    model.close()
+    unit = "img/s" if kind == "det" else "crops/s"
+    out = {"metric": f"{kind} {unit} @{shape[2]}x{shape[3]} ({size}, batch {batch}/GPU{', text-like pages' if text else ''})",
+           "value": round(batch * world * steps / (total / 1000.0), 2), "unit": unit,
+           "ms_per_step": round(total / steps, 4), "dtype": "f32" if precision == "fp32" else "bf16",
+           "roofline": roof, "families": table}
+    if cpu and rank == 0 and world == 1:
+        out["cpu_baseline"] = _cpu_rate(kind, size, shape)
+    return out
+
+
+def measure_latency_b1(gpu, tmp, kind, size, precision, warmup=5, runs=30, cpu=False):
+    """Configs 1 / 2 as the reference's bench reports them (src/bin/benchmark.rs:
+    303-320): batch 1, `warmup` untimed and `runs` timed forwards on the resident
+    input (Detector::benchmark), average / p50 / p90 / p95 in ms."""
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded
+
+    path = os.path.join(tmp, f"{kind}_{size}.safetensors")
+    if not os.path.exists(path):
+        seeded.write_weights(path, kind, size, 0, "spec")
+    shape = (1, 3, 416, 736) if kind == "det" else (1, 3, 48, 320)
+    x = seeded.det_batch(1, 416, 736, seed=1) if kind == "det" else seeded.rec_batch(1, 320, seed=1)
+    M = P.Detector if kind == "det" else P.Recognizer
+    model = M.load(gpu, path, size, shape, precision=precision)
+    samples = sorted(1000.0 * t for t in model.benchmark(x, warmup, runs))   # seconds -> ms
+    roof, _, _, _ = family_roofline(model, precision)
+    model.close()
+    pct = lambda q: samples[int(round((len(samples) - 1) * q))]
+    avg = sum(samples) / len(samples)
+    out = {"metric": f"{kind} latency @{shape[2]}x{shape[3]} ({size}, batch 1)", "average_ms": round(avg, 4),
+           "p50_ms": round(pct(0.5), 4), "p90_ms": round(pct(0.9), 4), "p95_ms": round(pct(0.95), 4),
+           "throughput": round(1000.0 / avg, 2), "unit": "img/s" if kind == "det" else "crops/s", "runs": runs,
+           "warmup": warmup, "dtype": "f32" if precision == "fp32" else "bf16", "roofline": roof}
+    if cpu:
+        out["cpu_baseline"] = _cpu_rate(kind, size, shape)
+    return out
+
+
+def measure_config4(gpu, world, rank, barrier, tmp, crops=4096, batch=256, steps=3, warmup=2, cpu=False):
+    """Config 4: 4096 crops per GPU, widths drawn uniformly from {160, 320, 480},
+    bucketed by width into batches of 256, medium recognizer in BF16.  One step
+    runs every batch of the rank's crops (one graph replay each, inputs
+    resident); value = crops of all ranks / (max over ranks of the step time)."""
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded, sharding
+
+    path = os.path.join(tmp, "rec_medium.safetensors")
+    if not os.path.exists(path):
+        seeded.write_weights(path, "rec", "medium", 0, "spec")
+    rng = np.random.default_rng(4000 + rank)
+    widths = rng.choice([160, 320, 480], size=crops)
+    runs, models, shared = [], [], None
+    counts = {}
+    for wdt in (160, 320, 480):
+        count = int((widths == wdt).sum())
+        counts[wdt] = count
+        if count == 0:
+            continue
+        x = seeded.rec_batch(batch, wdt, seed=5000 + rank + wdt)
+        m = _load_resident(P, gpu, path, "rec", "medium", (batch, 3, 48, wdt), "bf16", x, shared)
+        shared = shared or m
+        models.append(m)
+        runs += [m] * ((count + batch - 1) // batch)
+    total = sharding.max_over_ranks(_timed(runs, steps, warmup, barrier))
+    roof, table, _, _ = family_roofline(models[len(models) // 2], "bf16")
+    for m in models:
+        m.close()
+    out = {"metric": "rec crops/s (medium, 4096 crops/GPU, widths {160,320,480} bucketed into batches of 256)",
+           "value": round(crops * world * steps / (total / 1000.0), 2), "unit": "crops/s",
+           "ms_per_step": round(total / steps, 3), "batches_per_step": len(runs), "crops_per_width": counts,
+           "dtype": "bf16", "roofline_w320": roof, "families_w320": table}
+    if cpu and rank == 0 and world == 1:
+        out["cpu_baseline"] = _cpu_rate("rec", "medium", (batch, 3, 48, 320))
+    return out
+
+
+def measure_rec(gpu, world, barrier, tmp, steps=10, warmup=3, batch=256):
+    """Medium recognizer BF16 at width 320, batch 256: crops/s device-timed (max
+    over ranks), the tcgen05 GEMM family against the BF16 tensor peak."""
+    import ppocr_b200 as P
+    from ppocr_b200 import seeded, sharding
+
+    path = os.path.join(tmp, "rec_medium.safetensors")
+    if not os.path.exists(path):
+        seeded.write_weights(path, "rec", "medium", 0, "spec")
+    shape = (batch, 3, 48, 320)
+    x = seeded.rec_batch(batch, 320, seed=2000 + int(os.environ.get("RANK", "0")))
+    model = _load_resident(P, gpu, path, "rec", "medium", shape, "bf16", x)
+    total = sharding.max_over_ranks(_timed([model], steps, warmup, barrier))
+    roof, table, _, _ = family_roofline(model, "bf16", families="gemm")
+    model.close()
+    return {"metric": "rec crops/s @48x320 (medium recognizer, batch 256/GPU)",
+            "value": round(batch * world * steps / (total / 1000.0), 2), "unit": "crops/s",
+            "ms_per_step": round(total / steps, 4), "dtype": "bf16", "gemm_roofline": roof, "families": table}
 
 
 def run_e2e(args):
@@ -501,51 +670,14 @@ def run_b200(args):
     finite = bool(torch.isfinite(out).all().item())
 
     # Per-kernel timing (events around every op) for the roofline.
-    ops = model.ops()
-    prof = model.profile(runs=3)
-    fam = {}
-    for op, ms in zip(ops, prof):
-        f = fam.setdefault(op["kind"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "launches": 0})
-        f["ms"] += ms
-        f["bytes"] += op["bytes"]
-        f["flops"] += op["flops"]
-        f["launches"] += 1
-    dom_kind = max(fam, key=lambda k: fam[k]["ms"])
-    dom = fam[dom_kind]
-    hbm, tflops, peak_src = _peaks()
-    launches = dom["launches"]
-    per_launch_ms = dom["ms"] / launches
-    tensor_bound = dom_kind == "gemm" and precision == "bf16"
-    if tensor_bound:
-        achieved = dom["flops"] / launches / (per_launch_ms / 1000.0) / 1e12
-        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
-                "frac": round(achieved / tflops, 4)}
-    else:
-        achieved = dom["bytes"] / launches / (per_launch_ms / 1000.0) / 1e9
-        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(achieved / hbm, 4)}
+    roof, table, ops, prof = family_roofline(model, precision)
+    dom_kind = roof["kernel"]
     top = sorted(zip(ops, prof), key=lambda t: -t[1])[:8]
     roof["top_ops"] = [{"op": o["name"], "kind": o["kind"], "ms": round(ms, 4),
                         "GBps": round(o["bytes"] / (ms / 1000.0) / 1e9, 1),
                         "TFLOPs": round(o["flops"] / (ms / 1000.0) / 1e12, 2)} for o, ms in top]
-    roof.update({"kernel": dom_kind, "launches_per_step": launches, "time_share": round(dom["ms"] / sum(prof), 4),
-                 "peak_source": peak_src, "traffic": None,
-                 "algorithmic_bytes_per_launch": round(dom["bytes"] / launches),
-                 "families": {k: {"ms": round(v["ms"], 4), "launches": v["launches"],
-                                  "GBps": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1)} for k, v in fam.items()}})
-    if precision == "fp32":
-        # The FP32 mode's GEMMs and convs run on the CUDA cores: their ceiling is
-        # the FP32 FMA rate, measured here on the same GPU (no driver figure covers it).
-        fma, fma2 = gpu.measure_fp32_peak()
-        simt_peak = max(fma, fma2)
-        achieved_tf = dom["flops"] / launches / (per_launch_ms / 1000.0) / 1e12
-        total_flops = sum(o["flops"] for o in ops)
-        roof["simt_roofline"] = {
-            "bound": "fp32", "kernel": dom_kind, "achieved": round(achieved_tf, 2), "peak": round(simt_peak, 2),
-            "unit": "TFLOP/s", "frac": round(achieved_tf / simt_peak, 4),
-            "peak_source": "measured on this GPU (ppocr_measure_fp32_peak: FMA chains, no memory traffic)",
-            "forward_tflops": round(total_flops / (sum(prof) / 1000.0) / 1e12, 2),
-            "forward_frac": round(total_flops / (sum(prof) / 1000.0) / 1e12 / simt_peak, 4)}
+    roof["families"] = table
+    roof["traffic"] = None
     traffic_path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(traffic_path):
         try:
@@ -592,9 +724,18 @@ def run_b200(args):
     secondary = None
     if args.kind == "det" and not args.no_secondary:
         model.close()
+        cpu_ok = not args.no_cpu_baseline
         secondary = {"rec": measure_rec(gpu, world, barrier, tmp),
-                     "e2e_pages": measure_e2e(gpu, 8, 4, 2, world, rank, barrier, tmp),
-                     "e2e_pages_rec_bf16": measure_e2e(gpu, 8, 4, 2, world, rank, barrier, tmp, rec_precision="bf16")}
+                     "config4_rec": measure_config4(gpu, world, rank, barrier, tmp, cpu=cpu_ok),
+                     "config3_small_det": measure_config(gpu, world, rank, barrier, tmp, "det", "small", 32, "fp32", True,
+                                                         cpu=cpu_ok),
+                     "config3_medium_det": measure_config(gpu, world, rank, barrier, tmp, "det", "medium", 32, "fp32", True,
+                                                          steps=5, cpu=cpu_ok),
+                     "e2e_pages": measure_e2e(gpu, 8, 10, 2, world, rank, barrier, tmp),
+                     "e2e_pages_rec_bf16": measure_e2e(gpu, 8, 10, 2, world, rank, barrier, tmp, rec_precision="bf16")}
+        if rank == 0:
+            secondary["config1_det_b1"] = measure_latency_b1(gpu, tmp, "det", "tiny", "fp32")
+            secondary["config2_rec_b1"] = measure_latency_b1(gpu, tmp, "rec", "tiny", "fp32", cpu=cpu_ok and world == 1)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

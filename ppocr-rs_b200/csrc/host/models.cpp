@@ -484,6 +484,29 @@ public:
         const size_t w2 = m_.blob.add_f32(expand.w), b2 = m_.blob.add_f32(expand.b);
         const DType dt = m_.dtype;
         const int f64 = dt == DT_F32 ? 1 : 0;
+        const double mlp_bytes = (double)(reduce.w.size() + expand.w.size()) * 4;
+        if ((double)n * mlp_bytes > 8e6) {
+            // Large batches of wide SE blocks (the recognizers at batch 256): a
+            // separate MLP launch in which each block serves several images and
+            // streams the weights once for them.
+            m_.plan.add_op(name + ".pool", {xt}, {sum}, [n, c, hw, chunks, xt, sum, dt](const Ctx& ctx, cudaStream_t st) {
+                PoolParams p;
+                p.n = n; p.hw = hw; p.c = c; p.in = ctx.act(xt); p.in_cstride = c; p.chunks = chunks;
+                p.sum = static_cast<float*>(ctx.act(sum)); p.dtype = dt;
+                return launch_channel_sum(p, st);
+            }, "se.pool", 0, (double)n * hw * c);
+            m_.plan.add_op(name + ".mlp", {sum}, {gate}, [n, c, r, hw, chunks, sum, gate, w1, b1, w2, b2, alpha, f64](const Ctx& ctx, cudaStream_t st) {
+                SeMlpParams p;
+                p.n = n; p.c = c; p.r = r; p.hw = hw; p.chunks = chunks;
+                p.sum = static_cast<const float*>(ctx.act(sum));
+                p.w1 = ctx.wf(w1); p.b1 = ctx.wf(b1); p.w2 = ctx.wf(w2); p.b2 = ctx.wf(b2);
+                p.alpha = alpha;
+                p.gate = static_cast<float*>(ctx.act(gate));
+                p.f64 = f64;
+                return launch_se_mlp(p, st);
+            }, "se.mlp", mlp_bytes, 4.0 * n * c * r);
+            return gate;
+        }
         // One launch: chunk sums, then the MLP in each image's last block.
         const int slot = m_.counter_slots;
         m_.counter_slots += n;

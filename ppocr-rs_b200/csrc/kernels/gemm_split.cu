@@ -74,23 +74,31 @@ struct SplitArgs {
 
 __device__ __forceinline__ void report(const SplitGemmParams& p, int code) { atomicExch(p.err ? p.err : &g_split_error, code); }
 
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
 
-// Eight consecutive values -> their three BF16 pieces, packed as 16-byte chunks.
+// Eight consecutive values -> their three BF16 pieces, packed as 16-byte
+// chunks.  A is split by truncation: x0 = the top 8 significant bits of x (its
+// upper 16 bits), x1 = the top 8 of r = x - x0 (exact), x2 = r - x1 (exact,
+// at most 8 significant bits, so a BF16 holds it exactly): x0 + x1 + x2 == x
+// with no rounding, |x1| < 2^-7 |x|, |x2| < 2^-15 |x|.  With the weights split
+// to nearest on the host (|w1| <= 2^-9 |w|, |w2| <= 2^-18 |w|), the three
+// dropped products are below 2^-24 of |x w|.  Packed FP32 subtractions; each
+// BF16 pair is the upper halves of two FP32 words (one byte permute).
 __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& mid, uint4& lo) {
     uint32_t h[4], m[4], l[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        const float a = x[2 * t], b = x[2 * t + 1];
-        const float a0 = __bfloat162float(__float2bfloat16_rn(a)), b0 = __bfloat162float(__float2bfloat16_rn(b));
-        const float ar = a - a0, br = b - b0;   // exact
-        const float a1 = __bfloat162float(__float2bfloat16_rn(ar)), b1 = __bfloat162float(__float2bfloat16_rn(br));
-        h[t] = pack2(a0, b0);
-        m[t] = pack2(a1, b1);
-        l[t] = pack2(ar - a1, br - b1);
+        const uint32_t ua = __float_as_uint(x[2 * t]), ub = __float_as_uint(x[2 * t + 1]);
+        h[t] = __byte_perm(ua, ub, 0x7632);
+        // -x0 in one logic op: the upper half with the sign flipped.
+        const float2 nx0 = make_float2(__uint_as_float((ua & 0xFFFF0000u) ^ 0x80000000u),
+                                       __uint_as_float((ub & 0xFFFF0000u) ^ 0x80000000u));
+        const float2 r = __fadd2_rn(make_float2(x[2 * t], x[2 * t + 1]), nx0);
+        const uint32_t ra = __float_as_uint(r.x), rb = __float_as_uint(r.y);
+        m[t] = __byte_perm(ra, rb, 0x7632);
+        const float2 nx1 = make_float2(__uint_as_float((ra & 0xFFFF0000u) ^ 0x80000000u),
+                                       __uint_as_float((rb & 0xFFFF0000u) ^ 0x80000000u));
+        const float2 r2 = __fadd2_rn(r, nx1);
+        l[t] = __byte_perm(__float_as_uint(r2.x), __float_as_uint(r2.y), 0x7632);
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     mid = make_uint4(m[0], m[1], m[2], m[3]);
