@@ -369,6 +369,30 @@ def family_roofline(model, precision, families=None):
         achieved = dom["flops"] / launches / per_launch_s / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
                 "frac": round(achieved / tflops, 4)}
+        # Each GEMM against the roof that bounds it: at an arithmetic intensity
+        # (algorithmic FLOPs per algorithmic byte) above the ridge point
+        # (tensor peak / HBM bandwidth) the tensor pipe, below it HBM.
+        ridge = tflops * 1e12 / (hbm * 1e9)
+        groups = {"tensor": [0.0, 0.0, 0], "hbm": [0.0, 0.0, 0]}   # work, seconds, launches
+        for op, ms in zip(ops, prof):
+            if op["kind"] != "gemm" or ms <= 0:
+                continue
+            bound = "tensor" if op["flops"] / max(op["bytes"], 1.0) >= ridge else "hbm"
+            g = groups[bound]
+            g[0] += op["flops"] if bound == "tensor" else op["bytes"]
+            g[1] += ms / 1000.0
+            g[2] += 1
+        per = {}
+        for bound, (work, secs, n) in groups.items():
+            if n == 0:
+                continue
+            rate = work / secs / (1e12 if bound == "tensor" else 1e9)
+            peak = tflops if bound == "tensor" else hbm
+            per[bound] = {"launches": n, "achieved": round(rate, 2), "peak": peak,
+                          "unit": "TFLOP/s" if bound == "tensor" else "GB/s", "frac": round(rate / peak, 4),
+                          "ms": round(secs * 1000.0, 4)}
+        roof["per_roof"] = per
+        roof["ridge_flops_per_byte"] = round(ridge, 1)
     else:
         achieved = dom["bytes"] / launches / per_launch_s / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
