@@ -490,6 +490,38 @@ int ppocr_engine_recognize_batch(ppocr_engine* engine, size_t count, const uint8
  * result assembly.  Writes min(count, 5) values. */
 int ppocr_engine_stage_times(const ppocr_engine* engine, double* ms, size_t count);
 
+/* New: several GPUs behind one OcrEngine call.  One ppocr_gpu + ppocr_engine
+ * per listed device (the same models, dictionary and options on each), each
+ * driven by its own host thread.  The reference drives one backend per
+ * OcrEngine (src/ocr.rs:365-604); this is its recognize over a batch of pages
+ * spread across devices, with no device-to-device traffic. */
+typedef struct ppocr_engine_pool ppocr_engine_pool;
+int ppocr_engine_pool_create(const int* devices, size_t count, const char* detector_model,
+                             const char* recognizer_model, const char* dictionary,
+                             const ppocr_engine_options* options, ppocr_engine_pool** out);
+/* Waits for any worker still running a late shard, then frees every device. */
+void ppocr_engine_pool_destroy(ppocr_engine_pool* pool);
+int ppocr_engine_pool_size(const ppocr_engine_pool* pool, size_t* count);
+/* ppocr_engine_recognize_batch over the pool: pages dealt round-robin to the
+ * devices, results in page order.  A device whose shard is not done within
+ * timeout_ms (<= 0: no limit) has its pages dealt again to the devices that
+ * answered and gets no work until that shard has returned (its results are
+ * dropped; it reads the caller's memory only before this call returns).  A
+ * device failing with PPOCR_ERR_GPU is left out of the call and its pages
+ * dealt again; PPOCR_ERR_GPU when no device is left.  devices_used[i] (may
+ * be null) receives the CUDA ordinal that produced results[i]. */
+int ppocr_engine_pool_recognize_batch(ppocr_engine_pool* pool, size_t count, const uint8_t* const* rgb,
+                                      const size_t* rgb_lengths, const uint32_t* widths, const uint32_t* heights,
+                                      int format, int timeout_ms, char** results, size_t* result_lengths,
+                                      int* devices_used);
+/* Diagnostic (new), host only: the pool's dispatcher over `workers` fake
+ * devices (<= 32) and `items` items.  A worker whose bit is set in
+ * stall_mask answers after stall_ms, one in fail_mask fails with
+ * PPOCR_ERR_GPU, the others after 2 ms; every answer is item * 10.
+ * owner[i] / values[i] receive the worker that produced item i and its value. */
+int ppocr_selftest_dispatch(size_t workers, size_t items, uint32_t stall_mask, uint32_t fail_mask, int stall_ms,
+                            int timeout_ms, int* owner, int* values);
+
 #ifdef __cplusplus
 }
 #endif

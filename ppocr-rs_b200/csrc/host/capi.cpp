@@ -433,6 +433,7 @@ int ppocr_upload_rgb(ppocr_gpu* gpu, uint32_t width, uint32_t height, const uint
         img->gpu = gpu;
         img->width = width;
         img->height = height;
+        img->capacity = expected;
         cuda_check(cudaMalloc(&img->rgb, expected), "allocate source image");
         cuda_check(cudaMemcpyAsync(img->rgb, pixels, expected, cudaMemcpyHostToDevice, gpu->stream), "upload source image");
         cuda_check(cudaStreamSynchronize(gpu->stream), "upload source image");

@@ -116,12 +116,22 @@ struct ppocr_engine {
     // Wall time of the last batch call per stage (ms): upload, detector,
     // DB postprocess, recognizer forwards (model loads included), assembly.
     double stage_ms[5] = {0, 0, 0, 0, 0};
+    // Page staging reused across batch calls: device RGB buffers (grown, never
+    // shrunk) and one pinned host buffer the pages are copied through, so a
+    // call makes no allocation once the sizes have been seen (a cudaMalloc /
+    // cudaFree pair per page per call stalled whole calls for up to a second).
+    std::vector<ppocr_image*> page_pool;
+    uint8_t* pinned = nullptr;
+    size_t pinned_bytes = 0;
 
     ~ppocr_engine() {
         for (auto& e : det_cache) ppocr_model_destroy(e.second);
         for (auto& e : rec_cache) ppocr_model_destroy(e.second);
         if (rec_weights) ppocr_model_destroy(rec_weights);
+        for (ppocr_image* im : page_pool) ppocr_image_destroy(im);
+        if (pinned) cudaFreeHost(pinned);
     }
+
 
     ppocr_model* detector(const Shape& shape) {
         for (auto& e : det_cache)
@@ -159,7 +169,12 @@ struct ppocr_engine {
         uint32_t width, height;
     };
 
-    std::vector<OcrResult> recognize_batch(const std::vector<Page>& pages) {
+    // Uploads the pages into the reused device buffers: one host copy into
+    // pinned memory, one asynchronous copy per page, one stream wait.  The page
+    // bytes are read inside `gate` only (null: no gate).
+    void upload_pages(const std::vector<Page>& pages, CallGate* gate);
+
+    std::vector<OcrResult> recognize_batch(const std::vector<Page>& pages, CallGate* gate = nullptr) {
         using clock = std::chrono::steady_clock;
         auto t_prev = clock::now();
         auto lap = [&](int stage) {
@@ -169,14 +184,18 @@ struct ppocr_engine {
         };
         const size_t np = pages.size();
         std::vector<OcrResult> res(np);
-        std::vector<ImageHandle> imgs(np);
         for (size_t i = 0; i < np; ++i) {
             if (!pages[i].rgb) fail(PPOCR_ERR_INVALID_INPUT, "image pixels are null");
             res[i].source_w = pages[i].width;
             res[i].source_h = pages[i].height;
             detector_input_size(pages[i].width, pages[i].height, max_side, &res[i].input_w, &res[i].input_h);
-            check(ppocr_upload_rgb(gpu, pages[i].width, pages[i].height, pages[i].rgb, pages[i].len, &imgs[i].p));
         }
+        upload_pages(pages, gate);
+        struct PageRef {
+            ppocr_image* p;
+        };
+        std::vector<PageRef> imgs(np);
+        for (size_t i = 0; i < np; ++i) imgs[i].p = page_pool[i];
         lap(0);
         // Detector: pages of one input size, kDetectorBatch per forward.
         std::vector<std::vector<float>> probs(np);
@@ -326,6 +345,84 @@ struct ppocr_engine {
         return r;
     }
 };
+
+namespace ppocr {
+
+std::vector<std::string> engine_recognize(ppocr_engine* engine, size_t count, const uint8_t* const* rgb,
+                                          const size_t* rgb_lengths, const uint32_t* widths, const uint32_t* heights,
+                                          int format, CallGate* gate) {
+    if (format != 0 && format != 1) fail(PPOCR_ERR_INVALID_INPUT, "format must be 0 (JSON) or 1 (text)");
+    std::vector<ppocr_engine::Page> pages(count);
+    for (size_t i = 0; i < count; ++i) pages[i] = ppocr_engine::Page{rgb[i], rgb_lengths[i], widths[i], heights[i]};
+    const std::vector<OcrResult> r = engine->recognize_batch(pages, gate);
+    std::vector<std::string> out(count);
+    for (size_t i = 0; i < count; ++i) out[i] = format == 0 ? result_json(r[i]) : result_text(r[i]);
+    return out;
+}
+
+}  // namespace ppocr
+
+void ppocr_engine::upload_pages(const std::vector<Page>& pages, CallGate* gate) {
+    size_t total = 0;
+    for (const Page& pg : pages) {
+        const size_t expected = (size_t)pg.width * pg.height * 3;
+        // Gpu::upload_rgb checks (src/gpu/runtime.rs:175-197)
+        if (pg.width == 0 || pg.height == 0) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: source image dimensions must be non-zero");
+        if (pg.len != expected)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: source image has " + std::to_string(pg.len) + " RGB bytes; expected " +
+                                              std::to_string(expected) + " for " + std::to_string(pg.width) + "x" +
+                                              std::to_string(pg.height));
+        total += (expected + 255) & ~(size_t)255;
+    }
+    std::lock_guard<std::mutex> lock(gpu->mu);
+    gpu->bind();
+    if (total > pinned_bytes) {
+        if (pinned) cudaFreeHost(pinned);
+        pinned = nullptr;
+        pinned_bytes = 0;
+        cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&pinned), total, cudaHostAllocPortable), "allocate page staging");
+        pinned_bytes = total;
+    }
+    struct Lease {
+        CallGate* g;
+        ~Lease() {
+            if (g) g->leave();
+        }
+    } lease{nullptr};
+    if (gate) {
+        if (!gate->enter()) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the call returned before its pages were read");
+        lease.g = gate;
+    }
+    size_t off = 0;
+    for (size_t i = 0; i < pages.size(); ++i) {
+        const Page& pg = pages[i];
+        if (i == page_pool.size()) page_pool.push_back(nullptr);
+        ppocr_image*& im = page_pool[i];
+        if (!im) {
+            im = new ppocr_image();
+            im->gpu = gpu;
+            gpu_retain(gpu);
+        }
+        if (im->capacity < pg.len) {
+            if (im->rgb) cudaFree(im->rgb);
+            im->rgb = nullptr;
+            im->capacity = 0;
+            cuda_check(cudaMalloc(&im->rgb, pg.len), "allocate page buffer");
+            im->capacity = pg.len;
+        }
+        im->width = pg.width;
+        im->height = pg.height;
+        std::memcpy(pinned + off, pg.rgb, pg.len);
+        cuda_check(cudaMemcpyAsync(im->rgb, pinned + off, pg.len, cudaMemcpyHostToDevice, gpu->stream), "upload page");
+        off += (pg.len + 255) & ~(size_t)255;
+    }
+    if (lease.g) {
+        lease.g->leave();
+        lease.g = nullptr;
+    }
+    // The pinned staging is rewritten by the next call: the copies land first.
+    wait_stream(gpu->stream, 0, gpu);
+}
 
 extern "C" {
 
@@ -502,14 +599,11 @@ int ppocr_engine_recognize_batch(ppocr_engine* engine, size_t count, const uint8
                                  size_t* result_lengths) {
     return guard([&] {
         if (!engine || !rgb || !rgb_lengths || !widths || !heights || !results) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
-        if (format != 0 && format != 1) fail(PPOCR_ERR_INVALID_INPUT, "format must be 0 (JSON) or 1 (text)");
-        std::vector<ppocr_engine::Page> pages(count);
-        for (size_t i = 0; i < count; ++i) pages[i] = ppocr_engine::Page{rgb[i], rgb_lengths[i], widths[i], heights[i]};
-        const std::vector<OcrResult> r = engine->recognize_batch(pages);
+        const std::vector<std::string> r = engine_recognize(engine, count, rgb, rgb_lengths, widths, heights, format, nullptr);
         std::vector<char*> out(count, nullptr);
         try {
             for (size_t i = 0; i < count; ++i) {
-                const std::string s = format == 0 ? result_json(r[i]) : result_text(r[i]);
+                const std::string& s = r[i];
                 out[i] = static_cast<char*>(std::malloc(s.size() + 1));
                 if (!out[i]) fail(PPOCR_ERR_GPU, "out of host memory");
                 std::memcpy(out[i], s.c_str(), s.size() + 1);

@@ -5,10 +5,12 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <condition_variable>
 #include <cstdint>
 #include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../kernels/kernels.h"
 #include "common.hpp"
@@ -84,6 +86,7 @@ struct ppocr_image {
     ppocr_gpu* gpu = nullptr;
     uint8_t* rgb = nullptr;
     uint32_t width = 0, height = 0;
+    size_t capacity = 0;   // bytes allocated at rgb (a reused engine page buffer may hold a smaller page)
 };
 
 namespace ppocr {
@@ -93,4 +96,41 @@ void gpu_release(ppocr_gpu* gpu);
 // Quad-resample parameters for `image` (Normalization::new, src/preprocess/kernels.rs:9-18).
 PreprocessParams make_preprocess(const ppocr_image* image, const float corners[8], size_t content_width, size_t out_h,
                                  size_t out_w, bool detector);
+
+// Guards a caller's input memory for work that may outlive the call (an engine
+// pool worker that missed the call's deadline): the memory is read only
+// between a successful enter() and leave(); close() (the call returning)
+// refuses later entries and waits for the readers inside.
+class CallGate {
+public:
+    bool enter() {
+        std::lock_guard<std::mutex> lock(mu_);
+        if (!open_) return false;
+        ++readers_;
+        return true;
+    }
+    void leave() {
+        std::lock_guard<std::mutex> lock(mu_);
+        --readers_;
+        cv_.notify_all();
+    }
+    void close() {
+        std::unique_lock<std::mutex> lock(mu_);
+        open_ = false;
+        cv_.wait(lock, [&] { return readers_ == 0; });
+    }
+
+private:
+    std::mutex mu_;
+    std::condition_variable cv_;
+    bool open_ = true;
+    int readers_ = 0;
+};
+
+// ppocr_engine_recognize_batch with the results as strings; the page bytes
+// are read only inside `gate` (null: no gate).  Error::InvalidInput when the
+// gate has closed before the pages were read.
+std::vector<std::string> engine_recognize(ppocr_engine* engine, size_t count, const uint8_t* const* rgb,
+                                          const size_t* rgb_lengths, const uint32_t* widths, const uint32_t* heights,
+                                          int format, CallGate* gate);
 }  // namespace ppocr

@@ -55,6 +55,7 @@ constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows
 constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
 constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 FP32 columns
+constexpr int STAGE_BUFS = 2;                          // per epilogue warp: a store drains while the next group is written
 constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory per block
 
 // Shared memory, 1024-byte aligned pieces: [resident W] [plane ring]
@@ -65,6 +66,7 @@ struct SplitArgs {
     int tiles_y, tiles_x;   // conv mode: tile grid per image
     int w_resident;         // 1: one K block and one N tile, W loaded once per CTA
     int stages;             // FP32 ring depth
+    int plane_stages;       // BF16 plane ring depth (1 when one K block covers the GEMM)
     int a_stage_bytes;      // one FP32 ring stage (A boxes + streamed W), 1024-aligned
     int a_box_bytes;        // the A boxes of a stage (1 or 2 boxes of 16 KB)
     int w_bytes;            // the three W pieces of one (K block, N tile)
@@ -162,9 +164,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sw_res = smem;
     uint8_t* splanes = smem + args.w_region;
-    uint8_t* sout = splanes + PLANE_STAGES * PLANES_STAGE;
-    uint8_t* sring = sout + EPI_WARPS * STAGE_OUT;
+    uint8_t* sout = splanes + args.plane_stages * PLANES_STAGE;
+    uint8_t* sring = sout + EPI_WARPS * STAGE_BUFS * STAGE_OUT;
     const int S = args.stages;
+    const int PS = args.plane_stages;
     const int bn = args.bn;
     const bool wres = args.w_resident != 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -177,7 +180,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             tc::mbar_init(&f32_empty[s], 128);
             tc::mbar_init(&w_free[s], 1);
         }
-        for (int s = 0; s < PLANE_STAGES; ++s) {
+        for (int s = 0; s < PS; ++s) {
             tc::mbar_init(&planes_full[s], 128);
             tc::mbar_init(&planes_empty[s], 1);
         }
@@ -276,8 +279,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 tc::fence_after();
                 const uint32_t acc = tmem + (uint32_t)(b * 3 * bn);
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
-                    const int s = it % S, sp = it % PLANE_STAGES;
-                    if (!tc::mbar_wait(&planes_full[sp], (it / PLANE_STAGES) & 1, false, wait_ns, &abort_flag) ||
+                    const int s = it % S, sp = it % PS;
+                    if (!tc::mbar_wait(&planes_full[sp], (it / PS) & 1, false, wait_ns, &abort_flag) ||
                         (!wres && !tc::mbar_wait(&full[s], (it / S) & 1, false, wait_ns, &abort_flag))) {
                         report(p, 3);
                         abort_flag = 1;
@@ -319,10 +322,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             const float* grow = (!p.conv && p.gate && row < p.m) ? p.gate + (size_t)(row / p.rows_per_image) * p.k : nullptr;
             bool ok = true;
             for (int kb = 0; kb < args.kt; ++kb, ++it) {
-                const int s = it % S, sp = it % PLANE_STAGES;
+                const int s = it % S, sp = it % PS;
                 if (!tc::mbar_wait(&full[s], (it / S) & 1, true, wait_ns, &abort_flag) ||
-                    (it >= PLANE_STAGES &&
-                     !tc::mbar_wait(&planes_empty[sp], ((it / PLANE_STAGES) + 1) & 1, true, wait_ns, &abort_flag))) {
+                    (it >= PS && !tc::mbar_wait(&planes_empty[sp], ((it / PS) + 1) & 1, true, wait_ns, &abort_flag))) {
                     report(p, 4);
                     abort_flag = 1;
                     ok = false;
@@ -366,8 +368,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         // accumulator buffer g and so every other tile: two tiles' epilogues
         // run at once, and each warp walks all of its tile's 16-column groups.
         const int q = warp & 3, grp = (warp - 6) >> 2;
-        uint8_t* stage = sout + (warp - 6) * STAGE_OUT;
-        uint8_t* line = stage + lane * 64;
+        uint8_t* stage0 = sout + (warp - 6) * STAGE_BUFS * STAGE_OUT;
+        int sbuf = 0;
         const int swz = (lane >> 1) & 3;   // 64-byte swizzle: chunk ^= row bits 1-2
         int ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
@@ -457,7 +459,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
 #pragma unroll
                     for (int j = 0; j < 16; ++j) o[j] += res[j];
                 }
-                if (lane == 0) tc::bulk_wait_read();
+                // This staging buffer's previous store (two groups back) has
+                // finished reading it once at most one store is pending.
+                uint8_t* stage = stage0 + sbuf * STAGE_OUT;
+                uint8_t* line = stage + lane * 64;
+                sbuf ^= 1;
+                if (lane == 0) tc::bulk_wait_read_1();
                 __syncwarp();
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
@@ -617,7 +624,8 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.w_region = a.w_resident ? up(a.w_bytes) : 0;
     a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
     a.a_stage_bytes = a.a_box_bytes + (a.w_resident ? 0 : up(a.w_bytes));
-    const int fixed = align + a.w_region + PLANE_STAGES * PLANES_STAGE + EPI_WARPS * STAGE_OUT;
+    a.plane_stages = a.kt == 1 ? 1 : PLANE_STAGES;
+    const int fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * STAGE_BUFS * STAGE_OUT;
     a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
     if (a.stages > MAX_A) a.stages = MAX_A;
     if (a.stages < 2) return cudaErrorInvalidConfiguration;

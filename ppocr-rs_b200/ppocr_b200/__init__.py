@@ -21,7 +21,7 @@ __all__ = [
     "Error", "ReadFile", "Safetensors", "TensorNotFound", "UnsupportedDtype", "ShapeMismatch",
     "TensorSizeOverflow", "TensorByteLength", "InvalidTensorRange", "InvalidModel", "InvalidInput", "GpuError",
     "ModelSize", "Precision", "Gpu", "GpuImage", "ImagePreprocess", "ModelOutput", "Detector", "Recognizer",
-    "library", "library_path", "gpu_count", "inspect_model",
+    "library", "library_path", "gpu_count", "inspect_model", "Engine", "EnginePool", "selftest_dispatch",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -223,6 +223,15 @@ def library() -> C.CDLL:
         "ppocr_model_tensor_info": (I, [P, S, C.c_char_p, S, _SIZE4, C.POINTER(C.c_int)]),
         "ppocr_model_read_tensor": (I, [P, S, FP, S]),
         "ppocr_write_seeded_weights": (I, [C.c_char_p, I, I, C.c_uint64]),
+        "ppocr_engine_pool_create": (I, [C.POINTER(C.c_int), S, C.c_char_p, C.c_char_p, C.c_char_p,
+                                         C.POINTER(_EngineOptions), C.POINTER(P)]),
+        "ppocr_engine_pool_destroy": (None, [P]),
+        "ppocr_engine_pool_size": (I, [P, C.POINTER(S)]),
+        "ppocr_engine_pool_recognize_batch": (I, [P, S, C.POINTER(C.c_void_p), C.POINTER(S), C.POINTER(C.c_uint32),
+                                                  C.POINTER(C.c_uint32), I, I, C.POINTER(C.c_void_p), C.POINTER(S),
+                                                  C.POINTER(C.c_int)]),
+        "ppocr_selftest_dispatch": (I, [S, S, C.c_uint32, C.c_uint32, I, I, C.POINTER(C.c_int),
+                                        C.POINTER(C.c_int)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -786,22 +795,52 @@ class Dictionary:
             pass
 
 
+def _engine_options(detector_size, recognizer_size, precision, detector_max_side, postprocess, recognizer_precision):
+    o = _EngineOptions()
+    library().ppocr_engine_options_default(C.byref(o))
+    o.detector_size = ModelSize.parse(detector_size)
+    o.recognizer_size = ModelSize.parse(recognizer_size)
+    o.precision = Precision.parse(precision)
+    if recognizer_precision is not None:
+        o.recognizer_precision = 1 + Precision.parse(recognizer_precision)
+    o.detector_max_side = int(detector_max_side or 0)
+    if postprocess is not None:
+        o.postprocess = postprocess._c()
+    return o
+
+
+def _page_arrays(pages):
+    pages = [np.ascontiguousarray(p, dtype=np.uint8) for p in pages]
+    n = len(pages)
+    ptrs = (C.c_void_p * n)(*[p.ctypes.data for p in pages])
+    lens = (C.c_size_t * n)(*[p.size for p in pages])
+    ws = (C.c_uint32 * n)(*[p.shape[1] for p in pages])
+    hs = (C.c_uint32 * n)(*[p.shape[0] for p in pages])
+    return pages, n, ptrs, lens, ws, hs
+
+
+def _take_strings(outs, olens, n, fmt):
+    import json
+
+    res = []
+    try:
+        for i in range(n):
+            text = C.string_at(outs[i], olens[i]).decode("utf-8")
+            res.append(json.loads(text) if fmt == "json" else text)
+    finally:
+        for i in range(n):
+            library().ppocr_string_free(outs[i])
+    return res
+
+
 class Engine:
     """OcrEngine (src/ocr.rs:364-540) on this library's GPU backend."""
 
     def __init__(self, gpu: Gpu, detector_model: str, recognizer_model: str, dictionary: str,
                  detector_size="tiny", recognizer_size="tiny", precision="fp32", detector_max_side: int = 736,
                  postprocess: PostprocessOptions = None, recognizer_precision=None):
-        o = _EngineOptions()
-        library().ppocr_engine_options_default(C.byref(o))
-        o.detector_size = ModelSize.parse(detector_size)
-        o.recognizer_size = ModelSize.parse(recognizer_size)
-        o.precision = Precision.parse(precision)
-        if recognizer_precision is not None:
-            o.recognizer_precision = 1 + Precision.parse(recognizer_precision)
-        o.detector_max_side = int(detector_max_side or 0)
-        if postprocess is not None:
-            o.postprocess = postprocess._c()
+        o = _engine_options(detector_size, recognizer_size, precision, detector_max_side, postprocess,
+                            recognizer_precision)
         h = C.c_void_p()
         _check(library().ppocr_engine_create(gpu._h, str(detector_model).encode(), str(recognizer_model).encode(),
                                              str(dictionary).encode(), C.byref(o), C.byref(h)))
@@ -830,27 +869,12 @@ class Engine:
 
     def recognize_batch(self, pages, fmt: str = "json"):
         """OcrEngine::recognize over several RGB8 pages at once (same per-page results)."""
-        import json
-
-        pages = [np.ascontiguousarray(p, dtype=np.uint8) for p in pages]
-        n = len(pages)
-        ptrs = (C.c_void_p * n)(*[p.ctypes.data for p in pages])
-        lens = (C.c_size_t * n)(*[p.size for p in pages])
-        ws = (C.c_uint32 * n)(*[p.shape[1] for p in pages])
-        hs = (C.c_uint32 * n)(*[p.shape[0] for p in pages])
+        pages, n, ptrs, lens, ws, hs = _page_arrays(pages)
         outs = (C.c_void_p * n)()
         olens = (C.c_size_t * n)()
         _check(library().ppocr_engine_recognize_batch(self._h, n, ptrs, lens, ws, hs, 0 if fmt == "json" else 1,
                                                       outs, olens))
-        res = []
-        try:
-            for i in range(n):
-                text = C.string_at(outs[i], olens[i]).decode("utf-8")
-                res.append(json.loads(text) if fmt == "json" else text)
-        finally:
-            for i in range(n):
-                library().ppocr_string_free(outs[i])
-        return res
+        return _take_strings(outs, olens, n, fmt)
 
     def close(self):
         if getattr(self, "_h", None):
@@ -862,3 +886,66 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+class EnginePool:
+    """Several GPUs behind one OcrEngine call (new): one engine per device, each
+    on its own host thread; pages are dealt round-robin and the results come
+    back in page order.  A device whose shard misses `timeout_ms` has its pages
+    dealt again to the others (the reference drives one backend per engine,
+    src/ocr.rs:365-604)."""
+
+    def __init__(self, devices, detector_model: str, recognizer_model: str, dictionary: str,
+                 detector_size="tiny", recognizer_size="tiny", precision="fp32", detector_max_side: int = 736,
+                 postprocess: PostprocessOptions = None, recognizer_precision=None):
+        devices = [int(d) for d in devices]
+        o = _engine_options(detector_size, recognizer_size, precision, detector_max_side, postprocess,
+                            recognizer_precision)
+        devs = (C.c_int * len(devices))(*devices)
+        h = C.c_void_p()
+        _check(library().ppocr_engine_pool_create(devs, len(devices), str(detector_model).encode(),
+                                                  str(recognizer_model).encode(), str(dictionary).encode(),
+                                                  C.byref(o), C.byref(h)))
+        self._h, self.devices = h, devices
+        self.last_devices = []
+
+    def __len__(self):
+        n = C.c_size_t()
+        _check(library().ppocr_engine_pool_size(self._h, C.byref(n)))
+        return n.value
+
+    def recognize_batch(self, pages, fmt: str = "json", timeout_ms: int = 0):
+        """Engine.recognize_batch spread over the pool's devices; `last_devices`
+        then lists the CUDA ordinal that produced each page."""
+        pages, n, ptrs, lens, ws, hs = _page_arrays(pages)
+        outs = (C.c_void_p * n)()
+        olens = (C.c_size_t * n)()
+        used = (C.c_int * n)()
+        _check(library().ppocr_engine_pool_recognize_batch(self._h, n, ptrs, lens, ws, hs, 0 if fmt == "json" else 1,
+                                                           int(timeout_ms), outs, olens, used))
+        self.last_devices = list(used)
+        return _take_strings(outs, olens, n, fmt)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            library().ppocr_engine_pool_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def selftest_dispatch(workers: int, items: int, stall=(), fail=(), stall_ms: int = 300, timeout_ms: int = 100):
+    """The engine pool's dispatcher over fake host workers (no GPU): workers in
+    `stall` answer after stall_ms, those in `fail` raise a device error.
+    Returns (owner per item, value per item); every value is item * 10."""
+    owner = (C.c_int * max(items, 1))()
+    values = (C.c_int * max(items, 1))()
+    stall_mask = sum(1 << w for w in stall)
+    fail_mask = sum(1 << w for w in fail)
+    _check(library().ppocr_selftest_dispatch(workers, items, stall_mask, fail_mask, stall_ms, timeout_ms, owner,
+                                             values))
+    return list(owner)[:items], list(values)[:items]

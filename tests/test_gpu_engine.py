@@ -137,3 +137,23 @@ def test_engine_batch_matches_single_pages(gpu, setup):
     single = [P.Engine(gpu, det_path, rec_path, dict_path).recognize(p) for p in pages]
     assert batch == single
     assert sum(len(r["lines"]) for r in batch) > 0
+
+
+def test_engine_pool_matches_single_engine(gpu, setup):
+    # Two engines on device 0 (two handles, two streams, two host threads)
+    # plus, on a multi-GPU box, one per device: pages dealt round-robin must
+    # give exactly the single-engine batch results, in page order.
+    det_path, rec_path, dict_path, _, rgb = setup
+    pages = [rgb] + [seeded.text_page_rgb8(180, 320, seed=40 + i, blocks=(6, 10), block_h=(12, 28),
+                                           block_w=(40, 200), max_angle=15.0, background=(170, 250))
+                     for i in range(4)]
+    expect = P.Engine(gpu, det_path, rec_path, dict_path).recognize_batch(pages)
+    devices = [0, 0] + list(range(1, P.gpu_count()))
+    pool = P.EnginePool(devices, det_path, rec_path, dict_path)
+    assert len(pool) == len(devices)
+    assert pool.recognize_batch(pages, timeout_ms=120000) == expect
+    assert pool.last_devices == [devices[i % len(devices)] for i in range(len(pages))]
+    # A second call reuses every engine's page staging and model cache.
+    assert pool.recognize_batch(pages[::-1], fmt="text") == \
+        P.Engine(gpu, det_path, rec_path, dict_path).recognize_batch(pages[::-1], fmt="text")
+    pool.close()
