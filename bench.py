@@ -576,10 +576,34 @@ def measure_rec(gpu, world, barrier, tmp, steps=10, warmup=3, batch=256):
     model = _load_resident(P, gpu, path, "rec", "medium", shape, "bf16", x)
     total = sharding.max_over_ranks(_timed([model], steps, warmup, barrier))
     roof, table, _, _ = family_roofline(model, "bf16", families="gemm")
+    # End to end from pinned host crops to host CTC classes and probabilities:
+    # one ppocr_recognizer_forward_pipelined_ctc call over e_steps batches.
+    import ctypes as C
+
+    import torch
+
+    e_steps = 5
+    rows = batch * model.output_shape[1]
+    hin = torch.from_numpy(np.tile(x.reshape(-1), e_steps)).pin_memory()
+    hidx = torch.empty(rows * e_steps, dtype=torch.int32).pin_memory()
+    hprob = torch.empty(rows * e_steps, dtype=torch.float32).pin_memory()
+    lib = P.library()
+    args = (model._h, C.cast(C.c_void_p(hin.data_ptr()), C.POINTER(C.c_float)), batch * e_steps,
+            C.cast(C.c_void_p(hidx.data_ptr()), C.POINTER(C.c_int32)),
+            C.cast(C.c_void_p(hprob.data_ptr()), C.POINTER(C.c_float)), rows * e_steps)
+    for _ in range(2):
+        P._check(lib.ppocr_recognizer_forward_pipelined_ctc(*args))
+    barrier()
+    t0 = time.perf_counter()
+    P._check(lib.ppocr_recognizer_forward_pipelined_ctc(*args))
+    et = sharding.max_over_ranks(time.perf_counter() - t0)
     model.close()
     return {"metric": "rec crops/s @48x320 (medium recognizer, batch 256/GPU)",
             "value": round(batch * world * steps / (total / 1000.0), 2), "unit": "crops/s",
-            "ms_per_step": round(total / steps, 4), "dtype": "bf16", "gemm_roofline": roof, "families": table}
+            "ms_per_step": round(total / steps, 4), "dtype": "bf16", "gemm_roofline": roof, "families": table,
+            "e2e": {"value": round(batch * e_steps * world / et, 2), "unit": "crops/s",
+                    "h2d_bytes_per_step": int(x.size * 4), "d2h_bytes_per_step": int(rows * 8), "steps": e_steps,
+                    "api": "ppocr_recognizer_forward_pipelined_ctc (pinned host crops in, CTC class + probability out)"}}
 
 
 def run_e2e(args):
@@ -712,35 +736,55 @@ def run_b200(args):
         except Exception:
             pass
 
-    # End to end through the C ABI with pinned host buffers: one call of
-    # ppocr_model_forward_pipelined over e_steps batches (a distinct host copy of
-    # the input per batch), which uploads batch i + 1 and downloads batch i - 1
-    # while batch i runs; every batch's host-to-device and device-to-host copies
-    # are inside the timed region.
+    # End to end through the C ABI with pinned host buffers: one pipelined call
+    # over e_steps batches (a distinct host copy of the input per batch), which
+    # uploads batch i + 1 and downloads batch i - 1 while batch i runs; every
+    # batch's host-to-device and device-to-host copies are inside the timed
+    # region.  The detector downloads its probability maps
+    # (ppocr_model_forward_pipelined); the recognizer only the greedy-CTC class
+    # and probability per step (ppocr_recognizer_forward_pipelined_ctc), which is
+    # all the reference's decoder reads (src/ocr.rs:800-853).
     e2e = None
     if not args.no_e2e:
-        e_steps = max(3, args.steps // 2) if args.kind == "det" else 3
-        per_out = model.output_elements
-        hin = torch.from_numpy(np.tile(x.reshape(-1), e_steps)).pin_memory()
-        hout = torch.empty(per_out * e_steps, dtype=torch.float32).pin_memory()
         import ctypes as C
 
-        lib = P.library()
-        fin = C.cast(C.c_void_p(hin.data_ptr()), C.POINTER(C.c_float))
-        fout = C.cast(C.c_void_p(hout.data_ptr()), C.POINTER(C.c_float))
+        e_steps = max(3, args.steps // 2) if args.kind == "det" else 5
         images = shape[0] * e_steps
+        hin = torch.from_numpy(np.tile(x.reshape(-1), e_steps)).pin_memory()
+        fin = C.cast(C.c_void_p(hin.data_ptr()), C.POINTER(C.c_float))
+        lib = P.library()
+        if args.kind == "det":
+            per_out = model.output_elements
+            hout = [torch.empty(per_out * e_steps, dtype=torch.float32).pin_memory()]
+            fout = C.cast(C.c_void_p(hout[0].data_ptr()), C.POINTER(C.c_float))
+            d2h = per_out * 4
+
+            def call():
+                P._check(lib.ppocr_model_forward_pipelined(model._h, fin, images, fout, per_out * e_steps))
+            api = f"ppocr_model_forward_pipelined (one call over {e_steps} batches of {shape[0]}, pinned host buffers)"
+        else:
+            rows = shape[0] * model.output_shape[1]
+            hout = [torch.empty(rows * e_steps, dtype=torch.int32).pin_memory(),
+                    torch.empty(rows * e_steps, dtype=torch.float32).pin_memory()]
+            iout = C.cast(C.c_void_p(hout[0].data_ptr()), C.POINTER(C.c_int32))
+            pout = C.cast(C.c_void_p(hout[1].data_ptr()), C.POINTER(C.c_float))
+            d2h = rows * 8
+
+            def call():
+                P._check(lib.ppocr_recognizer_forward_pipelined_ctc(model._h, fin, images, iout, pout, rows * e_steps))
+            api = (f"ppocr_recognizer_forward_pipelined_ctc (one call over {e_steps} batches of {shape[0]}, "
+                   "pinned host buffers, CTC class + probability per step downloaded)")
         for _ in range(2):
-            P._check(lib.ppocr_model_forward_pipelined(model._h, fin, images, fout, per_out * e_steps))
+            call()
         barrier()
         t0 = time.perf_counter()
-        P._check(lib.ppocr_model_forward_pipelined(model._h, fin, images, fout, per_out * e_steps))
+        call()
         et = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": round(images * world / float(et.item()), 2), "unit": unit,
-               "h2d_bytes_per_step": int(x.size * 4), "d2h_bytes_per_step": int(per_out * 4),
-               "steps": e_steps,
-               "api": f"ppocr_model_forward_pipelined (one call over {e_steps} batches of {shape[0]}, pinned host buffers)"}
+               "h2d_bytes_per_step": int(x.size * 4), "d2h_bytes_per_step": int(d2h),
+               "steps": e_steps, "api": api}
         del hin, hout
 
     # The secondary figures run before the CPU baseline, whose torch thread pool

@@ -161,6 +161,15 @@ int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len
  * asynchronously; pageable ones still work.  Errors as ppocr_model_forward. */
 int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t images, float* output,
                                   size_t output_capacity);
+/* New, recognizer only: ppocr_model_forward_pipelined that returns, per
+ * (image, step), only the greedy-CTC arg-max class and its probability (what
+ * decode_ctc_greedy_for_input reads, src/ocr.rs:800-853), in the layout of
+ * ppocr_recognizer_forward_ctc: `indices` and `probabilities` receive
+ * images x T entries each (capacity = entries each array holds).  The full
+ * probability rows stay on the device (their finiteness is still checked), so
+ * 8 bytes per step cross to the host instead of 4 x classes. */
+int ppocr_recognizer_forward_pipelined_ctc(ppocr_model* model, const float* input, size_t images, int32_t* indices,
+                                           float* probabilities, size_t capacity);
 
 /* forward_image(&GpuImage, ImagePreprocess) (src/gpu/model.rs:116-138,
  * 240-259; ImagePreprocess::{detector, recognizer} src/gpu/runtime.rs:50-69):

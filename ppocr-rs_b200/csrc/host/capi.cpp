@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -554,78 +555,143 @@ int ppocr_model_forward(ppocr_model* model, const float* input, size_t input_len
     });
 }
 
+namespace {
+
+// What a pipelined forward hands back per chunk: `stage` enqueues, on the
+// compute stream, the copy of the chunk's results into a download slot
+// (stage_bytes bytes); `download` enqueues that slot's copy to the host on the
+// download stream.
+struct PipeOutput {
+    size_t stage_bytes = 0;
+    std::function<void(cudaStream_t, void* slot)> stage;
+    std::function<void(size_t chunk, const void* slot, cudaStream_t)> download;
+};
+
+// images / batch chunks: each chunk's upload, forward and download run on
+// their own streams through two slots, so chunk c + 1 uploads while chunk c
+// computes and chunk c - 1 downloads.
+void forward_pipelined(ppocr_model* model, const float* input, size_t images, const PipeOutput& out) {
+    if (!input) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+    const size_t batch = (size_t)model->m.n;
+    if (images == 0 || images % batch)
+        fail(PPOCR_ERR_INVALID_INPUT, "invalid input: image count " + std::to_string(images) + " is not a multiple of the model batch " +
+                                          std::to_string(batch));
+    const size_t chunks = images / batch;
+    const size_t in_elems = model->input_elements(), out_elems = model->m.output_elements;
+    if (out.stage_bytes > out_elems * 4) fail(PPOCR_ERR_INVALID_INPUT, "pipelined output larger than the model output");
+    std::lock_guard<std::mutex> lock(model->gpu->mu);
+    model->gpu->bind();
+    model->gpu->ensure_arena(model->m.plan.arena_bytes);
+    if (!model->pipe) {
+        std::unique_ptr<ForwardPipe> p(new ForwardPipe());
+        cuda_check(cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking), "create upload stream");
+        cuda_check(cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking), "create download stream");
+        for (int i = 0; i < 2; ++i) {
+            cuda_check(cudaMalloc(&p->in_stage[i], in_elems * 4), "allocate input staging");
+            cuda_check(cudaMalloc(&p->out_stage[i], out_elems * 4), "allocate output staging");
+            for (cudaEvent_t* e : {&p->arrived[i], &p->consumed[i], &p->computed[i], &p->downloaded[i]})
+                cuda_check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "create pipeline event");
+        }
+        model->pipe = std::move(p);
+    }
+    ForwardPipe& pp = *model->pipe;
+    cudaStream_t cs = model->gpu->stream;
+    float* dinput = static_cast<float*>(model->tensor(model->m.input));
+    try {
+        cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), cs), "reset flags");
+        for (size_t c = 0; c < chunks; ++c) {
+            const int slot = (int)(c & 1);
+            // Upload chunk c once the forward of chunk c - 2 has taken its copy of the slot.
+            cuda_check(cudaStreamWaitEvent(pp.h2d, pp.consumed[slot], 0), "order upload");
+            cuda_check(cudaMemcpyAsync(pp.in_stage[slot], input + c * in_elems, in_elems * 4, cudaMemcpyHostToDevice, pp.h2d),
+                       "upload input");
+            cuda_check(cudaEventRecord(pp.arrived[slot], pp.h2d), "record upload");
+            // Forward chunk c on the model stream.
+            cuda_check(cudaStreamWaitEvent(cs, pp.arrived[slot], 0), "order forward");
+            // Staging copies run as kernels (with the finiteness checks folded
+            // in): a copy-engine copy here would queue behind the next chunk's upload.
+            cuda_check(launch_copy_check(static_cast<const float*>(pp.in_stage[slot]), dinput, in_elems, model->dflags, cs),
+                       "stage input");
+            cuda_check(cudaEventRecord(pp.consumed[slot], cs), "record staging");
+            model->run(cs);
+            // Hand the results to the download slot once chunk c - 2 has left it.
+            cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[slot], 0), "order output staging");
+            out.stage(cs, pp.out_stage[slot]);
+            cuda_check(cudaEventRecord(pp.computed[slot], cs), "record forward");
+            cuda_check(cudaStreamWaitEvent(pp.d2h, pp.computed[slot], 0), "order download");
+            out.download(c, pp.out_stage[slot], pp.d2h);
+            cuda_check(cudaEventRecord(pp.downloaded[slot], pp.d2h), "record download");
+        }
+        cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[(chunks - 1) & 1], 0), "join download");
+        cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
+        wait_stream(cs, 0, model->gpu);
+    } catch (...) {
+        // The caller's buffers must not be touched after return.
+        cudaStreamSynchronize(pp.h2d);
+        cudaStreamSynchronize(cs);
+        cudaStreamSynchronize(pp.d2h);
+        throw;
+    }
+    raise_flags(model);
+}
+
+}  // namespace
+
 int ppocr_model_forward_pipelined(ppocr_model* model, const float* input, size_t images, float* output,
                                   size_t output_capacity) {
     return guard([&] {
         if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
         if (!input || !output) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
-        const size_t batch = (size_t)model->m.n;
-        if (images == 0 || images % batch)
-            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: image count " + std::to_string(images) + " is not a multiple of the model batch " +
-                                              std::to_string(batch));
+        const size_t batch = (size_t)model->m.n, out_elems = model->m.output_elements;
         const size_t chunks = images / batch;
-        const size_t in_elems = model->input_elements(), out_elems = model->m.output_elements;
-        if (output_capacity < chunks * out_elems)
+        if (images % batch == 0 && output_capacity < chunks * out_elems)
             fail(PPOCR_ERR_INVALID_INPUT, "output buffer holds " + std::to_string(output_capacity) + " values; " +
                                               std::to_string(chunks * out_elems) + " required");
-        std::lock_guard<std::mutex> lock(model->gpu->mu);
-        model->gpu->bind();
-        model->gpu->ensure_arena(model->m.plan.arena_bytes);
-        if (!model->pipe) {
-            std::unique_ptr<ForwardPipe> p(new ForwardPipe());
-            cuda_check(cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking), "create upload stream");
-            cuda_check(cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking), "create download stream");
-            for (int i = 0; i < 2; ++i) {
-                cuda_check(cudaMalloc(&p->in_stage[i], in_elems * 4), "allocate input staging");
-                cuda_check(cudaMalloc(&p->out_stage[i], out_elems * 4), "allocate output staging");
-                for (cudaEvent_t* e : {&p->arrived[i], &p->consumed[i], &p->computed[i], &p->downloaded[i]})
-                    cuda_check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "create pipeline event");
-            }
-            model->pipe = std::move(p);
-        }
-        ForwardPipe& pp = *model->pipe;
-        cudaStream_t cs = model->gpu->stream;
-        float* dinput = static_cast<float*>(model->tensor(model->m.input));
         const int otid = model->output_tid();
-        try {
-            cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), cs), "reset flags");
-            for (size_t c = 0; c < chunks; ++c) {
-                const int slot = (int)(c & 1);
-                // Upload chunk c once the forward of chunk c - 2 has taken its copy of the slot.
-                cuda_check(cudaStreamWaitEvent(pp.h2d, pp.consumed[slot], 0), "order upload");
-                cuda_check(cudaMemcpyAsync(pp.in_stage[slot], input + c * in_elems, in_elems * 4, cudaMemcpyHostToDevice, pp.h2d),
-                           "upload input");
-                cuda_check(cudaEventRecord(pp.arrived[slot], pp.h2d), "record upload");
-                // Forward chunk c on the model stream.
-                cuda_check(cudaStreamWaitEvent(cs, pp.arrived[slot], 0), "order forward");
-                // Staging copies run as kernels (with the finiteness checks folded
-                // in): a copy-engine copy here would queue behind the next chunk's upload.
-                cuda_check(launch_copy_check(static_cast<const float*>(pp.in_stage[slot]), dinput, in_elems, model->dflags, cs),
-                           "stage input");
-                cuda_check(cudaEventRecord(pp.consumed[slot], cs), "record staging");
-                model->run(cs);
-                // Hand the output to the download slot once chunk c - 2 has left it.
-                cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[slot], 0), "order output staging");
-                cuda_check(launch_copy_check(static_cast<const float*>(model->tensor(otid)), static_cast<float*>(pp.out_stage[slot]),
-                                             out_elems, model->dflags + 1, cs),
-                           "stage output");
-                cuda_check(cudaEventRecord(pp.computed[slot], cs), "record forward");
-                cuda_check(cudaStreamWaitEvent(pp.d2h, pp.computed[slot], 0), "order download");
-                cuda_check(cudaMemcpyAsync(output + c * out_elems, pp.out_stage[slot], out_elems * 4, cudaMemcpyDeviceToHost, pp.d2h),
-                           "read output");
-                cuda_check(cudaEventRecord(pp.downloaded[slot], pp.d2h), "record download");
-            }
-            cuda_check(cudaStreamWaitEvent(cs, pp.downloaded[(chunks - 1) & 1], 0), "join download");
-            cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, cs), "read flags");
-            wait_stream(cs, 0, model->gpu);
-        } catch (...) {
-            // The caller's buffers must not be touched after return.
-            cudaStreamSynchronize(pp.h2d);
-            cudaStreamSynchronize(cs);
-            cudaStreamSynchronize(pp.d2h);
-            throw;
-        }
-        raise_flags(model);
+        PipeOutput po;
+        po.stage_bytes = out_elems * 4;
+        po.stage = [&](cudaStream_t cs, void* slot) {
+            cuda_check(launch_copy_check(static_cast<const float*>(model->tensor(otid)), static_cast<float*>(slot), out_elems,
+                                         model->dflags + 1, cs),
+                       "stage output");
+        };
+        po.download = [&](size_t c, const void* slot, cudaStream_t d2h) {
+            cuda_check(cudaMemcpyAsync(output + c * out_elems, slot, out_elems * 4, cudaMemcpyDeviceToHost, d2h), "read output");
+        };
+        forward_pipelined(model, input, images, po);
+    });
+}
+
+int ppocr_recognizer_forward_pipelined_ctc(ppocr_model* model, const float* input, size_t images, int32_t* indices,
+                                           float* probabilities, size_t capacity) {
+    return guard([&] {
+        if (!model) fail(PPOCR_ERR_INVALID_INPUT, "model is null");
+        if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "CTC decode needs a recognizer");
+        if (!input || !indices || !probabilities) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        const size_t batch = (size_t)model->m.n, rows = batch * (size_t)model->m.t;
+        const size_t chunks = images / batch;
+        if (images % batch == 0 && capacity < chunks * rows)
+            fail(PPOCR_ERR_INVALID_INPUT, "output arrays hold " + std::to_string(capacity) + " rows; " +
+                                              std::to_string(chunks * rows) + " required");
+        PipeOutput po;
+        po.stage_bytes = rows * 8;
+        po.stage = [&](cudaStream_t cs, void* slot) {
+            // The finiteness check of the full probability rows (as
+            // ppocr_recognizer_forward_ctc does), then the two compact rows.
+            cuda_check(launch_check_finite(static_cast<const float*>(model->tensor(model->m.probs)), model->m.output_elements,
+                                           model->dflags + 1, cs),
+                       "check output");
+            cuda_check(launch_copy_words(model->tensor(model->m.index), slot, rows, cs), "stage indices");
+            cuda_check(launch_copy_words(model->tensor(model->m.max_prob), static_cast<uint8_t*>(slot) + rows * 4, rows, cs),
+                       "stage probabilities");
+        };
+        po.download = [&](size_t c, const void* slot, cudaStream_t d2h) {
+            cuda_check(cudaMemcpyAsync(indices + c * rows, slot, rows * 4, cudaMemcpyDeviceToHost, d2h), "read indices");
+            cuda_check(cudaMemcpyAsync(probabilities + c * rows, static_cast<const uint8_t*>(slot) + rows * 4, rows * 4,
+                                       cudaMemcpyDeviceToHost, d2h),
+                       "read probabilities");
+        };
+        forward_pipelined(model, input, images, po);
     });
 }
 

@@ -424,6 +424,9 @@ cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cu
 cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream);
 // dst[0, count) = src[0, count), *flag = 1 if any value is not finite (16-byte aligned buffers).
 cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* flag, cudaStream_t stream);
+// Copies `count` 32-bit words on `stream` as a kernel (a copy-engine copy
+// would queue behind the copies of other streams).
+cudaError_t launch_copy_words(const void* src, void* dst, size_t count, cudaStream_t stream);
 // Same over `rows` rows of `cols` values at row stride `ld`.
 cudaError_t launch_check_finite_rows(const float* in, size_t rows, size_t cols, size_t ld, int* flag, cudaStream_t stream);
 // FP32 CUDA-core throughput probe (fp32_peak.cu): blocks x 512 threads, each

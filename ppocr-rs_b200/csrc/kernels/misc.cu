@@ -634,6 +634,11 @@ __global__ void copy_check_kernel(const float* __restrict__ src, float* __restri
     if (bad) *flag = 1;
 }
 
+__global__ void copy_words_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, size_t count) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) dst[i] = src[i];
+}
+
 inline unsigned grid_for(long long total, int threads) {
     long long b = (total + threads - 1) / threads;
     if (b > 148LL * 32) b = 148LL * 32;
@@ -826,6 +831,13 @@ cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* f
     if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return cudaErrorInvalidValue;
     if (count == 0) return cudaSuccess;
     copy_check_kernel<<<grid_for((long long)(count / 4 + 1), 256), 256, 0, stream>>>(src, dst, count, flag);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_words(const void* src, void* dst, size_t count, cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    copy_words_kernel<<<grid_for((long long)count, 256), 256, 0, stream>>>(static_cast<const uint32_t*>(src),
+                                                                          static_cast<uint32_t*>(dst), count);
     return cudaGetLastError();
 }
 

@@ -171,6 +171,7 @@ def library() -> C.CDLL:
         "ppocr_model_input_shape": (I, [P, _SIZE4]),
         "ppocr_model_forward": (I, [P, FP, S, FP, S]),
         "ppocr_model_forward_pipelined": (I, [P, FP, S, FP, S]),
+        "ppocr_recognizer_forward_pipelined_ctc": (I, [P, FP, S, C.POINTER(C.c_int32), FP, S]),
         "ppocr_model_forward_image": (I, [P, P, FP, S, FP, S]),
         "ppocr_model_benchmark": (I, [P, FP, S, S, S, C.POINTER(C.c_double)]),
         "ppocr_model_forward_device": (I, [P, P, P, P]),
@@ -694,6 +695,22 @@ class Recognizer(_Model):
                                                       idx.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
                                                       _fptr(margin)))
         return idx, prob, margin
+
+    def forward_pipelined_ctc(self, values):
+        """forward_pipelined over any multiple of the batch, returning only the greedy-CTC
+        arg-max class and its probability per step, each [images, t]
+        (ppocr_recognizer_forward_pipelined_ctc)."""
+        x = np.ascontiguousarray(values, dtype=np.float32)
+        per_in = int(np.prod(self.input_shape[1:]))
+        if x.size % per_in:
+            raise InvalidInput(f"invalid input: {x.size} values are not whole {self.input_shape[1:]} images")
+        images, t = x.size // per_in, self.output_shape[1]
+        idx = np.empty((images, t), dtype=np.int32)
+        prob = np.empty((images, t), dtype=np.float32)
+        _check(library().ppocr_recognizer_forward_pipelined_ctc(self._h, _fptr(x), images,
+                                                                idx.ctypes.data_as(C.POINTER(C.c_int32)), _fptr(prob),
+                                                                idx.size))
+        return idx, prob
 
 
 # ---------------------------------------------------------------------------
