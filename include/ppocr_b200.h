@@ -269,6 +269,14 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
                            int act, const float* residual, int out_bf16, int ldc, int coff, float* c,
                            int* used_tensor_cores, int* wait_error);
 
+/* Diagnostic (new): the split GEMM's implicit-conv mode (FP32 operands in
+ * three BF16 pieces on tcgen05) on an NHWC FP32 input x [n, hi, wi, cin]
+ * (cin 32 or 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
+ * padding `pad` and stride 1 or 2; out receives [n, ho, wo, cout] NHWC,
+ * act as for ppocr_selftest_gemm_ex.  The model's dense FP32 convs over one
+ * 32- or 64-channel source use this path. */
+int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride,
+                              int pad, const float* x, const float* w, const float* bias, int act, float* out);
 /* Diagnostic (new): the FP32 pointwise GEMM of the FP32 mode,
  * C[m, n] = act((A * gate) W[n, k]^T + bias) + residual, all in F32, through
  * one chosen kernel: kernel 0 = the model's dispatch, 1 = the register-tiled

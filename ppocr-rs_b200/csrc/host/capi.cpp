@@ -1061,7 +1061,7 @@ int ppocr_selftest_wait_expiry(ppocr_gpu* gpu, int kernel, int wait_ms, int* cod
         cw.w.assign((size_t)n * k, 0.5f);
         cw.b.assign(n, 0.f);
         WeightBlob blob;
-        const int bn = kernel == 3 ? gemm_split_tile_n(n) : tc_engine_tile_n(n, planes);
+        const int bn = kernel == 3 ? gemm_split_tile_n(n, k) : tc_engine_tile_n(n, planes);
         const int n_pad = kernel == 0 ? (n + 15) / 16 * 16 : (n + bn - 1) / bn * bn, k_pad = (k + 63) / 64 * 64;
         const size_t wo = kernel == 0 ? blob.add_bf16(pack_gemm_nk(cw, n_pad, k_pad)) : blob.add_bf16(pack_engine_kn(cw, planes, n_pad, k_pad));
         const std::vector<float> av((size_t)m * k, 0.25f);
@@ -1345,6 +1345,62 @@ int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, 
     });
 }
 
+int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
+                              const float* x, const float* w, const float* bias, int act, float* out) {
+    return guard([&] {
+        if (!gpu || !x || !w || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
+        if (n <= 0 || hi <= 0 || wi <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0)
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: conv shape");
+        if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
+        const int ho = (hi + 2 * pad - kh) / stride + 1, wo = (wi + 2 * pad - kw) / stride + 1;
+        if (ho <= 0 || wo <= 0) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: empty conv output");
+        SplitGemmParams p;
+        p.conv = 1;
+        p.n_img = n; p.hi = hi; p.wi = wi; p.ho = ho; p.wo = wo; p.kh = kh; p.kw = kw; p.stride = stride; p.pt = pad; p.pl = pad;
+        p.k = kh * kw * cin; p.n = cout; p.lda = cin; p.ldc = cout; p.coff = 0; p.act = act;
+        const int bn = gemm_split_tile_n(cout, p.k);
+        p.n_pad = bn > 0 ? (cout + bn - 1) / bn * bn : 0;
+        p.k_pad = (p.k + 63) / 64 * 64;
+        p.m = n * ((ho + 7) / 8) * ((wo + 15) / 16) * 128;
+        if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split conv takes 32 or 64 input channels");
+        std::lock_guard<std::mutex> lock(gpu->mu);
+        gpu->bind();
+        ConvWeight cw;
+        cw.cout = cout; cw.cin = cin; cw.kh = kh; cw.kw = kw;
+        cw.w.assign(w, w + (size_t)cout * cin * kh * kw);
+        cw.b = bias ? std::vector<float>(bias, bias + cout) : std::vector<float>(cout, 0.f);
+        const size_t out_elems = (size_t)n * ho * wo * cout;
+        WeightBlob blob;
+        const size_t wo_ = blob.add_bf16(pack_engine_kn(cw, 3, p.n_pad, p.k_pad));
+        const size_t bo = blob.add_f32(cw.b);
+        const size_t xo = blob.add_f32(std::vector<float>(x, x + (size_t)n * hi * wi * cin));
+        const size_t co = blob.add_f32(std::vector<float>(out_elems, 0.f));
+        const size_t fo = blob.add_f32(std::vector<float>(64, 0.f));
+        const std::vector<uint8_t>& bytes = blob.bytes();
+        char* d = nullptr;
+        cuda_check(cudaMalloc(&d, bytes.size()), "allocate conv test buffers");
+        p.a = reinterpret_cast<const float*>(d + xo); p.w = d + wo_; p.bias = reinterpret_cast<const float*>(d + bo);
+        p.c = reinterpret_cast<float*>(d + co);
+        p.err = reinterpret_cast<int*>(d + fo);
+        int flag = 0;
+        cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+        if (e == cudaSuccess) e = launch_gemm_split(p, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(out, p.c, out_elems * 4, cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&flag, p.err, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
+        if (e == cudaSuccess) {
+            try {
+                wait_stream(gpu->stream, 0, gpu);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+        }
+        cudaFree(d);
+        cuda_check(e, "split conv self-test");
+        if (flag) fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(flag) + ")");
+    });
+}
+
 int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used) {
@@ -1359,8 +1415,8 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             SplitGemmParams p;
             p.m = m; p.n = n; p.k = k; p.lda = k; p.ldc = n; p.ldr = n; p.act = act;
             p.rows_per_image = gate ? rows_per_image : 1;
-            const int bn = gemm_split_tile_n(n);
-            p.n_pad = (n + bn - 1) / bn * bn;
+            const int bn = gemm_split_tile_n(n, k);
+            p.n_pad = bn > 0 ? (n + bn - 1) / bn * bn : 0;
             p.k_pad = (k + 63) / 64 * 64;
             if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split GEMM needs k % 16 == 0");
             std::lock_guard<std::mutex> lock(gpu->mu);

@@ -56,17 +56,28 @@ constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 12
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
 constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 FP32 columns
 constexpr int STAGE_BUFS = 2;                          // per epilogue warp: a store drains while the next group is written
+                                                       // (one when shared memory would leave a single FP32 stage)
 constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory per block
+
+// K blocks (64 wide) summed into one dominant-sum accumulator.  The tensor
+// core rounds its FP32 accumulator toward zero once per 16-wide K step, so the
+// error of a sum grows with the steps and the magnitude accumulated; 5 blocks
+// (K = 320) keep it at the CUDA-core FP32 kernels' level, and longer sums are
+// split over several accumulators added in the epilogue (round to nearest).
+constexpr int KCHUNK = 5;
 
 // Shared memory, 1024-byte aligned pieces: [resident W] [plane ring]
 // [epilogue staging] [FP32 ring: per stage the A boxes, then (streamed) W].
 struct SplitArgs {
     SplitGemmParams p;
     int bn, kt, m_tiles, n_tiles, tmem_cols;
+    int kchunk, dchunks;    // K blocks per dominant-sum accumulator, and their count
     int tiles_y, tiles_x;   // conv mode: tile grid per image
+    int cpt;                // conv mode: input channels per tap (32: two taps per K block; 64: one)
     int w_resident;         // 1: one K block and one N tile, W loaded once per CTA
     int stages;             // FP32 ring depth
     int plane_stages;       // BF16 plane ring depth (1 when one K block covers the GEMM)
+    int stage_bufs;         // output staging buffers per epilogue warp (1 or 2)
     int a_stage_bytes;      // one FP32 ring stage (A boxes + streamed W), 1024-aligned
     int a_box_bytes;        // the A boxes of a stage (1 or 2 boxes of 16 KB)
     int w_bytes;            // the three W pieces of one (K block, N tile)
@@ -165,7 +176,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
     uint8_t* sw_res = smem;
     uint8_t* splanes = smem + args.w_region;
     uint8_t* sout = splanes + args.plane_stages * PLANES_STAGE;
-    uint8_t* sring = sout + EPI_WARPS * STAGE_BUFS * STAGE_OUT;
+    uint8_t* sring = sout + EPI_WARPS * args.stage_bufs * STAGE_OUT;
     const int S = args.stages;
     const int PS = args.plane_stages;
     const int bn = args.bn;
@@ -229,17 +240,20 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     uint8_t* f = sring + (size_t)s * args.a_stage_bytes;
                     tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + (wres ? 0u : (uint32_t)args.w_bytes));
                     if (p.conv) {
-                        // Taps 2 kb and 2 kb + 1 (K order tap, channel), one box each:
-                        // the tile's 8 x 16 output pixels read input pixels
-                        // (oy s + ky - pt, ox s + kx - pl); outside the image reads 0.
+                        // K order (tap, channel).  32 channels: taps 2 kb and
+                        // 2 kb + 1, one box each; 64: tap kb, channels 0-31 and
+                        // 32-63 in two boxes.  The tile's 8 x 16 output pixels
+                        // read input pixels (oy s + ky - pt, ox s + kx - pl);
+                        // outside the image reads 0.
                         const int mt = tile / args.n_tiles, per = args.tiles_y * args.tiles_x;
                         const int img = mt / per, rt = mt - img * per;
                         const int yb = (rt / args.tiles_x) * 8 * p.stride - p.pt;
                         const int xb = (rt % args.tiles_x) * 16 * p.stride - p.pl;
                         for (int h = 0; h < (two ? 2 : 1); ++h) {
-                            const int tap = 2 * kb + h;
+                            const int tap = args.cpt == 32 ? 2 * kb + h : kb;
                             const int ky = tap / p.kw, kx = tap - ky * p.kw;
-                            tc::tma_load_4d(f + h * BOX_BYTES, &tma_a, &full[s], 0, xb + kx, yb + ky, img);
+                            tc::tma_load_4d(f + h * BOX_BYTES, &tma_a, &full[s], args.cpt == 32 ? 0 : 32 * h, xb + kx, yb + ky,
+                                            img);
                         }
                     } else {
                         tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
@@ -262,6 +276,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         if (lane == 0) {
             const uint32_t id3 = tc::idesc_bf16(BM, 3 * bn), id2 = tc::idesc_bf16(BM, 2 * bn), id1 = tc::idesc_bf16(BM, bn);
             const uint64_t a_step = (uint64_t)(PLANE_BYTES >> 4);
+            const uint64_t w1_step = (uint64_t)((bn * 128) >> 4);   // W piece 1 follows piece 0 (BN rows of 128 bytes)
             const int w_off = args.a_box_bytes;
             bool ok = !wres || tc::mbar_wait(&w_ready, 0, false, wait_ns, &abort_flag);
             if (!ok) {
@@ -277,7 +292,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     break;
                 }
                 tc::fence_after();
-                const uint32_t acc = tmem + (uint32_t)(b * 3 * bn);
+                const uint32_t acc = tmem + (uint32_t)(b * (2 + args.dchunks) * bn);
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
                     const int s = it % S, sp = it % PS;
                     if (!tc::mbar_wait(&planes_full[sp], (it / PS) & 1, false, wait_ns, &abort_flag) ||
@@ -292,12 +307,24 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     const uint64_t bd = tc::sw128_desc(tc::smem_u32(wres ? sw_res : sring + (size_t)s * args.a_stage_bytes + w_off));
                     const int rem = (p.k - kb * BK) / 16;
                     const int nk = rem < 4 ? rem : 4;
+                    const int chunk = kb / args.kchunk;
+                    const bool chunk_start = kb == chunk * args.kchunk;
                     for (int kk = 0; kk < nk; ++kk) {   // +32 bytes per 16-element K step
                         // a0 x [w0 w1 w2] -> [D | S1 | S2]; a1 x [w0 w1] -> [S1 | S2];
                         // a2 x w0 -> S1.  D only ever receives a0 w0, so the
                         // accumulation rounding of the dominant sum happens once
                         // per step; S1 (2^-8 D) and S2 (2^-16 D) take the rest.
-                        tc::mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, id3, (kb | kk) != 0 ? 1u : 0u);
+                        // Past the first kchunk K blocks the dominant sum moves to
+                        // a fresh accumulator D_c (a0 x w0 alone, a0 x [w1 w2]
+                        // into [S1 | S2]): the tensor core's accumulator rounding
+                        // error grows with the magnitude summed into it.
+                        if (chunk == 0) {
+                            tc::mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, id3, (kb | kk) != 0 ? 1u : 0u);
+                        } else {
+                            tc::mma_bf16(acc + (uint32_t)((2 + chunk) * bn), ad + 2 * kk, bd + 2 * kk, id1,
+                                         (chunk_start && kk == 0) ? 0u : 1u);
+                            tc::mma_bf16(acc + (uint32_t)bn, ad + 2 * kk, bd + w1_step + 2 * kk, id2, 1u);
+                        }
                         tc::mma_bf16(acc + (uint32_t)bn, ad + a_step + 2 * kk, bd + 2 * kk, id2, 1u);
                         tc::mma_bf16(acc + (uint32_t)bn, ad + 2 * a_step + 2 * kk, bd + 2 * kk, id1, 1u);
                     }
@@ -368,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         // accumulator buffer g and so every other tile: two tiles' epilogues
         // run at once, and each warp walks all of its tile's 16-column groups.
         const int q = warp & 3, grp = (warp - 6) >> 2;
-        uint8_t* stage0 = sout + (warp - 6) * STAGE_BUFS * STAGE_OUT;
+        uint8_t* stage0 = sout + (warp - 6) * args.stage_bufs * STAGE_OUT;
         int sbuf = 0;
         const int swz = (lane >> 1) & 3;   // 64-byte swizzle: chunk ^= row bits 1-2
         int ti = 0;
@@ -422,11 +449,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 break;
             }
             tc::fence_after();
-            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 3 * bn);
+            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * (2 + args.dchunks) * bn);
             for (int cb = 0; cb < bn && n0 + cb < p.n; cb += 16) {
                 const int col0 = n0 + cb;
                 uint32_t r0[16], r1[16], r2[16];
                 tc::tmem_ld16_async(tb + (uint32_t)cb, r0);
+                // Dominant sum: D_0 + D_1 + ... in order, rounded to nearest.
+                for (int c = 1; c < args.dchunks; ++c) {
+                    tc::tmem_ld16_async(tb + (uint32_t)((2 + c) * bn + cb), r1);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) r0[j] = __float_as_uint(__uint_as_float(r0[j]) + __uint_as_float(r1[j]));
+                }
                 tc::tmem_ld16_async(tb + (uint32_t)(bn + cb), r1);
                 tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb), r2);
                 float nres[16];
@@ -463,8 +497,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 // finished reading it once at most one store is pending.
                 uint8_t* stage = stage0 + sbuf * STAGE_OUT;
                 uint8_t* line = stage + lane * 64;
-                sbuf ^= 1;
-                if (lane == 0) tc::bulk_wait_read_1();
+                if (args.stage_bufs == 2) {
+                    sbuf ^= 1;
+                    if (lane == 0) tc::bulk_wait_read_1();
+                } else if (lane == 0) {
+                    tc::bulk_wait_read();
+                }
                 __syncwarp();
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
@@ -559,31 +597,60 @@ int sm_count() {
 
 }  // namespace
 
-int gemm_split_tile_n(int n) {
+int gemm_split_tile_n(int n, int k) {
     // One tile when it fits, else equal tiles; any multiple of 16 (the
-    // epilogue stores 16-column boxes, so none reaches the next tile).
+    // epilogue stores 16-column boxes, so none reaches the next tile).  The
+    // widest tile is 64 columns, less when the dominant-sum accumulators of a
+    // long K need the TMEM: two buffers of (2 + chunks) tile widths in 512
+    // columns.  0 when K needs more accumulators than fit at width 16.
+    const int kt = (k + BK - 1) / BK;
+    const int chunks = kt < 1 ? 1 : (kt + KCHUNK - 1) / KCHUNK;
+    int max_bn = 256 / (2 + chunks) / 16 * 16;
+    if (max_bn > MAX_BN) max_bn = MAX_BN;
+    if (max_bn < 16) return 0;
     const int n16 = (n + 15) / 16 * 16;
-    if (n16 <= MAX_BN) return n16;
-    const int tiles = (n16 + MAX_BN - 1) / MAX_BN;
+    if (n16 <= max_bn) return n16;
+    const int tiles = (n16 + max_bn - 1) / max_bn;
     const int bn = (n16 + tiles - 1) / tiles;
     return (bn + 15) / 16 * 16;
 }
 
+namespace {
+
+// K blocks of the GEMM: two 32-channel taps or one 64-channel tap per block in
+// conv mode, else ceil(K / 64).
+int split_k_blocks(const SplitGemmParams& p) {
+    if (p.conv) {
+        const int taps = p.kh * p.kw, cpt = taps > 0 ? p.k / taps : 0;
+        return cpt == 32 ? (taps + 1) / 2 : taps;
+    }
+    return (p.k + BK - 1) / BK;
+}
+
+// TMEM columns: two accumulator buffers of (2 + chunks) BN columns each,
+// rounded up to a power of two (0 when more than the 512 of an SM).
+int split_tmem_cols(int bn, int dchunks) {
+    int cols = 32;
+    while (cols < 2 * (2 + dchunks) * bn) cols <<= 1;
+    return cols > 512 ? 0 : cols;
+}
+
+}  // namespace
+
 bool gemm_split_supported(const SplitGemmParams& p) {
+    if (p.n <= 0 || p.k <= 0) return false;
+    const int bn = gemm_split_tile_n(p.n, p.k);
+    if (bn <= 0 || p.n_pad < (p.n + bn - 1) / bn * bn || p.k_pad % BK || p.k_pad < p.k) return false;
+    if (p.ldc % 4 || p.coff % 4 || p.ldc < p.coff + p.n) return false;
+    const int kt = split_k_blocks(p);
+    if (kt <= 0 || !split_tmem_cols(bn, (kt + KCHUNK - 1) / KCHUNK)) return false;
     if (p.conv) {
         const int cin = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
-        if (cin != 32 || p.k != p.kh * p.kw * 32 || p.lda % 4 || p.lda < 32 || p.gate || p.residual) return false;
-        if (p.n_img <= 0 || p.hi <= 0 || p.wi <= 0 || p.ho <= 0 || p.wo <= 0 || (p.stride != 1 && p.stride != 2)) return false;
-        if (p.ldc % 4 || p.coff % 4 || p.ldc < p.coff + p.n || p.n <= 0) return false;
-        if (p.k_pad % BK || p.k_pad < p.k) return false;
-        const int bn = gemm_split_tile_n(p.n);
-        return p.n_pad >= (p.n + bn - 1) / bn * bn;
+        if ((cin != 32 && cin != 64) || p.k != p.kh * p.kw * cin || p.lda % 4 || p.lda < cin || p.gate || p.residual)
+            return false;
+        return p.n_img > 0 && p.hi > 0 && p.wi > 0 && p.ho > 0 && p.wo > 0 && (p.stride == 1 || p.stride == 2);
     }
-    if (p.m <= 0 || p.n <= 0 || p.k <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k) return false;
-    if (p.k_pad % BK || p.k_pad < p.k) return false;
-    const int bn = gemm_split_tile_n(p.n);
-    if (p.n_pad < (p.n + bn - 1) / bn * bn) return false;
-    if (p.ldc % 4 || p.coff % 4 || p.ldc < p.coff + p.n) return false;
+    if (p.m <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k) return false;
     if (p.res_scale < 1 || (p.res_scale & (p.res_scale - 1))) return false;
     if ((p.gate || p.res_gate) && p.rows_per_image < 1) return false;
     return true;
@@ -596,23 +663,22 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     if (reinterpret_cast<uintptr_t>(cbase) % 16) return cudaErrorInvalidValue;
     SplitArgs a;
     a.p = in;
-    a.bn = gemm_split_tile_n(in.n);
+    a.bn = gemm_split_tile_n(in.n, in.k);
     a.n_tiles = (in.n + a.bn - 1) / a.bn;
+    a.kt = split_k_blocks(in);
+    a.cpt = in.conv ? in.k / (in.kh * in.kw) : 0;
     if (in.conv) {
         a.tiles_y = (in.ho + 7) / 8;
         a.tiles_x = (in.wo + 15) / 16;
         a.m_tiles = in.n_img * a.tiles_y * a.tiles_x;
-        a.kt = (in.kh * in.kw + 1) / 2;   // two taps of 32 channels per 64-wide K block
     } else {
         a.tiles_y = a.tiles_x = 0;
         a.m_tiles = (in.m + BM - 1) / BM;
-        a.kt = (in.k + BK - 1) / BK;
     }
-    // Two accumulators of 3 BN columns (BN a multiple of 16).
-    int cols = 32;
-    while (cols < 6 * a.bn) cols <<= 1;
-    if (cols > 512) return cudaErrorInvalidConfiguration;
-    a.tmem_cols = cols;
+    a.kchunk = KCHUNK;
+    a.dchunks = (a.kt + KCHUNK - 1) / KCHUNK;
+    a.tmem_cols = split_tmem_cols(a.bn, a.dchunks);
+    if (!a.tmem_cols) return cudaErrorInvalidConfiguration;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
     // Shared memory: the plane ring and the staging tiles are fixed; W is
     // resident when one K block and one N tile cover the GEMM; the rest is
@@ -625,14 +691,18 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
     a.a_stage_bytes = a.a_box_bytes + (a.w_resident ? 0 : up(a.w_bytes));
     a.plane_stages = a.kt == 1 ? 1 : PLANE_STAGES;
-    const int fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * STAGE_BUFS * STAGE_OUT;
-    a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
+    int fixed = 0;
+    for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
+        fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;
+        a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
+        if (a.stages >= 2) break;
+    }
     if (a.stages > MAX_A) a.stages = MAX_A;
     if (a.stages < 2) return cudaErrorInvalidConfiguration;
     const int smem = fixed + a.stages * a.a_stage_bytes;
     CUtensorMap ma, mw, mc;
     if (in.conv) {
-        if (!make_map4(&ma, in.a, 32, (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
+        if (!make_map4(&ma, in.a, (uint64_t)a.cpt, (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
                        16 * (uint32_t)in.stride, 8 * (uint32_t)in.stride, (uint32_t)in.stride, CU_TENSOR_MAP_SWIZZLE_128B) ||
             !make_map4(&mc, cbase, (uint64_t)in.n, (uint64_t)in.wo, (uint64_t)in.ho, (uint64_t)in.n_img, (uint64_t)in.ldc * 4,
                        16, 16, 2, 1, CU_TENSOR_MAP_SWIZZLE_64B))

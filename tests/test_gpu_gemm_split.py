@@ -5,7 +5,10 @@ are accumulated in FP32 in TMEM, so the result must stay within a few FP32
 ulps of the sum of |products| of the float64 result (the same bound the
 CUDA-core FP32 kernels meet), and close to the CUDA-core kernel's output.
 Shapes cover the detector's pointwise layers (k 32..320, n 16..320), ragged
-last tiles, several N tiles, the SE gate on A and the residual.
+last tiles, several N tiles, the SE gate on A, the residual, and K up to
+1,792 (the dominant sum split over up to six TMEM accumulators).  The
+implicit-conv mode (32 or 64 input channels per tap, stride 1 or 2, zero
+padding through the TMA box) is checked the same way against a float64 conv.
 """
 
 import math
@@ -37,6 +40,10 @@ SHAPES = [
     (299, 320, 160, 3, False, False, 1),         # stage-3 pw1: five N tiles, three K blocks
     (299, 160, 320, 0, False, True, 1),          # stage-3 pw2: K = 320
     (4096, 64, 32, 0, False, False, 1),
+    # K past 320: the dominant sum spread over several accumulators
+    (700, 64, 576, 1, False, False, 1),          # two accumulators (5 + 4 K blocks)
+    (300, 32, 1024, 3, True, False, 100),        # four
+    (257, 16, 1792, 0, False, True, 1),          # six (the medium detector's longest K)
 ]
 
 
@@ -65,3 +72,52 @@ def test_split_gemm_fp32_class(gpu, m, n, k, act, gated, res, rpi):
     c2, _ = gpu.selftest_gemm_f32(a, w, b, act, g, rpi, r, kernel=1)
     assert np.abs(c - c2).max() <= 1e-4 * max(1.0, float(np.abs(c2).max()))
 
+
+
+def _conv_ref(x, w, b, stride, pad):
+    n, hi, wi, cin = x.shape
+    cout, _, kh, kw = w.shape
+    ho, wo = (hi + 2 * pad - kh) // stride + 1, (wi + 2 * pad - kw) // stride + 1
+    xp = np.zeros((n, hi + 2 * pad, wi + 2 * pad, cin), np.float64)
+    xp[:, pad:pad + hi, pad:pad + wi] = x
+    out = np.zeros((n, ho, wo, cout), np.float64)
+    mag = np.zeros_like(out)
+    wd = w.astype(np.float64)
+    for ky in range(kh):
+        for kx in range(kw):
+            patch = xp[:, ky:ky + stride * (ho - 1) + 1:stride, kx:kx + stride * (wo - 1) + 1:stride]
+            out += patch @ wd[:, :, ky, kx].T
+            mag += np.abs(patch) @ np.abs(wd[:, :, ky, kx]).T
+    return out + b, mag + np.abs(b)
+
+
+CONVS = [
+    # n, hi, wi, cin, cout, k, stride, pad, act
+    (2, 33, 70, 32, 16, 3, 2, 1, 1),     # stem3: 32 channels, stride 2, ragged tiles
+    (2, 24, 40, 64, 16, 3, 1, 1, 1),     # head.conv_down: 64 channels, K = 576, two accumulators
+    (1, 17, 35, 64, 48, 3, 1, 1, 0),
+    (3, 9, 20, 32, 64, 3, 1, 1, 0),
+]
+
+
+@pytest.mark.parametrize("n,hi,wi,cin,cout,k,stride,pad,act", CONVS)
+def test_split_conv_fp32_class(gpu, n, hi, wi, cin, cout, k, stride, pad, act):
+    rng = np.random.default_rng(hi * 7 + wi + cin + cout)
+    x = rng.normal(0, 1, (n, hi, wi, cin)).astype(np.float32)
+    w = rng.normal(0, 1 / np.sqrt(cin * k * k), (cout, cin, k, k)).astype(np.float32)
+    b = rng.normal(0, 0.1, cout).astype(np.float32)
+    got = gpu.selftest_conv_split(x, w, b, stride=stride, pad=pad, act=act)
+    pre, mag = _conv_ref(x.astype(np.float64), w, b.astype(np.float64), stride, pad)
+    ref = _act(pre, act)
+    bound = 16 * 2.0 ** -24 * mag + 1e-30
+    err = np.abs(got - ref)
+    assert np.all(err <= bound * 1.5), f"worst {float((err / bound).max()):.2f}x the bound"
+
+
+def test_split_conv_rejects_other_channel_counts(gpu):
+    import ppocr_b200 as P
+
+    x = np.zeros((1, 8, 8, 48), np.float32)
+    w = np.zeros((16, 48, 3, 3), np.float32)
+    with pytest.raises(P.InvalidInput):
+        gpu.selftest_conv_split(x, w)
