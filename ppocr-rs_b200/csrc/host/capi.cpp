@@ -822,11 +822,9 @@ int ppocr_recognizer_forward_ctc(ppocr_model* model, const float* input, size_t 
 
 namespace {
 
-// Rectifies crops of (possibly different) images into the recognizer's input
-// slots 0..count-1, zero-fills the unused slots, runs the forward and returns
-// the greedy-CTC statistics of the first `count` rows.
-void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
-                   const size_t* content_widths, int32_t* indices, float* probabilities, float* margins) {
+// Checks of a crop forward's arguments.
+void check_crops(const ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+                 const size_t* content_widths) {
     if (!model || !images || !corners || !content_widths) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
     if (model->m.kind != Kind::Recognizer) fail(PPOCR_ERR_INVALID_INPUT, "crop forward needs a recognizer");
     if (count == 0 || count > (size_t)model->m.n)
@@ -839,7 +837,14 @@ void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t 
     }
     for (size_t i = 0; i < count * 8; ++i)
         if (!std::isfinite(corners[i])) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: corners must be finite");
-    std::lock_guard<std::mutex> lock(model->gpu->mu);
+}
+
+// Enqueues on the model's stream (lock held): the rectification of the
+// crops into input slots 0..count-1, zeros in the unused slots, the forward
+// and the copies of the first `count` rows' greedy-CTC statistics to the
+// host arrays (any may be null).
+void enqueue_crops(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+                   const size_t* content_widths, int32_t* indices, float* probabilities, float* margins, bool reset_flags) {
     model->gpu->bind();
     model->gpu->ensure_arena(model->m.plan.arena_bytes);
     cudaStream_t s = model->gpu->stream;
@@ -854,26 +859,72 @@ void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t 
     if (count < (size_t)model->m.n)
         cuda_check(cudaMemsetAsync(in + count * per, 0, ((size_t)model->m.n - count) * per * sizeof(float), s),
                    "clear unused crop slots");
-    cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
+    if (reset_flags) cuda_check(cudaMemsetAsync(model->dflags, 0, kFlags * sizeof(int), s), "reset flags");
     model->run(s);
     const size_t rows = count * model->m.t;
-    std::vector<int32_t> idx(rows);
-    std::vector<float> prob(rows);
-    download(model, model->m.index, idx.data(), rows * 4);
-    download(model, model->m.max_prob, prob.data(), rows * 4);
+    if (indices) download(model, model->m.index, indices, rows * 4);
+    if (probabilities) download(model, model->m.max_prob, probabilities, rows * 4);
     if (margins) download(model, model->m.margin, margins, rows * 4);
-    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
-    wait_stream(s, 0, model->gpu);
-    raise_flags(model);
-    // A non-finite logit row leaves no arg-max (index -1) or a non-finite probability.
+}
+
+// After the stream wait: a non-finite logit row leaves no arg-max (index -1)
+// or a non-finite probability.
+void check_ctc_rows(const ppocr_model* model, const int32_t* idx, const float* prob, size_t rows) {
     for (size_t r = 0; r < rows; ++r)
         if (idx[r] < 0 || idx[r] >= model->m.classes || !std::isfinite(prob[r]))
             fail(PPOCR_ERR_GPU, "GPU error: model output contains non-finite values");
+}
+
+// Rectifies crops of (possibly different) images into the recognizer's input
+// slots 0..count-1, zero-fills the unused slots, runs the forward and returns
+// the greedy-CTC statistics of the first `count` rows.
+void forward_crops(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+                   const size_t* content_widths, int32_t* indices, float* probabilities, float* margins) {
+    check_crops(model, images, count, corners, content_widths);
+    std::lock_guard<std::mutex> lock(model->gpu->mu);
+    const size_t rows = count * model->m.t;
+    std::vector<int32_t> idx(rows);
+    std::vector<float> prob(rows);
+    enqueue_crops(model, images, count, corners, content_widths, idx.data(), prob.data(), margins, true);
+    cudaStream_t s = model->gpu->stream;
+    cuda_check(cudaMemcpyAsync(model->hflags, model->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, s), "read flags");
+    wait_stream(s, 0, model->gpu);
+    raise_flags(model);
+    check_ctc_rows(model, idx.data(), prob.data(), rows);
     if (indices) std::memcpy(indices, idx.data(), rows * 4);
     if (probabilities) std::memcpy(probabilities, prob.data(), rows * 4);
 }
 
 }  // namespace
+
+void ppocr::CropBatch::add(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+                           const size_t* content_widths, int32_t* indices, float* probabilities) {
+    check_crops(model, images, count, corners, content_widths);
+    if (gpu_ && model->gpu != gpu_) fail(PPOCR_ERR_INVALID_INPUT, "crop batch spans two GPUs");
+    gpu_ = model->gpu;
+    std::lock_guard<std::mutex> lock(model->gpu->mu);
+    const bool first = std::find(models_.begin(), models_.end(), model) == models_.end();
+    enqueue_crops(model, images, count, corners, content_widths, indices, probabilities, nullptr, first);
+    if (first) models_.push_back(model);
+    rows_.push_back({model, indices, probabilities, count * (size_t)model->m.t});
+}
+
+void ppocr::CropBatch::wait() {
+    if (!gpu_) return;
+    {
+        std::lock_guard<std::mutex> lock(gpu_->mu);
+        gpu_->bind();
+        for (ppocr_model* m : models_)
+            cuda_check(cudaMemcpyAsync(m->hflags, m->dflags, kFlags * sizeof(int), cudaMemcpyDeviceToHost, gpu_->stream),
+                       "read flags");
+        wait_stream(gpu_->stream, 0, gpu_);
+    }
+    for (ppocr_model* m : models_) raise_flags(m);
+    for (const Rows& r : rows_) check_ctc_rows(r.model, r.idx, r.prob, r.rows);
+    models_.clear();
+    rows_.clear();
+    gpu_ = nullptr;
+}
 
 int ppocr_recognizer_forward_crops(ppocr_model* model, const ppocr_image* image, size_t count, const float* corners,
                                    const size_t* content_widths, int32_t* indices, float* probabilities,

@@ -123,6 +123,10 @@ struct ppocr_engine {
     std::vector<ppocr_image*> page_pool;
     uint8_t* pinned = nullptr;
     size_t pinned_bytes = 0;
+    // Page-locked staging of the recognition stage's greedy-CTC rows
+    // (indices, then probabilities), grown as needed.
+    uint8_t* ctc_host = nullptr;
+    size_t ctc_bytes = 0;
 
     ~ppocr_engine() {
         for (auto& e : det_cache) ppocr_model_destroy(e.second);
@@ -130,6 +134,7 @@ struct ppocr_engine {
         if (rec_weights) ppocr_model_destroy(rec_weights);
         for (ppocr_image* im : page_pool) ppocr_image_destroy(im);
         if (pinned) cudaFreeHost(pinned);
+        if (ctc_host) cudaFreeHost(ctc_host);
     }
 
 
@@ -146,12 +151,18 @@ struct ppocr_engine {
         return m;
     }
 
-    ppocr_model* recognizer(const Shape& shape) {
+    // The session of `shape` (loaded on first use).  A full cache drops its
+    // oldest session that is not in `keep` (the sessions a pending batch uses).
+    ppocr_model* recognizer(const Shape& shape, const std::vector<ppocr_model*>& keep = {}) {
         for (auto& e : rec_cache)
             if (e.first == shape) return e.second;
-        if (rec_cache.size() == kRecognizerCache) {
-            ppocr_model_destroy(rec_cache.front().second);
-            rec_cache.erase(rec_cache.begin());
+        if (rec_cache.size() >= kRecognizerCache) {
+            for (auto it = rec_cache.begin(); it != rec_cache.end(); ++it)
+                if (std::find(keep.begin(), keep.end(), it->second) == keep.end()) {
+                    ppocr_model_destroy(it->second);
+                    rec_cache.erase(it);
+                    break;
+                }
         }
         ppocr_model* m = nullptr;
         check(ppocr_recognizer_load_ex(gpu, rec_path.c_str(), rec_size, shape.data(), &rec_load, rec_weights, &m));
@@ -246,39 +257,66 @@ struct ppocr_engine {
             for (const RecBatch& b : recognition_batches(dets[i]))
                 for (size_t k = 0; k < b.index.size(); ++k) by_width[b.width].push_back(Crop{i, b.index[k], b.content[k]});
         }
+        // One forward per (canvas width, up to kRecognizerBatch crops), all
+        // enqueued back to back and waited for once; the greedy-CTC rows land
+        // in the engine's page-locked staging.
+        struct Forward {
+            ppocr_model* rec;
+            const std::vector<Crop>* crops;
+            size_t first, n, width, steps, row0;
+        };
+        std::vector<Forward> forwards;
+        std::vector<ppocr_model*> in_use;
+        size_t total_rows = 0;
         for (const auto& [width, crops] : by_width) {
             for (size_t s = 0; s < crops.size(); s += kRecognizerBatch) {
                 const size_t n = std::min(kRecognizerBatch, crops.size() - s);
                 size_t shape_n = kRecognizerBatch;
                 for (size_t b : kTailBatches)
                     if (n <= b) { shape_n = b; break; }
-                ppocr_model* rec = recognizer(Shape{shape_n, 3, 48, width});
+                ppocr_model* rec = recognizer(Shape{shape_n, 3, 48, width}, in_use);
+                in_use.push_back(rec);
                 size_t out_shape[4] = {0, 0, 0, 0};
                 check(ppocr_model_output_shape(rec, out_shape, nullptr, nullptr));
-                const size_t steps = out_shape[1];
-                std::vector<const ppocr_image*> ims(n);
-                std::vector<float> corners(n * 8);
-                std::vector<size_t> contents(n);
-                for (size_t k = 0; k < n; ++k) {
-                    const Crop& c = crops[s + k];
-                    ims[k] = imgs[c.page].p;
-                    contents[k] = c.content;
-                    for (int q = 0; q < 4; ++q) {
-                        corners[k * 8 + 2 * q] = dets[c.page][c.det].poly[q].x;
-                        corners[k * 8 + 2 * q + 1] = dets[c.page][c.det].poly[q].y;
-                    }
-                }
-                std::vector<int32_t> idx(n * steps);
-                std::vector<float> p(n * steps);
-                check(ppocr_recognizer_forward_crops_ex(rec, ims.data(), n, corners.data(), contents.data(), idx.data(),
-                                                        p.data(), nullptr));
-                for (size_t k = 0; k < n; ++k) {
-                    const Crop& c = crops[s + k];
-                    decoded[c.page][c.det] = decode_ctc_steps(idx.data() + k * steps, p.data() + k * steps, steps, classes,
-                                                              dict, c.content, width);
-                }
+                forwards.push_back(Forward{rec, &crops, s, n, width, out_shape[1], total_rows});
+                total_rows += n * out_shape[1];
             }
         }
+        if (total_rows * 8 > ctc_bytes) {
+            std::lock_guard<std::mutex> lock(gpu->mu);
+            gpu->bind();
+            if (ctc_host) cudaFreeHost(ctc_host);
+            ctc_host = nullptr;
+            ctc_bytes = 0;
+            cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&ctc_host), total_rows * 8, cudaHostAllocPortable),
+                       "allocate CTC staging");
+            ctc_bytes = total_rows * 8;
+        }
+        int32_t* all_idx = reinterpret_cast<int32_t*>(ctc_host);
+        float* all_prob = reinterpret_cast<float*>(ctc_host + total_rows * 4);
+        CropBatch batch;
+        for (const Forward& f : forwards) {
+            std::vector<const ppocr_image*> ims(f.n);
+            std::vector<float> corners(f.n * 8);
+            std::vector<size_t> contents(f.n);
+            for (size_t k = 0; k < f.n; ++k) {
+                const Crop& c = (*f.crops)[f.first + k];
+                ims[k] = imgs[c.page].p;
+                contents[k] = c.content;
+                for (int q = 0; q < 4; ++q) {
+                    corners[k * 8 + 2 * q] = dets[c.page][c.det].poly[q].x;
+                    corners[k * 8 + 2 * q + 1] = dets[c.page][c.det].poly[q].y;
+                }
+            }
+            batch.add(f.rec, ims.data(), f.n, corners.data(), contents.data(), all_idx + f.row0, all_prob + f.row0);
+        }
+        batch.wait();
+        for (const Forward& f : forwards)
+            for (size_t k = 0; k < f.n; ++k) {
+                const Crop& c = (*f.crops)[f.first + k];
+                const size_t r = f.row0 + k * f.steps;
+                decoded[c.page][c.det] = decode_ctc_steps(all_idx + r, all_prob + r, f.steps, classes, dict, c.content, f.width);
+            }
         lap(3);
         for (size_t i = 0; i < np; ++i)
             for (size_t d = 0; d < dets[i].size(); ++d) {

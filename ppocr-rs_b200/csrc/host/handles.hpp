@@ -127,6 +127,42 @@ private:
     int readers_ = 0;
 };
 
+// Recognizer crop forwards enqueued back to back on one device's stream and
+// waited for once (the engine's recognition stage: one forward per chunk
+// canvas width).  add() enqueues what ppocr_recognizer_forward_crops_ex runs,
+// with the greedy-CTC rows copied to `indices` / `probabilities`, which must be
+// page-locked host memory valid until wait(); wait() synchronises, then raises
+// the models' errors as the single-forward call would.  A model's device
+// flags are reset at its first forward of the batch and read back once.
+class CropBatch {
+public:
+    CropBatch() = default;
+    CropBatch(const CropBatch&) = delete;
+    CropBatch& operator=(const CropBatch&) = delete;
+    // An unfinished batch (an error between add() and wait()) still waits for
+    // its copies before the host buffers can be reused.
+    ~CropBatch() {
+        try {
+            wait();
+        } catch (...) {
+        }
+    }
+    void add(ppocr_model* model, const ppocr_image* const* images, size_t count, const float* corners,
+             const size_t* content_widths, int32_t* indices, float* probabilities);
+    void wait();
+
+private:
+    struct Rows {
+        const ppocr_model* model;
+        const int32_t* idx;
+        const float* prob;
+        size_t rows;
+    };
+    ppocr_gpu* gpu_ = nullptr;
+    std::vector<ppocr_model*> models_;
+    std::vector<Rows> rows_;
+};
+
 // ppocr_engine_recognize_batch with the results as strings; the page bytes
 // are read only inside `gate` (null: no gate).  Error::InvalidInput when the
 // gate has closed before the pages were read.

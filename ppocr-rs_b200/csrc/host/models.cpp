@@ -6,6 +6,7 @@
 #include "models.hpp"
 
 #include <algorithm>
+#include <memory>
 #include <sstream>
 
 #include "common.hpp"
@@ -163,35 +164,6 @@ public:
             fail(PPOCR_ERR_INVALID_MODEL, name + ": concatenation slice does not fit");
         Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
-        if (split_gemms() && (srcs.size() > 1 || srcs[0].scale != 1 || srcs[0].coff != 0) && (cin == 32 || cin == 64) &&
-            residual < 0 && sh == sw && split_conv_ok(cw, n, hi, wi, ho, wo, sh, pt, pl)) {
-            // FP32 mode, several (upsampled) NHWC sources: materialise their
-            // concatenation (upsample_and_cat_nchw, src/cpu/model.rs:1322) and
-            // run the split conv over it.
-            bool plain = true;
-            for (auto& s : srcs)
-                plain = plain && s.mode == SRC_NHWC && s.channels % 4 == 0 && s.cstride % 4 == 0 && s.coff % 4 == 0 &&
-                        s.scale >= 1 && hi % s.scale == 0 && wi % s.scale == 0;
-            if (plain && srcs.size() <= 4) {
-                Act4 cat = tensor(name + ".cat", n, hi, wi, cin);
-                UpsampleCatParams up;
-                up.n = n; up.h = hi; up.w = wi; up.nsrc = (int)srcs.size(); up.out_c = cin;
-                std::vector<int> reads;
-                for (size_t i = 0; i < srcs.size(); ++i) {
-                    up.src[i].channels = srcs[i].channels; up.src[i].cstride = srcs[i].cstride;
-                    up.src[i].coff = srcs[i].coff; up.src[i].scale = srcs[i].scale; up.src[i].mode = SRC_NHWC;
-                    reads.push_back(srcs[i].tid);
-                }
-                const int ctid = cat.tid;
-                m_.plan.add_op(name + ".cat", reads, {ctid}, [up, reads, ctid](const Ctx& c, cudaStream_t st) mutable {
-                    for (size_t i = 0; i < reads.size(); ++i) up.src[i].ptr = c.act(reads[i]);
-                    up.out = static_cast<float*>(c.act(ctid));
-                    return launch_upsample_cat(up, st);
-                }, "cat", 0, 0.0);
-                return conv(name, cw, {{cat.tid, cin, cin, 0, 1, SRC_NHWC}}, n, hi, wi, sh, sw, pt, pl, pb, pr, act, residual,
-                            res_scale, into, into_coff, any_order);
-            }
-        }
         if (split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 && srcs[0].coff == 0 &&
             residual < 0 && sh == sw) {
             // FP32 mode: a dense conv over one plain 32-channel NHWC source as an
@@ -364,23 +336,6 @@ public:
     // zero, so the kernel sums at most K = 320 into one accumulator and adds
     // longer sums' partial accumulators in the epilogue (K up to 1,792 on the
     // medium detector).
-    // The split GEMM's implicit conv takes this conv (over one plain NHWC
-    // source of cw.cin channels).
-    bool split_conv_ok(const ConvWeight& cw, int n, int hi, int wi, int ho, int wo, int stride, int pt, int pl) const {
-        if (!split_gemms()) return false;
-        SplitGemmParams sp;
-        sp.conv = 1;
-        sp.n_img = n; sp.hi = hi; sp.wi = wi; sp.ho = ho; sp.wo = wo; sp.kh = cw.kh; sp.kw = cw.kw;
-        sp.stride = stride; sp.pt = pt; sp.pl = pl;
-        sp.k = cw.kh * cw.kw * cw.cin; sp.n = cw.cout; sp.lda = cw.cin; sp.ldc = cw.cout;
-        const int bn = gemm_split_tile_n(cw.cout, sp.k);
-        if (bn <= 0) return false;
-        sp.n_pad = (cw.cout + bn - 1) / bn * bn;
-        sp.k_pad = (sp.k + 63) / 64 * 64;
-        sp.m = 1;
-        return gemm_split_supported(sp);
-    }
-
     bool split_gemm_ok(int k, int n) const {
         if (!split_gemms()) return false;
         SplitGemmParams p;

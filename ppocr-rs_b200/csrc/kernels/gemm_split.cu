@@ -55,8 +55,19 @@ constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows
 constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
 constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 FP32 columns
-constexpr int STAGE_BUFS = 2;                          // per epilogue warp: a store drains while the next group is written
-                                                       // (one when shared memory would leave a single FP32 stage)
+#ifndef SPLIT_STAGE_BUFS
+#define SPLIT_STAGE_BUFS 2
+#endif
+#ifndef SPLIT_SINGLE_BLOCK_PLANES
+#define SPLIT_SINGLE_BLOCK_PLANES 2
+#endif
+// Output staging buffers per epilogue warp: with two, a store drains while the
+// next group is written (one when shared memory would leave a single FP32
+// stage).  BF16 plane ring depth of single-K-block GEMMs: with two, the
+// converters split tile i + 1 while the MMAs read tile i (measured 97 -> 86 us
+// on the detector's stage-0 GEMMs against one buffer and a deeper FP32 ring).
+constexpr int STAGE_BUFS = SPLIT_STAGE_BUFS;
+constexpr int SINGLE_BLOCK_PLANES = SPLIT_SINGLE_BLOCK_PLANES;
 constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory per block
 
 // K blocks (64 wide) summed into one dominant-sum accumulator.  The tensor
@@ -690,7 +701,7 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.w_region = a.w_resident ? up(a.w_bytes) : 0;
     a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
     a.a_stage_bytes = a.a_box_bytes + (a.w_resident ? 0 : up(a.w_bytes));
-    a.plane_stages = a.kt == 1 ? 1 : PLANE_STAGES;
+    a.plane_stages = a.kt == 1 ? SINGLE_BLOCK_PLANES : PLANE_STAGES;
     int fixed = 0;
     for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
         fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;

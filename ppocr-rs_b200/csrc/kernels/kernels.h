@@ -352,6 +352,7 @@ struct MaxPoolParams {
 };
 cudaError_t launch_maxpool_same_upper(const MaxPoolParams& p, cudaStream_t stream);
 
+
 // ---------------------------------------------------------------------------
 // Recognizer ops
 // ---------------------------------------------------------------------------
@@ -423,18 +424,6 @@ cudaError_t launch_nchw_to_nhwc(const float* in, void* out, int n, int c, int h,
 cudaError_t launch_to_f32(const void* in, float* out, size_t count, DType dt, cudaStream_t stream);
 cudaError_t launch_check_finite(const float* in, size_t count, int* flag, cudaStream_t stream);
 // dst[0, count) = src[0, count), *flag = 1 if any value is not finite (16-byte aligned buffers).
-// Concatenation of up to four FP32 NHWC sources, each nearest-upsampled by
-// its `scale`, into one FP32 NHWC tensor [n, h, w, out_c] (the channel counts
-// and strides multiples of 4): upsample_and_cat_nchw of the detector head
-// (src/cpu/model.rs:1322), materialised for the tensor-core conv that follows.
-struct UpsampleCatParams {
-    int n = 0, h = 0, w = 0;
-    ConvSource src[4];
-    int nsrc = 0;
-    float* out = nullptr;
-    int out_c = 0;
-};
-cudaError_t launch_upsample_cat(const UpsampleCatParams& p, cudaStream_t stream);
 cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* flag, cudaStream_t stream);
 // Copies `count` 32-bit words on `stream` as a kernel (a copy-engine copy
 // would queue behind the copies of other streams).

@@ -634,28 +634,6 @@ __global__ void copy_check_kernel(const float* __restrict__ src, float* __restri
     if (bad) *flag = 1;
 }
 
-// One thread per (pixel, 4-channel group) of the output: a 16-byte load from
-// the owning source's upsampled pixel, a 16-byte store.
-__global__ void __launch_bounds__(256) upsample_cat_kernel(UpsampleCatParams p) {
-    const int groups = p.out_c >> 2;
-    const size_t total = (size_t)p.n * p.h * p.w * groups;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const size_t px = i / groups;
-        int g = (int)(i - px * groups) * 4;
-        const int x = (int)(px % p.w);
-        const size_t t = px / p.w;
-        const int y = (int)(t % p.h), img = (int)(t / p.h);
-        int s = 0;
-        while (s + 1 < p.nsrc && g >= p.src[s].channels) g -= p.src[s++].channels;
-        const ConvSource& src = p.src[s];
-        const int sh = p.h / src.scale, sw = p.w / src.scale;
-        const size_t spx = ((size_t)img * sh + y / src.scale) * sw + x / src.scale;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(src.ptr) + spx * src.cstride + src.coff + g));
-        reinterpret_cast<float4*>(p.out)[i] = v;
-    }
-}
-
 __global__ void copy_words_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, size_t count) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) dst[i] = src[i];
@@ -853,22 +831,6 @@ cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* f
     if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return cudaErrorInvalidValue;
     if (count == 0) return cudaSuccess;
     copy_check_kernel<<<grid_for((long long)(count / 4 + 1), 256), 256, 0, stream>>>(src, dst, count, flag);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_upsample_cat(const UpsampleCatParams& p, cudaStream_t stream) {
-    if (p.n <= 0 || p.h <= 0 || p.w <= 0 || p.nsrc < 1 || p.nsrc > 4 || !p.out || p.out_c % 4) return cudaErrorInvalidValue;
-    int total_c = 0;
-    for (int s = 0; s < p.nsrc; ++s) {
-        const ConvSource& src = p.src[s];
-        if (!src.ptr || src.mode != SRC_NHWC || src.channels % 4 || src.cstride % 4 || src.coff % 4 || src.scale < 1 ||
-            p.h % src.scale || p.w % src.scale || reinterpret_cast<uintptr_t>(src.ptr) % 16)
-            return cudaErrorInvalidValue;
-        total_c += src.channels;
-    }
-    if (total_c != p.out_c || reinterpret_cast<uintptr_t>(p.out) % 16) return cudaErrorInvalidValue;
-    const long long items = (long long)p.n * p.h * p.w * (p.out_c / 4);
-    upsample_cat_kernel<<<grid_for(items, 256), 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
