@@ -67,6 +67,9 @@ constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 
 // converters split tile i + 1 while the MMAs read tile i (measured 97 -> 86 us
 // on the detector's stage-0 GEMMs against one buffer and a deeper FP32 ring).
 constexpr int STAGE_BUFS = SPLIT_STAGE_BUFS;
+// Resident W of a CTA's N tile (all K blocks) up to this size; larger W
+// streams through the FP32 ring beside each A stage.
+constexpr int W_RESIDENT_MAX = 48 * 1024;
 constexpr int SINGLE_BLOCK_PLANES = SPLIT_SINGLE_BLOCK_PLANES;
 constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory per block
 
@@ -85,7 +88,8 @@ struct SplitArgs {
     int kchunk, dchunks;    // K blocks per dominant-sum accumulator, and their count
     int tiles_y, tiles_x;   // conv mode: tile grid per image
     int cpt;                // conv mode: input channels per tap (32: two taps per K block; 64: one)
-    int w_resident;         // 1: one K block and one N tile, W loaded once per CTA
+    int w_resident;         // 1: every tile of a CTA has the same N tile, whose W (all K blocks) is loaded once
+    int w_block;            // resident W bytes per K block, 1024-aligned
     int stages;             // FP32 ring depth
     int plane_stages;       // BF16 plane ring depth (1 when one K block covers the GEMM)
     int stage_bufs;         // output staging buffers per epilogue warp (1 or 2)
@@ -226,10 +230,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             int last_it[MAX_A];
             for (int s = 0; s < MAX_A; ++s) last_it[s] = -1;
             if (wres) {
-                // One K block and one N tile: the CTA's W never changes.
-                tc::mbar_expect_tx(&w_ready, (uint32_t)args.w_bytes);
+                // The CTA's tiles share one N tile (the grid is a multiple of
+                // the N tile count, or one tile per CTA): its W never changes.
+                const int n0w = (blockIdx.x % args.n_tiles) * bn;
+                tc::mbar_expect_tx(&w_ready, (uint32_t)(args.kt * args.w_bytes));
+                for (int kb = 0; kb < args.kt; ++kb)
 #pragma unroll
-                for (int j = 0; j < 3; ++j) tc::tma_load_2d(sw_res + j * bn * 128, &tma_w, &w_ready, 0, j * p.n_pad);
+                    for (int j = 0; j < 3; ++j)
+                        tc::tma_load_2d(sw_res + kb * args.w_block + j * bn * 128, &tma_w, &w_ready, kb * BK, j * p.n_pad + n0w);
             }
             int it = 0;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
@@ -315,7 +323,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     }
                     tc::fence_after();
                     const uint64_t ad = tc::sw128_desc(tc::smem_u32(splanes + sp * PLANES_STAGE));
-                    const uint64_t bd = tc::sw128_desc(tc::smem_u32(wres ? sw_res : sring + (size_t)s * args.a_stage_bytes + w_off));
+                    const uint64_t bd = tc::sw128_desc(
+                        tc::smem_u32(wres ? sw_res + kb * args.w_block : sring + (size_t)s * args.a_stage_bytes + w_off));
                     const int rem = (p.k - kb * BK) / 16;
                     const int nk = rem < 4 ? rem : 4;
                     const int chunk = kb / args.kchunk;
@@ -692,21 +701,33 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     if (!a.tmem_cols) return cudaErrorInvalidConfiguration;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
     // Shared memory: the plane ring and the staging tiles are fixed; W is
-    // resident when one K block and one N tile cover the GEMM; the rest is
+    // resident when each CTA keeps one N tile and its K blocks fit; the rest is
     // the FP32 ring, as deep as fits (deeper rings keep more loads in flight).
     const int align = 1024;
     auto up = [&](int v) { return (v + align - 1) / align * align; };
     a.w_bytes = 3 * a.bn * BK * 2;
-    a.w_resident = (a.kt == 1 && a.n_tiles == 1) ? 1 : 0;
-    a.w_region = a.w_resident ? up(a.w_bytes) : 0;
+    a.w_block = up(a.w_bytes);
+    // Grid: one CTA per SM; with several N tiles, a multiple of their count
+    // (dropping at most n_tiles - 1 SMs) so that each CTA keeps one N tile and
+    // its W can stay in shared memory for the launch.
+    const int tiles = a.m_tiles * a.n_tiles;
+    const int sms = sm_count();
+    int grid = tiles < sms ? tiles : sms;
+    if (tiles > sms && a.n_tiles > 1 && a.n_tiles <= sms / 2) grid = sms - sms % a.n_tiles;
+    const bool fixed_n = tiles <= grid || grid % a.n_tiles == 0;
     a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
-    a.a_stage_bytes = a.a_box_bytes + (a.w_resident ? 0 : up(a.w_bytes));
     a.plane_stages = a.kt == 1 ? SINGLE_BLOCK_PLANES : PLANE_STAGES;
     int fixed = 0;
-    for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
-        fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;
-        a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
-        if (a.stages >= 2) break;
+    a.stages = 0;
+    for (int resident = (fixed_n && a.kt * a.w_block <= W_RESIDENT_MAX) ? 1 : 0; resident >= 0 && a.stages < 2; --resident) {
+        a.w_resident = resident;
+        a.w_region = resident ? a.kt * a.w_block : 0;
+        a.a_stage_bytes = a.a_box_bytes + (resident ? 0 : a.w_block);
+        for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
+            fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;
+            a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
+            if (a.stages >= 2) break;
+        }
     }
     if (a.stages > MAX_A) a.stages = MAX_A;
     if (a.stages < 2) return cudaErrorInvalidConfiguration;
@@ -728,8 +749,6 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
         return cudaErrorInvalidValue;
 
-    const int tiles = a.m_tiles * a.n_tiles;
-    const int grid = tiles < sm_count() ? tiles : sm_count();
     switch (in.act) {
         case ACT_NONE: return launch_act<ACT_NONE>(ma, mw, mc, a, grid, smem, stream);
         case ACT_RELU: return launch_act<ACT_RELU>(ma, mw, mc, a, grid, smem, stream);
