@@ -67,6 +67,13 @@ constexpr int EPI_WARPS = 8, STAGE_OUT = 32 * 64;      // staging: 32 rows x 16 
 // converters split tile i + 1 while the MMAs read tile i (measured 97 -> 86 us
 // on the detector's stage-0 GEMMs against one buffer and a deeper FP32 ring).
 constexpr int STAGE_BUFS = SPLIT_STAGE_BUFS;
+#ifndef SPLIT_ROLE_BACKOFF
+#define SPLIT_ROLE_BACKOFF 1
+#endif
+// The single-thread producer and MMA roles sleep briefly between polls once a
+// wait has spun a while, leaving the issue slots of their sub-partitions to
+// the converter and epilogue warps that share them.
+constexpr bool ROLE_BACKOFF = SPLIT_ROLE_BACKOFF != 0;
 // Resident W of a CTA's N tile (all K blocks) up to this size; larger W
 // streams through the FP32 ring beside each A stage.
 constexpr int W_RESIDENT_MAX = 48 * 1024;
@@ -187,7 +194,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         planes_empty[PLANE_STAGES], w_ready, acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // Up to the next 1024-byte boundary by offsetting the shared pointer itself:
+    // the compiler keeps its address space, so the tile reads and writes below
+    // are shared-memory instructions rather than generic ones.
+    uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sw_res = smem;
     uint8_t* splanes = smem + args.w_region;
     uint8_t* sout = splanes + args.plane_stages * PLANES_STAGE;
@@ -246,8 +256,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     const int s = it % S;
                     if (it >= S) {
                         const uint32_t par = ((it / S) + 1) & 1;
-                        if (!tc::mbar_wait(&f32_empty[s], par, false, wait_ns, &abort_flag) ||
-                            (!wres && !tc::mbar_wait(&w_free[s], par, false, wait_ns, &abort_flag))) {
+                        if (!tc::mbar_wait(&f32_empty[s], par, ROLE_BACKOFF, wait_ns, &abort_flag) ||
+                            (!wres && !tc::mbar_wait(&w_free[s], par, ROLE_BACKOFF, wait_ns, &abort_flag))) {
                             report(p, 1);
                             abort_flag = 1;
                             break;
@@ -305,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; ok && tile < total && !abort_flag; tile += gridDim.x, ++ti) {
                 const int b = ti & 1;
-                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, false, wait_ns, &abort_flag)) {
+                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, ROLE_BACKOFF, wait_ns, &abort_flag)) {
                     report(p, 2);
                     abort_flag = 1;
                     break;
@@ -314,8 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 const uint32_t acc = tmem + (uint32_t)(b * (2 + args.dchunks) * bn);
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
                     const int s = it % S, sp = it % PS;
-                    if (!tc::mbar_wait(&planes_full[sp], (it / PS) & 1, false, wait_ns, &abort_flag) ||
-                        (!wres && !tc::mbar_wait(&full[s], (it / S) & 1, false, wait_ns, &abort_flag))) {
+                    if (!tc::mbar_wait(&planes_full[sp], (it / PS) & 1, ROLE_BACKOFF, wait_ns, &abort_flag) ||
+                        (!wres && !tc::mbar_wait(&full[s], (it / S) & 1, ROLE_BACKOFF, wait_ns, &abort_flag))) {
                         report(p, 3);
                         abort_flag = 1;
                         ok = false;

@@ -219,7 +219,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     __shared__ __align__(8) uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // Up to the next 1024-byte boundary by offsetting the shared pointer itself:
+    // the compiler keeps its address space, so the tile reads and writes below
+    // are shared-memory instructions rather than generic ones.
+    uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
     const int a_bytes = BM * BK * 2;
     const int b_bytes = p.bn * BK * 2;
     const uint64_t wait_ns = p.wait_ns;

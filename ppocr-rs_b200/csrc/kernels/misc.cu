@@ -227,39 +227,95 @@ __global__ void __launch_bounds__(128) det_head_kernel(HeadParams p) {
     const int W = p.w * 4;
     // First transposed conv tap (a, b) puts hidden pixel (2y + a, 2x + b);
     // the second tap (c, d) of that pixel lands at (4y + 2a + c, 4x + 2b + d).
-    for (int a = 0; a < 2; ++a) {
-        for (int b = 0; b < 2; ++b) {
-            float h[CH];
+    // Hidden units of tap (a, b): bias, then the inputs in ci order (packed
+    // pairs of output channels, each lane rounded as fmaf), then ReLU.
+    auto hidden = [&](int a, int b, float (&h)[CH]) {
 #pragma unroll
-            for (int co = 0; co < CH; ++co) h[co] = bup[co];
-            const float* w0 = wup + (a * 2 + b) * CH * CH;
-            // Packed pairs of output channels: each lane is rounded as fmaf, and
-            // every channel still sums its inputs in ci order.
-#pragma unroll 2
-            for (int ci = 0; ci < CH; ++ci) {
-                const float v = in[ci];
+        for (int co = 0; co < CH; ++co) h[co] = bup[co];
+        const float* w0 = wup + (a * 2 + b) * CH * CH;
+        // Fully unrolled for the narrow heads so the input row stays in
+        // registers; the weights come four per 16-byte shared load (every
+        // thread reads the same address: a broadcast), not two per packed FMA.
+#pragma unroll (CH <= 24 ? CH : 2)
+        for (int ci = 0; ci < CH; ++ci) {
+            const float v = in[ci];
+            const float4* wr = reinterpret_cast<const float4*>(w0 + ci * CH);
 #pragma unroll
-                for (int co = 0; co < CH; co += 2) fma2(h[co], h[co + 1], v, v, w0[ci * CH + co], w0[ci * CH + co + 1]);
+            for (int q = 0; q < CH / 4; ++q) {
+                const float4 w4 = wr[q];
+                fma2(h[4 * q], h[4 * q + 1], v, v, w4.x, w4.y);
+                fma2(h[4 * q + 2], h[4 * q + 3], v, v, w4.z, w4.w);
             }
+        }
 #pragma unroll
-            for (int co = 0; co < CH; ++co) h[co] = fmaxf(h[co], 0.f);
+        for (int co = 0; co < CH; ++co) h[co] = fmaxf(h[co], 0.f);
+    };
+    // Output columns 2b, 2b + 1 of row c from hidden tap b: the two d as one
+    // packed pair of co-ordered sums.
+    auto final_pair = [&](const float (&h)[CH], int c, float& l0, float& l1) {
+        l0 = p.b_fin;
+        l1 = p.b_fin;
+        const float4* wf0 = reinterpret_cast<const float4*>(wfin + (c * 2) * CH);
+        const float4* wf1 = reinterpret_cast<const float4*>(wfin + (c * 2 + 1) * CH);
+#pragma unroll
+        for (int q = 0; q < CH / 4; ++q) {
+            const float4 a4 = wf0[q], b4 = wf1[q];
+            fma2(l0, l1, h[4 * q], h[4 * q], a4.x, b4.x);
+            fma2(l0, l1, h[4 * q + 1], h[4 * q + 1], a4.y, b4.y);
+            fma2(l0, l1, h[4 * q + 2], h[4 * q + 2], a4.z, b4.z);
+            fma2(l0, l1, h[4 * q + 3], h[4 * q + 3], a4.w, b4.w);
+        }
+    };
+    if constexpr (CH <= 24) {
+        // Both hidden taps of a row pair in registers: each output row of the
+        // 4 x 4 patch leaves as one 16-byte probability store and one 4-byte
+        // mask store (a warp's stores are contiguous).
+        for (int a = 0; a < 2; ++a) {
+            float h0[CH], h1[CH];
+            hidden(a, 0, h0);
+            hidden(a, 1, h1);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                // The two columns d = 0, 1 as one packed pair of co-ordered sums.
-                float l[2] = {p.b_fin, p.b_fin};
-                const float* wf0 = wfin + (c * 2) * CH;
-                const float* wf1 = wf0 + CH;
-#pragma unroll
-                for (int co = 0; co < CH; ++co) fma2(l[0], l[1], h[co], h[co], wf0[co], wf1[co]);
-                const size_t o = ((size_t)img * p.h * 4 + (size_t)(4 * y + 2 * a + c)) * W + 4 * x + 2 * b;
-                if (p.logits) *reinterpret_cast<float2*>(p.logits + o) = make_float2(l[0], l[1]);
-                const float2 pr = make_float2(1.f / (1.f + expf(-l[0])), 1.f / (1.f + expf(-l[1])));
-                if (p.prob) *reinterpret_cast<float2*>(p.prob + o) = pr;
+                float l[4];
+                final_pair(h0, c, l[0], l[1]);
+                final_pair(h1, c, l[2], l[3]);
+                const size_t o = ((size_t)img * p.h * 4 + (size_t)(4 * y + 2 * a + c)) * W + 4 * x;
+                if (p.logits) *reinterpret_cast<float4*>(p.logits + o) = make_float4(l[0], l[1], l[2], l[3]);
+                float4 pr;
+                pr.x = 1.f / (1.f + expf(-l[0]));
+                pr.y = 1.f / (1.f + expf(-l[1]));
+                pr.z = 1.f / (1.f + expf(-l[2]));
+                pr.w = 1.f / (1.f + expf(-l[3]));
+                if (p.prob) *reinterpret_cast<float4*>(p.prob + o) = pr;
                 if (p.mask) {
-                    uchar2 m;
+                    uchar4 m;
                     m.x = pr.x >= p.threshold;
                     m.y = pr.y >= p.threshold;
-                    *reinterpret_cast<uchar2*>(p.mask + o) = m;
+                    m.z = pr.z >= p.threshold;
+                    m.w = pr.w >= p.threshold;
+                    *reinterpret_cast<uchar4*>(p.mask + o) = m;
+                }
+            }
+        }
+    } else {
+        for (int a = 0; a < 2; ++a) {
+            for (int b = 0; b < 2; ++b) {
+                float h[CH];
+                hidden(a, b, h);
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    float l0, l1;
+                    final_pair(h, c, l0, l1);
+                    const size_t o = ((size_t)img * p.h * 4 + (size_t)(4 * y + 2 * a + c)) * W + 4 * x + 2 * b;
+                    if (p.logits) *reinterpret_cast<float2*>(p.logits + o) = make_float2(l0, l1);
+                    const float2 pr = make_float2(1.f / (1.f + expf(-l0)), 1.f / (1.f + expf(-l1)));
+                    if (p.prob) *reinterpret_cast<float2*>(p.prob + o) = pr;
+                    if (p.mask) {
+                        uchar2 m;
+                        m.x = pr.x >= p.threshold;
+                        m.y = pr.y >= p.threshold;
+                        *reinterpret_cast<uchar2*>(p.mask + o) = m;
+                    }
                 }
             }
         }
