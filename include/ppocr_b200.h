@@ -45,8 +45,11 @@ enum ppocr_status {
 enum ppocr_model_size { PPOCR_MEDIUM = 0, PPOCR_SMALL = 1, PPOCR_TINY = 2 };
 
 /* Activation storage / GEMM precision of a loaded model.
- * FP32:   FP32 activations, FP32 FMA arithmetic throughout on the CUDA cores
- *         (the reference's own arithmetic; the parity mode).
+ * FP32:   FP32 activations and FP32-class arithmetic (the parity mode): the
+ *         1x1 convs and the dense convs over 32 or 64 k input channels on tcgen05 with both
+ *         operands carried as three BF16 pieces (the six leading products
+ *         accumulated in FP32, the dominant sum in its own accumulators); the
+ *         other convs, depthwise, head and SE on CUDA-core FP32 FMA.
  * BF16:   BF16 activations in HBM, tcgen05 BF16 tensor-core GEMMs with FP32
  *         accumulation; all other arithmetic FP32 in registers.
  * FP32_TC: FP32 activations; pointwise and dense convs on tcgen05 with each
@@ -271,10 +274,10 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
 
 /* Diagnostic (new): the split GEMM's implicit-conv mode (FP32 operands in
  * three BF16 pieces on tcgen05) on an NHWC FP32 input x [n, hi, wi, cin]
- * (cin 32 or 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
+ * (cin 32 or a multiple of 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
  * padding `pad` and stride 1 or 2; out receives [n, ho, wo, cout] NHWC,
  * act as for ppocr_selftest_gemm_ex.  The model's dense FP32 convs over one
- * 32- or 64-channel source use this path. */
+ * such source use this path. */
 int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride,
                               int pad, const float* x, const float* w, const float* bias, int act, float* out);
 /* Diagnostic (new): the FP32 pointwise GEMM of the FP32 mode,

@@ -1413,7 +1413,7 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
         p.n_pad = bn > 0 ? (cout + bn - 1) / bn * bn : 0;
         p.k_pad = (p.k + 63) / 64 * 64;
         p.m = n * ((ho + 7) / 8) * ((wo + 15) / 16) * 128;
-        if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split conv takes 32 or 64 input channels");
+        if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split conv takes 32 input channels or a multiple of 64");
         std::lock_guard<std::mutex> lock(gpu->mu);
         gpu->bind();
         ConvWeight cw;

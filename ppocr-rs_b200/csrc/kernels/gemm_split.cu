@@ -94,7 +94,7 @@ struct SplitArgs {
     int bn, kt, m_tiles, n_tiles, tmem_cols;
     int kchunk, dchunks;    // K blocks per dominant-sum accumulator, and their count
     int tiles_y, tiles_x;   // conv mode: tile grid per image
-    int cpt;                // conv mode: input channels per tap (32: two taps per K block; 64: one)
+    int cpt;                // conv mode: input channels per tap (32: two taps per K block; a multiple of 64: cpt / 64 blocks per tap)
     int w_resident;         // 1: every tile of a CTA has the same N tile, whose W (all K blocks) is loaded once
     int w_block;            // resident W bytes per K block, 1024-aligned
     int stages;             // FP32 ring depth
@@ -270,19 +270,21 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                     tc::mbar_expect_tx(&full[s], (two ? 2u : 1u) * BOX_BYTES + (wres ? 0u : (uint32_t)args.w_bytes));
                     if (p.conv) {
                         // K order (tap, channel).  32 channels: taps 2 kb and
-                        // 2 kb + 1, one box each; 64: tap kb, channels 0-31 and
-                        // 32-63 in two boxes.  The tile's 8 x 16 output pixels
+                        // 2 kb + 1, one box each; a multiple of 64: block kb is
+                        // channels [64 (kb mod bpt), + 64) of tap kb / bpt, in
+                        // two 32-channel boxes.  The tile's 8 x 16 output pixels
                         // read input pixels (oy s + ky - pt, ox s + kx - pl);
                         // outside the image reads 0.
                         const int mt = tile / args.n_tiles, per = args.tiles_y * args.tiles_x;
                         const int img = mt / per, rt = mt - img * per;
                         const int yb = (rt / args.tiles_x) * 8 * p.stride - p.pt;
                         const int xb = (rt % args.tiles_x) * 16 * p.stride - p.pl;
+                        const int bpt = args.cpt / 64;   // K blocks per tap (cpt >= 64)
                         for (int h = 0; h < (two ? 2 : 1); ++h) {
-                            const int tap = args.cpt == 32 ? 2 * kb + h : kb;
+                            const int tap = args.cpt == 32 ? 2 * kb + h : kb / bpt;
+                            const int c0 = args.cpt == 32 ? 0 : (kb - tap * bpt) * 64 + 32 * h;
                             const int ky = tap / p.kw, kx = tap - ky * p.kw;
-                            tc::tma_load_4d(f + h * BOX_BYTES, &tma_a, &full[s], args.cpt == 32 ? 0 : 32 * h, xb + kx, yb + ky,
-                                            img);
+                            tc::tma_load_4d(f + h * BOX_BYTES, &tma_a, &full[s], c0, xb + kx, yb + ky, img);
                         }
                     } else {
                         tc::tma_load_2d(f, &tma_a, &full[s], k0, m0);
@@ -652,7 +654,7 @@ namespace {
 int split_k_blocks(const SplitGemmParams& p) {
     if (p.conv) {
         const int taps = p.kh * p.kw, cpt = taps > 0 ? p.k / taps : 0;
-        return cpt == 32 ? (taps + 1) / 2 : taps;
+        return cpt == 32 ? (taps + 1) / 2 : taps * (cpt / 64);
     }
     return (p.k + BK - 1) / BK;
 }
@@ -676,7 +678,7 @@ bool gemm_split_supported(const SplitGemmParams& p) {
     if (kt <= 0 || !split_tmem_cols(bn, (kt + KCHUNK - 1) / KCHUNK)) return false;
     if (p.conv) {
         const int cin = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
-        if ((cin != 32 && cin != 64) || p.k != p.kh * p.kw * cin || p.lda % 4 || p.lda < cin || p.gate || p.residual)
+        if ((cin != 32 && cin % 64) || cin <= 0 || p.k != p.kh * p.kw * cin || p.lda % 4 || p.lda < cin || p.gate || p.residual)
             return false;
         return p.n_img > 0 && p.hi > 0 && p.wi > 0 && p.ho > 0 && p.wo > 0 && (p.stride == 1 || p.stride == 2);
     }

@@ -90,6 +90,26 @@ __device__ __forceinline__ void se_dot_rows(const float* __restrict__ w, const f
     }
 }
 
+// Sum of `count` chunk partials at `stride`, in chunk order, with the loads
+// issued sixteen at a time (the same sums as one load-add chain, without a
+// cache round trip per partial).  L2: read through to L2, for partials other
+// blocks of the same launch have just written.
+template <typename ACC, bool L2>
+__device__ __forceinline__ ACC ordered_chunk_sum(const float* src, int count, size_t stride) {
+    ACC s = 0;
+    for (int ch = 0; ch < count; ch += 16) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float* q = src + (size_t)(ch + j) * stride;
+            v[j] = ch + j < count ? (L2 ? __ldcg(q) : __ldg(q)) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s += (ACC)v[j];   // adding a zero past the end is exact
+    }
+    return s;
+}
+
 template <typename ACC, int IMG>
 __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
     extern __shared__ float4 sm4[];
@@ -101,11 +121,7 @@ __global__ void __launch_bounds__(256) se_mlp_kernel(SeMlpParams p) {
     for (int t = threadIdx.x; t < IMG * p.c; t += blockDim.x) {
         const int k = t / p.c, i = t % p.c;
         ACC s = 0;
-        if (k < nimg) {
-            const float* src = p.sum + (size_t)(img0 + k) * p.chunks * p.c + i;
-#pragma unroll 8
-            for (int ch = 0; ch < p.chunks; ++ch) s += (ACC)__ldg(src + (size_t)ch * p.c);
-        }
+        if (k < nimg) s = ordered_chunk_sum<ACC, false>(p.sum + (size_t)(img0 + k) * p.chunks * p.c + i, p.chunks, (size_t)p.c);
         mean[t] = s * inv;
     }
     for (int t = threadIdx.x; t < IMG * p.r; t += blockDim.x) hid[t] = 0;
@@ -154,9 +170,7 @@ __global__ void __launch_bounds__(256) se_pool_mlp_kernel(SePoolParams sp) {
     ACC* hid = mean + m.c;                     // [r]
     const ACC inv = (ACC)1 / (ACC)m.hw;
     for (int i = threadIdx.x; i < m.c; i += blockDim.x) {
-        ACC s = 0;
-        const float* src = p.sum + (size_t)img * p.chunks * p.c + i;
-        for (int ch = 0; ch < p.chunks; ++ch) s += (ACC)__ldcg(src + (size_t)ch * p.c);
+        const ACC s = ordered_chunk_sum<ACC, true>(p.sum + (size_t)img * p.chunks * p.c + i, p.chunks, (size_t)p.c);
         mean[i] = s * inv;
     }
     for (int i = threadIdx.x; i < m.r; i += blockDim.x) hid[i] = 0;

@@ -7,7 +7,7 @@ CUDA-core FP32 kernels meet), and close to the CUDA-core kernel's output.
 Shapes cover the detector's pointwise layers (k 32..320, n 16..320), ragged
 last tiles, several N tiles, the SE gate on A, the residual, and K up to
 1,792 (the dominant sum split over up to six TMEM accumulators).  The
-implicit-conv mode (32 or 64 input channels per tap, stride 1 or 2, zero
+implicit-conv mode (32 input channels or a multiple of 64 per tap, stride 1 or 2, zero
 padding through the TMA box) is checked the same way against a float64 conv.
 """
 
@@ -97,6 +97,7 @@ CONVS = [
     (2, 24, 40, 64, 16, 3, 1, 1, 1),     # head.conv_down: 64 channels, K = 576, two accumulators
     (1, 17, 35, 64, 48, 3, 1, 1, 0),
     (3, 9, 20, 32, 64, 3, 1, 1, 0),
+    (2, 21, 38, 128, 64, 3, 2, 1, 1),    # the medium stem3: 128 channels (two K blocks per tap), K = 1,152
 ]
 
 
@@ -117,7 +118,7 @@ def test_split_conv_fp32_class(gpu, n, hi, wi, cin, cout, k, stride, pad, act):
 def test_split_conv_rejects_other_channel_counts(gpu):
     import ppocr_b200 as P
 
-    x = np.zeros((1, 8, 8, 48), np.float32)
-    w = np.zeros((16, 48, 3, 3), np.float32)
+    x = np.zeros((1, 8, 8, 96), np.float32)
+    w = np.zeros((16, 96, 3, 3), np.float32)
     with pytest.raises(P.InvalidInput):
         gpu.selftest_conv_split(x, w)
