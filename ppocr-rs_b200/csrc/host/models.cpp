@@ -153,12 +153,9 @@ public:
     // `any_order`: the conv may sum its products input quad by quad (the
     // halo-tiled kernel) rather than tap by tap.  Kept to convs whose rounding
     // differences reach the output unamplified (the detector head).
-    // `cls` (optional, FP32 halo kernel): (tensor, scale) of class addends
-    // (ClassAddParams) summed into the conv before its bias and activation.
     Act4 conv(const std::string& name, const ConvWeight& cw, const std::vector<Src>& srcs, int n, int hi, int wi, int sh,
               int sw, int pt, int pl, int pb, int pr, int act, int residual = -1, int res_scale = 1,
-              const Act4* into = nullptr, int into_coff = 0, bool any_order = false,
-              const std::vector<std::pair<int, int>>& cls = {}) {
+              const Act4* into = nullptr, int into_coff = 0, bool any_order = false) {
         int cin = 0;
         for (auto& s : srcs) cin += s.channels;
         if (cin != cw.cin) fail(PPOCR_ERR_INVALID_MODEL, name + ": conv input channels do not match the weight");
@@ -167,8 +164,8 @@ public:
             fail(PPOCR_ERR_INVALID_MODEL, name + ": concatenation slice does not fit");
         Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
-        if (cls.empty() && split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 &&
-            srcs[0].coff == 0 && residual < 0 && sh == sw) {
+        if (split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 && srcs[0].coff == 0 &&
+            residual < 0 && sh == sw) {
             // FP32 mode: a dense conv over one plain 32-channel NHWC source as an
             // implicit split GEMM on tcgen05 (one strided TMA box per tap).
             SplitGemmParams sp;
@@ -196,7 +193,7 @@ public:
                 return out;
             }
         }
-        if (cls.empty() && tensor_core_f32()) {
+        if (tensor_core_f32()) {
             // FP32_TC: the tensor-core engine for NHWC sources whose channels split
             // into 16-byte chunks.  (BF16 convs stay on the register-tiled SIMT
             // implicit GEMM, which measured faster than the engine's gather.)
@@ -250,15 +247,9 @@ public:
         // detector's chaotic spec-weight parity check flipped a pixel when the
         // stem and neck convs were re-associated, so those keep the tap-major
         // order.
-        const bool tcconv = cls.empty() && tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
+        const bool tcconv = tc_ && m_.dtype == DT_BF16 && residual < 0 && conv_tc_supported(p);
         p.halo_order = any_order ? 2 : 1;
-        p.cls_count = (int)cls.size();
-        for (size_t k = 0; k < cls.size(); ++k) {
-            p.cls_scale[k] = cls[k].second;
-            reads.push_back(cls[k].first);
-        }
         const bool halo = !tcconv && m_.dtype == DT_F32 && conv_halo_supported(p);
-        if (!cls.empty() && !halo) fail(PPOCR_ERR_INVALID_MODEL, name + ": class addends need the halo conv");
         const bool gemm = !tcconv && !halo && m_.dtype == DT_BF16 && conv_gemm_supported(p);
         // The NCHW image input has 3 channels: one thread covers up to 64 output
         // channels so each loaded input feeds 64 FMAs.
@@ -283,9 +274,8 @@ public:
         p.n_pad = n_pad;
         const int otid = out.tid;
         std::vector<Src> s2 = srcs;
-        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid, gemm, tcconv, cls](const Ctx& c, cudaStream_t st) mutable {
+        m_.plan.add_op(name, reads, {otid}, [p, s2, woff, boff, residual, otid, gemm, tcconv](const Ctx& c, cudaStream_t st) mutable {
             for (size_t i = 0; i < s2.size(); ++i) p.src[i].ptr = c.act(s2[i].tid);
-            for (size_t k = 0; k < cls.size(); ++k) p.cls_add[k] = static_cast<const float*>(c.act(cls[k].first));
             p.weight = (gemm || tcconv) ? nullptr : c.wf(woff);
             p.weight_kn = gemm ? c.wf(woff) : nullptr;
             p.w_tc = tcconv ? c.wb(woff) : nullptr;
@@ -302,108 +292,6 @@ public:
                int act, int residual = -1, int res_scale = 1, const Act4* into = nullptr, int into_coff = 0) {
         return conv(name, cw, {{in.tid, in.c, in.c, 0, 1, SRC_NHWC}}, in.n, in.h, in.w, sh, sw, pt, pl, pb, pr, act, residual,
                     res_scale, into, into_coff);
-    }
-
-    // The detector head's conv_down: 3x3 (stride 1, zero padding 1) + BN +
-    // ReLU over the concatenation of nearest-upsampled sources (the last one
-    // at scale 1).  FP32 where the kernels take it: the scale-1 source through
-    // the halo conv, each upsampled source as per-class low-resolution
-    // contributions (ClassAddParams) that the conv adds before its bias and
-    // ReLU; the conv's sums are re-associated (any order is allowed here: the
-    // head's rounding differences reach the map unamplified).  Elsewhere one
-    // halo / direct conv over the virtual concatenation.
-    Act4 head_down(const std::string& name, const ConvWeight& cw, const std::vector<Src>& srcs, int n, int h, int w) {
-        const int cs = srcs.empty() ? 0 : srcs[0].channels;
-        bool ok = m_.dtype == DT_F32 && srcs.size() >= 2 && srcs.size() <= 4 && srcs.back().scale == 1 && cw.kh == 3 &&
-                  cw.kw == 3 && class_add_supported(cs, cw.cout);
-        for (size_t i = 0; ok && i + 1 < srcs.size(); ++i)
-            ok = srcs[i].channels == cs && srcs[i].mode == SRC_NHWC && srcs[i].coff % 4 == 0 && srcs[i].cstride % 4 == 0 &&
-                 srcs[i].scale >= 2 && h % srcs[i].scale == 0 && w % srcs[i].scale == 0;
-        ok = ok && srcs.back().channels == cs && srcs.back().mode == SRC_NHWC;
-        if (ok) {
-            ConvParams probe;
-            probe.n = n; probe.hi = h; probe.wi = w; probe.cin = cs; probe.nsrc = 1;
-            probe.src[0].channels = cs; probe.src[0].cstride = srcs.back().cstride; probe.src[0].coff = srcs.back().coff;
-            probe.src[0].scale = 1; probe.src[0].mode = SRC_NHWC;
-            probe.ho = h; probe.wo = w; probe.cout = cw.cout; probe.kh = 3; probe.kw = 3; probe.pt = 1; probe.pl = 1;
-            probe.out_cstride = cw.cout; probe.dtype = DT_F32; probe.halo_order = 2;
-            probe.cls_count = (int)srcs.size() - 1;
-            for (int k = 0; k < probe.cls_count; ++k) probe.cls_scale[k] = srcs[k].scale;
-            ok = conv_halo_supported(probe);
-        }
-        if (!ok)
-            return conv(name, cw, srcs, n, h, w, 1, 1, 1, 1, 1, 1, ACT_RELU, -1, 1, nullptr, 0, true);
-        // Weights of source i: input channels [i cs, (i + 1) cs) of cw.
-        auto slice = [&](size_t i) {
-            ConvWeight s1;
-            s1.cout = cw.cout; s1.cin = cs; s1.kh = 3; s1.kw = 3;
-            s1.w.resize((size_t)cw.cout * cs * 9);
-            for (int co = 0; co < cw.cout; ++co)
-                for (int ci = 0; ci < cs; ++ci)
-                    for (int t = 0; t < 9; ++t)
-                        s1.w[((size_t)co * cs + ci) * 9 + t] = cw.w[((size_t)co * cw.cin + i * cs + ci) * 9 + t];
-            s1.b.assign(cw.cout, 0.f);
-            return s1;
-        };
-        ClassAddParams cp;
-        cp.n = n; cp.ho = h; cp.wo = w; cp.cs = cs; cp.cout = cw.cout; cp.count = (int)srcs.size() - 1;
-        std::vector<size_t> woffs;
-        std::vector<int> outs, reads;
-        std::vector<std::pair<int, int>> cls;
-        for (int k = 0; k < cp.count; ++k) {
-            const int sc = srcs[k].scale, ncls = cls_classes(sc);
-            const ConvWeight wk = slice(k);
-            ClassAddSource& S = cp.s[k];
-            S.cstride = srcs[k].cstride; S.coff = srcs[k].coff; S.scale = sc;
-            // Row (column) offset of tap d in {-1, 0, 1} for class a: the
-            // first row of a block reaches the block above, the last the one
-            // below, the others stay in the block.
-            auto off = [](int a, int d) { return a == 0 ? (d < 0 ? -1 : 0) : a == 2 ? (d > 0 ? 1 : 0) : 0; };
-            std::vector<float> wc((size_t)ncls * 4 * cs * cw.cout, 0.f);
-            for (int c = 0; c < ncls; ++c) {
-                const int ra = sc == 2 ? (c / 2) * 2 : c / 3, ca = sc == 2 ? (c % 2) * 2 : c % 3;
-                int nslot = 0;
-                for (int oi = -1; oi <= 1; ++oi)
-                    for (int oj = -1; oj <= 1; ++oj) {
-                        bool any = false;
-                        for (int dy = -1; dy <= 1; ++dy)
-                            for (int dx = -1; dx <= 1; ++dx) any = any || (off(ra, dy) == oi && off(ca, dx) == oj);
-                        if (!any) continue;
-                        if (nslot == 4) fail(PPOCR_ERR_INVALID_MODEL, name + ": more than four offsets in a class");
-                        S.slot_dy[c][nslot] = oi; S.slot_dx[c][nslot] = oj;
-                        for (int ci = 0; ci < cs; ++ci)
-                            for (int co = 0; co < cw.cout; ++co) {
-                                double sum = 0;   // the class's taps, in (ky, kx) order, in double
-                                for (int dy = -1; dy <= 1; ++dy)
-                                    for (int dx = -1; dx <= 1; ++dx)
-                                        if (off(ra, dy) == oi && off(ca, dx) == oj)
-                                            sum += wk.w[((size_t)co * cs + ci) * 9 + (dy + 1) * 3 + (dx + 1)];
-                                wc[(((size_t)c * 4 + nslot) * cs + ci) * cw.cout + co] = (float)sum;
-                            }
-                        ++nslot;
-                    }
-                S.slots[c] = nslot;
-            }
-            woffs.push_back(m_.blob.add_f32(wc));
-            const int ot = m_.plan.add_raw(name + ".cls" + std::to_string(k), (size_t)n * (h / sc) * (w / sc) * ncls * cw.cout * 4);
-            outs.push_back(ot);
-            reads.push_back(srcs[k].tid);
-            cls.push_back({ot, sc});
-        }
-        double flops = 0;
-        for (int k = 0; k < cp.count; ++k)
-            flops += 2.0 * n * (h / srcs[k].scale) * (w / srcs[k].scale) * cls_classes(srcs[k].scale) * 4 * cs * cw.cout;
-        m_.plan.add_op(name + ".cls", reads, outs, [cp, woffs, reads, outs](const Ctx& c, cudaStream_t st) mutable {
-            for (int k = 0; k < cp.count; ++k) {
-                cp.s[k].src = static_cast<const float*>(c.act(reads[k]));
-                cp.s[k].w = c.wf(woffs[k]);
-                cp.s[k].out = static_cast<float*>(c.act(outs[k]));
-            }
-            return launch_class_add(cp, st);
-        }, "conv", 0, flops);
-        ConvWeight w1 = slice(srcs.size() - 1);
-        w1.b = cw.b;
-        return conv(name, w1, {srcs.back()}, n, h, w, 1, 1, 1, 1, 1, 1, ACT_RELU, -1, 1, nullptr, 0, true, cls);
     }
 
     // 2x2 stride-1 "same-upper" max pool of `x` into channels [coff, coff + x.c) of `into`.
@@ -883,8 +771,8 @@ void detector_head(Builder& b, const std::vector<Act4>& feats, int channels) {
     }
     if (total != channels) fail(PPOCR_ERR_INVALID_MODEL, "detector neck produced the wrong channel count");
     const Act4& base = feats[0];
-    const ConvWeight down_w = r.conv_bn("head.conv_down", hidden, channels, 3, 3, false, "norm");
-    Act4 down = b.head_down("head.conv_down", down_w, srcs, base.n, base.h, base.w);
+    Act4 down = b.conv("head.conv_down", r.conv_bn("head.conv_down", hidden, channels, 3, 3, false, "norm"), srcs, base.n, base.h,
+                       base.w, 1, 1, 1, 1, 1, 1, ACT_RELU, -1, 1, nullptr, 0, true);
     std::vector<float> up_w = r.get("head.conv_up.convolution.weight", {(size_t)hidden, (size_t)hidden, 2, 2});
     std::vector<float> up_b = r.get("head.conv_up.convolution.bias", {(size_t)hidden});
     fold_transpose_bn(up_w, up_b, hidden, hidden, r, "head.conv_up.norm");

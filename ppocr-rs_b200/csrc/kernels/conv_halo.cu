@@ -42,8 +42,6 @@
 #include <algorithm>
 #include <atomic>
 
-#include <type_traits>
-
 #include "common.cuh"
 #include "kernels.h"
 
@@ -334,22 +332,10 @@ __global__ void __launch_bounds__(kThreads, 2) conv_halo_kernel(ConvParams p, Ha
                         res = static_cast<const T*>(p.residual) +
                               ((size_t)(img * rh + oy / p.res_scale) * rw + ox / p.res_scale) * p.cout + co0;
                     }
-                    // Upsampled sources' class contributions (FP32 only), in source order.
-                    const float* cls[3] = {nullptr, nullptr, nullptr};
-                    if constexpr (std::is_same<T, float>::value) {
-                        for (int k = 0; k < p.cls_count; ++k) {
-                            const int sc = p.cls_scale[k];
-                            const size_t cell = ((size_t)(img * (p.ho / sc) + oy / sc) * (p.wo / sc) + ox / sc) * cls_classes(sc) +
-                                                cls_index(oy % sc, ox % sc, sc);
-                            cls[k] = p.cls_add[k] + cell * p.cout + co0;
-                        }
-                    }
 #pragma unroll
                     for (int j = 0; j < TN; j += 4) {
                         if (co0 + j >= p.cout) break;
                         float4 v = make_float4(acc[i][j], acc[i][j + 1], acc[i][j + 2], acc[i][j + 3]);
-                        for (int k = 0; k < 3; ++k)
-                            if (cls[k]) v = f4_add(v, __ldg(reinterpret_cast<const float4*>(cls[k] + j)));
                         if (p.bias) v = f4_add(v, *reinterpret_cast<const float4*>(p.bias + co0 + j));
                         v = f4_act(v, p.act);
                         if (res) v = f4_add(v, load4(res + j));
@@ -532,13 +518,6 @@ int conv_halo_bn(int cout) { return halo_bn(cout); }
 
 bool conv_halo_supported(const ConvParams& p) {
     if (p.cout < 8 || p.cout % 8 || p.cout > 64 || p.nsrc < 1 || p.nsrc > 4) return false;
-    if (p.cls_count < 0 || p.cls_count > 3) return false;
-    if (p.cls_count > 0) {
-        // Class addends: FP32, a 3x3 stride-1 conv with one-pixel zero padding.
-        if (p.dtype != DT_F32 || p.kh != 3 || p.kw != 3 || p.sh != 1 || p.sw != 1 || p.pt != 1 || p.pl != 1) return false;
-        for (int k = 0; k < p.cls_count; ++k)
-            if (p.cls_scale[k] < 2 || p.ho % p.cls_scale[k] || p.wo % p.cls_scale[k]) return false;
-    }
     const bool geom = (p.kh == 3 && p.kw == 3 && ((p.sh == 1 && p.sw == 1) || (p.sh == 2 && p.sw == 2))) ||
                       (p.kh == 2 && p.kw == 2 && p.sh == 1 && p.sw == 1);
     if (!geom) return false;

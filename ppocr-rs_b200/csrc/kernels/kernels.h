@@ -63,12 +63,6 @@ struct ConvParams {
     int act = 0;
     const void* residual = nullptr;       // NHWC [n, ho/res_scale, wo/res_scale, cout], added after act
     int res_scale = 1;
-    // FP32 halo kernel only: contributions of nearest-upsampled sources, added
-    // before the bias and activation (see ClassAddParams): for each k,
-    // sum += cls_add[k][((img * ho/s + oy/s) * wo/s + ox/s) * classes(s) + class(oy mod s, ox mod s)][0..cout).
-    const float* cls_add[3] = {nullptr, nullptr, nullptr};
-    int cls_scale[3] = {0, 0, 0};
-    int cls_count = 0;
     void* out = nullptr;
     int out_cstride = 0, out_coff = 0;
     DType dtype = DT_F32;
@@ -78,37 +72,6 @@ struct ConvParams {
     uint64_t wait_ns = 0;
 };
 cudaError_t launch_conv(const ConvParams& p, cudaStream_t stream);
-
-// A 3x3 stride-1 zero-padded conv over a nearest-upsampled source (scale s)
-// reads, for the output pixels of one s x s block, at most a 2x2 set of
-// source pixels, and which ones (and which taps add up on each) depends only
-// on the pixel's row and column class within the block: 0 first row/column,
-// 1 interior, 2 last (s = 2 has no interior).  ClassAdd computes, per source
-// pixel P and class, sum over the class's source offsets o of
-// f[P + o] . Wc[class][o] (weights summed per class on the host), so the
-// full-resolution conv only gathers one vector per source instead of running
-// nine taps over it (the detector head's conv_down, DetectorHead,
-// src/cpu/model.rs:1479-1521).
-__host__ __device__ inline int cls_classes(int s) { return s == 2 ? 4 : 9; }
-__host__ __device__ inline int cls_row(int r, int s) { return r == 0 ? 0 : r == s - 1 ? 2 : 1; }
-__host__ __device__ inline int cls_index(int ry, int rx, int s) {
-    const int a = cls_row(ry, s), b = cls_row(rx, s);
-    return s == 2 ? (a >> 1) * 2 + (b >> 1) : a * 3 + b;
-}
-struct ClassAddSource {
-    const float* src = nullptr;   // NHWC [n, ho/scale, wo/scale, cstride], channels [coff, coff + cs)
-    int cstride = 0, coff = 0, scale = 0;
-    const float* w = nullptr;     // [classes][4 slots][cs][cout] (unused slots zero)
-    int slot_dy[9][4] = {}, slot_dx[9][4] = {}, slots[9] = {};
-    float* out = nullptr;         // [n, ho/scale, wo/scale, classes, cout]
-};
-struct ClassAddParams {
-    int n = 0, ho = 0, wo = 0, cs = 0, cout = 0;
-    ClassAddSource s[3];
-    int count = 0;
-};
-bool class_add_supported(int cs, int cout);
-cudaError_t launch_class_add(const ClassAddParams& p, cudaStream_t stream);
 
 // tcgen05 implicit-GEMM conv of one NHWC BF16 source (gemm_tc.cu): 8 x 16
 // output-pixel tiles, each K step a strided 4D TMA box of 64 channels at one

@@ -704,54 +704,6 @@ __global__ void copy_check_kernel(const float* __restrict__ src, float* __restri
     if (bad) *flag = 1;
 }
 
-// One thread per (class, source pixel) of one source (blockIdx.y), pixels
-// fastest so a warp shares its class and reads the class weights by
-// broadcast.  Each output sums the class's source offsets in slot order and,
-// per offset, the channels in order.
-template <int CS, int CO>
-__global__ void __launch_bounds__(128) class_add_kernel(ClassAddParams p) {
-    const int k = blockIdx.y;
-    const ClassAddSource& S = p.s[k];
-    const int s = S.scale, hs = p.ho / s, ws = p.wo / s, ncls = cls_classes(s);
-    const long long npx = (long long)p.n * hs * ws;
-    const long long total = npx * ncls;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const int cls = (int)(i / npx);
-        const long long px = i - (long long)cls * npx;
-        const int x = (int)(px % ws);
-        const long long t = px / ws;
-        const int y = (int)(t % hs), img = (int)(t / hs);
-        float acc[CO];
-#pragma unroll
-        for (int o = 0; o < CO; ++o) acc[o] = 0.f;
-        for (int sl = 0; sl < S.slots[cls]; ++sl) {
-            const int yy = y + S.slot_dy[cls][sl], xx = x + S.slot_dx[cls][sl];
-            if (yy < 0 || yy >= hs || xx < 0 || xx >= ws) continue;   // the conv's zero padding
-            const float* f = S.src + (((size_t)img * hs + yy) * ws + xx) * S.cstride + S.coff;
-            const float4* w = reinterpret_cast<const float4*>(S.w + ((size_t)cls * 4 + sl) * CS * CO);
-#pragma unroll
-            for (int c4 = 0; c4 < CS; c4 += 4) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(f + c4));
-                const float xv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                    for (int o4 = 0; o4 < CO / 4; ++o4) {
-                        const float4 wv = __ldg(w + (c4 + j) * (CO / 4) + o4);
-                        acc[4 * o4] = fmaf(xv[j], wv.x, acc[4 * o4]);
-                        acc[4 * o4 + 1] = fmaf(xv[j], wv.y, acc[4 * o4 + 1]);
-                        acc[4 * o4 + 2] = fmaf(xv[j], wv.z, acc[4 * o4 + 2]);
-                        acc[4 * o4 + 3] = fmaf(xv[j], wv.w, acc[4 * o4 + 3]);
-                    }
-                }
-            }
-        }
-        float4* out = reinterpret_cast<float4*>(S.out + ((size_t)px * ncls + cls) * CO);
-#pragma unroll
-        for (int o4 = 0; o4 < CO / 4; ++o4) out[o4] = make_float4(acc[4 * o4], acc[4 * o4 + 1], acc[4 * o4 + 2], acc[4 * o4 + 3]);
-    }
-}
-
 __global__ void copy_words_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, size_t count) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) dst[i] = src[i];
@@ -949,29 +901,6 @@ cudaError_t launch_copy_check(const float* src, float* dst, size_t count, int* f
     if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return cudaErrorInvalidValue;
     if (count == 0) return cudaSuccess;
     copy_check_kernel<<<grid_for((long long)(count / 4 + 1), 256), 256, 0, stream>>>(src, dst, count, flag);
-    return cudaGetLastError();
-}
-
-bool class_add_supported(int cs, int cout) { return (cs == 16 && cout == 16) || (cs == 24 && cout == 24); }
-
-cudaError_t launch_class_add(const ClassAddParams& p, cudaStream_t stream) {
-    if (p.count < 1 || p.count > 3 || p.n <= 0 || p.ho <= 0 || p.wo <= 0 || !class_add_supported(p.cs, p.cout))
-        return cudaErrorInvalidValue;
-    long long most = 0;
-    for (int k = 0; k < p.count; ++k) {
-        const ClassAddSource& S = p.s[k];
-        if (!S.src || !S.w || !S.out || S.scale < 2 || p.ho % S.scale || p.wo % S.scale || S.cstride % 4 || S.coff % 4 ||
-            S.coff + p.cs > S.cstride || reinterpret_cast<uintptr_t>(S.src) % 16 || reinterpret_cast<uintptr_t>(S.w) % 16 ||
-            reinterpret_cast<uintptr_t>(S.out) % 16)
-            return cudaErrorInvalidValue;
-        for (int c = 0; c < cls_classes(S.scale); ++c)
-            if (S.slots[c] < 0 || S.slots[c] > 4) return cudaErrorInvalidValue;
-        const long long t = (long long)p.n * (p.ho / S.scale) * (p.wo / S.scale) * cls_classes(S.scale);
-        if (t > most) most = t;
-    }
-    const dim3 grid(grid_for(most, 128), (unsigned)p.count);
-    if (p.cs == 16) class_add_kernel<16, 16><<<grid, 128, 0, stream>>>(p);
-    else class_add_kernel<24, 24><<<grid, 128, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
