@@ -425,12 +425,16 @@ template <typename T, int KH, int KW, int SH, int SW, int TN, int TM, int NST, b
 cudaError_t launch_halo(const ConvParams& p, HaloArgs a, size_t smem, cudaStream_t stream) {
     auto kernel = conv_halo_kernel<T, KH, KW, SH, SW, TN, TM, NST, NCHW, MODE>;
     static std::atomic<int> regs{0};
+    // The shared-memory limit is a per-device attribute: set on every device
+    // the kernel runs on (the register count below is the same on all).
+    {
+        const cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), (int)kSmemLimit);
+        if (e != cudaSuccess) return e;
+    }
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        if (e != cudaSuccess) return e;
         cudaFuncAttributes fa{};
-        e = cudaFuncGetAttributes(&fa, kernel);
+        cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
         if (e != cudaSuccess) return e;
         nregs = fa.numRegs > 0 ? fa.numRegs : 1;
         regs.store(nregs, std::memory_order_release);

@@ -225,12 +225,16 @@ cudaError_t launch_tiled(const DwParams& p, cudaStream_t stream) {
     auto kernel = plain ? dwconv_tiled_kernel<T, CG, KH, KW, SH, SW, true> : dwconv_tiled_kernel<T, CG, KH, KW, SH, SW, false>;
     static std::atomic<int> regs_by_plain[2] = {0, 0};   // each kernel's registers, queried once
     std::atomic<int>& regs = regs_by_plain[plain ? 1 : 0];
+    // The shared-memory limit is a per-device attribute: set on every device
+    // the kernel runs on (the register count below is the same on all).
+    {
+        const cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), (int)kSmemLimit);
+        if (e != cudaSuccess) return e;
+    }
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        if (e != cudaSuccess) return e;
         cudaFuncAttributes fa{};
-        e = cudaFuncGetAttributes(&fa, kernel);
+        cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
         if (e != cudaSuccess) return e;
         nregs = fa.numRegs > 0 ? fa.numRegs : 1;
         regs.store(nregs, std::memory_order_release);
@@ -470,12 +474,16 @@ cudaError_t launch_band_nr(const DwParams& p, const DwBand& g, int nt, cudaStrea
     auto kernel = dwconv_band_kernel<T, CG, K, SH, SW, NR, PLAIN>;
     const size_t smem = 2 * (K * K + 1) * CG * sizeof(float4) + (size_t)NR * g.iw * CG * 4 * sizeof(T);
     static std::atomic<int> regs{0};
+    // The shared-memory limit is a per-device attribute: set on every device
+    // the kernel runs on (the register count below is the same on all).
+    {
+        const cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), (int)kSmemLimit);
+        if (e != cudaSuccess) return e;
+    }
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        if (e != cudaSuccess) return e;
         cudaFuncAttributes fa{};
-        e = cudaFuncGetAttributes(&fa, kernel);
+        cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
         if (e != cudaSuccess) return e;
         nregs = fa.numRegs > 0 ? fa.numRegs : 1;
         regs.store(nregs, std::memory_order_release);

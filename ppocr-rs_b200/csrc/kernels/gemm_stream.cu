@@ -198,12 +198,16 @@ cudaError_t launch_cfg(const GemmParams& p, cudaStream_t stream) {
     if (tiles == 0) return cudaSuccess;
     auto kernel = gemm_stream_kernel<BN, TN, TM>;
     static std::atomic<int> regs{0};
+    // The shared-memory limit is a per-device attribute: set on every device
+    // the kernel runs on (the register count below is the same on all).
+    {
+        const cudaError_t e = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), (int)kSmemLimit);
+        if (e != cudaSuccess) return e;
+    }
     int nregs = regs.load(std::memory_order_acquire);
     if (!nregs) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        if (e != cudaSuccess) return e;
         cudaFuncAttributes fa{};
-        e = cudaFuncGetAttributes(&fa, kernel);
+        cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
         if (e != cudaSuccess) return e;
         nregs = fa.numRegs > 0 ? fa.numRegs : 1;
         regs.store(nregs, std::memory_order_release);
