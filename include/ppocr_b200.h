@@ -288,9 +288,12 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
  * scales A; residual (may be NULL) is [m][n].  kernel_used returns the kernel
  * that ran (1..3).  k must be a multiple of 4; a kernel that does not
  * support the shape fails with PPOCR_ERR_INVALID_INPUT.  kernel 4 = the
- * tcgen05 split GEMM of the FP32_TC mode (k a multiple of 16): A and W carried
+ * tcgen05 split GEMM of the FP32 mode (k a multiple of 16): A and W carried
  * as three BF16 pieces each, the six leading products accumulated in FP32 in
- * TMEM (FP32-class rounding, not bit-identical to the CUDA-core kernels). */
+ * TMEM (FP32-class rounding, not bit-identical to the CUDA-core kernels);
+ * kernel 5 = the same with A split into its pieces by a kernel of its own
+ * first (the model's choice when A would otherwise be split once per output
+ * tile of three or more): bit-identical to kernel 4. */
 int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used);

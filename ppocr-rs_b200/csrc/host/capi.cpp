@@ -1459,10 +1459,11 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
         if (!gpu || !a || !w || !c) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
         if (m <= 0 || n <= 0 || k <= 0 || k % 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: GEMM shape (k must be a multiple of 4)");
         if (act < ACT_NONE || act > ACT_SIGMOID) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: activation");
-        if (kernel < 0 || kernel > 4) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..4");
+        if (kernel < 0 || kernel > 5) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: kernel must be 0..5");
         if (gate && (rows_per_image <= 0 || m % rows_per_image)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: rows_per_image must divide m");
-        if (kernel == 4) {
-            // The FP32-class tcgen05 split GEMM.
+        if (kernel == 4 || kernel == 5) {
+            // The FP32-class tcgen05 split GEMM (5: A pre-split into its pieces by
+            // its own kernel first).
             SplitGemmParams p;
             p.m = m; p.n = n; p.k = k; p.lda = k; p.ldc = n; p.ldr = n; p.act = act;
             p.rows_per_image = gate ? rows_per_image : 1;
@@ -1484,6 +1485,7 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             const size_t ro = residual ? blob.add_f32(std::vector<float>(residual, residual + (size_t)m * n)) : 0;
             const size_t co = blob.add_f32(std::vector<float>((size_t)m * n, 0.f));
             const size_t fo = blob.add_f32(std::vector<float>(64, 0.f));
+            const size_t po = kernel == 5 ? blob.add_f32(std::vector<float>((size_t)3 * m * p.k_pad / 2, 0.f)) : 0;
             const std::vector<uint8_t>& bytes = blob.bytes();
             char* d = nullptr;
             cuda_check(cudaMalloc(&d, bytes.size()), "allocate GEMM test buffers");
@@ -1494,6 +1496,10 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             p.err = reinterpret_cast<int*>(d + fo);
             int flag = 0;
             cudaError_t e = cudaMemcpyAsync(d, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, gpu->stream);
+            if (e == cudaSuccess && kernel == 5) {
+                e = launch_split_planes(p, d + po, gpu->stream);
+                p.a_planes = d + po;
+            }
             if (e == cudaSuccess) e = launch_gemm_split(p, gpu->stream);
             if (e == cudaSuccess) e = cudaMemcpyAsync(c, p.c, (size_t)m * n * 4, cudaMemcpyDeviceToHost, gpu->stream);
             if (e == cudaSuccess) e = cudaMemcpyAsync(&flag, p.err, sizeof(int), cudaMemcpyDeviceToHost, gpu->stream);
@@ -1508,7 +1514,7 @@ int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a,
             cudaFree(d);
             cuda_check(e, "split GEMM self-test");
             if (flag) fail(PPOCR_ERR_GPU, "GPU error: a tensor-core pipeline wait ran out (code " + std::to_string(flag) + ")");
-            if (kernel_used) *kernel_used = 4;
+            if (kernel_used) *kernel_used = kernel;
             return;
         }
         std::lock_guard<std::mutex> lock(gpu->mu);

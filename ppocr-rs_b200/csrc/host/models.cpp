@@ -365,12 +365,26 @@ public:
         const size_t boff = m_.blob.add_f32(cw.b);
         const bool has_bias = o.has_bias;
         const int gate = o.gate, res_gate = o.res_gate, residual = o.residual;
-        m_.plan.add_op(name, {in_tid, gate, res_gate, residual}, {out_tid},
-                       [p, woff, boff, has_bias, in_tid, gate, res_gate, residual, out_tid](const Ctx& c, cudaStream_t st) mutable {
-                           p.a = static_cast<const float*>(c.act(in_tid));
+        // Many N tiles: A is split into its three BF16 pieces once, by its own
+        // op, instead of once per N tile inside the GEMM (same pieces, same C).
+        int planes = -1;
+        if (gemm_split_presplit_pays(rows, cw.cout, k)) {
+            planes = m_.plan.add_raw(name + ".planes", (size_t)6 * rows * p.k_pad);
+            m_.plan.add_op(name + ".split", {in_tid, gate}, {planes}, [p, in_tid, gate, planes](const Ctx& c, cudaStream_t st) mutable {
+                p.a = static_cast<const float*>(c.act(in_tid));
+                p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
+                return launch_split_planes(p, c.act(planes), st);
+            }, "gemm", 0, 0.0);
+        }
+        const std::vector<int> reads = planes >= 0 ? std::vector<int>{planes, res_gate, residual}
+                                                   : std::vector<int>{in_tid, gate, res_gate, residual};
+        m_.plan.add_op(name, reads, {out_tid},
+                       [p, woff, boff, has_bias, in_tid, gate, res_gate, residual, out_tid, planes](const Ctx& c, cudaStream_t st) mutable {
+                           p.a = planes >= 0 ? nullptr : static_cast<const float*>(c.act(in_tid));
+                           p.a_planes = planes >= 0 ? c.act(planes) : nullptr;
                            p.w = c.wb(woff);
                            p.bias = has_bias ? c.wf(boff) : nullptr;
-                           p.gate = gate >= 0 ? static_cast<const float*>(c.act(gate)) : nullptr;
+                           p.gate = (gate >= 0 && planes < 0) ? static_cast<const float*>(c.act(gate)) : nullptr;
                            p.res_gate = res_gate >= 0 ? static_cast<const float*>(c.act(res_gate)) : nullptr;
                            p.residual = static_cast<const float*>(c.act(residual));
                            p.c = static_cast<float*>(c.act(out_tid));

@@ -51,6 +51,7 @@ namespace {
 
 constexpr int BM = 128, BK = 64, THREADS = 448, MAX_BN = 64;
 constexpr int MAX_A = 6, PLANE_STAGES = 2;             // FP32 ring depth bound; BF16 plane ring
+constexpr int MAX_PLANE_STAGES = 4;                    // plane ring bound (pre-split A has no FP32 ring)
 constexpr int BOX_BYTES = BM * 32 * 4;                 // one FP32 box: 128 rows x 32 columns
 constexpr int PLANE_BYTES = BM * BK * 2;               // one BF16 piece of a 128 x 64 tile
 constexpr int PLANES_STAGE = 3 * PLANE_BYTES;          // 48 KB
@@ -100,6 +101,7 @@ struct SplitArgs {
     int stages;             // FP32 ring depth
     int plane_stages;       // BF16 plane ring depth (1 when one K block covers the GEMM)
     int stage_bufs;         // output staging buffers per epilogue warp (1 or 2)
+    int presplit;           // 1: A arrives as BF16 pieces (p.a_planes) straight into the plane ring
     int a_stage_bytes;      // one FP32 ring stage (A boxes + streamed W), 1024-aligned
     int a_box_bytes;        // the A boxes of a stage (1 or 2 boxes of 16 KB)
     int w_bytes;            // the three W pieces of one (K block, N tile)
@@ -190,8 +192,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
     // full: TMA of a FP32 stage landed; f32_empty: its A rows converted;
     // w_free: the MMAs are done with its streamed W; planes_full / planes_empty:
     // the BF16 plane ring between converters and MMA.
-    __shared__ __align__(8) uint64_t full[MAX_A], f32_empty[MAX_A], w_free[MAX_A], planes_full[PLANE_STAGES],
-        planes_empty[PLANE_STAGES], w_ready, acc_full[2], acc_empty[2], drain_bar;
+    __shared__ __align__(8) uint64_t full[MAX_A], f32_empty[MAX_A], w_free[MAX_A], planes_full[MAX_PLANE_STAGES],
+        planes_empty[MAX_PLANE_STAGES], w_ready, acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     // Up to the next 1024-byte boundary by offsetting the shared pointer itself:
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
     const int PS = args.plane_stages;
     const int bn = args.bn;
     const bool wres = args.w_resident != 0;
+    const bool presplit = args.presplit != 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = args.m_tiles * args.n_tiles;
     const uint64_t wait_ns = args.wait_ns;
@@ -217,7 +220,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             tc::mbar_init(&w_free[s], 1);
         }
         for (int s = 0; s < PS; ++s) {
-            tc::mbar_init(&planes_full[s], 128);
+            // Converted planes: one arrival per converter thread; pre-split
+            // planes: the producer's arrival plus the copies' bytes.
+            tc::mbar_init(&planes_full[s], presplit ? 1 : 128);
             tc::mbar_init(&planes_empty[s], 1);
         }
         tc::mbar_init(&w_ready, 1);
@@ -250,10 +255,43 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                         tc::tma_load_2d(sw_res + kb * args.w_block + j * bn * 128, &tma_w, &w_ready, kb * BK, j * p.n_pad + n0w);
             }
             int it = 0;
+            int last_pit[MAX_PLANE_STAGES];
+            for (int s = 0; s < MAX_PLANE_STAGES; ++s) last_pit[s] = -1;
             for (int tile = blockIdx.x; tile < total && !abort_flag; tile += gridDim.x) {
                 const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
                 for (int kb = 0; kb < args.kt; ++kb, ++it) {
                     const int s = it % S;
+                    if (presplit) {
+                        // The three pieces of the A tile straight into plane
+                        // stage sp once the MMAs have released it (piece j of
+                        // row r is row j m + r of the planes; rows past m of
+                        // the last tile read the next piece's rows, whose
+                        // outputs are never stored), W as before.
+                        const int sp = it % PS;
+                        const uint32_t par = ((it / PS) + 1) & 1;
+                        if ((it >= PS && !tc::mbar_wait(&planes_empty[sp], par, ROLE_BACKOFF, wait_ns, &abort_flag)) ||
+                            (!wres && it >= S &&
+                             !tc::mbar_wait(&w_free[s], ((it / S) + 1) & 1, ROLE_BACKOFF, wait_ns, &abort_flag))) {
+                            report(p, 1);
+                            abort_flag = 1;
+                            break;
+                        }
+                        if (p.skip_load && it == 0 && blockIdx.x == 0) continue;
+                        const int k0 = kb * BK;
+                        uint8_t* pl = splanes + sp * PLANES_STAGE;
+                        tc::mbar_expect_tx(&planes_full[sp], 3u * PLANE_BYTES);
+#pragma unroll
+                        for (int j = 0; j < 3; ++j) tc::tma_load_2d(pl + j * PLANE_BYTES, &tma_a, &planes_full[sp], k0, j * p.m + m0);
+                        last_pit[sp] = it;
+                        if (!wres) {
+                            uint8_t* w = sring + (size_t)s * args.a_stage_bytes;
+                            tc::mbar_expect_tx(&full[s], (uint32_t)args.w_bytes);
+#pragma unroll
+                            for (int j = 0; j < 3; ++j) tc::tma_load_2d(w + j * bn * 128, &tma_w, &full[s], k0, j * p.n_pad + n0);
+                            last_it[s] = it;
+                        }
+                        continue;
+                    }
                     if (it >= S) {
                         const uint32_t par = ((it / S) + 1) & 1;
                         if (!tc::mbar_wait(&f32_empty[s], par, ROLE_BACKOFF, wait_ns, &abort_flag) ||
@@ -301,6 +339,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             // Every copy issued has landed before the CTA can exit.
             for (int s = 0; s < S; ++s)
                 if (last_it[s] >= 0) tc::mbar_wait(&full[s], (last_it[s] / S) & 1, false, wait_ns);
+            for (int s = 0; s < PS; ++s)
+                if (last_pit[s] >= 0) tc::mbar_wait(&planes_full[s], (last_pit[s] / PS) & 1, false, wait_ns);
             if (wres) tc::mbar_wait(&w_ready, 0, false, wait_ns);
         }
     } else if (warp == 1) {
@@ -370,11 +410,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             tc::mbar_wait(&drain_bar, 0, false, wait_ns);
         }
     } else if (warp < 6) {
-        // Converters: thread r owns row r of every tile.
+        // Converters: thread r owns row r of every tile (idle when A arrives
+        // pre-split).
         const int r = threadIdx.x - 64;
         const int swz = r & 7;
         int it = 0;
-        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        for (int tile = presplit ? total : (int)blockIdx.x; tile < total; tile += gridDim.x) {
             if (abort_flag) break;
             const int m0 = (tile / args.n_tiles) * BM;
             const int row = m0 + r;
@@ -677,20 +718,24 @@ bool gemm_split_supported(const SplitGemmParams& p) {
     const int kt = split_k_blocks(p);
     if (kt <= 0 || !split_tmem_cols(bn, (kt + KCHUNK - 1) / KCHUNK)) return false;
     if (p.conv) {
+        if (p.a_planes) return false;
         const int cin = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
         if ((cin != 32 && cin % 64) || cin <= 0 || p.k != p.kh * p.kw * cin || p.lda % 4 || p.lda < cin || p.gate || p.residual)
             return false;
         return p.n_img > 0 && p.hi > 0 && p.wi > 0 && p.ho > 0 && p.wo > 0 && (p.stride == 1 || p.stride == 2);
     }
-    if (p.m <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k) return false;
+    if (p.m <= 0 || p.k % 16) return false;
+    if (!p.a_planes && (p.lda % 4 || p.lda < p.k)) return false;
     if (p.res_scale < 1 || (p.res_scale & (p.res_scale - 1))) return false;
     if ((p.gate || p.res_gate) && p.rows_per_image < 1) return false;
     return true;
 }
 
 cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
-    if (!gemm_split_supported(in) || !in.a || !in.w || !in.c) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(in.a) % 16) || (reinterpret_cast<uintptr_t>(in.w) % 16)) return cudaErrorInvalidValue;
+    const bool presplit = in.a_planes != nullptr;
+    if (!gemm_split_supported(in) || (!presplit && !in.a) || !in.w || !in.c) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(presplit ? in.a_planes : in.a) % 16) || (reinterpret_cast<uintptr_t>(in.w) % 16))
+        return cudaErrorInvalidValue;
     float* cbase = in.c + in.coff;
     if (reinterpret_cast<uintptr_t>(cbase) % 16) return cudaErrorInvalidValue;
     SplitArgs a;
@@ -727,22 +772,48 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     int grid = tiles < sms ? tiles : sms;
     if (tiles > sms && a.n_tiles > 1 && a.n_tiles <= sms / 2) grid = sms - sms % a.n_tiles;
     const bool fixed_n = tiles <= grid || grid % a.n_tiles == 0;
-    a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
-    a.plane_stages = a.kt == 1 ? SINGLE_BLOCK_PLANES : PLANE_STAGES;
+    a.presplit = presplit ? 1 : 0;
     int fixed = 0;
     a.stages = 0;
-    for (int resident = (fixed_n && a.kt * a.w_block <= W_RESIDENT_MAX) ? 1 : 0; resident >= 0 && a.stages < 2; --resident) {
-        a.w_resident = resident;
-        a.w_region = resident ? a.kt * a.w_block : 0;
-        a.a_stage_bytes = a.a_box_bytes + (resident ? 0 : a.w_block);
-        for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
-            fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;
-            a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
-            if (a.stages >= 2) break;
+    const int can_resident = (fixed_n && a.kt * a.w_block <= W_RESIDENT_MAX) ? 1 : 0;
+    if (presplit) {
+        // No FP32 A: the ring holds only streamed W (nothing when W is
+        // resident), so the shared memory goes to a deeper plane ring.
+        a.a_box_bytes = 0;
+        for (int resident = can_resident; resident >= 0 && !a.stages; --resident) {
+            a.w_resident = resident;
+            a.w_region = resident ? a.kt * a.w_block : 0;
+            a.a_stage_bytes = resident ? 0 : a.w_block;
+            for (int ps = MAX_PLANE_STAGES; ps >= 2 && !a.stages; --ps)
+                for (int bufs = STAGE_BUFS; bufs >= 1 && !a.stages; --bufs) {
+                    const int f = align + a.w_region + ps * PLANES_STAGE + EPI_WARPS * bufs * STAGE_OUT;
+                    const int avail = SMEM_MAX - 1024 - f;   // 1 KB left for the static barriers
+                    if (avail < 0) continue;
+                    const int st = resident ? 1 : avail / a.a_stage_bytes;
+                    if (!resident && st < 2) continue;
+                    a.stages = st > MAX_A ? MAX_A : st;
+                    a.plane_stages = ps;
+                    a.stage_bufs = bufs;
+                    fixed = f;
+                }
         }
+        if (!a.stages) return cudaErrorInvalidConfiguration;
+    } else {
+        a.a_box_bytes = (in.conv || in.k > 32) ? 2 * BOX_BYTES : BOX_BYTES;
+        a.plane_stages = a.kt == 1 ? SINGLE_BLOCK_PLANES : PLANE_STAGES;
+        for (int resident = can_resident; resident >= 0 && a.stages < 2; --resident) {
+            a.w_resident = resident;
+            a.w_region = resident ? a.kt * a.w_block : 0;
+            a.a_stage_bytes = a.a_box_bytes + (resident ? 0 : a.w_block);
+            for (a.stage_bufs = STAGE_BUFS; a.stage_bufs >= 1; --a.stage_bufs) {
+                fixed = align + a.w_region + a.plane_stages * PLANES_STAGE + EPI_WARPS * a.stage_bufs * STAGE_OUT;
+                a.stages = (SMEM_MAX - 1024 - fixed) / a.a_stage_bytes;   // 1 KB left for the static barriers
+                if (a.stages >= 2) break;
+            }
+        }
+        if (a.stages > MAX_A) a.stages = MAX_A;
+        if (a.stages < 2) return cudaErrorInvalidConfiguration;
     }
-    if (a.stages > MAX_A) a.stages = MAX_A;
-    if (a.stages < 2) return cudaErrorInvalidConfiguration;
     const int smem = fixed + a.stages * a.a_stage_bytes;
     CUtensorMap ma, mw, mc;
     if (in.conv) {
@@ -751,8 +822,10 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
             !make_map4(&mc, cbase, (uint64_t)in.n, (uint64_t)in.wo, (uint64_t)in.ho, (uint64_t)in.n_img, (uint64_t)in.ldc * 4,
                        16, 16, 2, 1, CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
-    } else if (!make_map(&ma, in.a, (uint64_t)in.k, (uint64_t)in.m, (uint64_t)in.lda * 4, 32, BM,
-                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32) ||
+    } else if (!(presplit ? make_map(&ma, in.a_planes, (uint64_t)in.k_pad, (uint64_t)3 * in.m, (uint64_t)in.k_pad * 2, BK, BM,
+                                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)
+                          : make_map(&ma, in.a, (uint64_t)in.k, (uint64_t)in.m, (uint64_t)in.lda * 4, 32, BM,
+                                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
                !make_map(&mc, cbase, (uint64_t)in.n, (uint64_t)in.m, (uint64_t)in.ldc * 4, 16, 32,
                          CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B)) {
         return cudaErrorInvalidValue;
@@ -772,5 +845,58 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     }
 }
 
+
+namespace {
+
+// One thread per (row, 8 columns): the gated A values split exactly as the
+// converter warps split them (split8), each piece's 8 columns one 16-byte
+// store into its plane.  Zeros past column k.
+__global__ void __launch_bounds__(256) split_planes_kernel(SplitGemmParams p, uint4* planes) {
+    const int q_row = p.k_pad / 8;
+    const long long total = (long long)p.m * q_row;
+    const size_t plane = (size_t)p.m * q_row;   // uint4 per plane
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / q_row), q = (int)(i - (long long)row * q_row), k0 = q * 8;
+        float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (k0 < p.k) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(p.a + (size_t)row * p.lda + k0));
+            const float4 v = __ldg(reinterpret_cast<const float4*>(p.a + (size_t)row * p.lda + k0 + 4));
+            x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w; x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
+            if (p.gate) {
+                const float* g = p.gate + (size_t)(row / p.rows_per_image) * p.k + k0;
+                const float4 g0 = __ldg(reinterpret_cast<const float4*>(g));
+                const float4 g1 = __ldg(reinterpret_cast<const float4*>(g + 4));
+                x[0] *= g0.x; x[1] *= g0.y; x[2] *= g0.z; x[3] *= g0.w;
+                x[4] *= g1.x; x[5] *= g1.y; x[6] *= g1.z; x[7] *= g1.w;
+            }
+        }
+        uint4 hi, mid, lo;
+        split8(x, hi, mid, lo);
+        planes[(size_t)i] = hi;
+        planes[plane + (size_t)i] = mid;
+        planes[2 * plane + (size_t)i] = lo;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_split_planes(const SplitGemmParams& p, void* planes, cudaStream_t stream) {
+    if (!p.a || !planes || p.conv || p.m <= 0 || p.k <= 0 || p.k % 16 || p.lda % 4 || p.lda < p.k || p.k_pad % BK ||
+        p.k_pad < p.k || (p.gate && p.rows_per_image < 1))
+        return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(p.a) % 16 || reinterpret_cast<uintptr_t>(planes) % 16 ||
+        (p.gate && reinterpret_cast<uintptr_t>(p.gate) % 16) || (p.gate && p.k % 4))
+        return cudaErrorInvalidValue;
+    const long long total = (long long)p.m * (p.k_pad / 8);
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148LL * 32) blocks = 148LL * 32;
+    split_planes_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, stream>>>(p, static_cast<uint4*>(planes));
+    return cudaGetLastError();
+}
+
+bool gemm_split_presplit_pays(int m, int n, int k) {
+    const int bn = gemm_split_tile_n(n, k);
+    return m > 0 && bn > 0 && (n + bn - 1) / bn >= 3;
+}
 
 }  // namespace ppocr

@@ -243,16 +243,28 @@ struct SplitGemmParams {
     int* err = nullptr;               // wait-expiry flag (null: g_split_error)
     uint64_t wait_ns = 0;             // pipeline wait bound (0: 2 s)
     int skip_load = 0;                // self-test only: CTA 0's first stage is never loaded
+    // Pre-split A (dense mode only): BF16 [3][m][k_pad], the three pieces of
+    // the gated A as launch_split_planes writes them.  The GEMM then loads the
+    // pieces like W instead of splitting A in shared memory for every N tile
+    // (`a` and `gate` unused); the products, and so C, are bit-identical.
+    const void* a_planes = nullptr;
     // Implicit-GEMM convolution (conv = 1): A is the NHWC FP32 input
-    // [n_img][hi][wi] with pixel pitch lda, cin == 32 (K order (ky, kx,
-    // channel), k = kh * kw * 32); a tile is 8 x 16 output pixels of one image,
-    // each 64-wide K block two taps, each loaded as a strided 4D TMA box; C is
-    // NHWC [n_img][ho][wo] with pixel pitch ldc at channel coff.
-    // No gate and no residual in this mode.
+    // [n_img][hi][wi] with pixel pitch lda, cin == 32 or a multiple of 64 (K
+    // order (ky, kx, channel), k = kh * kw * cin); a tile is 8 x 16 output
+    // pixels of one image, each 64-wide K block one or two taps in strided 4D
+    // TMA boxes; C is NHWC [n_img][ho][wo] with pixel pitch ldc at channel
+    // coff.  No gate, residual or pre-split A in this mode.
     int conv = 0;
     int n_img = 0, hi = 0, wi = 0, ho = 0, wo = 0, kh = 0, kw = 0, stride = 1, pt = 0, pl = 0;
 };
 int gemm_split_tile_n(int n, int k);  // output channels per tile for K = k (n_pad is a multiple of it; 0: K too long)
+// The three BF16 pieces of A (gated as the GEMM would gate it) into
+// planes [3][m][k_pad], zeros past column k: p.a, p.lda, p.gate,
+// p.rows_per_image, p.m, p.k, p.k_pad of a dense SplitGemmParams.
+cudaError_t launch_split_planes(const SplitGemmParams& p, void* planes, cudaStream_t stream);
+// Whether pre-splitting A pays for this shape: A would otherwise be split once
+// per N tile, and three or more tiles cost more than the pieces' round trip.
+bool gemm_split_presplit_pays(int m, int n, int k);
 bool gemm_split_supported(const SplitGemmParams& p);
 cudaError_t launch_gemm_split(const SplitGemmParams& p, cudaStream_t stream);
 

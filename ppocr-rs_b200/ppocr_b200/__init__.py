@@ -431,7 +431,8 @@ class Gpu:
 
     def selftest_gemm_f32(self, a, w, bias=None, act: int = 0, gate=None, rows_per_image: int = 1, residual=None,
                           kernel: int = 0):
-        """FP32 GEMM diagnostic through one kernel (0 dispatch, 1 SIMT, 2 rows, 3 streaming);
+        """FP32 GEMM diagnostic through one kernel (0 dispatch, 1 SIMT, 2 rows, 3 streaming,
+        4 the tcgen05 split GEMM, 5 the split GEMM with A pre-split by its own kernel);
         returns (C float32 [m, n], kernel that ran)."""
         a = np.ascontiguousarray(a, dtype=np.float32)
         w = np.ascontiguousarray(w, dtype=np.float32)

@@ -44,6 +44,7 @@ SHAPES = [
     (700, 64, 576, 1, False, False, 1),          # two accumulators (5 + 4 K blocks)
     (300, 32, 1024, 3, True, False, 100),        # four
     (257, 16, 1792, 0, False, True, 1),          # six (the medium detector's longest K)
+    (1000, 512, 1024, 0, True, True, 500),       # the medium detector's stage-2 pw2 shape: 16 N tiles, gated
 ]
 
 
@@ -68,6 +69,10 @@ def test_split_gemm_fp32_class(gpu, m, n, k, act, gated, res, rpi):
     bound = 16 * 2.0 ** -24 * mag + (2.0 ** -24 * np.abs(r) if res else 0) + 1e-30
     err = np.abs(c - ref)
     assert np.all(err <= bound * 1.5 + 1e-6 * (act == 3)), f"worst {float((err / bound).max()):.2f}x the bound"
+    # A pre-split into its pieces by its own kernel: the same products, bit for bit.
+    c5, used5 = gpu.selftest_gemm_f32(a, w, b, act, g, rpi, r, kernel=5)
+    assert used5 == 5
+    np.testing.assert_array_equal(c5, c)
     # Close to the CUDA-core FP32 kernel on the same inputs.
     c2, _ = gpu.selftest_gemm_f32(a, w, b, act, g, rpi, r, kernel=1)
     assert np.abs(c - c2).max() <= 1e-4 * max(1.0, float(np.abs(c2).max()))
