@@ -293,7 +293,7 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
  * TMEM (FP32-class rounding, not bit-identical to the CUDA-core kernels);
  * kernel 5 = the same with A split into its pieces by a kernel of its own
  * first (the model's choice when A would otherwise be split once per output
- * tile of three or more): bit-identical to kernel 4. */
+ * tile of four or more): bit-identical to kernel 4. */
 int ppocr_selftest_gemm_f32(ppocr_gpu* gpu, int m, int n, int k, const float* a, const float* w, const float* bias,
                             int act, const float* gate, int rows_per_image, const float* residual, int kernel, float* c,
                             int* kernel_used);

@@ -895,8 +895,10 @@ cudaError_t launch_split_planes(const SplitGemmParams& p, void* planes, cudaStre
 }
 
 bool gemm_split_presplit_pays(int m, int n, int k) {
+    // Measured on B200: the pieces' round trip (10 bytes per element) costs
+    // about as much as splitting A in shared memory for 2-3 N tiles.
     const int bn = gemm_split_tile_n(n, k);
-    return m > 0 && bn > 0 && (n + bn - 1) / bn >= 3;
+    return m > 0 && bn > 0 && (n + bn - 1) / bn >= 4;
 }
 
 }  // namespace ppocr

@@ -263,7 +263,7 @@ int gemm_split_tile_n(int n, int k);  // output channels per tile for K = k (n_p
 // p.rows_per_image, p.m, p.k, p.k_pad of a dense SplitGemmParams.
 cudaError_t launch_split_planes(const SplitGemmParams& p, void* planes, cudaStream_t stream);
 // Whether pre-splitting A pays for this shape: A would otherwise be split once
-// per N tile, and three or more tiles cost more than the pieces' round trip.
+// per N tile, and four or more tiles cost more than the pieces' round trip.
 bool gemm_split_presplit_pays(int m, int n, int k);
 bool gemm_split_supported(const SplitGemmParams& p);
 cudaError_t launch_gemm_split(const SplitGemmParams& p, cudaStream_t stream);
