@@ -13,9 +13,10 @@
 // zero-filled), so every input element is read from HBM about once instead
 // of k^2 times.  Blocks are persistent and double-buffer the input tile: the
 // copies of the next tile are in flight while the current one is computed.
-// Each thread computes RUN = 4 horizontally adjacent outputs of one channel
-// quad: per kernel row it loads the (RUN - 1) * SW + KW window pixels once
-// into registers and each weight once for all RUN outputs.  Kernel size and
+// Each thread computes RUN horizontally adjacent outputs of one channel
+// quad (tiled_run: 8 for square kernels of 5x5 and up, else 4): per kernel
+// row it loads the (RUN - 1) * SW + KW window pixels once into registers and
+// each weight once for all RUN outputs.  Kernel size and
 // strides are template parameters, so the window stays in registers; the
 // tile shape is chosen per launch to divide the output evenly.
 #include <algorithm>
@@ -30,13 +31,19 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kRun = 4;
 
+// Outputs per thread along a tile row in the tiled kernel: 8 for the square
+// 5x5 and larger kernels, whose wide windows are mostly shared between
+// neighbouring outputs (a 9x9 run of 8 loads 16 window pixels per row for 72
+// multiply-adds), 4 for the rest.
+__host__ __device__ constexpr int tiled_run(int kh, int kw) { return kh == kw && kh >= 5 ? 8 : kRun; }
+
 // Tile geometry, chosen per launch from the output extent: about TH0 x TW0
 // outputs (8 x 32 at stride 1, halved along a strided axis) reshaped so the
 // tiles divide the output evenly (a 3-row recognizer map gets 3-row tiles
 // twice as wide instead of 8-row tiles that are mostly empty).  The input tile
 // (ih x iw) covers every window the tile's outputs read.
 struct DwGeom {
-    int th, tw, ih, iw, runs;          // output tile, input tile, kRun-wide runs per tile row
+    int th, tw, ih, iw, runs;          // output tile, input tile, tiled_run-wide runs per tile row
     int tiles_x, tiles_y, groups, total;
     float inv_runs, inv_iw;            // reciprocals for exact small-integer division
 };
@@ -125,15 +132,16 @@ __global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, DwGe
         const int c = c0 + q * 4;
         const float4 bias = p.bias ? *reinterpret_cast<const float4*>(p.bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         constexpr int PX = kThreads / CG;
-        constexpr int SPAN = (kRun - 1) * SW + KW;
+        constexpr int RUN = tiled_run(KH, KW);
+        constexpr int SPAN = (RUN - 1) * SW + KW;
         const int items = g.th * g.runs;
         for (int pp = threadIdx.x / CG; pp < items; pp += PX) {
-            const int ty = div_small(pp, g.inv_runs), tx0 = (pp - ty * g.runs) * kRun;
+            const int ty = div_small(pp, g.inv_runs), tx0 = (pp - ty * g.runs) * RUN;
             const int oy = oy0 + ty;
             if (oy >= p.ho || ox0 + tx0 >= p.wo) continue;
-            float4 acc[kRun];
+            float4 acc[RUN];
 #pragma unroll
-            for (int r = 0; r < kRun; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < RUN; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int ky = 0; ky < KH; ++ky) {
                 const T* row = tileb + ((size_t)((ty * SH + ky) * g.iw + tx0 * SW) * CG + q) * 4;
@@ -145,11 +153,11 @@ __global__ void __launch_bounds__(kThreads) dwconv_tiled_kernel(DwParams p, DwGe
                 for (int kx = 0; kx < KW; ++kx) {
                     const float4 w = wr[kx * CG];
 #pragma unroll
-                    for (int r = 0; r < kRun; ++r) acc[r] = f4_vfma(win[r * SW + kx], w, acc[r]);
+                    for (int r = 0; r < RUN; ++r) acc[r] = f4_vfma(win[r * SW + kx], w, acc[r]);
                 }
             }
 #pragma unroll
-            for (int r = 0; r < kRun; ++r) {
+            for (int r = 0; r < RUN; ++r) {
                 const int ox = ox0 + tx0 + r;
                 if (ox >= p.wo) break;
                 float4 v = f4_add(acc[r], bias);
@@ -190,20 +198,21 @@ inline int resident_blocks(int nregs, int threads, size_t smem) {
 // evenly, then fits the double-buffered input tile into shared memory.
 inline DwGeom dw_geometry(const DwParams& p, int th0, int tw0, int groups, size_t pix_bytes, size_t wbytes) {
     DwGeom g{};
+    const int run = tiled_run(p.kh, p.kw);
     g.tiles_y = (p.ho + th0 - 1) / th0;
     g.th = (p.ho + g.tiles_y - 1) / g.tiles_y;
-    int tw_max = (th0 * tw0 / g.th) / kRun * kRun;
-    if (tw_max < kRun) tw_max = kRun;
+    int tw_max = (th0 * tw0 / g.th) / run * run;
+    if (tw_max < run) tw_max = run;
     for (;;) {
         g.tiles_x = (p.wo + tw_max - 1) / tw_max;
         const int tw = (p.wo + g.tiles_x - 1) / g.tiles_x;
-        g.tw = (tw + kRun - 1) / kRun * kRun;
+        g.tw = (tw + run - 1) / run * run;
         g.ih = (g.th - 1) * p.sh + p.kh;
         g.iw = (g.tw - 1) * p.sw + p.kw;
-        if (2 * (size_t)g.ih * g.iw * pix_bytes + wbytes <= kSmemLimit || tw_max == kRun) break;
-        tw_max -= kRun;
+        if (2 * (size_t)g.ih * g.iw * pix_bytes + wbytes <= kSmemLimit || tw_max == run) break;
+        tw_max -= run;
     }
-    g.runs = g.tw / kRun;
+    g.runs = g.tw / run;
     g.groups = groups;
     const long long total = (long long)p.n * groups * g.tiles_x * g.tiles_y;
     g.total = total > 0x7fffffffLL ? -1 : (int)total;
