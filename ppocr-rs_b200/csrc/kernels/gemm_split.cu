@@ -22,13 +22,16 @@
 //                     S2 = a0 w2 + a1 w1 side by side, each A plane is read
 //                     once per step, and the dominant sum D is rounded once
 //                     per step; two accumulators, so a tile's MMAs overlap
-//                     the previous tile's epilogue;
+//                     the previous tile's epilogue (one, twice as wide, for
+//                     the long-K GEMMs whose dominant-sum chunks fill TMEM);
 //   warps 6-13        epilogue: (S2 + S1) + D, bias, activation, optional
 //                     gated / upsampled residual, 64-byte-swizzled staging
 //                     tile, TMA store.  Two groups of four warps (one per
 //                     TMEM lane quarter) take alternate tiles, each owning
-//                     one accumulator buffer, so two tiles' epilogues overlap;
-//                     the residual is fetched one 16-column group ahead.
+//                     one accumulator buffer, so two tiles' epilogues overlap
+//                     (with one buffer each group takes half of every tile's
+//                     columns); the residual is fetched one 16-column group
+//                     ahead.
 //
 // Every mbarrier wait is bounded by the GPU's global timer; on expiry the
 // kernel records a code in *err (or g_split_error), stops, lets its copies
@@ -87,6 +90,10 @@ constexpr int SMEM_MAX = 227 * 1024;                   // opt-in shared memory p
 // (K = 320) keep it at the CUDA-core FP32 kernels' level, and longer sums are
 // split over several accumulators added in the epilogue (round to nearest).
 constexpr int KCHUNK = 5;
+#ifndef SPLIT_SINGLE_ACC_CHUNKS
+#define SPLIT_SINGLE_ACC_CHUNKS 3
+#endif
+constexpr int SINGLE_ACC_CHUNKS = SPLIT_SINGLE_ACC_CHUNKS;
 
 // Shared memory, 1024-byte aligned pieces: [resident W] [plane ring]
 // [epilogue staging] [FP32 ring: per stage the A boxes, then (streamed) W].
@@ -94,6 +101,7 @@ struct SplitArgs {
     SplitGemmParams p;
     int bn, kt, m_tiles, n_tiles, tmem_cols;
     int kchunk, dchunks;    // K blocks per dominant-sum accumulator, and their count
+    int nacc;               // TMEM accumulator buffers: 2 (a tile's MMAs overlap the previous tile's epilogue) or 1
     int tiles_y, tiles_x;   // conv mode: tile grid per image
     int cpt;                // conv mode: input channels per tap (32: two taps per K block; a multiple of 64: cpt / 64 blocks per tap)
     int w_resident;         // 1: every tile of a CTA has the same N tile, whose W (all K blocks) is loaded once
@@ -228,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         tc::mbar_init(&w_ready, 1);
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], 4 * 32);   // one epilogue group per buffer
+            tc::mbar_init(&acc_empty[b], (args.nacc == 2 ? 4 : 8) * 32);   // the epilogue warps of a buffer's tiles
         }
         tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
@@ -356,8 +364,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             }
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; ok && tile < total && !abort_flag; tile += gridDim.x, ++ti) {
-                const int b = ti & 1;
-                if (ti >= 2 && !tc::mbar_wait(&acc_empty[b], ((ti >> 1) + 1) & 1, ROLE_BACKOFF, wait_ns, &abort_flag)) {
+                const int b = ti % args.nacc;
+                if (ti >= args.nacc &&
+                    !tc::mbar_wait(&acc_empty[b], ((ti / args.nacc) + 1) & 1, ROLE_BACKOFF, wait_ns, &abort_flag)) {
                     report(p, 2);
                     abort_flag = 1;
                     break;
@@ -464,18 +473,21 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
         }
     } else {
         // Epilogue warps 6-13: two groups of four, one warp per TMEM lane
-        // quarter (warp % 4) in each.  Group g = (warp - 6) / 4 owns
-        // accumulator buffer g and so every other tile: two tiles' epilogues
-        // run at once, and each warp walks all of its tile's 16-column groups.
+        // quarter (warp % 4) in each.  With two accumulator buffers group
+        // g = (warp - 6) / 4 owns buffer g and so every other tile: two tiles'
+        // epilogues run at once, and each warp walks all of its tile's
+        // 16-column groups.  With one buffer both groups take every tile, group
+        // g the g-th half of its 16-column groups (so neither can wait on a
+        // later tile's phase of the shared barrier).
         const int q = warp & 3, grp = (warp - 6) >> 2;
         uint8_t* stage0 = sout + (warp - 6) * args.stage_bufs * STAGE_OUT;
         int sbuf = 0;
         const int swz = (lane >> 1) & 3;   // 64-byte swizzle: chunk ^= row bits 1-2
         int ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
-            if ((ti & 1) != grp) continue;
+            if (args.nacc == 2 && (ti & 1) != grp) continue;
             if (abort_flag) break;
-            const int b = grp;
+            const int b = ti % args.nacc;
             const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * bn;
             const int row = m0 + q * 32 + lane;
             const bool live = row < p.m;
@@ -513,8 +525,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 }
             };
             float res[16];
-            load_res(n0, res);
-            bool got = tc::mbar_wait(&acc_full[b], (ti >> 1) & 1, true, wait_ns, &abort_flag);
+            const int ngroups = bn / 16, gsplit = (ngroups + 1) / 2;
+            const int cb0 = args.nacc == 2 || grp == 0 ? 0 : gsplit * 16;
+            const int cb1 = args.nacc == 2 || grp == 1 ? bn : gsplit * 16;
+            load_res(n0 + cb0, res);
+            bool got = tc::mbar_wait(&acc_full[b], (ti / args.nacc) & 1, true, wait_ns, &abort_flag);
             got = __all_sync(0xffffffffu, got);
             if (!got) {
                 if (lane == 0) report(p, 5);
@@ -523,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             }
             tc::fence_after();
             const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * (2 + args.dchunks) * bn);
-            for (int cb = 0; cb < bn && n0 + cb < p.n; cb += 16) {
+            for (int cb = cb0; cb < cb1 && n0 + cb < p.n; cb += 16) {
                 const int col0 = n0 + cb;
                 uint32_t r0[16], r1[16], r2[16];
                 tc::tmem_ld16_async(tb + (uint32_t)cb, r0);
@@ -537,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
                 tc::tmem_ld16_async(tb + (uint32_t)(bn + cb), r1);
                 tc::tmem_ld16_async(tb + (uint32_t)(2 * bn + cb), r2);
                 float nres[16];
-                load_res(col0 + 16 < n0 + bn ? col0 + 16 : p.n, nres);
+                load_res(col0 + 16 < n0 + cb1 ? col0 + 16 : p.n, nres);
                 const bool full_cols = col0 + 16 <= p.n;
                 float bias[16];
                 if (p.bias && full_cols) {
@@ -675,10 +690,13 @@ int gemm_split_tile_n(int n, int k) {
     // epilogue stores 16-column boxes, so none reaches the next tile).  The
     // widest tile is 64 columns, less when the dominant-sum accumulators of a
     // long K need the TMEM: two buffers of (2 + chunks) tile widths in 512
-    // columns.  0 when K needs more accumulators than fit at width 16.
+    // columns, or from SPLIT_SINGLE_ACC_CHUNKS chunks on one buffer of twice
+    // the width (fewer N tiles, so A is read and split fewer times, for a
+    // tile's MMAs no longer overlapping the previous tile's epilogue).  0 when
+    // K needs more accumulators than fit at width 16.
     const int kt = (k + BK - 1) / BK;
     const int chunks = kt < 1 ? 1 : (kt + KCHUNK - 1) / KCHUNK;
-    int max_bn = 256 / (2 + chunks) / 16 * 16;
+    int max_bn = (chunks >= SINGLE_ACC_CHUNKS ? 512 : 256) / (2 + chunks) / 16 * 16;
     if (max_bn > MAX_BN) max_bn = MAX_BN;
     if (max_bn < 16) return 0;
     const int n16 = (n + 15) / 16 * 16;
@@ -700,11 +718,16 @@ int split_k_blocks(const SplitGemmParams& p) {
     return (p.k + BK - 1) / BK;
 }
 
-// TMEM columns: two accumulator buffers of (2 + chunks) BN columns each,
-// rounded up to a power of two (0 when more than the 512 of an SM).
+// Accumulator buffers of (2 + chunks) BN columns each: two when both fit in
+// the 512 TMEM columns of an SM, else one (the long-K tiles of
+// gemm_split_tile_n, whose MMAs then wait for the previous tile's epilogue).
+int split_acc_buffers(int bn, int dchunks) { return 2 * (2 + dchunks) * bn <= 512 ? 2 : 1; }
+
+// TMEM columns of those buffers, rounded up to a power of two (0 when one
+// buffer needs more than 512).
 int split_tmem_cols(int bn, int dchunks) {
     int cols = 32;
-    while (cols < 2 * (2 + dchunks) * bn) cols <<= 1;
+    while (cols < split_acc_buffers(bn, dchunks) * (2 + dchunks) * bn) cols <<= 1;
     return cols > 512 ? 0 : cols;
 }
 
@@ -755,6 +778,7 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     a.kchunk = KCHUNK;
     a.dchunks = (a.kt + KCHUNK - 1) / KCHUNK;
     a.tmem_cols = split_tmem_cols(a.bn, a.dchunks);
+    a.nacc = split_acc_buffers(a.bn, a.dchunks);
     if (!a.tmem_cols) return cudaErrorInvalidConfiguration;
     a.wait_ns = in.wait_ns ? in.wait_ns : tc::kWaitNs;
     // Shared memory: the plane ring and the staging tiles are fixed; W is
