@@ -274,7 +274,8 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
 
 /* Diagnostic (new): the split GEMM's implicit-conv mode (FP32 operands in
  * three BF16 pieces on tcgen05) on an NHWC FP32 input x [n, hi, wi, cin]
- * (cin 32 or a multiple of 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
+ * (cin 32, or above 32 in multiples of 4: each tap's channels are read
+ * zero-padded to a multiple of 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
  * padding `pad` and stride 1 or 2; out receives [n, ho, wo, cout] NHWC,
  * act as for ppocr_selftest_gemm_ex.  The model's dense FP32 convs over one
  * such source use this path. */

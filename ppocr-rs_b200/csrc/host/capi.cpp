@@ -1408,12 +1408,14 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
         SplitGemmParams p;
         p.conv = 1;
         p.n_img = n; p.hi = hi; p.wi = wi; p.ho = ho; p.wo = wo; p.kh = kh; p.kw = kw; p.stride = stride; p.pt = pad; p.pl = pad;
-        p.k = kh * kw * cin; p.n = cout; p.lda = cin; p.ldc = cout; p.coff = 0; p.act = act;
+        const int cpt = gemm_split_conv_cpt(cin);
+        p.k = kh * kw * cpt; p.cin = cin; p.n = cout; p.lda = cin; p.ldc = cout; p.coff = 0; p.act = act;
         const int bn = gemm_split_tile_n(cout, p.k);
         p.n_pad = bn > 0 ? (cout + bn - 1) / bn * bn : 0;
         p.k_pad = (p.k + 63) / 64 * 64;
         p.m = n * ((ho + 7) / 8) * ((wo + 15) / 16) * 128;
-        if (!gemm_split_supported(p)) fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split conv takes 32 input channels or a multiple of 64");
+        if (!cpt || !gemm_split_supported(p))
+            fail(PPOCR_ERR_INVALID_INPUT, "invalid input: the split conv takes 32 input channels or more than 32 in multiples of 4");
         std::lock_guard<std::mutex> lock(gpu->mu);
         gpu->bind();
         ConvWeight cw;
@@ -1422,7 +1424,7 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
         cw.b = bias ? std::vector<float>(bias, bias + cout) : std::vector<float>(cout, 0.f);
         const size_t out_elems = (size_t)n * ho * wo * cout;
         WeightBlob blob;
-        const size_t wo_ = blob.add_bf16(pack_engine_kn(cw, 3, p.n_pad, p.k_pad));
+        const size_t wo_ = blob.add_bf16(pack_engine_kn(cw, 3, p.n_pad, p.k_pad, cpt));
         const size_t bo = blob.add_f32(cw.b);
         const size_t xo = blob.add_f32(std::vector<float>(x, x + (size_t)n * hi * wi * cin));
         const size_t co = blob.add_f32(std::vector<float>(out_elems, 0.f));

@@ -166,20 +166,22 @@ public:
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
         if (split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 && srcs[0].coff == 0 &&
             residual < 0 && sh == sw) {
-            // FP32 mode: a dense conv over one plain 32-channel NHWC source as an
-            // implicit split GEMM on tcgen05 (one strided TMA box per tap).
+            // FP32 mode: a dense conv over one plain NHWC source as an implicit
+            // split GEMM on tcgen05 (strided TMA boxes per tap; each tap's
+            // channels padded with zeros to 32 or a multiple of 64).
+            const int cpt = gemm_split_conv_cpt(cin);
             SplitGemmParams sp;
             sp.conv = 1;
             sp.n_img = n; sp.hi = hi; sp.wi = wi; sp.ho = ho; sp.wo = wo; sp.kh = cw.kh; sp.kw = cw.kw;
             sp.stride = sh; sp.pt = pt; sp.pl = pl;
-            sp.k = cw.kh * cw.kw * cin; sp.n = cw.cout; sp.lda = srcs[0].cstride;
+            sp.k = cw.kh * cw.kw * cpt; sp.cin = cin; sp.n = cw.cout; sp.lda = srcs[0].cstride;
             sp.ldc = out_cstride; sp.coff = out_coff; sp.act = act;
-            const int bn = gemm_split_tile_n(cw.cout, cw.kh * cw.kw * cin);
+            const int bn = gemm_split_tile_n(cw.cout, sp.k);
             sp.n_pad = bn > 0 ? (cw.cout + bn - 1) / bn * bn : 0;
             sp.k_pad = (sp.k + 63) / 64 * 64;
             sp.m = n * ((ho + 7) / 8) * ((wo + 15) / 16) * 128;
-            if (gemm_split_supported(sp)) {
-                const size_t woff = m_.blob.add_bf16(pack_engine_kn(cw, 3, sp.n_pad, sp.k_pad));
+            if (cpt > 0 && gemm_split_supported(sp)) {
+                const size_t woff = m_.blob.add_bf16(pack_engine_kn(cw, 3, sp.n_pad, sp.k_pad, cpt));
                 const size_t boff = m_.blob.add_f32(cw.b);
                 const int stid = srcs[0].tid, otid = out.tid;
                 m_.plan.add_op(name, {stid}, {otid}, [sp, woff, boff, stid, otid](const Ctx& c, cudaStream_t st) mutable {

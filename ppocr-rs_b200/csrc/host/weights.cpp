@@ -230,14 +230,15 @@ float bf16_round(float f) {
     return r;
 }
 
-std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad) {
+std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad, int cin_pad) {
     const int taps = cw.kh * cw.kw;
+    const int cpt = cin_pad > 0 ? cin_pad : cw.cin;   // K columns per tap (the padding stays zero)
     std::vector<float> out((size_t)planes * n_pad * k_pad, 0.f);
     for (int o = 0; o < cw.cout; ++o)
         for (int t = 0; t < taps; ++t)
             for (int i = 0; i < cw.cin; ++i) {
                 float v = cw.w[((size_t)o * cw.cin + i) * taps + t];
-                const size_t col = (size_t)t * cw.cin + i;
+                const size_t col = (size_t)t * cpt + i;
                 for (int pl = 0; pl < planes; ++pl) {
                     const float piece = bf16_round(v);   // x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1)
                     out[((size_t)pl * n_pad + o) * k_pad + col] = piece;

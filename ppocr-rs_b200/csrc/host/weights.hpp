@@ -67,7 +67,8 @@ std::vector<float> pack_conv_halo(const ConvWeight& cw, int bn);          // [ce
 // Tensor-core engine weights: [planes][n_pad][k_pad] with k = (ky, kx, i); plane
 // p holds the p-th BF16 piece of each value (planes 1: bf16(w); planes 3: the
 // three-way split w = w0 + w1 + w2), every value exactly representable in BF16.
-std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad);
+// cin_pad > cin: each tap takes cin_pad K columns, the last cin_pad - cin zero.
+std::vector<float> pack_engine_kn(const ConvWeight& cw, int planes, int n_pad, int k_pad, int cin_pad = 0);
 float bf16_round(float f);                                                // round to nearest even
 // tcgen05 conv weights: [n_pad][kh][kw][cin_pad], channels past cin zero.
 std::vector<float> pack_conv_tc(const ConvWeight& cw, int n_pad, int cin_pad);

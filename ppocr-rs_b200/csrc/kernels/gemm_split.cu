@@ -685,6 +685,11 @@ int sm_count() {
 
 }  // namespace
 
+int gemm_split_conv_cpt(int cin) {
+    if (cin == 32) return 32;
+    return cin > 32 && cin % 4 == 0 ? (cin + 63) / 64 * 64 : 0;
+}
+
 int gemm_split_tile_n(int n, int k) {
     // One tile when it fits, else equal tiles; any multiple of 16 (the
     // epilogue stores 16-column boxes, so none reaches the next tile).  The
@@ -742,8 +747,10 @@ bool gemm_split_supported(const SplitGemmParams& p) {
     if (kt <= 0 || !split_tmem_cols(bn, (kt + KCHUNK - 1) / KCHUNK)) return false;
     if (p.conv) {
         if (p.a_planes) return false;
-        const int cin = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
-        if ((cin != 32 && cin % 64) || cin <= 0 || p.k != p.kh * p.kw * cin || p.lda % 4 || p.lda < cin || p.gate || p.residual)
+        const int cpt = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
+        const int cin = p.cin > 0 ? p.cin : cpt;
+        if (cpt <= 0 || gemm_split_conv_cpt(cin) != cpt || p.k != p.kh * p.kw * cpt || p.lda % 4 || p.lda < cin || p.gate ||
+            p.residual)
             return false;
         return p.n_img > 0 && p.hi > 0 && p.wi > 0 && p.ho > 0 && p.wo > 0 && (p.stride == 1 || p.stride == 2);
     }
@@ -841,7 +848,9 @@ cudaError_t launch_gemm_split(const SplitGemmParams& in, cudaStream_t stream) {
     const int smem = fixed + a.stages * a.a_stage_bytes;
     CUtensorMap ma, mw, mc;
     if (in.conv) {
-        if (!make_map4(&ma, in.a, (uint64_t)a.cpt, (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
+        // The map spans the input's own channels: a tap's padding channels
+        // (cpt > cin) fall outside it and load as zeros.
+        if (!make_map4(&ma, in.a, (uint64_t)(in.cin > 0 ? in.cin : a.cpt), (uint64_t)in.wi, (uint64_t)in.hi, (uint64_t)in.n_img, (uint64_t)in.lda * 4, 32,
                        16 * (uint32_t)in.stride, 8 * (uint32_t)in.stride, (uint32_t)in.stride, CU_TENSOR_MAP_SWIZZLE_128B) ||
             !make_map4(&mc, cbase, (uint64_t)in.n, (uint64_t)in.wo, (uint64_t)in.ho, (uint64_t)in.n_img, (uint64_t)in.ldc * 4,
                        16, 16, 2, 1, CU_TENSOR_MAP_SWIZZLE_64B))

@@ -249,14 +249,21 @@ struct SplitGemmParams {
     // (`a` and `gate` unused); the products, and so C, are bit-identical.
     const void* a_planes = nullptr;
     // Implicit-GEMM convolution (conv = 1): A is the NHWC FP32 input
-    // [n_img][hi][wi] with pixel pitch lda, cin == 32 or a multiple of 64 (K
-    // order (ky, kx, channel), k = kh * kw * cin); a tile is 8 x 16 output
-    // pixels of one image, each 64-wide K block one or two taps in strided 4D
-    // TMA boxes; C is NHWC [n_img][ho][wo] with pixel pitch ldc at channel
-    // coff.  No gate, residual or pre-split A in this mode.
+    // [n_img][hi][wi] with pixel pitch lda and `cin` channels; K order (ky,
+    // kx, channel) with each tap's channels padded to cpt = k / (kh * kw) =
+    // gemm_split_conv_cpt(cin) (the padding reads zeros: outside the TMA
+    // map); a tile is 8 x 16 output pixels of one image, each 64-wide K block
+    // one or two taps in strided 4D TMA boxes; C is NHWC [n_img][ho][wo] with
+    // pixel pitch ldc at channel coff.  No gate, residual or pre-split A in
+    // this mode.
     int conv = 0;
     int n_img = 0, hi = 0, wi = 0, ho = 0, wo = 0, kh = 0, kw = 0, stride = 1, pt = 0, pl = 0;
+    int cin = 0;                      // conv mode: input channels (0: cpt)
 };
+// Channels per tap of the split conv for `cin` input channels: 32 for 32, else
+// cin rounded up to a multiple of 64 (cin > 32, cin % 4 == 0); 0 when the
+// mode does not take cin.
+int gemm_split_conv_cpt(int cin);
 int gemm_split_tile_n(int n, int k);  // output channels per tile for K = k (n_pad is a multiple of it; 0: K too long)
 // The three BF16 pieces of A (gated as the GEMM would gate it) into
 // planes [3][m][k_pad], zeros past column k: p.a, p.lda, p.gate,

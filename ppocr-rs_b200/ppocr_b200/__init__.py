@@ -450,7 +450,8 @@ class Gpu:
 
     def selftest_conv_split(self, x, w, bias=None, stride: int = 1, pad: int = 1, act: int = 0):
         """The split GEMM's implicit conv (FP32 operands in three BF16 pieces on tcgen05):
-        x NHWC float32 [n, hi, wi, cin] (cin 32 or a multiple of 64), w OIHW [cout, cin, kh, kw];
+        x NHWC float32 [n, hi, wi, cin] (cin 32, or above 32 in multiples of 4: each tap's channels
+        read zero-padded to a multiple of 64), w OIHW [cout, cin, kh, kw];
         returns NHWC [n, ho, wo, cout]."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         w = np.ascontiguousarray(w, dtype=np.float32)

@@ -103,6 +103,9 @@ CONVS = [
     (1, 17, 35, 64, 48, 3, 1, 1, 0),
     (3, 9, 20, 32, 64, 3, 1, 1, 0),
     (2, 21, 38, 128, 64, 3, 2, 1, 1),    # the medium stem3: 128 channels (two K blocks per tap), K = 1,152
+    (2, 27, 46, 48, 24, 3, 2, 1, 1),     # the small stem3: 48 channels, each tap zero-padded to 64
+    (1, 12, 30, 96, 32, 3, 1, 1, 0),     # 96 channels: a tap's second K block half padding
+    (1, 14, 22, 36, 16, 2, 1, 0, 1),     # 36 channels, 2 x 2 kernel
 ]
 
 
@@ -123,7 +126,8 @@ def test_split_conv_fp32_class(gpu, n, hi, wi, cin, cout, k, stride, pad, act):
 def test_split_conv_rejects_other_channel_counts(gpu):
     import ppocr_b200 as P
 
-    x = np.zeros((1, 8, 8, 96), np.float32)
-    w = np.zeros((16, 96, 3, 3), np.float32)
-    with pytest.raises(P.InvalidInput):
-        gpu.selftest_conv_split(x, w)
+    for cin in (16, 34):   # below 32; not a multiple of 4
+        x = np.zeros((1, 8, 8, cin), np.float32)
+        w = np.zeros((16, cin, 3, 3), np.float32)
+        with pytest.raises(P.InvalidInput):
+            gpu.selftest_conv_split(x, w)
