@@ -362,8 +362,13 @@ struct HaloPlan {
 // it and has more than one input quad: every quad of a tile shares one stage.
 inline bool halo_tapq(const ConvParams& p) { return p.halo_order == 1 && p.src[0].mode != SRC_NCHW_F32 && p.cin > 4; }
 
-// Output channels the packed weights and the bias are padded to.
-inline int halo_bn(int cout) { return (cout + 7) / 8 * 8; }
+// Output channels the packed weights and the bias are padded to.  Up to 32
+// channels: 8, 16 or 32, so that the channel groups of TN = 8 or 16 divide the
+// block's eight warps (24 output channels run as 32, the last 8 computed and
+// not stored: the small detector's head conv_down 1.35 -> 0.87 ms).  Above,
+// multiples of 8 (48 channels padded to 64 measured slower than the direct
+// kernel: the small recognizer's stem2b 405 -> 528 us).
+inline int halo_bn(int cout) { return cout <= 8 ? 8 : cout <= 16 ? 16 : cout <= 32 ? 32 : (cout + 7) / 8 * 8; }
 
 // Tile shape and pipeline depth for one launch.  Candidates: TN in {16, 8}
 // channels per thread (G = bn / TN channel groups, TY = 8 / G rows), TM in
