@@ -526,7 +526,8 @@ cudaError_t launch_geom(const ConvParams& p, cudaStream_t stream) {
 int conv_halo_bn(int cout) { return halo_bn(cout); }
 
 bool conv_halo_supported(const ConvParams& p) {
-    if (p.cout < 8 || p.cout % 8 || p.cout > 64 || p.nsrc < 1 || p.nsrc > 4) return false;
+    // Output channels in whole quads (the store loop writes quads up to cout).
+    if (p.cout < 4 || p.cout % 4 || p.cout > 64 || p.nsrc < 1 || p.nsrc > 4) return false;
     const bool geom = (p.kh == 3 && p.kw == 3 && ((p.sh == 1 && p.sw == 1) || (p.sh == 2 && p.sw == 2))) ||
                       (p.kh == 2 && p.kw == 2 && p.sh == 1 && p.sw == 1);
     if (!geom) return false;
