@@ -277,10 +277,12 @@ int ppocr_selftest_gemm_ex(ppocr_gpu* gpu, int m, int n, int k, const float* a, 
  * (cin 32, or above 32 in multiples of 4: each tap's channels are read
  * zero-padded to a multiple of 64) with OIHW weights w [cout, cin, kh, kw], symmetric zero
  * padding `pad` and stride 1 or 2; out receives [n, ho, wo, cout] NHWC,
- * act as for ppocr_selftest_gemm_ex.  The model's dense FP32 convs over one
+ * act as for ppocr_selftest_gemm_ex, then + residual (may be NULL; NHWC
+ * [n, ho, wo, cout]).  The model's dense FP32 convs over one
  * such source use this path. */
 int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride,
-                              int pad, const float* x, const float* w, const float* bias, int act, float* out);
+                              int pad, const float* x, const float* w, const float* bias, int act,
+                              const float* residual, float* out);
 /* Diagnostic (new): the FP32 pointwise GEMM of the FP32 mode,
  * C[m, n] = act((A * gate) W[n, k]^T + bias) + residual, all in F32, through
  * one chosen kernel: kernel 0 = the model's dispatch, 1 = the register-tiled

@@ -1397,7 +1397,8 @@ int ppocr_selftest_dwconv(ppocr_gpu* gpu, int n, int hi, int wi, int c, int kh, 
 }
 
 int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, int cout, int kh, int kw, int stride, int pad,
-                              const float* x, const float* w, const float* bias, int act, float* out) {
+                              const float* x, const float* w, const float* bias, int act, const float* residual,
+                              float* out) {
     return guard([&] {
         if (!gpu || !x || !w || !out) fail(PPOCR_ERR_INVALID_INPUT, "null argument");
         if (n <= 0 || hi <= 0 || wi <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0)
@@ -1410,6 +1411,10 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
         p.n_img = n; p.hi = hi; p.wi = wi; p.ho = ho; p.wo = wo; p.kh = kh; p.kw = kw; p.stride = stride; p.pt = pad; p.pl = pad;
         const int cpt = gemm_split_conv_cpt(cin);
         p.k = kh * kw * cpt; p.cin = cin; p.n = cout; p.lda = cin; p.ldc = cout; p.coff = 0; p.act = act;
+        if (residual) {
+            p.residual = residual;   // host pointer for the support check; replaced by the device copy below
+            p.ldr = cout;
+        }
         const int bn = gemm_split_tile_n(cout, p.k);
         p.n_pad = bn > 0 ? (cout + bn - 1) / bn * bn : 0;
         p.k_pad = (p.k + 63) / 64 * 64;
@@ -1429,9 +1434,11 @@ int ppocr_selftest_conv_split(ppocr_gpu* gpu, int n, int hi, int wi, int cin, in
         const size_t xo = blob.add_f32(std::vector<float>(x, x + (size_t)n * hi * wi * cin));
         const size_t co = blob.add_f32(std::vector<float>(out_elems, 0.f));
         const size_t fo = blob.add_f32(std::vector<float>(64, 0.f));
+        const size_t ro = residual ? blob.add_f32(std::vector<float>(residual, residual + out_elems)) : 0;
         const std::vector<uint8_t>& bytes = blob.bytes();
         char* d = nullptr;
         cuda_check(cudaMalloc(&d, bytes.size()), "allocate conv test buffers");
+        if (residual) p.residual = reinterpret_cast<const float*>(d + ro);
         p.a = reinterpret_cast<const float*>(d + xo); p.w = d + wo_; p.bias = reinterpret_cast<const float*>(d + bo);
         p.c = reinterpret_cast<float*>(d + co);
         p.err = reinterpret_cast<int*>(d + fo);

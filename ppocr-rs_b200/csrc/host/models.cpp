@@ -165,7 +165,7 @@ public:
         Act4 out = into ? *into : tensor(name, n, ho, wo, cw.cout);
         const int out_cstride = into ? into->c : cw.cout, out_coff = into ? into_coff : 0;
         if (split_gemms() && srcs.size() == 1 && srcs[0].mode == SRC_NHWC && srcs[0].scale == 1 && srcs[0].coff == 0 &&
-            residual < 0 && sh == sw) {
+            (residual < 0 || res_scale == 1) && sh == sw) {
             // FP32 mode: a dense conv over one plain NHWC source as an implicit
             // split GEMM on tcgen05 (strided TMA boxes per tap; each tap's
             // channels padded with zeros to 32 or a multiple of 64).
@@ -176,6 +176,10 @@ public:
             sp.stride = sh; sp.pt = pt; sp.pl = pl;
             sp.k = cw.kh * cw.kw * cpt; sp.cin = cin; sp.n = cw.cout; sp.lda = srcs[0].cstride;
             sp.ldc = out_cstride; sp.coff = out_coff; sp.act = act;
+            if (residual >= 0) {
+                sp.residual = reinterpret_cast<const float*>(1);   // placeholder for the support check
+                sp.ldr = cw.cout;
+            }
             const int bn = gemm_split_tile_n(cw.cout, sp.k);
             sp.n_pad = bn > 0 ? (cw.cout + bn - 1) / bn * bn : 0;
             sp.k_pad = (sp.k + 63) / 64 * 64;
@@ -184,8 +188,9 @@ public:
                 const size_t woff = m_.blob.add_bf16(pack_engine_kn(cw, 3, sp.n_pad, sp.k_pad, cpt));
                 const size_t boff = m_.blob.add_f32(cw.b);
                 const int stid = srcs[0].tid, otid = out.tid;
-                m_.plan.add_op(name, {stid}, {otid}, [sp, woff, boff, stid, otid](const Ctx& c, cudaStream_t st) mutable {
+                m_.plan.add_op(name, {stid, residual}, {otid}, [sp, woff, boff, stid, otid, residual](const Ctx& c, cudaStream_t st) mutable {
                     sp.a = static_cast<const float*>(c.act(stid));
+                    sp.residual = residual >= 0 ? static_cast<const float*>(c.act(residual)) : nullptr;
                     sp.w = c.wb(woff);
                     sp.bias = c.wf(boff);
                     sp.c = static_cast<float*>(c.act(otid));

@@ -493,6 +493,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_split_kernel(const __grid_con
             const bool live = row < p.m;
             const float* rp = nullptr;
             const float* hrow = nullptr;
+            if (p.residual && p.conv) {
+                // Conv mode: row r of the tile is output pixel (r / 16, r % 16)
+                // of its 8 x 16 block; rows past the image edge add nothing.
+                const int mt = tile / args.n_tiles, per = args.tiles_y * args.tiles_x;
+                const int img = mt / per, rt = mt - img * per, r = q * 32 + lane;
+                const int oy = (rt / args.tiles_x) * 8 + r / 16, ox = (rt % args.tiles_x) * 16 + r % 16;
+                if (oy < p.ho && ox < p.wo) rp = p.residual + ((size_t)(img * p.ho + oy) * p.wo + ox) * p.ldr;
+            }
             if (live && p.residual && !p.conv) {
                 size_t rrow = (size_t)row;
                 if (p.res_scale > 1) {
@@ -750,7 +758,7 @@ bool gemm_split_supported(const SplitGemmParams& p) {
         const int cpt = p.kh * p.kw > 0 ? p.k / (p.kh * p.kw) : 0;
         const int cin = p.cin > 0 ? p.cin : cpt;
         if (cpt <= 0 || gemm_split_conv_cpt(cin) != cpt || p.k != p.kh * p.kw * cpt || p.lda % 4 || p.lda < cin || p.gate ||
-            p.residual)
+            (p.residual && (p.res_scale != 1 || p.res_gate || p.ldr < p.n)))
             return false;
         return p.n_img > 0 && p.hi > 0 && p.wi > 0 && p.ho > 0 && p.wo > 0 && (p.stride == 1 || p.stride == 2);
     }

@@ -254,7 +254,8 @@ struct SplitGemmParams {
     // gemm_split_conv_cpt(cin) (the padding reads zeros: outside the TMA
     // map); a tile is 8 x 16 output pixels of one image, each 64-wide K block
     // one or two taps in strided 4D TMA boxes; C is NHWC [n_img][ho][wo] with
-    // pixel pitch ldc at channel coff.  No gate, residual or pre-split A in
+    // pixel pitch ldc at channel coff; the residual (res_scale 1, no gate) is
+    // NHWC [n_img][ho][wo] with pixel pitch ldr.  No gate or pre-split A in
     // this mode.
     int conv = 0;
     int n_img = 0, hi = 0, wi = 0, ho = 0, wo = 0, kh = 0, kw = 0, stride = 1, pt = 0, pl = 0;

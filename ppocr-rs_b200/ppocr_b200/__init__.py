@@ -188,7 +188,7 @@ def library() -> C.CDLL:
         "ppocr_selftest_gemm_ex": (I, [P, I, I, I, FP, FP, FP, I, FP, I, I, I, FP, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]),
         "ppocr_selftest_gemm_f32": (I, [P, I, I, I, FP, FP, FP, I, FP, I, FP, I, FP, C.POINTER(C.c_int)]),
-        "ppocr_selftest_conv_split": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP]),
+        "ppocr_selftest_conv_split": (I, [P, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, FP]),
         "ppocr_measure_fp32_peak": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "ppocr_selftest_dwconv": (I, [P, I, I, I, I, I, I, I, I, I, I, I, I, FP, FP, FP, I, FP, I, I, FP,
                                       C.POINTER(C.c_int)]),
@@ -448,10 +448,11 @@ class Gpu:
                                                  None if r is None else _fptr(r), int(kernel), _fptr(c), C.byref(used)))
         return c, used.value
 
-    def selftest_conv_split(self, x, w, bias=None, stride: int = 1, pad: int = 1, act: int = 0):
+    def selftest_conv_split(self, x, w, bias=None, stride: int = 1, pad: int = 1, act: int = 0, residual=None):
         """The split GEMM's implicit conv (FP32 operands in three BF16 pieces on tcgen05):
         x NHWC float32 [n, hi, wi, cin] (cin 32, or above 32 in multiples of 4: each tap's channels
-        read zero-padded to a multiple of 64), w OIHW [cout, cin, kh, kw];
+        read zero-padded to a multiple of 64), w OIHW [cout, cin, kh, kw], residual (optional) NHWC
+        [n, ho, wo, cout] added after the activation;
         returns NHWC [n, ho, wo, cout]."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         w = np.ascontiguousarray(w, dtype=np.float32)
@@ -460,8 +461,12 @@ class Gpu:
         ho, wo = (hi + 2 * pad - kh) // stride + 1, (wi + 2 * pad - kw) // stride + 1
         out = np.zeros((n, ho, wo, cout), np.float32)
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        if r is not None and r.shape != out.shape:
+            raise InvalidInput("residual must have the output's shape")
         _check(library().ppocr_selftest_conv_split(self._h, n, hi, wi, cin, cout, kh, kw, int(stride), int(pad), _fptr(x),
-                                                   _fptr(w), None if b is None else _fptr(b), int(act), _fptr(out)))
+                                                   _fptr(w), None if b is None else _fptr(b), int(act),
+                                                   None if r is None else _fptr(r), _fptr(out)))
         return out
 
     def close(self) -> None:

@@ -123,6 +123,28 @@ def test_split_conv_fp32_class(gpu, n, hi, wi, cin, cout, k, stride, pad, act):
     assert np.all(err <= bound * 1.5), f"worst {float((err / bound).max()):.2f}x the bound"
 
 
+@pytest.mark.parametrize("n,hi,wi,cin,cout,stride,act", [
+    (2, 26, 46, 64, 64, 2, 0),    # the medium neck's bottom-up 3x3 s2 conv + the projection residual
+    (1, 19, 37, 48, 24, 1, 1),    # padded taps, ragged tiles, ReLU before the residual
+])
+def test_split_conv_residual(gpu, n, hi, wi, cin, cout, stride, act):
+    rng = np.random.default_rng(hi + wi * 3 + cin + cout)
+    x = rng.normal(0, 1, (n, hi, wi, cin)).astype(np.float32)
+    w = rng.normal(0, 1 / np.sqrt(cin * 9), (cout, cin, 3, 3)).astype(np.float32)
+    b = rng.normal(0, 0.1, cout).astype(np.float32)
+    ho, wo = (hi + 2 - 3) // stride + 1, (wi + 2 - 3) // stride + 1
+    r = rng.normal(0, 1, (n, ho, wo, cout)).astype(np.float32)
+    got = gpu.selftest_conv_split(x, w, b, stride=stride, pad=1, act=act, residual=r)
+    pre, mag = _conv_ref(x.astype(np.float64), w, b.astype(np.float64), stride, 1)
+    ref = _act(pre, act) + r
+    bound = 16 * 2.0 ** -24 * mag + 2.0 ** -24 * np.abs(ref) + 1e-30
+    err = np.abs(got - ref)
+    assert np.all(err <= bound * 1.5), f"worst {float((err / bound).max()):.2f}x the bound"
+    # The residual is added after the activation, once: without it the output differs by r.
+    plain = gpu.selftest_conv_split(x, w, b, stride=stride, pad=1, act=act)
+    np.testing.assert_array_equal(got, (plain + r).astype(np.float32))
+
+
 def test_split_conv_rejects_other_channel_counts(gpu):
     import ppocr_b200 as P
 
